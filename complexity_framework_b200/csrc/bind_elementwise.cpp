@@ -1,0 +1,227 @@
+// Python bindings of the memory-bound kernels (elementwise.cu).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "kernels.h"
+
+namespace {
+
+using cfb::bf16;
+
+void chk(const torch::Tensor& t, torch::ScalarType dt, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be CUDA");
+  TORCH_CHECK(t.scalar_type() == dt, name, " has wrong dtype ", t.scalar_type());
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+template <typename T>
+T* P(const torch::Tensor& t) {
+  return reinterpret_cast<T*>(t.data_ptr());
+}
+template <typename T>
+T* Popt(const c10::optional<torch::Tensor>& t) {
+  return t.has_value() ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+cudaStream_t cur() { return at::cuda::getCurrentCUDAStream(); }
+
+void rmsnorm_fwd(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& y,
+                 torch::Tensor& rstd, double eps) {
+  chk(x, torch::kBFloat16, "x");
+  chk(w, torch::kBFloat16, "w");
+  chk(y, torch::kBFloat16, "y");
+  chk(rstd, torch::kFloat32, "rstd");
+  const int64_t H = x.size(-1);
+  TORCH_CHECK(H % 8 == 0 && w.numel() == H, "rmsnorm: H must be a multiple of 8");
+  const int64_t T = x.numel() / H;
+  TORCH_CHECK(y.numel() == x.numel() && rstd.numel() >= T, "rmsnorm: output sizes");
+  const c10::cuda::CUDAGuard g(x.device());
+  cfb::rmsnorm_fwd(P<bf16>(x), P<bf16>(w), P<bf16>(y), P<float>(rstd), T, static_cast<int>(H),
+                   static_cast<float>(eps), cur());
+}
+
+void rmsnorm_bwd(const torch::Tensor& dy, const torch::Tensor& x, const torch::Tensor& w,
+                 const torch::Tensor& rstd, const c10::optional<torch::Tensor>& dres,
+                 torch::Tensor& dx, torch::Tensor& dw) {
+  chk(dy, torch::kBFloat16, "dy");
+  chk(x, torch::kBFloat16, "x");
+  chk(w, torch::kBFloat16, "w");
+  chk(rstd, torch::kFloat32, "rstd");
+  chk(dx, torch::kBFloat16, "dx");
+  chk(dw, torch::kFloat32, "dw");
+  if (dres.has_value()) chk(*dres, torch::kBFloat16, "dres");
+  const int64_t H = x.size(-1);
+  TORCH_CHECK(H % 8 == 0, "rmsnorm: H must be a multiple of 8");
+  const int64_t T = x.numel() / H;
+  TORCH_CHECK(dy.numel() == x.numel() && dx.numel() == x.numel() && dw.numel() == H,
+              "rmsnorm_bwd sizes");
+  const c10::cuda::CUDAGuard g(x.device());
+  cfb::rmsnorm_bwd(P<bf16>(dy), P<bf16>(x), P<bf16>(w), P<float>(rstd), Popt<bf16>(dres),
+                   P<bf16>(dx), P<float>(dw), T, static_cast<int>(H), cur());
+}
+
+void qk_norm_rope_fwd(const torch::Tensor& kqv, const torch::Tensor& qw, const torch::Tensor& kw,
+                      const torch::Tensor& cos_t, const torch::Tensor& sin_t,
+                      const c10::optional<torch::Tensor>& pos, torch::Tensor& q, torch::Tensor& k,
+                      torch::Tensor& v, torch::Tensor& rstd, int64_t B, int64_t S, int64_t Hq,
+                      int64_t Hkv, int64_t D, double eps, bool qk_norm) {
+  chk(kqv, torch::kBFloat16, "kqv");
+  chk(qw, torch::kBFloat16, "q_norm.weight");
+  chk(kw, torch::kBFloat16, "k_norm.weight");
+  chk(cos_t, torch::kFloat32, "cos");
+  chk(sin_t, torch::kFloat32, "sin");
+  chk(q, torch::kBFloat16, "q");
+  chk(k, torch::kBFloat16, "k");
+  chk(v, torch::kBFloat16, "v");
+  chk(rstd, torch::kFloat32, "rstd");
+  TORCH_CHECK(D == 64 || D == 128, "qk_norm_rope: head_dim must be 64 or 128");
+  TORCH_CHECK(kqv.numel() == B * S * (Hq + 2 * Hkv) * D, "kqv size");
+  TORCH_CHECK(q.numel() == B * Hq * S * D && k.numel() == B * Hkv * S * D &&
+                  v.numel() == B * Hkv * S * D,
+              "q/k/v size");
+  TORCH_CHECK(rstd.numel() >= B * S * (Hq + Hkv), "rstd size");
+  TORCH_CHECK(cos_t.size(-1) == D / 2, "cos table must be [P, D/2]");
+  if (pos.has_value()) {
+    chk(*pos, torch::kInt32, "pos");
+  } else {
+    TORCH_CHECK(cos_t.size(0) >= S, "cos table shorter than sequence");
+  }
+  const c10::cuda::CUDAGuard g(kqv.device());
+  cfb::qk_norm_rope_fwd(P<bf16>(kqv), P<bf16>(qw), P<bf16>(kw), P<float>(cos_t), P<float>(sin_t),
+                        Popt<int32_t>(pos), P<bf16>(q), P<bf16>(k), P<bf16>(v), P<float>(rstd),
+                        static_cast<int>(B), static_cast<int>(S), static_cast<int>(Hq),
+                        static_cast<int>(Hkv), static_cast<int>(D), static_cast<float>(eps),
+                        qk_norm, cur());
+}
+
+void qk_norm_rope_bwd(const torch::Tensor& dq, const torch::Tensor& dk, const torch::Tensor& dv,
+                      const torch::Tensor& kqv, const torch::Tensor& qw, const torch::Tensor& kw,
+                      const torch::Tensor& cos_t, const torch::Tensor& sin_t,
+                      const c10::optional<torch::Tensor>& pos, const torch::Tensor& rstd,
+                      torch::Tensor& dkqv, torch::Tensor& dqw, torch::Tensor& dkw, int64_t B,
+                      int64_t S, int64_t Hq, int64_t Hkv, int64_t D, bool qk_norm) {
+  chk(dq, torch::kBFloat16, "dq");
+  chk(dk, torch::kBFloat16, "dk");
+  chk(dv, torch::kBFloat16, "dv");
+  chk(kqv, torch::kBFloat16, "kqv");
+  chk(dkqv, torch::kBFloat16, "dkqv");
+  chk(dqw, torch::kFloat32, "dqw");
+  chk(dkw, torch::kFloat32, "dkw");
+  chk(rstd, torch::kFloat32, "rstd");
+  TORCH_CHECK(D == 64 || D == 128, "qk_norm_rope: head_dim must be 64 or 128");
+  TORCH_CHECK(dkqv.numel() == kqv.numel() && kqv.numel() == B * S * (Hq + 2 * Hkv) * D,
+              "dkqv size");
+  if (pos.has_value()) chk(*pos, torch::kInt32, "pos");
+  const c10::cuda::CUDAGuard g(kqv.device());
+  cfb::qk_norm_rope_bwd(P<bf16>(dq), P<bf16>(dk), P<bf16>(dv), P<bf16>(kqv), P<bf16>(qw),
+                        P<bf16>(kw), P<float>(cos_t), P<float>(sin_t), Popt<int32_t>(pos),
+                        P<float>(rstd), P<bf16>(dkqv), P<float>(dqw), P<float>(dkw),
+                        static_cast<int>(B), static_cast<int>(S), static_cast<int>(Hq),
+                        static_cast<int>(Hkv), static_cast<int>(D), qk_norm, cur());
+}
+
+void embedding_fwd(const torch::Tensor& ids, const torch::Tensor& table, torch::Tensor& out) {
+  chk(ids, torch::kInt64, "ids");
+  chk(table, torch::kBFloat16, "table");
+  chk(out, torch::kBFloat16, "out");
+  const int64_t H = table.size(1);
+  TORCH_CHECK(H % 8 == 0 && out.numel() == ids.numel() * H, "embedding sizes");
+  const c10::cuda::CUDAGuard g(ids.device());
+  cfb::embedding_fwd(P<int64_t>(ids), P<bf16>(table), P<bf16>(out), ids.numel(),
+                     static_cast<int>(H), table.size(0), cur());
+}
+
+void embedding_bwd(const torch::Tensor& ids, const torch::Tensor& dy, torch::Tensor& dtable) {
+  chk(ids, torch::kInt64, "ids");
+  chk(dy, torch::kBFloat16, "dy");
+  chk(dtable, torch::kFloat32, "dtable");
+  const int64_t H = dtable.size(1);
+  TORCH_CHECK(H % 8 == 0 && dy.numel() == ids.numel() * H, "embedding_bwd sizes");
+  const c10::cuda::CUDAGuard g(ids.device());
+  cfb::embedding_bwd(P<int64_t>(ids), P<bf16>(dy), P<float>(dtable), ids.numel(),
+                     static_cast<int>(H), dtable.size(0), cur());
+}
+
+void ce_loss_grad(torch::Tensor& logits, const torch::Tensor& stats, int64_t ntiles,
+                  const torch::Tensor& targets, torch::Tensor& loss, const torch::Tensor& scale,
+                  int64_t ignore_index) {
+  chk(logits, torch::kBFloat16, "logits");
+  chk(stats, torch::kFloat32, "stats");
+  chk(targets, torch::kInt64, "targets");
+  chk(loss, torch::kFloat32, "loss");
+  chk(scale, torch::kFloat32, "scale");
+  TORCH_CHECK(logits.dim() == 2 && logits.size(1) % 8 == 0, "logits must be [T, V], V % 8 == 0");
+  const int64_t T = logits.size(0);
+  TORCH_CHECK(targets.numel() == T && loss.numel() == T && stats.numel() >= T * ntiles * 2,
+              "ce sizes");
+  const c10::cuda::CUDAGuard g(logits.device());
+  cfb::ce_loss_grad(P<bf16>(logits), P<float>(stats), static_cast<int>(ntiles),
+                    P<int64_t>(targets), P<float>(loss), P<float>(scale), T,
+                    static_cast<int>(logits.size(1)), ignore_index, cur());
+}
+
+void route_scales(const torch::Tensor& ids, const torch::Tensor& table, const torch::Tensor& rw,
+                  torch::Tensor& out, int64_t E, double routed_scale) {
+  chk(ids, torch::kInt64, "ids");
+  chk(table, torch::kInt64, "route_table");
+  chk(rw, torch::kFloat32, "route_weights");
+  chk(out, torch::kFloat32, "out");
+  TORCH_CHECK(E >= 1 && E <= 16, "route_scales supports up to 16 experts");
+  TORCH_CHECK(table.dim() == 2 && rw.numel() == table.size(0), "route table/weights");
+  TORCH_CHECK(out.numel() == ids.numel() * E, "route_scales out size");
+  const c10::cuda::CUDAGuard g(ids.device());
+  cfb::route_scales(P<int64_t>(ids), P<int64_t>(table), P<float>(rw), P<float>(out), ids.numel(),
+                    static_cast<int>(table.size(0)), table.size(1), static_cast<int>(E),
+                    static_cast<float>(routed_scale), cur());
+}
+
+void adamw_flat(torch::Tensor& p, torch::Tensor& m, torch::Tensor& v, const torch::Tensor& g,
+                const c10::optional<torch::Tensor>& p_out, double lr, double b1, double b2,
+                double eps, double wd, double bc1, double bc2,
+                const c10::optional<torch::Tensor>& clip) {
+  chk(p, torch::kFloat32, "p");
+  chk(m, torch::kFloat32, "exp_avg");
+  chk(v, torch::kFloat32, "exp_avg_sq");
+  chk(g, torch::kBFloat16, "grad");
+  const int64_t n = p.numel();
+  TORCH_CHECK(m.numel() == n && v.numel() == n && g.numel() == n, "adamw sizes");
+  if (p_out.has_value()) {
+    chk(*p_out, torch::kBFloat16, "p_out");
+    TORCH_CHECK(p_out->numel() == n, "p_out size");
+  }
+  if (clip.has_value()) chk(*clip, torch::kFloat32, "clip");
+  const c10::cuda::CUDAGuard guard(p.device());
+  cfb::adamw_flat(P<float>(p), P<float>(m), P<float>(v), P<bf16>(g), Popt<bf16>(p_out), n,
+                  static_cast<float>(lr), static_cast<float>(b1), static_cast<float>(b2),
+                  static_cast<float>(eps), static_cast<float>(wd), static_cast<float>(bc1),
+                  static_cast<float>(bc2), Popt<float>(clip), cur());
+}
+
+void sumsq_bf16(const torch::Tensor& g, torch::Tensor& out) {
+  chk(g, torch::kBFloat16, "g");
+  chk(out, torch::kFloat32, "out");
+  const c10::cuda::CUDAGuard guard(g.device());
+  cfb::sumsq_bf16(P<bf16>(g), g.numel(), P<float>(out), cur());
+}
+
+void clip_coef(const torch::Tensor& sumsq, double max_norm, torch::Tensor& clip,
+               torch::Tensor& norm) {
+  const c10::cuda::CUDAGuard guard(sumsq.device());
+  cfb::clip_coef(P<float>(sumsq), static_cast<float>(max_norm), P<float>(clip), P<float>(norm),
+                 cur());
+}
+
+}  // namespace
+
+void register_elementwise(pybind11::module& m) {
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);
+  m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd);
+  m.def("embedding_fwd", &embedding_fwd);
+  m.def("embedding_bwd", &embedding_bwd);
+  m.def("ce_loss_grad", &ce_loss_grad);
+  m.def("route_scales", &route_scales);
+  m.def("adamw_flat", &adamw_flat);
+  m.def("sumsq_bf16", &sumsq_bf16);
+  m.def("clip_coef", &clip_coef);
+}

@@ -1,0 +1,199 @@
+// Python bindings of the sm_100a kernels.  Every entry point validates shapes,
+// dtypes, devices and alignment on the host and raises on violation: no silent
+// fallback.  Kernels report device-side failures (bounded-wait timeouts,
+// bounds checks) through a per-device error word read by check_errors().
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "gemm_tc.h"
+#include "kernels.h"
+
+namespace {
+
+std::mutex g_err_mu;
+std::unordered_map<int, torch::Tensor> g_err;
+
+int* err_ptr(int device) {
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  auto it = g_err.find(device);
+  if (it == g_err.end()) {
+    auto t = torch::zeros({4}, torch::dtype(torch::kInt32).device(torch::kCUDA, device));
+    it = g_err.emplace(device, t).first;
+  }
+  return it->second.data_ptr<int>();
+}
+
+torch::Tensor error_buffer(int64_t device) {
+  err_ptr(static_cast<int>(device));
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  return g_err[static_cast<int>(device)];
+}
+
+int num_sms(int device) {
+  static std::unordered_map<int, int> cache;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(device);
+  if (it != cache.end()) return it->second;
+  int v = 0;
+  cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device);
+  cache[device] = v;
+  return v;
+}
+
+void check_bf16_cuda(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == torch::kBFloat16, name, " must be bfloat16");
+}
+
+// Row-major 2-D view check: last stride 1, leading dim multiple of 8 elements,
+// base 16-byte aligned (TMA requirements).
+int64_t ld_of(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.dim() == 2, name, " must be 2-D");
+  TORCH_CHECK(t.stride(1) == 1, name, " must have unit inner stride");
+  const int64_t ld = t.size(0) > 1 ? t.stride(0) : t.size(1);
+  TORCH_CHECK(ld % 8 == 0, name, " leading dimension must be a multiple of 8 elements");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name,
+              " must be 16-byte aligned");
+  return ld;
+}
+
+void raise_rc(int rc, const char* what) {
+  TORCH_CHECK(rc == 0, what, " launch failed with code ", rc,
+              rc > 0 && rc < 1000 ? cudaGetErrorString(static_cast<cudaError_t>(rc)) : "");
+}
+
+// C[M,N] = epi(sum_k A(m,k) B(n,k)).  See gemm_tc.h for operand conventions.
+void gemm(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, int64_t M,
+          int64_t N, int64_t K, int64_t epi, const c10::optional<torch::Tensor>& out,
+          const c10::optional<torch::Tensor>& residual, double alpha,
+          const c10::optional<torch::Tensor>& gu, const c10::optional<torch::Tensor>& act,
+          const c10::optional<torch::Tensor>& row_scale, int64_t shared_width,
+          int64_t expert_width, int64_t n_experts, double shared_scale,
+          const c10::optional<torch::Tensor>& stats, int64_t bn) {
+  check_bf16_cuda(A, "A");
+  check_bf16_cuda(B, "B");
+  const c10::cuda::CUDAGuard guard(A.device());
+  cfb::GemmArgs g;
+  g.A = A.data_ptr();
+  g.lda = ld_of(A, "A");
+  g.a_mn = a_mn;
+  g.B = B.data_ptr();
+  g.ldb = ld_of(B, "B");
+  g.b_mn = b_mn;
+  g.M = static_cast<int>(M);
+  g.N = static_cast<int>(N);
+  g.K = static_cast<int>(K);
+  g.epi = static_cast<int>(epi);
+  g.bn = static_cast<int>(bn);
+  g.num_sms = num_sms(A.get_device());
+  TORCH_CHECK(N % 32 == 0, "gemm: N must be a multiple of 32");
+  // operand extents
+  if (!a_mn) {
+    TORCH_CHECK(A.size(0) >= M && A.size(1) >= K, "gemm: A too small");
+  } else {
+    TORCH_CHECK(A.size(0) >= K && A.size(1) >= M, "gemm: A too small");
+  }
+  if (!b_mn) {
+    TORCH_CHECK(B.size(0) >= N && B.size(1) >= K, "gemm: B too small");
+  } else {
+    TORCH_CHECK(B.size(0) >= K && B.size(1) >= N, "gemm: B too small");
+  }
+
+  cfb::GemmEpi ep;
+  ep.alpha = static_cast<float>(alpha);
+  if (epi == cfb::EPI_SWIGLU_FWD) {
+    TORCH_CHECK(gu.has_value() && act.has_value(), "swiglu fwd needs gu and act");
+    check_bf16_cuda(*gu, "gu");
+    check_bf16_cuda(*act, "act");
+    TORCH_CHECK(gu->size(0) >= M && gu->size(1) >= N, "gu too small");
+    TORCH_CHECK(act->size(0) >= M && act->size(1) >= N / 2, "act too small");
+    TORCH_CHECK(N % (2 * cfb::kSwigluBlock) == 0, "swiglu fwd: N must be a multiple of 256");
+    ep.gu = reinterpret_cast<__nv_bfloat16*>(gu->data_ptr());
+    ep.ldgu = ld_of(*gu, "gu");
+    ep.act = reinterpret_cast<__nv_bfloat16*>(act->data_ptr());
+    ep.ldact = ld_of(*act, "act");
+  } else {
+    TORCH_CHECK(out.has_value(), "gemm needs out");
+    TORCH_CHECK(out->is_cuda(), "out must be CUDA");
+    const bool f32 = epi == cfb::EPI_F32 || epi == cfb::EPI_F32_ACC;
+    TORCH_CHECK(out->scalar_type() == (f32 ? torch::kFloat32 : torch::kBFloat16),
+                "out dtype mismatch for epilogue");
+    TORCH_CHECK(out->dim() == 2 && out->stride(1) == 1, "out must be row-major 2-D");
+    ep.c = out->data_ptr();
+    ep.ldc = out->size(0) > 1 ? out->stride(0) : out->size(1);
+    TORCH_CHECK(ep.ldc % 8 == 0, "out leading dim must be a multiple of 8");
+    if (epi == cfb::EPI_SWIGLU_BWD) {
+      TORCH_CHECK(out->size(0) >= M && out->size(1) >= 2 * N, "d(gu) too small");
+      TORCH_CHECK(N % cfb::kSwigluBlock == 0, "swiglu bwd: N must be a multiple of 128");
+      TORCH_CHECK(gu.has_value(), "swiglu bwd needs gu");
+      check_bf16_cuda(*gu, "gu");
+      ep.gu = reinterpret_cast<__nv_bfloat16*>(gu->data_ptr());
+      ep.ldgu = ld_of(*gu, "gu");
+    } else {
+      TORCH_CHECK(out->size(0) >= M && out->size(1) >= N, "out too small");
+    }
+  }
+  if (epi == cfb::EPI_RESID) {
+    TORCH_CHECK(residual.has_value(), "residual epilogue needs residual");
+    check_bf16_cuda(*residual, "residual");
+    TORCH_CHECK(residual->size(0) >= M && residual->size(1) >= N, "residual too small");
+    ep.r = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    ep.ldr = ld_of(*residual, "residual");
+  }
+  if (epi == cfb::EPI_SWIGLU_FWD || epi == cfb::EPI_SWIGLU_BWD) {
+    ep.shared_width = static_cast<int>(shared_width);
+    ep.expert_width = static_cast<int>(expert_width > 0 ? expert_width : 1);
+    ep.n_experts = static_cast<int>(n_experts);
+    ep.shared_scale = static_cast<float>(shared_scale);
+    const int64_t act_width = epi == cfb::EPI_SWIGLU_FWD ? N / 2 : N;
+    TORCH_CHECK(shared_width % 32 == 0 && (n_experts == 0 || expert_width % 32 == 0),
+                "swiglu widths must be multiples of 32");
+    TORCH_CHECK(shared_width + n_experts * expert_width == act_width,
+                "swiglu: shared_width + n_experts*expert_width must equal activation width");
+    if (n_experts > 0) {
+      TORCH_CHECK(row_scale.has_value(), "routed experts need row_scale");
+      TORCH_CHECK(row_scale->scalar_type() == torch::kFloat32 && row_scale->is_contiguous(),
+                  "row_scale must be contiguous fp32");
+      TORCH_CHECK(row_scale->numel() >= M * n_experts, "row_scale too small");
+      ep.row_scale = row_scale->data_ptr<float>();
+    }
+  }
+  if (epi == cfb::EPI_CE_STATS) {
+    TORCH_CHECK(stats.has_value() && stats->scalar_type() == torch::kFloat32 &&
+                    stats->is_contiguous(),
+                "ce stats epilogue needs contiguous fp32 stats");
+    const int use_bn = bn ? static_cast<int>(bn) : cfb::choose_bn(g.M, g.N, g.num_sms);
+    g.bn = use_bn;
+    TORCH_CHECK(stats->numel() >= M * ((N + use_bn - 1) / use_bn) * 2, "stats too small");
+    ep.stats = stats->data_ptr<float>();
+  }
+  const int rc = cfb::gemm_tc_launch(g, ep, at::cuda::getCurrentCUDAStream(),
+                                     err_ptr(A.get_device()));
+  raise_rc(rc, "gemm");
+}
+
+int64_t gemm_choose_bn(int64_t M, int64_t N, int64_t device) {
+  return cfb::choose_bn(static_cast<int>(M), static_cast<int>(N), num_sms(static_cast<int>(device)));
+}
+
+}  // namespace
+
+void register_elementwise(pybind11::module& m);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("error_buffer", &error_buffer);
+  m.def("gemm", &gemm, "tcgen05 GEMM with fused epilogues", py::arg("A"), py::arg("a_mn"),
+        py::arg("B"), py::arg("b_mn"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epi"),
+        py::arg("out") = py::none(), py::arg("residual") = py::none(), py::arg("alpha") = 1.0,
+        py::arg("gu") = py::none(), py::arg("act") = py::none(),
+        py::arg("row_scale") = py::none(), py::arg("shared_width") = 0,
+        py::arg("expert_width") = 0, py::arg("n_experts") = 0, py::arg("shared_scale") = 1.0,
+        py::arg("stats") = py::none(), py::arg("bn") = 0);
+  m.def("gemm_choose_bn", &gemm_choose_bn);
+  register_elementwise(m);
+}

@@ -1,0 +1,479 @@
+// Persistent, warp-specialised bf16 GEMM for sm_100a on the 5th-generation
+// tensor cores (tcgen05.mma, accumulators in tensor memory, operands staged by
+// TMA into 128-byte-swizzled shared memory).
+//
+//   C[M,N] = epilogue( sum_k A(m,k) * B(n,k) )
+//
+// Operand storage (row-major, leading dimension in elements):
+//   A K-major : A[M][lda]     (lda >= K)      A MN-major : A[K][lda] (lda >= M)
+//   B K-major : B[N][ldb]     (ldb >= K)      B MN-major : B[K][ldb] (ldb >= N)
+// so forward (X W^T), data-gradient (dY W) and weight-gradient (dY^T X) of a
+// linear layer are all one kernel with different major flags, no transposes.
+//
+// CTA layout (256 threads, one CTA per SM, grid = #SMs, static tile striding):
+//   warp 0      : TMA producer (one elected lane)
+//   warp 1      : TMEM allocator + MMA issuer (one elected lane)
+//   warps 4..7  : epilogue warpgroup; warp w reads TMEM lanes 32*(w%4)..+31
+// The accumulator is double-buffered in TMEM (2 x BN fp32 columns) so the
+// epilogue of tile i overlaps the main loop of tile i+1.
+//
+// Epilogues fuse the elementwise work that follows each GEMM of the TR-Hash
+// decoder layer: residual add (o_proj, MLP down), SwiGLU with the per-token
+// routing weights of the deterministic experts (gate|up GEMM), the SwiGLU
+// backward (data-gradient of the down projection), fp32 stores/accumulation
+// for weight gradients, and per-tile softmax statistics for the fused LM-head
+// cross-entropy.  Reference counterparts: the cuBLAS F.linear calls in
+// complexity/core/attention/gqa.py:215-217,165 and
+// complexity/tr_hash/engine.py:333-349, the Triton grouped GEMMs K4/K5/K7 of
+// complexity_cuda/triton_token_routed.py:1031-1229,751-838 and the SwiGLU
+// kernel K6 (:1232-1259).
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "gemm_tc.h"
+
+namespace cfb {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int A_BYTES = kBM * kBK * 2;
+  static constexpr int B_BYTES = BN * kBK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = BN >= 256 ? 4 : 6;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v, float alpha) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w;
+    w.x = pack_bf16x2(v[q * 8 + 0] * alpha, v[q * 8 + 1] * alpha);
+    w.y = pack_bf16x2(v[q * 8 + 2] * alpha, v[q * 8 + 3] * alpha);
+    w.z = pack_bf16x2(v[q * 8 + 4] * alpha, v[q * 8 + 5] * alpha);
+    w.w = pack_bf16x2(v[q * 8 + 6] * alpha, v[q * 8 + 7] * alpha);
+    d[q] = w;
+  }
+}
+
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w = s[q];
+    float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y), c = unpack_bf16x2(w.z),
+           d = unpack_bf16x2(w.w);
+    v[q * 8 + 0] = a.x; v[q * 8 + 1] = a.y; v[q * 8 + 2] = b.x; v[q * 8 + 3] = b.y;
+    v[q * 8 + 4] = c.x; v[q * 8 + 5] = c.y; v[q * 8 + 6] = d.x; v[q * 8 + 7] = d.y;
+  }
+}
+
+// Scale that multiplies SwiGLU activation column `c` of row `row`.
+__device__ __forceinline__ float swiglu_col_scale(const GemmEpi& ep, int row, int c) {
+  if (c < ep.shared_width) return ep.shared_scale;
+  int e = (c - ep.shared_width) / ep.expert_width;
+  return ep.row_scale[static_cast<int64_t>(row) * ep.n_experts + e];
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(256, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   int M, int N, int K, GemmEpi ep, int* err) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr uint32_t IDESC = idesc_bf16(kBM, BN, A_MN, B_MN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* tiles = smem;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  const int num_m = (M + kBM - 1) / kBM;
+  const int num_n = (N + BN - 1) / BN;
+  const int total = num_m * num_n;
+  const int nk = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const int m0 = (t / num_n) * kBM;
+        const int n0 = (t % num_n) * BN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty, 10)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sA = tiles + stage * Cfg::STAGE_BYTES;
+          uint8_t* sB = sA + Cfg::A_BYTES;
+          mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+          if constexpr (!A_MN) {
+            tma_load_2d(sA, &tmA, &full_bar[stage], kb * kBK, m0);
+          } else {
+#pragma unroll
+            for (int i = 0; i < kBM / 64; ++i)
+              tma_load_2d(sA + i * 64 * kBK * 2, &tmA, &full_bar[stage], m0 + 64 * i, kb * kBK);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d(sB, &tmB, &full_bar[stage], kb * kBK, n0);
+          } else {
+#pragma unroll
+            for (int i = 0; i < BN / 64; ++i)
+              tma_load_2d(sB + i * 64 * kBK * 2, &tmB, &full_bar[stage], n0 + 64 * i, kb * kBK);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, abort_flag, err, kErrTimeoutTmem, 11)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, err, kErrTimeoutFull, 12)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(tiles + stage * Cfg::STAGE_BYTES);
+          const uint32_t b_base = a_base + Cfg::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t adesc = A_MN ? sw128_desc(a_base + k * 2048, 64 * kBK * 2, 1024)
+                                        : sw128_desc(a_base + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? sw128_desc(b_base + k * 2048, 64 * kBK * 2, 1024)
+                                        : sw128_desc(b_base + k * 32, 16, 1024);
+            umma_bf16(d_tmem, adesc, bdesc, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    const int wq = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const int m_blk = t / num_n;
+      const int n_blk = t % num_n;
+      const int m0 = m_blk * kBM;
+      const int n0 = n_blk * BN;
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, err, kErrTimeoutTmem, 13)) break;
+      tc_fence_after();
+      const int row = m0 + wq * 32 + lane;
+      const bool row_ok = row < M;
+      const uint32_t tbase = tmem_base + acc * BN + (static_cast<uint32_t>(wq * 32) << 16);
+
+      if constexpr (EPI == EPI_SWIGLU_FWD) {
+        // Tile columns [0, BN/2) are gate, [BN/2, BN) are the matching up columns.
+        constexpr int HALF = BN / 2;
+#pragma unroll 1
+        for (int c = 0; c < HALF; c += 32) {
+          float g[32], u[32];
+          tmem_ld32(tbase + c, g);
+          tmem_ld32(tbase + HALF + c, u);
+          tmem_wait_ld();
+          const int act_col = n_blk * HALF + c;
+          if (row_ok && n0 + c < N) {
+            __nv_bfloat16* gu_row = ep.gu + static_cast<int64_t>(row) * ep.ldgu;
+            store_bf16x32(gu_row + n0 + c, g, 1.0f);
+            store_bf16x32(gu_row + n0 + HALF + c, u, 1.0f);
+            const float s = swiglu_col_scale(ep, row, act_col);
+            float a[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              // Round the pre-activations to bf16 first so that forward and the
+              // recomputation in backward see identical inputs.
+              const float gb = __bfloat162float(__float2bfloat16(g[i]));
+              const float ub = __bfloat162float(__float2bfloat16(u[i]));
+              a[i] = silu_f(gb) * ub * s;
+            }
+            store_bf16x32(ep.act + static_cast<int64_t>(row) * ep.ldact + act_col, a, 1.0f);
+          }
+        }
+      } else if constexpr (EPI == EPI_SWIGLU_BWD) {
+        // Accumulator = d(act) for activation columns [n0, n0+BN).
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.c);
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float da[32];
+          tmem_ld32(tbase + c, da);
+          tmem_wait_ld();
+          const int act_col = n0 + c;
+          if (row_ok && act_col < N) {
+            const int blk = act_col / kSwigluBlock;
+            const int w = act_col % kSwigluBlock;
+            const int64_t goff = static_cast<int64_t>(row) * ep.ldgu + blk * 2 * kSwigluBlock + w;
+            float g[32], u[32];
+            load_bf16x32(ep.gu + goff, g);
+            load_bf16x32(ep.gu + goff + kSwigluBlock, u);
+            const float s = swiglu_col_scale(ep, row, act_col);
+            float dg[32], du[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float sg = 1.0f / (1.0f + __expf(-g[i]));
+              const float sl = g[i] * sg;
+              const float d = da[i] * s;
+              du[i] = d * sl;
+              dg[i] = d * u[i] * sg * (1.0f + g[i] * (1.0f - sg));
+            }
+            const int64_t ooff = static_cast<int64_t>(row) * ep.ldc + blk * 2 * kSwigluBlock + w;
+            store_bf16x32(out + ooff, dg, 1.0f);
+            store_bf16x32(out + ooff + kSwigluBlock, du, 1.0f);
+          }
+        }
+      } else if constexpr (EPI == EPI_CE_STATS) {
+        // Store bf16 logits and, per (row, n-tile), the max and sum(exp(x-max)).
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.c);
+        float mx = -INFINITY, se = 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld32(tbase + c, v);
+          tmem_wait_ld();
+          if (row_ok && n0 + c < N) {
+            float lm = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              v[i] = __bfloat162float(__float2bfloat16(v[i] * ep.alpha));
+              if (n0 + c + i < N) lm = fmaxf(lm, v[i]);
+            }
+            const float nm = fmaxf(mx, lm);
+            float acc_e = se * __expf(mx - nm);
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (n0 + c + i < N) acc_e += __expf(v[i] - nm);
+            mx = nm;
+            se = acc_e;
+            store_bf16x32(out + static_cast<int64_t>(row) * ep.ldc + n0 + c, v, 1.0f);
+          }
+        }
+        if (row_ok) {
+          float2* st = reinterpret_cast<float2*>(ep.stats);
+          st[static_cast<int64_t>(row) * num_n + n_blk] = make_float2(mx, se);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld32(tbase + c, v);
+          tmem_wait_ld();
+          if (row_ok && n0 + c < N) {
+            if constexpr (EPI == EPI_STORE) {
+              __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.c);
+              store_bf16x32(out + static_cast<int64_t>(row) * ep.ldc + n0 + c, v, ep.alpha);
+            } else if constexpr (EPI == EPI_RESID) {
+              __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.c);
+              float r[32];
+              load_bf16x32(ep.r + static_cast<int64_t>(row) * ep.ldr + n0 + c, r);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = v[i] * ep.alpha + r[i];
+              store_bf16x32(out + static_cast<int64_t>(row) * ep.ldc + n0 + c, v, 1.0f);
+            } else if constexpr (EPI == EPI_F32 || EPI == EPI_F32_ACC) {
+              float4* out = reinterpret_cast<float4*>(reinterpret_cast<float*>(ep.c) +
+                                                      static_cast<int64_t>(row) * ep.ldc + n0 + c);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                float4 w = make_float4(v[4 * q] * ep.alpha, v[4 * q + 1] * ep.alpha,
+                                       v[4 * q + 2] * ep.alpha, v[4 * q + 3] * ep.alpha);
+                if constexpr (EPI == EPI_F32_ACC) {
+                  float4 o = out[q];
+                  w.x += o.x; w.y += o.y; w.z += o.z; w.w += o.w;
+                }
+                out[q] = w;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q);
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+}  // namespace
+
+// Map a row-major bf16 matrix [rows][ld] (inner extent `cols`) as 2-D tiles of
+// box_inner x box_outer with 128-byte swizzle.
+int make_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                 int box_inner, int box_outer) {
+  auto fn = get_encode_fn();
+  if (fn == nullptr) return -1;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : static_cast<int>(r) + 1000;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+static int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
+                       const GemmEpi& ep, int num_sms, cudaStream_t stream, int* err) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI>;
+  static bool attr_set = false;  // one per instantiation
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    attr_set = true;
+  }
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  kern<<<grid, 256, Cfg::SMEM_BYTES, stream>>>(ta, tb, M, N, K, ep, err);
+  return static_cast<int>(cudaGetLastError());
+}
+
+template <int BN, int EPI>
+static int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+                          int M, int N, int K, const GemmEpi& ep, int sms, cudaStream_t s,
+                          int* err) {
+  if (!a_mn && !b_mn) return launch_impl<BN, false, false, EPI>(ta, tb, M, N, K, ep, sms, s, err);
+  if (!a_mn && b_mn) return launch_impl<BN, false, true, EPI>(ta, tb, M, N, K, ep, sms, s, err);
+  if (a_mn && !b_mn) return launch_impl<BN, true, false, EPI>(ta, tb, M, N, K, ep, sms, s, err);
+  return launch_impl<BN, true, true, EPI>(ta, tb, M, N, K, ep, sms, s, err);
+}
+
+int choose_bn(int M, int N, int num_sms) {
+  auto cost = [&](int bn) {
+    long tiles = static_cast<long>((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
+    long waves = (tiles + num_sms - 1) / num_sms;
+    return waves * bn;
+  };
+  return cost(128) < cost(256) ? 128 : 256;
+}
+
+int gemm_tc_launch(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream, int* err) {
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0) return -2;
+  int bn = g.bn;
+  if (g.epi == EPI_SWIGLU_FWD) bn = 2 * kSwigluBlock;
+  if (bn == 0) bn = choose_bn(g.M, g.N, g.num_sms);
+  if (bn != 128 && bn != 256) return -3;
+  CUtensorMap ta, tb;
+  int rc;
+  if (!g.a_mn)
+    rc = make_tmap_2d(&ta, g.A, g.M, g.K, g.lda, kBK, kBM);
+  else
+    rc = make_tmap_2d(&ta, g.A, g.K, g.M, g.lda, 64, kBK);
+  if (rc) return rc;
+  if (!g.b_mn)
+    rc = make_tmap_2d(&tb, g.B, g.N, g.K, g.ldb, kBK, bn);
+  else
+    rc = make_tmap_2d(&tb, g.B, g.K, g.N, g.ldb, 64, kBK);
+  if (rc) return rc;
+
+#define CFB_EPI_CASE(E)                                                                          \
+  case E:                                                                                        \
+    return bn == 256 ? dispatch_major<256, E>(g.a_mn, g.b_mn, ta, tb, g.M, g.N, g.K, ep,          \
+                                              g.num_sms, stream, err)                            \
+                     : dispatch_major<128, E>(g.a_mn, g.b_mn, ta, tb, g.M, g.N, g.K, ep,          \
+                                              g.num_sms, stream, err);
+  switch (g.epi) {
+    CFB_EPI_CASE(EPI_STORE)
+    CFB_EPI_CASE(EPI_RESID)
+    CFB_EPI_CASE(EPI_F32)
+    CFB_EPI_CASE(EPI_F32_ACC)
+    CFB_EPI_CASE(EPI_CE_STATS)
+    case EPI_SWIGLU_FWD:
+      if (g.a_mn || g.b_mn) return -4;
+      return launch_impl<256, false, false, EPI_SWIGLU_FWD>(ta, tb, g.M, g.N, g.K, ep, g.num_sms,
+                                                            stream, err);
+    case EPI_SWIGLU_BWD:
+      if (g.a_mn || !g.b_mn) return -4;
+      return bn == 256 ? launch_impl<256, false, true, EPI_SWIGLU_BWD>(ta, tb, g.M, g.N, g.K, ep,
+                                                                       g.num_sms, stream, err)
+                       : launch_impl<128, false, true, EPI_SWIGLU_BWD>(ta, tb, g.M, g.N, g.K, ep,
+                                                                       g.num_sms, stream, err);
+    default:
+      return -5;
+  }
+#undef CFB_EPI_CASE
+}
+
+}  // namespace cfb

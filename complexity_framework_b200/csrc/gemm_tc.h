@@ -1,0 +1,61 @@
+// Host interface of the tcgen05 GEMM (see gemm_tc.cu for the kernel design).
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace cfb {
+
+enum GemmEpilogue : int {
+  EPI_STORE = 0,       // C(bf16) = alpha * acc
+  EPI_RESID = 1,       // C(bf16) = alpha * acc + R(bf16)
+  EPI_SWIGLU_FWD = 2,  // gate|up tile -> GU(bf16 pre-activations), ACT = silu(g)*u*scale
+  EPI_SWIGLU_BWD = 3,  // acc = d(ACT) -> C = d(GU) using saved GU
+  EPI_F32 = 4,         // C(fp32) = alpha * acc
+  EPI_F32_ACC = 5,     // C(fp32) += alpha * acc
+  EPI_CE_STATS = 6,    // C(bf16) logits = alpha*acc; stats[row, ntile] = (max, sumexp)
+};
+
+// Width (in activation columns) of one gate block in the packed gate|up weight:
+// packed rows [256j, 256j+128) are gate rows [128j, 128j+128) and rows
+// [256j+128, 256j+256) the matching up rows.
+constexpr int kSwigluBlock = 128;
+
+struct GemmEpi {
+  void* c = nullptr;
+  int64_t ldc = 0;
+  const __nv_bfloat16* r = nullptr;
+  int64_t ldr = 0;
+  float alpha = 1.0f;
+  __nv_bfloat16* gu = nullptr;
+  int64_t ldgu = 0;
+  __nv_bfloat16* act = nullptr;
+  int64_t ldact = 0;
+  const float* row_scale = nullptr;  // [M, n_experts]
+  int shared_width = 0;
+  int expert_width = 1;
+  int n_experts = 0;
+  float shared_scale = 1.0f;
+  float* stats = nullptr;  // [M, ceil(N/BN)] float2
+};
+
+struct GemmArgs {
+  const void* A = nullptr;
+  int64_t lda = 0;
+  bool a_mn = false;
+  const void* B = nullptr;
+  int64_t ldb = 0;
+  bool b_mn = false;
+  int M = 0, N = 0, K = 0;
+  int epi = EPI_STORE;
+  int bn = 0;  // 0 = choose
+  int num_sms = 148;
+};
+
+int gemm_tc_launch(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream, int* err);
+int choose_bn(int M, int N, int num_sms);
+int make_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                 int box_inner, int box_outer);
+
+}  // namespace cfb

@@ -1,0 +1,55 @@
+// Host launchers of the memory-bound sm_100a kernels (elementwise.cu).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace cfb {
+
+using bf16 = __nv_bfloat16;
+
+// RMSNorm over the last dim H (H % 8 == 0).  y = bf16(bf16(x*rstd) * w).
+void rmsnorm_fwd(const bf16* x, const bf16* w, bf16* y, float* rstd, int64_t T, int H, float eps,
+                 cudaStream_t s);
+// dx = rmsnorm'(x)^T dy (+ dres);  dw (fp32, [H]) += sum_rows dy * x*rstd.
+void rmsnorm_bwd(const bf16* dy, const bf16* x, const bf16* w, const float* rstd,
+                 const bf16* dres, bf16* dx, float* dw, int64_t T, int H, cudaStream_t s);
+
+// kqv [T, (2*Hkv+Hq)*D] in k|q|v order -> per-head RMSNorm of q and k, RoPE
+// (rotate-half, cos/sin tables [P, D/2]) and scatter to head-major q/k/v
+// [B, H, S, D].  rstd [T, Hq+Hkv] (q heads first).
+void qk_norm_rope_fwd(const bf16* kqv, const bf16* qw, const bf16* kw, const float* cos_t,
+                      const float* sin_t, const int32_t* pos, bf16* q, bf16* k, bf16* v,
+                      float* rstd, int B, int S, int Hq, int Hkv, int D, float eps, bool qk_norm,
+                      cudaStream_t s);
+void qk_norm_rope_bwd(const bf16* dq, const bf16* dk, const bf16* dv, const bf16* kqv,
+                      const bf16* qw, const bf16* kw, const float* cos_t, const float* sin_t,
+                      const int32_t* pos, const float* rstd, bf16* dkqv, float* dqw, float* dkw,
+                      int B, int S, int Hq, int Hkv, int D, bool qk_norm, cudaStream_t s);
+
+void embedding_fwd(const int64_t* ids, const bf16* table, bf16* out, int64_t T, int H, int64_t V,
+                   cudaStream_t s);
+void embedding_bwd(const int64_t* ids, const bf16* dy, float* dtable, int64_t T, int H, int64_t V,
+                   cudaStream_t s);
+
+// Cross-entropy from bf16 logits and per-(row, n-tile) (max, sumexp) partials.
+// Writes loss[row] and overwrites logits with d(loss_sum*scale)/d(logits).
+void ce_loss_grad(bf16* logits, const float* stats, int ntiles, const int64_t* targets,
+                  float* loss, const float* scale, int64_t T, int V, int64_t ignore_index,
+                  cudaStream_t s);
+
+// Per-token routed expert scales: row_scale[t, e] = routed_scale * sum_j w_j [R[j, id_t] == e].
+void route_scales(const int64_t* ids, const int64_t* table, const float* route_w, float* out,
+                  int64_t T, int top_k, int64_t V, int E, float routed_scale, cudaStream_t s);
+
+// Flat-buffer AdamW (torch.optim.AdamW semantics) with fp32 master weights;
+// writes the bf16 compute copy.  clip (device scalar or nullptr) scales grads.
+void adamw_flat(float* p, float* m, float* v, const bf16* g, bf16* p_out, int64_t n, float lr,
+                float beta1, float beta2, float eps, float wd, float bc1, float bc2,
+                const float* clip, cudaStream_t s);
+// sumsq (+=) of a bf16 vector into *out (fp32, caller zeroes).
+void sumsq_bf16(const bf16* g, int64_t n, float* out, cudaStream_t s);
+// clip = min(1, max_norm / (sqrt(sumsq) + 1e-6)); norm = sqrt(sumsq).
+void clip_coef(const float* sumsq, float max_norm, float* clip, float* norm, cudaStream_t s);
+
+}  // namespace cfb

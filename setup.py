@@ -1,0 +1,44 @@
+"""Build the sm_100a CUDA extension of complexity_framework_b200 in place.
+
+    python setup.py build_ext --inplace
+
+Only Blackwell (sm_100a) code is generated; there is no other target.
+"""
+import os
+from setuptools import setup, find_packages
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join("complexity_framework_b200", "csrc")
+
+SOURCES = [
+    "bindings.cpp",
+    "bind_elementwise.cpp",
+    "gemm_tc.cu",
+    "elementwise.cu",
+]
+
+NVCC_FLAGS = [
+    "-O3",
+    "-std=c++17",
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-lineinfo",
+    "--expt-relaxed-constexpr",
+    "-DNDEBUG",
+]
+
+ext = CUDAExtension(
+    name="complexity_framework_b200._C",
+    sources=[os.path.join(CSRC, s) for s in SOURCES],
+    include_dirs=[os.path.join(HERE, CSRC)],
+    extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+    libraries=["cuda"],
+)
+
+setup(
+    name="complexity_framework_b200",
+    version="0.1.0",
+    packages=find_packages(include=["complexity_framework_b200*"]),
+    ext_modules=[ext],
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+)
