@@ -1,0 +1,30 @@
+"""Causal GQA/MHA attention entry point for the fused path.
+
+``attention(q, k, v)`` takes head-major ``q [B, Hq, S, D]``, ``k/v [B, Hkv, S, D]``
+(no K/V head replication) and returns ``[B, S, Hq*D]`` token-major output ready
+for the o_proj GEMM.  It dispatches to the sm_100a flash-attention kernel when
+the extension provides it, else to PyTorch SDPA with grouped K/V.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from ._ext import load
+
+
+def _kernel_available() -> bool:
+    C = load()
+    return C is not None and hasattr(C, "flash_attn_fwd")
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: bool = True,
+              scale: float) -> torch.Tensor:
+    B, Hq, S, D = q.shape
+    if _kernel_available():
+        from .flash import flash_attention
+
+        return flash_attention(q, k, v, causal=causal, scale=scale)
+    o = F.scaled_dot_product_attention(q, k, v, is_causal=causal, scale=scale,
+                                       enable_gqa=k.shape[1] != Hq)
+    return o.transpose(1, 2).reshape(B, S, Hq * D)

@@ -1,0 +1,356 @@
+"""Autograd operators over the sm_100a kernels.
+
+Every operator here runs only on CUDA bf16 tensors and calls the compiled
+extension; callers choose between these and the eager reference math (CPU,
+fp32, or ``use_custom_kernels=False``).  GEMM conventions are those of
+``gemm_tc.cu``: ``C[M,N] = sum_k A(m,k) B(n,k)`` with each operand either
+K-major or MN-major, so the data and weight gradients of ``y = x W^T`` need no
+transposed copies:
+
+    forward  y  = x  @ W^T   : A = x  (K-major)  B = W  (K-major)
+    dgrad    dx = dy @ W     : A = dy (K-major)  B = W  (MN-major)
+    wgrad    dW = dy^T @ x   : A = dy (MN-major) B = x  (MN-major)
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from ._ext import require
+
+EPI_STORE, EPI_RESID, EPI_SWIGLU_FWD, EPI_SWIGLU_BWD, EPI_F32, EPI_F32_ACC, EPI_CE_STATS = range(7)
+
+
+def _c(t: torch.Tensor) -> torch.Tensor:
+    return t if t.is_contiguous() else t.contiguous()
+
+
+# --------------------------------------------------------------------- GEMMs
+def gemm_nt(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None,
+            alpha: float = 1.0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``alpha * x @ w.T (+ residual)`` for 2-D bf16 ``x [M,K]``, ``w [N,K]``."""
+    C = require()
+    M, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty(M, N, device=x.device, dtype=torch.bfloat16)
+    if residual is not None:
+        C.gemm(x, False, w, False, M, N, K, EPI_RESID, out=out, residual=_c(residual), alpha=alpha)
+    else:
+        C.gemm(x, False, w, False, M, N, K, EPI_STORE, out=out, alpha=alpha)
+    return out
+
+
+def gemm_nn(dy: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """``dy @ w`` for ``dy [M,N]``, ``w [N,K]`` (data gradient of a linear layer)."""
+    C = require()
+    M, N = dy.shape
+    K = w.shape[1]
+    out = torch.empty(M, K, device=dy.device, dtype=torch.bfloat16)
+    C.gemm(dy, False, w, True, M, K, N, EPI_STORE, out=out)
+    return out
+
+
+def gemm_tn(dy: torch.Tensor, x: torch.Tensor, out_dtype=torch.bfloat16,
+            accumulate_into: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``dy.T @ x`` for ``dy [T,N]``, ``x [T,K]`` (weight gradient of a linear layer)."""
+    C = require()
+    T, N = dy.shape
+    K = x.shape[1]
+    if accumulate_into is not None:
+        C.gemm(dy, True, x, True, N, K, T, EPI_F32_ACC, out=accumulate_into)
+        return accumulate_into
+    if out_dtype == torch.float32:
+        out = torch.empty(N, K, device=dy.device, dtype=torch.float32)
+        C.gemm(dy, True, x, True, N, K, T, EPI_F32, out=out)
+    else:
+        out = torch.empty(N, K, device=dy.device, dtype=torch.bfloat16)
+        C.gemm(dy, True, x, True, N, K, T, EPI_STORE, out=out)
+    return out
+
+
+class LinearFn(torch.autograd.Function):
+    """``y = x @ W^T (+ residual)`` on the tcgen05 GEMM."""
+
+    @staticmethod
+    def forward(ctx, x, w, residual):
+        shape = x.shape
+        x2 = _c(x.reshape(-1, shape[-1]))
+        r2 = None if residual is None else residual.reshape(-1, w.shape[0])
+        y = gemm_nt(x2, _c(w), r2)
+        ctx.save_for_backward(x2, w)
+        ctx.has_res = residual is not None
+        ctx.shape = shape
+        return y.view(*shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w = ctx.saved_tensors
+        dy2 = _c(dy.reshape(-1, w.shape[0]))
+        dx = gemm_nn(dy2, _c(w)).view(ctx.shape) if ctx.needs_input_grad[0] else None
+        dw = gemm_tn(dy2, x2) if ctx.needs_input_grad[1] else None
+        dr = dy if ctx.has_res else None
+        return dx, dw, dr
+
+
+def linear(x, w, residual=None):
+    return LinearFn.apply(x, w, residual)
+
+
+# ------------------------------------------------------------ TR-Hash MLP
+def pack_gate_up(shared_gate: Optional[torch.Tensor], shared_up: Optional[torch.Tensor],
+                 expert_gate: torch.Tensor, expert_up: torch.Tensor, block: int = 128):
+    """Interleave gate and up rows in blocks of ``block`` for the SwiGLU epilogue.
+
+    Row order of the result: gate[0:128], up[0:128], gate[128:256], up[128:256] ...
+    where gate = [shared_gate ; expert_gate as (E*W, H)] and likewise up.
+    """
+    E, H, W = expert_gate.shape
+    g_parts = [expert_gate.permute(0, 2, 1).reshape(E * W, H)]
+    u_parts = [expert_up.permute(0, 2, 1).reshape(E * W, H)]
+    if shared_gate is not None:
+        g_parts.insert(0, shared_gate)
+        u_parts.insert(0, shared_up)
+    g = torch.cat(g_parts, 0) if len(g_parts) > 1 else g_parts[0]
+    u = torch.cat(u_parts, 0) if len(u_parts) > 1 else u_parts[0]
+    A = g.shape[0]
+    nb = A // block
+    return torch.stack((g.view(nb, block, H), u.view(nb, block, H)), 1).reshape(2 * A, H)
+
+
+def pack_down(shared_down: Optional[torch.Tensor], expert_down: torch.Tensor) -> torch.Tensor:
+    """``[H, shared + E*W]`` down weight: shared columns then expert e's W columns."""
+    E, W, H = expert_down.shape
+    ed = expert_down.permute(2, 0, 1).reshape(H, E * W)
+    return torch.cat((shared_down, ed), 1) if shared_down is not None else _c(ed)
+
+
+class TRHashMLPFn(torch.autograd.Function):
+    """Shared SwiGLU + deterministic routed experts (+ residual) as two GEMMs.
+
+    act[:, c] = silu(g_c) * u_c * s(row, c), where s = shared_scale for shared
+    columns and routed_scale * sum_j w_j [route_j(token) == expert(c)] for
+    expert columns (zero when the token is not routed to that expert), then
+    out = act @ Wd^T (+ residual).  Mathematically identical to
+    reference_topk_swiglu (complexity/tr_hash/engine.py:66-104) with the shared
+    branch of engine._shared (:333-349).
+    """
+
+    @staticmethod
+    def forward(ctx, h, w_gu, w_down, row_scale, residual, shared_width, expert_width,
+                n_experts, shared_scale):
+        C = require()
+        shape = h.shape
+        h2 = _c(h.reshape(-1, shape[-1]))
+        T, H = h2.shape
+        A2 = w_gu.shape[0]
+        A = A2 // 2
+        w_gu = _c(w_gu)
+        w_down = _c(w_down)
+        gu = torch.empty(T, A2, device=h.device, dtype=torch.bfloat16)
+        act = torch.empty(T, A, device=h.device, dtype=torch.bfloat16)
+        C.gemm(h2, False, w_gu, False, T, A2, H, EPI_SWIGLU_FWD, gu=gu, act=act,
+               row_scale=row_scale, shared_width=shared_width, expert_width=expert_width,
+               n_experts=n_experts, shared_scale=shared_scale)
+        Hout = w_down.shape[0]
+        r2 = None if residual is None else residual.reshape(-1, Hout)
+        out = gemm_nt(act, w_down, r2)
+        ctx.save_for_backward(h2, w_gu, w_down, row_scale, gu, act)
+        ctx.meta = (shared_width, expert_width, n_experts, shared_scale)
+        ctx.has_res = residual is not None
+        ctx.shape = shape
+        return out.view(*shape[:-1], Hout)
+
+    @staticmethod
+    def backward(ctx, dout):
+        C = require()
+        h2, w_gu, w_down, row_scale, gu, act = ctx.saved_tensors
+        sw, ew, ne, ss = ctx.meta
+        T, H = h2.shape
+        Hout, A = w_down.shape
+        d2 = _c(dout.reshape(-1, Hout))
+        dw_down = gemm_tn(d2, act)
+        dgu = torch.empty(T, 2 * A, device=d2.device, dtype=torch.bfloat16)
+        C.gemm(d2, False, w_down, True, T, A, Hout, EPI_SWIGLU_BWD, out=dgu, gu=gu,
+               row_scale=row_scale, shared_width=sw, expert_width=ew, n_experts=ne,
+               shared_scale=ss)
+        dh = gemm_nn(dgu, w_gu).view(ctx.shape)
+        dw_gu = gemm_tn(dgu, h2)
+        dr = dout if ctx.has_res else None
+        return dh, dw_gu, dw_down, None, dr, None, None, None, None
+
+
+def trhash_mlp(h, w_gu, w_down, row_scale, residual, shared_width, expert_width, n_experts,
+               shared_scale):
+    return TRHashMLPFn.apply(h, w_gu, w_down, row_scale, residual, shared_width, expert_width,
+                             n_experts, shared_scale)
+
+
+def route_scales(token_ids: torch.Tensor, route_table: torch.Tensor, route_weights: torch.Tensor,
+                 num_experts: int, routed_scale: float) -> torch.Tensor:
+    C = require()
+    ids = _c(token_ids.reshape(-1).long())
+    out = torch.empty(ids.numel(), num_experts, device=ids.device, dtype=torch.float32)
+    C.route_scales(ids, _c(route_table.long()), _c(route_weights.float()), out, num_experts,
+                   float(routed_scale))
+    return out
+
+
+# ------------------------------------------------------------------ RMSNorm
+class RMSNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        C = require()
+        xc = _c(x)
+        y = torch.empty_like(xc)
+        H = x.shape[-1]
+        rstd = torch.empty(xc.numel() // H, device=x.device, dtype=torch.float32)
+        C.rmsnorm_fwd(xc, _c(w), y, rstd, float(eps))
+        ctx.save_for_backward(xc, w, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        C = require()
+        x, w, rstd = ctx.saved_tensors
+        dx = torch.empty_like(x)
+        dw = torch.zeros(w.numel(), device=x.device, dtype=torch.float32)
+        C.rmsnorm_bwd(_c(dy), x, _c(w), rstd, None, dx, dw)
+        return dx, dw.to(w.dtype), None
+
+
+def rmsnorm(x, w, eps):
+    return RMSNormFn.apply(x, w, eps)
+
+
+# ---------------------------------------------------------- QK-norm + RoPE
+class QKNormRopeFn(torch.autograd.Function):
+    """kqv [B,S,(2Hkv+Hq)D] -> head-major q [B,Hq,S,D], k/v [B,Hkv,S,D]."""
+
+    @staticmethod
+    def forward(ctx, kqv, qw, kw, cos, sin, pos, Hq, Hkv, D, eps, qk_norm):
+        C = require()
+        B, S = kqv.shape[0], kqv.shape[1]
+        kqv = _c(kqv)
+        dev = kqv.device
+        q = torch.empty(B, Hq, S, D, device=dev, dtype=torch.bfloat16)
+        k = torch.empty(B, Hkv, S, D, device=dev, dtype=torch.bfloat16)
+        v = torch.empty(B, Hkv, S, D, device=dev, dtype=torch.bfloat16)
+        rstd = torch.empty(B * S, Hq + Hkv, device=dev, dtype=torch.float32)
+        C.qk_norm_rope_fwd(kqv, _c(qw), _c(kw), cos, sin, pos, q, k, v, rstd, B, S, Hq, Hkv, D,
+                           float(eps), bool(qk_norm))
+        ctx.save_for_backward(kqv, qw, kw, cos, sin, rstd, pos)
+        ctx.meta = (B, S, Hq, Hkv, D, bool(qk_norm))
+        return q, k, v
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        C = require()
+        kqv, qw, kw, cos, sin, rstd, pos = ctx.saved_tensors
+        B, S, Hq, Hkv, D, qk_norm = ctx.meta
+        dev = kqv.device
+        dkqv = torch.empty_like(kqv)
+        dqw = torch.zeros(D, device=dev, dtype=torch.float32)
+        dkw = torch.zeros(D, device=dev, dtype=torch.float32)
+
+        def z(shape):
+            return torch.zeros(shape, device=dev, dtype=torch.bfloat16)
+
+        dq = _c(dq) if dq is not None else z((B, Hq, S, D))
+        dk = _c(dk) if dk is not None else z((B, Hkv, S, D))
+        dv = _c(dv) if dv is not None else z((B, Hkv, S, D))
+        C.qk_norm_rope_bwd(dq, dk, dv, kqv, _c(qw), _c(kw), cos, sin, pos, rstd, dkqv, dqw, dkw,
+                           B, S, Hq, Hkv, D, qk_norm)
+        n = None
+        return (dkqv, dqw.to(qw.dtype), dkw.to(kw.dtype), n, n, n, n, n, n, n, n)
+
+
+def qk_norm_rope(kqv, qw, kw, cos, sin, pos, Hq, Hkv, D, eps, qk_norm=True):
+    return QKNormRopeFn.apply(kqv, qw, kw, cos, sin, pos, Hq, Hkv, D, eps, qk_norm)
+
+
+# ---------------------------------------------------------------- embedding
+class EmbeddingFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, ids, table):
+        C = require()
+        ids_c = _c(ids.long())
+        out = torch.empty(*ids.shape, table.shape[1], device=table.device, dtype=table.dtype)
+        C.embedding_fwd(ids_c, _c(table), out)
+        ctx.save_for_backward(ids_c)
+        ctx.vshape = table.shape
+        ctx.dtype = table.dtype
+        return out
+
+    @staticmethod
+    def backward(ctx, dy):
+        C = require()
+        (ids,) = ctx.saved_tensors
+        dtable = torch.zeros(ctx.vshape, device=dy.device, dtype=torch.float32)
+        C.embedding_bwd(ids, _c(dy), dtable)
+        return None, dtable.to(ctx.dtype)
+
+
+def embedding(ids, table):
+    return EmbeddingFn.apply(ids, table)
+
+
+# -------------------------------------------------- fused linear cross-entropy
+class LinearCrossEntropyFn(torch.autograd.Function):
+    """Mean next-token CE of ``hidden @ weight.T`` without a persistent logits tensor.
+
+    Rows are processed in chunks: one tcgen05 GEMM writes the bf16 logits of a
+    chunk and per-(row, 256-column tile) max/sum-exp partials; one kernel turns
+    them into the row loss and overwrites the logits with d(loss)/d(logits);
+    two GEMMs then produce d(hidden) for the chunk and accumulate d(weight) in
+    fp32.  Gradients are computed in forward (the loss is the last op of the
+    graph) and scaled by the incoming gradient in backward.  Reference
+    counterpart: Liger's fused linear cross-entropy used by
+    complexity/core/losses/fused_ce.py:138-161.
+    """
+
+    @staticmethod
+    def forward(ctx, hidden, weight, targets, ignore_index, chunk_rows):
+        C = require()
+        H = hidden.shape[-1]
+        h = _c(hidden.reshape(-1, H))
+        t = _c(targets.reshape(-1).long())
+        w = _c(weight)
+        T, V = h.shape[0], w.shape[0]
+        valid = (t != ignore_index).sum().clamp_min(1).float()
+        scale = (1.0 / valid).reshape(1)
+        dh = torch.empty_like(h)
+        dw = torch.zeros(V, H, device=h.device, dtype=torch.float32)
+        losses = torch.empty(T, device=h.device, dtype=torch.float32)
+        bn = 256
+        nt = (V + bn - 1) // bn
+        chunk = max(128, min(T, int(chunk_rows)))
+        logits = torch.empty(chunk, V, device=h.device, dtype=torch.bfloat16)
+        stats = torch.empty(chunk, nt, 2, device=h.device, dtype=torch.float32)
+        for r0 in range(0, T, chunk):
+            r1 = min(T, r0 + chunk)
+            n = r1 - r0
+            hc = h[r0:r1]
+            lg = logits[:n]
+            C.gemm(hc, False, w, False, n, V, H, EPI_CE_STATS, out=lg, stats=stats, bn=bn)
+            C.ce_loss_grad(lg, stats, nt, t[r0:r1], losses[r0:r1], scale, ignore_index)
+            C.gemm(lg, False, w, True, n, H, V, EPI_STORE, out=dh[r0:r1])
+            C.gemm(lg, True, hc, True, V, H, n, EPI_F32_ACC, out=dw)
+        loss = losses.sum() * scale[0]
+        ctx.save_for_backward(dh, dw)
+        ctx.hshape = hidden.shape
+        ctx.wdtype = weight.dtype
+        return loss
+
+    @staticmethod
+    def backward(ctx, gout):
+        dh, dw = ctx.saved_tensors
+        dhidden = (dh * gout.to(dh.dtype)).view(ctx.hshape)
+        dweight = (dw * gout.float()).to(ctx.wdtype)
+        return dhidden, dweight, None, None, None
+
+
+def linear_cross_entropy(hidden, weight, targets, ignore_index: int = -100,
+                         chunk_rows: int = 65536):
+    return LinearCrossEntropyFn.apply(hidden, weight, targets, ignore_index, chunk_rows)

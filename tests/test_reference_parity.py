@@ -1,0 +1,88 @@
+"""CPU parity with the reference framework on identical weights.
+
+The reference package is imported from its offline install (baseline/_ref);
+the test is skipped when that install is absent.
+"""
+import os
+import sys
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF = os.path.join(ROOT, "baseline", "_ref")
+
+
+@pytest.fixture(scope="module")
+def ref():
+    if not os.path.isdir(os.path.join(REF, "complexity")):
+        pytest.skip("reference install not present")
+    sys.path.insert(0, REF)
+    try:
+        import complexity
+    except Exception as exc:  # pragma: no cover
+        pytest.skip(f"reference import failed: {exc}")
+    finally:
+        sys.path.remove(REF)
+    return complexity
+
+
+TINY = dict(hidden_size=128, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+            vocab_size=1024, intermediate_size=128, shared_intermediate_size=384,
+            num_experts=4, top_k=2, max_position_embeddings=128)
+
+
+@pytest.mark.parametrize("strategy", ["modulo_cyclic", "token_id_multi_hash",
+                                      "token_id_balanced_hash", "token_id_hierarchical_hash"])
+def test_state_dict_and_logits_match(ref, strategy):
+    from complexity_framework_b200 import ComplexityModel, ModelConfig
+
+    kw = dict(TINY, routing_strategy=strategy)
+    torch.manual_seed(0)
+    rm = ref.ComplexityModel(ref.ModelConfig(**kw))
+    mm = ComplexityModel(ModelConfig(**kw))
+    rsd, msd = rm.state_dict(), mm.state_dict()
+    assert set(rsd) == set(msd)
+    for k in rsd:
+        assert rsd[k].shape == msd[k].shape and rsd[k].dtype == msd[k].dtype, k
+        if "route" in k or "pairs" in k:
+            assert torch.equal(rsd[k], msd[k]), k
+    mm.load_state_dict(rsd)
+    ids = torch.randint(0, 1024, (2, 64), generator=torch.Generator().manual_seed(0))
+    a = rm(ids)["logits"]
+    b = mm(ids)["logits"]
+    assert torch.allclose(a, b, atol=1e-5, rtol=1e-5)
+
+
+def test_route_tables_match_engine_strategies(ref):
+    from complexity_framework_b200.tr_hash import TRHashEngineConfig, build_route_table
+
+    for strategy in ("modulo_cyclic", "token_id_balanced_hash", "token_id_affine_hash",
+                     "token_id_multi_hash", "token_id_hierarchical_hash"):
+        for E, k in ((4, 2), (8, 2), (16, 4), (8, 1)):
+            for layer in (0, 3):
+                kw = dict(hidden_size=64, vocab_size=5000, num_experts=E, top_k=k,
+                          routing_strategy=strategy, layer_index=layer, route_hash_count=3)
+                try:
+                    r = ref.tr_hash.build_route_table(ref.tr_hash.TRHashEngineConfig(**kw))
+                except (ValueError, RuntimeError):
+                    with pytest.raises((ValueError, RuntimeError)):
+                        build_route_table(TRHashEngineConfig(**kw))
+                    continue
+                assert torch.equal(r, build_route_table(TRHashEngineConfig(**kw))), (strategy, E, k)
+
+
+def test_tuple_cache_decode_matches_reference(ref):
+    from complexity_framework_b200 import ComplexityModel, ModelConfig
+
+    torch.manual_seed(1)
+    rm = ref.ComplexityModel(ref.ModelConfig(**TINY))
+    mm = ComplexityModel(ModelConfig(**TINY))
+    mm.load_state_dict(rm.state_dict())
+    ids = torch.randint(0, 1024, (2, 16), generator=torch.Generator().manual_seed(2))
+    r = rm(ids, use_cache=True)
+    m = mm(ids, use_cache=True)
+    nxt = ids[:, -1:]
+    r2 = rm(nxt, past_key_values=r["past_key_values"], use_cache=True)["logits"]
+    m2 = mm(nxt, past_key_values=m["past_key_values"], use_cache=True)["logits"]
+    assert torch.allclose(r2, m2, atol=1e-5, rtol=1e-5)
