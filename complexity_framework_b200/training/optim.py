@@ -1,0 +1,288 @@
+"""Flat-buffer AdamW with fp32 master weights.
+
+Each param group is laid out in one contiguous buffer: the model parameters
+become views into a flat compute buffer (bf16 on GPU), their ``.grad`` views
+into a flat gradient buffer, and the optimizer keeps flat fp32 master weights
+and moments.  A step is one sm_100a kernel launch per group (plus two tiny
+launches for the gradient norm when clipping), never a per-parameter loop, and
+needs no host synchronisation: the clip coefficient stays on the device.
+
+Semantics are those of ``torch.optim.AdamW`` (decoupled weight decay applied
+as ``p *= 1 - lr*wd``, bias-corrected moments, ``eps`` added to
+``sqrt(v_hat)``), which the reference trainer uses with betas (0.9, 0.95)
+(complexity/training/trainer.py:196-334).  Unlike the reference FSDP path
+(parallel/data_parallel.py:105-108) the master weights and moments are fp32.
+
+Sharded mode (``shard_state=True`` with a process group of W > 1 ranks) is
+ZeRO-2: gradients are reduce-scattered into a per-rank shard, each rank
+updates the fp32 master/moments of its shard only, and the bf16 compute
+buffer is all-gathered.
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, List, Optional
+
+import torch
+
+
+def default_param_groups(model: torch.nn.Module, weight_decay: float) -> List[dict]:
+    """Decay / no-decay split by name, as the reference trainer does."""
+    decay, no_decay = [], []
+    for name, p in model.named_parameters():
+        if not p.requires_grad:
+            continue
+        if "bias" in name or "norm" in name or ".mu" in name:
+            no_decay.append(p)
+        else:
+            decay.append(p)
+    groups = [{"params": decay, "weight_decay": weight_decay}]
+    if no_decay:
+        groups.append({"params": no_decay, "weight_decay": 0.0})
+    return groups
+
+
+class _FlatGroup:
+    """Flat storage of one parameter group (optionally with sharded optimizer state)."""
+
+    def __init__(self, params: List[torch.nn.Parameter], compute_dtype: torch.dtype,
+                 pad_to: int = 128, world: int = 1, rank: int = 0):
+        self.params = params
+        dev = params[0].device
+        self.sizes = [p.numel() for p in params]
+        self.offsets = []
+        off = 0
+        for n in self.sizes:
+            self.offsets.append(off)
+            off += (n + pad_to - 1) // pad_to * pad_to  # 256-byte aligned starts
+        unit = pad_to * world
+        off = (off + unit - 1) // unit * unit
+        self.numel = off
+        self.world, self.rank = world, rank
+        self.shard = off // world
+        self.lo = rank * self.shard
+        self.compute = torch.zeros(off, device=dev, dtype=compute_dtype)
+        self.grad = torch.zeros(off, device=dev, dtype=compute_dtype)
+        with torch.no_grad():
+            for p, o, n in zip(params, self.offsets, self.sizes):
+                self.compute[o:o + n].copy_(p.detach().reshape(-1))
+            masters = torch.zeros(off, device=dev, dtype=torch.float32)
+            for p, o, n in zip(params, self.offsets, self.sizes):
+                masters[o:o + n].copy_(p.detach().reshape(-1).float())
+        self.master = masters[self.lo:self.lo + self.shard].clone()
+        del masters
+        self.exp_avg = torch.zeros(self.shard, device=dev, dtype=torch.float32)
+        self.exp_avg_sq = torch.zeros(self.shard, device=dev, dtype=torch.float32)
+        self.grad_shard = (self.grad[self.lo:self.lo + self.shard] if world == 1 else
+                           torch.zeros(self.shard, device=dev, dtype=compute_dtype))
+        self.rebind()
+
+    @property
+    def compute_shard(self) -> torch.Tensor:
+        return self.compute[self.lo:self.lo + self.shard]
+
+    def rebind(self) -> None:
+        """Point every parameter's data and grad at its slice of the flat buffers."""
+        for p, o, n in zip(self.params, self.offsets, self.sizes):
+            p.data = self.compute[o:o + n].view(p.shape)
+            p.grad = self.grad[o:o + n].view(p.shape)
+
+    def view(self, flat: torch.Tensor, i: int) -> Optional[torch.Tensor]:
+        """View of parameter i inside a full-length flat buffer, or inside a
+        shard-length buffer when the parameter lies entirely in this shard."""
+        o, n = self.offsets[i], self.sizes[i]
+        if flat.numel() == self.numel:
+            return flat[o:o + n].view(self.params[i].shape)
+        if o >= self.lo and o + n <= self.lo + self.shard:
+            return flat[o - self.lo:o - self.lo + n].view(self.params[i].shape)
+        return None
+
+
+class FusedAdamW(torch.optim.Optimizer):
+    def __init__(self, params, lr: float = 3e-4, betas=(0.9, 0.95), eps: float = 1e-8,
+                 weight_decay: float = 0.1, compute_dtype: Optional[torch.dtype] = None,
+                 process_group=None, shard_state: bool = False):
+        defaults = dict(lr=lr, betas=tuple(betas), eps=eps, weight_decay=weight_decay)
+        super().__init__(params, defaults)
+        import torch.distributed as dist
+
+        self.process_group = process_group
+        self.world, self.rank = 1, 0
+        if dist.is_available() and dist.is_initialized():
+            self.world = dist.get_world_size(process_group)
+            self.rank = dist.get_rank(process_group)
+        self.sharded = bool(shard_state) and self.world > 1
+        self._flat: List[Optional[_FlatGroup]] = []
+        self._step_count = 0
+        for group in self.param_groups:
+            ps = [p for p in group["params"] if p.requires_grad]
+            if not ps:
+                self._flat.append(None)
+                continue
+            fg = _FlatGroup(ps, compute_dtype or ps[0].dtype,
+                            world=self.world if self.sharded else 1,
+                            rank=self.rank if self.sharded else 0)
+            self._flat.append(fg)
+            for i, p in enumerate(ps):
+                st = {"step": torch.zeros((), dtype=torch.float32)}
+                for key, buf in (("exp_avg", fg.exp_avg), ("exp_avg_sq", fg.exp_avg_sq),
+                                 ("master", fg.master)):
+                    v = fg.view(buf, i)
+                    if v is not None:
+                        st[key] = v
+                self.state[p] = st
+        dev = next((fg.master.device for fg in self._flat if fg is not None), torch.device("cpu"))
+        self._sumsq = torch.zeros(1, device=dev, dtype=torch.float32)
+        self._clip = torch.ones(1, device=dev, dtype=torch.float32)
+        self._norm = torch.zeros(1, device=dev, dtype=torch.float32)
+
+    # ----------------------------------------------------------- flat access
+    @property
+    def flat_groups(self) -> List[_FlatGroup]:
+        return [fg for fg in self._flat if fg is not None]
+
+    def group_flat_grads(self) -> List[torch.Tensor]:
+        return [fg.grad for fg in self.flat_groups]
+
+    def zero_grad(self, set_to_none: bool = False) -> None:
+        for fg in self.flat_groups:
+            fg.grad.zero_()
+            if any(p.grad is None for p in fg.params):
+                fg.rebind()
+
+    @torch.no_grad()
+    def reduce_gradients(self) -> None:
+        """Average gradients over the data-parallel group (one collective per group)."""
+        if self.world == 1:
+            return
+        import torch.distributed as dist
+
+        avg = dist.get_backend(self.process_group) == "nccl"
+        op = dist.ReduceOp.AVG if avg else dist.ReduceOp.SUM
+        for fg in self.flat_groups:
+            if self.sharded:
+                dist.reduce_scatter_tensor(fg.grad_shard, fg.grad, op=op, group=self.process_group)
+                out = fg.grad_shard
+            else:
+                dist.all_reduce(fg.grad, op=op, group=self.process_group)
+                out = fg.grad
+            if not avg:
+                out.div_(self.world)
+
+    def _use_kernels(self) -> bool:
+        fg = self.flat_groups[0] if self.flat_groups else None
+        if fg is None or not fg.master.is_cuda or fg.compute.dtype != torch.bfloat16:
+            return False
+        from ..ops import available
+
+        return available()
+
+    # ------------------------------------------------------------- clipping
+    def _allreduce_sumsq(self) -> None:
+        if self.sharded:
+            import torch.distributed as dist
+
+            dist.all_reduce(self._sumsq, op=dist.ReduceOp.SUM, group=self.process_group)
+
+    @torch.no_grad()
+    def clip_grad_norm_(self, max_norm: float) -> torch.Tensor:
+        """Compute the global grad norm on the device; the next ``step(clip=True)``
+        scales by ``min(1, max_norm / (norm + 1e-6))``.  Returns the norm (no sync)."""
+        if self._use_kernels():
+            from ..ops import require
+
+            C = require()
+            self._sumsq.zero_()
+            for fg in self.flat_groups:
+                C.sumsq_bf16(fg.grad_shard, self._sumsq)
+            self._allreduce_sumsq()
+            C.clip_coef(self._sumsq, float(max_norm), self._clip, self._norm)
+        else:
+            sq = sum((fg.grad_shard.float() ** 2).sum() for fg in self.flat_groups)
+            self._sumsq.copy_(torch.as_tensor(sq, dtype=torch.float32).reshape(1))
+            self._allreduce_sumsq()
+            self._norm.copy_(torch.sqrt(self._sumsq))
+            if max_norm > 0:
+                self._clip.copy_(torch.clamp(max_norm / (self._norm + 1e-6), max=1.0))
+            else:
+                self._clip.fill_(1.0)
+        return self._norm[0]
+
+    # ----------------------------------------------------------------- step
+    @torch.no_grad()
+    def step(self, closure=None, clip: bool = False):
+        loss = closure() if closure is not None else None
+        self._step_count += 1
+        t = self._step_count
+        kernels = self._use_kernels()
+        if kernels:
+            from ..ops import require
+
+            C = require()
+        for group, fg in zip(self.param_groups, self._flat):
+            if fg is None:
+                continue
+            b1, b2 = group["betas"]
+            bc1 = 1.0 - b1 ** t
+            bc2 = 1.0 - b2 ** t
+            lr, wd, eps = group["lr"], group["weight_decay"], group["eps"]
+            if kernels:
+                C.adamw_flat(fg.master, fg.exp_avg, fg.exp_avg_sq, fg.grad_shard, fg.compute_shard,
+                             lr, b1, b2, eps, wd, bc1, bc2, self._clip if clip else None)
+            else:
+                g = fg.grad_shard.float() * (self._clip if clip else 1.0)
+                fg.exp_avg.mul_(b1).add_(g, alpha=1 - b1)
+                fg.exp_avg_sq.mul_(b2).addcmul_(g, g, value=1 - b2)
+                fg.master.mul_(1 - lr * wd)
+                denom = (fg.exp_avg_sq.sqrt() / math.sqrt(bc2)).add_(eps)
+                fg.master.addcdiv_(fg.exp_avg, denom, value=-lr / bc1)
+                fg.compute_shard.copy_(fg.master)
+            if self.sharded:
+                import torch.distributed as dist
+
+                dist.all_gather_into_tensor(fg.compute, fg.compute_shard,
+                                            group=self.process_group)
+            for p in fg.params:
+                self.state[p]["step"].fill_(t)
+        return loss
+
+    # ------------------------------------------------------------ state dict
+    def state_dict(self) -> Dict:
+        sd = super().state_dict()
+        sd["flat_step"] = self._step_count
+        return sd
+
+    def load_state_dict(self, state_dict: Dict) -> None:
+        """Copy saved moments/master weights into the existing flat views."""
+        saved_groups = state_dict["param_groups"]
+        if len(saved_groups) != len(self.param_groups):
+            raise ValueError("optimizer state has a different number of param groups")
+        id_map = {}
+        for group, sg in zip(self.param_groups, saved_groups):
+            if len(group["params"]) != len(sg["params"]):
+                raise ValueError("optimizer param group sizes differ")
+            for p, sid in zip(group["params"], sg["params"]):
+                id_map[sid] = p
+            for k, v in sg.items():
+                if k != "params":
+                    group[k] = v
+        for sid, st in state_dict["state"].items():
+            p = id_map.get(sid)
+            if p is None:
+                continue
+            mine = self.state[p]
+            for key in ("exp_avg", "exp_avg_sq", "master"):
+                if key in st and key in mine:
+                    mine[key].copy_(st[key].to(mine[key].device, mine[key].dtype))
+            if "step" in st:
+                mine["step"].fill_(float(st["step"]))
+        self._step_count = int(state_dict.get("flat_step", self._step_count))
+        with torch.no_grad():
+            for fg in self.flat_groups:
+                fg.compute_shard.copy_(fg.master)
+                if self.sharded:
+                    import torch.distributed as dist
+
+                    dist.all_gather_into_tensor(fg.compute, fg.compute_shard,
+                                                group=self.process_group)
+                fg.rebind()

@@ -1,0 +1,211 @@
+"""Trainer: one process per GPU, flat fp32-master AdamW, fused loss.
+
+A training step is: H2D of the micro-batch (pinned, non-blocking) -> forward
+through the sm_100a kernels -> fused linear cross-entropy -> backward ->
+data-parallel gradient reduction over the flat gradient buffers (all-reduce
+for ``ddp``, reduce-scatter + sharded update + all-gather for ``fsdp``) ->
+device-side grad-norm clip -> one fused AdamW launch per parameter group.
+
+Public surface follows complexity/training/trainer.py:42-774 (``Trainer``,
+``train``, ``evaluate``, checkpoint save/resume, the canary parameter-update
+check after the first step) with a flat-buffer optimizer in place of
+per-parameter loops.
+"""
+from __future__ import annotations
+
+import logging
+import time
+from typing import Callable, Iterable, List, Optional
+
+import torch
+import torch.distributed as dist
+
+from ..utils.checkpointing import CheckpointManager
+from .config import TrainingConfig
+from .optim import FusedAdamW, default_param_groups
+from .scheduler import build_scheduler
+
+logger = logging.getLogger(__name__)
+
+
+class Trainer:
+    def __init__(self, model: torch.nn.Module, config: Optional[TrainingConfig] = None, *,
+                 device: Optional[torch.device] = None, process_group=None,
+                 callbacks: Optional[List] = None, compute_loss: Optional[Callable] = None):
+        self.config = config or TrainingConfig()
+        on = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(process_group) if on else 1
+        self.rank = dist.get_rank(process_group) if on else 0
+        self.is_main = self.rank == 0
+        if device is None:
+            device = (torch.device("cuda", torch.cuda.current_device())
+                      if torch.cuda.is_available() else torch.device("cpu"))
+        self.device = torch.device(device)
+        dtype = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[
+            self.config.precision]
+        if self.device.type == "cpu":
+            dtype = torch.float32
+        self.model = model.to(device=self.device, dtype=dtype)
+        mode = self.config.distributed_mode
+        if mode == "auto":
+            mode = ("fsdp" if self.config.use_fsdp else "ddp") if self.world > 1 else "none"
+        self.distributed_mode = mode
+        if self.world > 1:
+            self._broadcast_parameters(process_group)
+        groups = default_param_groups(self.model, self.config.weight_decay)
+        self.optimizer = FusedAdamW(groups, lr=self.config.learning_rate, betas=(0.9, 0.95),
+                                    weight_decay=self.config.weight_decay,
+                                    process_group=process_group, shard_state=(mode == "fsdp"))
+        self.scheduler = build_scheduler(self.optimizer, kind=self.config.lr_scheduler,
+                                         warmup_steps=self.config.warmup_steps,
+                                         total_steps=self.config.max_steps,
+                                         min_lr_ratio=self.config.min_lr_ratio,
+                                         wsd_decay_ratio=self.config.wsd_decay_ratio)
+        self.ckpt = CheckpointManager(self.config.checkpoint_dir, self.config.save_total_limit)
+        self.callbacks = list(callbacks or [])
+        self.global_step = 0
+        self.epoch = 0
+        self.total_tokens = 0
+        self.best_loss = float("inf")
+        self._compute_loss = compute_loss
+        self._canary = None
+
+    # ----------------------------------------------------------------- setup
+    @torch.no_grad()
+    def _broadcast_parameters(self, pg) -> None:
+        src = dist.get_global_rank(pg, 0) if pg is not None else 0
+        for p in self.model.parameters():
+            dist.broadcast(p.data, src=src, group=pg)
+        for b in self.model.buffers():
+            if b.is_floating_point():
+                dist.broadcast(b, src=src, group=pg)
+
+    # ------------------------------------------------------------------ step
+    def compute_loss(self, input_ids: torch.Tensor, labels: Optional[torch.Tensor] = None):
+        if self._compute_loss is not None:
+            return self._compute_loss(self.model, input_ids, labels)
+        return self.model.loss(input_ids, labels)
+
+    def train_step(self, input_ids: torch.Tensor, labels: Optional[torch.Tensor] = None, *,
+                   sync: bool = True):
+        """One optimizer step on one micro-batch.
+
+        ``input_ids`` may live on the host (pinned memory is copied
+        asynchronously).  Returns the loss as a Python float when ``sync``
+        (one device-to-host read), else the detached device scalar.
+        """
+        self.model.train()
+        ids = input_ids.to(self.device, non_blocking=True)
+        lab = labels.to(self.device, non_blocking=True) if labels is not None else None
+        loss = self.compute_loss(ids, lab)
+        loss.backward()
+        self._finish_step()
+        self.total_tokens += ids.numel() * self.world
+        return float(loss.detach()) if sync else loss.detach()
+
+    def accumulate_step(self, micro_batches: Iterable[torch.Tensor], *, sync: bool = True):
+        """Gradient accumulation over micro-batches, one optimizer step at the end."""
+        self.model.train()
+        batches = list(micro_batches)
+        total = None
+        n = 0
+        for mb in batches:
+            ids = mb.to(self.device, non_blocking=True)
+            loss = self.compute_loss(ids) / len(batches)
+            loss.backward()
+            total = loss.detach() if total is None else total + loss.detach()
+            n += ids.numel()
+        self._finish_step()
+        self.total_tokens += n * self.world
+        return float(total) if sync else total
+
+    def _finish_step(self) -> None:
+        opt = self.optimizer
+        check = (self.global_step == 0 and not self.config.skip_param_update_check)
+        if check:
+            self._canary = self._snapshot()
+        opt.reduce_gradients()
+        clip = self.config.grad_clip > 0
+        if clip:
+            opt.clip_grad_norm_(self.config.grad_clip)
+        opt.step(clip=clip)
+        self.scheduler.step()
+        opt.zero_grad()
+        self.global_step += 1
+        if check:
+            self._verify_canary()
+
+    # ------------------------------------------------- canary update check
+    def _snapshot(self):
+        ps = [p for p in self.model.parameters() if p.requires_grad]
+        picks = [ps[0], ps[len(ps) // 2], ps[-1]]
+        return [(p, p.detach().reshape(-1)[:64].clone()) for p in picks]
+
+    def _verify_canary(self) -> None:
+        """After the first step at least one sampled parameter must have moved."""
+        moved = any(not torch.equal(p.detach().reshape(-1)[:64], before)
+                    for p, before in self._canary)
+        self._canary = None
+        if self.is_main:
+            logger.info("canary param-update check: %s", "ok" if moved else "NO UPDATE")
+        if not moved:
+            raise RuntimeError("parameters did not change after the first optimizer step")
+
+    # ------------------------------------------------------------------ loop
+    def train(self, batches: Iterable[torch.Tensor], max_steps: Optional[int] = None) -> dict:
+        """Run optimizer steps over an iterable of [B, S] token batches."""
+        max_steps = max_steps or self.config.max_steps
+        t0 = time.perf_counter()
+        last = None
+        try:
+            for batch in batches:
+                if self.global_step >= max_steps:
+                    break
+                sync = (self.global_step % self.config.log_steps == 0)
+                out = self.train_step(batch, sync=sync)
+                last_val = out if sync else None
+                if last_val is not None:
+                    last = last_val
+                    self.best_loss = min(self.best_loss, last_val)
+                for cb in self.callbacks:
+                    if hasattr(cb, "on_step_end"):
+                        cb.on_step_end(self, self.global_step, last_val)
+                if self.global_step % self.config.save_steps == 0:
+                    self.save_checkpoint()
+        except KeyboardInterrupt:
+            self.save_checkpoint(tag="interrupted")
+            raise
+        return {"steps": self.global_step, "tokens": self.total_tokens,
+                "seconds": time.perf_counter() - t0, "last_loss": last}
+
+    @torch.no_grad()
+    def evaluate(self, batches: Iterable[torch.Tensor]) -> float:
+        self.model.eval()
+        tot = torch.zeros(2, device=self.device, dtype=torch.float64)
+        for b in batches:
+            ids = b.to(self.device, non_blocking=True)
+            loss = self.compute_loss(ids)
+            tot[0] += loss.double() * ids.numel()
+            tot[1] += ids.numel()
+        if self.world > 1:
+            dist.all_reduce(tot)
+        self.model.train()
+        return float(tot[0] / tot[1].clamp_min(1))
+
+    # ----------------------------------------------------------- checkpoints
+    def save_checkpoint(self, tag: str = "step"):
+        return self.ckpt.save(self.model, self.optimizer, step=self.global_step,
+                              scheduler=self.scheduler, epoch=self.epoch,
+                              best_loss=self.best_loss, total_tokens=self.total_tokens, tag=tag)
+
+    def resume(self, path: Optional[str] = "auto") -> bool:
+        """Restore model/optimizer/scheduler/step from ``path`` or the newest checkpoint."""
+        target = self.ckpt.latest() if path in (None, "auto") else path
+        if target is None:
+            return False
+        state = self.ckpt.load(target, self.model, self.optimizer, self.scheduler)
+        self.global_step = int(state["step"])
+        self.epoch = int(state.get("epoch", 0))
+        self.best_loss = float(state.get("best_loss", float("inf")))
+        self.total_tokens = int(state.get("total_tokens", 0))
+        return True
