@@ -45,6 +45,7 @@ def parse():
     p.add_argument("--seq", type=int, default=2048)
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-count", action="store_true", help="skip the kernel-launch count step")
     return p.parse_args()
 
 
@@ -272,7 +273,7 @@ def main():
                        args.impl == "ours" else "reference model + fused_linear_causal_lm_loss")}
 
     launches = None
-    if args.impl == "ours":
+    if args.impl == "ours" and not args.no_count:
         ours, total = count_our_kernels(step, dev[0])
         launches = ours * args.steps
         launches_total = total * args.steps
@@ -291,7 +292,7 @@ def main():
                        "l2": "inputs/activations larger than L2 (no flush needed)"},
             "clocks": clk, "e2e": e2e,
         }
-        if args.impl == "ours":
+        if args.impl == "ours" and launches is not None:
             line["gpu_launches"] = launches
             line["gpu_launches_all"] = launches_total
         else:
