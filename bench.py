@@ -292,9 +292,10 @@ def main():
                        "l2": "inputs/activations larger than L2 (no flush needed)"},
             "clocks": clk, "e2e": e2e,
         }
-        if args.impl == "ours" and launches is not None:
-            line["gpu_launches"] = launches
-            line["gpu_launches_all"] = launches_total
+        if args.impl == "ours":
+            if launches is not None:
+                line["gpu_launches"] = launches
+                line["gpu_launches_all"] = launches_total
         else:
             line["impl"] = "reference"
         print(json.dumps(line))

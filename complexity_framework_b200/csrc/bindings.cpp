@@ -167,9 +167,9 @@ void gemm(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, 
     TORCH_CHECK(stats.has_value() && stats->scalar_type() == torch::kFloat32 &&
                     stats->is_contiguous(),
                 "ce stats epilogue needs contiguous fp32 stats");
-    const int use_bn = bn ? static_cast<int>(bn) : cfb::choose_bn(g.M, g.N, g.num_sms);
-    g.bn = use_bn;
-    TORCH_CHECK(stats->numel() >= M * ((N + use_bn - 1) / use_bn) * 2, "stats too small");
+    TORCH_CHECK(bn == 0 || bn == 256, "ce stats epilogue runs with 256-column tiles");
+    g.bn = 256;
+    TORCH_CHECK(stats->numel() >= M * 2 * ((N + 255) / 256) * 2, "stats too small");
     ep.stats = stats->data_ptr<float>();
   }
   const int rc = cfb::gemm_tc_launch(g, ep, at::cuda::getCurrentCUDAStream(),

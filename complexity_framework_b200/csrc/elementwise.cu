@@ -127,6 +127,77 @@ __global__ void rmsnorm_bwd_k(const bf16* __restrict__ dy, const bf16* __restric
   for (int i = threadIdx.x; i < H; i += blockDim.x) atomicAdd(&dw[i], sdw[i]);
 }
 
+// Register-accumulating variant for H <= NV*256: lane l owns vectors l, l+32, ...
+// so its d(weight) partials live in registers for the whole row loop.
+template <int NV>
+__global__ void rmsnorm_bwd_reg_k(const bf16* __restrict__ dy, const bf16* __restrict__ x,
+                                  const bf16* __restrict__ w, const float* __restrict__ rstd,
+                                  const bf16* __restrict__ dres, bf16* __restrict__ dx,
+                                  float* __restrict__ dw, int64_t T, int H) {
+  extern __shared__ float sdw[];
+  for (int i = threadIdx.x; i < H; i += blockDim.x) sdw[i] = 0.f;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int nv = H >> 3;
+  float acc[NV][8];
+  float wv[NV][8];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = lane + 32 * k;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[k][j] = 0.f;
+    if (i < nv) load8(w + i * 8, wv[k]);
+  }
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < T;
+       row += warps) {
+    const float r = rstd[row];
+    float xv[NV][8], gv[NV][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int i = lane + 32 * k;
+      if (i < nv) {
+        load8(x + row * H + i * 8, xv[k]);
+        load8(dy + row * H + i * 8, gv[k]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          dot += gv[k][j] * wv[k][j] * xv[k][j];
+          acc[k][j] += gv[k][j] * rb(xv[k][j] * r);
+        }
+      }
+    }
+    dot = warp_sum(dot);
+    const float c = dot * r * r * r / H;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int i = lane + 32 * k;
+      if (i < nv) {
+        float o[8];
+        if (dres != nullptr) {
+          load8(dres + row * H + i * 8, o);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] += r * gv[k][j] * wv[k][j] - xv[k][j] * c;
+        store8(dx + row * H + i * 8, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = lane + 32 * k;
+    if (i < nv) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) atomicAdd(&sdw[i * 8 + j], acc[k][j]);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < H; i += blockDim.x) atomicAdd(&dw[i], sdw[i]);
+}
+
 // ------------------------------------------------------- QK-norm + RoPE
 // One warp per (token, head).  Head index hh: [0,Hq) q heads, [Hq, Hq+Hkv) k
 // heads, [Hq+Hkv, Hq+2Hkv) v heads.  Lane l holds EPL = D/32 consecutive
@@ -231,6 +302,11 @@ __global__ void qk_norm_rope_bwd_k(const bf16* __restrict__ dq, const bf16* __re
   const int64_t T = (int64_t)B * S;
   const int64_t total = T * Htot;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  // lane-owned partial sums of d(q_norm.weight) / d(k_norm.weight): lane l
+  // always handles elements [l*EPL, l*EPL+EPL), so no atomics inside the loop
+  float accq[EPL], acck[EPL];
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) accq[j] = acck[j] = 0.f;
   for (int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); item < total;
        item += warps) {
     const int64_t t = item / Htot;
@@ -286,7 +362,6 @@ __global__ void qk_norm_rope_bwd_k(const bf16* __restrict__ dq, const bf16* __re
     }
     const float r = rstd[t * (Hq + Hkv) + hh];
     const bf16* w = is_q ? qw : kw;
-    float* sw = is_q ? s_dqw : s_dkw;
     const bf16* xs = kqv + t * C + col + lane * EPL;
     float x[EPL];
 #pragma unroll
@@ -302,7 +377,8 @@ __global__ void qk_norm_rope_bwd_k(const bf16* __restrict__ dq, const bf16* __re
       const float wj = __bfloat162float(w[lane * EPL + j]);
       dxr[j] = dn[j] * wj;
       dot += dxr[j] * x[j];
-      atomicAdd(&sw[lane * EPL + j], dn[j] * rb(x[j] * r));
+      const float contrib = dn[j] * rb(x[j] * r);
+      if (is_q) accq[j] += contrib; else acck[j] += contrib;
     }
     dot = warp_sum(dot);
     const float c3 = dot * r * r * r / D;
@@ -312,6 +388,13 @@ __global__ void qk_norm_rope_bwd_k(const bf16* __restrict__ dq, const bf16* __re
 #pragma unroll
     for (int j = 0; j < EPL; j += 2)
       *reinterpret_cast<uint32_t*>(dst + j) = pack_bf16x2(o[j], o[j + 1]);
+  }
+  if (qk_norm) {
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) {
+      atomicAdd(&s_dqw[lane * EPL + j], accq[j]);
+      atomicAdd(&s_dkw[lane * EPL + j], acck[j]);
+    }
   }
   __syncthreads();
   if (qk_norm) {
@@ -467,8 +550,17 @@ void rmsnorm_fwd(const bf16* x, const bf16* w, bf16* y, float* rstd, int64_t T, 
 
 void rmsnorm_bwd(const bf16* dy, const bf16* x, const bf16* w, const float* rstd,
                  const bf16* dres, bf16* dx, float* dw, int64_t T, int H, cudaStream_t s) {
-  rmsnorm_bwd_k<<<grid_for(T, 8, 148 * 4), 256, H * sizeof(float), s>>>(dy, x, w, rstd, dres, dx,
-                                                                        dw, T, H);
+  const int nv = H / 8;
+  const int grid = grid_for(T, 8, 148 * 4);
+  const size_t sm = H * sizeof(float);
+  if (nv <= 32)
+    rmsnorm_bwd_reg_k<1><<<grid, 256, sm, s>>>(dy, x, w, rstd, dres, dx, dw, T, H);
+  else if (nv <= 64)
+    rmsnorm_bwd_reg_k<2><<<grid, 256, sm, s>>>(dy, x, w, rstd, dres, dx, dw, T, H);
+  else if (nv <= 128)
+    rmsnorm_bwd_reg_k<4><<<grid, 256, sm, s>>>(dy, x, w, rstd, dres, dx, dw, T, H);
+  else
+    rmsnorm_bwd_k<<<grid, 256, sm, s>>>(dy, x, w, rstd, dres, dx, dw, T, H);
 }
 
 void qk_norm_rope_fwd(const bf16* kqv, const bf16* qw, const bf16* kw, const float* cos_t,

@@ -82,12 +82,11 @@ __device__ __forceinline__ float swiglu_col_scale(const GemmEpi& ep, int row, in
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(384, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    int M, int N, int K, GemmEpi ep, int* err) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
-  constexpr uint32_t IDESC = idesc_bf16(kBM, BN, A_MN, B_MN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -115,7 +114,7 @@ __global__ void __launch_bounds__(256, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 128);
+      mbar_init(&tempty_bar[a], 256);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -183,6 +182,9 @@ __global__ void __launch_bounds__(256, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
+        // the last column tile may be narrower than BN: issue a narrower MMA
+        const int n_rem = N - (t % num_n) * BN;
+        const uint32_t idesc = idesc_bf16(kBM, n_rem < BN ? n_rem : BN, A_MN, B_MN);
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, abort_flag, err, kErrTimeoutFull, 12)) {
             ok = false;
@@ -197,7 +199,7 @@ __global__ void __launch_bounds__(256, 1)
                                         : sw128_desc(a_base + k * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? sw128_desc(b_base + k * 2048, 64 * kBK * 2, 1024)
                                         : sw128_desc(b_base + k * 32, 16, 1024);
-            umma_bf16(d_tmem, adesc, bdesc, IDESC, (kb | k) != 0 ? 1u : 0u);
+            umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(&empty_bar[stage]);
           if (++stage == STAGES) {
@@ -213,7 +215,10 @@ __global__ void __launch_bounds__(256, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
+    // two epilogue warpgroups (warps 4-7 and 8-11) split the tile's columns;
+    // warp w reads TMEM lanes 32*(w%4)..+31, i.e. rows of the tile
     const int wq = warp & 3;
+    const int wg = (warp - 4) >> 2;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
@@ -231,7 +236,7 @@ __global__ void __launch_bounds__(256, 1)
         // Tile columns [0, BN/2) are gate, [BN/2, BN) are the matching up columns.
         constexpr int HALF = BN / 2;
 #pragma unroll 1
-        for (int c = 0; c < HALF; c += 32) {
+        for (int c = wg * HALF / 2; c < (wg + 1) * HALF / 2; c += 32) {
           float g[32], u[32];
           tmem_ld32(tbase + c, g);
           tmem_ld32(tbase + HALF + c, u);
@@ -258,18 +263,22 @@ __global__ void __launch_bounds__(256, 1)
         // Accumulator = d(act) for activation columns [n0, n0+BN).
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.c);
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = wg * BN / 2; c < (wg + 1) * BN / 2; c += 32) {
+          const int act_col = n0 + c;
+          const bool col_ok = row_ok && act_col < N;
+          const int blk = act_col / kSwigluBlock;
+          const int w = act_col % kSwigluBlock;
+          const int64_t goff = static_cast<int64_t>(row) * ep.ldgu + blk * 2 * kSwigluBlock + w;
+          // issue the global loads of the saved pre-activations before reading TMEM
+          float g[32], u[32];
+          if (col_ok) {
+            load_bf16x32(ep.gu + goff, g);
+            load_bf16x32(ep.gu + goff + kSwigluBlock, u);
+          }
           float da[32];
           tmem_ld32(tbase + c, da);
           tmem_wait_ld();
-          const int act_col = n0 + c;
-          if (row_ok && act_col < N) {
-            const int blk = act_col / kSwigluBlock;
-            const int w = act_col % kSwigluBlock;
-            const int64_t goff = static_cast<int64_t>(row) * ep.ldgu + blk * 2 * kSwigluBlock + w;
-            float g[32], u[32];
-            load_bf16x32(ep.gu + goff, g);
-            load_bf16x32(ep.gu + goff + kSwigluBlock, u);
+          if (col_ok) {
             const float s = swiglu_col_scale(ep, row, act_col);
             float dg[32], du[32];
 #pragma unroll
@@ -290,7 +299,7 @@ __global__ void __launch_bounds__(256, 1)
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.c);
         float mx = -INFINITY, se = 0.0f;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = wg * BN / 2; c < (wg + 1) * BN / 2; c += 32) {
           float v[32];
           tmem_ld32(tbase + c, v);
           tmem_wait_ld();
@@ -313,11 +322,17 @@ __global__ void __launch_bounds__(256, 1)
         }
         if (row_ok) {
           float2* st = reinterpret_cast<float2*>(ep.stats);
-          st[static_cast<int64_t>(row) * num_n + n_blk] = make_float2(mx, se);
+          // one (max, sumexp) pair per half tile (BN/2 columns)
+          st[static_cast<int64_t>(row) * num_n * 2 + n_blk * 2 + wg] = make_float2(mx, se);
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = wg * BN / 2; c < (wg + 1) * BN / 2; c += 32) {
+          float r[32];
+          if constexpr (EPI == EPI_RESID) {
+            if (row_ok && n0 + c < N)
+              load_bf16x32(ep.r + static_cast<int64_t>(row) * ep.ldr + n0 + c, r);
+          }
           float v[32];
           tmem_ld32(tbase + c, v);
           tmem_wait_ld();
@@ -327,8 +342,6 @@ __global__ void __launch_bounds__(256, 1)
               store_bf16x32(out + static_cast<int64_t>(row) * ep.ldc + n0 + c, v, ep.alpha);
             } else if constexpr (EPI == EPI_RESID) {
               __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.c);
-              float r[32];
-              load_bf16x32(ep.r + static_cast<int64_t>(row) * ep.ldr + n0 + c, r);
 #pragma unroll
               for (int i = 0; i < 32; ++i) v[i] = v[i] * ep.alpha + r[i];
               store_bf16x32(out + static_cast<int64_t>(row) * ep.ldc + n0 + c, v, 1.0f);
@@ -406,7 +419,7 @@ static int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, int M, int 
   }
   const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int grid = tiles < num_sms ? tiles : num_sms;
-  kern<<<grid, 256, Cfg::SMEM_BYTES, stream>>>(ta, tb, M, N, K, ep, err);
+  kern<<<grid, 384, Cfg::SMEM_BYTES, stream>>>(ta, tb, M, N, K, ep, err);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -420,13 +433,14 @@ static int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUt
   return launch_impl<BN, true, true, EPI>(ta, tb, M, N, K, ep, sms, s, err);
 }
 
+// 128x256 tiles keep shared-memory traffic per MMA at 96 B/clk (128x128 tiles
+// need 128 B/clk, the whole shared-memory bandwidth, leaving none for TMA
+// writes), so 256 is used unless N itself is at most 128.  A narrower last
+// column tile issues a narrower MMA instead of computing padding.
 int choose_bn(int M, int N, int num_sms) {
-  auto cost = [&](int bn) {
-    long tiles = static_cast<long>((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
-    long waves = (tiles + num_sms - 1) / num_sms;
-    return waves * bn;
-  };
-  return cost(128) < cost(256) ? 128 : 256;
+  (void)M;
+  (void)num_sms;
+  return N <= 128 ? 128 : 256;
 }
 
 int gemm_tc_launch(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream, int* err) {

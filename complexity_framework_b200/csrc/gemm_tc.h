@@ -14,7 +14,7 @@ enum GemmEpilogue : int {
   EPI_SWIGLU_BWD = 3,  // acc = d(ACT) -> C = d(GU) using saved GU
   EPI_F32 = 4,         // C(fp32) = alpha * acc
   EPI_F32_ACC = 5,     // C(fp32) += alpha * acc
-  EPI_CE_STATS = 6,    // C(bf16) logits = alpha*acc; stats[row, ntile] = (max, sumexp)
+  EPI_CE_STATS = 6,    // C(bf16) logits = alpha*acc; stats[row, N/128] = (max, sumexp); BN=256
 };
 
 // Width (in activation columns) of one gate block in the packed gate|up weight:
@@ -37,7 +37,7 @@ struct GemmEpi {
   int expert_width = 1;
   int n_experts = 0;
   float shared_scale = 1.0f;
-  float* stats = nullptr;  // [M, ceil(N/BN)] float2
+  float* stats = nullptr;  // [M, 2*ceil(N/BN)] float2 (one per 128-column half tile)
 };
 
 struct GemmArgs {

@@ -301,7 +301,7 @@ class LinearCrossEntropyFn(torch.autograd.Function):
     """Mean next-token CE of ``hidden @ weight.T`` without a persistent logits tensor.
 
     Rows are processed in chunks: one tcgen05 GEMM writes the bf16 logits of a
-    chunk and per-(row, 256-column tile) max/sum-exp partials; one kernel turns
+    chunk and per-(row, 128-column) max/sum-exp partials; one kernel turns
     them into the row loss and overwrites the logits with d(loss)/d(logits);
     two GEMMs then produce d(hidden) for the chunk and accumulate d(weight) in
     fp32.  Gradients are computed in forward (the loss is the last op of the
@@ -324,7 +324,7 @@ class LinearCrossEntropyFn(torch.autograd.Function):
         dw = torch.zeros(V, H, device=h.device, dtype=torch.float32)
         losses = torch.empty(T, device=h.device, dtype=torch.float32)
         bn = 256
-        nt = (V + bn - 1) // bn
+        nt = 2 * ((V + bn - 1) // bn)  # one partial per 128-column half tile
         chunk = max(128, min(T, int(chunk_rows)))
         logits = torch.empty(chunk, V, device=h.device, dtype=torch.bfloat16)
         stats = torch.empty(chunk, nt, 2, device=h.device, dtype=torch.float32)

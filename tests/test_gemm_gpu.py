@@ -104,7 +104,7 @@ def test_gemm_ce_stats():
     M, N, K = 256, 1024, 128
     A, B, ref = _operands(M, N, K, False, False)
     bn = 256
-    nt = N // bn
+    nt = N // 128
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
     stats = torch.empty(M, nt, 2, device="cuda")
     C.gemm(A, False, B, False, M, N, K, EPI_CE_STATS, out=out, stats=stats, bn=bn)
