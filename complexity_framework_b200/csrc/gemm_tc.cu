@@ -39,13 +39,19 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 
-template <int BN>
+template <int BN, bool PAIR>
 struct GemmCfg {
+  // With PAIR, a 256-row tile is split over a CTA pair: each CTA holds its 128
+  // A rows and half of the BN B rows; the even CTA issues M=256 MMAs.
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
   static constexpr int A_BYTES = kBM * kBK * 2;
-  static constexpr int B_BYTES = BN * kBK * 2;
+  static constexpr int B_BYTES = B_ROWS * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = BN >= 256 ? 4 : 6;
+  static constexpr int STAGES = (227 * 1024 - 2048) / STAGE_BYTES > 8
+                                    ? 8
+                                    : (227 * 1024 - 2048) / STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int TILE_M = PAIR ? 2 * kBM : kBM;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
@@ -81,12 +87,13 @@ __device__ __forceinline__ float swiglu_col_scale(const GemmEpi& ep, int row, in
   return ep.row_scale[static_cast<int64_t>(row) * ep.n_experts + e];
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(384, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    int M, int N, int K, GemmEpi ep, int* err) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, PAIR>;
   constexpr int STAGES = Cfg::STAGES;
+  constexpr int B_ROWS = Cfg::B_ROWS;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -101,8 +108,12 @@ __global__ void __launch_bounds__(384, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;   // position inside the CTA pair
+  const bool leader = rank == 0;
+  const int unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int units = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
-  const int num_m = (M + kBM - 1) / kBM;
+  const int num_m = (M + Cfg::TILE_M - 1) / Cfg::TILE_M;
   const int num_n = (N + BN - 1) / BN;
   const int total = num_m * num_n;
   const int nk = (K + kBK - 1) / kBK;
@@ -114,7 +125,8 @@ __global__ void __launch_bounds__(384, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 256);
+      // one arrival per epilogue warp of every CTA in the MMA group
+      mbar_init(&tempty_bar[a], PAIR ? 16 : 8);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -123,9 +135,17 @@ __global__ void __launch_bounds__(384, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
   }
-  if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  if (warp == 1) {
+    if constexpr (PAIR)
+      tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    else
+      tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync_all();  // peer barriers initialised before any remote arrive / TMA
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -135,9 +155,13 @@ __global__ void __launch_bounds__(384, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        const int m0 = (t / num_n) * kBM;
+      for (int t = unit; t < total && ok; t += units) {
+        const int m0 = (t / num_n) * Cfg::TILE_M + static_cast<int>(rank) * kBM;
         const int n0 = (t % num_n) * BN;
+        // this CTA's B rows: half of the (possibly narrower) tail tile when paired
+        const int n_rem = N - n0;
+        const int n_this = n_rem < BN ? n_rem : BN;
+        const int nb0 = PAIR ? n0 + static_cast<int>(rank) * (n_this / 2) : n0;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty, 10)) {
             ok = false;
@@ -145,20 +169,39 @@ __global__ void __launch_bounds__(384, 1)
           }
           uint8_t* sA = tiles + stage * Cfg::STAGE_BYTES;
           uint8_t* sB = sA + Cfg::A_BYTES;
-          mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
-          if constexpr (!A_MN) {
-            tma_load_2d(sA, &tmA, &full_bar[stage], kb * kBK, m0);
-          } else {
+          if constexpr (PAIR) {
+            const uint32_t bar = mapa_shared(smem_u32(&full_bar[stage]), 0);
+            if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::STAGE_BYTES);
+            if constexpr (!A_MN) {
+              tma_load_2d_pair(sA, &tmA, bar, kb * kBK, m0);
+            } else {
 #pragma unroll
-            for (int i = 0; i < kBM / 64; ++i)
-              tma_load_2d(sA + i * 64 * kBK * 2, &tmA, &full_bar[stage], m0 + 64 * i, kb * kBK);
-          }
-          if constexpr (!B_MN) {
-            tma_load_2d(sB, &tmB, &full_bar[stage], kb * kBK, n0);
-          } else {
+              for (int i = 0; i < kBM / 64; ++i)
+                tma_load_2d_pair(sA + i * 64 * kBK * 2, &tmA, bar, m0 + 64 * i, kb * kBK);
+            }
+            if constexpr (!B_MN) {
+              tma_load_2d_pair(sB, &tmB, bar, kb * kBK, nb0);
+            } else {
 #pragma unroll
-            for (int i = 0; i < BN / 64; ++i)
-              tma_load_2d(sB + i * 64 * kBK * 2, &tmB, &full_bar[stage], n0 + 64 * i, kb * kBK);
+              for (int i = 0; i < B_ROWS / 64; ++i)
+                tma_load_2d_pair(sB + i * 64 * kBK * 2, &tmB, bar, nb0 + 64 * i, kb * kBK);
+            }
+          } else {
+            mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+            if constexpr (!A_MN) {
+              tma_load_2d(sA, &tmA, &full_bar[stage], kb * kBK, m0);
+            } else {
+#pragma unroll
+              for (int i = 0; i < kBM / 64; ++i)
+                tma_load_2d(sA + i * 64 * kBK * 2, &tmA, &full_bar[stage], m0 + 64 * i, kb * kBK);
+            }
+            if constexpr (!B_MN) {
+              tma_load_2d(sB, &tmB, &full_bar[stage], kb * kBK, n0);
+            } else {
+#pragma unroll
+              for (int i = 0; i < BN / 64; ++i)
+                tma_load_2d(sB + i * 64 * kBK * 2, &tmB, &full_bar[stage], n0 + 64 * i, kb * kBK);
+            }
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -169,13 +212,13 @@ __global__ void __launch_bounds__(384, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (elect_one()) {
+    if (leader && elect_one()) {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      for (int t = unit; t < total && ok; t += units) {
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, abort_flag, err, kErrTimeoutTmem, 11)) {
           ok = false;
           break;
@@ -184,7 +227,7 @@ __global__ void __launch_bounds__(384, 1)
         const uint32_t d_tmem = tmem_base + acc * BN;
         // the last column tile may be narrower than BN: issue a narrower MMA
         const int n_rem = N - (t % num_n) * BN;
-        const uint32_t idesc = idesc_bf16(kBM, n_rem < BN ? n_rem : BN, A_MN, B_MN);
+        const uint32_t idesc = idesc_bf16(Cfg::TILE_M, n_rem < BN ? n_rem : BN, A_MN, B_MN);
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, abort_flag, err, kErrTimeoutFull, 12)) {
             ok = false;
@@ -199,16 +242,25 @@ __global__ void __launch_bounds__(384, 1)
                                         : sw128_desc(a_base + k * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? sw128_desc(b_base + k * 2048, 64 * kBK * 2, 1024)
                                         : sw128_desc(b_base + k * 32, 16, 1024);
-            umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            if constexpr (PAIR)
+              umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            else
+              umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
-          umma_commit(&empty_bar[stage]);
+          if constexpr (PAIR)
+            umma_commit_pair(&empty_bar[stage], 0x3);
+          else
+            umma_commit(&empty_bar[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull_bar[acc]);
+        if constexpr (PAIR)
+          umma_commit_pair(&tfull_bar[acc], 0x3);
+        else
+          umma_commit(&tfull_bar[acc]);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
@@ -221,10 +273,12 @@ __global__ void __launch_bounds__(384, 1)
     const int wg = (warp - 4) >> 2;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+    const uint32_t tempty_peer0 = mapa_shared(smem_u32(&tempty_bar[0]), 0);
+    const uint32_t tempty_peer1 = mapa_shared(smem_u32(&tempty_bar[1]), 0);
+    for (int t = unit; t < total; t += units) {
       const int m_blk = t / num_n;
       const int n_blk = t % num_n;
-      const int m0 = m_blk * kBM;
+      const int m0 = m_blk * Cfg::TILE_M + static_cast<int>(rank) * kBM;
       const int n0 = n_blk * BN;
       if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, err, kErrTimeoutTmem, 13)) break;
       tc_fence_after();
@@ -363,17 +417,29 @@ __global__ void __launch_bounds__(384, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&tempty_bar[acc]);
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (PAIR)
+          mbar_arrive_cluster(acc ? tempty_peer1 : tempty_peer0);
+        else
+          mbar_arrive(&tempty_bar[acc]);
+      }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync_all();  // both CTAs' epilogues are done before the pair frees TMEM
+  else
+    __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
 }
 
@@ -407,36 +473,65 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
   return r == CUDA_SUCCESS ? 0 : static_cast<int>(r) + 1000;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool PAIR>
 static int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
                        const GemmEpi& ep, int num_sms, cudaStream_t stream, int* err) {
-  using Cfg = GemmCfg<BN>;
-  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI>;
-  static bool attr_set = false;  // one per instantiation
-  if (!attr_set) {
+  using Cfg = GemmCfg<BN, PAIR>;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI, PAIR>;
+  static int max_units = -1;  // resident CTAs (or CTA pairs), one query per instantiation
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.blockDim = dim3(384, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = stream;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = PAIR ? 2 : 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (max_units < 0) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
-    attr_set = true;
+    if (PAIR) {
+      cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters <= 0)
+        clusters = num_sms / 2;
+      max_units = clusters;
+    } else {
+      max_units = num_sms;
+    }
   }
-  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
-  const int grid = tiles < num_sms ? tiles : num_sms;
-  kern<<<grid, 384, Cfg::SMEM_BYTES, stream>>>(ta, tb, M, N, K, ep, err);
-  return static_cast<int>(cudaGetLastError());
+  const int tiles = ((M + Cfg::TILE_M - 1) / Cfg::TILE_M) * ((N + BN - 1) / BN);
+  const int units = tiles < max_units ? tiles : max_units;
+  cfg.gridDim = dim3(PAIR ? 2 * units : units, 1, 1);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, ep, err);
+  return static_cast<int>(e);
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+static int launch_pair_or_single(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
+                                 int K, const GemmEpi& ep, int sms, cudaStream_t s, int* err) {
+  // 256-row tiles over an SM pair halve each SM's operand traffic per FLOP;
+  // a single 128-row tile is used only when M itself fits in one.
+  // (keep in sync with the B tensor-map box chosen in gemm_tc_launch)
+  if (M > kBM) return launch_impl<BN, A_MN, B_MN, EPI, true>(ta, tb, M, N, K, ep, sms, s, err);
+  return launch_impl<BN, A_MN, B_MN, EPI, false>(ta, tb, M, N, K, ep, sms, s, err);
 }
 
 template <int BN, int EPI>
 static int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
                           int M, int N, int K, const GemmEpi& ep, int sms, cudaStream_t s,
                           int* err) {
-  if (!a_mn && !b_mn) return launch_impl<BN, false, false, EPI>(ta, tb, M, N, K, ep, sms, s, err);
-  if (!a_mn && b_mn) return launch_impl<BN, false, true, EPI>(ta, tb, M, N, K, ep, sms, s, err);
-  if (a_mn && !b_mn) return launch_impl<BN, true, false, EPI>(ta, tb, M, N, K, ep, sms, s, err);
-  return launch_impl<BN, true, true, EPI>(ta, tb, M, N, K, ep, sms, s, err);
+  if (!a_mn && !b_mn)
+    return launch_pair_or_single<BN, false, false, EPI>(ta, tb, M, N, K, ep, sms, s, err);
+  if (!a_mn && b_mn)
+    return launch_pair_or_single<BN, false, true, EPI>(ta, tb, M, N, K, ep, sms, s, err);
+  if (a_mn && !b_mn)
+    return launch_pair_or_single<BN, true, false, EPI>(ta, tb, M, N, K, ep, sms, s, err);
+  return launch_pair_or_single<BN, true, true, EPI>(ta, tb, M, N, K, ep, sms, s, err);
 }
 
-// 128x256 tiles keep shared-memory traffic per MMA at 96 B/clk (128x128 tiles
-// need 128 B/clk, the whole shared-memory bandwidth, leaving none for TMA
-// writes), so 256 is used unless N itself is at most 128.  A narrower last
-// column tile issues a narrower MMA instead of computing padding.
 int choose_bn(int M, int N, int num_sms) {
   (void)M;
   (void)num_sms;
@@ -457,7 +552,7 @@ int gemm_tc_launch(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream, in
     rc = make_tmap_2d(&ta, g.A, g.K, g.M, g.lda, 64, kBK);
   if (rc) return rc;
   if (!g.b_mn)
-    rc = make_tmap_2d(&tb, g.B, g.N, g.K, g.ldb, kBK, bn);
+    rc = make_tmap_2d(&tb, g.B, g.N, g.K, g.ldb, kBK, g.M > kBM ? bn / 2 : bn);  // pair: half B
   else
     rc = make_tmap_2d(&tb, g.B, g.K, g.N, g.ldb, 64, kBK);
   if (rc) return rc;
@@ -476,14 +571,14 @@ int gemm_tc_launch(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream, in
     CFB_EPI_CASE(EPI_CE_STATS)
     case EPI_SWIGLU_FWD:
       if (g.a_mn || g.b_mn) return -4;
-      return launch_impl<256, false, false, EPI_SWIGLU_FWD>(ta, tb, g.M, g.N, g.K, ep, g.num_sms,
-                                                            stream, err);
+      return launch_pair_or_single<256, false, false, EPI_SWIGLU_FWD>(ta, tb, g.M, g.N, g.K, ep,
+                                                                      g.num_sms, stream, err);
     case EPI_SWIGLU_BWD:
       if (g.a_mn || !g.b_mn) return -4;
-      return bn == 256 ? launch_impl<256, false, true, EPI_SWIGLU_BWD>(ta, tb, g.M, g.N, g.K, ep,
-                                                                       g.num_sms, stream, err)
-                       : launch_impl<128, false, true, EPI_SWIGLU_BWD>(ta, tb, g.M, g.N, g.K, ep,
-                                                                       g.num_sms, stream, err);
+      return bn == 256 ? launch_pair_or_single<256, false, true, EPI_SWIGLU_BWD>(
+                             ta, tb, g.M, g.N, g.K, ep, g.num_sms, stream, err)
+                       : launch_pair_or_single<128, false, true, EPI_SWIGLU_BWD>(
+                             ta, tb, g.M, g.N, g.K, ep, g.num_sms, stream, err);
     default:
       return -5;
   }
