@@ -120,7 +120,7 @@ void gemm(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, 
   } else {
     TORCH_CHECK(out.has_value(), "gemm needs out");
     TORCH_CHECK(out->is_cuda(), "out must be CUDA");
-    const bool f32 = epi == cfb::EPI_F32 || epi == cfb::EPI_F32_ACC;
+    const bool f32 = epi == cfb::EPI_F32 || epi == cfb::EPI_F32_ACC || epi == cfb::EPI_F32_ATOMIC;
     TORCH_CHECK(out->scalar_type() == (f32 ? torch::kFloat32 : torch::kBFloat16),
                 "out dtype mismatch for epilogue");
     TORCH_CHECK(out->dim() == 2 && out->stride(1) == 1, "out must be row-major 2-D");

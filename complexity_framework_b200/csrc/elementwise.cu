@@ -551,7 +551,7 @@ void rmsnorm_fwd(const bf16* x, const bf16* w, bf16* y, float* rstd, int64_t T, 
 void rmsnorm_bwd(const bf16* dy, const bf16* x, const bf16* w, const float* rstd,
                  const bf16* dres, bf16* dx, float* dw, int64_t T, int H, cudaStream_t s) {
   const int nv = H / 8;
-  const int grid = grid_for(T, 8, 148 * 4);
+  const int grid = grid_for(T, 8, 148 * 8);
   const size_t sm = H * sizeof(float);
   if (nv <= 32)
     rmsnorm_bwd_reg_k<1><<<grid, 256, sm, s>>>(dy, x, w, rstd, dres, dx, dw, T, H);
@@ -582,7 +582,7 @@ void qk_norm_rope_bwd(const bf16* dq, const bf16* dk, const bf16* dv, const bf16
                       const int32_t* pos, const float* rstd, bf16* dkqv, float* dqw, float* dkw,
                       int B, int S, int Hq, int Hkv, int D, bool qk_norm, cudaStream_t s) {
   const int64_t items = (int64_t)B * S * (Hq + 2 * Hkv);
-  const int grid = grid_for(items, 8, 148 * 4);
+  const int grid = grid_for(items, 8, 148 * 16);
   if (D == 64)
     qk_norm_rope_bwd_k<2><<<grid, 256, 0, s>>>(dq, dk, dv, kqv, qw, kw, cos_t, sin_t, pos, rstd,
                                                dkqv, dqw, dkw, B, S, Hq, Hkv, qk_norm);

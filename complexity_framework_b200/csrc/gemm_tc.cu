@@ -90,7 +90,7 @@ __device__ __forceinline__ float swiglu_col_scale(const GemmEpi& ep, int row, in
 template <int BN, bool A_MN, bool B_MN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(384, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   int M, int N, int K, GemmEpi ep, int* err) {
+                   int M, int N, int K, int ksplit, GemmEpi ep, int* err) {
   using Cfg = GemmCfg<BN, PAIR>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int B_ROWS = Cfg::B_ROWS;
@@ -115,8 +115,11 @@ __global__ void __launch_bounds__(384, 1)
 
   const int num_m = (M + Cfg::TILE_M - 1) / Cfg::TILE_M;
   const int num_n = (N + BN - 1) / BN;
-  const int total = num_m * num_n;
+  const int num_tiles = num_m * num_n;
   const int nk = (K + kBK - 1) / kBK;
+  // work unit u = (tile u / ksplit, K slice u % ksplit); ksplit > 1 only with the
+  // fp32 atomic epilogue, which sums the partial products of the slices
+  const int total = num_tiles * ksplit;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -155,14 +158,16 @@ __global__ void __launch_bounds__(384, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = unit; t < total && ok; t += units) {
+      for (int u = unit; u < total && ok; u += units) {
+        const int t = u / ksplit;
+        const int kb0 = (u % ksplit) * nk / ksplit, kb1 = ((u % ksplit) + 1) * nk / ksplit;
         const int m0 = (t / num_n) * Cfg::TILE_M + static_cast<int>(rank) * kBM;
         const int n0 = (t % num_n) * BN;
         // this CTA's B rows: half of the (possibly narrower) tail tile when paired
         const int n_rem = N - n0;
         const int n_this = n_rem < BN ? n_rem : BN;
         const int nb0 = PAIR ? n0 + static_cast<int>(rank) * (n_this / 2) : n0;
-        for (int kb = 0; kb < nk; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty, 10)) {
             ok = false;
             break;
@@ -218,7 +223,9 @@ __global__ void __launch_bounds__(384, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = unit; t < total && ok; t += units) {
+      for (int u = unit; u < total && ok; u += units) {
+        const int t = u / ksplit;
+        const int kb0 = (u % ksplit) * nk / ksplit, kb1 = ((u % ksplit) + 1) * nk / ksplit;
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, abort_flag, err, kErrTimeoutTmem, 11)) {
           ok = false;
           break;
@@ -228,7 +235,7 @@ __global__ void __launch_bounds__(384, 1)
         // the last column tile may be narrower than BN: issue a narrower MMA
         const int n_rem = N - (t % num_n) * BN;
         const uint32_t idesc = idesc_bf16(Cfg::TILE_M, n_rem < BN ? n_rem : BN, A_MN, B_MN);
-        for (int kb = 0; kb < nk; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, abort_flag, err, kErrTimeoutFull, 12)) {
             ok = false;
             break;
@@ -243,9 +250,9 @@ __global__ void __launch_bounds__(384, 1)
             const uint64_t bdesc = B_MN ? sw128_desc(b_base + k * 2048, 64 * kBK * 2, 1024)
                                         : sw128_desc(b_base + k * 32, 16, 1024);
             if constexpr (PAIR)
-              umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+              umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
             else
-              umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+              umma_bf16(d_tmem, adesc, bdesc, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           if constexpr (PAIR)
             umma_commit_pair(&empty_bar[stage], 0x3);
@@ -275,7 +282,8 @@ __global__ void __launch_bounds__(384, 1)
     uint32_t acc_phase = 0;
     const uint32_t tempty_peer0 = mapa_shared(smem_u32(&tempty_bar[0]), 0);
     const uint32_t tempty_peer1 = mapa_shared(smem_u32(&tempty_bar[1]), 0);
-    for (int t = unit; t < total; t += units) {
+    for (int u = unit; u < total; u += units) {
+      const int t = u / ksplit;
       const int m_blk = t / num_n;
       const int n_blk = t % num_n;
       const int m0 = m_blk * Cfg::TILE_M + static_cast<int>(rank) * kBM;
@@ -399,6 +407,12 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
               for (int i = 0; i < 32; ++i) v[i] = v[i] * ep.alpha + r[i];
               store_bf16x32(out + static_cast<int64_t>(row) * ep.ldc + n0 + c, v, 1.0f);
+            } else if constexpr (EPI == EPI_F32_ATOMIC) {
+              float* out = reinterpret_cast<float*>(ep.c) + static_cast<int64_t>(row) * ep.ldc + n0 + c;
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                red_add_v4(out + 4 * q, v[4 * q] * ep.alpha, v[4 * q + 1] * ep.alpha,
+                           v[4 * q + 2] * ep.alpha, v[4 * q + 3] * ep.alpha);
             } else if constexpr (EPI == EPI_F32 || EPI == EPI_F32_ACC) {
               float4* out = reinterpret_cast<float4*>(reinterpret_cast<float*>(ep.c) +
                                                       static_cast<int64_t>(row) * ep.ldc + n0 + c);
@@ -475,7 +489,8 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
 
 template <int BN, bool A_MN, bool B_MN, int EPI, bool PAIR>
 static int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
-                       const GemmEpi& ep, int num_sms, cudaStream_t stream, int* err) {
+                       const GemmEpi& ep, int num_sms, cudaStream_t stream, int* err,
+                       int ksplit = 1) {
   using Cfg = GemmCfg<BN, PAIR>;
   auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI, PAIR>;
   static int max_units = -1;  // resident CTAs (or CTA pairs), one query per instantiation
@@ -503,20 +518,39 @@ static int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, int M, int 
     }
   }
   const int tiles = ((M + Cfg::TILE_M - 1) / Cfg::TILE_M) * ((N + BN - 1) / BN);
-  const int units = tiles < max_units ? tiles : max_units;
+  if (EPI == EPI_F32_ATOMIC && ksplit == 0) {
+    // pick the K split that fills the machine best (>= 8 K blocks per slice)
+    const int nk = (K + kBK - 1) / kBK;
+    int best = 1;
+    double best_eff = 0.0;
+    for (int ks = 1; ks <= 16 && nk / ks >= 8; ++ks) {
+      const int work = tiles * ks;
+      const int waves = (work + max_units - 1) / max_units;
+      const double eff = static_cast<double>(work) / (static_cast<double>(waves) * max_units);
+      if (eff > best_eff + 0.02) {
+        best_eff = eff;
+        best = ks;
+      }
+    }
+    ksplit = best;
+  }
+  if (ksplit < 1) ksplit = 1;
+  const int work = tiles * ksplit;
+  const int units = work < max_units ? work : max_units;
   cfg.gridDim = dim3(PAIR ? 2 * units : units, 1, 1);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, ep, err);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, ksplit, ep, err);
   return static_cast<int>(e);
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 static int launch_pair_or_single(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
                                  int K, const GemmEpi& ep, int sms, cudaStream_t s, int* err) {
+  const int ks = EPI == EPI_F32_ATOMIC ? 0 : 1;  // 0 = choose
   // 256-row tiles over an SM pair halve each SM's operand traffic per FLOP;
   // a single 128-row tile is used only when M itself fits in one.
   // (keep in sync with the B tensor-map box chosen in gemm_tc_launch)
-  if (M > kBM) return launch_impl<BN, A_MN, B_MN, EPI, true>(ta, tb, M, N, K, ep, sms, s, err);
-  return launch_impl<BN, A_MN, B_MN, EPI, false>(ta, tb, M, N, K, ep, sms, s, err);
+  if (M > kBM) return launch_impl<BN, A_MN, B_MN, EPI, true>(ta, tb, M, N, K, ep, sms, s, err, ks);
+  return launch_impl<BN, A_MN, B_MN, EPI, false>(ta, tb, M, N, K, ep, sms, s, err, ks);
 }
 
 template <int BN, int EPI>
@@ -568,6 +602,7 @@ int gemm_tc_launch(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream, in
     CFB_EPI_CASE(EPI_RESID)
     CFB_EPI_CASE(EPI_F32)
     CFB_EPI_CASE(EPI_F32_ACC)
+    CFB_EPI_CASE(EPI_F32_ATOMIC)
     CFB_EPI_CASE(EPI_CE_STATS)
     case EPI_SWIGLU_FWD:
       if (g.a_mn || g.b_mn) return -4;

@@ -14,6 +14,7 @@ enum GemmEpilogue : int {
   EPI_SWIGLU_BWD = 3,  // acc = d(ACT) -> C = d(GU) using saved GU
   EPI_F32 = 4,         // C(fp32) = alpha * acc
   EPI_F32_ACC = 5,     // C(fp32) += alpha * acc
+  EPI_F32_ATOMIC = 7,  // C(fp32) += alpha * acc with atomics; K may be split across CTAs
   EPI_CE_STATS = 6,    // C(bf16) logits = alpha*acc; stats[row, N/128] = (max, sumexp); BN=256
 };
 

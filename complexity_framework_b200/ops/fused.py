@@ -20,6 +20,14 @@ import torch
 from ._ext import require
 
 EPI_STORE, EPI_RESID, EPI_SWIGLU_FWD, EPI_SWIGLU_BWD, EPI_F32, EPI_F32_ACC, EPI_CE_STATS = range(7)
+EPI_F32_ATOMIC = 7
+
+_PAIR_UNITS = 74  # resident CTA pairs on a 148-SM B200
+
+
+def _few_tiles(M: int, N: int) -> bool:
+    """True when an M x N output has under two waves of 256x256 pair tiles."""
+    return ((M + 255) // 256) * ((N + 255) // 256) < 2 * _PAIR_UNITS
 
 
 def _c(t: torch.Tensor) -> torch.Tensor:
@@ -61,9 +69,11 @@ def gemm_tn(dy: torch.Tensor, x: torch.Tensor, out_dtype=torch.bfloat16,
     if accumulate_into is not None:
         C.gemm(dy, True, x, True, N, K, T, EPI_F32_ACC, out=accumulate_into)
         return accumulate_into
-    if out_dtype == torch.float32:
-        out = torch.empty(N, K, device=dy.device, dtype=torch.float32)
-        C.gemm(dy, True, x, True, N, K, T, EPI_F32, out=out)
+    if out_dtype == torch.float32 or _few_tiles(N, K):
+        # split the token (K) dimension over CTAs and sum the slices with fp32 atomics
+        out = torch.zeros(N, K, device=dy.device, dtype=torch.float32)
+        C.gemm(dy, True, x, True, N, K, T, EPI_F32_ATOMIC, out=out)
+        return out if out_dtype == torch.float32 else out.to(out_dtype)
     else:
         out = torch.empty(N, K, device=dy.device, dtype=torch.bfloat16)
         C.gemm(dy, True, x, True, N, K, T, EPI_STORE, out=out)

@@ -121,3 +121,13 @@ def test_gemm_no_device_errors():
 
     torch.cuda.synchronize()
     check_errors(0)
+
+
+@pytest.mark.parametrize("M,N,K", [(896, 3328, 8192), (256, 512, 4096), (6656, 896, 16384)])
+def test_gemm_split_k_atomic(M, N, K):
+    C = _C()
+    A, B, ref = _operands(M, N, K, True, True)
+    out = torch.zeros(M, N, device="cuda", dtype=torch.float32)
+    C.gemm(A, True, B, True, M, N, K, 7, out=out)
+    torch.cuda.synchronize()
+    _check(out, ref, 1e-3)
