@@ -1,0 +1,12 @@
+"""Inference: paged KV cache, continuous-batching engine, sampling."""
+from .batching import AsyncBatcher, BatchConfig, ContinuousBatcher, Request, RequestStatus
+from .engine import (DecodingStrategy, GenerationConfig, InferenceConfig, InferenceEngine,
+                     forward_paged, sample_next)
+from .paged import KVCache, OutOfPages, PagedBatch, PagePool, SeqChunk
+
+PagedKVCache = PagePool
+
+__all__ = ["AsyncBatcher", "BatchConfig", "ContinuousBatcher", "DecodingStrategy",
+           "GenerationConfig", "InferenceConfig", "InferenceEngine", "KVCache", "OutOfPages",
+           "PagedBatch", "PagedKVCache", "PagePool", "Request", "RequestStatus", "SeqChunk",
+           "forward_paged", "sample_next"]

@@ -1,0 +1,222 @@
+"""Paged KV cache.
+
+Memory: one pool per layer of ``num_pages`` pages, each page holding
+``page_size`` tokens of K and V for all KV heads:
+``k_pool[layer] : [num_pages, page_size, Hkv, D]`` (bf16 on GPU).  A sequence
+owns a list of pages; the page table maps logical block i of a sequence to a
+physical page.  Pages are allocated once per sequence for all layers (the
+reference allocated per layer while its pool held all layers, SURVEY A.3
+item 1) and attention reads the pages in place instead of gathering them into
+a new tensor per token (reference kv_cache.py:295-308).
+
+A forward step processes a ragged batch of new tokens (prefill chunks and
+single decode tokens of several sequences concatenated, N tokens total).
+``PagedBatch`` carries the per-token positions and write slots and the
+per-sequence page tables; ``write`` scatters the new K/V into the pools and
+``attend`` runs causal attention of each sequence's new queries over all of
+its cached keys.  On CUDA ``attend`` calls the sm_100a paged-attention kernel;
+elsewhere a PyTorch gather + SDPA reference.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence
+
+import torch
+import torch.nn.functional as F
+
+
+class OutOfPages(RuntimeError):
+    pass
+
+
+class PagePool:
+    def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, num_pages: int,
+                 page_size: int = 16, dtype=torch.bfloat16, device="cpu"):
+        self.num_layers = num_layers
+        self.num_kv_heads = num_kv_heads
+        self.head_dim = head_dim
+        self.num_pages = num_pages
+        self.page_size = page_size
+        self.dtype = dtype
+        self.device = torch.device(device)
+        shape = (num_layers, num_pages, page_size, num_kv_heads, head_dim)
+        self.k = torch.zeros(shape, dtype=dtype, device=self.device)
+        self.v = torch.zeros(shape, dtype=dtype, device=self.device)
+        self.free: List[int] = list(range(num_pages - 1, -1, -1))
+        self.pages: Dict[int, List[int]] = {}
+        self.lengths: Dict[int, int] = {}
+
+    # ------------------------------------------------------------ bookkeeping
+    def allocate_sequence(self, seq_id: int) -> None:
+        if seq_id in self.pages:
+            raise ValueError(f"sequence {seq_id} already allocated")
+        self.pages[seq_id] = []
+        self.lengths[seq_id] = 0
+
+    def free_sequence(self, seq_id: int) -> None:
+        for p in self.pages.pop(seq_id, []):
+            self.free.append(p)
+        self.lengths.pop(seq_id, None)
+
+    def reset(self) -> None:
+        for sid in list(self.pages):
+            self.free_sequence(sid)
+
+    def reserve(self, seq_id: int, new_tokens: int) -> None:
+        """Make room for ``new_tokens`` more tokens of ``seq_id`` (raises OutOfPages)."""
+        need = self.lengths[seq_id] + new_tokens
+        pages = self.pages[seq_id]
+        while len(pages) * self.page_size < need:
+            if not self.free:
+                raise OutOfPages("KV page pool exhausted")
+            pages.append(self.free.pop())
+
+    def can_reserve(self, seq_id: Optional[int], length_after: int, current: int = 0) -> bool:
+        have = len(self.pages.get(seq_id, [])) if seq_id is not None else 0
+        need = -(-length_after // self.page_size) - have
+        return need <= len(self.free)
+
+    def memory_usage(self) -> Dict[str, float]:
+        used = self.num_pages - len(self.free)
+        per_page = 2 * self.num_layers * self.page_size * self.num_kv_heads * self.head_dim * \
+            self.k.element_size()
+        return {"pages_used": used, "pages_total": self.num_pages,
+                "gb_used": used * per_page / 1e9, "gb_total": self.num_pages * per_page / 1e9}
+
+    def get_seq_len(self, seq_id: int) -> int:
+        return self.lengths[seq_id]
+
+
+@dataclass
+class SeqChunk:
+    seq_id: int
+    start: int      # position of the first new token
+    length: int     # number of new tokens
+
+
+class PagedBatch:
+    """Per-step view of the pool for a ragged batch of new tokens."""
+
+    def __init__(self, pool: PagePool, chunks: Sequence[SeqChunk]):
+        self.pool = pool
+        self.chunks = list(chunks)
+        dev = pool.device
+        pos, slots, seq_of_tok = [], [], []
+        for i, c in enumerate(self.chunks):
+            pool.reserve(c.seq_id, c.start + c.length - pool.lengths[c.seq_id])
+            pages = pool.pages[c.seq_id]
+            for t in range(c.start, c.start + c.length):
+                pos.append(t)
+                slots.append(pages[t // pool.page_size] * pool.page_size + t % pool.page_size)
+                seq_of_tok.append(i)
+        self.num_tokens = len(pos)
+        self.positions = torch.tensor(pos, dtype=torch.long, device=dev)
+        self.slots = torch.tensor(slots, dtype=torch.long, device=dev)
+        self.max_position = max(pos) if pos else 0
+        cu = [0]
+        for c in self.chunks:
+            cu.append(cu[-1] + c.length)
+        self.cu_q = torch.tensor(cu, dtype=torch.int32, device=dev)
+        self.kv_lens = torch.tensor([c.start + c.length for c in self.chunks], dtype=torch.int32,
+                                    device=dev)
+        max_pages = max(len(pool.pages[c.seq_id]) for c in self.chunks) if self.chunks else 1
+        table = torch.zeros(len(self.chunks), max(1, max_pages), dtype=torch.int32)
+        for i, c in enumerate(self.chunks):
+            pg = pool.pages[c.seq_id]
+            table[i, :len(pg)] = torch.tensor(pg, dtype=torch.int32)
+        self.page_table = table.to(dev)
+        self._cu_host = cu
+
+    def commit(self) -> None:
+        """Advance the recorded sequence lengths after the forward step."""
+        for c in self.chunks:
+            self.pool.lengths[c.seq_id] = max(self.pool.lengths[c.seq_id], c.start + c.length)
+
+    # ---------------------------------------------------------------- compute
+    def write(self, layer: int, k: torch.Tensor, v: torch.Tensor) -> None:
+        """k, v: [N, Hkv, D] for the N new tokens."""
+        P = self.pool
+        kf = P.k[layer].view(-1, P.num_kv_heads, P.head_dim)
+        vf = P.v[layer].view(-1, P.num_kv_heads, P.head_dim)
+        kf.index_copy_(0, self.slots, k.to(P.dtype))
+        vf.index_copy_(0, self.slots, v.to(P.dtype))
+
+    def attend(self, layer: int, q: torch.Tensor, scale: float) -> torch.Tensor:
+        """Causal attention of q [N, Hq, D] over each sequence's cached keys -> [N, Hq, D]."""
+        from ..ops._ext import load
+
+        C = load()
+        P = self.pool
+        if (q.is_cuda and C is not None and hasattr(C, "paged_attention")
+                and q.dtype == torch.bfloat16 and P.dtype == torch.bfloat16):
+            out = torch.empty_like(q)
+            C.paged_attention(q.contiguous(), P.k[layer], P.v[layer], self.page_table, self.cu_q,
+                              self.kv_lens, out, float(scale), int(self.max_q_len()))
+            return out
+        return self._attend_reference(layer, q, scale)
+
+    def max_q_len(self) -> int:
+        return max((c.length for c in self.chunks), default=1)
+
+    def _attend_reference(self, layer: int, q: torch.Tensor, scale: float) -> torch.Tensor:
+        P = self.pool
+        out = torch.empty_like(q)
+        Hq, Hkv = q.shape[1], P.num_kv_heads
+        for i, c in enumerate(self.chunks):
+            kv_len = c.start + c.length
+            pages = P.pages[c.seq_id][: -(-kv_len // P.page_size)]
+            idx = torch.tensor(pages, device=q.device)
+            k = P.k[layer][idx].reshape(-1, Hkv, P.head_dim)[:kv_len]
+            v = P.v[layer][idx].reshape(-1, Hkv, P.head_dim)[:kv_len]
+            qs = q[self._cu_host[i]:self._cu_host[i + 1]]
+            qh = qs.transpose(0, 1)[None].float()
+            kh = k.transpose(0, 1)[None].float()
+            vh = v.transpose(0, 1)[None].float()
+            if Hq != Hkv:
+                kh = kh.repeat_interleave(Hq // Hkv, 1)
+                vh = vh.repeat_interleave(Hq // Hkv, 1)
+            qpos = torch.arange(c.start, kv_len, device=q.device)[:, None]
+            kpos = torch.arange(kv_len, device=q.device)[None, :]
+            mask = torch.zeros(c.length, kv_len, device=q.device)
+            mask = mask.masked_fill(kpos > qpos, float("-inf"))
+            o = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=mask, scale=scale)
+            out[self._cu_host[i]:self._cu_host[i + 1]] = o[0].transpose(0, 1).to(q.dtype)
+        return out
+
+
+class KVCache:
+    """Contiguous per-layer KV cache ``[L, B, Hkv, Smax, D]`` (API of the reference KVCache)."""
+
+    def __init__(self, num_layers: int, batch_size: int, num_heads: int, head_dim: int,
+                 max_seq_len: int, dtype=torch.float32, device="cpu"):
+        shape = (num_layers, batch_size, num_heads, max_seq_len, head_dim)
+        self.k = torch.zeros(shape, dtype=dtype, device=device)
+        self.v = torch.zeros(shape, dtype=dtype, device=device)
+        self.max_seq_len = max_seq_len
+        self._len = 0
+
+    def update(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor):
+        n = k.shape[2]
+        if self._len + n > self.max_seq_len:
+            raise ValueError("KV cache full")
+        self.k[layer_idx, :, :, self._len:self._len + n] = k
+        self.v[layer_idx, :, :, self._len:self._len + n] = v
+        return self.get(layer_idx, self._len + n)
+
+    def get(self, layer_idx: int, length: Optional[int] = None):
+        n = self._len if length is None else length
+        return self.k[layer_idx, :, :, :n], self.v[layer_idx, :, :, :n]
+
+    def advance(self, num_tokens: int = 1) -> None:
+        self._len += num_tokens
+
+    def reset(self) -> None:
+        self._len = 0
+
+    @property
+    def seq_len(self) -> int:
+        return self._len
+
+    def memory_usage(self) -> float:
+        return 2 * self.k.numel() * self.k.element_size() / 1e9

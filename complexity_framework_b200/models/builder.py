@@ -208,7 +208,7 @@ class ComplexityModel(nn.Module):
                                top_k=top_k, top_p=top_p, do_sample=do_sample,
                                eos_token_id=eos_token_id)
         rows = [r.tolist() for r in input_ids.cpu()]
-        outs = eng.generate(rows, gen)
+        outs = eng.generate_tokens(rows, gen)
         return [r + o for r, o in zip(rows, outs)]
 
     # -------------------------------------------------------------- save/load
