@@ -115,6 +115,18 @@ class GroupedQueryAttention(nn.Module):
                 past_key_value: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
                 use_cache: bool = False, residual: Optional[torch.Tensor] = None, **kwargs):
         """Returns ``(out, new_kv)``; ``out`` includes ``residual`` when one is given."""
+        tp = getattr(self, "tp_group", None)
+        if tp is not None:
+            # tensor parallel: local heads, partial o_proj, one all-reduce, then residual
+            from ..parallel.tensor_parallel import copy_to_tp, reduce_from_tp
+
+            x = copy_to_tp(hidden_states, tp)
+            if self.fused_eligible(x, attention_mask, past_key_value, use_cache):
+                out, kv = self._forward_fused(x, None), None
+            else:
+                out, kv = self._forward_reference(x, attention_mask, past_key_value, use_cache)
+            out = reduce_from_tp(out, tp)
+            return (out if residual is None else residual + out), kv
         if self.fused_eligible(hidden_states, attention_mask, past_key_value, use_cache):
             return self._forward_fused(hidden_states, residual), None
         out, kv = self._forward_reference(hidden_states, attention_mask, past_key_value, use_cache)

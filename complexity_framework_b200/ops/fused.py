@@ -129,6 +129,13 @@ def pack_gate_up(shared_gate: Optional[torch.Tensor], shared_up: Optional[torch.
     return torch.stack((g.view(nb, block, H), u.view(nb, block, H)), 1).reshape(2 * A, H)
 
 
+def pack_shared_gate_up(gate: torch.Tensor, up: torch.Tensor, block: int = 128) -> torch.Tensor:
+    """Interleave gate/up rows in blocks of ``block`` (shared SwiGLU only, no experts)."""
+    A, H = gate.shape
+    nb = A // block
+    return torch.stack((gate.view(nb, block, H), up.view(nb, block, H)), 1).reshape(2 * A, H)
+
+
 def pack_down(shared_down: Optional[torch.Tensor], expert_down: torch.Tensor) -> torch.Tensor:
     """``[H, shared + E*W]`` down weight: shared columns then expert e's W columns."""
     E, W, H = expert_down.shape

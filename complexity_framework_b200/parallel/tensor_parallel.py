@@ -1,0 +1,285 @@
+"""Megatron-style tensor parallelism for the TR-Hash decoder.
+
+Shards, over a TP group of size P:
+  * attention: q heads (and k/v heads when divisible by P, else replicated),
+    o_proj input columns;
+  * the shared SwiGLU: gate/up output rows, down input columns;
+  * every routed expert: its width W (gate/up columns, down rows);
+so one decoder block needs exactly one all-reduce after attention and one
+after the FFN.  The reference shards attention only and leaves the FFN
+replicated (complexity/parallel/tensor_parallel.py:371-446), and
+its backward never all-reduces the gradient of the replicated input
+(``_AllReduceFunc`` backward is identity with no copy-to-region op, SURVEY
+A.3 item 2); here ``copy_to_tp`` (identity forward, all-reduce backward) and
+``reduce_from_tp`` (all-reduce forward, identity backward) pair up correctly.
+
+The primitives and ``ColumnParallelLinear`` / ``RowParallelLinear`` /
+``ParallelEmbedding`` keep the reference names.  Each sharded parameter
+records ``_tp_shard_dim`` so checkpoints can be re-assembled
+(``gather_tp_state_dict``).
+"""
+from __future__ import annotations
+
+from dataclasses import replace
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+import torch.nn.functional as F
+
+_TP = {"group": None}
+
+
+def initialize_tensor_parallel(group) -> None:
+    _TP["group"] = group
+
+
+def get_tp_group():
+    return _TP["group"]
+
+
+def tp_world(group=None) -> int:
+    g = group if group is not None else _TP["group"]
+    return dist.get_world_size(g) if (g is not None and dist.is_initialized()) else 1
+
+
+def tp_rank(group=None) -> int:
+    g = group if group is not None else _TP["group"]
+    return dist.get_rank(g) if (g is not None and dist.is_initialized()) else 0
+
+
+# ------------------------------------------------------------- primitives
+class _CopyToTP(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        return x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        g = g.contiguous()
+        dist.all_reduce(g, group=ctx.group)
+        return g, None
+
+
+class _ReduceFromTP(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, group):
+        x = x.contiguous().clone()
+        dist.all_reduce(x, group=group)
+        return x
+
+    @staticmethod
+    def backward(ctx, g):
+        return g, None
+
+
+class _GatherLastDim(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        P = dist.get_world_size(group)
+        parts = [torch.empty_like(x) for _ in range(P)]
+        dist.all_gather(parts, x.contiguous(), group=group)
+        return torch.cat(parts, -1)
+
+    @staticmethod
+    def backward(ctx, g):
+        P = dist.get_world_size(ctx.group)
+        r = dist.get_rank(ctx.group)
+        return g.chunk(P, -1)[r].contiguous(), None
+
+
+class _ScatterLastDim(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        P = dist.get_world_size(group)
+        return x.chunk(P, -1)[dist.get_rank(group)].contiguous()
+
+    @staticmethod
+    def backward(ctx, g):
+        P = dist.get_world_size(ctx.group)
+        parts = [torch.empty_like(g) for _ in range(P)]
+        dist.all_gather(parts, g.contiguous(), group=ctx.group)
+        return torch.cat(parts, -1), None
+
+
+def copy_to_tp(x, group=None):
+    g = group if group is not None else _TP["group"]
+    return x if tp_world(g) == 1 else _CopyToTP.apply(x, g)
+
+
+def reduce_from_tp(x, group=None):
+    g = group if group is not None else _TP["group"]
+    return x if tp_world(g) == 1 else _ReduceFromTP.apply(x, g)
+
+
+def gather_from_tp(x, group=None):
+    g = group if group is not None else _TP["group"]
+    return x if tp_world(g) == 1 else _GatherLastDim.apply(x, g)
+
+
+def scatter_to_tp(x, group=None):
+    g = group if group is not None else _TP["group"]
+    return x if tp_world(g) == 1 else _ScatterLastDim.apply(x, g)
+
+
+# ------------------------------------------------------------------ layers
+class ColumnParallelLinear(nn.Module):
+    """y = x W^T with W split by output rows; optional gather of the output."""
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = False,
+                 gather_output: bool = False, group=None):
+        super().__init__()
+        self.group = group if group is not None else _TP["group"]
+        P = tp_world(self.group)
+        if out_features % P:
+            raise ValueError("out_features must be divisible by the TP size")
+        self.gather_output = gather_output
+        self.weight = nn.Parameter(torch.empty(out_features // P, in_features))
+        self.weight._tp_shard_dim = 0
+        self.bias = nn.Parameter(torch.zeros(out_features // P)) if bias else None
+        nn.init.normal_(self.weight, std=0.02)
+
+    def forward(self, x):
+        y = F.linear(copy_to_tp(x, self.group), self.weight, self.bias)
+        return gather_from_tp(y, self.group) if self.gather_output else y
+
+
+class RowParallelLinear(nn.Module):
+    """y = sum_ranks x_r W_r^T with W split by input columns (all-reduce of the output)."""
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = False,
+                 input_is_parallel: bool = True, group=None):
+        super().__init__()
+        self.group = group if group is not None else _TP["group"]
+        P = tp_world(self.group)
+        if in_features % P:
+            raise ValueError("in_features must be divisible by the TP size")
+        self.input_is_parallel = input_is_parallel
+        self.weight = nn.Parameter(torch.empty(out_features, in_features // P))
+        self.weight._tp_shard_dim = 1
+        self.bias = nn.Parameter(torch.zeros(out_features)) if bias else None
+        nn.init.normal_(self.weight, std=0.02)
+
+    def forward(self, x):
+        if not self.input_is_parallel:
+            x = scatter_to_tp(x, self.group)
+        y = reduce_from_tp(F.linear(x, self.weight), self.group)
+        return y + self.bias if self.bias is not None else y
+
+
+class ParallelEmbedding(nn.Module):
+    """Vocabulary-sharded embedding: each rank owns V/P rows; outputs are all-reduced."""
+
+    def __init__(self, num_embeddings: int, embedding_dim: int, group=None):
+        super().__init__()
+        self.group = group if group is not None else _TP["group"]
+        P, r = tp_world(self.group), tp_rank(self.group)
+        if num_embeddings % P:
+            raise ValueError("vocab must be divisible by the TP size")
+        self.per = num_embeddings // P
+        self.lo = r * self.per
+        self.weight = nn.Parameter(torch.empty(self.per, embedding_dim))
+        self.weight._tp_shard_dim = 0
+        nn.init.normal_(self.weight, std=0.02)
+
+    def forward(self, ids):
+        local = ids - self.lo
+        mask = (local < 0) | (local >= self.per)
+        out = F.embedding(local.clamp(0, self.per - 1), self.weight)
+        out = out.masked_fill(mask[..., None], 0.0)
+        return reduce_from_tp(out, self.group)
+
+
+# ------------------------------------------------------------- model surgery
+def _shard(p: torch.Tensor, dim: int, P: int, r: int) -> nn.Parameter:
+    n = p.shape[dim]
+    if n % P:
+        raise ValueError(f"dimension {dim} of size {n} is not divisible by TP size {P}")
+    out = nn.Parameter(p.detach().narrow(dim, r * (n // P), n // P).clone(),
+                       requires_grad=p.requires_grad)
+    out._tp_shard_dim = dim
+    return out
+
+
+def make_parallel(model: nn.Module, group=None) -> nn.Module:
+    """Shard a full-weight ``ComplexityModel`` in place over ``group`` (default: TP group).
+
+    Load the full checkpoint first; each rank keeps its slice.  Embedding and
+    LM head stay replicated (their gradients are averaged by data parallelism
+    or are identical across TP ranks).
+    """
+    group = group if group is not None else _TP["group"]
+    P, r = tp_world(group), tp_rank(group)
+    if P == 1:
+        return model
+    initialize_tensor_parallel(group)
+    for layer in model.layers:
+        a = layer.self_attn
+        if a.num_heads % P:
+            raise ValueError("num_attention_heads must be divisible by the TP size")
+        D = a.head_dim
+        a.q_proj.weight = _shard(a.q_proj.weight, 0, P, r)
+        if a.num_kv_heads % P == 0:
+            a.k_proj.weight = _shard(a.k_proj.weight, 0, P, r)
+            a.v_proj.weight = _shard(a.v_proj.weight, 0, P, r)
+            a.num_kv_heads //= P
+        else:
+            # keep every KV head; this rank's q heads use the kv heads they map to
+            keep = a.num_kv_heads
+            per_q = a.num_heads // P
+            groups = a.num_heads // keep
+            first_kv = (r * per_q) // groups
+            last_kv = ((r + 1) * per_q - 1) // groups
+            n_kv = last_kv - first_kv + 1
+            if per_q % n_kv:
+                raise ValueError("KV heads cannot be assigned evenly to the TP ranks")
+            sl = slice(first_kv * D, (last_kv + 1) * D)
+            for name in ("k_proj", "v_proj"):
+                lin = getattr(a, name)
+                lin.weight = nn.Parameter(lin.weight.detach()[sl].clone())
+                lin.weight._tp_replicated_kv = True
+            a.num_kv_heads = n_kv
+        a.num_heads //= P
+        a.num_kv_groups = a.num_heads // a.num_kv_heads
+        a.o_proj.weight = _shard(a.o_proj.weight, 1, P, r)
+        a.tp_group = group
+        eng = getattr(layer.mlp, "engine", None)
+        if eng is not None:
+            cfg = eng.config
+            if cfg.expert_width % P or cfg.shared_width % P:
+                raise ValueError("expert and shared widths must be divisible by the TP size")
+            if eng.shared_gate is not None:
+                eng.shared_gate.weight = _shard(eng.shared_gate.weight, 0, P, r)
+                eng.shared_up.weight = _shard(eng.shared_up.weight, 0, P, r)
+                eng.shared_down.weight = _shard(eng.shared_down.weight, 1, P, r)
+            eng.expert_gate = _shard(eng.expert_gate, 2, P, r)
+            eng.expert_up = _shard(eng.expert_up, 2, P, r)
+            eng.expert_down = _shard(eng.expert_down, 1, P, r)
+            eng.config = replace(cfg, shared_width=cfg.shared_width // P,
+                                 expert_width=cfg.expert_width // P)
+            eng._active_expert_width = eng.config.expert_width
+            eng.tp_group = group
+    model.tp_group = group
+    return model
+
+
+def gather_tp_state_dict(model: nn.Module, group=None) -> dict:
+    """Full (unsharded) state dict from a TP-sharded model (collective over the TP group)."""
+    group = group if group is not None else getattr(model, "tp_group", _TP["group"])
+    P = tp_world(group)
+    shard_dims = {}
+    for name, p in model.named_parameters():
+        if hasattr(p, "_tp_shard_dim"):
+            shard_dims[name] = p._tp_shard_dim
+    out = {}
+    for name, t in model.state_dict().items():
+        if name in shard_dims and P > 1:
+            parts = [torch.empty_like(t) for _ in range(P)]
+            dist.all_gather(parts, t.contiguous(), group=group)
+            t = torch.cat(parts, shard_dims[name])
+        out[name] = t
+    return out

@@ -211,6 +211,21 @@ class TRHashEngine(nn.Module):
             g, u = self.shared_gate(flat_x), self.shared_up(flat_x)
         return self.shared_down(_silu_mul(g, u))
 
+    def _shared_ep(self, flat_x: torch.Tensor) -> torch.Tensor:
+        """shared_scale * shared SwiGLU; one fused gate|up + down GEMM pair on CUDA bf16."""
+        cfg = self.config
+        if self.shared_gate is None:
+            return torch.zeros_like(flat_x)
+        if (flat_x.is_cuda and flat_x.dtype == torch.bfloat16 and cfg.shared_width % 128 == 0
+                and self.shared_gate.weight.dtype == torch.bfloat16):
+            from ..ops import fused
+
+            w_gu = fused.pack_shared_gate_up(self.shared_gate.weight, self.shared_up.weight)
+            dummy = flat_x.new_zeros(1, dtype=torch.float32)
+            return fused.trhash_mlp(flat_x, w_gu, self.shared_down.weight, dummy, None,
+                                    cfg.shared_width, 32, 0, cfg.shared_output_scale)
+        return cfg.shared_output_scale * self._shared(flat_x)
+
     def refresh_fused_shared_lora_weight(self) -> bool:
         if not (getattr(self.shared_gate, "is_lora_adapter", False)
                 and getattr(self.shared_up, "is_lora_adapter", False)):
@@ -274,9 +289,16 @@ class TRHashEngine(nn.Module):
             raise ValueError(f"expected hidden size {self.config.hidden_size}, "
                              f"got {hidden_states.size(-1)}")
         B, S, H = hidden_states.shape
-        if backend is TRHashBackend.FUSED_CUDA:
+        ep = getattr(self, "ep", None)
+        if backend is TRHashBackend.FUSED_CUDA and ep is None:
             return self._fused_forward(hidden_states, token_ids, residual)
         flat = hidden_states.reshape(-1, H)
+        if ep is not None:
+            # expert parallel: shared SwiGLU locally, routed experts via all-to-all
+            routes = self._routes(token_ids).reshape(self.config.top_k, -1)
+            routed = ep(flat, routes, self._route_weights)
+            out = (self._shared_ep(flat) + self.config.routed_output_scale * routed).view(B, S, H)
+            return out if residual is None else residual + out
         shared = self._shared(flat)
         if backend is TRHashBackend.CGGR:
             routed = self._grouped_forward(flat, token_ids.reshape(-1))
@@ -306,6 +328,14 @@ class TRHashEngine(nn.Module):
                                        ("fused path computes in bf16; input is "
                                         f"{hidden_states.dtype}",), False, False)
         self.last_backend = decision
+        tp = getattr(self, "tp_group", None)
+        if tp is not None:
+            # tensor parallel: this rank holds a slice of every width; sum the slices
+            from ..parallel.tensor_parallel import copy_to_tp, reduce_from_tp
+
+            x = copy_to_tp(hidden_states, tp)
+            out = reduce_from_tp(self._forward_eager(x, token_ids, decision.selected), tp)
+            return out if residual is None else residual + out
         if decision.selected is TRHashBackend.CUDA_GRAPH:
             out = self._forward_cuda_graph(hidden_states, token_ids)
             return out if residual is None else residual + out

@@ -28,17 +28,22 @@ import torch
 
 def default_param_groups(model: torch.nn.Module, weight_decay: float) -> List[dict]:
     """Decay / no-decay split by name, as the reference trainer does."""
-    decay, no_decay = [], []
+    decay, no_decay, local = [], [], []
     for name, p in model.named_parameters():
         if not p.requires_grad:
             continue
-        if "bias" in name or "norm" in name or ".mu" in name:
+        if getattr(p, "_ep_local", False):
+            local.append(p)
+        elif "bias" in name or "norm" in name or ".mu" in name:
             no_decay.append(p)
         else:
             decay.append(p)
     groups = [{"params": decay, "weight_decay": weight_decay}]
     if no_decay:
         groups.append({"params": no_decay, "weight_decay": 0.0})
+    if local:
+        # expert-parallel shards: owned by one rank, not averaged over data parallel
+        groups.append({"params": local, "weight_decay": weight_decay, "dp_reduce": False})
     return groups
 
 
@@ -119,9 +124,10 @@ class FusedAdamW(torch.optim.Optimizer):
             if not ps:
                 self._flat.append(None)
                 continue
+            shard = self.sharded and group.get("dp_reduce", True)
             fg = _FlatGroup(ps, compute_dtype or ps[0].dtype,
-                            world=self.world if self.sharded else 1,
-                            rank=self.rank if self.sharded else 0)
+                            world=self.world if shard else 1, rank=self.rank if shard else 0)
+            fg.dp_reduce = group.get("dp_reduce", True)
             self._flat.append(fg)
             for i, p in enumerate(ps):
                 st = {"step": torch.zeros((), dtype=torch.float32)}
@@ -135,6 +141,7 @@ class FusedAdamW(torch.optim.Optimizer):
         self._sumsq = torch.zeros(1, device=dev, dtype=torch.float32)
         self._clip = torch.ones(1, device=dev, dtype=torch.float32)
         self._norm = torch.zeros(1, device=dev, dtype=torch.float32)
+        self._sq_distinct = None
 
     # ----------------------------------------------------------- flat access
     @property
@@ -160,7 +167,12 @@ class FusedAdamW(torch.optim.Optimizer):
         avg = dist.get_backend(self.process_group) == "nccl"
         op = dist.ReduceOp.AVG if avg else dist.ReduceOp.SUM
         for fg in self.flat_groups:
-            if self.sharded:
+            if not fg.dp_reduce:
+                # rank-local parameters (expert-parallel shards): loss is a mean
+                # over this rank's tokens, the global loss a mean over ranks
+                fg.grad.div_(self.world)
+                continue
+            if fg.world > 1:
                 dist.reduce_scatter_tensor(fg.grad_shard, fg.grad, op=op, group=self.process_group)
                 out = fg.grad_shard
             else:
@@ -179,10 +191,19 @@ class FusedAdamW(torch.optim.Optimizer):
 
     # ------------------------------------------------------------- clipping
     def _allreduce_sumsq(self) -> None:
-        if self.sharded:
-            import torch.distributed as dist
+        """Sum the squared-norm partials of rank-distinct gradient pieces over ranks.
 
-            dist.all_reduce(self._sumsq, op=dist.ReduceOp.SUM, group=self.process_group)
+        Sharded groups and expert-parallel groups hold different elements on
+        each rank; replicated groups (plain data parallel) hold identical
+        gradients and are counted once.
+        """
+        if self.world == 1:
+            return
+        import torch.distributed as dist
+
+        if self._sq_distinct is not None:
+            dist.all_reduce(self._sq_distinct, op=dist.ReduceOp.SUM, group=self.process_group)
+            self._sumsq.add_(self._sq_distinct)
 
     @torch.no_grad()
     def clip_grad_norm_(self, max_norm: float) -> torch.Tensor:
@@ -193,13 +214,19 @@ class FusedAdamW(torch.optim.Optimizer):
 
             C = require()
             self._sumsq.zero_()
+            self._sq_distinct = None if self.world == 1 else torch.zeros_like(self._sumsq)
             for fg in self.flat_groups:
-                C.sumsq_bf16(fg.grad_shard, self._sumsq)
+                distinct = self.world > 1 and (fg.world > 1 or not fg.dp_reduce)
+                C.sumsq_bf16(fg.grad_shard, self._sq_distinct if distinct else self._sumsq)
             self._allreduce_sumsq()
             C.clip_coef(self._sumsq, float(max_norm), self._clip, self._norm)
         else:
-            sq = sum((fg.grad_shard.float() ** 2).sum() for fg in self.flat_groups)
-            self._sumsq.copy_(torch.as_tensor(sq, dtype=torch.float32).reshape(1))
+            self._sumsq.zero_()
+            self._sq_distinct = None if self.world == 1 else torch.zeros_like(self._sumsq)
+            for fg in self.flat_groups:
+                distinct = self.world > 1 and (fg.world > 1 or not fg.dp_reduce)
+                target = self._sq_distinct if distinct else self._sumsq
+                target.add_((fg.grad_shard.float() ** 2).sum())
             self._allreduce_sumsq()
             self._norm.copy_(torch.sqrt(self._sumsq))
             if max_norm > 0:
@@ -237,7 +264,7 @@ class FusedAdamW(torch.optim.Optimizer):
                 denom = (fg.exp_avg_sq.sqrt() / math.sqrt(bc2)).add_(eps)
                 fg.master.addcdiv_(fg.exp_avg, denom, value=-lr / bc1)
                 fg.compute_shard.copy_(fg.master)
-            if self.sharded:
+            if fg.world > 1:
                 import torch.distributed as dist
 
                 dist.all_gather_into_tensor(fg.compute, fg.compute_shard,
@@ -280,7 +307,7 @@ class FusedAdamW(torch.optim.Optimizer):
         with torch.no_grad():
             for fg in self.flat_groups:
                 fg.compute_shard.copy_(fg.master)
-                if self.sharded:
+                if fg.world > 1:
                     import torch.distributed as dist
 
                     dist.all_gather_into_tensor(fg.compute, fg.compute_shard,

@@ -1,0 +1,162 @@
+"""Multi-process (gloo, CPU) checks of tensor, pipeline, expert and ZeRO-2 data parallelism.
+
+Every parallel run is compared with a single-process run of the same model,
+weights and data.
+"""
+import copy
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from complexity_framework_b200 import ComplexityModel, ModelConfig
+
+CFG = dict(hidden_size=64, num_hidden_layers=4, num_attention_heads=4, num_key_value_heads=2,
+           vocab_size=256, intermediate_size=128, shared_intermediate_size=128, num_experts=4,
+           top_k=2, routing_strategy="token_id_multi_hash", max_position_embeddings=64)
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _run(world, fn, *args):
+    port = _port()
+    ctx = mp.get_context("spawn")
+    with tempfile.TemporaryDirectory() as d:
+        procs = [ctx.Process(target=_entry, args=(r, world, port, fn, d) + args)
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(180)
+        codes = [p.exitcode for p in procs]
+        assert all(c == 0 for c in codes), codes
+
+
+def _entry(rank, world, port, fn, tmp, *args):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.manual_seed(0)
+    try:
+        fn(rank, world, tmp, *args)
+    finally:
+        dist.destroy_process_group()
+
+
+def _model():
+    torch.manual_seed(0)
+    return ComplexityModel(ModelConfig(**CFG))
+
+
+def _ids(n=2, s=16, seed=1):
+    return torch.randint(0, 256, (n, s), generator=torch.Generator().manual_seed(seed))
+
+
+def _tp_body(rank, world, tmp):
+    from complexity_framework_b200.parallel import gather_tp_state_dict, make_parallel
+
+    ref = _model()
+    ids = _ids()
+    l_ref = ref.loss(ids)
+    l_ref.backward()
+    m = make_parallel(_model(), dist.group.WORLD)
+    loss = m.loss(ids)
+    loss.backward()
+    assert torch.allclose(loss, l_ref, atol=1e-5), (loss, l_ref)
+    # gradient of a sharded weight matches the matching slice of the full gradient
+    a_ref = ref.layers[1].self_attn.q_proj.weight.grad
+    a = m.layers[1].self_attn.q_proj.weight.grad
+    rows = a.shape[0]
+    assert torch.allclose(a, a_ref[rank * rows:(rank + 1) * rows], atol=1e-5)
+    e_ref = ref.layers[0].mlp.engine.expert_down.grad
+    e = m.layers[0].mlp.engine.expert_down.grad
+    w = e.shape[1]
+    assert torch.allclose(e, e_ref[:, rank * w:(rank + 1) * w], atol=1e-5)
+    # replicated embedding grads are complete on every rank (input-grad all-reduce works)
+    assert torch.allclose(m.embed_tokens.weight.grad, ref.embed_tokens.weight.grad, atol=1e-5)
+    full = gather_tp_state_dict(m)
+    for k, v in ref.state_dict().items():
+        assert torch.allclose(full[k].float(), v.float()), k
+
+
+def test_tensor_parallel_matches_single():
+    _run(2, _tp_body)
+
+
+def _pp_body(rank, world, tmp, schedule):
+    from complexity_framework_b200.parallel import PipelineModel
+
+    ref = _model()
+    ids = _ids(4)
+    mbs = list(ids.chunk(4))
+    l_ref = sum(ref.loss(mb) for mb in mbs) / 4
+    l_ref.backward()
+    pm = PipelineModel(_model(), schedule=schedule)
+    loss = pm.train_step(mbs)
+    if pm.last:
+        assert torch.allclose(loss, l_ref, atol=1e-5), (loss, l_ref)
+    for layer in pm.stage.layers:
+        g = layer.self_attn.o_proj.weight.grad
+        g_ref = ref.layers[layer.layer_idx].self_attn.o_proj.weight.grad
+        assert torch.allclose(g, g_ref, atol=1e-5)
+    tied = pm.stage.embed_tokens.weight.grad if pm.first else pm.stage.head_weight.grad
+    assert torch.allclose(tied, ref.embed_tokens.weight.grad, atol=1e-5)
+
+
+@pytest.mark.parametrize("schedule", ["1f1b", "gpipe"])
+def test_pipeline_matches_single(schedule):
+    _run(2, _pp_body, schedule)
+
+
+def _ep_body(rank, world, tmp):
+    from complexity_framework_b200.parallel import make_expert_parallel
+
+    ref = _model()
+    ids_all = _ids(4, seed=3)
+    l_ref = ref.loss(ids_all)
+    l_ref.backward()
+    m = make_expert_parallel(_model(), dist.group.WORLD)
+    ids = ids_all.chunk(world)[rank]
+    loss = m.loss(ids)
+    (loss / world).backward()
+    t = loss.detach().clone()
+    dist.all_reduce(t)
+    assert torch.allclose(t / world, l_ref, atol=1e-5)
+    ep = m.layers[2].mlp.engine.ep
+    g_ref = ref.layers[2].mlp.engine.expert_gate.grad[ep.lo:ep.lo + ep.E_local]
+    assert torch.allclose(ep.expert_gate.grad, g_ref, atol=1e-5)
+
+
+def test_expert_parallel_matches_single():
+    _run(2, _ep_body)
+
+
+def _zero_body(rank, world, tmp, mode):
+    from complexity_framework_b200.training import Trainer, TrainingConfig
+
+    ids_all = _ids(4, seed=7)
+    cfg = TrainingConfig(learning_rate=1e-3, warmup_steps=0, lr_scheduler="constant",
+                         precision="fp32", distributed_mode=mode, checkpoint_dir=tmp)
+    single = Trainer(_model(), cfg, device="cpu", process_group=dist.new_group([rank]))
+    for _ in range(3):
+        single.train_step(ids_all)
+    tr = Trainer(_model(), cfg, device="cpu")
+    for _ in range(3):
+        tr.train_step(ids_all.chunk(world)[rank])
+    for (n, p), q in zip(tr.model.named_parameters(), single.model.parameters()):
+        assert torch.allclose(p, q, atol=2e-5), n
+
+
+@pytest.mark.parametrize("mode", ["ddp", "fsdp"])
+def test_data_parallel_matches_single(mode):
+    _run(2, _zero_body, mode)
