@@ -9,6 +9,7 @@
 #include <mutex>
 #include <unordered_map>
 
+#include "flash.h"
 #include "gemm_tc.h"
 #include "kernels.h"
 
@@ -177,6 +178,32 @@ void gemm(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, 
   raise_rc(rc, "gemm");
 }
 
+// Causal/full attention forward; writes out [B,S,Hq*D] and lse [B,Hq,S].
+void flash_attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
+                    torch::Tensor& out, torch::Tensor& lse, double scale, bool causal) {
+  check_bf16_cuda(q, "q");
+  check_bf16_cuda(k, "k");
+  check_bf16_cuda(v, "v");
+  check_bf16_cuda(out, "out");
+  TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && out.is_contiguous(),
+              "flash_attn_fwd: tensors must be contiguous");
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.sizes() == k.sizes(), "q/k/v must be [B,H,S,D]");
+  const int64_t B = q.size(0), Hq = q.size(1), S = q.size(2), D = q.size(3), Hkv = k.size(1);
+  TORCH_CHECK(k.size(0) == B && k.size(2) == S && k.size(3) == D, "k shape");
+  TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128");
+  TORCH_CHECK(Hq % Hkv == 0, "Hq must be a multiple of Hkv");
+  TORCH_CHECK(out.numel() == B * S * Hq * D, "out size");
+  TORCH_CHECK(lse.scalar_type() == torch::kFloat32 && lse.is_contiguous() &&
+                  lse.numel() == B * Hq * S,
+              "lse must be fp32 [B,Hq,S]");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int rc = cfb::flash_fwd_launch(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                       lse.data_ptr<float>(), B, Hq, Hkv, S, D,
+                                       static_cast<float>(scale), causal,
+                                       at::cuda::getCurrentCUDAStream(), err_ptr(q.get_device()));
+  raise_rc(rc, "flash_attn_fwd");
+}
+
 int64_t gemm_choose_bn(int64_t M, int64_t N, int64_t device) {
   return cfb::choose_bn(static_cast<int>(M), static_cast<int>(N), num_sms(static_cast<int>(device)));
 }
@@ -195,5 +222,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("expert_width") = 0, py::arg("n_experts") = 0, py::arg("shared_scale") = 1.0,
         py::arg("stats") = py::none(), py::arg("bn") = 0);
   m.def("gemm_choose_bn", &gemm_choose_bn);
+  m.def("flash_attn_fwd", &flash_attn_fwd);
   register_elementwise(m);
 }

@@ -13,15 +13,19 @@ import torch.nn.functional as F
 from ._ext import load
 
 
-def _kernel_available() -> bool:
+def _kernel_available(needs_grad: bool) -> bool:
     C = load()
-    return C is not None and hasattr(C, "flash_attn_fwd")
+    if C is None or not hasattr(C, "flash_attn_fwd"):
+        return False
+    return hasattr(C, "flash_attn_bwd") or not needs_grad
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: bool = True,
               scale: float) -> torch.Tensor:
     B, Hq, S, D = q.shape
-    if _kernel_available():
+    needs_grad = torch.is_grad_enabled() and (q.requires_grad or k.requires_grad
+                                              or v.requires_grad)
+    if q.shape[-1] in (64, 128) and _kernel_available(needs_grad):
         from .flash import flash_attention
 
         return flash_attention(q, k, v, causal=causal, scale=scale)

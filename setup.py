@@ -16,6 +16,7 @@ SOURCES = [
     "bind_elementwise.cpp",
     "gemm_tc.cu",
     "elementwise.cu",
+    "flash_fwd.cu",
 ]
 
 NVCC_FLAGS = [
