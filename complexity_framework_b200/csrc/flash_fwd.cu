@@ -244,15 +244,21 @@ __global__ void __launch_bounds__(FlashCfg<D>::THREADS, 1)
       const int k0 = j * kKT;
       int kmax = S - k0;   // keys valid for this row: < S and (causal) <= qpos
       if (causal) kmax = min(kmax, qpos - k0 + 1);
+      const bool full = kmax >= kKT;  // interior tile: no masking needed
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < kKT; c += 32) {
         float v[32];
         tmem_ld32(t_s + c, v);
         tmem_wait_ld();
+        if (full) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c + i < kmax) mx = fmaxf(mx, v[i]);
+          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c + i < kmax) mx = fmaxf(mx, v[i]);
+        }
       }
       const float m_new = fmaxf(m, mx * scale_log2);
       const float alpha = (m == -INFINITY) ? 0.f : ex2(m - m_new);
@@ -283,23 +289,28 @@ __global__ void __launch_bounds__(FlashCfg<D>::THREADS, 1)
         tmem_ld32(t_s + c, v);
         tmem_wait_ld();
         uint32_t pk[16];
+        if (full) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float p0 = (c + i < kmax) ? ex2(v[i] * scale_log2 - msub) : 0.f;
-          const float p1 = (c + i + 1 < kmax) ? ex2(v[i + 1] * scale_log2 - msub) : 0.f;
-          // the row sum uses the bf16-rounded values the PV product sees
-          const uint32_t w = pack_bf16x2(p0, p1);
-          const float2 back = unpack_bf16x2(w);
-          rs += back.x + back.y;
-          pk[i / 2] = w;
+          for (int i = 0; i < 32; i += 2) {
+            const float p0 = ex2(v[i] * scale_log2 - msub);
+            const float p1 = ex2(v[i + 1] * scale_log2 - msub);
+            rs += p0 + p1;
+            pk[i / 2] = pack_bf16x2(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const float p0 = (c + i < kmax) ? ex2(v[i] * scale_log2 - msub) : 0.f;
+            const float p1 = (c + i + 1 < kmax) ? ex2(v[i + 1] * scale_log2 - msub) : 0.f;
+            rs += p0 + p1;
+            pk[i / 2] = pack_bf16x2(p0, p1);
+          }
         }
         uint8_t* chunk = pt + (c >> 6) * (kQT * 128);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int col = (c & 63) + u * 8;
-          *reinterpret_cast<uint4*>(chunk + sw128_off(r, col)) =
+        for (int u = 0; u < 4; ++u)
+          *reinterpret_cast<uint4*>(chunk + sw128_off(r, (c & 63) + u * 8)) =
               make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-        }
       }
       // S_j has been read: the MMA warp may overwrite this buffer
       tc_fence_before();
