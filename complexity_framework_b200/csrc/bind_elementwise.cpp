@@ -210,6 +210,37 @@ void clip_coef(const torch::Tensor& sumsq, double max_norm, torch::Tensor& clip,
                  cur());
 }
 
+void paged_attention(const torch::Tensor& q, const torch::Tensor& k_pool,
+                     const torch::Tensor& v_pool, const torch::Tensor& page_table,
+                     const torch::Tensor& cu_q, const torch::Tensor& kv_lens, torch::Tensor& out,
+                     double scale, int64_t max_q_len) {
+  chk(q, torch::kBFloat16, "q");
+  chk(k_pool, torch::kBFloat16, "k_pool");
+  chk(v_pool, torch::kBFloat16, "v_pool");
+  chk(page_table, torch::kInt32, "page_table");
+  chk(cu_q, torch::kInt32, "cu_q");
+  chk(kv_lens, torch::kInt32, "kv_lens");
+  chk(out, torch::kBFloat16, "out");
+  TORCH_CHECK(q.dim() == 3 && k_pool.dim() == 4 && v_pool.sizes() == k_pool.sizes(),
+              "q [N,Hq,D], pools [pages,page,Hkv,D]");
+  const int64_t N = q.size(0), Hq = q.size(1), D = q.size(2);
+  const int64_t page = k_pool.size(1), Hkv = k_pool.size(2);
+  TORCH_CHECK(k_pool.size(3) == D && Hq % Hkv == 0, "head shapes");
+  const int64_t num_seqs = kv_lens.numel();
+  TORCH_CHECK(cu_q.numel() == num_seqs + 1 && page_table.size(0) == num_seqs, "batch metadata");
+  TORCH_CHECK(out.sizes() == q.sizes(), "out shape");
+  (void)max_q_len;
+  const c10::cuda::CUDAGuard g(q.device());
+  const int rc = cfb::paged_attention(P<bf16>(q), P<bf16>(k_pool), P<bf16>(v_pool),
+                                      P<int32_t>(page_table), P<int32_t>(cu_q),
+                                      P<int32_t>(kv_lens), P<bf16>(out), static_cast<int>(N),
+                                      static_cast<int>(num_seqs),
+                                      static_cast<int>(page_table.size(1)), static_cast<int>(Hq),
+                                      static_cast<int>(Hkv), static_cast<int>(D),
+                                      static_cast<int>(page), static_cast<float>(scale), cur());
+  TORCH_CHECK(rc == 0, "paged_attention failed with code ", rc);
+}
+
 }  // namespace
 
 void register_elementwise(pybind11::module& m) {
@@ -224,4 +255,5 @@ void register_elementwise(pybind11::module& m) {
   m.def("adamw_flat", &adamw_flat);
   m.def("sumsq_bf16", &sumsq_bf16);
   m.def("clip_coef", &clip_coef);
+  m.def("paged_attention", &paged_attention);
 }

@@ -52,4 +52,12 @@ void sumsq_bf16(const bf16* g, int64_t n, float* out, cudaStream_t s);
 // clip = min(1, max_norm / (sqrt(sumsq) + 1e-6)); norm = sqrt(sumsq).
 void clip_coef(const float* sumsq, float max_norm, float* clip, float* norm, cudaStream_t s);
 
+// Causal attention of ragged new-token queries q [N,Hq,D] over paged K/V pools
+// [pages, page_size, Hkv, D]; page_table [num_seqs, max_pages], cu_q [num_seqs+1],
+// kv_lens [num_seqs] (int32).  Writes out [N,Hq,D].
+int paged_attention(const bf16* q, const bf16* k_pool, const bf16* v_pool,
+                    const int32_t* page_table, const int32_t* cu_q, const int32_t* kv_lens,
+                    bf16* out, int N, int num_seqs, int max_pages, int Hq, int Hkv, int D,
+                    int page_size, float scale, cudaStream_t s);
+
 }  // namespace cfb

@@ -127,6 +127,21 @@ class PagedBatch:
             table[i, :len(pg)] = torch.tensor(pg, dtype=torch.int32)
         self.page_table = table.to(dev)
         self._cu_host = cu
+        # chunks that start a sequence run dense causal flash attention over the
+        # chunk itself; the others (decode tokens, continued prefill) read pages
+        self.fresh = [i for i, c in enumerate(self.chunks) if c.start == 0 and c.length > 1]
+        paged = [i for i in range(len(self.chunks)) if i not in set(self.fresh)]
+        self.paged = paged
+        tok_idx, pcu = [], [0]
+        for i in paged:
+            tok_idx.extend(range(cu[i], cu[i + 1]))
+            pcu.append(pcu[-1] + self.chunks[i].length)
+        self.paged_tokens = torch.tensor(tok_idx, dtype=torch.long, device=dev)
+        self.paged_cu = torch.tensor(pcu, dtype=torch.int32, device=dev)
+        sel = torch.tensor(paged, dtype=torch.long)
+        self.paged_table = table[sel].contiguous().to(dev) if paged else None
+        self.paged_kv_lens = (torch.tensor([self.chunks[i].start + self.chunks[i].length
+                                            for i in paged], dtype=torch.int32, device=dev))
 
     def commit(self) -> None:
         """Advance the recorded sequence lengths after the forward step."""
@@ -148,13 +163,31 @@ class PagedBatch:
 
         C = load()
         P = self.pool
-        if (q.is_cuda and C is not None and hasattr(C, "paged_attention")
-                and q.dtype == torch.bfloat16 and P.dtype == torch.bfloat16):
-            out = torch.empty_like(q)
-            C.paged_attention(q.contiguous(), P.k[layer], P.v[layer], self.page_table, self.cu_q,
-                              self.kv_lens, out, float(scale), int(self.max_q_len()))
-            return out
-        return self._attend_reference(layer, q, scale)
+        D = q.shape[-1]
+        if not (q.is_cuda and C is not None and hasattr(C, "paged_attention")
+                and q.dtype == torch.bfloat16 and P.dtype == torch.bfloat16 and D in (64, 128)):
+            return self._attend_reference(layer, q, scale)
+        from ..ops.flash import flash_forward
+
+        out = torch.empty_like(q)
+        Hq, Hkv = q.shape[1], P.num_kv_heads
+        for i in self.fresh:
+            a, e = self._cu_host[i], self._cu_host[i + 1]
+            # the chunk's own K/V were just written; take them from the pool slots
+            slots = self.slots[a:e]
+            kf = P.k[layer].view(-1, Hkv, D).index_select(0, slots)
+            vf = P.v[layer].view(-1, Hkv, D).index_select(0, slots)
+            o, _ = flash_forward(q[a:e].transpose(0, 1)[None].contiguous(),
+                                 kf.transpose(0, 1)[None].contiguous(),
+                                 vf.transpose(0, 1)[None].contiguous(), True, scale)
+            out[a:e] = o.view(e - a, Hq, D)
+        if self.paged:
+            qs = q.index_select(0, self.paged_tokens).contiguous()
+            os_ = torch.empty_like(qs)
+            C.paged_attention(qs, P.k[layer], P.v[layer], self.paged_table, self.paged_cu,
+                              self.paged_kv_lens, os_, float(scale), int(self.max_q_len()))
+            out.index_copy_(0, self.paged_tokens, os_)
+        return out
 
     def max_q_len(self) -> int:
         return max((c.length for c in self.chunks), default=1)

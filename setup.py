@@ -17,6 +17,7 @@ SOURCES = [
     "gemm_tc.cu",
     "elementwise.cu",
     "flash_fwd.cu",
+    "paged_attn.cu",
 ]
 
 NVCC_FLAGS = [
