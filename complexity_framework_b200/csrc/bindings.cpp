@@ -7,8 +7,10 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include <mutex>
+#include <vector>
 #include <unordered_map>
 
+#include "dist_fused.h"
 #include "flash.h"
 #include "gemm_tc.h"
 #include "kernels.h"
@@ -204,6 +206,64 @@ void flash_attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch:
   raise_rc(rc, "flash_attn_fwd");
 }
 
+cfb::PeerPtrs make_peers(const std::vector<int64_t>& grad, const std::vector<int64_t>& param,
+                         const std::vector<int64_t>& pad, const std::vector<int64_t>& slots,
+                         int64_t rank) {
+  const size_t P = grad.size();
+  TORCH_CHECK(P >= 1 && P <= static_cast<size_t>(cfb::kMaxRanks), "1..8 ranks supported");
+  TORCH_CHECK(param.size() == P && pad.size() == P && slots.size() == P, "peer pointer lists");
+  cfb::PeerPtrs pp{};
+  for (size_t i = 0; i < P; ++i) {
+    pp.grad[i] = reinterpret_cast<const __nv_bfloat16*>(grad[i]);
+    pp.param[i] = reinterpret_cast<__nv_bfloat16*>(param[i]);
+    pp.pad[i] = reinterpret_cast<int*>(pad[i]);
+    pp.slots[i] = reinterpret_cast<float*>(slots[i]);
+  }
+  pp.world = static_cast<int>(P);
+  pp.rank = static_cast<int>(rank);
+  return pp;
+}
+
+// Reduce this rank's shard of the flat gradients of all peers (NVLink loads).
+void dp_reduce_shard(const std::vector<int64_t>& grad, const std::vector<int64_t>& param,
+                     const std::vector<int64_t>& pad, const std::vector<int64_t>& slots,
+                     int64_t rank, int64_t lo, int64_t n, torch::Tensor& gs,
+                     torch::Tensor& sumsq_local, torch::Tensor& ticket, int64_t epoch,
+                     bool publish) {
+  TORCH_CHECK(gs.is_cuda() && gs.scalar_type() == torch::kFloat32 && gs.numel() >= n, "gs");
+  const c10::cuda::CUDAGuard guard(gs.device());
+  const auto pp = make_peers(grad, param, pad, slots, rank);
+  const int rc = cfb::fused_reduce_shard(pp, lo, n, gs.data_ptr<float>(),
+                                         sumsq_local.data_ptr<float>(), ticket.data_ptr<int>(),
+                                         static_cast<int>(epoch), publish,
+                                         num_sms(gs.get_device()),
+                                         at::cuda::getCurrentCUDAStream(), err_ptr(gs.get_device()));
+  raise_rc(rc, "dp_reduce_shard");
+}
+
+// AdamW on the shard and store the new bf16 parameters into every peer.
+void dp_adamw_shard(const std::vector<int64_t>& grad, const std::vector<int64_t>& param,
+                    const std::vector<int64_t>& pad, const std::vector<int64_t>& slots,
+                    int64_t rank, int64_t lo, int64_t n, torch::Tensor& master, torch::Tensor& m,
+                    torch::Tensor& v, const torch::Tensor& gs, double lr, double b1, double b2,
+                    double eps, double wd, double bc1, double bc2, double max_norm,
+                    torch::Tensor& norm_out, torch::Tensor& ticket, int64_t epoch) {
+  for (const auto* t : {&master, &m, &v}) {
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat32 && t->numel() >= n,
+                "fp32 optimizer shard");
+  }
+  const c10::cuda::CUDAGuard guard(master.device());
+  const auto pp = make_peers(grad, param, pad, slots, rank);
+  const int rc = cfb::fused_adamw_shard(
+      pp, lo, n, master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+      gs.data_ptr<float>(), static_cast<float>(lr), static_cast<float>(b1),
+      static_cast<float>(b2), static_cast<float>(eps), static_cast<float>(wd),
+      static_cast<float>(bc1), static_cast<float>(bc2), static_cast<float>(max_norm),
+      norm_out.data_ptr<float>(), ticket.data_ptr<int>(), static_cast<int>(epoch),
+      num_sms(master.get_device()), at::cuda::getCurrentCUDAStream(), err_ptr(master.get_device()));
+  raise_rc(rc, "dp_adamw_shard");
+}
+
 int64_t gemm_choose_bn(int64_t M, int64_t N, int64_t device) {
   return cfb::choose_bn(static_cast<int>(M), static_cast<int>(N), num_sms(static_cast<int>(device)));
 }
@@ -223,5 +283,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("stats") = py::none(), py::arg("bn") = 0);
   m.def("gemm_choose_bn", &gemm_choose_bn);
   m.def("flash_attn_fwd", &flash_attn_fwd);
+  m.def("dp_reduce_shard", &dp_reduce_shard);
+  m.def("dp_adamw_shard", &dp_adamw_shard);
   register_elementwise(m);
 }

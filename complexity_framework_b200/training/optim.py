@@ -21,6 +21,7 @@ buffer is all-gathered.
 from __future__ import annotations
 
 import math
+import os
 from typing import Dict, List, Optional
 
 import torch
@@ -106,7 +107,8 @@ class _FlatGroup:
 class FusedAdamW(torch.optim.Optimizer):
     def __init__(self, params, lr: float = 3e-4, betas=(0.9, 0.95), eps: float = 1e-8,
                  weight_decay: float = 0.1, compute_dtype: Optional[torch.dtype] = None,
-                 process_group=None, shard_state: bool = False):
+                 process_group=None, shard_state: bool = False,
+                 fused_collectives: Optional[bool] = None):
         defaults = dict(lr=lr, betas=tuple(betas), eps=eps, weight_decay=weight_decay)
         super().__init__(params, defaults)
         import torch.distributed as dist
@@ -142,6 +144,12 @@ class FusedAdamW(torch.optim.Optimizer):
         self._clip = torch.ones(1, device=dev, dtype=torch.float32)
         self._norm = torch.zeros(1, device=dev, dtype=torch.float32)
         self._sq_distinct = None
+        self._max_norm = 0.0
+        self._fused = None
+        if fused_collectives is None:
+            fused_collectives = os.environ.get("CFB_FUSED_DP", "1") != "0"
+        if fused_collectives and self._fused_eligible():
+            self._fused = _FusedDP(self)
 
     # ----------------------------------------------------------- flat access
     @property
@@ -160,7 +168,7 @@ class FusedAdamW(torch.optim.Optimizer):
     @torch.no_grad()
     def reduce_gradients(self) -> None:
         """Average gradients over the data-parallel group (one collective per group)."""
-        if self.world == 1:
+        if self.world == 1 or self._fused is not None:
             return
         import torch.distributed as dist
 
@@ -180,6 +188,20 @@ class FusedAdamW(torch.optim.Optimizer):
                 out = fg.grad
             if not avg:
                 out.div_(self.world)
+
+    def _fused_eligible(self) -> bool:
+        """NVLink-fused reduce + AdamW: sharded, NCCL, one GPU per rank, <= 8 ranks."""
+        import torch.distributed as dist
+
+        if not (self.sharded and 1 < self.world <= 8 and self._use_kernels()):
+            return False
+        if any(not (fg.dp_reduce and fg.world > 1) for fg in self.flat_groups):
+            return False  # mixed replicated / rank-local groups use the NCCL path
+        if dist.get_backend(self.process_group) != "nccl":
+            return False
+        from ..ops import require
+
+        return hasattr(require(), "dp_reduce_shard")
 
     def _use_kernels(self) -> bool:
         fg = self.flat_groups[0] if self.flat_groups else None
@@ -209,6 +231,9 @@ class FusedAdamW(torch.optim.Optimizer):
     def clip_grad_norm_(self, max_norm: float) -> torch.Tensor:
         """Compute the global grad norm on the device; the next ``step(clip=True)``
         scales by ``min(1, max_norm / (norm + 1e-6))``.  Returns the norm (no sync)."""
+        self._max_norm = float(max_norm)
+        if self._fused is not None:
+            return self._norm[0]  # computed inside the fused reduce kernels during step()
         if self._use_kernels():
             from ..ops import require
 
@@ -241,6 +266,9 @@ class FusedAdamW(torch.optim.Optimizer):
         loss = closure() if closure is not None else None
         self._step_count += 1
         t = self._step_count
+        if self._fused is not None:
+            self._fused.step(t, self._max_norm if clip else 0.0)
+            return loss
         kernels = self._use_kernels()
         if kernels:
             from ..ops import require
@@ -313,3 +341,79 @@ class FusedAdamW(torch.optim.Optimizer):
                     dist.all_gather_into_tensor(fg.compute, fg.compute_shard,
                                                 group=self.process_group)
                 fg.rebind()
+
+
+class _FusedDP:
+    """Symmetric-memory buffers and epochs for the fused NVLink reduce + AdamW kernels.
+
+    The flat bf16 gradient and parameter buffers of every group are moved into
+    symmetric memory (torch's symmetric-memory allocator is used only to map
+    the peers' buffers); the kernels are ``csrc/dist_fused.cu``.
+    """
+
+    def __init__(self, opt: "FusedAdamW"):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        self.opt = opt
+        pg = opt.process_group or dist.group.WORLD
+        self.rank = dist.get_rank(pg)
+        self.groups = []
+        for fg in opt.flat_groups:
+            if not (fg.dp_reduce and fg.world > 1):
+                continue
+            grad = symm.empty(fg.numel, dtype=fg.grad.dtype, device=fg.grad.device)
+            param = symm.empty(fg.numel, dtype=fg.compute.dtype, device=fg.compute.device)
+            grad.zero_()
+            param.copy_(fg.compute)
+            fg.grad, fg.compute = grad, param
+            fg.rebind()
+            hg = symm.rendezvous(grad, pg)
+            hp = symm.rendezvous(param, pg)
+            ctrl = symm.empty(64, dtype=torch.int32, device=fg.grad.device)
+            ctrl.zero_()
+            hc = symm.rendezvous(ctrl, pg)
+            torch.cuda.synchronize()
+            dist.barrier(group=pg)
+
+            def peer(h, t):
+                off = t.data_ptr() - h.buffer_ptrs[h.rank]
+                return [int(b) + off for b in h.buffer_ptrs]
+
+            pads = peer(hc, ctrl)
+            slots = [p + 3 * 8 * 4 for p in pads]  # floats after 3 rounds x 8 ranks of ints
+            self.groups.append(dict(
+                fg=fg, grad=peer(hg, grad), param=peer(hp, param), pad=pads, slots=slots,
+                gs=torch.empty(fg.shard, device=grad.device, dtype=torch.float32),
+                handles=(hg, hp, hc), ctrl=ctrl))
+        dev = opt.flat_groups[0].compute.device
+        self.sumsq = torch.zeros(1, device=dev, dtype=torch.float32)
+        self.ticket = torch.zeros(2, device=dev, dtype=torch.int32)
+
+    def step(self, t: int, max_norm: float) -> None:
+        from ..ops import require
+
+        C = require()
+        opt = self.opt
+        base = t * 16
+        # reduce every group first: the partial norms of all groups accumulate in
+        # one counter; the last group's last block publishes the total
+        for i, g in enumerate(self.groups):
+            fg = g["fg"]
+            C.dp_reduce_shard(g["grad"], g["param"], g["pad"], g["slots"], self.rank, fg.lo,
+                              fg.shard, g["gs"], self.sumsq, self.ticket[0:1], base + i + 1,
+                              i == len(self.groups) - 1)
+        for i, g in enumerate(self.groups):
+            fg = g["fg"]
+            group = next(gr for gr, f in zip(opt.param_groups, opt._flat) if f is fg)
+            b1, b2 = group["betas"]
+            C.dp_adamw_shard(g["grad"], g["param"], g["pad"], g["slots"], self.rank, fg.lo,
+                             fg.shard, fg.master, fg.exp_avg, fg.exp_avg_sq, g["gs"],
+                             group["lr"], b1, b2, group["eps"], group["weight_decay"],
+                             1.0 - b1 ** t, 1.0 - b2 ** t, max_norm, opt._norm,
+                             self.ticket[1:2], base + i + 1)
+        for p_group, fg in zip(opt.param_groups, opt._flat):
+            if fg is None:
+                continue
+            for p in fg.params:
+                opt.state[p]["step"].fill_(t)

@@ -18,6 +18,7 @@ SOURCES = [
     "elementwise.cu",
     "flash_fwd.cu",
     "paged_attn.cu",
+    "dist_fused.cu",
 ]
 
 NVCC_FLAGS = [
