@@ -230,10 +230,12 @@ void dp_reduce_shard(const std::vector<int64_t>& grad, const std::vector<int64_t
                      int64_t rank, int64_t lo, int64_t n, torch::Tensor& gs,
                      torch::Tensor& sumsq_local, torch::Tensor& ticket, int64_t epoch,
                      bool publish) {
-  TORCH_CHECK(gs.is_cuda() && gs.scalar_type() == torch::kFloat32 && gs.numel() >= n, "gs");
+  TORCH_CHECK(gs.is_cuda() && gs.scalar_type() == torch::kBFloat16 && gs.numel() >= n,
+              "gs must be this rank's bf16 gradient shard");
   const c10::cuda::CUDAGuard guard(gs.device());
   const auto pp = make_peers(grad, param, pad, slots, rank);
-  const int rc = cfb::fused_reduce_shard(pp, lo, n, gs.data_ptr<float>(),
+  const int rc = cfb::fused_reduce_shard(pp, lo, n,
+                                         reinterpret_cast<__nv_bfloat16*>(gs.data_ptr()),
                                          sumsq_local.data_ptr<float>(), ticket.data_ptr<int>(),
                                          static_cast<int>(epoch), publish,
                                          num_sms(gs.get_device()),
@@ -256,7 +258,8 @@ void dp_adamw_shard(const std::vector<int64_t>& grad, const std::vector<int64_t>
   const auto pp = make_peers(grad, param, pad, slots, rank);
   const int rc = cfb::fused_adamw_shard(
       pp, lo, n, master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
-      gs.data_ptr<float>(), static_cast<float>(lr), static_cast<float>(b1),
+      reinterpret_cast<const __nv_bfloat16*>(gs.data_ptr()), static_cast<float>(lr),
+      static_cast<float>(b1),
       static_cast<float>(b2), static_cast<float>(eps), static_cast<float>(wd),
       static_cast<float>(bc1), static_cast<float>(bc2), static_cast<float>(max_norm),
       norm_out.data_ptr<float>(), ticket.data_ptr<int>(), static_cast<int>(epoch),

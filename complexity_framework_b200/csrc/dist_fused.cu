@@ -8,9 +8,10 @@
 //
 //   reduce kernel : device barrier on the signal pads (all peers finished
 //                   backward) -> for its shard, load the bf16 gradient slice
-//                   of every peer over NVLink, sum in fp32, scale by 1/P,
-//                   keep the fp32 result, accumulate the squared norm; the last
-//                   block publishes the partial norm into every peer's slot.
+//                   of every peer over NVLink, sum in fp32, scale by 1/P, write
+//                   the bf16 result in place over this rank's own shard (no peer
+//                   reads it), accumulate the squared norm; the last block of
+//                   the step publishes the norm partial into every peer's slot.
 //   update kernel : device barrier (all partial norms published) -> global
 //                   clip coefficient -> AdamW on the fp32 master shard ->
 //                   store the new bf16 parameters straight into EVERY peer's
@@ -64,7 +65,8 @@ __device__ bool wait_peers(const PeerPtrs& pp, int round, int epoch, int* err) {
   return true;
 }
 
-__global__ void reduce_shard_kernel(PeerPtrs pp, int64_t lo, int64_t n, float* __restrict__ gs,
+__global__ void reduce_shard_kernel(PeerPtrs pp, int64_t lo, int64_t n,
+                                    __nv_bfloat16* __restrict__ gs,
                                     float* __restrict__ sumsq_local, int* __restrict__ ticket,
                                     int epoch, int publish, int* err) {
   __shared__ int ok;
@@ -88,14 +90,20 @@ __global__ void reduce_shard_kernel(PeerPtrs pp, int64_t lo, int64_t n, float* _
         s[0] += a.x; s[1] += a.y; s[2] += b.x; s[3] += b.y;
         s[4] += c.x; s[5] += c.y; s[6] += d.x; s[7] += d.y;
       }
-      float4* o = reinterpret_cast<float4*>(gs + i * 8);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        s[j] *= inv;
-        acc += s[j] * s[j];
-      }
-      o[0] = make_float4(s[0], s[1], s[2], s[3]);
-      o[1] = make_float4(s[4], s[5], s[6], s[7]);
+      for (int j = 0; j < 8; ++j) s[j] *= inv;
+      uint4 w;
+      w.x = pack_bf16x2(s[0], s[1]);
+      w.y = pack_bf16x2(s[2], s[3]);
+      w.z = pack_bf16x2(s[4], s[5]);
+      w.w = pack_bf16x2(s[6], s[7]);
+      // the norm uses the bf16 values the optimizer will read
+      const float2 r0 = unpack_bf16x2(w.x), r1 = unpack_bf16x2(w.y), r2 = unpack_bf16x2(w.z),
+                   r3 = unpack_bf16x2(w.w);
+      acc += r0.x * r0.x + r0.y * r0.y + r1.x * r1.x + r1.y * r1.y + r2.x * r2.x + r2.y * r2.y +
+             r3.x * r3.x + r3.y * r3.y;
+      // this rank's shard of its own gradient buffer is read by no peer: reduce in place
+      *reinterpret_cast<uint4*>(gs + i * 8) = w;
     }
   }
 #pragma unroll
@@ -125,7 +133,7 @@ __global__ void reduce_shard_kernel(PeerPtrs pp, int64_t lo, int64_t n, float* _
 
 __global__ void adamw_shard_kernel(PeerPtrs pp, int64_t lo, int64_t n, float* __restrict__ master,
                                    float* __restrict__ m, float* __restrict__ v,
-                                   const float* __restrict__ gs, float lr, float b1, float b2,
+                                   const __nv_bfloat16* __restrict__ gs, float lr, float b1, float b2,
                                    float eps, float wd, float bc1, float bc2_sqrt, float max_norm,
                                    float* __restrict__ norm_out, int* __restrict__ ticket,
                                    int epoch, int* err) {
@@ -144,26 +152,43 @@ __global__ void adamw_shard_kernel(PeerPtrs pp, int64_t lo, int64_t n, float* __
   if (ok) {
     const float step = lr / bc1;
     const float decay = 1.f - lr * wd;
-    const int64_t nv = n / 2;
+    const int64_t nv = n / 8;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nv;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-      float out[2];
+      const uint4 gw = *reinterpret_cast<const uint4*>(gs + i * 8);
+      const float2 g0 = unpack_bf16x2(gw.x), g1 = unpack_bf16x2(gw.y), g2 = unpack_bf16x2(gw.z),
+                   g3 = unpack_bf16x2(gw.w);
+      const float g[8] = {g0.x, g0.y, g1.x, g1.y, g2.x, g2.y, g3.x, g3.y};
+      float4* m4 = reinterpret_cast<float4*>(m + i * 8);
+      float4* v4 = reinterpret_cast<float4*>(v + i * 8);
+      float4* p4 = reinterpret_cast<float4*>(master + i * 8);
+      float mm[8], vv[8], pp8[8];
+      *reinterpret_cast<float4*>(mm) = m4[0];
+      *reinterpret_cast<float4*>(mm + 4) = m4[1];
+      *reinterpret_cast<float4*>(vv) = v4[0];
+      *reinterpret_cast<float4*>(vv + 4) = v4[1];
+      *reinterpret_cast<float4*>(pp8) = p4[0];
+      *reinterpret_cast<float4*>(pp8 + 4) = p4[1];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int64_t e = i * 2 + j;
-        const float g = gs[e] * coef;
-        const float mi = b1 * m[e] + (1.f - b1) * g;
-        const float vi = b2 * v[e] + (1.f - b2) * g * g;
-        m[e] = mi;
-        v[e] = vi;
-        float p = master[e] * decay;
-        p -= step * mi / (sqrtf(vi) / bc2_sqrt + eps);
-        master[e] = p;
-        out[j] = p;
+      for (int j = 0; j < 8; ++j) {
+        const float gj = g[j] * coef;
+        mm[j] = b1 * mm[j] + (1.f - b1) * gj;
+        vv[j] = b2 * vv[j] + (1.f - b2) * gj * gj;
+        pp8[j] = pp8[j] * decay - step * mm[j] / (sqrtf(vv[j]) / bc2_sqrt + eps);
       }
-      const uint32_t w = pack_bf16x2(out[0], out[1]);
+      m4[0] = *reinterpret_cast<float4*>(mm);
+      m4[1] = *reinterpret_cast<float4*>(mm + 4);
+      v4[0] = *reinterpret_cast<float4*>(vv);
+      v4[1] = *reinterpret_cast<float4*>(vv + 4);
+      p4[0] = *reinterpret_cast<float4*>(pp8);
+      p4[1] = *reinterpret_cast<float4*>(pp8 + 4);
+      uint4 w;
+      w.x = pack_bf16x2(pp8[0], pp8[1]);
+      w.y = pack_bf16x2(pp8[2], pp8[3]);
+      w.z = pack_bf16x2(pp8[4], pp8[5]);
+      w.w = pack_bf16x2(pp8[6], pp8[7]);
       for (int p = 0; p < pp.world; ++p)
-        *reinterpret_cast<uint32_t*>(pp.param[p] + lo + i * 2) = w;
+        *reinterpret_cast<uint4*>(pp.param[p] + lo + i * 8) = w;
     }
   }
   // closing barrier: my stores into every peer are complete before I signal
@@ -181,7 +206,8 @@ __global__ void adamw_shard_kernel(PeerPtrs pp, int64_t lo, int64_t n, float* __
 
 }  // namespace
 
-int fused_reduce_shard(const PeerPtrs& pp, int64_t lo, int64_t n, float* gs, float* sumsq_local,
+int fused_reduce_shard(const PeerPtrs& pp, int64_t lo, int64_t n, __nv_bfloat16* gs,
+                       float* sumsq_local,
                        int* ticket, int epoch, bool publish, int num_sms, cudaStream_t s,
                        int* err) {
   if (pp.world < 1 || pp.world > kMaxRanks || n % 8 != 0 || lo % 8 != 0) return -2;
@@ -192,10 +218,11 @@ int fused_reduce_shard(const PeerPtrs& pp, int64_t lo, int64_t n, float* gs, flo
 }
 
 int fused_adamw_shard(const PeerPtrs& pp, int64_t lo, int64_t n, float* master, float* m, float* v,
-                      const float* gs, float lr, float b1, float b2, float eps, float wd, float bc1,
+                      const __nv_bfloat16* gs, float lr, float b1, float b2, float eps, float wd,
+                      float bc1,
                       float bc2, float max_norm, float* norm_out, int* ticket, int epoch,
                       int num_sms, cudaStream_t s, int* err) {
-  if (pp.world < 1 || pp.world > kMaxRanks || n % 2 != 0 || lo % 2 != 0) return -2;
+  if (pp.world < 1 || pp.world > kMaxRanks || n % 8 != 0 || lo % 8 != 0) return -2;
   adamw_shard_kernel<<<num_sms, 512, 0, s>>>(pp, lo, n, master, m, v, gs, lr, b1, b2, eps, wd,
                                              bc1, sqrtf(bc2), max_norm, norm_out, ticket, epoch,
                                              err);

@@ -18,11 +18,13 @@ struct PeerPtrs {
   int rank;
 };
 
-int fused_reduce_shard(const PeerPtrs& pp, int64_t lo, int64_t n, float* gs, float* sumsq_local,
+int fused_reduce_shard(const PeerPtrs& pp, int64_t lo, int64_t n, __nv_bfloat16* gs,
+                       float* sumsq_local,
                        int* ticket, int epoch, bool publish, int num_sms, cudaStream_t s,
                        int* err);
 int fused_adamw_shard(const PeerPtrs& pp, int64_t lo, int64_t n, float* master, float* m, float* v,
-                      const float* gs, float lr, float b1, float b2, float eps, float wd, float bc1,
+                      const __nv_bfloat16* gs, float lr, float b1, float b2, float eps, float wd,
+                      float bc1,
                       float bc2, float max_norm, float* norm_out, int* ticket, int epoch,
                       int num_sms, cudaStream_t s, int* err);
 

@@ -384,7 +384,7 @@ class _FusedDP:
             slots = [p + 3 * 8 * 4 for p in pads]  # floats after 3 rounds x 8 ranks of ints
             self.groups.append(dict(
                 fg=fg, grad=peer(hg, grad), param=peer(hp, param), pad=pads, slots=slots,
-                gs=torch.empty(fg.shard, device=grad.device, dtype=torch.float32),
+                gs=grad[fg.lo:fg.lo + fg.shard],
                 handles=(hg, hp, hc), ctrl=ctrl))
         dev = opt.flat_groups[0].compute.device
         self.sumsq = torch.zeros(1, device=dev, dtype=torch.float32)

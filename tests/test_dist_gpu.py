@@ -23,7 +23,7 @@ def test_peer_timeout_reports_error():
     grad = torch.zeros(n, device="cuda", dtype=torch.bfloat16)
     param = torch.zeros(n, device="cuda", dtype=torch.bfloat16)
     pads = [torch.zeros(64, device="cuda", dtype=torch.int32) for _ in range(2)]
-    gs = torch.empty(n // 2, device="cuda")
+    gs = torch.empty(n // 2, device="cuda", dtype=torch.bfloat16)
     sumsq = torch.zeros(1, device="cuda")
     ticket = torch.zeros(1, device="cuda", dtype=torch.int32)
     ptr = [grad.data_ptr(), grad.data_ptr()]
