@@ -19,6 +19,7 @@ SOURCES = [
     "flash_fwd.cu",
     "paged_attn.cu",
     "dist_fused.cu",
+    "noalloc.cu",
 ]
 
 NVCC_FLAGS = [
