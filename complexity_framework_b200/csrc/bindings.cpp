@@ -130,6 +130,7 @@ void gemm(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, 
     ep.c = out->data_ptr();
     ep.ldc = out->size(0) > 1 ? out->stride(0) : out->size(1);
     TORCH_CHECK(ep.ldc % 8 == 0, "out leading dim must be a multiple of 8");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(ep.c) % 16 == 0, "out must be 16-byte aligned");
     if (epi == cfb::EPI_SWIGLU_BWD) {
       TORCH_CHECK(out->size(0) >= M && out->size(1) >= 2 * N, "d(gu) too small");
       TORCH_CHECK(N % cfb::kSwigluBlock == 0, "swiglu bwd: N must be a multiple of 128");

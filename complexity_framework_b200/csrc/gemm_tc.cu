@@ -29,6 +29,8 @@
 // kernel K6 (:1232-1259).
 #include <cudaTypedefs.h>
 
+#include <cstring>
+
 #include "common.cuh"
 #include "gemm_tc.h"
 
@@ -39,7 +41,18 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 
-template <int BN, bool PAIR>
+// 32x32 bf16 staging boxes (2 KB) per epilogue warp: enough to keep each
+// output of a column chunk in flight while the next chunk is converted.
+__host__ __device__ constexpr int epi_slots(int epi) {
+  return epi == EPI_SWIGLU_FWD ? 3
+         : (epi == EPI_STORE || epi == EPI_RESID || epi == EPI_CE_STATS || epi == EPI_SWIGLU_BWD)
+             ? 2
+             : 0;
+}
+constexpr int kEpiWarps = 8;
+constexpr int kBoxBytes = 32 * 32 * 2;
+
+template <int BN, bool PAIR, int SLOTS>
 struct GemmCfg {
   // With PAIR, a 256-row tile is split over a CTA pair: each CTA holds its 128
   // A rows and half of the BN B rows; the even CTA issues M=256 MMAs.
@@ -47,26 +60,15 @@ struct GemmCfg {
   static constexpr int A_BYTES = kBM * kBK * 2;
   static constexpr int B_BYTES = B_ROWS * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (227 * 1024 - 2048) / STAGE_BYTES > 8
+  static constexpr int STAGING_BYTES = SLOTS * kBoxBytes * kEpiWarps;
+  static constexpr int STAGES = (227 * 1024 - 2048 - STAGING_BYTES) / STAGE_BYTES > 8
                                     ? 8
-                                    : (227 * 1024 - 2048) / STAGE_BYTES;
+                                    : (227 * 1024 - 2048 - STAGING_BYTES) / STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int TILE_M = PAIR ? 2 * kBM : kBM;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM_BYTES =
+      STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
-
-__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v, float alpha) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint4 w;
-    w.x = pack_bf16x2(v[q * 8 + 0] * alpha, v[q * 8 + 1] * alpha);
-    w.y = pack_bf16x2(v[q * 8 + 2] * alpha, v[q * 8 + 3] * alpha);
-    w.z = pack_bf16x2(v[q * 8 + 4] * alpha, v[q * 8 + 5] * alpha);
-    w.w = pack_bf16x2(v[q * 8 + 6] * alpha, v[q * 8 + 7] * alpha);
-    d[q] = w;
-  }
-}
 
 __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v) {
   const uint4* s = reinterpret_cast<const uint4*>(src);
@@ -80,6 +82,47 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v)
   }
 }
 
+// Lane `lane` writes row `lane` of a 32x32 bf16 box in the 64-byte-swizzled
+// layout the store tensor map expects (16-byte unit q of row r sits at unit
+// q ^ ((r >> 1) & 3)); eight consecutive lanes then hit distinct banks.
+__device__ __forceinline__ void stage_row_bf16(uint8_t* box, int lane, const float* v,
+                                               float alpha) {
+  uint4* rowp = reinterpret_cast<uint4*>(box + lane * 64);
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w;
+    w.x = pack_bf16x2(v[q * 8 + 0] * alpha, v[q * 8 + 1] * alpha);
+    w.y = pack_bf16x2(v[q * 8 + 2] * alpha, v[q * 8 + 3] * alpha);
+    w.z = pack_bf16x2(v[q * 8 + 4] * alpha, v[q * 8 + 5] * alpha);
+    w.w = pack_bf16x2(v[q * 8 + 6] * alpha, v[q * 8 + 7] * alpha);
+    rowp[q ^ sw] = w;
+  }
+}
+
+// Per-warp ring of staging boxes written to global memory by TMA stores.
+template <int SLOTS>
+struct BoxRing {
+  uint8_t* base;
+  int slot;
+  int lane;
+  // stage one 32x32 box (this lane's row = v) and store it at (x, y)
+  __device__ __forceinline__ void put(const CUtensorMap* map, const float* v, float alpha, int x,
+                                      int y) {
+    if (lane == 0) bulk_wait_group_read<SLOTS - 1>();  // the slot's previous store has read it
+    __syncwarp();
+    uint8_t* box = base + slot * kBoxBytes;
+    stage_row_bf16(box, lane, v, alpha);
+    fence_proxy_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(map, box, x, y);
+      bulk_commit_group();
+    }
+    slot = slot + 1 == SLOTS ? 0 : slot + 1;
+  }
+};
+
 // Scale that multiplies SwiGLU activation column `c` of row `row`.
 __device__ __forceinline__ float swiglu_col_scale(const GemmEpi& ep, int row, int c) {
   if (c < ep.shared_width) return ep.shared_scale;
@@ -90,8 +133,11 @@ __device__ __forceinline__ float swiglu_col_scale(const GemmEpi& ep, int row, in
 template <int BN, bool A_MN, bool B_MN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(384, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   int M, int N, int K, int ksplit, GemmEpi ep, int* err) {
-  using Cfg = GemmCfg<BN, PAIR>;
+                   const __grid_constant__ CUtensorMap tmC0,
+                   const __grid_constant__ CUtensorMap tmC1, int M, int N, int K, int ksplit,
+                   GemmEpi ep, int* err) {
+  constexpr int SLOTS = epi_slots(EPI);
+  using Cfg = GemmCfg<BN, PAIR, SLOTS>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int B_ROWS = Cfg::B_ROWS;
 
@@ -99,7 +145,8 @@ __global__ void __launch_bounds__(384, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* tiles = smem;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint8_t* staging = smem + STAGES * Cfg::STAGE_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(staging + Cfg::STAGING_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -137,6 +184,10 @@ __global__ void __launch_bounds__(384, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+  }
+  if (SLOTS > 0 && warp == 4 && lane == 0) {
+    tma_prefetch_desc(&tmC0);
+    if (EPI == EPI_SWIGLU_FWD) tma_prefetch_desc(&tmC1);
   }
   if (warp == 1) {
     if constexpr (PAIR)
@@ -282,6 +333,7 @@ __global__ void __launch_bounds__(384, 1)
     uint32_t acc_phase = 0;
     const uint32_t tempty_peer0 = mapa_shared(smem_u32(&tempty_bar[0]), 0);
     const uint32_t tempty_peer1 = mapa_shared(smem_u32(&tempty_bar[1]), 0);
+    BoxRing<SLOTS ? SLOTS : 1> ring{staging + (warp - 4) * SLOTS * kBoxBytes, 0, lane};
     for (int u = unit; u < total; u += units) {
       const int t = u / ksplit;
       const int m_blk = t / num_n;
@@ -304,11 +356,11 @@ __global__ void __launch_bounds__(384, 1)
           tmem_ld32(tbase + HALF + c, u);
           tmem_wait_ld();
           const int act_col = n_blk * HALF + c;
-          if (row_ok && n0 + c < N) {
-            __nv_bfloat16* gu_row = ep.gu + static_cast<int64_t>(row) * ep.ldgu;
-            store_bf16x32(gu_row + n0 + c, g, 1.0f);
-            store_bf16x32(gu_row + n0 + HALF + c, u, 1.0f);
-            const float s = swiglu_col_scale(ep, row, act_col);
+          if (n0 + c < N) {  // warp-uniform; rows >= M are clipped by the stores
+            const int y = m0 + wq * 32;
+            ring.put(&tmC0, g, 1.0f, n0 + c, y);
+            ring.put(&tmC0, u, 1.0f, n0 + HALF + c, y);
+            const float s = row_ok ? swiglu_col_scale(ep, row, act_col) : 0.0f;
             float a[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
@@ -318,12 +370,11 @@ __global__ void __launch_bounds__(384, 1)
               const float ub = __bfloat162float(__float2bfloat16(u[i]));
               a[i] = silu_f(gb) * ub * s;
             }
-            store_bf16x32(ep.act + static_cast<int64_t>(row) * ep.ldact + act_col, a, 1.0f);
+            ring.put(&tmC1, a, 1.0f, act_col, y);
           }
         }
       } else if constexpr (EPI == EPI_SWIGLU_BWD) {
         // Accumulator = d(act) for activation columns [n0, n0+BN).
-        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.c);
 #pragma unroll 1
         for (int c = wg * BN / 2; c < (wg + 1) * BN / 2; c += 32) {
           const int act_col = n0 + c;
@@ -336,12 +387,15 @@ __global__ void __launch_bounds__(384, 1)
           if (col_ok) {
             load_bf16x32(ep.gu + goff, g);
             load_bf16x32(ep.gu + goff + kSwigluBlock, u);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) g[i] = u[i] = 0.0f;
           }
           float da[32];
           tmem_ld32(tbase + c, da);
           tmem_wait_ld();
-          if (col_ok) {
-            const float s = swiglu_col_scale(ep, row, act_col);
+          if (act_col < N) {  // warp-uniform
+            const float s = col_ok ? swiglu_col_scale(ep, row, act_col) : 0.0f;
             float dg[32], du[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
@@ -351,21 +405,20 @@ __global__ void __launch_bounds__(384, 1)
               du[i] = d * sl;
               dg[i] = d * u[i] * sg * (1.0f + g[i] * (1.0f - sg));
             }
-            const int64_t ooff = static_cast<int64_t>(row) * ep.ldc + blk * 2 * kSwigluBlock + w;
-            store_bf16x32(out + ooff, dg, 1.0f);
-            store_bf16x32(out + ooff + kSwigluBlock, du, 1.0f);
+            const int x = blk * 2 * kSwigluBlock + w;
+            ring.put(&tmC0, dg, 1.0f, x, m0 + wq * 32);
+            ring.put(&tmC0, du, 1.0f, x + kSwigluBlock, m0 + wq * 32);
           }
         }
       } else if constexpr (EPI == EPI_CE_STATS) {
         // Store bf16 logits and, per (row, n-tile), the max and sum(exp(x-max)).
-        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.c);
         float mx = -INFINITY, se = 0.0f;
 #pragma unroll 1
         for (int c = wg * BN / 2; c < (wg + 1) * BN / 2; c += 32) {
           float v[32];
           tmem_ld32(tbase + c, v);
           tmem_wait_ld();
-          if (row_ok && n0 + c < N) {
+          if (n0 + c < N) {  // warp-uniform
             float lm = -INFINITY;
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
@@ -379,7 +432,7 @@ __global__ void __launch_bounds__(384, 1)
               if (n0 + c + i < N) acc_e += __expf(v[i] - nm);
             mx = nm;
             se = acc_e;
-            store_bf16x32(out + static_cast<int64_t>(row) * ep.ldc + n0 + c, v, 1.0f);
+            ring.put(&tmC0, v, 1.0f, n0 + c, m0 + wq * 32);
           }
         }
         if (row_ok) {
@@ -398,16 +451,16 @@ __global__ void __launch_bounds__(384, 1)
           float v[32];
           tmem_ld32(tbase + c, v);
           tmem_wait_ld();
-          if (row_ok && n0 + c < N) {
-            if constexpr (EPI == EPI_STORE) {
-              __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.c);
-              store_bf16x32(out + static_cast<int64_t>(row) * ep.ldc + n0 + c, v, ep.alpha);
-            } else if constexpr (EPI == EPI_RESID) {
-              __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.c);
+          if constexpr (EPI == EPI_STORE) {
+            if (n0 + c < N) ring.put(&tmC0, v, ep.alpha, n0 + c, m0 + wq * 32);
+          } else if constexpr (EPI == EPI_RESID) {
+            if (n0 + c < N) {
 #pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] = v[i] * ep.alpha + r[i];
-              store_bf16x32(out + static_cast<int64_t>(row) * ep.ldc + n0 + c, v, 1.0f);
-            } else if constexpr (EPI == EPI_F32_ATOMIC) {
+              for (int i = 0; i < 32; ++i) v[i] = v[i] * ep.alpha + (row_ok ? r[i] : 0.0f);
+              ring.put(&tmC0, v, 1.0f, n0 + c, m0 + wq * 32);
+            }
+          } else if (row_ok && n0 + c < N) {
+            if constexpr (EPI == EPI_F32_ATOMIC) {
               float* out = reinterpret_cast<float*>(ep.c) + static_cast<int64_t>(row) * ep.ldc + n0 + c;
 #pragma unroll
               for (int q = 0; q < 8; ++q)
@@ -441,6 +494,7 @@ __global__ void __launch_bounds__(384, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (SLOTS > 0 && lane == 0) bulk_wait_group_all();
   }
 
   tc_fence_before();
@@ -487,11 +541,25 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
   return r == CUDA_SUCCESS ? 0 : static_cast<int>(r) + 1000;
 }
 
+int make_tmap_2d_store(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
+                       int64_t ld) {
+  auto fn = get_encode_fn();
+  if (fn == nullptr) return -1;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : static_cast<int>(r) + 1000;
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI, bool PAIR>
-static int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
-                       const GemmEpi& ep, int num_sms, cudaStream_t stream, int* err,
-                       int ksplit = 1) {
-  using Cfg = GemmCfg<BN, PAIR>;
+static int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap* tc,
+                       int M, int N, int K, const GemmEpi& ep, int num_sms, cudaStream_t stream,
+                       int* err, int ksplit = 1) {
+  using Cfg = GemmCfg<BN, PAIR, epi_slots(EPI)>;
   auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI, PAIR>;
   static int max_units = -1;  // resident CTAs (or CTA pairs), one query per instantiation
   cudaLaunchConfig_t cfg = {};
@@ -538,32 +606,33 @@ static int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, int M, int 
   const int work = tiles * ksplit;
   const int units = work < max_units ? work : max_units;
   cfg.gridDim = dim3(PAIR ? 2 * units : units, 1, 1);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, ksplit, ep, err);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tc[0], tc[1], M, N, K, ksplit, ep, err);
   return static_cast<int>(e);
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
-static int launch_pair_or_single(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
-                                 int K, const GemmEpi& ep, int sms, cudaStream_t s, int* err) {
+static int launch_pair_or_single(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap* tc,
+                                 int M, int N, int K, const GemmEpi& ep, int sms, cudaStream_t s,
+                                 int* err) {
   const int ks = EPI == EPI_F32_ATOMIC ? 0 : 1;  // 0 = choose
   // 256-row tiles over an SM pair halve each SM's operand traffic per FLOP;
   // a single 128-row tile is used only when M itself fits in one.
   // (keep in sync with the B tensor-map box chosen in gemm_tc_launch)
-  if (M > kBM) return launch_impl<BN, A_MN, B_MN, EPI, true>(ta, tb, M, N, K, ep, sms, s, err, ks);
-  return launch_impl<BN, A_MN, B_MN, EPI, false>(ta, tb, M, N, K, ep, sms, s, err, ks);
+  if (M > kBM) return launch_impl<BN, A_MN, B_MN, EPI, true>(ta, tb, tc, M, N, K, ep, sms, s, err, ks);
+  return launch_impl<BN, A_MN, B_MN, EPI, false>(ta, tb, tc, M, N, K, ep, sms, s, err, ks);
 }
 
 template <int BN, int EPI>
 static int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
-                          int M, int N, int K, const GemmEpi& ep, int sms, cudaStream_t s,
+                          const CUtensorMap* tc, int M, int N, int K, const GemmEpi& ep, int sms, cudaStream_t s,
                           int* err) {
   if (!a_mn && !b_mn)
-    return launch_pair_or_single<BN, false, false, EPI>(ta, tb, M, N, K, ep, sms, s, err);
+    return launch_pair_or_single<BN, false, false, EPI>(ta, tb, tc, M, N, K, ep, sms, s, err);
   if (!a_mn && b_mn)
-    return launch_pair_or_single<BN, false, true, EPI>(ta, tb, M, N, K, ep, sms, s, err);
+    return launch_pair_or_single<BN, false, true, EPI>(ta, tb, tc, M, N, K, ep, sms, s, err);
   if (a_mn && !b_mn)
-    return launch_pair_or_single<BN, true, false, EPI>(ta, tb, M, N, K, ep, sms, s, err);
-  return launch_pair_or_single<BN, true, true, EPI>(ta, tb, M, N, K, ep, sms, s, err);
+    return launch_pair_or_single<BN, true, false, EPI>(ta, tb, tc, M, N, K, ep, sms, s, err);
+  return launch_pair_or_single<BN, true, true, EPI>(ta, tb, tc, M, N, K, ep, sms, s, err);
 }
 
 int choose_bn(int M, int N, int num_sms) {
@@ -590,12 +659,35 @@ int gemm_tc_launch(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream, in
   else
     rc = make_tmap_2d(&tb, g.B, g.K, g.N, g.ldb, 64, kBK);
   if (rc) return rc;
+  // epilogue store maps (bf16 outputs written by TMA from staging boxes)
+  CUtensorMap tc[2];
+  memset(tc, 0, sizeof(tc));
+  switch (g.epi) {
+    case EPI_STORE:
+    case EPI_RESID:
+    case EPI_CE_STATS:
+      rc = make_tmap_2d_store(&tc[0], ep.c, g.M, g.N, ep.ldc);
+      break;
+    case EPI_SWIGLU_FWD:
+      rc = make_tmap_2d_store(&tc[0], ep.gu, g.M, g.N, ep.ldgu);
+      if (!rc) rc = make_tmap_2d_store(&tc[1], ep.act, g.M, g.N / 2, ep.ldact);
+      break;
+    case EPI_SWIGLU_BWD: {
+      int64_t cols = 2 * static_cast<int64_t>((g.N + kSwigluBlock - 1) / kSwigluBlock) * kSwigluBlock;
+      if (cols > ep.ldc) cols = ep.ldc;
+      rc = make_tmap_2d_store(&tc[0], ep.c, g.M, cols, ep.ldc);
+      break;
+    }
+    default:
+      break;
+  }
+  if (rc) return rc;
 
 #define CFB_EPI_CASE(E)                                                                          \
   case E:                                                                                        \
-    return bn == 256 ? dispatch_major<256, E>(g.a_mn, g.b_mn, ta, tb, g.M, g.N, g.K, ep,          \
+    return bn == 256 ? dispatch_major<256, E>(g.a_mn, g.b_mn, ta, tb, tc, g.M, g.N, g.K, ep,          \
                                               g.num_sms, stream, err)                            \
-                     : dispatch_major<128, E>(g.a_mn, g.b_mn, ta, tb, g.M, g.N, g.K, ep,          \
+                     : dispatch_major<128, E>(g.a_mn, g.b_mn, ta, tb, tc, g.M, g.N, g.K, ep,          \
                                               g.num_sms, stream, err);
   switch (g.epi) {
     CFB_EPI_CASE(EPI_STORE)
@@ -606,14 +698,14 @@ int gemm_tc_launch(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream, in
     CFB_EPI_CASE(EPI_CE_STATS)
     case EPI_SWIGLU_FWD:
       if (g.a_mn || g.b_mn) return -4;
-      return launch_pair_or_single<256, false, false, EPI_SWIGLU_FWD>(ta, tb, g.M, g.N, g.K, ep,
+      return launch_pair_or_single<256, false, false, EPI_SWIGLU_FWD>(ta, tb, tc, g.M, g.N, g.K, ep,
                                                                       g.num_sms, stream, err);
     case EPI_SWIGLU_BWD:
       if (g.a_mn || !g.b_mn) return -4;
       return bn == 256 ? launch_pair_or_single<256, false, true, EPI_SWIGLU_BWD>(
-                             ta, tb, g.M, g.N, g.K, ep, g.num_sms, stream, err)
+                             ta, tb, tc, g.M, g.N, g.K, ep, g.num_sms, stream, err)
                        : launch_pair_or_single<128, false, true, EPI_SWIGLU_BWD>(
-                             ta, tb, g.M, g.N, g.K, ep, g.num_sms, stream, err);
+                             ta, tb, tc, g.M, g.N, g.K, ep, g.num_sms, stream, err);
     default:
       return -5;
   }

@@ -58,5 +58,8 @@ int gemm_tc_launch(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream, in
 int choose_bn(int M, int N, int num_sms);
 int make_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
                  int box_inner, int box_outer);
+// Same, for epilogue stores: 32 x 32 boxes with 64-byte swizzle.
+int make_tmap_2d_store(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
+                       int64_t ld);
 
 }  // namespace cfb
