@@ -52,11 +52,9 @@ class Trainer:
         self.distributed_mode = mode
         if self.world > 1:
             self._broadcast_parameters(process_group)
-        groups = default_param_groups(self.model, self.config.weight_decay)
-        self.optimizer = FusedAdamW(groups, lr=self.config.learning_rate, betas=(0.9, 0.95),
-                                    weight_decay=self.config.weight_decay,
-                                    process_group=process_group, shard_state=(mode == "fsdp"))
-        self.scheduler = build_scheduler(self.optimizer, kind=self.config.lr_scheduler,
+        self.optimizer = self._build_optimizer(process_group, mode)
+        sched_opt = getattr(self.optimizer, "optimizer", self.optimizer)
+        self.scheduler = build_scheduler(sched_opt, kind=self.config.lr_scheduler,
                                          warmup_steps=self.config.warmup_steps,
                                          total_steps=self.config.max_steps,
                                          min_lr_ratio=self.config.min_lr_ratio,
@@ -71,6 +69,34 @@ class Trainer:
         self._canary = None
 
     # ----------------------------------------------------------------- setup
+    def _build_optimizer(self, process_group, mode: str):
+        """``adamw`` -> the flat fused AdamW (ZeRO-2 sharded under fsdp); any other
+        ``optimizer_type`` (muon, muon_tr, adam_tr, lion, sophia, adam8bit, came,
+        adalomo, musgd, adam, sgd) -> that optimizer behind a bucketed all-reduce."""
+        cfg = self.config
+        kind = cfg.optimizer_type.lower()
+        if kind == "adamw":
+            groups = default_param_groups(self.model, cfg.weight_decay)
+            return FusedAdamW(groups, lr=cfg.learning_rate, betas=(0.9, 0.95),
+                              weight_decay=cfg.weight_decay, process_group=process_group,
+                              shard_state=(mode == "fsdp"))
+        from .optimizers import DistributedOptimizer, get_optimizer
+
+        kw = {}
+        if kind in ("muon", "muon_tr"):
+            kw["muon_lr"] = cfg.muon_lr
+        if kind in ("muon_tr", "adam_tr"):
+            mc = getattr(self.model, "config", None)
+            kw["num_experts"] = int(getattr(mc, "num_experts", 4) or 4)
+        if kind == "adam_tr":
+            kw["expert_lr_scale"] = cfg.expert_lr_scale
+            kw["expert_weight_decay"] = cfg.expert_weight_decay
+        if kind == "muon_tr":
+            kw["adaptive_ns"] = cfg.adaptive_ns
+        opt = get_optimizer(self.model, kind, lr=cfg.learning_rate,
+                            weight_decay=cfg.weight_decay, **kw)
+        return DistributedOptimizer(opt, process_group)
+
     @torch.no_grad()
     def _broadcast_parameters(self, pg) -> None:
         src = dist.get_global_rank(pg, 0) if pg is not None else 0
