@@ -6,7 +6,7 @@ Only Blackwell (sm_100a) code is generated; there is no other target.
 """
 import os
 from setuptools import setup, find_packages
-from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+from torch.utils.cpp_extension import BuildExtension, CppExtension, CUDAExtension
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join("complexity_framework_b200", "csrc")
@@ -39,10 +39,17 @@ ext = CUDAExtension(
     libraries=["cuda"],
 )
 
+# host-side data IO (memory-mapped token shards, batch gather, packing)
+io_ext = CppExtension(
+    name="complexity_framework_b200._io",
+    sources=[os.path.join(CSRC, "io", "token_io.cpp")],
+    extra_compile_args={"cxx": ["-O3", "-std=c++17"]},
+)
+
 setup(
     name="complexity_framework_b200",
     version="0.1.0",
     packages=find_packages(include=["complexity_framework_b200*"]),
-    ext_modules=[ext],
+    ext_modules=[ext, io_ext],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )
