@@ -67,6 +67,7 @@ class Trainer:
         self.best_loss = float("inf")
         self._compute_loss = compute_loss
         self._canary = None
+        self.should_stop = False
 
     # ----------------------------------------------------------------- setup
     def _build_optimizer(self, process_group, mode: str):
@@ -178,39 +179,69 @@ class Trainer:
             raise RuntimeError("parameters did not change after the first optimizer step")
 
     # ------------------------------------------------------------------ loop
-    def train(self, batches: Iterable[torch.Tensor], max_steps: Optional[int] = None) -> dict:
-        """Run optimizer steps over an iterable of [B, S] token batches."""
+    @staticmethod
+    def _split_batch(batch):
+        if isinstance(batch, dict):
+            return batch["input_ids"], batch.get("labels")
+        if isinstance(batch, (tuple, list)):
+            return batch[0], (batch[1] if len(batch) > 1 else None)
+        return batch, None
+
+    def _emit(self, hook: str, *args) -> None:
+        for cb in self.callbacks:
+            fn = getattr(cb, hook, None)
+            if fn is not None:
+                fn(self, *args)
+
+    def train(self, batches: Iterable, max_steps: Optional[int] = None,
+              eval_batches: Optional[Callable[[], Iterable]] = None) -> dict:
+        """Run optimizer steps over an iterable of batches (``[B, S]`` token
+        tensors, ``(input_ids, labels)`` pairs or dicts with those keys).
+
+        ``eval_batches`` is a factory of evaluation iterables, used every
+        ``eval_steps`` steps.  A callback may stop training early by setting
+        ``trainer.should_stop``.
+        """
         max_steps = max_steps or self.config.max_steps
         t0 = time.perf_counter()
         last = None
+        self.should_stop = False
+        self._emit("on_train_begin")
         try:
             for batch in batches:
-                if self.global_step >= max_steps:
+                if self.global_step >= max_steps or self.should_stop:
                     break
+                ids, labels = self._split_batch(batch)
                 sync = (self.global_step % self.config.log_steps == 0)
-                out = self.train_step(batch, sync=sync)
+                out = self.train_step(ids, labels, sync=sync)
                 last_val = out if sync else None
                 if last_val is not None:
                     last = last_val
                     self.best_loss = min(self.best_loss, last_val)
-                for cb in self.callbacks:
-                    if hasattr(cb, "on_step_end"):
-                        cb.on_step_end(self, self.global_step, last_val)
+                self._emit("on_step_end", self.global_step, last_val)
+                if (eval_batches is not None and self.config.eval_steps
+                        and self.global_step % self.config.eval_steps == 0):
+                    ev = self.evaluate(eval_batches())
+                    self._emit("on_evaluate", self.global_step, ev)
                 if self.global_step % self.config.save_steps == 0:
                     self.save_checkpoint()
         except KeyboardInterrupt:
             self.save_checkpoint(tag="interrupted")
             raise
-        return {"steps": self.global_step, "tokens": self.total_tokens,
-                "seconds": time.perf_counter() - t0, "last_loss": last}
+        summary = {"steps": self.global_step, "tokens": self.total_tokens,
+                   "seconds": time.perf_counter() - t0, "last_loss": last}
+        self._emit("on_train_end", summary)
+        return summary
 
     @torch.no_grad()
     def evaluate(self, batches: Iterable[torch.Tensor]) -> float:
         self.model.eval()
         tot = torch.zeros(2, device=self.device, dtype=torch.float64)
         for b in batches:
-            ids = b.to(self.device, non_blocking=True)
-            loss = self.compute_loss(ids)
+            ids, labels = self._split_batch(b)
+            ids = ids.to(self.device, non_blocking=True)
+            lab = labels.to(self.device, non_blocking=True) if labels is not None else None
+            loss = self.compute_loss(ids, lab)
             tot[0] += loss.double() * ids.numel()
             tot[1] += ids.numel()
         if self.world > 1:
