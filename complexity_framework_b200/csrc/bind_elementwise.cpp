@@ -64,6 +64,7 @@ void qk_norm_rope_fwd(const torch::Tensor& kqv, const torch::Tensor& qw, const t
                       const c10::optional<torch::Tensor>& pos, torch::Tensor& q, torch::Tensor& k,
                       torch::Tensor& v, torch::Tensor& rstd, int64_t B, int64_t S, int64_t Hq,
                       int64_t Hkv, int64_t D, double eps, bool qk_norm) {
+  TORCH_CHECK(B * S * (Hq + 2 * Hkv) < (int64_t(1) << 31), "qk_norm_rope: too many (token, head) items");
   chk(kqv, torch::kBFloat16, "kqv");
   chk(qw, torch::kBFloat16, "q_norm.weight");
   chk(kw, torch::kBFloat16, "k_norm.weight");
@@ -99,6 +100,7 @@ void qk_norm_rope_bwd(const torch::Tensor& dq, const torch::Tensor& dk, const to
                       const c10::optional<torch::Tensor>& pos, const torch::Tensor& rstd,
                       torch::Tensor& dkqv, torch::Tensor& dqw, torch::Tensor& dkw, int64_t B,
                       int64_t S, int64_t Hq, int64_t Hkv, int64_t D, bool qk_norm) {
+  TORCH_CHECK(B * S * (Hq + 2 * Hkv) < (int64_t(1) << 31), "qk_norm_rope: too many (token, head) items");
   chk(dq, torch::kBFloat16, "dq");
   chk(dk, torch::kBFloat16, "dk");
   chk(dv, torch::kBFloat16, "dv");

@@ -128,42 +128,51 @@ __global__ void rmsnorm_bwd_k(const bf16* __restrict__ dy, const bf16* __restric
 }
 
 // Register-accumulating variant for H <= NV*256: lane l owns vectors l, l+32, ...
-// so its d(weight) partials live in registers for the whole row loop.
+// so its d(weight) partials live in registers for the whole row loop.  The
+// weight row sits in shared memory and the second pass re-reads x / dy
+// (L1-resident, just loaded) instead of holding them, which keeps the kernel
+// near 64 registers so three 256-thread blocks fit per SM.
 template <int NV>
-__global__ void rmsnorm_bwd_reg_k(const bf16* __restrict__ dy, const bf16* __restrict__ x,
-                                  const bf16* __restrict__ w, const float* __restrict__ rstd,
-                                  const bf16* __restrict__ dres, bf16* __restrict__ dx,
-                                  float* __restrict__ dw, int64_t T, int H) {
-  extern __shared__ float sdw[];
-  for (int i = threadIdx.x; i < H; i += blockDim.x) sdw[i] = 0.f;
+__global__ void __launch_bounds__(256, 3)
+    rmsnorm_bwd_reg_k(const bf16* __restrict__ dy, const bf16* __restrict__ x,
+                      const bf16* __restrict__ w, const float* __restrict__ rstd,
+                      const bf16* __restrict__ dres, bf16* __restrict__ dx,
+                      float* __restrict__ dw, int64_t T, int H) {
+  extern __shared__ float sdw[];   // [H] d(weight) partials, then [H] weights
+  float* sw = sdw + H;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    sdw[i] = 0.f;
+    sw[i] = __bfloat162float(w[i]);
+  }
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int nv = H >> 3;
   float acc[NV][8];
-  float wv[NV][8];
 #pragma unroll
-  for (int k = 0; k < NV; ++k) {
-    const int i = lane + 32 * k;
+  for (int k = 0; k < NV; ++k)
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[k][j] = 0.f;
-    if (i < nv) load8(w + i * 8, wv[k]);
-  }
   for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < T;
        row += warps) {
     const float r = rstd[row];
-    float xv[NV][8], gv[NV][8];
+    const bf16* xr = x + row * H;
+    const bf16* gr = dy + row * H;
     float dot = 0.f;
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int i = lane + 32 * k;
       if (i < nv) {
-        load8(x + row * H + i * 8, xv[k]);
-        load8(dy + row * H + i * 8, gv[k]);
+        float xv[8], gv[8];
+        load8(xr + i * 8, xv);
+        load8(gr + i * 8, gv);
+        const float4 w0 = *reinterpret_cast<const float4*>(sw + i * 8);
+        const float4 w1 = *reinterpret_cast<const float4*>(sw + i * 8 + 4);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          dot += gv[k][j] * wv[k][j] * xv[k][j];
-          acc[k][j] += gv[k][j] * rb(xv[k][j] * r);
+          dot += gv[j] * wv[j] * xv[j];
+          acc[k][j] += gv[j] * rb(xv[j] * r);
         }
       }
     }
@@ -173,15 +182,20 @@ __global__ void rmsnorm_bwd_reg_k(const bf16* __restrict__ dy, const bf16* __res
     for (int k = 0; k < NV; ++k) {
       const int i = lane + 32 * k;
       if (i < nv) {
-        float o[8];
+        float xv[8], gv[8], o[8];
+        load8(xr + i * 8, xv);
+        load8(gr + i * 8, gv);
         if (dres != nullptr) {
           load8(dres + row * H + i * 8, o);
         } else {
 #pragma unroll
           for (int j = 0; j < 8; ++j) o[j] = 0.f;
         }
+        const float4 w0 = *reinterpret_cast<const float4*>(sw + i * 8);
+        const float4 w1 = *reinterpret_cast<const float4*>(sw + i * 8 + 4);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] += r * gv[k][j] * wv[k][j] - xv[k][j] * c;
+        for (int j = 0; j < 8; ++j) o[j] += r * gv[j] * wv[j] - xv[j] * c;
         store8(dx + row * H + i * 8, o);
       }
     }
@@ -199,89 +213,120 @@ __global__ void rmsnorm_bwd_reg_k(const bf16* __restrict__ dy, const bf16* __res
 }
 
 // ------------------------------------------------------- QK-norm + RoPE
-// One warp per (token, head).  Head index hh: [0,Hq) q heads, [Hq, Hq+Hkv) k
-// heads, [Hq+Hkv, Hq+2Hkv) v heads.  Lane l holds EPL = D/32 consecutive
-// elements; the rotate-half partner of lane l is lane l^16.
-template <int EPL>
+// LPH = D/8 lanes cooperate on one (token, head) item with 16-byte vectors
+// (lane gl of a group owns elements 8*gl .. 8*gl+7); a warp handles 32/LPH
+// consecutive items of the flattened [token, head] order.  Head index hh:
+// [0,Hq) q heads, [Hq, Hq+Hkv) k heads, [Hq+Hkv, Hq+2Hkv) v heads; the fused
+// projection output kqv stores columns in k | q | v order.  The rotate-half
+// partner of element j (j +- D/2) lives in lane gl ^ (LPH/2) of the group.
+struct HeadItem {
+  int64_t t;
+  int hh;
+  int col;
+  int64_t hm;  // element offset of (b, head, s, 0) in the head-major tensor
+  int kind;    // 0 = q, 1 = k, 2 = v
+};
+
+template <int D>
+__device__ __forceinline__ HeadItem decode_item(int64_t item, int Htot, int S, int Hq, int Hkv) {
+  // item < 2^31 (checked by the launcher): 32-bit divisions are far cheaper
+  HeadItem it;
+  const uint32_t i32 = static_cast<uint32_t>(item);
+  const uint32_t t32 = i32 / static_cast<uint32_t>(Htot);
+  it.t = t32;
+  it.hh = static_cast<int>(i32 - t32 * static_cast<uint32_t>(Htot));
+  const int b = static_cast<int>(t32 / static_cast<uint32_t>(S));
+  const int s = static_cast<int>(t32 - static_cast<uint32_t>(b) * static_cast<uint32_t>(S));
+  if (it.hh < Hq) {
+    it.kind = 0;
+    it.col = Hkv * D + it.hh * D;
+    it.hm = (((int64_t)b * Hq + it.hh) * S + s) * D;
+  } else if (it.hh < Hq + Hkv) {
+    const int h = it.hh - Hq;
+    it.kind = 1;
+    it.col = h * D;
+    it.hm = (((int64_t)b * Hkv + h) * S + s) * D;
+  } else {
+    const int h = it.hh - Hq - Hkv;
+    it.kind = 2;
+    it.col = (Hkv + Hq) * D + h * D;
+    it.hm = (((int64_t)b * Hkv + h) * S + s) * D;
+  }
+  return it;
+}
+
+__device__ __forceinline__ int s_of(int64_t t, int S) {
+  return static_cast<int>(static_cast<uint32_t>(t) % static_cast<uint32_t>(S));
+}
+
+template <int LPH>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = LPH / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void load8f(const float* p, float* v) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+template <int D>
 __global__ void qk_norm_rope_fwd_k(const bf16* __restrict__ kqv, const bf16* __restrict__ qw,
                                    const bf16* __restrict__ kw, const float* __restrict__ cos_t,
                                    const float* __restrict__ sin_t, const int32_t* __restrict__ pos,
                                    bf16* __restrict__ q, bf16* __restrict__ k,
                                    bf16* __restrict__ v, float* __restrict__ rstd, int B, int S,
                                    int Hq, int Hkv, float eps, bool qk_norm) {
-  constexpr int D = EPL * 32;
+  constexpr int LPH = D / 8, GPW = 32 / LPH, HALF = LPH / 2;
   const int lane = threadIdx.x & 31;
+  const int grp = lane / LPH, gl = lane % LPH;
   const int Htot = Hq + 2 * Hkv;
   const int C = Htot * D;
-  const int64_t T = (int64_t)B * S;
-  const int64_t total = T * Htot;
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); item < total;
-       item += warps) {
-    const int64_t t = item / Htot;
-    const int hh = static_cast<int>(item % Htot);
-    const int b = static_cast<int>(t / S), s = static_cast<int>(t % S);
-    int col;  // column offset of this head inside kqv (k | q | v order)
-    bf16* dst;
-    bool is_q = false, is_k = false;
-    if (hh < Hq) {
-      col = Hkv * D + hh * D;
-      dst = q + (((int64_t)b * Hq + hh) * S + s) * D;
-      is_q = true;
-    } else if (hh < Hq + Hkv) {
-      const int h = hh - Hq;
-      col = h * D;
-      dst = k + (((int64_t)b * Hkv + h) * S + s) * D;
-      is_k = true;
-    } else {
-      const int h = hh - Hq - Hkv;
-      col = (Hkv + Hq) * D + h * D;
-      dst = v + (((int64_t)b * Hkv + h) * S + s) * D;
-    }
-    const bf16* src = kqv + t * C + col + lane * EPL;
-    float x[EPL];
-#pragma unroll
-    for (int j = 0; j < EPL; j += 2) {
-      float2 p = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + j));
-      x[j] = p.x;
-      x[j + 1] = p.y;
-    }
-    if (!(is_q || is_k)) {
-#pragma unroll
-      for (int j = 0; j < EPL; j += 2)
-        *reinterpret_cast<uint32_t*>(dst + lane * EPL + j) = pack_bf16x2(x[j], x[j + 1]);
-      continue;
-    }
+  const int64_t total = (int64_t)B * S * Htot;
+  const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t base = wid * GPW; base < total; base += nw * GPW) {
+    const int64_t item = base + grp;
+    const bool valid = item < total;
+    HeadItem it = decode_item<D>(valid ? item : total - 1, Htot, S, Hq, Hkv);
+    float x[8];
+    load8(kqv + it.t * C + it.col + gl * 8, x);
+    const bool qk = it.kind != 2;
     if (qk_norm) {
       float ss = 0.f;
 #pragma unroll
-      for (int j = 0; j < EPL; ++j) ss += x[j] * x[j];
-      ss = warp_sum(ss);
+      for (int j = 0; j < 8; ++j) ss += x[j] * x[j];
+      ss = group_sum<LPH>(ss);
       const float r = rsqrtf(ss / D + eps);
-      const bf16* w = is_q ? qw : kw;
+      if (qk) {
+        float wv[8];
+        load8((it.kind == 0 ? qw : kw) + gl * 8, wv);
 #pragma unroll
-      for (int j = 0; j < EPL; ++j)
-        x[j] = rb(rb(x[j] * r) * __bfloat162float(w[lane * EPL + j]));
-      if (lane == 0) rstd[t * (Hq + Hkv) + (is_q ? hh : hh)] = r;
+        for (int j = 0; j < 8; ++j) x[j] = rb(rb(x[j] * r) * wv[j]);
+        if (gl == 0 && valid) rstd[it.t * (Hq + Hkv) + it.hh] = r;
+      }
     }
-    const int p = pos != nullptr ? pos[t] : s;
-    const int fi0 = (lane & 15) * EPL;  // frequency index of element j is fi0 + j
-    float o[EPL];
+    const int p = pos != nullptr ? pos[it.t] : s_of(it.t, S);
+    float c[8], sn[8], o[8];
+    load8f(cos_t + (int64_t)p * (D / 2) + (gl % HALF) * 8, c);
+    load8f(sin_t + (int64_t)p * (D / 2) + (gl % HALF) * 8, sn);
 #pragma unroll
-    for (int j = 0; j < EPL; ++j) {
-      const float partner = __shfl_xor_sync(0xffffffffu, x[j], 16);
-      const float c = cos_t[(int64_t)p * (D / 2) + fi0 + j];
-      const float sn = sin_t[(int64_t)p * (D / 2) + fi0 + j];
-      o[j] = lane < 16 ? x[j] * c - partner * sn : x[j] * c + partner * sn;
+    for (int j = 0; j < 8; ++j) {
+      const float partner = __shfl_xor_sync(0xffffffffu, x[j], HALF);
+      o[j] = gl < HALF ? x[j] * c[j] - partner * sn[j] : x[j] * c[j] + partner * sn[j];
+      if (!qk) o[j] = x[j];
     }
-#pragma unroll
-    for (int j = 0; j < EPL; j += 2)
-      *reinterpret_cast<uint32_t*>(dst + lane * EPL + j) = pack_bf16x2(o[j], o[j + 1]);
+    if (valid) {
+      bf16* dst = it.kind == 0 ? q : (it.kind == 1 ? k : v);
+      store8(dst + it.hm + gl * 8, o);
+    }
   }
 }
 
-template <int EPL>
-__global__ void qk_norm_rope_bwd_k(const bf16* __restrict__ dq, const bf16* __restrict__ dk,
+template <int D>
+__global__ void __launch_bounds__(256, 3) qk_norm_rope_bwd_k(const bf16* __restrict__ dq, const bf16* __restrict__ dk,
                                    const bf16* __restrict__ dv, const bf16* __restrict__ kqv,
                                    const bf16* __restrict__ qw, const bf16* __restrict__ kw,
                                    const float* __restrict__ cos_t, const float* __restrict__ sin_t,
@@ -289,7 +334,7 @@ __global__ void qk_norm_rope_bwd_k(const bf16* __restrict__ dq, const bf16* __re
                                    bf16* __restrict__ dkqv, float* __restrict__ dqw,
                                    float* __restrict__ dkw, int B, int S, int Hq, int Hkv,
                                    bool qk_norm) {
-  constexpr int D = EPL * 32;
+  constexpr int LPH = D / 8, GPW = 32 / LPH, HALF = LPH / 2;
   __shared__ float s_dqw[D], s_dkw[D];
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
     s_dqw[i] = 0.f;
@@ -297,103 +342,68 @@ __global__ void qk_norm_rope_bwd_k(const bf16* __restrict__ dq, const bf16* __re
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
+  const int grp = lane / LPH, gl = lane % LPH;
   const int Htot = Hq + 2 * Hkv;
   const int C = Htot * D;
-  const int64_t T = (int64_t)B * S;
-  const int64_t total = T * Htot;
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  // lane-owned partial sums of d(q_norm.weight) / d(k_norm.weight): lane l
-  // always handles elements [l*EPL, l*EPL+EPL), so no atomics inside the loop
-  float accq[EPL], acck[EPL];
+  const int64_t total = (int64_t)B * S * Htot;
+  const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  float accq[8], acck[8], wq[8], wk[8];
 #pragma unroll
-  for (int j = 0; j < EPL; ++j) accq[j] = acck[j] = 0.f;
-  for (int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); item < total;
-       item += warps) {
-    const int64_t t = item / Htot;
-    const int hh = static_cast<int>(item % Htot);
-    const int b = static_cast<int>(t / S), s = static_cast<int>(t % S);
-    int col;
-    const bf16* src;
-    bool is_q = false, is_k = false;
-    if (hh < Hq) {
-      col = Hkv * D + hh * D;
-      src = dq + (((int64_t)b * Hq + hh) * S + s) * D;
-      is_q = true;
-    } else if (hh < Hq + Hkv) {
-      const int h = hh - Hq;
-      col = h * D;
-      src = dk + (((int64_t)b * Hkv + h) * S + s) * D;
-      is_k = true;
+  for (int j = 0; j < 8; ++j) accq[j] = acck[j] = 0.f;
+  load8(qw + gl * 8, wq);
+  load8(kw + gl * 8, wk);
+  for (int64_t base = wid * GPW; base < total; base += nw * GPW) {
+    const int64_t item = base + grp;
+    const bool valid = item < total;
+    HeadItem it = decode_item<D>(valid ? item : total - 1, Htot, S, Hq, Hkv);
+    const bf16* src = it.kind == 0 ? dq : (it.kind == 1 ? dk : dv);
+    float g[8];
+    load8(src + it.hm + gl * 8, g);
+    const bool qk = it.kind != 2;
+    // inverse rotation: dn_j = g_j cos_j + (first half ? g_{j+D/2} : -g_{j-D/2}) sin_j
+    const int p = pos != nullptr ? pos[it.t] : s_of(it.t, S);
+    float c[8], sn[8], dn[8];
+    load8f(cos_t + (int64_t)p * (D / 2) + (gl % HALF) * 8, c);
+    load8f(sin_t + (int64_t)p * (D / 2) + (gl % HALF) * 8, sn);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float partner = __shfl_xor_sync(0xffffffffu, g[j], HALF);
+      dn[j] = gl < HALF ? g[j] * c[j] + partner * sn[j] : g[j] * c[j] - partner * sn[j];
+      if (!qk) dn[j] = g[j];
+    }
+    float o[8];
+    if (qk_norm) {
+      const float r = qk ? rstd[it.t * (Hq + Hkv) + it.hh] : 0.f;
+      float x[8];
+      load8(kqv + it.t * C + it.col + gl * 8, x);
+      const float* wv = it.kind == 0 ? wq : wk;
+      float dot = 0.f, dxr[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        dxr[j] = dn[j] * wv[j];
+        dot += dxr[j] * x[j];
+      }
+      dot = group_sum<LPH>(dot);
+      const float c3 = dot * r * r * r / D;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        o[j] = qk ? r * dxr[j] - x[j] * c3 : dn[j];
+        const float contrib = valid ? dn[j] * rb(x[j] * r) : 0.f;
+        if (it.kind == 0) accq[j] += contrib;
+        else if (it.kind == 1) acck[j] += contrib;
+      }
     } else {
-      const int h = hh - Hq - Hkv;
-      col = (Hkv + Hq) * D + h * D;
-      src = dv + (((int64_t)b * Hkv + h) * S + s) * D;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = dn[j];
     }
-    float g[EPL];
-#pragma unroll
-    for (int j = 0; j < EPL; j += 2) {
-      float2 p = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + lane * EPL + j));
-      g[j] = p.x;
-      g[j + 1] = p.y;
-    }
-    bf16* dst = dkqv + t * C + col + lane * EPL;
-    if (!(is_q || is_k)) {
-#pragma unroll
-      for (int j = 0; j < EPL; j += 2)
-        *reinterpret_cast<uint32_t*>(dst + j) = pack_bf16x2(g[j], g[j + 1]);
-      continue;
-    }
-    // inverse rotation: dn_j = g_j cos_j + (j < D/2 ? g_{j+D/2} : -g_{j-D/2}) sin_j
-    const int p = pos != nullptr ? pos[t] : s;
-    const int fi0 = (lane & 15) * EPL;
-    float dn[EPL];
-#pragma unroll
-    for (int j = 0; j < EPL; ++j) {
-      const float partner = __shfl_xor_sync(0xffffffffu, g[j], 16);
-      const float c = cos_t[(int64_t)p * (D / 2) + fi0 + j];
-      const float sn = sin_t[(int64_t)p * (D / 2) + fi0 + j];
-      dn[j] = lane < 16 ? g[j] * c + partner * sn : g[j] * c - partner * sn;
-    }
-    if (!qk_norm) {
-#pragma unroll
-      for (int j = 0; j < EPL; j += 2)
-        *reinterpret_cast<uint32_t*>(dst + j) = pack_bf16x2(dn[j], dn[j + 1]);
-      continue;
-    }
-    const float r = rstd[t * (Hq + Hkv) + hh];
-    const bf16* w = is_q ? qw : kw;
-    const bf16* xs = kqv + t * C + col + lane * EPL;
-    float x[EPL];
-#pragma unroll
-    for (int j = 0; j < EPL; j += 2) {
-      float2 pp = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(xs + j));
-      x[j] = pp.x;
-      x[j + 1] = pp.y;
-    }
-    float dot = 0.f;
-    float dxr[EPL];
-#pragma unroll
-    for (int j = 0; j < EPL; ++j) {
-      const float wj = __bfloat162float(w[lane * EPL + j]);
-      dxr[j] = dn[j] * wj;
-      dot += dxr[j] * x[j];
-      const float contrib = dn[j] * rb(x[j] * r);
-      if (is_q) accq[j] += contrib; else acck[j] += contrib;
-    }
-    dot = warp_sum(dot);
-    const float c3 = dot * r * r * r / D;
-    float o[EPL];
-#pragma unroll
-    for (int j = 0; j < EPL; ++j) o[j] = r * dxr[j] - x[j] * c3;
-#pragma unroll
-    for (int j = 0; j < EPL; j += 2)
-      *reinterpret_cast<uint32_t*>(dst + j) = pack_bf16x2(o[j], o[j + 1]);
+    if (valid) store8(dkqv + it.t * C + it.col + gl * 8, o);
   }
   if (qk_norm) {
 #pragma unroll
-    for (int j = 0; j < EPL; ++j) {
-      atomicAdd(&s_dqw[lane * EPL + j], accq[j]);
-      atomicAdd(&s_dkw[lane * EPL + j], acck[j]);
+    for (int j = 0; j < 8; ++j) {
+      atomicAdd(&s_dqw[gl * 8 + j], accq[j]);
+      atomicAdd(&s_dkw[gl * 8 + j], acck[j]);
     }
   }
   __syncthreads();
@@ -551,8 +561,8 @@ void rmsnorm_fwd(const bf16* x, const bf16* w, bf16* y, float* rstd, int64_t T, 
 void rmsnorm_bwd(const bf16* dy, const bf16* x, const bf16* w, const float* rstd,
                  const bf16* dres, bf16* dx, float* dw, int64_t T, int H, cudaStream_t s) {
   const int nv = H / 8;
-  const int grid = grid_for(T, 8, 148 * 8);
-  const size_t sm = H * sizeof(float);
+  const int grid = grid_for(T, 8, 148 * 3);
+  const size_t sm = 2 * H * sizeof(float);
   if (nv <= 32)
     rmsnorm_bwd_reg_k<1><<<grid, 256, sm, s>>>(dy, x, w, rstd, dres, dx, dw, T, H);
   else if (nv <= 64)
@@ -560,7 +570,8 @@ void rmsnorm_bwd(const bf16* dy, const bf16* x, const bf16* w, const float* rstd
   else if (nv <= 128)
     rmsnorm_bwd_reg_k<4><<<grid, 256, sm, s>>>(dy, x, w, rstd, dres, dx, dw, T, H);
   else
-    rmsnorm_bwd_k<<<grid, 256, sm, s>>>(dy, x, w, rstd, dres, dx, dw, T, H);
+    rmsnorm_bwd_k<<<grid_for(T, 8, 148 * 8), 256, H * sizeof(float), s>>>(dy, x, w, rstd, dres,
+                                                                         dx, dw, T, H);
 }
 
 void qk_norm_rope_fwd(const bf16* kqv, const bf16* qw, const bf16* kw, const float* cos_t,
@@ -568,12 +579,12 @@ void qk_norm_rope_fwd(const bf16* kqv, const bf16* qw, const bf16* kw, const flo
                       float* rstd, int B, int S, int Hq, int Hkv, int D, float eps, bool qk_norm,
                       cudaStream_t s) {
   const int64_t items = (int64_t)B * S * (Hq + 2 * Hkv);
-  const int grid = grid_for(items, 8);
+  const int grid = grid_for(items, 8 * (256 / D), 148 * 16);
   if (D == 64)
-    qk_norm_rope_fwd_k<2><<<grid, 256, 0, s>>>(kqv, qw, kw, cos_t, sin_t, pos, q, k, v, rstd, B, S,
+    qk_norm_rope_fwd_k<64><<<grid, 256, 0, s>>>(kqv, qw, kw, cos_t, sin_t, pos, q, k, v, rstd, B, S,
                                                Hq, Hkv, eps, qk_norm);
   else
-    qk_norm_rope_fwd_k<4><<<grid, 256, 0, s>>>(kqv, qw, kw, cos_t, sin_t, pos, q, k, v, rstd, B, S,
+    qk_norm_rope_fwd_k<128><<<grid, 256, 0, s>>>(kqv, qw, kw, cos_t, sin_t, pos, q, k, v, rstd, B, S,
                                                Hq, Hkv, eps, qk_norm);
 }
 
@@ -582,12 +593,12 @@ void qk_norm_rope_bwd(const bf16* dq, const bf16* dk, const bf16* dv, const bf16
                       const int32_t* pos, const float* rstd, bf16* dkqv, float* dqw, float* dkw,
                       int B, int S, int Hq, int Hkv, int D, bool qk_norm, cudaStream_t s) {
   const int64_t items = (int64_t)B * S * (Hq + 2 * Hkv);
-  const int grid = grid_for(items, 8, 148 * 16);
+  const int grid = grid_for(items, 8 * (256 / D), 148 * 3);
   if (D == 64)
-    qk_norm_rope_bwd_k<2><<<grid, 256, 0, s>>>(dq, dk, dv, kqv, qw, kw, cos_t, sin_t, pos, rstd,
+    qk_norm_rope_bwd_k<64><<<grid, 256, 0, s>>>(dq, dk, dv, kqv, qw, kw, cos_t, sin_t, pos, rstd,
                                                dkqv, dqw, dkw, B, S, Hq, Hkv, qk_norm);
   else
-    qk_norm_rope_bwd_k<4><<<grid, 256, 0, s>>>(dq, dk, dv, kqv, qw, kw, cos_t, sin_t, pos, rstd,
+    qk_norm_rope_bwd_k<128><<<grid, 256, 0, s>>>(dq, dk, dv, kqv, qw, kw, cos_t, sin_t, pos, rstd,
                                                dkqv, dqw, dkw, B, S, Hq, Hkv, qk_norm);
 }
 

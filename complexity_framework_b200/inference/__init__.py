@@ -2,6 +2,8 @@
 from .batching import AsyncBatcher, BatchConfig, ContinuousBatcher, Request, RequestStatus
 from .engine import (DecodingStrategy, GenerationConfig, InferenceConfig, InferenceEngine,
                      forward_paged, sample_next)
+from .decoding import (LayerSkipDraft, SlidingWindowCache, SpeculativeDecoder, SpeculativeStats,
+                       beam_search, paged_logits)
 from .paged import KVCache, OutOfPages, PagedBatch, PagePool, SeqChunk
 
 PagedKVCache = PagePool
@@ -9,4 +11,5 @@ PagedKVCache = PagePool
 __all__ = ["AsyncBatcher", "BatchConfig", "ContinuousBatcher", "DecodingStrategy",
            "GenerationConfig", "InferenceConfig", "InferenceEngine", "KVCache", "OutOfPages",
            "PagedBatch", "PagedKVCache", "PagePool", "Request", "RequestStatus", "SeqChunk",
-           "forward_paged", "sample_next"]
+           "forward_paged", "sample_next", "LayerSkipDraft", "SlidingWindowCache",
+           "SpeculativeDecoder", "SpeculativeStats", "beam_search", "paged_logits"]

@@ -77,6 +77,34 @@ class PagePool:
         need = -(-length_after // self.page_size) - have
         return need <= len(self.free)
 
+    def fork_sequence(self, src: int, dst: int) -> None:
+        """New sequence ``dst`` with a copy of ``src``'s cached tokens (beam search).
+
+        Full pages are copied whole; the copy is one gather/scatter per pool.
+        """
+        if dst in self.pages:
+            self.free_sequence(dst)
+        self.allocate_sequence(dst)
+        n = self.lengths[src]
+        self.reserve(dst, n)
+        k = -(-n // self.page_size)
+        if k:
+            s_idx = torch.tensor(self.pages[src][:k], device=self.device)
+            d_idx = torch.tensor(self.pages[dst][:k], device=self.device)
+            self.k[:, d_idx] = self.k[:, s_idx]
+            self.v[:, d_idx] = self.v[:, s_idx]
+        self.lengths[dst] = n
+
+    def truncate_sequence(self, seq_id: int, length: int) -> None:
+        """Drop cached tokens past ``length`` (speculative-decoding rollback);
+        pages beyond the new length go back to the free list."""
+        length = max(0, min(length, self.lengths[seq_id]))
+        self.lengths[seq_id] = length
+        keep = -(-length // self.page_size)
+        pages = self.pages[seq_id]
+        while len(pages) > keep:
+            self.free.append(pages.pop())
+
     def memory_usage(self) -> Dict[str, float]:
         used = self.num_pages - len(self.free)
         per_page = 2 * self.num_layers * self.page_size * self.num_kv_heads * self.head_dim * \

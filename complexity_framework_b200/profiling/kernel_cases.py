@@ -1,0 +1,121 @@
+"""Small, self-contained launches of the framework's kernels for profiling.
+
+    python -m complexity_framework_b200.profiling.kernel_cases gemm
+    python -m complexity_framework_b200.profiling.kernel_cases flash
+    python -m complexity_framework_b200.profiling.kernel_cases norms
+
+Each case runs the 200M-shape kernels (inputs larger than L2, a few GB at
+most) ``--iters`` times and prints CUDA-event timings with the fraction of
+the measured peaks, so the same command serves both as the plain run and
+as the target of an ``ncu`` capture (``-k regex:<kernel> -c 1..3``).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from ..ops import check_errors, require
+from .timing import cuda_time, load_measured_peaks
+
+
+def _report(name, ms, flops=0.0, nbytes=0.0):
+    pk = load_measured_peaks()
+    rec = {"case": name, "ms": round(ms, 4)}
+    if flops:
+        rec["tflops"] = round(flops / ms / 1e9, 1)
+        rec["tensor_frac_of_measured"] = round(flops / ms / 1e9 / pk["bf16_tflops"], 3)
+    if nbytes:
+        rec["gbs"] = round(nbytes / ms / 1e6, 1)
+        rec["hbm_frac_of_measured"] = round(nbytes / ms / 1e6 / pk["hbm_gbs"], 3)
+    print(json.dumps(rec), flush=True)
+
+
+def case_gemm(iters: int) -> None:
+    C = require()
+    T, H, A = 16384, 896, 3328
+    dev = "cuda"
+    x = torch.randn(T, H, device=dev).bfloat16()
+    w = (torch.randn(2 * A, H, device=dev) * 0.05).bfloat16()
+    gu = torch.empty(T, 2 * A, device=dev, dtype=torch.bfloat16)
+    act = torch.empty(T, A, device=dev, dtype=torch.bfloat16)
+    rs = torch.rand(T, 4, device=dev)
+    out = torch.empty(T, 2 * A, device=dev, dtype=torch.bfloat16)
+    dW = torch.zeros(A, H, device=dev)
+    fl = 2.0 * T * 2 * A * H
+    _report("gemm_fwd_store", cuda_time(lambda: C.gemm(x, False, w, False, T, 2 * A, H, 0, out=out),
+                                        iters), fl)
+    _report("gemm_swiglu_fwd", cuda_time(lambda: C.gemm(
+        x, False, w, False, T, 2 * A, H, 2, gu=gu, act=act, row_scale=rs, shared_width=3072,
+        expert_width=64, n_experts=4, shared_scale=1.0), iters), fl)
+    _report("gemm_wgrad_splitk", cuda_time(lambda: C.gemm(act, True, x, True, A, H, T, 7, out=dW),
+                                           iters), 2.0 * T * A * H)
+    torch.cuda.synchronize()
+    check_errors(0)
+
+
+def case_flash(iters: int) -> None:
+    from ..ops.flash import flash_forward
+
+    B, Hq, Hkv, S, D = 16, 14, 2, 2048, 64
+    q = torch.randn(B, Hq, S, D, device="cuda").bfloat16()
+    k = torch.randn(B, Hkv, S, D, device="cuda").bfloat16()
+    v = torch.randn(B, Hkv, S, D, device="cuda").bfloat16()
+    fl = 4.0 * B * Hq * S * S * D / 2
+    _report("flash_fwd_causal", cuda_time(lambda: flash_forward(q, k, v, True, D ** -0.5), iters), fl)
+    torch.cuda.synchronize()
+    check_errors(0)
+
+
+def case_norms(iters: int) -> None:
+    C = require()
+    T, H = 32768, 896
+    x = torch.randn(T, H, device="cuda").bfloat16()
+    w = torch.ones(H, device="cuda").bfloat16()
+    y = torch.empty_like(x)
+    rstd = torch.empty(T, device="cuda")
+    nbytes = 2.0 * T * H * 2
+    _report("rmsnorm_fwd", cuda_time(lambda: C.rmsnorm_fwd(x, w, y, rstd, 1e-6), iters),
+            nbytes=nbytes)
+    dy = torch.randn_like(x)
+    dx = torch.empty_like(x)
+    dw = torch.zeros(H, device="cuda")
+    _report("rmsnorm_bwd_resid", cuda_time(
+        lambda: C.rmsnorm_bwd(dy, x, w, rstd, dy, dx, dw), iters), nbytes=4.0 * T * H * 2)
+    B, S, Hq, Hkv, D = 16, 2048, 14, 2, 64
+    kqv = torch.randn(B, S, (Hq + 2 * Hkv) * D, device="cuda").bfloat16()
+    qw = torch.ones(D, device="cuda").bfloat16()
+    fr = torch.outer(torch.arange(S, device="cuda").float(),
+                     1.0 / (10000 ** (torch.arange(0, D, 2, device="cuda").float() / D)))
+    cos, sin = fr.cos().contiguous(), fr.sin().contiguous()
+    pos = torch.arange(S, device="cuda", dtype=torch.int32).repeat(B, 1).contiguous()
+    q = torch.empty(B, Hq, S, D, device="cuda", dtype=torch.bfloat16)
+    k = torch.empty(B, Hkv, S, D, device="cuda", dtype=torch.bfloat16)
+    v = torch.empty_like(k)
+    rs = torch.empty(B * S, Hq + Hkv, device="cuda")
+    nb = 2.0 * kqv.numel() * 2
+    _report("qk_norm_rope_fwd", cuda_time(lambda: C.qk_norm_rope_fwd(
+        kqv, qw, qw, cos, sin, pos, q, k, v, rs, B, S, Hq, Hkv, D, 1e-6, True), iters), nbytes=nb)
+    dk = torch.empty_like(kqv)
+    dqw = torch.zeros(D, device="cuda")
+    _report("qk_norm_rope_bwd", cuda_time(lambda: C.qk_norm_rope_bwd(
+        q, k, v, kqv, qw, qw, cos, sin, pos, rs, dk, dqw, dqw, B, S, Hq, Hkv, D, True), iters),
+        nbytes=3.0 * kqv.numel() * 2)
+    torch.cuda.synchronize()
+    check_errors(0)
+
+
+CASES = {"gemm": case_gemm, "flash": case_flash, "norms": case_norms}
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=sorted(CASES))
+    ap.add_argument("--iters", type=int, default=5)
+    a = ap.parse_args(argv)
+    CASES[a.case](a.iters)
+
+
+if __name__ == "__main__":
+    main()

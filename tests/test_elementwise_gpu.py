@@ -1,0 +1,76 @@
+"""Numerics of the memory-bound sm_100a kernels against fp32 PyTorch references:
+RMSNorm fwd/bwd and the fused per-head QK-RMSNorm + RoPE + head-major scatter."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _rms_ref(x, w, eps):
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)) * w.float()
+
+
+@pytest.mark.parametrize("T,H", [(4096, 896), (1000, 256), (333, 512), (64, 1024)])
+def test_rmsnorm_fwd_bwd(T, H):
+    from complexity_framework_b200.ops.fused import rmsnorm
+
+    torch.manual_seed(0)
+    x = torch.randn(T, H, device="cuda").bfloat16().requires_grad_()
+    w = (1 + 0.1 * torch.randn(H, device="cuda")).bfloat16().requires_grad_()
+    y = rmsnorm(x, w, 1e-6)
+    g = torch.randn_like(y)
+    y.backward(g)
+    xr = x.detach().float().requires_grad_()
+    wr = w.detach().float().requires_grad_()
+    yr = _rms_ref(xr, wr, 1e-6)
+    yr.backward(g.float())
+    assert (y.float() - yr).abs().max() < 3e-2
+    assert (x.grad.float() - xr.grad).abs().max() / xr.grad.abs().max() < 2e-2
+    assert (w.grad.float() - wr.grad).abs().max() / wr.grad.abs().max() < 2e-2
+
+
+def _rope_ref(x, cos, sin, pos):
+    # x [B, H, S, D]; cos/sin [maxpos, D/2]
+    c = torch.cat([cos, cos], -1)[pos][:, None]  # [B,1,S,D]
+    s = torch.cat([sin, sin], -1)[pos][:, None]
+    h = x.shape[-1] // 2
+    rot = torch.cat([-x[..., h:], x[..., :h]], -1)
+    return x * c + rot * s
+
+
+@pytest.mark.parametrize("D,Hq,Hkv", [(64, 14, 2), (128, 8, 8), (64, 4, 1)])
+def test_qk_norm_rope_fwd_bwd(D, Hq, Hkv):
+    from complexity_framework_b200.ops.fused import qk_norm_rope
+
+    torch.manual_seed(0)
+    B, S = 2, 300
+    dev = "cuda"
+    kqv = torch.randn(B, S, (Hq + 2 * Hkv) * D, device=dev).bfloat16().requires_grad_()
+    qw = (1 + 0.1 * torch.randn(D, device=dev)).bfloat16().requires_grad_()
+    kw = (1 + 0.1 * torch.randn(D, device=dev)).bfloat16().requires_grad_()
+    inv = 1.0 / (10000 ** (torch.arange(0, D, 2, device=dev).float() / D))
+    fr = torch.outer(torch.arange(512, device=dev).float(), inv)
+    cos, sin = fr.cos().contiguous(), fr.sin().contiguous()
+    pos = torch.arange(S, device=dev, dtype=torch.int32).repeat(B, 1).contiguous()
+    q, k, v = qk_norm_rope(kqv, qw, kw, cos, sin, pos, Hq, Hkv, D, 1e-6, True)
+    gq, gk, gv = torch.randn_like(q), torch.randn_like(k), torch.randn_like(v)
+    (q.float() * gq).sum().add((k.float() * gk).sum()).add((v.float() * gv).sum()).backward()
+
+    kr = kqv.detach().float().requires_grad_()
+    qwr = qw.detach().float().requires_grad_()
+    kwr = kw.detach().float().requires_grad_()
+    kk, qq, vv = kr.split([Hkv * D, Hq * D, Hkv * D], -1)
+    qh = qq.view(B, S, Hq, D).transpose(1, 2)
+    kh = kk.view(B, S, Hkv, D).transpose(1, 2)
+    vh = vv.view(B, S, Hkv, D).transpose(1, 2)
+    posl = pos.long()
+    qr = _rope_ref(_rms_ref(qh, qwr, 1e-6), cos, sin, posl)
+    kr2 = _rope_ref(_rms_ref(kh, kwr, 1e-6), cos, sin, posl)
+    (qr * gq.float()).sum().add((kr2 * gk.float()).sum()).add((vh * gv.float()).sum()).backward()
+    for a, b in ((q, qr), (k, kr2), (v, vh)):
+        assert (a.float() - b).abs().max() < 5e-2
+    rel = lambda a, b: float((a.float() - b).abs().max() / b.abs().max())  # noqa: E731
+    assert rel(kqv.grad, kr.grad) < 2e-2
+    assert rel(qw.grad, qwr.grad) < 2e-2
+    assert rel(kw.grad, kwr.grad) < 2e-2
