@@ -86,9 +86,10 @@ class RotaryEmbedding(nn.Module):
         self.max_seq_len = max_seq_len
         self.theta = theta
         self.scaling = scaling
-        inv = 1.0 / (theta ** (torch.arange(0, dim, 2).float() / dim))
+        with torch.device("cpu"):  # host copy, also under a meta default device
+            inv = 1.0 / (theta ** (torch.arange(0, dim, 2).float() / dim))
+            self._inv32 = inv.clone()
         self.register_buffer("inv_freq", inv)
-        self._inv32 = inv.clone()
         self._cos: torch.Tensor = torch.empty(0)
         self._sin: torch.Tensor = torch.empty(0)
         self._mscale = 1.0

@@ -108,9 +108,10 @@ class TRHashEngine(nn.Module):
         return self
 
     def _pair_metadata(self, table: torch.Tensor):
-        if has_pair_metadata(self.config):
-            return compile_top2_pair_metadata(table.cpu(), num_experts=self.config.num_experts)
-        return torch.empty(0, dtype=torch.uint8), torch.empty((0, 2), dtype=torch.int32)
+        with torch.device("cpu"):  # host-side metadata, also under a meta default device
+            if has_pair_metadata(self.config):
+                return compile_top2_pair_metadata(table.cpu(), num_experts=self.config.num_experts)
+            return torch.empty(0, dtype=torch.uint8), torch.empty((0, 2), dtype=torch.int32)
 
     @property
     def active_num_experts(self) -> int:

@@ -137,16 +137,21 @@ _BUILDERS = {
 
 
 def build_route_table(config: TRHashEngineConfig) -> torch.Tensor:
-    """CPU ``[top_k, vocab_size]`` int64 route table, validated."""
-    routes = _BUILDERS[config.routing_strategy](config)
+    """CPU ``[top_k, vocab_size]`` int64 route table, validated.
+
+    Always built on the CPU, also under a meta / CUDA default-device context
+    (e.g. deferred initialisation by model loaders)."""
+    with torch.device("cpu"):
+        routes = _BUILDERS[config.routing_strategy](config)
     if tuple(routes.shape) != (config.top_k, config.vocab_size):
         raise RuntimeError("route builder returned an invalid shape")
-    if int(routes.min()) < 0 or int(routes.max()) >= config.num_experts:
-        raise RuntimeError("route builder returned an invalid expert index")
-    if config.top_k > 1:
-        s = routes.sort(dim=0).values
-        if bool((s[1:] == s[:-1]).any()):
-            raise RuntimeError("route builder selected one expert twice")
+    with torch.device("cpu"):
+        if int(routes.min()) < 0 or int(routes.max()) >= config.num_experts:
+            raise RuntimeError("route builder returned an invalid expert index")
+        if config.top_k > 1:
+            s = routes.sort(dim=0).values
+            if bool((s[1:] == s[:-1]).any()):
+                raise RuntimeError("route builder selected one expert twice")
     return routes
 
 
