@@ -104,8 +104,7 @@ class FLOPSCounter:
         if type(mod).__name__ == "TRHashEngine" and torch.is_tensor(x):
             cfg = mod.config
             t = x.numel() // x.shape[-1]
-            routed = 2 * 3 * cfg.hidden_size * cfg.expert_intermediate_size * cfg.top_k
-            return t * routed
+            return t * 2 * 3 * cfg.hidden_size * cfg.active_mlp_width
         if isinstance(mod, (nn.Conv1d, nn.Conv2d)) and torch.is_tensor(out):
             k = mod.weight[0].numel()
             return 2 * out.numel() * k
@@ -114,6 +113,8 @@ class FLOPSCounter:
     def count(self, model: nn.Module, *args, **kwargs) -> ModelComplexity:
         self.reset()
         for name, m in model.named_modules():
+            if ".engine." in name:
+                continue  # the engine hook counts its shared and routed GEMMs
             if isinstance(m, (nn.Linear, nn.Conv1d, nn.Conv2d)) or type(m).__name__ == "TRHashEngine":
                 self._hooks.append(m.register_forward_hook(self._hook(name)))
         try:

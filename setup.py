@@ -52,4 +52,8 @@ setup(
     packages=find_packages(include=["complexity_framework_b200*"]),
     ext_modules=[ext, io_ext],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+    entry_points={"console_scripts": [
+        "cfb=complexity_framework_b200.cli.app:main",
+        "cf-plan-cluster=complexity_framework_b200.training.cluster_plan:main",
+    ]},
 )
