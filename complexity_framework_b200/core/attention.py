@@ -65,6 +65,34 @@ def window_mask(q_len: int, kv_len: int, window: Optional[int], device, dtype) -
     return mask.masked_fill(~ok, float("-inf"))[None, None]
 
 
+def build_rotary(config: AttentionConfig, head_dim: int) -> nn.Module:
+    """Position module for ``rope_type`` / ``rope_fraction`` (registry names:
+    standard/rope, partial_rope, yarn, dynamic_ntk, alibi, learned/none)."""
+    from . import positions  # noqa: F401  (registers partial_rope / alibi / learned)
+    from .registry import POSITION_REGISTRY
+
+    kind = (config.rope_type or "standard").lower()
+    L, th = config.max_position_embeddings, config.rope_theta
+    if kind in ("learned", "none", "nope"):
+        return NoRotary(head_dim, L, th)
+    if kind == "alibi":
+        return POSITION_REGISTRY.build("alibi", head_dim, L, th,
+                                       num_heads=config.num_attention_heads)
+    if config.rope_fraction < 1.0 and kind in ("standard", "rope", "partial_rope", "partial"):
+        return POSITION_REGISTRY.build("partial_rope", head_dim, L, th,
+                                       fraction=config.rope_fraction)
+    if kind in ("standard", "rope", "default"):
+        return RotaryEmbedding(head_dim, max_seq_len=L, theta=th)
+    return POSITION_REGISTRY.build(kind, head_dim, L, th)
+
+
+class NoRotary(RotaryEmbedding):
+    """Identity rotation (absolute learned positions live at the model input)."""
+
+    def rotate(self, q, k, cos, sin):
+        return q, k
+
+
 @register_attention("gqa")
 @register_attention("grouped_query")
 class GroupedQueryAttention(nn.Module):
@@ -85,8 +113,7 @@ class GroupedQueryAttention(nn.Module):
         if self.use_qk_norm:
             self.q_norm = RMSNorm(D, eps=config.norm_eps)
             self.k_norm = RMSNorm(D, eps=config.norm_eps)
-        self.rotary_emb = RotaryEmbedding(D, max_seq_len=config.max_position_embeddings,
-                                          theta=config.rope_theta)
+        self.rotary_emb = build_rotary(config, D)
         self.attention_dropout = config.attention_dropout
         self.sliding_window = config.sliding_window
         self.is_causal = config.is_causal
@@ -187,6 +214,11 @@ class GroupedQueryAttention(nn.Module):
                 mask = mask + attention_mask
         else:
             mask = attention_mask
+        if getattr(self.rotary_emb, "uses_bias", False):
+            bias = self.rotary_emb.bias(q_len, kv_len, q.device, q.dtype)
+            if mask is None and self.is_causal:
+                mask = window_mask(q_len, kv_len, self.sliding_window, q.device, q.dtype)
+            mask = bias if mask is None else mask + bias
         p = self.attention_dropout if self.training else 0.0
         causal = self.is_causal and mask is None and q_len == kv_len
         return F.scaled_dot_product_attention(q, k, v, attn_mask=mask, dropout_p=p,
@@ -218,12 +250,13 @@ class GroupedQueryAttention(nn.Module):
         if self.use_qk_norm:
             q = self.q_norm(q.contiguous())
             k = self.k_norm(k.contiguous())
+        if getattr(self.rotary_emb, "uses_bias", False):
+            raise NotImplementedError("paged decoding does not support ALiBi attention bias")
         cos_h, sin_h = self.rotary_emb.tables(cache.max_position + 1, x.device)
         pos = cache.positions
         c = torch.cat((cos_h[pos], cos_h[pos]), -1)[:, None].to(q.dtype)
         s = torch.cat((sin_h[pos], sin_h[pos]), -1)[:, None].to(q.dtype)
-        q = q * c + rotate_half(q) * s
-        k = k * c + rotate_half(k) * s
+        q, k = self.rotary_emb.rotate(q, k, c, s)
         cache.write(layer_idx, k, v)
         o = cache.attend(layer_idx, q, self.attn_scale)  # [N, Hq, D]
         o = o.reshape(1, N, qd)

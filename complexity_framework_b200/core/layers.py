@@ -66,9 +66,11 @@ def rotate_half(x: torch.Tensor) -> torch.Tensor:
 
 
 def apply_rotary_pos_emb(q, k, cos, sin):
-    """Rotate-half RoPE on [B, H, S, D] tensors with cos/sin of shape [S, D]."""
-    cos = cos[None, None]
-    sin = sin[None, None]
+    """Rotate-half RoPE on [B, H, S, D] tensors with cos/sin of shape [S, D]
+    (or any cos/sin already broadcastable against q and k)."""
+    if cos.dim() == 2:
+        cos = cos[None, None]
+        sin = sin[None, None]
     return q * cos + rotate_half(q) * sin, k * cos + rotate_half(k) * sin
 
 

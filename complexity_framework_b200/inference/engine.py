@@ -123,6 +123,9 @@ def forward_paged(model, ids: torch.Tensor, batch: PagedBatch) -> torch.Tensor:
     """Final-norm hidden states [N, H] of the N new tokens (``ids`` is [N])."""
     tok = ids.view(1, -1)
     x = model.embed(tok)
+    pe = getattr(model, "embed_positions", None)
+    if pe is not None:
+        x = x + pe.weight[batch.positions].to(x.dtype)[None]
     for layer in model.layers:
         x = layer.forward_paged(x, batch, tok)
     return model.norm(x)[0]

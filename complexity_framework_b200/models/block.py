@@ -45,7 +45,11 @@ class TransformerBlock(nn.Module):
             use_qk_norm=config.use_qk_norm, sliding_window=config.sliding_window,
             use_sdpa=config.use_sdpa, is_causal=config.is_causal, rope_type=config.rope_type,
             rope_fraction=config.rope_fraction, use_mup_attn_scale=config.use_mup_attn_scale,
-            layer_idx=layer_idx, vocab_size=config.vocab_size)
+            layer_idx=layer_idx, vocab_size=config.vocab_size,
+            extra={k: getattr(config, k) for k in (
+                "tr_mha_num_experts", "tr_mha_adapter_rank", "tr_mha_top_k", "tr_mha_targets",
+                "causal_conv_kernel_size")})
+        from ..core import attention_variants  # noqa: F401  (registers experimental types)
         attn_type = config.attention_type
         if attn_type not in ATTENTION_REGISTRY:
             raise ValueError(f"attention_type {attn_type!r} is not available; supported: "
@@ -72,6 +76,7 @@ class TransformerBlock(nn.Module):
             layer_idx=layer_idx, use_custom_kernels=config.use_custom_kernels,
             use_cggr=config.use_cggr, active_num_experts=config.active_num_experts,
             active_expert_width=config.active_expert_width, attention_type=attn_type)
+        from ..core import dense_mlp  # noqa: F401  (registers dense MLP types)
         self.mlp = MLP_REGISTRY.build(config.mlp_type, mlp_cfg)
 
     def forward(self, hidden_states: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,
@@ -79,6 +84,8 @@ class TransformerBlock(nn.Module):
                 token_ids: Optional[torch.Tensor] = None, **unused
                 ) -> Tuple[torch.Tensor, Optional[Any], None]:
         h = self.input_layernorm(hidden_states)
+        if token_ids is not None and hasattr(self.self_attn, "set_token_ids"):
+            self.self_attn.set_token_ids(token_ids)
         x, new_kv = self.self_attn(h, attention_mask=attention_mask,
                                    past_key_value=past_key_value, use_cache=use_cache,
                                    residual=hidden_states)
@@ -88,6 +95,8 @@ class TransformerBlock(nn.Module):
 
     def forward_paged(self, hidden_states: torch.Tensor, cache, token_ids: torch.Tensor):
         h = self.input_layernorm(hidden_states)
+        if hasattr(self.self_attn, "set_token_ids"):
+            self.self_attn.set_token_ids(token_ids)
         x = self.self_attn.forward_paged(h, cache, self.layer_idx, residual=hidden_states)
         h = self.post_attention_layernorm(x)
         return self.mlp(h, token_ids=token_ids, residual=x)

@@ -43,6 +43,11 @@ class ComplexityModel(nn.Module):
                                                  eps=config.norm_eps)
         self.lm_head = (None if config.tie_word_embeddings
                         else nn.Linear(config.hidden_size, config.vocab_size, bias=False))
+        if str(config.rope_type).lower() == "learned":
+            from ..core.positions import LearnedPositionalEmbedding
+
+            self.embed_positions = LearnedPositionalEmbedding(config.max_position_embeddings,
+                                                              config.hidden_size)
         self._gradient_checkpointing = False
         self.apply(self._init_weights)
         self._init_residual_scaling()
@@ -51,6 +56,8 @@ class ComplexityModel(nn.Module):
     # ------------------------------------------------------------------ init
     def _init_weights(self, module: nn.Module) -> None:
         std = self.config.initializer_range
+        if getattr(module, "_deterministic_init", False):
+            return  # initialised from its own seeded generator
         if isinstance(module, nn.Linear):
             nn.init.normal_(module.weight, mean=0.0, std=std)
             if module.bias is not None:
@@ -133,6 +140,11 @@ class ComplexityModel(nn.Module):
                 raise ValueError("inputs_embeds hidden size does not match the model configuration")
             hidden = inputs_embeds
         B, S = hidden.shape[:2]
+        if hasattr(self, "embed_positions"):
+            past_len = 0
+            if past_key_values is not None and past_key_values[0] is not None:
+                past_len = past_key_values[0][0].shape[2]
+            hidden = self.embed_positions(hidden, offset=past_len)
         token_ids = routing_ids if routing_ids is not None else input_ids
         if token_ids is None:
             token_ids = torch.zeros(B, S, dtype=torch.long, device=hidden.device)
