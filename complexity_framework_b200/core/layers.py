@@ -41,6 +41,14 @@ class RMSNorm(nn.Module):
         y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
         return self.weight * y.to(x.dtype)
 
+    def forward_with_skip(self, x: torch.Tensor):
+        """``(norm(x), x)`` where gradients of both outputs are summed in one kernel."""
+        if use_fused(x) and self.weight.dtype == torch.bfloat16 and x.shape[-1] % 8 == 0:
+            from ..ops.fused import rmsnorm_skip
+
+            return rmsnorm_skip(x, self.weight, self.eps)
+        return self(x), x
+
     def extra_repr(self) -> str:
         return f"{self.hidden_size}, eps={self.eps}"
 

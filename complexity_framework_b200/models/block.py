@@ -83,15 +83,23 @@ class TransformerBlock(nn.Module):
                 past_key_value: Optional[Any] = None, use_cache: bool = False,
                 token_ids: Optional[torch.Tensor] = None, **unused
                 ) -> Tuple[torch.Tensor, Optional[Any], None]:
-        h = self.input_layernorm(hidden_states)
+        h, hidden_states = self._norm_skip(self.input_layernorm, hidden_states)
         if token_ids is not None and hasattr(self.self_attn, "set_token_ids"):
             self.self_attn.set_token_ids(token_ids)
         x, new_kv = self.self_attn(h, attention_mask=attention_mask,
                                    past_key_value=past_key_value, use_cache=use_cache,
                                    residual=hidden_states)
-        h = self.post_attention_layernorm(x)
+        h, x = self._norm_skip(self.post_attention_layernorm, x)
         x = self.mlp(h, token_ids=token_ids, residual=x)
         return x, new_kv, None
+
+    @staticmethod
+    def _norm_skip(norm, x):
+        """Norm output plus the residual stream routed through the norm, so the
+        two gradients of ``x`` meet in the norm's backward kernel."""
+        if hasattr(norm, "forward_with_skip") and torch.is_grad_enabled() and x.requires_grad:
+            return norm.forward_with_skip(x)
+        return norm(x), x
 
     def forward_paged(self, hidden_states: torch.Tensor, cache, token_ids: torch.Tensor):
         h = self.input_layernorm(hidden_states)

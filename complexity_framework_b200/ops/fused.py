@@ -241,6 +241,41 @@ def rmsnorm(x, w, eps):
     return RMSNormFn.apply(x, w, eps)
 
 
+class RMSNormSkipFn(torch.autograd.Function):
+    """``(rmsnorm(x), x)``: the second output is the residual stream itself.
+
+    Routing the residual through the norm lets its backward receive both
+    gradients of ``x`` (through the norm and through the skip connection) and
+    sum them inside the RMSNorm-backward kernel instead of in a separate add.
+    """
+
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        C = require()
+        xc = _c(x)
+        y = torch.empty_like(xc)
+        H = x.shape[-1]
+        rstd = torch.empty(xc.numel() // H, device=x.device, dtype=torch.float32)
+        C.rmsnorm_fwd(xc, _c(w), y, rstd, float(eps))
+        ctx.save_for_backward(xc, w, rstd)
+        return y, x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, dy, dskip):
+        C = require()
+        x, w, rstd = ctx.saved_tensors
+        dx = torch.empty_like(x)
+        dw = torch.zeros(w.numel(), device=x.device, dtype=torch.float32)
+        if dy is None:
+            return dskip, None, None
+        C.rmsnorm_bwd(_c(dy), x, _c(w), rstd, None if dskip is None else _c(dskip), dx, dw)
+        return dx, dw.to(w.dtype), None
+
+
+def rmsnorm_skip(x, w, eps):
+    return RMSNormSkipFn.apply(x, w, eps)
+
+
 # ---------------------------------------------------------- QK-norm + RoPE
 class QKNormRopeFn(torch.autograd.Function):
     """kqv [B,S,(2Hkv+Hq)D] -> head-major q [B,Hq,S,D], k/v [B,Hkv,S,D]."""

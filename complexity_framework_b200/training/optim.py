@@ -93,6 +93,10 @@ class _FlatGroup:
             p.data = self.compute[o:o + n].view(p.shape)
             p.grad = self.grad[o:o + n].view(p.shape)
 
+    def rebind_grads(self) -> None:
+        for p, o, n in zip(self.params, self.offsets, self.sizes):
+            p.grad = self.grad[o:o + n].view(p.shape)
+
     def view(self, flat: torch.Tensor, i: int) -> Optional[torch.Tensor]:
         """View of parameter i inside a full-length flat buffer, or inside a
         shard-length buffer when the parameter lies entirely in this shard."""
@@ -160,14 +164,40 @@ class FusedAdamW(torch.optim.Optimizer):
         return [fg.grad for fg in self.flat_groups]
 
     def zero_grad(self, set_to_none: bool = False) -> None:
+        """Drop the gradient views: the next backward hands each parameter a fresh
+        gradient tensor (no accumulate-add kernel per parameter), and
+        ``_gather_grads`` copies them into the flat buffer with a few
+        multi-tensor launches."""
         for fg in self.flat_groups:
-            fg.grad.zero_()
-            if any(p.grad is None for p in fg.params):
-                fg.rebind()
+            for p in fg.params:
+                p.grad = None
+        self._gathered = False
+
+    @torch.no_grad()
+    def _gather_grads(self) -> None:
+        if getattr(self, "_gathered", True):
+            return
+        for fg in self.flat_groups:
+            dst, src, missing = [], [], []
+            for p, o, n in zip(fg.params, fg.offsets, fg.sizes):
+                view = fg.grad[o:o + n].view(p.shape)
+                g = p.grad
+                if g is None:
+                    missing.append(view)
+                elif g.data_ptr() != view.data_ptr():
+                    dst.append(view)
+                    src.append(g)
+            if dst:
+                torch._foreach_copy_(dst, src)
+            if missing:
+                torch._foreach_zero_(missing)
+            fg.rebind_grads()
+        self._gathered = True
 
     @torch.no_grad()
     def reduce_gradients(self) -> None:
         """Average gradients over the data-parallel group (one collective per group)."""
+        self._gather_grads()
         if self.world == 1 or self._fused is not None:
             return
         import torch.distributed as dist
@@ -232,6 +262,7 @@ class FusedAdamW(torch.optim.Optimizer):
         """Compute the global grad norm on the device; the next ``step(clip=True)``
         scales by ``min(1, max_norm / (norm + 1e-6))``.  Returns the norm (no sync)."""
         self._max_norm = float(max_norm)
+        self._gather_grads()
         if self._fused is not None:
             return self._norm[0]  # computed inside the fused reduce kernels during step()
         if self._use_kernels():
@@ -264,6 +295,7 @@ class FusedAdamW(torch.optim.Optimizer):
     @torch.no_grad()
     def step(self, closure=None, clip: bool = False):
         loss = closure() if closure is not None else None
+        self._gather_grads()
         self._step_count += 1
         t = self._step_count
         if self._fused is not None:
