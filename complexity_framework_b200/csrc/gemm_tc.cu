@@ -49,10 +49,17 @@ __host__ __device__ constexpr int epi_slots(int epi) {
              ? 2
              : 0;
 }
+// Epilogue operands read by TMA (32x32 bf16 boxes per column chunk): the
+// residual for EPI_RESID, the saved gate and up pre-activations for
+// EPI_SWIGLU_BWD.  Two chunks per warp are in flight (double buffer).
+__host__ __device__ constexpr int epi_loads(int epi) {
+  return epi == EPI_SWIGLU_BWD ? 2 : (epi == EPI_RESID ? 1 : 0);
+}
 constexpr int kEpiWarps = 8;
 constexpr int kBoxBytes = 32 * 32 * 2;
+constexpr int kBarrierBytes = 512;
 
-template <int BN, bool PAIR, int SLOTS>
+template <int BN, bool PAIR, int SLOTS, int LOADS = 0>
 struct GemmCfg {
   // With PAIR, a 256-row tile is split over a CTA pair: each CTA holds its 128
   // A rows and half of the BN B rows; the even CTA issues M=256 MMAs.
@@ -60,27 +67,16 @@ struct GemmCfg {
   static constexpr int A_BYTES = kBM * kBK * 2;
   static constexpr int B_BYTES = B_ROWS * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGING_BYTES = SLOTS * kBoxBytes * kEpiWarps;
+  static constexpr int WARP_STAGING = (SLOTS + 2 * LOADS) * kBoxBytes;
+  static constexpr int STAGING_BYTES = WARP_STAGING * kEpiWarps;
   static constexpr int STAGES = (227 * 1024 - 2048 - STAGING_BYTES) / STAGE_BYTES > 8
                                     ? 8
                                     : (227 * 1024 - 2048 - STAGING_BYTES) / STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int TILE_M = PAIR ? 2 * kBM : kBM;
   static constexpr int SMEM_BYTES =
-      STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+      STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + kBarrierBytes;
 };
-
-__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v) {
-  const uint4* s = reinterpret_cast<const uint4*>(src);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint4 w = s[q];
-    float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y), c = unpack_bf16x2(w.z),
-           d = unpack_bf16x2(w.w);
-    v[q * 8 + 0] = a.x; v[q * 8 + 1] = a.y; v[q * 8 + 2] = b.x; v[q * 8 + 3] = b.y;
-    v[q * 8 + 4] = c.x; v[q * 8 + 5] = c.y; v[q * 8 + 6] = d.x; v[q * 8 + 7] = d.y;
-  }
-}
 
 // Lane `lane` writes row `lane` of a 32x32 bf16 box in the 64-byte-swizzled
 // layout the store tensor map expects (16-byte unit q of row r sits at unit
@@ -123,6 +119,61 @@ struct BoxRing {
   }
 };
 
+// Row `lane` of a staged 32x32 bf16 box (64-byte swizzle, as written by TMA).
+__device__ __forceinline__ void read_box_row(const uint8_t* box, int lane, float* v) {
+  const uint4* rowp = reinterpret_cast<const uint4*>(box + lane * 64);
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 w = rowp[q ^ sw];
+    const float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y), c = unpack_bf16x2(w.z),
+                 d = unpack_bf16x2(w.w);
+    v[q * 8 + 0] = a.x; v[q * 8 + 1] = a.y; v[q * 8 + 2] = b.x; v[q * 8 + 3] = b.y;
+    v[q * 8 + 4] = c.x; v[q * 8 + 5] = c.y; v[q * 8 + 6] = d.x; v[q * 8 + 7] = d.y;
+  }
+}
+
+// Per-warp double-buffered TMA loads of epilogue operand boxes.  Tickets are
+// issued and consumed in the same order; ticket k uses slot k & 1.
+template <int LOADS>
+struct LoadRing {
+  uint8_t* base;    // 2 slots x LOADS boxes
+  uint64_t* bar;    // 2 mbarriers
+  uint32_t issued;
+  uint32_t consumed;
+  int lane;
+  __device__ __forceinline__ uint8_t* box(uint32_t ticket, int i) const {
+    return base + ((ticket & 1u) * LOADS + i) * kBoxBytes;
+  }
+  // lane 0 issues the LOADS boxes at (xs[i], y)
+  __device__ __forceinline__ void issue(const CUtensorMap* map, const int* xs, int y) {
+    if (lane == 0) {
+      uint64_t* b = &bar[issued & 1u];
+      mbar_arrive_expect_tx(b, LOADS * kBoxBytes);
+#pragma unroll
+      for (int i = 0; i < LOADS; ++i) tma_load_2d(box(issued, i), map, b, xs[i], y);
+    }
+    ++issued;
+  }
+  __device__ __forceinline__ bool wait(volatile int* abort_flag, int* err) {
+    const bool ok = mbar_wait(&bar[consumed & 1u], (consumed >> 1) & 1u, abort_flag, err,
+                              kErrTimeoutFull, 14);
+    return ok;
+  }
+  // every lane has read the consumed boxes; the slot may be refilled
+  __device__ __forceinline__ void release() {
+    __syncwarp();
+    ++consumed;
+  }
+  // bounded wait for copies still in flight before the CTA exits
+  __device__ __forceinline__ void drain(int* err) {
+    while (consumed < issued) {
+      mbar_wait(&bar[consumed & 1u], (consumed >> 1) & 1u, nullptr, err, kErrTimeoutFull, 15);
+      ++consumed;
+    }
+  }
+};
+
 // Scale that multiplies SwiGLU activation column `c` of row `row`.
 __device__ __forceinline__ float swiglu_col_scale(const GemmEpi& ep, int row, int c) {
   if (c < ep.shared_width) return ep.shared_scale;
@@ -137,7 +188,8 @@ __global__ void __launch_bounds__(384, 1)
                    const __grid_constant__ CUtensorMap tmC1, int M, int N, int K, int ksplit,
                    GemmEpi ep, int* err) {
   constexpr int SLOTS = epi_slots(EPI);
-  using Cfg = GemmCfg<BN, PAIR, SLOTS>;
+  constexpr int LOADS = epi_loads(EPI);
+  using Cfg = GemmCfg<BN, PAIR, SLOTS, LOADS>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int B_ROWS = Cfg::B_ROWS;
 
@@ -150,7 +202,8 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  uint64_t* load_bar = tempty_bar + 2;  // 2 per epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(load_bar + 2 * kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
@@ -178,6 +231,7 @@ __global__ void __launch_bounds__(384, 1)
       // one arrival per epilogue warp of every CTA in the MMA group
       mbar_init(&tempty_bar[a], PAIR ? 16 : 8);
     }
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&load_bar[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -333,13 +387,33 @@ __global__ void __launch_bounds__(384, 1)
     uint32_t acc_phase = 0;
     const uint32_t tempty_peer0 = mapa_shared(smem_u32(&tempty_bar[0]), 0);
     const uint32_t tempty_peer1 = mapa_shared(smem_u32(&tempty_bar[1]), 0);
-    BoxRing<SLOTS ? SLOTS : 1> ring{staging + (warp - 4) * SLOTS * kBoxBytes, 0, lane};
+    uint8_t* wstage = staging + (warp - 4) * Cfg::WARP_STAGING;
+    BoxRing<SLOTS ? SLOTS : 1> ring{wstage, 0, lane};
+    LoadRing<LOADS ? LOADS : 1> lring{wstage + SLOTS * kBoxBytes, load_bar + 2 * (warp - 4), 0u,
+                                      0u, lane};
+    bool ep_ok = true;
     for (int u = unit; u < total; u += units) {
       const int t = u / ksplit;
       const int m_blk = t / num_n;
       const int n_blk = t % num_n;
       const int m0 = m_blk * Cfg::TILE_M + static_cast<int>(rank) * kBM;
       const int n0 = n_blk * BN;
+      // operand boxes of the warp's first column chunk load while the MMA runs
+      const int cbeg = wg * (BN / 2);
+      if constexpr (EPI == EPI_SWIGLU_BWD) {
+        if (n0 + cbeg < N) {
+          const int ac = n0 + cbeg;
+          const int xs[2] = {(ac / kSwigluBlock) * 2 * kSwigluBlock + ac % kSwigluBlock,
+                             (ac / kSwigluBlock) * 2 * kSwigluBlock + ac % kSwigluBlock +
+                                 kSwigluBlock};
+          lring.issue(&tmC1, xs, m0 + wq * 32);
+        }
+      } else if constexpr (EPI == EPI_RESID) {
+        if (n0 + cbeg < N) {
+          const int xs[1] = {n0 + cbeg};
+          lring.issue(&tmC1, xs, m0 + wq * 32);
+        }
+      }
       if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, err, kErrTimeoutTmem, 13)) break;
       tc_fence_after();
       const int row = m0 + wq * 32 + lane;
@@ -374,42 +448,47 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
       } else if constexpr (EPI == EPI_SWIGLU_BWD) {
-        // Accumulator = d(act) for activation columns [n0, n0+BN).
+        // Accumulator = d(act) for activation columns [n0, n0+BN); the saved
+        // pre-activations g, u arrive in shared memory by TMA (prefetched).
 #pragma unroll 1
-        for (int c = wg * BN / 2; c < (wg + 1) * BN / 2; c += 32) {
+        for (int c = cbeg; c < cbeg + BN / 2; c += 32) {
           const int act_col = n0 + c;
-          const bool col_ok = row_ok && act_col < N;
-          const int blk = act_col / kSwigluBlock;
-          const int w = act_col % kSwigluBlock;
-          const int64_t goff = static_cast<int64_t>(row) * ep.ldgu + blk * 2 * kSwigluBlock + w;
-          // issue the global loads of the saved pre-activations before reading TMEM
-          float g[32], u[32];
-          if (col_ok) {
-            load_bf16x32(ep.gu + goff, g);
-            load_bf16x32(ep.gu + goff + kSwigluBlock, u);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) g[i] = u[i] = 0.0f;
+          if (act_col >= N) break;  // warp-uniform; later chunks are out of range too
+          if (c + 32 < cbeg + BN / 2 && act_col + 32 < N) {
+            const int ac = act_col + 32;
+            const int xs[2] = {(ac / kSwigluBlock) * 2 * kSwigluBlock + ac % kSwigluBlock,
+                               (ac / kSwigluBlock) * 2 * kSwigluBlock + ac % kSwigluBlock +
+                                   kSwigluBlock};
+            lring.issue(&tmC1, xs, m0 + wq * 32);
           }
           float da[32];
           tmem_ld32(tbase + c, da);
           tmem_wait_ld();
-          if (act_col < N) {  // warp-uniform
-            const float s = col_ok ? swiglu_col_scale(ep, row, act_col) : 0.0f;
-            float dg[32], du[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float sg = 1.0f / (1.0f + __expf(-g[i]));
-              const float sl = g[i] * sg;
-              const float d = da[i] * s;
-              du[i] = d * sl;
-              dg[i] = d * u[i] * sg * (1.0f + g[i] * (1.0f - sg));
-            }
-            const int x = blk * 2 * kSwigluBlock + w;
-            ring.put(&tmC0, dg, 1.0f, x, m0 + wq * 32);
-            ring.put(&tmC0, du, 1.0f, x + kSwigluBlock, m0 + wq * 32);
+          if (!lring.wait(abort_flag, err)) {
+            ep_ok = false;
+            break;
           }
+          float g[32], u[32];
+          read_box_row(lring.box(lring.consumed, 0), lane, g);
+          read_box_row(lring.box(lring.consumed, 1), lane, u);
+          lring.release();
+          const int blk = act_col / kSwigluBlock;
+          const int w = act_col % kSwigluBlock;
+          const float s = row_ok ? swiglu_col_scale(ep, row, act_col) : 0.0f;
+          float dg[32], du[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float sg = sigmoid_f(g[i]);
+            const float sl = g[i] * sg;
+            const float d = da[i] * s;
+            du[i] = d * sl;
+            dg[i] = d * u[i] * sg * (1.0f + g[i] * (1.0f - sg));
+          }
+          const int x = blk * 2 * kSwigluBlock + w;
+          ring.put(&tmC0, dg, 1.0f, x, m0 + wq * 32);
+          ring.put(&tmC0, du, 1.0f, x + kSwigluBlock, m0 + wq * 32);
         }
+        if (!ep_ok) break;
       } else if constexpr (EPI == EPI_CE_STATS) {
         // Store bf16 logits and, per (row, n-tile), the max and sum(exp(x-max)).
         float mx = -INFINITY, se = 0.0f;
@@ -445,8 +524,11 @@ __global__ void __launch_bounds__(384, 1)
         for (int c = wg * BN / 2; c < (wg + 1) * BN / 2; c += 32) {
           float r[32];
           if constexpr (EPI == EPI_RESID) {
-            if (row_ok && n0 + c < N)
-              load_bf16x32(ep.r + static_cast<int64_t>(row) * ep.ldr + n0 + c, r);
+            if (n0 + c >= N) break;  // warp-uniform
+            if (c + 32 < (wg + 1) * BN / 2 && n0 + c + 32 < N) {
+              const int xs[1] = {n0 + c + 32};
+              lring.issue(&tmC1, xs, m0 + wq * 32);
+            }
           }
           float v[32];
           tmem_ld32(tbase + c, v);
@@ -454,11 +536,15 @@ __global__ void __launch_bounds__(384, 1)
           if constexpr (EPI == EPI_STORE) {
             if (n0 + c < N) ring.put(&tmC0, v, ep.alpha, n0 + c, m0 + wq * 32);
           } else if constexpr (EPI == EPI_RESID) {
-            if (n0 + c < N) {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] = v[i] * ep.alpha + (row_ok ? r[i] : 0.0f);
-              ring.put(&tmC0, v, 1.0f, n0 + c, m0 + wq * 32);
+            if (!lring.wait(abort_flag, err)) {
+              ep_ok = false;
+              break;
             }
+            read_box_row(lring.box(lring.consumed, 0), lane, r);
+            lring.release();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = v[i] * ep.alpha + r[i];
+            ring.put(&tmC0, v, 1.0f, n0 + c, m0 + wq * 32);
           } else if (row_ok && n0 + c < N) {
             if constexpr (EPI == EPI_F32_ATOMIC) {
               float* out = reinterpret_cast<float*>(ep.c) + static_cast<int64_t>(row) * ep.ldc + n0 + c;
@@ -482,6 +568,7 @@ __global__ void __launch_bounds__(384, 1)
             }
           }
         }
+        if (!ep_ok) break;
       }
       tc_fence_before();
       __syncwarp();
@@ -494,6 +581,7 @@ __global__ void __launch_bounds__(384, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (LOADS > 0) lring.drain(err);
     if (SLOTS > 0 && lane == 0) bulk_wait_group_all();
   }
 
@@ -559,7 +647,7 @@ template <int BN, bool A_MN, bool B_MN, int EPI, bool PAIR>
 static int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap* tc,
                        int M, int N, int K, const GemmEpi& ep, int num_sms, cudaStream_t stream,
                        int* err, int ksplit = 1) {
-  using Cfg = GemmCfg<BN, PAIR, epi_slots(EPI)>;
+  using Cfg = GemmCfg<BN, PAIR, epi_slots(EPI), epi_loads(EPI)>;
   auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI, PAIR>;
   static int max_units = -1;  // resident CTAs (or CTA pairs), one query per instantiation
   cudaLaunchConfig_t cfg = {};
@@ -664,9 +752,12 @@ int gemm_tc_launch(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream, in
   memset(tc, 0, sizeof(tc));
   switch (g.epi) {
     case EPI_STORE:
-    case EPI_RESID:
     case EPI_CE_STATS:
       rc = make_tmap_2d_store(&tc[0], ep.c, g.M, g.N, ep.ldc);
+      break;
+    case EPI_RESID:
+      rc = make_tmap_2d_store(&tc[0], ep.c, g.M, g.N, ep.ldc);
+      if (!rc) rc = make_tmap_2d_store(&tc[1], ep.r, g.M, g.N, ep.ldr);  // residual loads
       break;
     case EPI_SWIGLU_FWD:
       rc = make_tmap_2d_store(&tc[0], ep.gu, g.M, g.N, ep.ldgu);
@@ -676,6 +767,10 @@ int gemm_tc_launch(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream, in
       int64_t cols = 2 * static_cast<int64_t>((g.N + kSwigluBlock - 1) / kSwigluBlock) * kSwigluBlock;
       if (cols > ep.ldc) cols = ep.ldc;
       rc = make_tmap_2d_store(&tc[0], ep.c, g.M, cols, ep.ldc);
+      int64_t gcols = 2 * static_cast<int64_t>((g.N + kSwigluBlock - 1) / kSwigluBlock) *
+                      kSwigluBlock;
+      if (gcols > ep.ldgu) gcols = ep.ldgu;
+      if (!rc) rc = make_tmap_2d_store(&tc[1], ep.gu, g.M, gcols, ep.ldgu);  // g/u loads
       break;
     }
     default:

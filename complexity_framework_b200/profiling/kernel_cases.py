@@ -51,6 +51,18 @@ def case_gemm(iters: int) -> None:
         expert_width=64, n_experts=4, shared_scale=1.0), iters), fl)
     _report("gemm_wgrad_splitk", cuda_time(lambda: C.gemm(act, True, x, True, A, H, T, 7, out=dW),
                                            iters), 2.0 * T * A * H)
+    # data gradient of the down projection with the SwiGLU-backward epilogue
+    wd = (torch.randn(H, A, device=dev) * 0.05).bfloat16()
+    dy = torch.randn(T, H, device=dev).bfloat16()
+    dgu = torch.empty(T, 2 * A, device=dev, dtype=torch.bfloat16)
+    _report("gemm_swiglu_bwd", cuda_time(lambda: C.gemm(
+        dy, False, wd, True, T, A, H, 3, out=dgu, gu=gu, row_scale=rs, shared_width=3072,
+        expert_width=64, n_experts=4, shared_scale=1.0), iters), 2.0 * T * A * H)
+    # down projection with the residual-add epilogue
+    res = torch.randn(T, H, device=dev).bfloat16()
+    o = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
+    _report("gemm_down_resid", cuda_time(lambda: C.gemm(act, False, wd, False, T, H, A, 1, out=o,
+                                                         residual=res), iters), 2.0 * T * A * H)
     torch.cuda.synchronize()
     check_errors(0)
 
