@@ -117,6 +117,24 @@ struct BoxRing {
     }
     slot = slot + 1 == SLOTS ? 0 : slot + 1;
   }
+  // two boxes staged together, one fence / sync / commit group (needs SLOTS >= 2)
+  __device__ __forceinline__ void put2(const CUtensorMap* map, const float* v0, int x0,
+                                       const float* v1, int x1, int y) {
+    if (lane == 0) bulk_wait_group_read<SLOTS / 2 - 1>();  // previous pair has been read
+    __syncwarp();
+    uint8_t* b0 = base + slot * kBoxBytes;
+    uint8_t* b1 = base + (slot + 1) * kBoxBytes;
+    stage_row_bf16(b0, lane, v0, 1.0f);
+    stage_row_bf16(b1, lane, v1, 1.0f);
+    fence_proxy_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(map, b0, x0, y);
+      tma_store_2d(map, b1, x1, y);
+      bulk_commit_group();
+    }
+    slot = slot + 2 >= SLOTS ? 0 : slot + 2;
+  }
 };
 
 // Row `lane` of a staged 32x32 bf16 box (64-byte swizzle, as written by TMA).
@@ -485,8 +503,7 @@ __global__ void __launch_bounds__(384, 1)
             dg[i] = d * u[i] * sg * (1.0f + g[i] * (1.0f - sg));
           }
           const int x = blk * 2 * kSwigluBlock + w;
-          ring.put(&tmC0, dg, 1.0f, x, m0 + wq * 32);
-          ring.put(&tmC0, du, 1.0f, x + kSwigluBlock, m0 + wq * 32);
+          ring.put2(&tmC0, dg, x, du, x + kSwigluBlock, m0 + wq * 32);
         }
         if (!ep_ok) break;
       } else if constexpr (EPI == EPI_CE_STATS) {
