@@ -11,6 +11,7 @@
 #include <unordered_map>
 
 #include "dist_fused.h"
+#include "tp_fused.h"
 #include "flash.h"
 #include "gemm_tc.h"
 #include "kernels.h"
@@ -71,7 +72,8 @@ void raise_rc(int rc, const char* what) {
 }
 
 // C[M,N] = epi(sum_k A(m,k) B(n,k)).  See gemm_tc.h for operand conventions.
-void gemm(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, int64_t M,
+static void build_gemm(cfb::GemmArgs& g, cfb::GemmEpi& ep, bool seg_a, bool seg_b, bool peer,
+                       const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, int64_t M,
           int64_t N, int64_t K, int64_t epi, const c10::optional<torch::Tensor>& out,
           const c10::optional<torch::Tensor>& residual, double alpha,
           const c10::optional<torch::Tensor>& gu, const c10::optional<torch::Tensor>& act,
@@ -81,7 +83,6 @@ void gemm(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, 
   check_bf16_cuda(A, "A");
   check_bf16_cuda(B, "B");
   const c10::cuda::CUDAGuard guard(A.device());
-  cfb::GemmArgs g;
   g.A = A.data_ptr();
   g.lda = ld_of(A, "A");
   g.a_mn = a_mn;
@@ -96,18 +97,21 @@ void gemm(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, 
   g.num_sms = num_sms(A.get_device());
   TORCH_CHECK(N % 32 == 0, "gemm: N must be a multiple of 32");
   // operand extents
-  if (!a_mn) {
-    TORCH_CHECK(A.size(0) >= M && A.size(1) >= K, "gemm: A too small");
-  } else {
-    TORCH_CHECK(A.size(0) >= K && A.size(1) >= M, "gemm: A too small");
+  if (!seg_a) {
+    if (!a_mn) {
+      TORCH_CHECK(A.size(0) >= M && A.size(1) >= K, "gemm: A too small");
+    } else {
+      TORCH_CHECK(A.size(0) >= K && A.size(1) >= M, "gemm: A too small");
+    }
   }
-  if (!b_mn) {
-    TORCH_CHECK(B.size(0) >= N && B.size(1) >= K, "gemm: B too small");
-  } else {
-    TORCH_CHECK(B.size(0) >= K && B.size(1) >= N, "gemm: B too small");
+  if (!seg_b) {
+    if (!b_mn) {
+      TORCH_CHECK(B.size(0) >= N && B.size(1) >= K, "gemm: B too small");
+    } else {
+      TORCH_CHECK(B.size(0) >= K && B.size(1) >= N, "gemm: B too small");
+    }
   }
 
-  cfb::GemmEpi ep;
   ep.alpha = static_cast<float>(alpha);
   if (epi == cfb::EPI_SWIGLU_FWD) {
     TORCH_CHECK(gu.has_value() && act.has_value(), "swiglu fwd needs gu and act");
@@ -123,7 +127,8 @@ void gemm(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, 
   } else {
     TORCH_CHECK(out.has_value(), "gemm needs out");
     TORCH_CHECK(out->is_cuda(), "out must be CUDA");
-    const bool f32 = epi == cfb::EPI_F32 || epi == cfb::EPI_F32_ACC || epi == cfb::EPI_F32_ATOMIC;
+    const bool f32 = epi == cfb::EPI_F32 || epi == cfb::EPI_F32_ACC ||
+                     epi == cfb::EPI_F32_ATOMIC || epi == cfb::EPI_PEER_STORE;
     TORCH_CHECK(out->scalar_type() == (f32 ? torch::kFloat32 : torch::kBFloat16),
                 "out dtype mismatch for epilogue");
     TORCH_CHECK(out->dim() == 2 && out->stride(1) == 1, "out must be row-major 2-D");
@@ -138,7 +143,7 @@ void gemm(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, 
       check_bf16_cuda(*gu, "gu");
       ep.gu = reinterpret_cast<__nv_bfloat16*>(gu->data_ptr());
       ep.ldgu = ld_of(*gu, "gu");
-    } else {
+    } else if (!peer) {
       TORCH_CHECK(out->size(0) >= M && out->size(1) >= N, "out too small");
     }
   }
@@ -176,9 +181,115 @@ void gemm(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, 
     TORCH_CHECK(stats->numel() >= M * 2 * ((N + 255) / 256) * 2, "stats too small");
     ep.stats = stats->data_ptr<float>();
   }
+}
+
+void gemm(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, int64_t M,
+          int64_t N, int64_t K, int64_t epi, const c10::optional<torch::Tensor>& out,
+          const c10::optional<torch::Tensor>& residual, double alpha,
+          const c10::optional<torch::Tensor>& gu, const c10::optional<torch::Tensor>& act,
+          const c10::optional<torch::Tensor>& row_scale, int64_t shared_width,
+          int64_t expert_width, int64_t n_experts, double shared_scale,
+          const c10::optional<torch::Tensor>& stats, int64_t bn) {
+  cfb::GemmArgs g;
+  cfb::GemmEpi ep;
+  build_gemm(g, ep, false, false, false, A, a_mn, B, b_mn, M, N, K, epi, out, residual, alpha, gu,
+             act, row_scale, shared_width, expert_width, n_experts, shared_scale, stats, bn);
   const int rc = cfb::gemm_tc_launch(g, ep, at::cuda::getCurrentCUDAStream(),
                                      err_ptr(A.get_device()));
   raise_rc(rc, "gemm");
+}
+
+// Tensor-parallel GEMMs: all-gather fused into the operand loads (segments of
+// A or B in peer memory) and reduce-scatter by peer stores of fp32 partials.
+void gemm_dist(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, int64_t M,
+               int64_t N, int64_t K, int64_t epi, const c10::optional<torch::Tensor>& out,
+               const c10::optional<torch::Tensor>& gu, const c10::optional<torch::Tensor>& act,
+               const c10::optional<torch::Tensor>& row_scale, int64_t shared_width,
+               int64_t expert_width, int64_t n_experts, double shared_scale,
+               const std::vector<int64_t>& a_seg, int64_t a_seg_rows,
+               const std::vector<int64_t>& b_seg, int64_t b_seg_rows,
+               const std::vector<int64_t>& peer_c, int64_t peer_rows,
+               const std::vector<int64_t>& pads, int64_t rank, int64_t round, int64_t epoch,
+               int64_t role, bool signal) {
+  TORCH_CHECK(a_seg.size() <= static_cast<size_t>(cfb::kMaxSeg) &&
+                  b_seg.size() <= static_cast<size_t>(cfb::kMaxSeg) &&
+                  peer_c.size() <= static_cast<size_t>(cfb::kMaxSeg) &&
+                  pads.size() <= static_cast<size_t>(cfb::kMaxSeg),
+              "at most 8 ranks");
+  const bool peer = epi == cfb::EPI_PEER_STORE;
+  cfb::GemmArgs g;
+  cfb::GemmEpi ep;
+  build_gemm(g, ep, !a_seg.empty(), !b_seg.empty(), peer, A, a_mn, B, b_mn, M, N, K, epi, out,
+             c10::nullopt, 1.0, gu, act, row_scale, shared_width, expert_width, n_experts,
+             shared_scale, c10::nullopt, 0);
+  g.a_nseg = static_cast<int>(a_seg.size());
+  g.a_seg_rows = a_seg_rows;
+  for (size_t i = 0; i < a_seg.size(); ++i) g.A_seg[i] = reinterpret_cast<const void*>(a_seg[i]);
+  g.b_nseg = static_cast<int>(b_seg.size());
+  g.b_seg_rows = b_seg_rows;
+  for (size_t i = 0; i < b_seg.size(); ++i) g.B_seg[i] = reinterpret_cast<const void*>(b_seg[i]);
+  if (peer) {
+    TORCH_CHECK(peer_c.size() == pads.size() && peer_rows > 0, "peer store needs peer buffers");
+    for (size_t i = 0; i < peer_c.size(); ++i) ep.peer_c[i] = reinterpret_cast<float*>(peer_c[i]);
+    ep.peer_rows = peer_rows;
+  }
+  ep.sync.world = static_cast<int>(pads.size());
+  for (size_t i = 0; i < pads.size(); ++i) ep.sync.pad[i] = reinterpret_cast<int*>(pads[i]);
+  ep.sync.rank = static_cast<int>(rank);
+  ep.sync.round = static_cast<int>(round);
+  ep.sync.epoch = static_cast<int>(epoch);
+  ep.sync.role = static_cast<int>(role);
+  ep.sync.signal = signal ? 1 : 0;
+  const int rc = cfb::gemm_tc_launch(g, ep, at::cuda::getCurrentCUDAStream(),
+                                     err_ptr(A.get_device()));
+  raise_rc(rc, "gemm_dist");
+}
+
+static cfb::TpSync make_tp_sync(const std::vector<int64_t>& pads, int64_t rank, int64_t round,
+                                 int64_t epoch) {
+  TORCH_CHECK(!pads.empty() && pads.size() <= 8, "1..8 ranks");
+  cfb::TpSync sy{};
+  for (size_t i = 0; i < pads.size(); ++i) sy.pad[i] = reinterpret_cast<int*>(pads[i]);
+  sy.world = static_cast<int>(pads.size());
+  sy.rank = static_cast<int>(rank);
+  sy.round = static_cast<int>(round);
+  sy.epoch = static_cast<int>(epoch);
+  return sy;
+}
+
+// Sum the world fp32 partial slots of this rank's rows (+ residual) into bf16 out.
+void tp_rs_finish(const torch::Tensor& slots, int64_t world, int64_t rows, int64_t n,
+                  const c10::optional<torch::Tensor>& residual, torch::Tensor& out,
+                  const std::vector<int64_t>& pads, int64_t rank, int64_t round, int64_t epoch) {
+  TORCH_CHECK(slots.is_cuda() && slots.scalar_type() == torch::kFloat32 && slots.dim() == 2 &&
+                  slots.stride(1) == 1 && slots.size(0) >= world * rows && slots.size(1) >= n,
+              "slots must be fp32 [world*rows, >= n]");
+  check_bf16_cuda(out, "out");
+  TORCH_CHECK(out.dim() == 2 && out.size(0) >= rows && out.size(1) >= n, "out too small");
+  const __nv_bfloat16* r = nullptr;
+  int64_t ldr = 0;
+  if (residual.has_value()) {
+    check_bf16_cuda(*residual, "residual");
+    r = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    ldr = residual->stride(0);
+  }
+  const c10::cuda::CUDAGuard guard(out.device());
+  const int rc = cfb::tp_rs_finish(slots.data_ptr<float>(), static_cast<int>(world), rows,
+                                   static_cast<int>(n), slots.stride(0), r, ldr,
+                                   reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                                   out.stride(0), make_tp_sync(pads, rank, round, epoch),
+                                   num_sms(out.get_device()),
+                                   at::cuda::getCurrentCUDAStream(), err_ptr(out.get_device()));
+  raise_rc(rc, "tp_rs_finish");
+}
+
+void tp_barrier(const std::vector<int64_t>& pads, int64_t rank, int64_t round, int64_t epoch,
+                int64_t device) {
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  const int rc = cfb::tp_barrier(make_tp_sync(pads, rank, round, epoch),
+                                 at::cuda::getCurrentCUDAStream(),
+                                 err_ptr(static_cast<int>(device)));
+  raise_rc(rc, "tp_barrier");
 }
 
 // Causal/full attention forward; writes out [B,S,Hq*D] and lse [B,Hq,S].
@@ -278,6 +389,9 @@ void register_elementwise(pybind11::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("error_buffer", &error_buffer);
+  m.def("gemm_dist", &gemm_dist);
+  m.def("tp_rs_finish", &tp_rs_finish);
+  m.def("tp_barrier", &tp_barrier);
   m.def("gemm", &gemm, "tcgen05 GEMM with fused epilogues", py::arg("A"), py::arg("a_mn"),
         py::arg("B"), py::arg("b_mn"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epi"),
         py::arg("out") = py::none(), py::arg("residual") = py::none(), py::arg("alpha") = 1.0,

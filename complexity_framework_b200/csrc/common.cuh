@@ -123,6 +123,46 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // ----------------------------------------------------------------------------
+// cross-GPU signals (symmetric-memory pads, system scope)
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void sys_store_release(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int sys_load_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// pad layout: int[rounds][8]; slot [round][r] of rank p's pad holds the last
+// epoch rank r announced to p for that round.
+__device__ __forceinline__ void sys_announce(int* const* pads, int world, int rank, int round,
+                                             int epoch) {
+  __threadfence_system();  // everything this rank wrote before is visible first
+  for (int p = 0; p < world; ++p) sys_store_release(pads[p] + round * 8 + rank, epoch);
+}
+// Bounded wait until every rank announced `epoch` on `round` of this rank's pad.
+__device__ __forceinline__ bool sys_wait_all(int* const* pads, int world, int rank, int round,
+                                             int epoch, volatile int* abort_flag, int* err,
+                                             int site) {
+  const int* mine = pads[rank] + round * 8;
+  const uint64_t start = globaltimer_ns();
+  for (int p = 0; p < world; ++p) {
+    uint32_t spins = 0;
+    while (sys_load_acquire(mine + p) < epoch) {
+      if ((++spins & 63u) == 0) {
+        if (abort_flag != nullptr && *abort_flag) return false;
+        if (globaltimer_ns() - start > kWaitBoundNs) {
+          report_error(err, kErrPeerTimeout, site * 100 + p);
+          if (abort_flag != nullptr) *abort_flag = 1;
+          return false;
+        }
+      }
+    }
+  }
+  return true;
+}
+
+// ----------------------------------------------------------------------------
 // TMA (no multicast anywhere in this code base)
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

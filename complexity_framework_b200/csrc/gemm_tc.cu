@@ -199,9 +199,32 @@ __device__ __forceinline__ float swiglu_col_scale(const GemmEpi& ep, int row, in
   return ep.row_scale[static_cast<int64_t>(row) * ep.n_experts + e];
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, bool PAIR>
+// Tensor maps of an operand: one map, or one per segment when the operand is
+// the row-concatenation of per-rank shards (all-gather fused into the loads).
+template <int NSEG>
+struct SegMaps {
+  CUtensorMap m[NSEG];
+  int seg_rows;  // storage rows per segment (NSEG > 1)
+  int nseg;
+  // map holding storage row `row`, and the row inside that segment; rows past
+  // the last segment stay out of range (TMA fills zeros)
+  __device__ __forceinline__ const CUtensorMap* pick(int row, int* local) const {
+    if constexpr (NSEG == 1) {
+      *local = row;
+      return &m[0];
+    } else {
+      int sidx = row / seg_rows;
+      if (sidx >= nseg) sidx = nseg - 1;
+      *local = row - sidx * seg_rows;
+      return &m[sidx];
+    }
+  }
+};
+
+template <int BN, bool A_MN, bool B_MN, int EPI, bool PAIR, int NA = 1, int NB = 1>
 __global__ void __launch_bounds__(384, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+    gemm_tc_kernel(const __grid_constant__ SegMaps<NA> tmA,
+                   const __grid_constant__ SegMaps<NB> tmB,
                    const __grid_constant__ CUtensorMap tmC0,
                    const __grid_constant__ CUtensorMap tmC1, int M, int N, int K, int ksplit,
                    GemmEpi ep, int* err) {
@@ -254,8 +277,11 @@ __global__ void __launch_bounds__(384, 1)
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
+    for (int i = 0; i < (NA > 1 ? tmA.nseg : 1); ++i) tma_prefetch_desc(&tmA.m[i]);
+    for (int i = 0; i < (NB > 1 ? tmB.nseg : 1); ++i) tma_prefetch_desc(&tmB.m[i]);
+    // this rank's operand shard is complete (written by earlier kernels)
+    if (ep.sync.world > 0 && ep.sync.signal && blockIdx.x == 0)
+      sys_announce(ep.sync.pad, ep.sync.world, ep.sync.rank, ep.sync.round, ep.sync.epoch);
   }
   if (SLOTS > 0 && warp == 4 && lane == 0) {
     tma_prefetch_desc(&tmC0);
@@ -281,6 +307,10 @@ __global__ void __launch_bounds__(384, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      // operands in peer memory: every rank's shard must be written first
+      if (ep.sync.world > 0 && ep.sync.role == 1)
+        ok = sys_wait_all(ep.sync.pad, ep.sync.world, ep.sync.rank, ep.sync.round, ep.sync.epoch,
+                          abort_flag, err, 16);
       for (int u = unit; u < total && ok; u += units) {
         const int t = u / ksplit;
         const int kb0 = (u % ksplit) * nk / ksplit, kb1 = ((u % ksplit) + 1) * nk / ksplit;
@@ -300,35 +330,45 @@ __global__ void __launch_bounds__(384, 1)
           if constexpr (PAIR) {
             const uint32_t bar = mapa_shared(smem_u32(&full_bar[stage]), 0);
             if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::STAGE_BYTES);
+            int ra, rb;
             if constexpr (!A_MN) {
-              tma_load_2d_pair(sA, &tmA, bar, kb * kBK, m0);
+              const CUtensorMap* ma = tmA.pick(m0, &ra);
+              tma_load_2d_pair(sA, ma, bar, kb * kBK, ra);
             } else {
+              const CUtensorMap* ma = tmA.pick(kb * kBK, &ra);
 #pragma unroll
               for (int i = 0; i < kBM / 64; ++i)
-                tma_load_2d_pair(sA + i * 64 * kBK * 2, &tmA, bar, m0 + 64 * i, kb * kBK);
+                tma_load_2d_pair(sA + i * 64 * kBK * 2, ma, bar, m0 + 64 * i, ra);
             }
             if constexpr (!B_MN) {
-              tma_load_2d_pair(sB, &tmB, bar, kb * kBK, nb0);
+              const CUtensorMap* mb = tmB.pick(nb0, &rb);
+              tma_load_2d_pair(sB, mb, bar, kb * kBK, rb);
             } else {
+              const CUtensorMap* mb = tmB.pick(kb * kBK, &rb);
 #pragma unroll
               for (int i = 0; i < B_ROWS / 64; ++i)
-                tma_load_2d_pair(sB + i * 64 * kBK * 2, &tmB, bar, nb0 + 64 * i, kb * kBK);
+                tma_load_2d_pair(sB + i * 64 * kBK * 2, mb, bar, nb0 + 64 * i, rb);
             }
           } else {
             mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+            int ra, rb;
             if constexpr (!A_MN) {
-              tma_load_2d(sA, &tmA, &full_bar[stage], kb * kBK, m0);
+              const CUtensorMap* ma = tmA.pick(m0, &ra);
+              tma_load_2d(sA, ma, &full_bar[stage], kb * kBK, ra);
             } else {
+              const CUtensorMap* ma = tmA.pick(kb * kBK, &ra);
 #pragma unroll
               for (int i = 0; i < kBM / 64; ++i)
-                tma_load_2d(sA + i * 64 * kBK * 2, &tmA, &full_bar[stage], m0 + 64 * i, kb * kBK);
+                tma_load_2d(sA + i * 64 * kBK * 2, ma, &full_bar[stage], m0 + 64 * i, ra);
             }
             if constexpr (!B_MN) {
-              tma_load_2d(sB, &tmB, &full_bar[stage], kb * kBK, n0);
+              const CUtensorMap* mb = tmB.pick(n0, &rb);
+              tma_load_2d(sB, mb, &full_bar[stage], kb * kBK, rb);
             } else {
+              const CUtensorMap* mb = tmB.pick(kb * kBK, &rb);
 #pragma unroll
               for (int i = 0; i < BN / 64; ++i)
-                tma_load_2d(sB + i * 64 * kBK * 2, &tmB, &full_bar[stage], n0 + 64 * i, kb * kBK);
+                tma_load_2d(sB + i * 64 * kBK * 2, mb, &full_bar[stage], n0 + 64 * i, rb);
             }
           }
           if (++stage == STAGES) {
@@ -563,7 +603,18 @@ __global__ void __launch_bounds__(384, 1)
             for (int i = 0; i < 32; ++i) v[i] = v[i] * ep.alpha + r[i];
             ring.put(&tmC0, v, 1.0f, n0 + c, m0 + wq * 32);
           } else if (row_ok && n0 + c < N) {
-            if constexpr (EPI == EPI_F32_ATOMIC) {
+            if constexpr (EPI == EPI_PEER_STORE) {
+              // this rank's partial rows go to the owner's slot for this rank
+              const int owner = static_cast<int>(row / ep.peer_rows);
+              const int64_t lrow = row - static_cast<int64_t>(owner) * ep.peer_rows;
+              float4* out = reinterpret_cast<float4*>(
+                  ep.peer_c[owner] +
+                  (static_cast<int64_t>(ep.sync.rank) * ep.peer_rows + lrow) * ep.ldc + n0 + c);
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                out[q] = make_float4(v[4 * q] * ep.alpha, v[4 * q + 1] * ep.alpha,
+                                     v[4 * q + 2] * ep.alpha, v[4 * q + 3] * ep.alpha);
+            } else if constexpr (EPI == EPI_F32_ATOMIC) {
               float* out = reinterpret_cast<float*>(ep.c) + static_cast<int64_t>(row) * ep.ldc + n0 + c;
 #pragma unroll
               for (int q = 0; q < 8; ++q)
@@ -600,6 +651,7 @@ __global__ void __launch_bounds__(384, 1)
     }
     if (LOADS > 0) lring.drain(err);
     if (SLOTS > 0 && lane == 0) bulk_wait_group_all();
+    if constexpr (EPI == EPI_PEER_STORE) __threadfence_system();  // peer stores before exit
   }
 
   tc_fence_before();
@@ -660,12 +712,12 @@ int make_tmap_2d_store(CUtensorMap* map, const void* base, int64_t rows, int64_t
   return r == CUDA_SUCCESS ? 0 : static_cast<int>(r) + 1000;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, bool PAIR>
-static int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap* tc,
+template <int BN, bool A_MN, bool B_MN, int EPI, bool PAIR, int NA = 1, int NB = 1>
+static int launch_impl(const SegMaps<NA>& ta, const SegMaps<NB>& tb, const CUtensorMap* tc,
                        int M, int N, int K, const GemmEpi& ep, int num_sms, cudaStream_t stream,
                        int* err, int ksplit = 1) {
   using Cfg = GemmCfg<BN, PAIR, epi_slots(EPI), epi_loads(EPI)>;
-  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI, PAIR>;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI, PAIR, NA, NB>;
   static int max_units = -1;  // resident CTAs (or CTA pairs), one query per instantiation
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -716,7 +768,7 @@ static int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
-static int launch_pair_or_single(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap* tc,
+static int launch_pair_or_single(const SegMaps<1>& ta, const SegMaps<1>& tb, const CUtensorMap* tc,
                                  int M, int N, int K, const GemmEpi& ep, int sms, cudaStream_t s,
                                  int* err) {
   const int ks = EPI == EPI_F32_ATOMIC ? 0 : 1;  // 0 = choose
@@ -728,9 +780,9 @@ static int launch_pair_or_single(const CUtensorMap& ta, const CUtensorMap& tb, c
 }
 
 template <int BN, int EPI>
-static int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
-                          const CUtensorMap* tc, int M, int N, int K, const GemmEpi& ep, int sms, cudaStream_t s,
-                          int* err) {
+static int dispatch_major(bool a_mn, bool b_mn, const SegMaps<1>& ta, const SegMaps<1>& tb,
+                          const CUtensorMap* tc, int M, int N, int K, const GemmEpi& ep, int sms,
+                          cudaStream_t s, int* err) {
   if (!a_mn && !b_mn)
     return launch_pair_or_single<BN, false, false, EPI>(ta, tb, tc, M, N, K, ep, sms, s, err);
   if (!a_mn && b_mn)
@@ -746,27 +798,17 @@ int choose_bn(int M, int N, int num_sms) {
   return N <= 128 ? 128 : 256;
 }
 
-int gemm_tc_launch(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream, int* err) {
-  if (g.M <= 0 || g.N <= 0 || g.K <= 0) return -2;
-  int bn = g.bn;
-  if (g.epi == EPI_SWIGLU_FWD) bn = 2 * kSwigluBlock;
-  if (bn == 0) bn = choose_bn(g.M, g.N, g.num_sms);
-  if (bn != 128 && bn != 256) return -3;
-  CUtensorMap ta, tb;
-  int rc;
-  if (!g.a_mn)
-    rc = make_tmap_2d(&ta, g.A, g.M, g.K, g.lda, kBK, kBM);
-  else
-    rc = make_tmap_2d(&ta, g.A, g.K, g.M, g.lda, 64, kBK);
-  if (rc) return rc;
-  if (!g.b_mn)
-    rc = make_tmap_2d(&tb, g.B, g.N, g.K, g.ldb, kBK, g.M > kBM ? bn / 2 : bn);  // pair: half B
-  else
-    rc = make_tmap_2d(&tb, g.B, g.K, g.N, g.ldb, 64, kBK);
-  if (rc) return rc;
+// Operand tensor maps.  `rows` x `cols` is the storage shape of one map.
+static int make_operand_map(CUtensorMap* map, const void* base, bool mn, int64_t rows, int64_t cols,
+                            int64_t ld, int box_rows_kmajor) {
+  return mn ? make_tmap_2d(map, base, rows, cols, ld, 64, kBK)
+            : make_tmap_2d(map, base, rows, cols, ld, kBK, box_rows_kmajor);
+}
+
+static int epilogue_maps(const GemmArgs& g, const GemmEpi& ep, CUtensorMap* tc) {
   // epilogue store maps (bf16 outputs written by TMA from staging boxes)
-  CUtensorMap tc[2];
-  memset(tc, 0, sizeof(tc));
+  memset(tc, 0, 2 * sizeof(CUtensorMap));
+  int rc = 0;
   switch (g.epi) {
     case EPI_STORE:
     case EPI_CE_STATS:
@@ -793,13 +835,116 @@ int gemm_tc_launch(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream, in
     default:
       break;
   }
+  return rc;
+}
+
+// Distributed variants (tensor parallel): all-gather fused into the operand
+// loads (segmented A or B) and reduce-scatter by peer stores.  256-row CTA
+// pairs, BN = 256.
+static int gemm_tc_launch_dist(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream,
+                               int* err) {
+  if (g.M <= kBM) return -6;
+  const int box_b = 256 / 2;
+  CUtensorMap tc[2];
+  int rc = epilogue_maps(g, ep, tc);
+  if (rc) return rc;
+  const int ks = g.epi == EPI_F32_ATOMIC ? 0 : 1;
+  if (g.a_nseg > 0) {
+    if (g.a_nseg > kMaxSeg || g.a_seg_rows % (g.a_mn ? kBK : kBM) != 0) return -7;
+    SegMaps<kMaxSeg> sa;
+    memset(&sa, 0, sizeof(sa));
+    sa.seg_rows = static_cast<int>(g.a_seg_rows);
+    sa.nseg = g.a_nseg;
+    for (int i = 0; i < g.a_nseg; ++i) {
+      rc = make_operand_map(&sa.m[i], g.A_seg[i], g.a_mn, g.a_seg_rows, g.a_mn ? g.M : g.K, g.lda,
+                            kBM);
+      if (rc) return rc;
+    }
+    SegMaps<1> sb;
+    rc = g.b_mn ? make_operand_map(&sb.m[0], g.B, true, g.K, g.N, g.ldb, box_b)
+                : make_operand_map(&sb.m[0], g.B, false, g.N, g.K, g.ldb, box_b);
+    if (rc) return rc;
+    sb.seg_rows = 0;
+    sb.nseg = 1;
+#define CFB_DIST_A(AM, BM, E)                                                                   \
+  if (g.a_mn == AM && g.b_mn == BM && g.epi == E)                                               \
+    return launch_impl<256, AM, BM, E, true, kMaxSeg, 1>(sa, sb, tc, g.M, g.N, g.K, ep,        \
+                                                          g.num_sms, stream, err, ks);
+    CFB_DIST_A(false, false, EPI_STORE)
+    CFB_DIST_A(false, false, EPI_SWIGLU_FWD)
+    CFB_DIST_A(false, true, EPI_STORE)
+    CFB_DIST_A(false, true, EPI_SWIGLU_BWD)
+    CFB_DIST_A(true, true, EPI_F32_ATOMIC)
+#undef CFB_DIST_A
+    return -8;
+  }
+  if (g.b_nseg > 0) {
+    if (g.b_nseg > kMaxSeg || !g.b_mn || g.b_seg_rows % kBK != 0) return -7;
+    SegMaps<1> sa;
+    rc = g.a_mn ? make_operand_map(&sa.m[0], g.A, true, g.K, g.M, g.lda, kBM)
+                : make_operand_map(&sa.m[0], g.A, false, g.M, g.K, g.lda, kBM);
+    if (rc) return rc;
+    sa.seg_rows = 0;
+    sa.nseg = 1;
+    SegMaps<kMaxSeg> sb;
+    memset(&sb, 0, sizeof(sb));
+    sb.seg_rows = static_cast<int>(g.b_seg_rows);
+    sb.nseg = g.b_nseg;
+    for (int i = 0; i < g.b_nseg; ++i) {
+      rc = make_operand_map(&sb.m[i], g.B_seg[i], true, g.b_seg_rows, g.N, g.ldb, box_b);
+      if (rc) return rc;
+    }
+    if (g.a_mn && g.epi == EPI_F32_ATOMIC)
+      return launch_impl<256, true, true, EPI_F32_ATOMIC, true, 1, kMaxSeg>(
+          sa, sb, tc, g.M, g.N, g.K, ep, g.num_sms, stream, err, ks);
+    return -8;
+  }
+  // reduce-scatter: plain operands, peer-store epilogue
+  if (g.epi != EPI_PEER_STORE || ep.peer_rows <= 0) return -8;
+  SegMaps<1> sa, sb;
+  rc = g.a_mn ? make_operand_map(&sa.m[0], g.A, true, g.K, g.M, g.lda, kBM)
+              : make_operand_map(&sa.m[0], g.A, false, g.M, g.K, g.lda, kBM);
+  if (rc) return rc;
+  rc = g.b_mn ? make_operand_map(&sb.m[0], g.B, true, g.K, g.N, g.ldb, box_b)
+              : make_operand_map(&sb.m[0], g.B, false, g.N, g.K, g.ldb, box_b);
+  if (rc) return rc;
+  sa.seg_rows = sb.seg_rows = 0;
+  sa.nseg = sb.nseg = 1;
+  if (g.a_mn) return -8;
+  if (g.b_mn)
+    return launch_impl<256, false, true, EPI_PEER_STORE, true>(sa, sb, tc, g.M, g.N, g.K, ep,
+                                                                 g.num_sms, stream, err, 1);
+  return launch_impl<256, false, false, EPI_PEER_STORE, true>(sa, sb, tc, g.M, g.N, g.K, ep,
+                                                                g.num_sms, stream, err, 1);
+}
+
+int gemm_tc_launch(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream, int* err) {
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0) return -2;
+  if (g.a_nseg > 0 || g.b_nseg > 0 || g.epi == EPI_PEER_STORE)
+    return gemm_tc_launch_dist(g, ep, stream, err);
+  int bn = g.bn;
+  if (g.epi == EPI_SWIGLU_FWD) bn = 2 * kSwigluBlock;
+  if (bn == 0) bn = choose_bn(g.M, g.N, g.num_sms);
+  if (bn != 128 && bn != 256) return -3;
+  SegMaps<1> ta, tb;
+  ta.seg_rows = tb.seg_rows = 0;
+  ta.nseg = tb.nseg = 1;
+  int rc = g.a_mn ? make_operand_map(&ta.m[0], g.A, true, g.K, g.M, g.lda, kBM)
+                  : make_operand_map(&ta.m[0], g.A, false, g.M, g.K, g.lda, kBM);
+  if (rc) return rc;
+  // pair mode: each CTA loads half of a K-major B tile
+  rc = g.b_mn ? make_operand_map(&tb.m[0], g.B, true, g.K, g.N, g.ldb, bn)
+              : make_operand_map(&tb.m[0], g.B, false, g.N, g.K, g.ldb, g.M > kBM ? bn / 2 : bn);
+  if (rc) return rc;
+  CUtensorMap tc[2];
+  rc = epilogue_maps(g, ep, tc);
   if (rc) return rc;
 
 #define CFB_EPI_CASE(E)                                                                          \
   case E:                                                                                        \
-    return bn == 256 ? dispatch_major<256, E>(g.a_mn, g.b_mn, ta, tb, tc, g.M, g.N, g.K, ep,          \
+    return bn == 256 ? dispatch_major<256, E>(g.a_mn, g.b_mn, ta, tb, tc, g.M, g.N, g.K, ep,      \
                                               g.num_sms, stream, err)                            \
-                     : dispatch_major<128, E>(g.a_mn, g.b_mn, ta, tb, tc, g.M, g.N, g.K, ep,          \
+                     : dispatch_major<128, E>(g.a_mn, g.b_mn, ta, tb, tc, g.M, g.N, g.K, ep,      \
                                               g.num_sms, stream, err);
   switch (g.epi) {
     CFB_EPI_CASE(EPI_STORE)

@@ -16,6 +16,25 @@ enum GemmEpilogue : int {
   EPI_F32_ACC = 5,     // C(fp32) += alpha * acc
   EPI_F32_ATOMIC = 7,  // C(fp32) += alpha * acc with atomics; K may be split across CTAs
   EPI_CE_STATS = 6,    // C(bf16) logits = alpha*acc; stats[row, N/128] = (max, sumexp); BN=256
+  EPI_PEER_STORE = 8,  // reduce-scatter partials: owner = row / peer_rows; fp32 tile stored
+                       // over NVLink into peer_c[owner][sync.rank][row % peer_rows][col]
+};
+
+constexpr int kMaxSeg = 8;
+
+// Device barrier over symmetric-memory signal pads (int[rounds][kMaxSeg] per
+// rank).  `role` 1: the TMA producer waits before its first load (operands
+// that live in peer memory must be written); role 2: the epilogue waits
+// before its first peer store (peer destinations must be cleared).  With
+// `signal`, CTA 0 first announces this rank's arrival.  world == 0: none.
+struct DistSync {
+  int* pad[kMaxSeg] = {};
+  int world = 0;
+  int rank = 0;
+  int round = 0;
+  int epoch = 0;
+  int role = 0;
+  int signal = 0;
 };
 
 // Width (in activation columns) of one gate block in the packed gate|up weight:
@@ -39,6 +58,9 @@ struct GemmEpi {
   int n_experts = 0;
   float shared_scale = 1.0f;
   float* stats = nullptr;  // [M, 2*ceil(N/BN)] float2 (one per 128-column half tile)
+  float* peer_c[kMaxSeg] = {};  // EPI_PEER_STORE: every rank's [world][peer_rows][ldc] fp32 slots
+  int64_t peer_rows = 0;        // rows owned by each rank
+  DistSync sync;
 };
 
 struct GemmArgs {
@@ -52,6 +74,16 @@ struct GemmArgs {
   int epi = EPI_STORE;
   int bn = 0;  // 0 = choose
   int num_sms = 148;
+  // Operand segments (all-gather fused into the GEMM): when a_nseg > 0 the A
+  // matrix is the concatenation, along its storage rows (M for K-major, K for
+  // MN-major), of a_nseg matrices of a_seg_rows rows each, at A_seg[i] (peer
+  // memory allowed; loads are plain TMA, never multicast).  Same for B.
+  const void* A_seg[kMaxSeg] = {};
+  int a_nseg = 0;
+  int64_t a_seg_rows = 0;
+  const void* B_seg[kMaxSeg] = {};
+  int b_nseg = 0;
+  int64_t b_seg_rows = 0;
 };
 
 int gemm_tc_launch(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream, int* err);

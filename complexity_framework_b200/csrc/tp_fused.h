@@ -1,0 +1,22 @@
+// Host interface of the tensor-parallel finish / barrier kernels (tp_fused.cu).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace cfb {
+
+struct TpSync {
+  int* pad[8];  // every rank's signal pad (int[rounds][8])
+  int world;
+  int rank;
+  int round;
+  int epoch;
+};
+
+int tp_rs_finish(const float* slots, int world, int64_t rows, int n, int64_t ld,
+                 const __nv_bfloat16* residual, int64_t ldr, __nv_bfloat16* out, int64_t ldo,
+                 const TpSync& sy, int num_sms, cudaStream_t s, int* err);
+int tp_barrier(const TpSync& sy, cudaStream_t s, int* err);
+
+}  // namespace cfb

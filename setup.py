@@ -20,6 +20,7 @@ SOURCES = [
     "paged_attn.cu",
     "dist_fused.cu",
     "noalloc.cu",
+    "tp_fused.cu",
 ]
 
 NVCC_FLAGS = [
