@@ -210,7 +210,8 @@ void gemm_dist(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b
                const std::vector<int64_t>& b_seg, int64_t b_seg_rows,
                const std::vector<int64_t>& peer_c, int64_t peer_rows,
                const std::vector<int64_t>& pads, int64_t rank, int64_t round, int64_t epoch,
-               int64_t role, bool signal) {
+               int64_t role, bool signal, const std::vector<int64_t>& ag_src,
+               const c10::optional<torch::Tensor>& ag_flags, int64_t ag_rows, int64_t ag_epoch) {
   TORCH_CHECK(a_seg.size() <= static_cast<size_t>(cfb::kMaxSeg) &&
                   b_seg.size() <= static_cast<size_t>(cfb::kMaxSeg) &&
                   peer_c.size() <= static_cast<size_t>(cfb::kMaxSeg) &&
@@ -240,6 +241,27 @@ void gemm_dist(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b
   ep.sync.epoch = static_cast<int>(epoch);
   ep.sync.role = static_cast<int>(role);
   ep.sync.signal = signal ? 1 : 0;
+  if (!ag_src.empty()) {
+    // fused all-gather: A is this rank's full gathered buffer [world*ag_rows, K]
+    TORCH_CHECK(ag_src.size() == pads.size() && !a_mn && a_seg.empty(),
+                "fused all-gather: one source per rank, K-major A");
+    TORCH_CHECK(ag_rows % 128 == 0 && ag_rows * static_cast<int64_t>(pads.size()) == M,
+                "fused all-gather: rows per rank must be a multiple of 128 and sum to M");
+    TORCH_CHECK(ag_flags.has_value() && ag_flags->scalar_type() == torch::kInt32 &&
+                    ag_flags->numel() >= M / 128,
+                "fused all-gather needs int32 flags, one per 128 rows");
+    TORCH_CHECK(A.size(0) >= M && A.stride(0) == K && K % 8 == 0,
+                "fused all-gather: A must be the contiguous gathered buffer");
+    for (size_t i = 0; i < ag_src.size(); ++i)
+      ep.ag.src[i] = reinterpret_cast<const __nv_bfloat16*>(ag_src[i]);
+    ep.ag.dst = reinterpret_cast<__nv_bfloat16*>(A.data_ptr());
+    ep.ag.flags = ag_flags->data_ptr<int>();
+    ep.ag.rows = static_cast<int>(ag_rows);
+    ep.ag.cols = static_cast<int>(K);
+    ep.ag.epoch = static_cast<int>(ag_epoch);
+    ep.ag.active = 1;
+    g.bn = 256;
+  }
   const int rc = cfb::gemm_tc_launch(g, ep, at::cuda::getCurrentCUDAStream(),
                                      err_ptr(A.get_device()));
   raise_rc(rc, "gemm_dist");
@@ -257,25 +279,27 @@ static cfb::TpSync make_tp_sync(const std::vector<int64_t>& pads, int64_t rank, 
   return sy;
 }
 
-// Sum the world fp32 partial slots of this rank's rows (+ residual) into bf16 out.
-void tp_rs_finish(const torch::Tensor& slots, int64_t world, int64_t rows, int64_t n,
+// Sum, for this rank's rows, the world bf16 partial products (+ residual) into bf16 out.
+void tp_rs_finish(const std::vector<int64_t>& parts, int64_t rows, int64_t n, int64_t ld,
                   const c10::optional<torch::Tensor>& residual, torch::Tensor& out,
                   const std::vector<int64_t>& pads, int64_t rank, int64_t round, int64_t epoch) {
-  TORCH_CHECK(slots.is_cuda() && slots.scalar_type() == torch::kFloat32 && slots.dim() == 2 &&
-                  slots.stride(1) == 1 && slots.size(0) >= world * rows && slots.size(1) >= n,
-              "slots must be fp32 [world*rows, >= n]");
+  TORCH_CHECK(parts.size() == pads.size(), "one partial buffer per rank");
   check_bf16_cuda(out, "out");
-  TORCH_CHECK(out.dim() == 2 && out.size(0) >= rows && out.size(1) >= n, "out too small");
+  TORCH_CHECK(out.dim() == 2 && out.size(0) >= rows && out.size(1) >= n && out.stride(1) == 1,
+              "out too small");
   const __nv_bfloat16* r = nullptr;
   int64_t ldr = 0;
   if (residual.has_value()) {
     check_bf16_cuda(*residual, "residual");
+    TORCH_CHECK(residual->stride(-1) == 1 && residual->stride(0) % 8 == 0, "residual layout");
     r = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
     ldr = residual->stride(0);
   }
+  cfb::TpPartials pp{};
+  for (size_t i = 0; i < parts.size(); ++i)
+    pp.part[i] = reinterpret_cast<const __nv_bfloat16*>(parts[i]);
   const c10::cuda::CUDAGuard guard(out.device());
-  const int rc = cfb::tp_rs_finish(slots.data_ptr<float>(), static_cast<int>(world), rows,
-                                   static_cast<int>(n), slots.stride(0), r, ldr,
+  const int rc = cfb::tp_rs_finish(pp, rows, static_cast<int>(n), ld, r, ldr,
                                    reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
                                    out.stride(0), make_tp_sync(pads, rank, round, epoch),
                                    num_sms(out.get_device()),

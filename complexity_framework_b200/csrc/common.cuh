@@ -133,6 +133,18 @@ __device__ __forceinline__ int sys_load_acquire(const int* p) {
   asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// orders generic-proxy global/shared accesses with later async-proxy (TMA) ones
+__device__ __forceinline__ void fence_proxy_async_all() {
+  asm volatile("fence.proxy.async;" ::: "memory");
+}
 // pad layout: int[rounds][8]; slot [round][r] of rank p's pad holds the last
 // epoch rank r announced to p for that round.
 __device__ __forceinline__ void sys_announce(int* const* pads, int world, int rank, int round,

@@ -255,6 +255,8 @@ __global__ void __launch_bounds__(384, 1)
   const int units = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   const int num_m = (M + Cfg::TILE_M - 1) / Cfg::TILE_M;
+  // with the fused all-gather, this rank's own row tiles come first
+  const int m_shift = ep.ag.active ? (ep.sync.rank * ep.ag.rows) / Cfg::TILE_M : 0;
   const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int nk = (K + kBK - 1) / kBK;
@@ -314,8 +316,26 @@ __global__ void __launch_bounds__(384, 1)
       for (int u = unit; u < total && ok; u += units) {
         const int t = u / ksplit;
         const int kb0 = (u % ksplit) * nk / ksplit, kb1 = ((u % ksplit) + 1) * nk / ksplit;
-        const int m0 = (t / num_n) * Cfg::TILE_M + static_cast<int>(rank) * kBM;
+        const int m0 = ((t / num_n + m_shift) % num_m) * Cfg::TILE_M + static_cast<int>(rank) * kBM;
         const int n0 = (t % num_n) * BN;
+        if (ep.ag.active) {
+          // rows owned by a peer: wait until a copier warp has gathered them
+          const int owner = m0 / ep.ag.rows;
+          if (owner != ep.sync.rank && m0 < M) {
+            const int* f = ep.ag.flags + m0 / kBM;
+            const uint64_t t0 = globaltimer_ns();
+            while (ld_acquire_gpu(f) < ep.ag.epoch * (kBM / 16)) {
+              if (*abort_flag || globaltimer_ns() - t0 > kWaitBoundNs) {
+                if (!*abort_flag) report_error(err, kErrTimeoutFull, 19);
+                *abort_flag = 1;
+                ok = false;
+                break;
+              }
+            }
+            if (!ok) break;
+            fence_proxy_async_all();  // gathered rows (generic stores) -> TMA reads
+          }
+        }
         // this CTA's B rows: half of the (possibly narrower) tail tile when paired
         const int n_rem = N - n0;
         const int n_this = n_rem < BN ? n_rem : BN;
@@ -435,6 +455,52 @@ __global__ void __launch_bounds__(384, 1)
         if (acc == 0) acc_phase ^= 1;
       }
     }
+  } else if (warp == 2 || warp == 3) {
+    // ------------------------------------------------------------ all-gather copiers
+    // two warps per CTA pull 128-row chunks of the peers' shards over NVLink
+    // (8 x 16-byte loads in flight per lane) into this rank's gathered buffer
+    if (ep.ag.active) {
+      bool ok = true;
+      if (ep.sync.world > 0 && lane == 0)
+        ok = sys_wait_all(ep.sync.pad, ep.sync.world, ep.sync.rank, ep.sync.round,
+                          ep.sync.epoch, abort_flag, err, 20);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      // work unit = 16-row piece of a 128-row chunk; a chunk is complete when
+      // its counter has grown by kPieces in this epoch
+      constexpr int kPieceRows = 16, kPieces = kBM / kPieceRows;
+      const int chunks_per_rank = ep.ag.rows / kBM;
+      const int world = ep.sync.world;
+      const int remote = (world - 1) * chunks_per_rank * kPieces;
+      const int64_t piece_elems = static_cast<int64_t>(kPieceRows) * ep.ag.cols;
+      const int64_t n16 = piece_elems / 8;
+      const int copier = 2 * static_cast<int>(blockIdx.x) + (warp - 2);
+      const int copiers = 2 * static_cast<int>(gridDim.x);
+      for (int j = copier; ok && j < remote; j += copiers) {
+        // pieces in the order the producers consume chunks: peers' rows after own
+        const int jc = j / kPieces, jp = j % kPieces;
+        const int q = (ep.sync.rank + 1 + jc / chunks_per_rank) % world;
+        const int chunk = q * chunks_per_rank + jc % chunks_per_rank;
+        const int64_t off = (static_cast<int64_t>(chunk) * kPieces + jp) * piece_elems;
+        const uint4* src = reinterpret_cast<const uint4*>(ep.ag.src[q] + off);
+        uint4* dst = reinterpret_cast<uint4*>(ep.ag.dst + off);
+        int64_t i = lane;
+        for (; i + 15 * 32 < n16; i += 16 * 32) {
+          uint4 r[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) r[k] = src[i + k * 32];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) dst[i + k * 32] = r[k];
+        }
+        for (; i < n16; i += 32) dst[i] = src[i];
+        __syncwarp();
+        if (lane == 0) {
+          __threadfence();
+          fence_proxy_async_all();
+          atomicAdd(ep.ag.flags + chunk, 1);  // release: fenced above
+        }
+        if (*abort_flag) break;
+      }
+    }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
     // two epilogue warpgroups (warps 4-7 and 8-11) split the tile's columns;
@@ -452,7 +518,7 @@ __global__ void __launch_bounds__(384, 1)
     bool ep_ok = true;
     for (int u = unit; u < total; u += units) {
       const int t = u / ksplit;
-      const int m_blk = t / num_n;
+      const int m_blk = (t / num_n + m_shift) % num_m;
       const int n_blk = t % num_n;
       const int m0 = m_blk * Cfg::TILE_M + static_cast<int>(rank) * kBM;
       const int n0 = n_blk * BN;

@@ -42,6 +42,22 @@ struct DistSync {
 // [256j+128, 256j+256) the matching up rows.
 constexpr int kSwigluBlock = 128;
 
+// All-gather of A's row shards performed inside the GEMM: warp 2 of every CTA
+// copies 128-row chunks of the peers' shards (P2P loads) into this rank's
+// gathered buffer `dst` (the A operand) and publishes a per-chunk flag; the
+// TMA producer waits for a chunk's flag before loading its rows.  Tiles of
+// this rank's own rows are scheduled first.  src[q] is rank q's gathered
+// buffer, whose rows [q*rows, (q+1)*rows) hold q's shard.
+struct AgCopy {
+  const __nv_bfloat16* src[kMaxSeg] = {};
+  __nv_bfloat16* dst = nullptr;
+  int* flags = nullptr;  // one per 128-row chunk of dst
+  int rows = 0;          // rows per rank
+  int cols = 0;          // row length (elements) of src/dst
+  int epoch = 0;
+  int active = 0;
+};
+
 struct GemmEpi {
   void* c = nullptr;
   int64_t ldc = 0;
@@ -61,6 +77,7 @@ struct GemmEpi {
   float* peer_c[kMaxSeg] = {};  // EPI_PEER_STORE: every rank's [world][peer_rows][ldc] fp32 slots
   int64_t peer_rows = 0;        // rows owned by each rank
   DistSync sync;
+  AgCopy ag;
 };
 
 struct GemmArgs {

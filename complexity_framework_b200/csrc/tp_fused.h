@@ -14,7 +14,12 @@ struct TpSync {
   int epoch;
 };
 
-int tp_rs_finish(const float* slots, int world, int64_t rows, int n, int64_t ld,
+// every rank's bf16 partial product [world*rows, ld] (peer pointers)
+struct TpPartials {
+  const __nv_bfloat16* part[8];
+};
+
+int tp_rs_finish(const TpPartials& pp, int64_t rows, int n, int64_t ld,
                  const __nv_bfloat16* residual, int64_t ldr, __nv_bfloat16* out, int64_t ldo,
                  const TpSync& sy, int num_sms, cudaStream_t s, int* err);
 int tp_barrier(const TpSync& sy, cudaStream_t s, int* err);

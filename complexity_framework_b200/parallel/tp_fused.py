@@ -1,22 +1,22 @@
 """Tensor parallelism with the collectives fused into the GEMMs (sequence parallel).
 
 Activations between tensor-parallel regions are sharded by token rows: rank p
-holds rows [p*T/P, (p+1)*T/P) of the flattened [T, H] stream.  The two
-collectives of a Megatron-style layer are fused into the sm_100a GEMM:
+holds rows [p*T/P, (p+1)*T/P) of the flattened [T, H] stream.
 
-* ``ag_linear`` (column parallel): Y[T, N/P] = AllGather(X)[T, H] @ W_p^T.
-  Each rank's X shard lives in symmetric memory; the GEMM's TMA producer loads
-  the A tiles of rows owned by rank q straight from q's buffer over NVLink
-  (one tensor map per rank, plain TMA loads, never multicast), after a bounded
-  device barrier that confirms every shard is written.  Backward: dX is a
-  reduce-scatter GEMM (below) of dY @ W_p; dW_p = dY^T @ AllGather(X) reads
-  the peers' X shards again through segmented TMA loads.
+* ``ag_linear`` (column parallel): Y[T, N/P] = AllGather(X)[T, H] @ W_p^T in ONE
+  GEMM kernel.  Two copier warps of every CTA pull the peers' 128-row chunks
+  over NVLink (each remote byte crosses once) into this rank's gathered buffer
+  and publish per-chunk flags; the TMA producer computes this rank's own row
+  tiles first and waits (bounded) for a chunk's flag before loading its rows,
+  so the transfer overlaps the tensor-core work tile by tile.  The gathered
+  buffer stays valid for the backward weight gradient.
 * ``rs_linear`` (row parallel): Out_p = sum_q (X_q @ W_q^T)[rows of p] (+ R_p).
-  The GEMM epilogue stores each fp32 partial tile straight into the owning
-  rank's slot for this source rank (NVLink stores); a finish kernel announces
-  completion, waits (bounded) for every peer and sums the slots of its own
-  rows (+ residual) into bf16.  Backward: d(X_p) = AllGather(dOut) @ W_p (the
-  gather fused into the loads again), dW_p = AllGather(dOut)^T @ X_p.
+  The GEMM stores its bf16 partial into this rank's symmetric buffer; the
+  finish kernel announces completion, waits (bounded) for every peer and sums
+  the owned rows of all partials (peer rows by 16-byte NVLink loads, read once)
+  with the residual in fp32.
+* Backward: d(ag_linear) is a reduce-scatter of dY @ W_p; d(rs_linear) is an
+  all-gather GEMM of dOut with W_p; weight gradients read the gathered buffers.
 
 Reference counterpart: the (unfused) ``ColumnParallelLinear`` /
 ``RowParallelLinear`` of complexity/parallel/tensor_parallel.py:181-311, which
@@ -54,6 +54,9 @@ class TPWorkspace:
         self.pad_buf, self.pads = self._alloc((4 * 8,), torch.int32, zero=True)
         self.epochs = [0, 0, 0, 0]
         self.buffers: Dict[str, Tuple[torch.Tensor, List[int]]] = {}
+        self.flag_bufs: Dict[str, torch.Tensor] = {}
+        self.flag_uses: Dict[str, int] = {}
+        self.views: Dict[str, torch.Tensor] = {}
 
     def _alloc(self, shape, dtype, zero=False):
         n = 1
@@ -78,7 +81,21 @@ class TPWorkspace:
             self.buffers[name] = self._alloc((n,), dtype)
             cur = self.buffers[name]
         t, ptrs = cur
-        return t[:n].view(*shape), ptrs
+        view = t[:n].view(*shape)
+        self.views[name] = view
+        return view, ptrs
+
+    def flags(self, name: str, n: int):
+        """Local int32 chunk counters of call site ``name`` and the number of uses
+        including this one (a chunk is complete when its counter reaches
+        uses x pieces-per-chunk; counters are never reset)."""
+        f = self.flag_bufs.get(name)
+        if f is None or f.numel() < n:
+            f = torch.zeros(n, dtype=torch.int32, device=self.device)
+            self.flag_bufs[name] = f
+            self.flag_uses[name] = 0
+        self.flag_uses[name] += 1
+        return f[:n], self.flag_uses[name]
 
     def epoch(self, rnd: int) -> int:
         self.epochs[rnd] += 1
@@ -97,74 +114,73 @@ def _shard_rows(T: int, world: int) -> int:
 
 def _ag_gemm(ws: TPWorkspace, name: str, x_shard: torch.Tensor, w: torch.Tensor, b_mn: bool,
              epi: int = EPI_STORE, **epi_kw) -> torch.Tensor:
-    """``AllGather(x_shard) @ op(w)`` with the gather fused into the GEMM loads."""
+    """``AllGather(x_shard) @ op(w)`` with the gather inside the GEMM: copier warps
+    pull the peers' row chunks (once each) into this rank's gathered buffer while
+    the tensor cores work on this rank's own rows."""
     C = require()
     rows, K = x_shard.shape
     T = rows * ws.world
-    buf, ptrs = ws.buffer(name, (rows, K), torch.bfloat16)
-    buf.copy_(x_shard)
+    g, ptrs = ws.buffer(name, (T, K), torch.bfloat16)
+    g[ws.rank * rows:(ws.rank + 1) * rows].copy_(x_shard)
+    flags, uses = ws.flags(name, T // 128)
     N = w.shape[1] if b_mn else w.shape[0]
     e = ws.epoch(ROUND_AG)
+    tail = (ws.pads, ws.rank, ROUND_AG, e, 0, True, ptrs, flags, rows, uses)
     if epi == EPI_SWIGLU_FWD:
-        C.gemm_dist(buf, False, w, b_mn, T, N, K, epi, None, epi_kw["gu"], epi_kw["act"],
+        C.gemm_dist(g, False, w, b_mn, T, N, K, epi, None, epi_kw["gu"], epi_kw["act"],
                     epi_kw.get("row_scale"), epi_kw["shared_width"], epi_kw["expert_width"],
-                    epi_kw["n_experts"], epi_kw["shared_scale"], ptrs, rows, [], 0, [], 0,
-                    ws.pads, ws.rank, ROUND_AG, e, 1, True)
+                    epi_kw["n_experts"], epi_kw["shared_scale"], [], 0, [], 0, [], 0, *tail)
         return epi_kw["act"]
     out = epi_kw.get("out")
     if out is None:
         out = torch.empty(T, N, device=x_shard.device, dtype=torch.bfloat16)
-    C.gemm_dist(buf, False, w, b_mn, T, N, K, epi, out, epi_kw.get("gu"), None,
+    C.gemm_dist(g, False, w, b_mn, T, N, K, epi, out, epi_kw.get("gu"), None,
                 epi_kw.get("row_scale"), epi_kw.get("shared_width", 0),
                 epi_kw.get("expert_width", 1), epi_kw.get("n_experts", 0),
-                epi_kw.get("shared_scale", 1.0), ptrs, rows, [], 0, [], 0, ws.pads, ws.rank,
-                ROUND_AG, e, 1, True)
+                epi_kw.get("shared_scale", 1.0), [], 0, [], 0, [], 0, *tail)
     return out
+
+
+def gathered(ws: TPWorkspace, name: str) -> torch.Tensor:
+    """This rank's complete gathered buffer of call site ``name`` (after its AG GEMM)."""
+    return ws.views[name]
 
 
 def _rs_gemm(ws: TPWorkspace, name: str, a: torch.Tensor, w: torch.Tensor, b_mn: bool,
              residual: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Reduce-scatter of ``a @ op(w)`` by rows: returns this rank's [T/P, N] rows."""
+    """Reduce-scatter of ``a @ op(w)`` by rows: returns this rank's [T/P, N] rows.
+
+    The GEMM writes its bf16 partial of all rows into this rank's symmetric
+    buffer (TMA stores); the finish kernel reads the peers' partials of the
+    rows this rank owns over NVLink, once, and sums them with its own.
+    """
     C = require()
     T, K = a.shape
     N = w.shape[1] if b_mn else w.shape[0]
     rows = _shard_rows(T, ws.world)
-    slots, ptrs = ws.buffer(name, (ws.world * rows, N), torch.float32)
-    C.gemm_dist(a, False, w, b_mn, T, N, K, EPI_PEER_STORE, slots, None, None, None, 0, 1, 0,
-                1.0, [], 0, [], 0, ptrs, rows, ws.pads, ws.rank, ROUND_RS, 0, 0, False)
+    part, ptrs = ws.buffer(name, (T, N), torch.bfloat16)
+    C.gemm(a, False, w, b_mn, T, N, K, EPI_STORE, out=part)
     out = torch.empty(rows, N, device=a.device, dtype=torch.bfloat16)
-    C.tp_rs_finish(slots, ws.world, rows, N, residual, out, ws.pads, ws.rank, ROUND_RS,
+    C.tp_rs_finish(ptrs, rows, N, N, residual, out, ws.pads, ws.rank, ROUND_RS,
                    ws.epoch(ROUND_RS))
     return out
 
 
 def _wgrad_gathered_b(ws: TPWorkspace, name: str, dy: torch.Tensor, n_rows: int, K: int
                       ) -> torch.Tensor:
-    """dW = dY^T @ AllGather(X) where X's shards sit in buffer ``name`` (MN-major B
-    segmented along the token dimension)."""
-    C = require()
-    T, N = dy.shape
-    buf, ptrs = ws.buffers[name]
-    rows = T // ws.world
-    out = torch.zeros(N, K, device=dy.device, dtype=torch.float32)
-    C.gemm_dist(dy, True, buf[:rows * K].view(rows, K), True, N, K, T, EPI_F32_ATOMIC, out, None,
-                None, None, 0, 1, 0, 1.0, [], 0, ptrs, rows, [], 0, [], 0, 0, 0, 0, False)
-    return out
+    """dW = dY^T @ AllGather(X), reading the gathered X that the forward GEMM left
+    in this rank's buffer ``name`` (no second transfer)."""
+    from ..ops.fused import gemm_tn
+
+    return gemm_tn(dy, gathered(ws, name), out_dtype=torch.float32)
 
 
 def _wgrad_gathered_a(ws: TPWorkspace, name: str, x_local: torch.Tensor, n_out: int
                       ) -> torch.Tensor:
-    """dW = AllGather(dOut)^T @ X_local where dOut's shards sit in buffer ``name``
-    (MN-major A segmented along the token dimension)."""
-    C = require()
-    T, K = x_local.shape
-    buf, ptrs = ws.buffers[name]
-    rows = T // ws.world
-    out = torch.zeros(n_out, K, device=x_local.device, dtype=torch.float32)
-    C.gemm_dist(buf[:rows * n_out].view(rows, n_out), True, x_local, True, n_out, K, T,
-                EPI_F32_ATOMIC, out, None, None, None, 0, 1, 0, 1.0, ptrs, rows, [], 0, [], 0,
-                [], 0, 0, 0, 0, False)
-    return out
+    """dW = AllGather(dOut)^T @ X_local, with the gathered dOut left in buffer ``name``."""
+    from ..ops.fused import gemm_tn
+
+    return gemm_tn(gathered(ws, name), x_local, out_dtype=torch.float32)
 
 
 class AGLinearFn(torch.autograd.Function):
