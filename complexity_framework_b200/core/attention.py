@@ -176,6 +176,29 @@ class GroupedQueryAttention(nn.Module):
         o = attn_ops.attention(q, k, v, causal=True, scale=self.attn_scale)  # [B, S, Hq*D]
         return fused.linear(o, self.o_proj.weight, residual)
 
+    def forward_sp(self, x_shard: torch.Tensor, residual: torch.Tensor, B: int, S: int,
+                   ws, name: str) -> torch.Tensor:
+        """Fused sequence-parallel TP: ``x_shard`` [T/P, H] -> [T/P, H] (+ residual).
+
+        K|Q|V is an all-gather GEMM (this rank's heads for all T tokens),
+        attention runs on full sequences, o_proj is a reduce-scatter GEMM.
+        """
+        from ..ops import attention as attn_ops
+        from ..ops import fused
+        from ..parallel.tp_fused import ag_linear, rs_linear
+
+        kqv = ag_linear(x_shard, self.kqv_weight(), ws, name + ".kqv").view(B, S, -1)
+        cos, sin = self.rotary_emb.tables(S, x_shard.device)
+        if self.use_qk_norm:
+            qw, kw, eps = self.q_norm.weight, self.k_norm.weight, self.q_norm.eps
+        else:
+            qw = kw = kqv.new_ones(self.head_dim)
+            eps = 1e-6
+        q, k, v = fused.qk_norm_rope(kqv, qw, kw, cos, sin, None, self.num_heads,
+                                     self.num_kv_heads, self.head_dim, eps, self.use_qk_norm)
+        o = attn_ops.attention(q, k, v, causal=True, scale=self.attn_scale)  # [B, S, Hq_p*D]
+        return rs_linear(o.reshape(B * S, -1), self.o_proj.weight, residual, ws, name + ".o")
+
     def _forward_reference(self, x, attention_mask, past_key_value, use_cache):
         B, S, _ = x.shape
         k, q, v = self._project(x)

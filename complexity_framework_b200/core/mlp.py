@@ -123,6 +123,20 @@ class TRHashEngineMLP(nn.Module):
             raise ValueError("tr_hash_engine requires token_ids")
         return self.engine(hidden_states, token_ids, residual=residual)
 
+    def forward_sp(self, h_shard, token_ids, residual, ws, name: str):
+        """Fused sequence-parallel TP: [T/P, H] -> [T/P, H] (+ residual); routes use
+        the token ids of all T tokens."""
+        from ..ops import fused
+        from ..parallel.tp_fused import TPMLPFn
+
+        eng = self.engine
+        cfg = eng.config
+        scales = fused.route_scales(token_ids, eng._active_route_table, eng._route_weights,
+                                    cfg.num_experts, cfg.routed_output_scale)
+        w_gu, w_down = eng.packed_weights()
+        return TPMLPFn.apply(h_shard, w_gu, w_down, scales, residual, ws, name, cfg.shared_width,
+                             cfg.expert_width, cfg.num_experts, cfg.shared_output_scale)
+
     def set_top_k_primary_weight(self, weight: float) -> None:
         """Re-blend route slots; unlike the reference, every backend sees the new weights."""
         if self.top_k == 1:

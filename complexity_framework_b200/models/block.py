@@ -93,6 +93,14 @@ class TransformerBlock(nn.Module):
         x = self.mlp(h, token_ids=token_ids, residual=x)
         return x, new_kv, None
 
+    def forward_sp(self, x_shard: torch.Tensor, token_ids: torch.Tensor, B: int, S: int, ws):
+        """Fused sequence-parallel block on a [T/P, H] token shard."""
+        name = f"layer{self.layer_idx}"
+        h, x = self._norm_skip(self.input_layernorm, x_shard)
+        x = self.self_attn.forward_sp(h, x, B, S, ws, name + ".attn")
+        h, x = self._norm_skip(self.post_attention_layernorm, x)
+        return self.mlp.forward_sp(h, token_ids, x, ws, name + ".mlp")
+
     @staticmethod
     def _norm_skip(norm, x):
         """Norm output plus the residual stream routed through the norm, so the

@@ -195,6 +195,8 @@ class ComplexityModel(nn.Module):
         """
         from ..core.losses import causal_lm_loss_from_hidden
 
+        if getattr(self, "sp_ws", None) is not None and input_ids.is_cuda:
+            return self._loss_sp(input_ids, labels, ignore_index)
         hidden = self(input_ids, return_logits=False)["last_hidden_state"]
         if labels is None:
             labels = torch.roll(input_ids, -1, dims=1)
@@ -204,6 +206,37 @@ class ComplexityModel(nn.Module):
             scale = 1.0 / max(1.0, self.config.hidden_size / self.config.mup_base_width)
         return causal_lm_loss_from_hidden(hidden, self.output_weight(), labels,
                                           ignore_index=ignore_index, logit_scale=scale)
+
+    def _loss_sp(self, input_ids: torch.Tensor, labels: Optional[torch.Tensor],
+                 ignore_index: int) -> torch.Tensor:
+        """Fused sequence-parallel TP loss: this rank embeds, normalises and scores
+        its T/P token rows; attention / MLP communicate inside their GEMMs.
+        Returns this rank's share of the global mean loss (shares sum to the
+        loss; replicated-parameter gradients are summed over the TP group by
+        ``parallel.tp_fused.allreduce_replicated_grads``)."""
+        from ..core.losses import causal_lm_loss_from_hidden
+
+        ws = self.sp_ws
+        P, r = ws.world, ws.rank
+        B, S = input_ids.shape
+        T = B * S
+        rows = T // P
+        if labels is None:
+            labels = torch.roll(input_ids, -1, dims=1)
+            labels[:, -1] = ignore_index
+        if self.training and torch.is_grad_enabled():
+            ws.begin_step()
+        flat = input_ids.reshape(-1)
+        x = self.embed(flat[r * rows:(r + 1) * rows].view(1, rows)).view(rows, -1)
+        for layer in self.layers:
+            x = layer.forward_sp(x, input_ids, B, S, ws)
+        x = self.norm(x)
+        lab = labels.reshape(-1)[r * rows:(r + 1) * rows]
+        n_local = (lab != ignore_index).sum()
+        n_total = (labels != ignore_index).sum().clamp_min(1)
+        loss = causal_lm_loss_from_hidden(x.view(1, rows, -1), self.output_weight(),
+                                          lab.view(1, rows), ignore_index=ignore_index)
+        return loss * (n_local / n_total)
 
     # ------------------------------------------------------------ generation
     @torch.no_grad()

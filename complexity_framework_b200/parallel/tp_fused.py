@@ -231,3 +231,80 @@ def ag_linear(x_shard, w, ws: TPWorkspace, name: str):
 
 def rs_linear(x, w, residual, ws: TPWorkspace, name: str):
     return RSLinearFn.apply(x, w, residual, ws, name)
+
+
+class TPMLPFn(torch.autograd.Function):
+    """TR-Hash MLP under fused sequence-parallel TP: gate|up all-gather GEMM with
+    the SwiGLU + route-scale epilogue, down projection as a reduce-scatter GEMM
+    with the residual added in the finish kernel.  Backward: the down data
+    gradient is an all-gather GEMM with the SwiGLU-backward epilogue."""
+
+    @staticmethod
+    def forward(ctx, h_shard, w_gu, w_down, row_scale, residual, ws, name, sw, ew, ne, ss):
+        rows, H = h_shard.shape
+        T = rows * ws.world
+        A2 = w_gu.shape[0]
+        dev = h_shard.device
+        gu = torch.empty(T, A2, device=dev, dtype=torch.bfloat16)
+        act = torch.empty(T, A2 // 2, device=dev, dtype=torch.bfloat16)
+        _ag_gemm(ws, name + ".h", h_shard.contiguous(), w_gu.contiguous(), False, EPI_SWIGLU_FWD,
+                 gu=gu, act=act, row_scale=row_scale, shared_width=sw, expert_width=ew,
+                 n_experts=ne, shared_scale=ss)
+        out = _rs_gemm(ws, name + ".down", act, w_down.contiguous(), False,
+                       residual.contiguous() if residual is not None else None)
+        ctx.save_for_backward(w_gu, w_down, row_scale, gu, act)
+        ctx.meta = (ws, name, sw, ew, ne, ss, residual is not None)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        w_gu, w_down, row_scale, gu, act = ctx.saved_tensors
+        ws, name, sw, ew, ne, ss, has_res = ctx.meta
+        from ..ops.fused import gemm_tn
+
+        T, A2 = gu.shape
+        dgu = torch.empty(T, A2, device=gu.device, dtype=torch.bfloat16)
+        _ag_gemm(ws, name + ".dy", dout.contiguous(), w_down, True, EPI_SWIGLU_BWD, out=dgu, gu=gu,
+                 row_scale=row_scale, shared_width=sw, expert_width=ew, n_experts=ne,
+                 shared_scale=ss)
+        dw_down = gemm_tn(gathered(ws, name + ".dy"), act).to(w_down.dtype)
+        dh = _rs_gemm(ws, name + ".dh", dgu, w_gu, True)
+        dw_gu = gemm_tn(dgu, gathered(ws, name + ".h")).to(w_gu.dtype)
+        return (dh, dw_gu, dw_down, None, dout if has_res else None, None, None, None, None, None,
+                None)
+
+
+def enable_fused_sequence_parallel(model, group=None):
+    """Shard ``model`` for tensor parallelism (heads, shared and expert widths)
+    and switch its CUDA forward to the fused sequence-parallel path."""
+    from .tensor_parallel import make_parallel, tp_world
+
+    group = group if group is not None else dist.group.WORLD
+    if tp_world(group) < 2:
+        raise ValueError("fused sequence parallelism needs a group of 2..8 ranks")
+    make_parallel(model, group)
+    ws = TPWorkspace(group)
+    model.sp_ws = ws
+    for layer in model.layers:
+        if getattr(layer.self_attn, "num_kv_heads", 1) and any(
+                getattr(p, "_tp_replicated_kv", False) for p in layer.self_attn.parameters()):
+            raise ValueError("fused sequence parallelism needs KV heads divisible by the TP size")
+    return model
+
+
+def replicated_parameters(model):
+    """Parameters every TP rank holds in full (embeddings, norms, LM head): their
+    gradients are partial per rank under sequence parallelism."""
+    return [p for p in model.parameters() if p.requires_grad and not hasattr(p, "_tp_shard_dim")]
+
+
+def allreduce_replicated_grads(model, group=None) -> None:
+    grads = [p.grad for p in replicated_parameters(model) if p.grad is not None]
+    if not grads:
+        return
+    flat = torch.cat([g.reshape(-1).float() for g in grads])
+    dist.all_reduce(flat, group=group or model.sp_ws.group)
+    off = 0
+    for g in grads:
+        g.copy_(flat[off:off + g.numel()].view_as(g))
+        off += g.numel()

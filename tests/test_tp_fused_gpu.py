@@ -81,3 +81,71 @@ def test_fused_tp_ag_rs_two_gpus():
     out = dict(q.get() for _ in range(2))
     for r, errs in out.items():
         assert max(errs.values()) < 3e-2, (r, errs)
+
+
+def _model_body(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", rank))
+    import copy
+
+    from complexity_framework_b200 import ComplexityModel, ModelConfig
+    from complexity_framework_b200.ops import check_errors
+    from complexity_framework_b200.parallel.tp_fused import (allreduce_replicated_grads,
+                                                             enable_fused_sequence_parallel)
+
+    cfg = ModelConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=4,
+                      num_key_value_heads=2, vocab_size=2048, intermediate_size=256,
+                      shared_intermediate_size=512, num_experts=4, top_k=2,
+                      routing_strategy="token_id_multi_hash", max_position_embeddings=256)
+    torch.manual_seed(0)
+    ref = ComplexityModel(cfg).cuda().bfloat16().train()
+    ids = torch.randint(0, 2048, (2, 256), generator=torch.Generator().manual_seed(1)).cuda()
+    loss_ref = ref.loss(ids)
+    loss_ref.backward()
+    sp = enable_fused_sequence_parallel(copy.deepcopy(ref).train())
+    for p in sp.parameters():
+        p.grad = None
+    share = sp.loss(ids)
+    share.backward()
+    allreduce_replicated_grads(sp)
+    tot = share.detach().float().clone()
+    dist.all_reduce(tot)
+    torch.cuda.synchronize()
+    check_errors(rank)
+    g_ref = dict(ref.named_parameters())
+
+    def rel(a, b):
+        return float((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-6))
+
+    errs = {"loss": abs(float(tot) - float(loss_ref)) / float(loss_ref)}
+    for name, p in sp.named_parameters():
+        if p.grad is None:
+            continue
+        full = g_ref[name].grad
+        if hasattr(p, "_tp_shard_dim"):
+            d = p._tp_shard_dim
+            n = p.shape[d]
+            full = full.narrow(d, rank * n, n)
+        errs[name] = rel(p.grad, full)
+    q.put((rank, errs))
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_sequence_parallel_model_two_gpus():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_model_body, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    out = dict(q.get() for _ in range(2))
+    for r, errs in out.items():
+        assert errs["loss"] < 1e-2, (r, errs["loss"])
+        bad = {k: round(v, 4) for k, v in errs.items() if v >= 6e-2}
+        assert not bad, (r, bad)
