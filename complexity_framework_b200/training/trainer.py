@@ -28,6 +28,17 @@ from .scheduler import build_scheduler
 logger = logging.getLogger(__name__)
 
 
+def _singleton_group(group):
+    """A process group holding only this rank (collective: every rank of ``group`` calls it)."""
+    mine = None
+    me = dist.get_rank()
+    for r in dist.get_process_group_ranks(group):
+        g = dist.new_group([r])
+        if r == me:
+            mine = g
+    return mine
+
+
 class Trainer:
     def __init__(self, model: torch.nn.Module, config: Optional[TrainingConfig] = None, *,
                  device: Optional[torch.device] = None, process_group=None,
@@ -50,6 +61,14 @@ class Trainer:
         if mode == "auto":
             mode = ("fsdp" if self.config.use_fsdp else "ddp") if self.world > 1 else "none"
         self.distributed_mode = mode
+        self.sp_ws = getattr(self.model, "sp_ws", None)
+        if self.sp_ws is not None:
+            # fused sequence-parallel TP: every rank of the group owns different
+            # parameter shards; only replicated parameters are reduced (below),
+            # so the optimizer works rank-locally
+            process_group = _singleton_group(self.sp_ws.group)
+            self.world, self.rank = 1, 0
+            mode = "none"
         if self.world > 1:
             self._broadcast_parameters(process_group)
         self.optimizer = self._build_optimizer(process_group, mode)
@@ -128,7 +147,12 @@ class Trainer:
         loss.backward()
         self._finish_step()
         self.total_tokens += ids.numel() * self.world
-        return float(loss.detach()) if sync else loss.detach()
+        out = loss.detach()
+        if self.sp_ws is not None:
+            # each TP rank returned its share of the global mean loss
+            out = out.float().clone()
+            dist.all_reduce(out, group=self.sp_ws.group)
+        return float(out) if sync else out
 
     def accumulate_step(self, micro_batches: Iterable[torch.Tensor], *, sync: bool = True):
         """Gradient accumulation over micro-batches, one optimizer step at the end."""
@@ -151,6 +175,12 @@ class Trainer:
         check = (self.global_step == 0 and not self.config.skip_param_update_check)
         if check:
             self._canary = self._snapshot()
+        if self.sp_ws is not None:
+            from ..parallel.tp_fused import allreduce_replicated_grads
+
+            if hasattr(opt, "_gather_grads"):
+                opt._gather_grads()  # bind the fresh gradients to the flat buffers first
+            allreduce_replicated_grads(self.model)
         opt.reduce_gradients()
         clip = self.config.grad_clip > 0
         if clip:

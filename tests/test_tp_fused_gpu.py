@@ -149,3 +149,73 @@ def test_fused_sequence_parallel_model_two_gpus():
         assert errs["loss"] < 1e-2, (r, errs["loss"])
         bad = {k: round(v, 4) for k, v in errs.items() if v >= 6e-2}
         assert not bad, (r, bad)
+
+
+def _trainer_body(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", rank))
+    import copy
+
+    from complexity_framework_b200 import ComplexityModel, ModelConfig
+    from complexity_framework_b200.ops import check_errors
+    from complexity_framework_b200.parallel.tp_fused import enable_fused_sequence_parallel
+    from complexity_framework_b200.training import Trainer, TrainingConfig
+
+    cfg = ModelConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=4,
+                      num_key_value_heads=2, vocab_size=2048, intermediate_size=256,
+                      shared_intermediate_size=512, num_experts=4, top_k=2,
+                      routing_strategy="token_id_multi_hash", max_position_embeddings=256)
+    tc = dict(learning_rate=2e-3, warmup_steps=0, lr_scheduler="constant",
+              skip_param_update_check=True)
+    ids = torch.randint(0, 2048, (2, 256), generator=torch.Generator().manual_seed(3))
+    torch.manual_seed(0)
+    base = ComplexityModel(cfg)
+    sp = enable_fused_sequence_parallel(copy.deepcopy(base).cuda().bfloat16())
+    tr_sp = Trainer(sp, TrainingConfig(**tc))
+    losses_sp = [tr_sp.train_step(ids) for _ in range(4)]
+    torch.cuda.synchronize()
+    check_errors(rank)
+    losses_ref = None
+    from complexity_framework_b200.training.trainer import _singleton_group
+
+    solo = _singleton_group(dist.group.WORLD)  # collective
+    if rank == 0:
+        # single-GPU reference run (no process group involvement)
+        ref_model = copy.deepcopy(base).cuda().bfloat16()
+        from complexity_framework_b200.training.optim import FusedAdamW, default_param_groups
+
+        opt = FusedAdamW(default_param_groups(ref_model, 0.1), lr=2e-3, betas=(0.9, 0.95),
+                         weight_decay=0.1, process_group=solo)
+        losses_ref = []
+        for _ in range(4):
+            loss = ref_model.loss(ids.cuda())
+            loss.backward()
+            opt.reduce_gradients()
+            opt.clip_grad_norm_(1.0)
+            opt.step(clip=True)
+            opt.zero_grad()
+            losses_ref.append(float(loss))
+    q.put((rank, losses_sp, losses_ref))
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_trainer_fused_sequence_parallel_two_gpus():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_trainer_body, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = {r: (a, b) for r, a, b in (q.get() for _ in range(2))}
+    sp0, ref = res[0]
+    sp1, _ = res[1]
+    assert sp0 == sp1  # every TP rank reports the same global loss
+    assert sp0[-1] < sp0[0]
+    for a, b in zip(sp0, ref):
+        assert abs(a - b) / b < 2e-2, (sp0, ref)
