@@ -1,0 +1,83 @@
+"""GPU/runtime helpers, integer ops, safety clamps (CPU parts)."""
+import os
+
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from complexity_framework_b200 import ComplexityModel, ModelConfig
+from complexity_framework_b200.core.integer_ops import Int8Linear, int8_matmul, lut_silu, quantize_int8_rows
+from complexity_framework_b200.utils.gpu import GradientCompressor, clip_grad_norm_fused, dtype_from_string
+from complexity_framework_b200.utils.safety import (MultiDirectionSafetyClamp, SafetyClamp,
+                                                    get_safety_stats, install_safety,
+                                                    remove_safety)
+
+
+def test_int8_and_lut():
+    torch.manual_seed(0)
+    lin = torch.nn.Linear(64, 32)
+    x = torch.randn(8, 64)
+    y = Int8Linear(lin)(x)
+    assert float((y - lin(x)).abs().max() / lin(x).abs().max()) < 0.03
+    qa, sa = quantize_int8_rows(x)
+    qw, sw = quantize_int8_rows(lin.weight.detach())
+    assert int8_matmul(qa, sa, qw, sw).shape == (8, 32)
+    t = torch.linspace(-6, 6, 100)
+    assert float((lut_silu()(t) - torch.nn.functional.silu(t)).abs().max()) < 0.05
+
+
+def test_clip_and_dtype():
+    m = torch.nn.Linear(8, 8)
+    m(torch.randn(4, 8)).sum().mul(100).backward()
+    ref = torch.nn.utils.get_total_norm([p.grad for p in m.parameters()])
+    n = clip_grad_norm_fused(m.parameters(), 1.0)
+    assert abs(float(n) - float(ref)) / float(ref) < 1e-5
+    assert float(torch.nn.utils.get_total_norm([p.grad for p in m.parameters()])) <= 1.0 + 1e-4
+    assert dtype_from_string("bf16") == torch.bfloat16
+
+
+def _comp(rank, port, method, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    torch.manual_seed(rank)
+    m = torch.nn.Linear(16, 16)
+    m.weight.grad = torch.full_like(m.weight, float(rank + 1))
+    m.bias.grad = torch.zeros_like(m.bias)
+    GradientCompressor(method, ratio=1.0).compress_and_allreduce(m)
+    q.put((rank, float(m.weight.grad.mean())))
+    dist.destroy_process_group()
+
+
+def test_gradient_compressor_gloo():
+    import socket
+
+    for method in ("none", "topk", "quantize"):
+        s = socket.socket()
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+        s.close()
+        ctx = mp.get_context("spawn")
+        q = ctx.Queue()
+        ps = [ctx.Process(target=_comp, args=(r, port, method, q)) for r in range(2)]
+        [p.start() for p in ps]
+        [p.join(120) for p in ps]
+        vals = dict(q.get() for _ in range(2))
+        assert all(abs(v - 1.5) < 0.02 for v in vals.values()), (method, vals)
+
+
+def test_safety_clamps():
+    d = torch.zeros(8)
+    d[0] = 1
+    c = SafetyClamp(d, threshold=1.0)
+    h = torch.tensor([[5.0] + [0.0] * 7])
+    assert float(c(h)[0, 0]) == 1.0
+    mc = MultiDirectionSafetyClamp(torch.eye(8)[:2], threshold=0.5)
+    assert float(mc(torch.ones(1, 8))[0, :2].max()) <= 0.5 + 1e-5
+    m = ComplexityModel(ModelConfig(hidden_size=64, num_hidden_layers=3, num_attention_heads=4,
+                                    num_key_value_heads=2, vocab_size=128, intermediate_size=64,
+                                    shared_intermediate_size=128, num_experts=4, top_k=2,
+                                    routing_strategy="modulo_cyclic"))
+    install_safety(m, torch.randn(64))
+    m(torch.randint(0, 128, (1, 8)))
+    assert get_safety_stats(m)["calls"] == 1
+    remove_safety(m)
