@@ -12,6 +12,7 @@
 
 #include "dist_fused.h"
 #include "tp_fused.h"
+#include "ep_fused.h"
 #include "flash.h"
 #include "gemm_tc.h"
 #include "kernels.h"
@@ -316,6 +317,52 @@ void tp_barrier(const std::vector<int64_t>& pads, int64_t rank, int64_t round, i
   raise_rc(rc, "tp_barrier");
 }
 
+// out[i] = residual[i] + sum_j w[i,j] * rows of peers' buffers (EP dispatch / combine).
+void ep_gather_combine(const std::vector<int64_t>& srcs, const torch::Tensor& idx,
+                       const c10::optional<torch::Tensor>& w, int64_t stride,
+                       const c10::optional<torch::Tensor>& residual, torch::Tensor& out,
+                       const std::vector<int64_t>& pads, int64_t rank, int64_t round,
+                       int64_t epoch) {
+  check_bf16_cuda(out, "out");
+  TORCH_CHECK(out.dim() == 2 && out.is_contiguous(), "out must be contiguous [rows, H]");
+  TORCH_CHECK(idx.is_cuda() && idx.scalar_type() == torch::kInt32 && idx.is_contiguous() &&
+                  idx.dim() == 2 && idx.size(0) == out.size(0),
+              "idx must be int32 [rows, k]");
+  TORCH_CHECK(!srcs.empty() && srcs.size() <= 8 && pads.size() <= 8, "1..8 ranks");
+  const int k = static_cast<int>(idx.size(1));
+  const float* wp = nullptr;
+  if (w.has_value()) {
+    TORCH_CHECK(w->scalar_type() == torch::kFloat32 && w->is_contiguous() &&
+                    w->numel() == idx.numel(),
+                "w must be fp32 like idx");
+    wp = w->data_ptr<float>();
+  }
+  const __nv_bfloat16* r = nullptr;
+  if (residual.has_value()) {
+    check_bf16_cuda(*residual, "residual");
+    TORCH_CHECK(residual->is_contiguous() && residual->sizes() == out.sizes(), "residual shape");
+    r = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+  }
+  cfb::EpSources es{};
+  for (size_t i = 0; i < srcs.size(); ++i)
+    es.p[i] = reinterpret_cast<const __nv_bfloat16*>(srcs[i]);
+  cfb::EpSync sy{};
+  for (size_t i = 0; i < pads.size(); ++i) sy.pad[i] = reinterpret_cast<int*>(pads[i]);
+  sy.world = static_cast<int>(pads.size());
+  sy.world_srcs = static_cast<int>(srcs.size());
+  sy.rank = static_cast<int>(rank);
+  sy.round = static_cast<int>(round);
+  sy.epoch = static_cast<int>(epoch);
+  const c10::cuda::CUDAGuard guard(out.device());
+  const int rc = cfb::ep_gather_combine(es, idx.data_ptr<int>(), wp, out.size(0),
+                                        static_cast<int>(out.size(1)), stride, r,
+                                        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), k, sy,
+                                        num_sms(out.get_device()),
+                                        at::cuda::getCurrentCUDAStream(),
+                                        err_ptr(out.get_device()));
+  raise_rc(rc, "ep_gather_combine");
+}
+
 // Causal/full attention forward; writes out [B,S,Hq*D] and lse [B,Hq,S].
 void flash_attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
                     torch::Tensor& out, torch::Tensor& lse, double scale, bool causal) {
@@ -416,6 +463,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_dist", &gemm_dist);
   m.def("tp_rs_finish", &tp_rs_finish);
   m.def("tp_barrier", &tp_barrier);
+  m.def("ep_gather_combine", &ep_gather_combine);
   m.def("gemm", &gemm, "tcgen05 GEMM with fused epilogues", py::arg("A"), py::arg("a_mn"),
         py::arg("B"), py::arg("b_mn"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epi"),
         py::arg("out") = py::none(), py::arg("residual") = py::none(), py::arg("alpha") = 1.0,

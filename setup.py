@@ -21,6 +21,7 @@ SOURCES = [
     "dist_fused.cu",
     "noalloc.cu",
     "tp_fused.cu",
+    "ep_fused.cu",
 ]
 
 NVCC_FLAGS = [
