@@ -63,7 +63,7 @@ void qk_norm_rope_fwd(const torch::Tensor& kqv, const torch::Tensor& qw, const t
                       const torch::Tensor& cos_t, const torch::Tensor& sin_t,
                       const c10::optional<torch::Tensor>& pos, torch::Tensor& q, torch::Tensor& k,
                       torch::Tensor& v, torch::Tensor& rstd, int64_t B, int64_t S, int64_t Hq,
-                      int64_t Hkv, int64_t D, double eps, bool qk_norm) {
+                      int64_t Hkv, int64_t D, double eps, bool qk_norm, bool q_tm) {
   TORCH_CHECK(B * S * (Hq + 2 * Hkv) < (int64_t(1) << 31), "qk_norm_rope: too many (token, head) items");
   chk(kqv, torch::kBFloat16, "kqv");
   chk(qw, torch::kBFloat16, "q_norm.weight");
@@ -91,7 +91,7 @@ void qk_norm_rope_fwd(const torch::Tensor& kqv, const torch::Tensor& qw, const t
                         Popt<int32_t>(pos), P<bf16>(q), P<bf16>(k), P<bf16>(v), P<float>(rstd),
                         static_cast<int>(B), static_cast<int>(S), static_cast<int>(Hq),
                         static_cast<int>(Hkv), static_cast<int>(D), static_cast<float>(eps),
-                        qk_norm, cur());
+                        qk_norm, q_tm, cur());
 }
 
 void qk_norm_rope_bwd(const torch::Tensor& dq, const torch::Tensor& dk, const torch::Tensor& dv,
@@ -99,7 +99,7 @@ void qk_norm_rope_bwd(const torch::Tensor& dq, const torch::Tensor& dk, const to
                       const torch::Tensor& cos_t, const torch::Tensor& sin_t,
                       const c10::optional<torch::Tensor>& pos, const torch::Tensor& rstd,
                       torch::Tensor& dkqv, torch::Tensor& dqw, torch::Tensor& dkw, int64_t B,
-                      int64_t S, int64_t Hq, int64_t Hkv, int64_t D, bool qk_norm) {
+                      int64_t S, int64_t Hq, int64_t Hkv, int64_t D, bool qk_norm, bool q_tm) {
   TORCH_CHECK(B * S * (Hq + 2 * Hkv) < (int64_t(1) << 31), "qk_norm_rope: too many (token, head) items");
   chk(dq, torch::kBFloat16, "dq");
   chk(dk, torch::kBFloat16, "dk");
@@ -118,7 +118,7 @@ void qk_norm_rope_bwd(const torch::Tensor& dq, const torch::Tensor& dk, const to
                         P<bf16>(kw), P<float>(cos_t), P<float>(sin_t), Popt<int32_t>(pos),
                         P<float>(rstd), P<bf16>(dkqv), P<float>(dqw), P<float>(dkw),
                         static_cast<int>(B), static_cast<int>(S), static_cast<int>(Hq),
-                        static_cast<int>(Hkv), static_cast<int>(D), qk_norm, cur());
+                        static_cast<int>(Hkv), static_cast<int>(D), qk_norm, q_tm, cur());
 }
 
 void embedding_fwd(const torch::Tensor& ids, const torch::Tensor& table, torch::Tensor& out) {

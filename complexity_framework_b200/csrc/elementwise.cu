@@ -228,7 +228,8 @@ struct HeadItem {
 };
 
 template <int D>
-__device__ __forceinline__ HeadItem decode_item(int64_t item, int Htot, int S, int Hq, int Hkv) {
+__device__ __forceinline__ HeadItem decode_item(int64_t item, int Htot, int S, int Hq, int Hkv,
+                                                bool q_tm) {
   // item < 2^31 (checked by the launcher): 32-bit divisions are far cheaper
   HeadItem it;
   const uint32_t i32 = static_cast<uint32_t>(item);
@@ -240,7 +241,9 @@ __device__ __forceinline__ HeadItem decode_item(int64_t item, int Htot, int S, i
   if (it.hh < Hq) {
     it.kind = 0;
     it.col = Hkv * D + it.hh * D;
-    it.hm = (((int64_t)b * Hq + it.hh) * S + s) * D;
+    // q is head-major [B, Hq, S, D], or token-major [B, S, Hq, D] with q_tm
+    it.hm = q_tm ? (((int64_t)b * S + s) * Hq + it.hh) * D
+                 : (((int64_t)b * Hq + it.hh) * S + s) * D;
   } else if (it.hh < Hq + Hkv) {
     const int h = it.hh - Hq;
     it.kind = 1;
@@ -278,7 +281,7 @@ __global__ void qk_norm_rope_fwd_k(const bf16* __restrict__ kqv, const bf16* __r
                                    const float* __restrict__ sin_t, const int32_t* __restrict__ pos,
                                    bf16* __restrict__ q, bf16* __restrict__ k,
                                    bf16* __restrict__ v, float* __restrict__ rstd, int B, int S,
-                                   int Hq, int Hkv, float eps, bool qk_norm) {
+                                   int Hq, int Hkv, float eps, bool qk_norm, bool q_tm) {
   constexpr int LPH = D / 8, GPW = 32 / LPH, HALF = LPH / 2;
   const int lane = threadIdx.x & 31;
   const int grp = lane / LPH, gl = lane % LPH;
@@ -290,7 +293,7 @@ __global__ void qk_norm_rope_fwd_k(const bf16* __restrict__ kqv, const bf16* __r
   for (int64_t base = wid * GPW; base < total; base += nw * GPW) {
     const int64_t item = base + grp;
     const bool valid = item < total;
-    HeadItem it = decode_item<D>(valid ? item : total - 1, Htot, S, Hq, Hkv);
+    HeadItem it = decode_item<D>(valid ? item : total - 1, Htot, S, Hq, Hkv, q_tm);
     float x[8];
     load8(kqv + it.t * C + it.col + gl * 8, x);
     const bool qk = it.kind != 2;
@@ -333,7 +336,7 @@ __global__ void __launch_bounds__(256, 3) qk_norm_rope_bwd_k(const bf16* __restr
                                    const int32_t* __restrict__ pos, const float* __restrict__ rstd,
                                    bf16* __restrict__ dkqv, float* __restrict__ dqw,
                                    float* __restrict__ dkw, int B, int S, int Hq, int Hkv,
-                                   bool qk_norm) {
+                                   bool qk_norm, bool q_tm) {
   constexpr int LPH = D / 8, GPW = 32 / LPH, HALF = LPH / 2;
   __shared__ float s_dqw[D], s_dkw[D];
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
@@ -356,7 +359,7 @@ __global__ void __launch_bounds__(256, 3) qk_norm_rope_bwd_k(const bf16* __restr
   for (int64_t base = wid * GPW; base < total; base += nw * GPW) {
     const int64_t item = base + grp;
     const bool valid = item < total;
-    HeadItem it = decode_item<D>(valid ? item : total - 1, Htot, S, Hq, Hkv);
+    HeadItem it = decode_item<D>(valid ? item : total - 1, Htot, S, Hq, Hkv, q_tm);
     const bf16* src = it.kind == 0 ? dq : (it.kind == 1 ? dk : dv);
     float g[8];
     load8(src + it.hm + gl * 8, g);
@@ -577,29 +580,30 @@ void rmsnorm_bwd(const bf16* dy, const bf16* x, const bf16* w, const float* rstd
 void qk_norm_rope_fwd(const bf16* kqv, const bf16* qw, const bf16* kw, const float* cos_t,
                       const float* sin_t, const int32_t* pos, bf16* q, bf16* k, bf16* v,
                       float* rstd, int B, int S, int Hq, int Hkv, int D, float eps, bool qk_norm,
-                      cudaStream_t s) {
+                      bool q_tm, cudaStream_t s) {
   const int64_t items = (int64_t)B * S * (Hq + 2 * Hkv);
   const int grid = grid_for(items, 8 * (256 / D), 148 * 16);
   if (D == 64)
     qk_norm_rope_fwd_k<64><<<grid, 256, 0, s>>>(kqv, qw, kw, cos_t, sin_t, pos, q, k, v, rstd, B, S,
-                                               Hq, Hkv, eps, qk_norm);
+                                               Hq, Hkv, eps, qk_norm, q_tm);
   else
     qk_norm_rope_fwd_k<128><<<grid, 256, 0, s>>>(kqv, qw, kw, cos_t, sin_t, pos, q, k, v, rstd, B, S,
-                                               Hq, Hkv, eps, qk_norm);
+                                               Hq, Hkv, eps, qk_norm, q_tm);
 }
 
 void qk_norm_rope_bwd(const bf16* dq, const bf16* dk, const bf16* dv, const bf16* kqv,
                       const bf16* qw, const bf16* kw, const float* cos_t, const float* sin_t,
                       const int32_t* pos, const float* rstd, bf16* dkqv, float* dqw, float* dkw,
-                      int B, int S, int Hq, int Hkv, int D, bool qk_norm, cudaStream_t s) {
+                      int B, int S, int Hq, int Hkv, int D, bool qk_norm, bool q_tm,
+                      cudaStream_t s) {
   const int64_t items = (int64_t)B * S * (Hq + 2 * Hkv);
   const int grid = grid_for(items, 8 * (256 / D), 148 * 3);
   if (D == 64)
     qk_norm_rope_bwd_k<64><<<grid, 256, 0, s>>>(dq, dk, dv, kqv, qw, kw, cos_t, sin_t, pos, rstd,
-                                               dkqv, dqw, dkw, B, S, Hq, Hkv, qk_norm);
+                                               dkqv, dqw, dkw, B, S, Hq, Hkv, qk_norm, q_tm);
   else
     qk_norm_rope_bwd_k<128><<<grid, 256, 0, s>>>(dq, dk, dv, kqv, qw, kw, cos_t, sin_t, pos, rstd,
-                                               dkqv, dqw, dkw, B, S, Hq, Hkv, qk_norm);
+                                               dkqv, dqw, dkw, B, S, Hq, Hkv, qk_norm, q_tm);
 }
 
 void embedding_fwd(const int64_t* ids, const bf16* table, bf16* out, int64_t T, int H, int64_t V,

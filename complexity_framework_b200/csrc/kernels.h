@@ -16,16 +16,17 @@ void rmsnorm_bwd(const bf16* dy, const bf16* x, const bf16* w, const float* rstd
                  const bf16* dres, bf16* dx, float* dw, int64_t T, int H, cudaStream_t s);
 
 // kqv [T, (2*Hkv+Hq)*D] in k|q|v order -> per-head RMSNorm of q and k, RoPE
-// (rotate-half, cos/sin tables [P, D/2]) and scatter to head-major q/k/v
-// [B, H, S, D].  rstd [T, Hq+Hkv] (q heads first).
+// (rotate-half, cos/sin tables [P, D/2]) and scatter to head-major k/v
+// [B, H, S, D] and q (head-major, or token-major [B, S, Hq, D] with q_tm).  rstd [T, Hq+Hkv] (q heads first).
 void qk_norm_rope_fwd(const bf16* kqv, const bf16* qw, const bf16* kw, const float* cos_t,
                       const float* sin_t, const int32_t* pos, bf16* q, bf16* k, bf16* v,
                       float* rstd, int B, int S, int Hq, int Hkv, int D, float eps, bool qk_norm,
-                      cudaStream_t s);
+                      bool q_tm, cudaStream_t s);
 void qk_norm_rope_bwd(const bf16* dq, const bf16* dk, const bf16* dv, const bf16* kqv,
                       const bf16* qw, const bf16* kw, const float* cos_t, const float* sin_t,
                       const int32_t* pos, const float* rstd, bf16* dkqv, float* dqw, float* dkw,
-                      int B, int S, int Hq, int Hkv, int D, bool qk_norm, cudaStream_t s);
+                      int B, int S, int Hq, int Hkv, int D, bool qk_norm, bool q_tm,
+                      cudaStream_t s);
 
 void embedding_fwd(const int64_t* ids, const bf16* table, bf16* out, int64_t T, int H, int64_t V,
                    cudaStream_t s);

@@ -1,7 +1,8 @@
 """Causal GQA/MHA attention entry point for the fused path.
 
-``attention(q, k, v)`` takes head-major ``q [B, Hq, S, D]``, ``k/v [B, Hkv, S, D]``
-(no K/V head replication) and returns ``[B, S, Hq*D]`` token-major output ready
+``attention(q, k, v)`` takes ``q [B, Hq, S, D]`` (head-major, or the transposed
+view of token-major memory), ``k/v [B, Hkv, S, D]`` (no K/V head replication)
+and returns ``[B, S, Hq*D]`` token-major output ready
 for the o_proj GEMM.  It dispatches to the sm_100a flash-attention kernel when
 the extension provides it, else to PyTorch SDPA with grouped K/V.
 """
@@ -28,7 +29,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: bool
     if q.shape[-1] in (64, 128) and _kernel_available(needs_grad):
         from .flash import flash_attention
 
-        return flash_attention(q, k, v, causal=causal, scale=scale)
+        return flash_attention(q.contiguous(), k, v, causal=causal, scale=scale)
     o = F.scaled_dot_product_attention(q, k, v, is_causal=causal, scale=scale,
                                        enable_gqa=k.shape[1] != Hq)
+    # a token-major q gives a token-major o: this reshape is then a view
     return o.transpose(1, 2).reshape(B, S, Hq * D)

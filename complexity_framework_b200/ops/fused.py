@@ -278,7 +278,13 @@ def rmsnorm_skip(x, w, eps):
 
 # ---------------------------------------------------------- QK-norm + RoPE
 class QKNormRopeFn(torch.autograd.Function):
-    """kqv [B,S,(2Hkv+Hq)D] -> head-major q [B,Hq,S,D], k/v [B,Hkv,S,D]."""
+    """kqv [B,S,(2Hkv+Hq)D] -> q [B,Hq,S,D], k/v [B,Hkv,S,D].
+
+    k/v are head-major contiguous.  q is stored token-major ([B,S,Hq,D]
+    memory, returned as its transposed view): SDPA then produces its output
+    and dq token-major too, so the attention output feeds o_proj as a free
+    ``[B,S,Hq*D]`` view instead of a per-layer transpose copy.
+    """
 
     @staticmethod
     def forward(ctx, kqv, qw, kw, cos, sin, pos, Hq, Hkv, D, eps, qk_norm):
@@ -286,15 +292,15 @@ class QKNormRopeFn(torch.autograd.Function):
         B, S = kqv.shape[0], kqv.shape[1]
         kqv = _c(kqv)
         dev = kqv.device
-        q = torch.empty(B, Hq, S, D, device=dev, dtype=torch.bfloat16)
+        q = torch.empty(B, S, Hq, D, device=dev, dtype=torch.bfloat16)
         k = torch.empty(B, Hkv, S, D, device=dev, dtype=torch.bfloat16)
         v = torch.empty(B, Hkv, S, D, device=dev, dtype=torch.bfloat16)
         rstd = torch.empty(B * S, Hq + Hkv, device=dev, dtype=torch.float32)
         C.qk_norm_rope_fwd(kqv, _c(qw), _c(kw), cos, sin, pos, q, k, v, rstd, B, S, Hq, Hkv, D,
-                           float(eps), bool(qk_norm))
+                           float(eps), bool(qk_norm), True)
         ctx.save_for_backward(kqv, qw, kw, cos, sin, rstd, pos)
         ctx.meta = (B, S, Hq, Hkv, D, bool(qk_norm))
-        return q, k, v
+        return q.transpose(1, 2), k, v
 
     @staticmethod
     def backward(ctx, dq, dk, dv):
@@ -309,11 +315,12 @@ class QKNormRopeFn(torch.autograd.Function):
         def z(shape):
             return torch.zeros(shape, device=dev, dtype=torch.bfloat16)
 
-        dq = _c(dq) if dq is not None else z((B, Hq, S, D))
+        # token-major dq; SDPA already returns it in that layout (no copy)
+        dq = dq.transpose(1, 2).contiguous() if dq is not None else z((B, S, Hq, D))
         dk = _c(dk) if dk is not None else z((B, Hkv, S, D))
         dv = _c(dv) if dv is not None else z((B, Hkv, S, D))
         C.qk_norm_rope_bwd(dq, dk, dv, kqv, _c(qw), _c(kw), cos, sin, pos, rstd, dkqv, dqw, dkw,
-                           B, S, Hq, Hkv, D, qk_norm)
+                           B, S, Hq, Hkv, D, qk_norm, True)
         n = None
         return (dkqv, dqw.to(qw.dtype), dkw.to(kw.dtype), n, n, n, n, n, n, n, n)
 

@@ -102,17 +102,17 @@ def case_norms(iters: int) -> None:
                      1.0 / (10000 ** (torch.arange(0, D, 2, device="cuda").float() / D)))
     cos, sin = fr.cos().contiguous(), fr.sin().contiguous()
     pos = torch.arange(S, device="cuda", dtype=torch.int32).repeat(B, 1).contiguous()
-    q = torch.empty(B, Hq, S, D, device="cuda", dtype=torch.bfloat16)
+    q = torch.empty(B, S, Hq, D, device="cuda", dtype=torch.bfloat16)  # token-major
     k = torch.empty(B, Hkv, S, D, device="cuda", dtype=torch.bfloat16)
     v = torch.empty_like(k)
     rs = torch.empty(B * S, Hq + Hkv, device="cuda")
     nb = 2.0 * kqv.numel() * 2
     _report("qk_norm_rope_fwd", cuda_time(lambda: C.qk_norm_rope_fwd(
-        kqv, qw, qw, cos, sin, pos, q, k, v, rs, B, S, Hq, Hkv, D, 1e-6, True), iters), nbytes=nb)
+        kqv, qw, qw, cos, sin, pos, q, k, v, rs, B, S, Hq, Hkv, D, 1e-6, True, True), iters), nbytes=nb)
     dk = torch.empty_like(kqv)
     dqw = torch.zeros(D, device="cuda")
     _report("qk_norm_rope_bwd", cuda_time(lambda: C.qk_norm_rope_bwd(
-        q, k, v, kqv, qw, qw, cos, sin, pos, rs, dk, dqw, dqw, B, S, Hq, Hkv, D, True), iters),
+        q, k, v, kqv, qw, qw, cos, sin, pos, rs, dk, dqw, dqw, B, S, Hq, Hkv, D, True, True), iters),
         nbytes=3.0 * kqv.numel() * 2)
     torch.cuda.synchronize()
     check_errors(0)
