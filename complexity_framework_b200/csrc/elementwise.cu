@@ -11,6 +11,10 @@
 // All kernels use 16-byte vector accesses (8 bf16) and warp-per-row layouts;
 // none uses scratch memory beyond its outputs.
 #include <cmath>
+#include <map>
+#include <mutex>
+#include <set>
+#include <utility>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -213,55 +217,8 @@ __global__ void __launch_bounds__(256, 3)
 }
 
 // ------------------------------------------------------- QK-norm + RoPE
-// LPH = D/8 lanes cooperate on one (token, head) item with 16-byte vectors
-// (lane gl of a group owns elements 8*gl .. 8*gl+7); a warp handles 32/LPH
-// consecutive items of the flattened [token, head] order.  Head index hh:
-// [0,Hq) q heads, [Hq, Hq+Hkv) k heads, [Hq+Hkv, Hq+2Hkv) v heads; the fused
-// projection output kqv stores columns in k | q | v order.  The rotate-half
-// partner of element j (j +- D/2) lives in lane gl ^ (LPH/2) of the group.
-struct HeadItem {
-  int64_t t;
-  int hh;
-  int col;
-  int64_t hm;  // element offset of (b, head, s, 0) in the head-major tensor
-  int kind;    // 0 = q, 1 = k, 2 = v
-};
-
-template <int D>
-__device__ __forceinline__ HeadItem decode_item(int64_t item, int Htot, int S, int Hq, int Hkv,
-                                                bool q_tm) {
-  // item < 2^31 (checked by the launcher): 32-bit divisions are far cheaper
-  HeadItem it;
-  const uint32_t i32 = static_cast<uint32_t>(item);
-  const uint32_t t32 = i32 / static_cast<uint32_t>(Htot);
-  it.t = t32;
-  it.hh = static_cast<int>(i32 - t32 * static_cast<uint32_t>(Htot));
-  const int b = static_cast<int>(t32 / static_cast<uint32_t>(S));
-  const int s = static_cast<int>(t32 - static_cast<uint32_t>(b) * static_cast<uint32_t>(S));
-  if (it.hh < Hq) {
-    it.kind = 0;
-    it.col = Hkv * D + it.hh * D;
-    // q is head-major [B, Hq, S, D], or token-major [B, S, Hq, D] with q_tm
-    it.hm = q_tm ? (((int64_t)b * S + s) * Hq + it.hh) * D
-                 : (((int64_t)b * Hq + it.hh) * S + s) * D;
-  } else if (it.hh < Hq + Hkv) {
-    const int h = it.hh - Hq;
-    it.kind = 1;
-    it.col = h * D;
-    it.hm = (((int64_t)b * Hkv + h) * S + s) * D;
-  } else {
-    const int h = it.hh - Hq - Hkv;
-    it.kind = 2;
-    it.col = (Hkv + Hq) * D + h * D;
-    it.hm = (((int64_t)b * Hkv + h) * S + s) * D;
-  }
-  return it;
-}
-
-__device__ __forceinline__ int s_of(int64_t t, int S) {
-  return static_cast<int>(static_cast<uint32_t>(t) % static_cast<uint32_t>(S));
-}
-
+// Head index hh: [0,Hq) q heads, [Hq, Hq+Hkv) k heads, [Hq+Hkv, Hq+2Hkv) v
+// heads; the fused projection output kqv stores columns in k | q | v order.
 template <int LPH>
 __device__ __forceinline__ float group_sum(float v) {
 #pragma unroll
@@ -269,144 +226,324 @@ __device__ __forceinline__ float group_sum(float v) {
   return v;
 }
 
-__device__ __forceinline__ void load8f(const float* p, float* v) {
+
+// One warp per token.  Each warp owns a ring of NS token slots in shared
+// memory and keeps NS-1 tokens of loads in flight with cp.async (16-byte
+// pieces, no spin-wait: cp.async.wait_group retires them), so HBM latency is
+// hidden without holding rows in registers.  Compute then reads shared memory
+// only.  Lane layout: LPH = D/8 lanes per head, lane gl holding elements
+// [4gl, 4gl+4) and their rotate-half partners [D/2+4gl, D/2+4gl+4), so RoPE is
+// lane-local; a warp covers GPW = 32/LPH heads per pass (q heads, then k heads,
+// in one uniform loop).  v heads are a plain copy.  Destination offsets are
+// formed once per token.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem)), "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void lds4(const bf16* p, float* v) {  // 4 bf16 (8 bytes)
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+__device__ __forceinline__ void st4(bf16* p, const float* v) {
+  uint2 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+__device__ __forceinline__ void lds4f(const float* p, float* v) {
   const float4 a = *reinterpret_cast<const float4*>(p);
-  const float4 b = *reinterpret_cast<const float4*>(p + 4);
-  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+}
+// bf16 rounding of two floats with one conversion
+__device__ __forceinline__ void rb2(float& a, float& b) {
+  const float2 f = unpack_bf16x2(pack_bf16x2(a, b));
+  a = f.x;
+  b = f.y;
 }
 
-template <int D>
-__global__ void qk_norm_rope_fwd_k(const bf16* __restrict__ kqv, const bf16* __restrict__ qw,
-                                   const bf16* __restrict__ kw, const float* __restrict__ cos_t,
-                                   const float* __restrict__ sin_t, const int32_t* __restrict__ pos,
-                                   bf16* __restrict__ q, bf16* __restrict__ k,
-                                   bf16* __restrict__ v, float* __restrict__ rstd, int B, int S,
-                                   int Hq, int Hkv, float eps, bool qk_norm, bool q_tm) {
-  constexpr int LPH = D / 8, GPW = 32 / LPH, HALF = LPH / 2;
-  const int lane = threadIdx.x & 31;
-  const int grp = lane / LPH, gl = lane % LPH;
-  const int Htot = Hq + 2 * Hkv;
-  const int C = Htot * D;
-  const int64_t total = (int64_t)B * S * Htot;
-  const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t base = wid * GPW; base < total; base += nw * GPW) {
-    const int64_t item = base + grp;
-    const bool valid = item < total;
-    HeadItem it = decode_item<D>(valid ? item : total - 1, Htot, S, Hq, Hkv, q_tm);
-    float x[8];
-    load8(kqv + it.t * C + it.col + gl * 8, x);
-    const bool qk = it.kind != 2;
-    if (qk_norm) {
-      float ss = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ss += x[j] * x[j];
-      ss = group_sum<LPH>(ss);
-      const float r = rsqrtf(ss / D + eps);
-      if (qk) {
-        float wv[8];
-        load8((it.kind == 0 ? qw : kw) + gl * 8, wv);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) x[j] = rb(rb(x[j] * r) * wv[j]);
-        if (gl == 0 && valid) rstd[it.t * (Hq + Hkv) + it.hh] = r;
-      }
-    }
-    const int p = pos != nullptr ? pos[it.t] : s_of(it.t, S);
-    float c[8], sn[8], o[8];
-    load8f(cos_t + (int64_t)p * (D / 2) + (gl % HALF) * 8, c);
-    load8f(sin_t + (int64_t)p * (D / 2) + (gl % HALF) * 8, sn);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float partner = __shfl_xor_sync(0xffffffffu, x[j], HALF);
-      o[j] = gl < HALF ? x[j] * c[j] - partner * sn[j] : x[j] * c[j] + partner * sn[j];
-      if (!qk) o[j] = x[j];
-    }
-    if (valid) {
-      bf16* dst = it.kind == 0 ? q : (it.kind == 1 ? k : v);
-      store8(dst + it.hm + gl * 8, o);
-    }
-  }
+// Per-token destination bases: q is head-major [B, Hq, S, D] or token-major
+// [B, S, Hq, D] (q_tm); k/v are head-major [B, Hkv, S, D].
+struct TokenBases {
+  int64_t q, kv;     // element offsets of head 0
+  int64_t q_stride;  // elements between consecutive q heads
+};
+__device__ __forceinline__ TokenBases token_bases(int b, int s, int S, int Hq, int Hkv, int D,
+                                                  bool q_tm) {
+  TokenBases tb;
+  tb.q = q_tm ? ((int64_t)b * S + s) * Hq * D : ((int64_t)b * Hq * S + s) * D;
+  tb.q_stride = q_tm ? D : (int64_t)S * D;
+  tb.kv = ((int64_t)b * Hkv * S + s) * D;
+  return tb;
 }
 
-template <int D>
-__global__ void __launch_bounds__(256, 3) qk_norm_rope_bwd_k(const bf16* __restrict__ dq, const bf16* __restrict__ dk,
-                                   const bf16* __restrict__ dv, const bf16* __restrict__ kqv,
-                                   const bf16* __restrict__ qw, const bf16* __restrict__ kw,
-                                   const float* __restrict__ cos_t, const float* __restrict__ sin_t,
-                                   const int32_t* __restrict__ pos, const float* __restrict__ rstd,
-                                   bf16* __restrict__ dkqv, float* __restrict__ dqw,
-                                   float* __restrict__ dkw, int B, int S, int Hq, int Hkv,
-                                   bool qk_norm, bool q_tm) {
-  constexpr int LPH = D / 8, GPW = 32 / LPH, HALF = LPH / 2;
-  __shared__ float s_dqw[D], s_dkw[D];
+// Forward slot: the token's whole fused k|q|v row (C = (Hq + 2 Hkv) D bf16),
+// then its cos and sin table rows (D/2 floats each).
+template <int D, int NS>
+__global__ void __launch_bounds__(128) qk_norm_rope_fwd_k(
+    const bf16* __restrict__ kqv, const bf16* __restrict__ qw, const bf16* __restrict__ kw,
+    const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+    const int32_t* __restrict__ pos, bf16* __restrict__ q, bf16* __restrict__ k,
+    bf16* __restrict__ v, float* __restrict__ rstd, int B, int S, int Hq, int Hkv, float eps,
+    bool qk_norm, bool q_tm) {
+  constexpr int LPH = D / 8, GPW = 32 / LPH, H2 = D / 2;
+  extern __shared__ __align__(16) unsigned char qk_smem[];
+  __shared__ __align__(16) float s_w[2][D];
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
-    s_dqw[i] = 0.f;
-    s_dkw[i] = 0.f;
+    s_w[0][i] = __bfloat162float(qw[i]);
+    s_w[1][i] = __bfloat162float(kw[i]);
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int grp = lane / LPH, gl = lane % LPH;
-  const int Htot = Hq + 2 * Hkv;
+  const int Htot = Hq + 2 * Hkv, Hqk = Hq + Hkv;
   const int C = Htot * D;
-  const int64_t total = (int64_t)B * S * Htot;
-  const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
-  float accq[8], acck[8], wq[8], wk[8];
+  const int T = B * S;
+  const int warp = threadIdx.x >> 5;
+  const int wpb = blockDim.x >> 5;
+  const int wid = blockIdx.x * wpb + warp;
+  const int nw = gridDim.x * wpb;
+  const int slot = C * 2 + D * 4;  // bytes
+  unsigned char* ring = qk_smem + (size_t)warp * NS * slot;
+  auto issue = [&](int i) {  // prefetch this warp's i-th token into slot i % NS
+    const int t = wid + i * nw;
+    if (t < T) {
+      const bf16* src = kqv + (int64_t)t * C;
+      unsigned char* dst = ring + (i % NS) * slot;
+      for (int c = lane; c < C / 8; c += 32) cp_async16(dst + c * 16, src + c * 8);
+      const int p = pos != nullptr ? pos[t] : t % S;
+      if (lane < D / 4) {  // D/2 floats of cos then of sin: D/8 16-byte pieces each
+        const float* tab = lane < D / 8 ? cos_t : sin_t;
+        cp_async16(dst + C * 2 + lane * 16, tab + (int64_t)p * H2 + (lane % (D / 8)) * 4);
+      }
+    }
+    cp_async_commit();
+  };
+  // this lane's norm weights (q, k) at its 8 element positions
+  float wq[8], wk[8];
+  lds4f(&s_w[0][4 * gl], wq);
+  lds4f(&s_w[0][H2 + 4 * gl], wq + 4);
+  lds4f(&s_w[1][4 * gl], wk);
+  lds4f(&s_w[1][H2 + 4 * gl], wk + 4);
+#pragma unroll
+  for (int i = 0; i < NS - 1; ++i) issue(i);
+  for (int i = 0; wid + i * nw < T; ++i) {
+    issue(i + NS - 1);
+    cp_async_wait<NS - 1>();
+    __syncwarp();
+    const int t = wid + i * nw;
+    const bf16* row = reinterpret_cast<const bf16*>(ring + (i % NS) * slot);
+    const float* cs = reinterpret_cast<const float*>(row + C);
+    const int b = t / S, s = t - b * S;
+    const TokenBases tb = token_bases(b, s, S, Hq, Hkv, D, q_tm);
+    float c[4], sn[4];
+    lds4f(cs + 4 * gl, c);
+    lds4f(cs + H2 + 4 * gl, sn);
+    for (int h0 = 0; h0 < Hqk; h0 += GPW) {  // uniform trip count: shuffles stay convergent
+      const int hh = min(h0 + grp, Hqk - 1);
+      const bool valid = h0 + grp < Hqk;
+      const bool isq = hh < Hq;
+      const int col = isq ? (Hkv + hh) * D : (hh - Hq) * D;
+      float x[8];
+      lds4(row + col + 4 * gl, x);
+      lds4(row + col + H2 + 4 * gl, x + 4);
+      if (qk_norm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += x[j] * x[j];
+        ss = group_sum<LPH>(ss);
+        const float r = rsqrtf(ss * (1.0f / D) + eps);
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+          float a = x[j] * r, bb = x[j + 1] * r;
+          rb2(a, bb);
+          a *= isq ? wq[j] : wk[j];
+          bb *= isq ? wq[j + 1] : wk[j + 1];
+          rb2(a, bb);
+          x[j] = a;
+          x[j + 1] = bb;
+        }
+        if (gl == 0 && valid) rstd[(int64_t)t * Hqk + hh] = r;
+      }
+      float lo[4], hi[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        lo[j] = x[j] * c[j] - x[j + 4] * sn[j];
+        hi[j] = x[j + 4] * c[j] + x[j] * sn[j];
+      }
+      if (valid) {
+        bf16* dst = isq ? q + tb.q + hh * tb.q_stride : k + tb.kv + (int64_t)(hh - Hq) * S * D;
+        st4(dst + 4 * gl, lo);
+        st4(dst + H2 + 4 * gl, hi);
+      }
+    }
+    // v heads: copy
+    const bf16* vrow = row + Hqk * D;
+    for (int c8 = lane; c8 < Hkv * D / 8; c8 += 32) {
+      const int h = c8 / (D / 8), e = (c8 % (D / 8)) * 8;
+      *reinterpret_cast<uint4*>(v + tb.kv + (int64_t)h * S * D + e) =
+          *reinterpret_cast<const uint4*>(vrow + h * D + e);
+    }
+    __syncwarp();  // the slot is refilled by the next iteration's prefetch
+  }
+  cp_async_wait<0>();
+}
+
+// Backward slot: the gradients of all Htot heads in q, k, v head order (head
+// hh at hh * D), the k|q part of the forward input row (only with qk_norm),
+// the cos and sin rows, and the token's saved 1/rms values (Hq + Hkv floats,
+// padded to 16 bytes).
+template <int D, int NS>
+__global__ void __launch_bounds__(128) qk_norm_rope_bwd_k(
+    const bf16* __restrict__ dq, const bf16* __restrict__ dk, const bf16* __restrict__ dv,
+    const bf16* __restrict__ kqv, const bf16* __restrict__ qw, const bf16* __restrict__ kw,
+    const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+    const int32_t* __restrict__ pos, const float* __restrict__ rstd, bf16* __restrict__ dkqv,
+    float* __restrict__ dqw, float* __restrict__ dkw, int B, int S, int Hq, int Hkv,
+    bool qk_norm, bool q_tm) {
+  constexpr int LPH = D / 8, GPW = 32 / LPH, H2 = D / 2;
+  extern __shared__ __align__(16) unsigned char qk_smem[];
+  __shared__ float s_dqw[D], s_dkw[D];
+  __shared__ __align__(16) float s_w[2][D];
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    s_dqw[i] = 0.f;
+    s_dkw[i] = 0.f;
+    s_w[0][i] = __bfloat162float(qw[i]);
+    s_w[1][i] = __bfloat162float(kw[i]);
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int grp = lane / LPH, gl = lane % LPH;
+  const int Htot = Hq + 2 * Hkv, Hqk = Hq + Hkv;
+  const int C = Htot * D;
+  const int CX = qk_norm ? Hqk * D : 0;  // k|q columns of the input row
+  const int slot = (C + CX) * 2 + D * 4 + ((Hqk * 4 + 15) & ~15);  // bytes
+  const int T = B * S;
+  const int warp = threadIdx.x >> 5;
+  const int wpb = blockDim.x >> 5;
+  const int wid = blockIdx.x * wpb + warp;
+  const int nw = gridDim.x * wpb;
+  unsigned char* ring = qk_smem + (size_t)warp * NS * slot;
+  auto issue = [&](int i) {
+    const int t = wid + i * nw;
+    if (t < T) {
+      const int b = t / S, s = t - b * S;
+      const TokenBases tb = token_bases(b, s, S, Hq, Hkv, D, q_tm);
+      bf16* dst = reinterpret_cast<bf16*>(ring + (i % NS) * slot);
+      for (int c8 = lane; c8 < Htot * LPH; c8 += 32) {
+        const int hh = c8 / LPH, e = (c8 % LPH) * 8;
+        const bf16* src = hh < Hq ? dq + tb.q + hh * tb.q_stride
+                                  : (hh < Hqk ? dk + tb.kv + (int64_t)(hh - Hq) * S * D
+                                              : dv + tb.kv + (int64_t)(hh - Hqk) * S * D);
+        cp_async16(dst + hh * D + e, src + e);
+      }
+      const bf16* xr = kqv + (int64_t)t * C;
+      for (int c8 = lane; c8 < CX / 8; c8 += 32) cp_async16(dst + C + c8 * 8, xr + c8 * 8);
+      float* fdst = reinterpret_cast<float*>(dst + C + CX);
+      const int p = pos != nullptr ? pos[t] : s;
+      if (lane < D / 4) {
+        const float* tab = lane < D / 8 ? cos_t : sin_t;
+        cp_async16(fdst + lane * 4, tab + (int64_t)p * H2 + (lane % (D / 8)) * 4);
+      }
+      if (qk_norm)
+        for (int c = lane; c < Hqk; c += 32) cp_async4(fdst + D + c, rstd + (int64_t)t * Hqk + c);
+    }
+    cp_async_commit();
+  };
+  float wq[8], wk[8], accq[8], acck[8];
+  lds4f(&s_w[0][4 * gl], wq);
+  lds4f(&s_w[0][H2 + 4 * gl], wq + 4);
+  lds4f(&s_w[1][4 * gl], wk);
+  lds4f(&s_w[1][H2 + 4 * gl], wk + 4);
 #pragma unroll
   for (int j = 0; j < 8; ++j) accq[j] = acck[j] = 0.f;
-  load8(qw + gl * 8, wq);
-  load8(kw + gl * 8, wk);
-  for (int64_t base = wid * GPW; base < total; base += nw * GPW) {
-    const int64_t item = base + grp;
-    const bool valid = item < total;
-    HeadItem it = decode_item<D>(valid ? item : total - 1, Htot, S, Hq, Hkv, q_tm);
-    const bf16* src = it.kind == 0 ? dq : (it.kind == 1 ? dk : dv);
-    float g[8];
-    load8(src + it.hm + gl * 8, g);
-    const bool qk = it.kind != 2;
-    // inverse rotation: dn_j = g_j cos_j + (first half ? g_{j+D/2} : -g_{j-D/2}) sin_j
-    const int p = pos != nullptr ? pos[it.t] : s_of(it.t, S);
-    float c[8], sn[8], dn[8];
-    load8f(cos_t + (int64_t)p * (D / 2) + (gl % HALF) * 8, c);
-    load8f(sin_t + (int64_t)p * (D / 2) + (gl % HALF) * 8, sn);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float partner = __shfl_xor_sync(0xffffffffu, g[j], HALF);
-      dn[j] = gl < HALF ? g[j] * c[j] + partner * sn[j] : g[j] * c[j] - partner * sn[j];
-      if (!qk) dn[j] = g[j];
-    }
-    float o[8];
-    if (qk_norm) {
-      const float r = qk ? rstd[it.t * (Hq + Hkv) + it.hh] : 0.f;
-      float x[8];
-      load8(kqv + it.t * C + it.col + gl * 8, x);
-      const float* wv = it.kind == 0 ? wq : wk;
-      float dot = 0.f, dxr[8];
+  for (int i = 0; i < NS - 1; ++i) issue(i);
+  for (int i = 0; wid + i * nw < T; ++i) {
+    issue(i + NS - 1);
+    cp_async_wait<NS - 1>();
+    __syncwarp();
+    const int t = wid + i * nw;
+    const bf16* sl = reinterpret_cast<const bf16*>(ring + (i % NS) * slot);
+    const float* fs = reinterpret_cast<const float*>(sl + C + CX);
+    bf16* drow = dkqv + (int64_t)t * C;
+    float c[4], sn[4];
+    lds4f(fs + 4 * gl, c);
+    lds4f(fs + H2 + 4 * gl, sn);
+    for (int h0 = 0; h0 < Hqk; h0 += GPW) {  // uniform trip count: shuffles stay convergent
+      const int hh = min(h0 + grp, Hqk - 1);
+      const bool valid = h0 + grp < Hqk;
+      const bool isq = hh < Hq;
+      const int col = isq ? (Hkv + hh) * D : (hh - Hq) * D;
+      float g[8];
+      lds4(sl + hh * D + 4 * gl, g);
+      lds4(sl + hh * D + H2 + 4 * gl, g + 4);
+      // inverse rotation
+      float dn[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        dxr[j] = dn[j] * wv[j];
-        dot += dxr[j] * x[j];
+      for (int j = 0; j < 4; ++j) {
+        dn[j] = g[j] * c[j] + g[j + 4] * sn[j];
+        dn[j + 4] = g[j + 4] * c[j] - g[j] * sn[j];
       }
-      dot = group_sum<LPH>(dot);
-      const float c3 = dot * r * r * r / D;
+      float o[8];
+      if (qk_norm) {
+        float x[8];
+        lds4(sl + C + col + 4 * gl, x);
+        lds4(sl + C + col + H2 + 4 * gl, x + 4);
+        const float rr = fs[D + hh];
+        float dot = 0.f, dxr[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        o[j] = qk ? r * dxr[j] - x[j] * c3 : dn[j];
-        const float contrib = valid ? dn[j] * rb(x[j] * r) : 0.f;
-        if (it.kind == 0) accq[j] += contrib;
-        else if (it.kind == 1) acck[j] += contrib;
+        for (int j = 0; j < 8; ++j) {
+          dxr[j] = dn[j] * (isq ? wq[j] : wk[j]);
+          dot += dxr[j] * x[j];
+        }
+        dot = group_sum<LPH>(dot);
+        const float c3 = dot * rr * rr * rr * (1.0f / D);
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+          o[j] = rr * dxr[j] - x[j] * c3;
+          o[j + 1] = rr * dxr[j + 1] - x[j + 1] * c3;
+          float a = x[j] * rr, bb = x[j + 1] * rr;
+          rb2(a, bb);
+          const float ca = valid ? dn[j] * a : 0.f, cb = valid ? dn[j + 1] * bb : 0.f;
+          accq[j] += isq ? ca : 0.f;
+          accq[j + 1] += isq ? cb : 0.f;
+          acck[j] += isq ? 0.f : ca;
+          acck[j + 1] += isq ? 0.f : cb;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = dn[j];
       }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = dn[j];
+      if (valid) {
+        st4(drow + col + 4 * gl, o);
+        st4(drow + col + H2 + 4 * gl, o + 4);
+      }
     }
-    if (valid) store8(dkqv + it.t * C + it.col + gl * 8, o);
+    // v heads: the gradient passes through unchanged
+    for (int c8 = lane; c8 < Hkv * D / 8; c8 += 32)
+      *reinterpret_cast<uint4*>(drow + Hqk * D + c8 * 8) =
+          *reinterpret_cast<const uint4*>(sl + Hqk * D + c8 * 8);
+    __syncwarp();
   }
+  cp_async_wait<0>();
   if (qk_norm) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      atomicAdd(&s_dqw[gl * 8 + j], accq[j]);
-      atomicAdd(&s_dkw[gl * 8 + j], acck[j]);
+      const int e = j < 4 ? 4 * gl + j : H2 + 4 * gl + (j - 4);
+      atomicAdd(&s_dqw[e], accq[j]);
+      atomicAdd(&s_dkw[e], acck[j]);
     }
   }
   __syncthreads();
@@ -577,18 +714,66 @@ void rmsnorm_bwd(const bf16* dy, const bf16* x, const bf16* w, const float* rstd
                                                                          dx, dw, T, H);
 }
 
+// Launch shape of the cp.async ring kernels: 4 warps x 4 stages, fewer when a
+// token slot is large (many heads), so the ring fits in shared memory.
+struct QkLaunch {
+  int warps, stages, grid;
+  size_t smem;
+};
+
+template <typename K4, typename K2>
+QkLaunch qk_launch(K4 k4, K2 k2, int slot_bytes, int64_t tokens) {
+  constexpr size_t kMaxSmem = 200 * 1024;
+  QkLaunch L{4, 4, 1, 0};
+  const size_t slot = (size_t)slot_bytes;
+  while (L.warps * L.stages * slot > kMaxSmem && (L.stages > 2 || L.warps > 1)) {
+    if (L.warps > 1) L.warps >>= 1;
+    else L.stages = 2;
+  }
+  L.smem = L.warps * L.stages * slot;
+  // The size attribute is raised once per kernel to the cap (it bounds, but
+  // does not set, the launch's shared memory); occupancy is cached per shape.
+  static std::mutex mu;
+  static std::set<const void*> raised;
+  static std::map<std::pair<const void*, size_t>, int> per_sm_cache;
+  const void* fn = L.stages == 4 ? reinterpret_cast<const void*>(k4)
+                                 : reinterpret_cast<const void*>(k2);
+  int per_sm = 0;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (raised.insert(fn).second)
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
+    const std::pair<const void*, size_t> key{fn, L.smem * 8 + L.warps};
+    auto it = per_sm_cache.find(key);
+    if (it != per_sm_cache.end()) {
+      per_sm = it->second;
+    } else {
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, L.warps * 32, L.smem) !=
+              cudaSuccess ||
+          per_sm < 1)
+        per_sm = 1;
+      per_sm_cache[key] = per_sm;
+    }
+  }
+  L.grid = grid_for(tokens, L.warps, 148 * per_sm);  // one resident wave
+  return L;
+}
+
 void qk_norm_rope_fwd(const bf16* kqv, const bf16* qw, const bf16* kw, const float* cos_t,
                       const float* sin_t, const int32_t* pos, bf16* q, bf16* k, bf16* v,
                       float* rstd, int B, int S, int Hq, int Hkv, int D, float eps, bool qk_norm,
                       bool q_tm, cudaStream_t s) {
-  const int64_t items = (int64_t)B * S * (Hq + 2 * Hkv);
-  const int grid = grid_for(items, 8 * (256 / D), 148 * 16);
-  if (D == 64)
-    qk_norm_rope_fwd_k<64><<<grid, 256, 0, s>>>(kqv, qw, kw, cos_t, sin_t, pos, q, k, v, rstd, B, S,
-                                               Hq, Hkv, eps, qk_norm, q_tm);
-  else
-    qk_norm_rope_fwd_k<128><<<grid, 256, 0, s>>>(kqv, qw, kw, cos_t, sin_t, pos, q, k, v, rstd, B, S,
-                                               Hq, Hkv, eps, qk_norm, q_tm);
+  const int slot = (Hq + 2 * Hkv) * D * 2 + D * 4;  // bytes; matches the kernel
+  const int64_t T = (int64_t)B * S;
+#define CFB_QK_FWD(DD)                                                                          \
+  {                                                                                             \
+    const QkLaunch L = qk_launch(qk_norm_rope_fwd_k<DD, 4>, qk_norm_rope_fwd_k<DD, 2>, slot, T); \
+    auto kern = L.stages == 4 ? qk_norm_rope_fwd_k<DD, 4> : qk_norm_rope_fwd_k<DD, 2>;          \
+    kern<<<L.grid, L.warps * 32, L.smem, s>>>(kqv, qw, kw, cos_t, sin_t, pos, q, k, v, rstd, B,  \
+                                              S, Hq, Hkv, eps, qk_norm, q_tm);                  \
+  }
+  if (D == 64) CFB_QK_FWD(64) else CFB_QK_FWD(128)
+#undef CFB_QK_FWD
 }
 
 void qk_norm_rope_bwd(const bf16* dq, const bf16* dk, const bf16* dv, const bf16* kqv,
@@ -596,14 +781,18 @@ void qk_norm_rope_bwd(const bf16* dq, const bf16* dk, const bf16* dv, const bf16
                       const int32_t* pos, const float* rstd, bf16* dkqv, float* dqw, float* dkw,
                       int B, int S, int Hq, int Hkv, int D, bool qk_norm, bool q_tm,
                       cudaStream_t s) {
-  const int64_t items = (int64_t)B * S * (Hq + 2 * Hkv);
-  const int grid = grid_for(items, 8 * (256 / D), 148 * 3);
-  if (D == 64)
-    qk_norm_rope_bwd_k<64><<<grid, 256, 0, s>>>(dq, dk, dv, kqv, qw, kw, cos_t, sin_t, pos, rstd,
-                                               dkqv, dqw, dkw, B, S, Hq, Hkv, qk_norm, q_tm);
-  else
-    qk_norm_rope_bwd_k<128><<<grid, 256, 0, s>>>(dq, dk, dv, kqv, qw, kw, cos_t, sin_t, pos, rstd,
-                                               dkqv, dqw, dkw, B, S, Hq, Hkv, qk_norm, q_tm);
+  const int nr = Hq + Hkv;  // bytes; matches the kernel
+  const int slot = ((Hq + 2 * Hkv) * D + (qk_norm ? nr * D : 0)) * 2 + D * 4 + ((nr * 4 + 15) & ~15);
+  const int64_t T = (int64_t)B * S;
+#define CFB_QK_BWD(DD)                                                                          \
+  {                                                                                             \
+    const QkLaunch L = qk_launch(qk_norm_rope_bwd_k<DD, 4>, qk_norm_rope_bwd_k<DD, 2>, slot, T); \
+    auto kern = L.stages == 4 ? qk_norm_rope_bwd_k<DD, 4> : qk_norm_rope_bwd_k<DD, 2>;          \
+    kern<<<L.grid, L.warps * 32, L.smem, s>>>(dq, dk, dv, kqv, qw, kw, cos_t, sin_t, pos, rstd,  \
+                                              dkqv, dqw, dkw, B, S, Hq, Hkv, qk_norm, q_tm);    \
+  }
+  if (D == 64) CFB_QK_BWD(64) else CFB_QK_BWD(128)
+#undef CFB_QK_BWD
 }
 
 void embedding_fwd(const int64_t* ids, const bf16* table, bf16* out, int64_t T, int H, int64_t V,

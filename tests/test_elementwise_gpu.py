@@ -39,8 +39,10 @@ def _rope_ref(x, cos, sin, pos):
     return x * c + rot * s
 
 
-@pytest.mark.parametrize("D,Hq,Hkv", [(64, 14, 2), (128, 8, 8), (64, 4, 1)])
-def test_qk_norm_rope_fwd_bwd(D, Hq, Hkv):
+@pytest.mark.parametrize("D,Hq,Hkv,qk_norm", [(64, 14, 2, True), (128, 8, 8, True),
+                                               (64, 4, 1, True), (64, 14, 2, False),
+                                               (128, 64, 8, True)])
+def test_qk_norm_rope_fwd_bwd(D, Hq, Hkv, qk_norm):
     from complexity_framework_b200.ops.fused import qk_norm_rope
 
     torch.manual_seed(0)
@@ -53,7 +55,7 @@ def test_qk_norm_rope_fwd_bwd(D, Hq, Hkv):
     fr = torch.outer(torch.arange(512, device=dev).float(), inv)
     cos, sin = fr.cos().contiguous(), fr.sin().contiguous()
     pos = torch.arange(S, device=dev, dtype=torch.int32).repeat(B, 1).contiguous()
-    q, k, v = qk_norm_rope(kqv, qw, kw, cos, sin, pos, Hq, Hkv, D, 1e-6, True)
+    q, k, v = qk_norm_rope(kqv, qw, kw, cos, sin, pos, Hq, Hkv, D, 1e-6, qk_norm)
     gq, gk, gv = torch.randn_like(q), torch.randn_like(k), torch.randn_like(v)
     (q.float() * gq).sum().add((k.float() * gk).sum()).add((v.float() * gv).sum()).backward()
 
@@ -65,12 +67,15 @@ def test_qk_norm_rope_fwd_bwd(D, Hq, Hkv):
     kh = kk.view(B, S, Hkv, D).transpose(1, 2)
     vh = vv.view(B, S, Hkv, D).transpose(1, 2)
     posl = pos.long()
-    qr = _rope_ref(_rms_ref(qh, qwr, 1e-6), cos, sin, posl)
-    kr2 = _rope_ref(_rms_ref(kh, kwr, 1e-6), cos, sin, posl)
+    nq = _rms_ref(qh, qwr, 1e-6) if qk_norm else qh
+    nk = _rms_ref(kh, kwr, 1e-6) if qk_norm else kh
+    qr = _rope_ref(nq, cos, sin, posl)
+    kr2 = _rope_ref(nk, cos, sin, posl)
     (qr * gq.float()).sum().add((kr2 * gk.float()).sum()).add((vh * gv.float()).sum()).backward()
     for a, b in ((q, qr), (k, kr2), (v, vh)):
         assert (a.float() - b).abs().max() < 5e-2
     rel = lambda a, b: float((a.float() - b).abs().max() / b.abs().max())  # noqa: E731
     assert rel(kqv.grad, kr.grad) < 2e-2
-    assert rel(qw.grad, qwr.grad) < 2e-2
-    assert rel(kw.grad, kwr.grad) < 2e-2
+    if qk_norm:
+        assert rel(qw.grad, qwr.grad) < 2e-2
+        assert rel(kw.grad, kwr.grad) < 2e-2
