@@ -243,9 +243,63 @@ void paged_attention(const torch::Tensor& q, const torch::Tensor& k_pool,
   TORCH_CHECK(rc == 0, "paged_attention failed with code ", rc);
 }
 
+// geom: 10 ints per job (rows, cols, s_div, s_hi, s_lo, s_cs, d_div, d_hi, d_lo,
+// d_cs), element offsets relative to each tensor's data pointer.  Every job's
+// largest source and destination offsets are checked against the tensors.
+void copy_jobs(const std::vector<torch::Tensor>& srcs, const std::vector<torch::Tensor>& dsts,
+               const std::vector<int64_t>& geom) {
+  const size_t n = srcs.size();
+  TORCH_CHECK(n >= 1 && n <= static_cast<size_t>(cfb::kMaxCopyJobs) && dsts.size() == n &&
+                  geom.size() == 10 * n,
+              "copy_jobs: 1..", cfb::kMaxCopyJobs, " jobs with 10 geometry values each");
+  cfb::CopyJobs jobs;
+  jobs.n = static_cast<int>(n);
+  auto max_off = [](int64_t rows, int64_t cols, int64_t div, int64_t hi, int64_t lo,
+                    int64_t cs) {
+    const int64_t r = rows - 1;
+    const int64_t inner = r < div - 1 ? r : div - 1;
+    return (r / div) * hi + inner * lo + (cols - 1) * cs;
+  };
+  for (size_t i = 0; i < n; ++i) {
+    const int64_t* g = geom.data() + 10 * i;
+    const torch::Tensor& s = srcs[i];
+    const torch::Tensor& d = dsts[i];
+    TORCH_CHECK(s.is_cuda() && d.is_cuda() && s.get_device() == d.get_device(),
+                "copy_jobs: CUDA tensors on one device");
+    TORCH_CHECK(s.scalar_type() == torch::kFloat32 || s.scalar_type() == torch::kBFloat16,
+                "copy_jobs: source must be fp32 or bf16");
+    TORCH_CHECK(d.scalar_type() == torch::kBFloat16, "copy_jobs: destination must be bf16");
+    TORCH_CHECK(g[0] > 0 && g[1] > 0 && g[0] < (1 << 30) && g[1] < (1 << 30) && g[2] > 0 &&
+                    g[6] > 0 && g[3] >= 0 && g[4] >= 0 && g[5] >= 0 && g[7] >= 0 &&
+                    g[8] >= 0 && g[9] >= 0,
+                "copy_jobs: bad geometry");
+    TORCH_CHECK(max_off(g[0], g[1], g[2], g[3], g[4], g[5]) < s.numel(),
+                "copy_jobs: job ", i, " reads past its source");
+    TORCH_CHECK(max_off(g[0], g[1], g[6], g[7], g[8], g[9]) < d.numel(),
+                "copy_jobs: job ", i, " writes past its destination");
+    cfb::CopyJob& J = jobs.j[i];
+    J.src = s.data_ptr();
+    J.dst = P<bf16>(d);
+    J.src_f32 = s.scalar_type() == torch::kFloat32;
+    J.rows = static_cast<int>(g[0]);
+    J.cols = static_cast<int>(g[1]);
+    J.s_div = static_cast<int>(std::min<int64_t>(g[2], 1 << 30));
+    J.s_hi = g[3];
+    J.s_lo = g[4];
+    J.s_cs = g[5];
+    J.d_div = static_cast<int>(std::min<int64_t>(g[6], 1 << 30));
+    J.d_hi = g[7];
+    J.d_lo = g[8];
+    J.d_cs = g[9];
+  }
+  const c10::cuda::CUDAGuard guard(srcs[0].device());
+  cfb::copy_jobs(jobs, cur());
+}
+
 }  // namespace
 
 void register_elementwise(pybind11::module& m) {
+  m.def("copy_jobs", &copy_jobs);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);

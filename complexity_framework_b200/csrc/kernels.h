@@ -61,4 +61,24 @@ int paged_attention(const bf16* q, const bf16* k_pool, const bf16* v_pool,
                     bf16* out, int N, int num_seqs, int max_pages, int Hq, int Hkv, int D,
                     int page_size, float scale, cudaStream_t s);
 
+// Batched strided 2-D copies (pack.cu): dst(r, c) = src(r, c) for r < rows,
+// c < cols, where a side's element offset is (r / div) * hi + (r % div) * lo
+// + c * cs; src is fp32 (src_f32) or bf16, dst bf16.
+constexpr int kMaxCopyJobs = 8;
+struct CopyJob {
+  const void* src = nullptr;
+  bf16* dst = nullptr;
+  int rows = 0, cols = 0;
+  int s_div = 1, d_div = 1;
+  int64_t s_hi = 0, s_lo = 0, s_cs = 1;
+  int64_t d_hi = 0, d_lo = 0, d_cs = 1;
+  int src_f32 = 0;
+  int vec = 0;  // set by copy_jobs: unit column strides and 16-byte aligned rows
+};
+struct CopyJobs {
+  CopyJob j[kMaxCopyJobs];
+  int n = 0;
+};
+void copy_jobs(const CopyJobs& jobs, cudaStream_t s);
+
 }  // namespace cfb

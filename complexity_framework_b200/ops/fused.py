@@ -13,6 +13,7 @@ transposed copies:
 """
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import torch
@@ -143,6 +144,148 @@ def pack_down(shared_down: Optional[torch.Tensor], expert_down: torch.Tensor) ->
     return torch.cat((shared_down, ed), 1) if shared_down is not None else _c(ed)
 
 
+_NO_SPLIT = 1 << 40  # row-index divisor meaning "no (outer, inner) split"
+
+
+def _trhash_pack_geometry(As: int, E: int, H: int, W: int, block: int = 128):
+    """Copy jobs packing (shared_gate, shared_up, expert_gate, expert_up,
+    shared_down, expert_down) into (w_gu [2A, H], w_down [H, A]).
+
+    Each job is ``(rows, cols, src(div, hi, lo, cs), dst offset, dst(div, hi, lo, cs))``
+    in elements; see ``copy_jobs`` in csrc/pack.cu.  Gate index g lands on
+    packed row ``(g // block) * 2 * block + g % block`` (+ block for up);
+    expert e's column w of ``[E, H, W]`` is gate index ``As + e * W + w``.
+    """
+    A = As + E * W
+    inter = (block, 2 * block * H, H, 1)
+    e_off = (As // block) * 2 * block * H
+    jobs = []
+    if As:
+        jobs.append(("sg", "gu", As, H, (_NO_SPLIT, 0, H, 1), 0, inter))
+        jobs.append(("su", "gu", As, H, (_NO_SPLIT, 0, H, 1), block * H, inter))
+    jobs.append(("eg", "gu", E * W, H, (W, H * W, 1, W), e_off, inter))
+    jobs.append(("eu", "gu", E * W, H, (W, H * W, 1, W), e_off + block * H, inter))
+    if As:
+        jobs.append(("sd", "down", H, As, (_NO_SPLIT, 0, As, 1), 0, (_NO_SPLIT, 0, A, 1)))
+    jobs.append(("ed", "down", H, E * W, (_NO_SPLIT, 0, 1, H), As, (_NO_SPLIT, 0, A, 1)))
+    return jobs
+
+
+def _run_jobs(jobs, tensors, reverse: bool):
+    """Run pack (reverse=False: weights -> packed) or unpack (packed -> weights) jobs."""
+    C = require()
+    srcs, dsts, geom = [], [], []
+    for name, packed, rows, cols, sg, off, pg in jobs:
+        w = tensors[name].reshape(-1)
+        pk = tensors[packed].reshape(-1)[off:]
+        if reverse:
+            srcs.append(pk)
+            dsts.append(w)
+            geom += [rows, cols, *pg, *sg]
+        else:
+            srcs.append(w)
+            dsts.append(pk)
+            geom += [rows, cols, *sg, *pg]
+    C.copy_jobs(srcs, dsts, geom)
+
+
+def pack_trhash_weights(sg, su, eg, eu, sd, ed, block: int = 128):
+    """(w_gu [2A, H], w_down [H, A]) in one copy-jobs launch (no autograd)."""
+    E, H, W = eg.shape
+    As = 0 if sg is None else sg.shape[0]
+    A = As + E * W
+    dev = eg.device
+    t = {"sg": sg, "su": su, "eg": _c(eg), "eu": _c(eu), "sd": sd, "ed": _c(ed),
+         "gu": torch.empty(2 * A, H, device=dev, dtype=torch.bfloat16),
+         "down": torch.empty(H, A, device=dev, dtype=torch.bfloat16)}
+    if As:
+        t.update(sg=_c(sg), su=_c(su), sd=_c(sd))
+    _run_jobs(_trhash_pack_geometry(As, E, H, W, block), t, reverse=False)
+    return t["gu"], t["down"]
+
+
+class PackTRHashFn(torch.autograd.Function):
+    """Differentiable ``pack_trhash_weights``: one launch each way."""
+
+    @staticmethod
+    def forward(ctx, sg, su, eg, eu, sd, ed):
+        ctx.geom = (0 if sg is None else sg.shape[0], *eg.shape)
+        return pack_trhash_weights(sg, su, eg, eu, sd, ed)
+
+    @staticmethod
+    def backward(ctx, d_gu, d_down):
+        return _unpack_trhash_grads(ctx.geom, _c(d_gu), _c(d_down))
+
+
+def _unpack_trhash_grads(geom, d_gu, d_down):
+    """(d shared_gate, d shared_up, d expert_gate, d expert_up, d shared_down,
+    d expert_down) in bf16 from packed gradients (fp32 or bf16)."""
+    As, E, H, W = geom
+    dev = d_gu.device
+    bf = torch.bfloat16
+    t = {"gu": d_gu, "down": d_down,
+         "eg": torch.empty(E, H, W, device=dev, dtype=bf),
+         "eu": torch.empty(E, H, W, device=dev, dtype=bf),
+         "ed": torch.empty(E, W, H, device=dev, dtype=bf)}
+    if As:
+        t.update(sg=torch.empty(As, H, device=dev, dtype=bf),
+                 su=torch.empty(As, H, device=dev, dtype=bf),
+                 sd=torch.empty(H, As, device=dev, dtype=bf))
+    _run_jobs(_trhash_pack_geometry(As, E, H, W), t, reverse=True)
+    return t.get("sg"), t.get("su"), t["eg"], t["eu"], t.get("sd"), t["ed"]
+
+
+def packable(sg, eg, block: int = 128) -> bool:
+    """Whether the copy-jobs packing applies (shared width a multiple of ``block``;
+    ``CFB_FUSED_PACK=0`` selects the torch packing ops instead)."""
+    if os.environ.get("CFB_FUSED_PACK", "1") == "0":
+        return False
+    As = 0 if sg is None else sg.shape[0]
+    E, H, W = eg.shape
+    return As % block == 0 and (As + E * W) % block == 0
+
+
+def _trhash_forward(ctx, h, w_gu, w_down, row_scale, residual, shared_width, expert_width,
+                    n_experts, shared_scale):
+    C = require()
+    shape = h.shape
+    h2 = _c(h.reshape(-1, shape[-1]))
+    T, H = h2.shape
+    A2 = w_gu.shape[0]
+    A = A2 // 2
+    gu = torch.empty(T, A2, device=h.device, dtype=torch.bfloat16)
+    act = torch.empty(T, A, device=h.device, dtype=torch.bfloat16)
+    C.gemm(h2, False, w_gu, False, T, A2, H, EPI_SWIGLU_FWD, gu=gu, act=act,
+           row_scale=row_scale, shared_width=shared_width, expert_width=expert_width,
+           n_experts=n_experts, shared_scale=shared_scale)
+    Hout = w_down.shape[0]
+    r2 = None if residual is None else residual.reshape(-1, Hout)
+    out = gemm_nt(act, w_down, r2)
+    ctx.save_for_backward(h2, w_gu, w_down, row_scale, gu, act)
+    ctx.meta = (shared_width, expert_width, n_experts, shared_scale)
+    ctx.has_res = residual is not None
+    ctx.shape = shape
+    return out.view(*shape[:-1], Hout)
+
+
+def _trhash_backward(ctx, dout, wgrad_dtype):
+    C = require()
+    h2, w_gu, w_down, row_scale, gu, act = ctx.saved_tensors
+    sw, ew, ne, ss = ctx.meta
+    T, H = h2.shape
+    Hout, A = w_down.shape
+    d2 = _c(dout.reshape(-1, Hout))
+    dw_down = gemm_tn(d2, act, out_dtype=wgrad_dtype)
+    dgu = torch.empty(T, 2 * A, device=d2.device, dtype=torch.bfloat16)
+    C.gemm(d2, False, w_down, True, T, A, Hout, EPI_SWIGLU_BWD, out=dgu, gu=gu,
+           row_scale=row_scale, shared_width=sw, expert_width=ew, n_experts=ne,
+           shared_scale=ss)
+    dh = gemm_nn(dgu, w_gu).view(ctx.shape)
+    dw_gu = gemm_tn(dgu, h2, out_dtype=wgrad_dtype)
+    dr = dout if ctx.has_res else None
+    return dh, dw_gu, dw_down, dr
+
+
 class TRHashMLPFn(torch.autograd.Function):
     """Shared SwiGLU + deterministic routed experts (+ residual) as two GEMMs.
 
@@ -157,51 +300,51 @@ class TRHashMLPFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, h, w_gu, w_down, row_scale, residual, shared_width, expert_width,
                 n_experts, shared_scale):
-        C = require()
-        shape = h.shape
-        h2 = _c(h.reshape(-1, shape[-1]))
-        T, H = h2.shape
-        A2 = w_gu.shape[0]
-        A = A2 // 2
-        w_gu = _c(w_gu)
-        w_down = _c(w_down)
-        gu = torch.empty(T, A2, device=h.device, dtype=torch.bfloat16)
-        act = torch.empty(T, A, device=h.device, dtype=torch.bfloat16)
-        C.gemm(h2, False, w_gu, False, T, A2, H, EPI_SWIGLU_FWD, gu=gu, act=act,
-               row_scale=row_scale, shared_width=shared_width, expert_width=expert_width,
-               n_experts=n_experts, shared_scale=shared_scale)
-        Hout = w_down.shape[0]
-        r2 = None if residual is None else residual.reshape(-1, Hout)
-        out = gemm_nt(act, w_down, r2)
-        ctx.save_for_backward(h2, w_gu, w_down, row_scale, gu, act)
-        ctx.meta = (shared_width, expert_width, n_experts, shared_scale)
-        ctx.has_res = residual is not None
-        ctx.shape = shape
-        return out.view(*shape[:-1], Hout)
+        return _trhash_forward(ctx, h, _c(w_gu), _c(w_down), row_scale, residual, shared_width,
+                               expert_width, n_experts, shared_scale)
 
     @staticmethod
     def backward(ctx, dout):
-        C = require()
-        h2, w_gu, w_down, row_scale, gu, act = ctx.saved_tensors
-        sw, ew, ne, ss = ctx.meta
-        T, H = h2.shape
-        Hout, A = w_down.shape
-        d2 = _c(dout.reshape(-1, Hout))
-        dw_down = gemm_tn(d2, act)
-        dgu = torch.empty(T, 2 * A, device=d2.device, dtype=torch.bfloat16)
-        C.gemm(d2, False, w_down, True, T, A, Hout, EPI_SWIGLU_BWD, out=dgu, gu=gu,
-               row_scale=row_scale, shared_width=sw, expert_width=ew, n_experts=ne,
-               shared_scale=ss)
-        dh = gemm_nn(dgu, w_gu).view(ctx.shape)
-        dw_gu = gemm_tn(dgu, h2)
-        dr = dout if ctx.has_res else None
+        dh, dw_gu, dw_down, dr = _trhash_backward(ctx, dout, torch.bfloat16)
         return dh, dw_gu, dw_down, None, dr, None, None, None, None
+
+
+class TRHashMLPParamsFn(torch.autograd.Function):
+    """``TRHashMLPFn`` over the unpacked parameters.
+
+    The packed gate|up and down weights are built by one copy-jobs launch
+    per forward, and the fp32 weight gradients (split-K atomics) are cast and
+    scattered back to the six parameters by one launch in backward, instead of
+    torch cat/stack/permute/cast kernels and their autograd inverses.
+    """
+
+    @staticmethod
+    def forward(ctx, h, sg, su, eg, eu, sd, ed, row_scale, residual, shared_width,
+                expert_width, n_experts, shared_scale):
+        w_gu, w_down = pack_trhash_weights(sg, su, eg, eu, sd, ed)
+        ctx.geom = (0 if sg is None else sg.shape[0], *eg.shape)
+        return _trhash_forward(ctx, h, w_gu, w_down, row_scale, residual, shared_width,
+                               expert_width, n_experts, shared_scale)
+
+    @staticmethod
+    def backward(ctx, dout):
+        dh, dw_gu, dw_down, dr = _trhash_backward(ctx, dout, torch.float32)
+        dsg, dsu, deg, deu, dsd, ded = _unpack_trhash_grads(ctx.geom, dw_gu, dw_down)
+        n = None
+        return dh, dsg, dsu, deg, deu, dsd, ded, n, dr, n, n, n, n
 
 
 def trhash_mlp(h, w_gu, w_down, row_scale, residual, shared_width, expert_width, n_experts,
                shared_scale):
     return TRHashMLPFn.apply(h, w_gu, w_down, row_scale, residual, shared_width, expert_width,
                              n_experts, shared_scale)
+
+
+def trhash_mlp_params(h, sg, su, eg, eu, sd, ed, row_scale, residual, shared_width,
+                      expert_width, n_experts, shared_scale):
+    """TR-Hash MLP from the module's own parameters (shared ones may be None)."""
+    return TRHashMLPParamsFn.apply(h, sg, su, eg, eu, sd, ed, row_scale, residual,
+                                   shared_width, expert_width, n_experts, shared_scale)
 
 
 def route_scales(token_ids: torch.Tensor, route_table: torch.Tensor, route_weights: torch.Tensor,

@@ -243,16 +243,23 @@ class TRHashEngine(nn.Module):
 
     def packed_weights(self):
         """(gate|up interleaved [2A, H], down [H, A]) for the fused path (autograd-tracked)."""
+        from ..ops import fused
         from ..ops.fused import pack_down, pack_gate_up
 
         if any(getattr(m, "is_lora_adapter", False)
                for m in (self.shared_gate, self.shared_up, self.shared_down) if m is not None):
             raise RuntimeError("fused path does not execute LoRA-adapted shared projections")
-        wg = None if self.shared_gate is None else self.shared_gate.weight
-        wu = None if self.shared_up is None else self.shared_up.weight
-        wd = None if self.shared_down is None else self.shared_down.weight
+        wg, wu, wd = self._shared_weights()
+        if fused.packable(wg, self.expert_gate):
+            return fused.PackTRHashFn.apply(wg, wu, self.expert_gate, self.expert_up, wd,
+                                            self.expert_down)
         return (pack_gate_up(wg, wu, self.expert_gate, self.expert_up),
                 pack_down(wd, self.expert_down))
+
+    def _shared_weights(self):
+        if self.shared_gate is None:
+            return None, None, None
+        return self.shared_gate.weight, self.shared_up.weight, self.shared_down.weight
 
     def _fused_forward(self, hidden: torch.Tensor, token_ids: torch.Tensor,
                        residual: Optional[torch.Tensor]) -> torch.Tensor:
@@ -268,6 +275,15 @@ class TRHashEngine(nn.Module):
         scales = fused.route_scales(token_ids, self._active_route_table,
                                     self._route_weights, cfg.num_experts,
                                     cfg.routed_output_scale)
+        wg, wu, wd = self._shared_weights()
+        if (fused.packable(wg, self.expert_gate) and not any(
+                getattr(m, "is_lora_adapter", False)
+                for m in (self.shared_gate, self.shared_up, self.shared_down) if m is not None)):
+            # packing and gradient unpacking fused into the MLP's own autograd node
+            return fused.trhash_mlp_params(hidden, wg, wu, self.expert_gate, self.expert_up, wd,
+                                           self.expert_down, scales, residual, cfg.shared_width,
+                                           cfg.expert_width, cfg.num_experts,
+                                           cfg.shared_output_scale)
         w_gu, w_down = self.packed_weights()
         return fused.trhash_mlp(hidden, w_gu, w_down, scales, residual, cfg.shared_width,
                                 cfg.expert_width, cfg.num_experts, cfg.shared_output_scale)

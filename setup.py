@@ -22,6 +22,7 @@ SOURCES = [
     "noalloc.cu",
     "tp_fused.cu",
     "ep_fused.cu",
+    "pack.cu",
 ]
 
 NVCC_FLAGS = [

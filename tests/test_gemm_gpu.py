@@ -131,3 +131,56 @@ def test_gemm_split_k_atomic(M, N, K):
     C.gemm(A, True, B, True, M, N, K, 7, out=out)
     torch.cuda.synchronize()
     _check(out, ref, 1e-3)
+
+
+@pytest.mark.parametrize("As,E,W", [(384, 4, 64), (0, 4, 64), (256, 2, 128)])
+def test_copy_jobs_pack_unpack(As, E, W):
+    """One-launch packing of the TR-Hash MLP weights equals the torch packing,
+    and the unpack jobs invert it (fp32 gradients cast to bf16)."""
+    from complexity_framework_b200.ops import fused
+
+    torch.manual_seed(0)
+    H = 192
+    dev = "cuda"
+    rnd = lambda *s: torch.randn(*s, device=dev).bfloat16()  # noqa: E731
+    sg, su, sd = (rnd(As, H), rnd(As, H), rnd(H, As)) if As else (None, None, None)
+    eg, eu, ed = rnd(E, H, W), rnd(E, H, W), rnd(E, W, H)
+    gu, down = fused.pack_trhash_weights(sg, su, eg, eu, sd, ed)
+    assert torch.equal(gu, fused.pack_gate_up(sg, su, eg, eu))
+    assert torch.equal(down, fused.pack_down(sd, ed))
+    d_gu = torch.randn(gu.shape, device=dev)
+    d_down = torch.randn(down.shape, device=dev)
+    got = fused._unpack_trhash_grads((As, E, H, W), d_gu, d_down)
+    ref_in = [t.float().requires_grad_() if t is not None else None
+              for t in (sg, su, eg, eu, sd, ed)]
+    rg, rd = fused.pack_gate_up(*ref_in[:4]), fused.pack_down(ref_in[4], ref_in[5])
+    torch.autograd.backward([rg, rd], [d_gu, d_down])
+    for g, r in zip(got, ref_in):
+        if r is None:
+            assert g is None
+        else:
+            assert torch.equal(g, r.grad.bfloat16())
+
+
+def test_trhash_mlp_params_matches_packed():
+    from complexity_framework_b200.ops import fused
+
+    torch.manual_seed(1)
+    T, H, As, E, W = 512, 256, 256, 4, 64
+    dev = "cuda"
+    mk = lambda *s: (0.05 * torch.randn(*s, device=dev)).bfloat16().requires_grad_()  # noqa: E731
+    params = [mk(As, H), mk(As, H), mk(E, H, W), mk(E, H, W), mk(H, As), mk(E, W, H)]
+    x = torch.randn(T, H, device=dev).bfloat16().requires_grad_()
+    scales = torch.rand(T, E, device=dev)
+    y1 = fused.trhash_mlp_params(x, *params, scales, None, As, W, E, 1.0)
+    g = torch.randn_like(y1)
+    grads1 = torch.autograd.grad(y1, [x, *params], g)
+    gu = fused.pack_gate_up(*params[:4])
+    dn = fused.pack_down(params[4], params[5])
+    y2 = fused.trhash_mlp(x, gu, dn, scales, None, As, W, E, 1.0)
+    grads2 = torch.autograd.grad(y2, [x, *params], g)
+    assert torch.equal(y1, y2)
+    for a, b in zip(grads1, grads2):
+        # same GEMMs; the packed path rounds the weight gradient to bf16 before
+        # the autograd scatter, this one after the fp32 split-K sum
+        assert float((a.float() - b.float()).abs().max()) <= 1e-2 * float(b.abs().max()) + 1e-6
