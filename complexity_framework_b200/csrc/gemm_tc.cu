@@ -990,7 +990,12 @@ int gemm_tc_launch(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream, in
     return gemm_tc_launch_dist(g, ep, stream, err);
   int bn = g.bn;
   if (g.epi == EPI_SWIGLU_FWD) bn = 2 * kSwigluBlock;
-  if (bn == 0) bn = choose_bn(g.M, g.N, g.num_sms);
+  if (bn == 0) {
+    bn = choose_bn(g.M, g.N, g.num_sms);
+    // split-K weight gradients with N an odd multiple of 128 (896, 1152 here):
+    // 128-column tiles leave no half-empty tile and measured 6-17% faster
+    if (g.epi == EPI_F32_ATOMIC && g.N % 256 != 0 && g.N % 128 == 0) bn = 128;
+  }
   if (bn != 128 && bn != 256) return -3;
   SegMaps<1> ta, tb;
   ta.seg_rows = tb.seg_rows = 0;

@@ -6,7 +6,7 @@
 // torch copy/cat/stack/permute/cast kernels per layer and direction.  One
 // launch here runs up to kMaxCopyJobs jobs, each an R x C copy whose row index
 // may split into (r / div, r % div) parts with their own strides: that covers
-// the block interleave and the expert transposes.  Tiles of 32 x 32 go
+// the block interleave and the expert transposes.  Tiles of 64 x 64 go
 // through shared memory so both the reads and the writes run along the unit
 // stride of their side.
 //
@@ -18,7 +18,7 @@
 namespace cfb {
 namespace {
 
-constexpr int kTile = 32;
+constexpr int kTile = 64;  // transpose tiles: 64 x 64, 16 elements per thread
 
 __device__ __forceinline__ int64_t row_off(int r, int div, int64_t hi, int64_t lo) {
   return (int64_t)(r / div) * hi + (int64_t)(r % div) * lo;
@@ -83,28 +83,34 @@ __global__ void __launch_bounds__(256) copy_jobs_k(CopyJobs jobs) {
   const int tiles_c = (J.cols + kTile - 1) / kTile;
   const int tiles = ((J.rows + kTile - 1) / kTile) * tiles_c;
   __shared__ float tile[kTile][kTile + 1];
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
+  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;  // 64 x 4 threads
+  constexpr int kPer = kTile / 4;
+  const bool src_cols = J.s_cs <= J.s_lo;  // lanes run along the smaller stride
+  const bool dst_cols = J.d_cs <= J.d_lo;
   for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int r0 = (t / tiles_c) * kTile, c0 = (t % tiles_c) * kTile;
-    // load: lanes run along the source's smaller stride
-    const bool src_cols = J.s_cs <= J.s_lo;
+    float v[kPer];
 #pragma unroll
-    for (int i = 0; i < kTile / 8; ++i) {
-      const int a = ty + 8 * i;
+    for (int i = 0; i < kPer; ++i) {  // all loads first
+      const int a = ty + 4 * i;
       const int r = r0 + (src_cols ? a : tx), c = c0 + (src_cols ? tx : a);
-      float v = 0.f;
+      v[i] = 0.f;
       if (r < J.rows && c < J.cols) {
         const int64_t o = row_off(r, J.s_div, J.s_hi, J.s_lo) + (int64_t)c * J.s_cs;
-        v = J.src_f32 ? static_cast<const float*>(J.src)[o]
-                      : __bfloat162float(static_cast<const bf16*>(J.src)[o]);
+        v[i] = J.src_f32 ? static_cast<const float*>(J.src)[o]
+                         : __bfloat162float(static_cast<const bf16*>(J.src)[o]);
       }
-      tile[r - r0][c - c0] = v;
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int a = ty + 4 * i;
+      if (src_cols) tile[a][tx] = v[i];
+      else tile[tx][a] = v[i];
     }
     __syncthreads();
-    const bool dst_cols = J.d_cs <= J.d_lo;
 #pragma unroll
-    for (int i = 0; i < kTile / 8; ++i) {
-      const int a = ty + 8 * i;
+    for (int i = 0; i < kPer; ++i) {
+      const int a = ty + 4 * i;
       const int r = r0 + (dst_cols ? a : tx), c = c0 + (dst_cols ? tx : a);
       if (r < J.rows && c < J.cols)
         J.dst[row_off(r, J.d_div, J.d_hi, J.d_lo) + (int64_t)c * J.d_cs] =

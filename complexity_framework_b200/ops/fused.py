@@ -217,9 +217,10 @@ class PackTRHashFn(torch.autograd.Function):
         return _unpack_trhash_grads(ctx.geom, _c(d_gu), _c(d_down))
 
 
-def _unpack_trhash_grads(geom, d_gu, d_down):
+def _unpack_trhash_grads(geom, d_gu, d_down, down_transposed: bool = False):
     """(d shared_gate, d shared_up, d expert_gate, d expert_up, d shared_down,
-    d expert_down) in bf16 from packed gradients (fp32 or bf16)."""
+    d expert_down) in bf16 from packed gradients (fp32 or bf16).  With
+    ``down_transposed`` the down gradient arrives as ``[A, H]`` (its transpose)."""
     As, E, H, W = geom
     dev = d_gu.device
     bf = torch.bfloat16
@@ -231,7 +232,27 @@ def _unpack_trhash_grads(geom, d_gu, d_down):
         t.update(sg=torch.empty(As, H, device=dev, dtype=bf),
                  su=torch.empty(As, H, device=dev, dtype=bf),
                  sd=torch.empty(H, As, device=dev, dtype=bf))
-    _run_jobs(_trhash_pack_geometry(As, E, H, W), t, reverse=True)
+    jobs = _trhash_pack_geometry(As, E, H, W)
+    if not down_transposed:
+        _run_jobs(jobs, t, reverse=True)
+    else:
+        C = require()
+        gu_jobs = [j for j in jobs if j[1] == "gu"]
+        srcs, dsts, geo = [], [], []
+        for name, packed, rows, cols, sg, off, pg in gu_jobs:
+            srcs.append(d_gu.reshape(-1)[off:])
+            dsts.append(t[name].reshape(-1))
+            geo += [rows, cols, *pg, *sg]
+        dT = d_down.reshape(-1)
+        if As:  # sd[h, c] = dT[c, h]
+            srcs.append(dT)
+            dsts.append(t["sd"].reshape(-1))
+            geo += [H, As, _NO_SPLIT, 0, 1, H, _NO_SPLIT, 0, As, 1]
+        # ed[e, w, h] = dT[As + e * W + w, h]: plain rows
+        srcs.append(dT[As * H:])
+        dsts.append(t["ed"].reshape(-1))
+        geo += [E * W, H, _NO_SPLIT, 0, H, 1, _NO_SPLIT, 0, H, 1]
+        C.copy_jobs(srcs, dsts, geo)
     return t.get("sg"), t.get("su"), t["eg"], t["eu"], t.get("sd"), t["ed"]
 
 
@@ -268,14 +289,18 @@ def _trhash_forward(ctx, h, w_gu, w_down, row_scale, residual, shared_width, exp
     return out.view(*shape[:-1], Hout)
 
 
-def _trhash_backward(ctx, dout, wgrad_dtype):
+def _trhash_backward(ctx, dout, wgrad_dtype, down_transposed: bool = False):
+    """(dh, dw_gu, dw_down, d residual); with ``down_transposed`` dw_down is
+    returned as ``[A, Hout]``: the 3328 x 896 split-K product tiles better than
+    its 896 x 3328 transpose."""
     C = require()
     h2, w_gu, w_down, row_scale, gu, act = ctx.saved_tensors
     sw, ew, ne, ss = ctx.meta
     T, H = h2.shape
     Hout, A = w_down.shape
     d2 = _c(dout.reshape(-1, Hout))
-    dw_down = gemm_tn(d2, act, out_dtype=wgrad_dtype)
+    dw_down = (gemm_tn(act, d2, out_dtype=wgrad_dtype) if down_transposed
+               else gemm_tn(d2, act, out_dtype=wgrad_dtype))
     dgu = torch.empty(T, 2 * A, device=d2.device, dtype=torch.bfloat16)
     C.gemm(d2, False, w_down, True, T, A, Hout, EPI_SWIGLU_BWD, out=dgu, gu=gu,
            row_scale=row_scale, shared_width=sw, expert_width=ew, n_experts=ne,
@@ -328,8 +353,9 @@ class TRHashMLPParamsFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dout):
-        dh, dw_gu, dw_down, dr = _trhash_backward(ctx, dout, torch.float32)
-        dsg, dsu, deg, deu, dsd, ded = _unpack_trhash_grads(ctx.geom, dw_gu, dw_down)
+        dh, dw_gu, dw_down, dr = _trhash_backward(ctx, dout, torch.float32, down_transposed=True)
+        dsg, dsu, deg, deu, dsd, ded = _unpack_trhash_grads(ctx.geom, dw_gu, dw_down,
+                                                            down_transposed=True)
         n = None
         return dh, dsg, dsu, deg, deu, dsd, ded, n, dr, n, n, n, n
 

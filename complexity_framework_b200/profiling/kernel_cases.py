@@ -67,6 +67,33 @@ def case_gemm(iters: int) -> None:
     check_errors(0)
 
 
+def case_gemm_bn(iters: int) -> None:
+    """128- vs 256-column tiles on the TR-Hash 200M step's narrow GEMMs (N = 896 or 1152)."""
+    C = require()
+    T, H, A, KQV = 32768, 896, 3328, 1152
+    dev = "cuda"
+    r = lambda *s: (torch.randn(*s, device=dev) * 0.05).bfloat16()  # noqa: E731
+    x, xk, act, dgu = r(T, H), r(T, KQV), r(T, A), r(T, 2 * A)
+    wk, wd, wgu = r(KQV, H), r(H, A), r(2 * A, H)
+    cases = [  # name, A, a_mn, B, b_mn, M, N, K, epi, out shape, out dtype
+        ("fwd_kqv", x, False, wk, False, T, KQV, H, 0, (T, KQV), torch.bfloat16),
+        ("fwd_down", act, False, wd, False, T, H, A, 0, (T, H), torch.bfloat16),
+        ("dgrad_kqv", xk, False, wk, True, T, H, KQV, 0, (T, H), torch.bfloat16),
+        ("dgrad_gu", dgu, False, wgu, True, T, H, 2 * A, 0, (T, H), torch.bfloat16),
+        ("wgrad_gu", dgu, True, x, True, 2 * A, H, T, 7, (2 * A, H), torch.float32),
+        ("wgrad_down", x, True, act, True, H, A, T, 7, (H, A), torch.float32),
+        ("wgrad_kqv", xk, True, x, True, KQV, H, T, 7, (KQV, H), torch.float32),
+    ]
+    for name, a, amn, b, bmn, M, N, K, epi, oshape, odt in cases:
+        out = torch.zeros(oshape, device=dev, dtype=odt)
+        for bn in (128, 256):
+            _report(f"{name}_bn{bn}", cuda_time(
+                lambda: C.gemm(a, amn, b, bmn, M, N, K, epi, out=out, bn=bn), iters),
+                2.0 * M * N * K)
+    torch.cuda.synchronize()
+    check_errors(0)
+
+
 def case_flash(iters: int) -> None:
     from ..ops.flash import flash_forward
 
@@ -118,7 +145,7 @@ def case_norms(iters: int) -> None:
     check_errors(0)
 
 
-CASES = {"gemm": case_gemm, "flash": case_flash, "norms": case_norms}
+CASES = {"gemm": case_gemm, "gemm_bn": case_gemm_bn, "flash": case_flash, "norms": case_norms}
 
 
 def main(argv=None) -> None:

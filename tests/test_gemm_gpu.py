@@ -151,6 +151,10 @@ def test_copy_jobs_pack_unpack(As, E, W):
     d_gu = torch.randn(gu.shape, device=dev)
     d_down = torch.randn(down.shape, device=dev)
     got = fused._unpack_trhash_grads((As, E, H, W), d_gu, d_down)
+    got_t = fused._unpack_trhash_grads((As, E, H, W), d_gu, d_down.t().contiguous(),
+                                       down_transposed=True)
+    for a, b in zip(got, got_t):
+        assert (a is None and b is None) or torch.equal(a, b)
     ref_in = [t.float().requires_grad_() if t is not None else None
               for t in (sg, su, eg, eu, sd, ed)]
     rg, rd = fused.pack_gate_up(*ref_in[:4]), fused.pack_down(ref_in[4], ref_in[5])
