@@ -73,7 +73,8 @@ struct CopyJob {
   int64_t s_hi = 0, s_lo = 0, s_cs = 1;
   int64_t d_hi = 0, d_lo = 0, d_cs = 1;
   int src_f32 = 0;
-  int vec = 0;  // set by copy_jobs: unit column strides and 16-byte aligned rows
+  int vec = 0;        // set by copy_jobs: unit column strides and 16-byte aligned rows
+  int64_t unit0 = 0;  // set by copy_jobs: first work unit of this job
 };
 struct CopyJobs {
   CopyJob j[kMaxCopyJobs];

@@ -24,99 +24,94 @@ __device__ __forceinline__ int64_t row_off(int r, int div, int64_t hi, int64_t l
   return (int64_t)(r / div) * hi + (int64_t)(r % div) * lo;
 }
 
-// Row copies with unit column stride on both sides: 8 elements per item,
-// 4 items per thread in flight.
-__device__ void copy_rows_vec(const CopyJob& J) {
+constexpr int kVecPerThread = 8;                    // 8-element vectors per thread per unit
+constexpr int kVecUnit = 256 * kVecPerThread;        // vectors per work unit
+
+// Row copies with unit column stride on both sides: one work unit is
+// kVecUnit 8-element vectors, all loads issued before the stores (values held
+// as packed bf16).
+__device__ void copy_vec_unit(const CopyJob& J, int64_t unit) {
   const int vpr = J.cols / 8;  // vectors per row
   const int64_t items = (int64_t)J.rows * vpr;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < items;
-       base += 4 * stride) {
-    float v[4][8];
-    int64_t dst_o[4];
-    bool ok[4];
+  uint4 q[kVecPerThread];
+  int64_t dst_o[kVecPerThread];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int64_t it = base + u * stride;
-      ok[u] = it < items;
-      const int r = ok[u] ? static_cast<int>(it / vpr) : 0;
-      const int c = ok[u] ? static_cast<int>(it % vpr) * 8 : 0;
+  for (int k = 0; k < kVecPerThread; ++k) {
+    const int64_t it = unit * kVecUnit + k * 256 + threadIdx.x;
+    dst_o[k] = -1;
+    if (it < items) {
+      const int r = static_cast<int>(it / vpr);
+      const int c = static_cast<int>(it - (int64_t)r * vpr) * 8;
       const int64_t so = row_off(r, J.s_div, J.s_hi, J.s_lo) + c;
-      dst_o[u] = row_off(r, J.d_div, J.d_hi, J.d_lo) + c;
+      dst_o[k] = row_off(r, J.d_div, J.d_hi, J.d_lo) + c;
       if (J.src_f32) {
-        const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(J.src) + so);
-        const float4 b =
-            *reinterpret_cast<const float4*>(static_cast<const float*>(J.src) + so + 4);
-        v[u][0] = a.x; v[u][1] = a.y; v[u][2] = a.z; v[u][3] = a.w;
-        v[u][4] = b.x; v[u][5] = b.y; v[u][6] = b.z; v[u][7] = b.w;
+        const float* f = static_cast<const float*>(J.src) + so;
+        const float4 a = *reinterpret_cast<const float4*>(f);
+        const float4 b = *reinterpret_cast<const float4*>(f + 4);
+        q[k].x = pack_bf16x2(a.x, a.y);
+        q[k].y = pack_bf16x2(a.z, a.w);
+        q[k].z = pack_bf16x2(b.x, b.y);
+        q[k].w = pack_bf16x2(b.z, b.w);
       } else {
-        const uint4 q = *reinterpret_cast<const uint4*>(static_cast<const bf16*>(J.src) + so);
-        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float2 f = unpack_bf16x2(w[k]);
-          v[u][2 * k] = f.x;
-          v[u][2 * k + 1] = f.y;
-        }
+        q[k] = *reinterpret_cast<const uint4*>(static_cast<const bf16*>(J.src) + so);
       }
     }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      if (!ok[u]) continue;
-      uint4 q;
-      q.x = pack_bf16x2(v[u][0], v[u][1]);
-      q.y = pack_bf16x2(v[u][2], v[u][3]);
-      q.z = pack_bf16x2(v[u][4], v[u][5]);
-      q.w = pack_bf16x2(v[u][6], v[u][7]);
-      *reinterpret_cast<uint4*>(J.dst + dst_o[u]) = q;
-    }
   }
+#pragma unroll
+  for (int k = 0; k < kVecPerThread; ++k)
+    if (dst_o[k] >= 0) *reinterpret_cast<uint4*>(J.dst + dst_o[k]) = q[k];
 }
 
-__global__ void __launch_bounds__(256) copy_jobs_k(CopyJobs jobs) {
-  if (blockIdx.y >= (unsigned)jobs.n) return;
-  const CopyJob& J = jobs.j[blockIdx.y];
-  if (J.vec) {
-    copy_rows_vec(J);
-    return;
-  }
+// Strided (transposing) copies: one work unit is one 64 x 64 tile through
+// shared memory, both sides accessed along their smaller stride.
+__device__ void copy_tile_unit(const CopyJob& J, int64_t unit, float (*tile)[kTile + 1]) {
   const int tiles_c = (J.cols + kTile - 1) / kTile;
-  const int tiles = ((J.rows + kTile - 1) / kTile) * tiles_c;
-  __shared__ float tile[kTile][kTile + 1];
   const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;  // 64 x 4 threads
   constexpr int kPer = kTile / 4;
-  const bool src_cols = J.s_cs <= J.s_lo;  // lanes run along the smaller stride
+  const bool src_cols = J.s_cs <= J.s_lo;
   const bool dst_cols = J.d_cs <= J.d_lo;
-  for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-    const int r0 = (t / tiles_c) * kTile, c0 = (t % tiles_c) * kTile;
-    float v[kPer];
+  const int r0 = static_cast<int>(unit / tiles_c) * kTile;
+  const int c0 = static_cast<int>(unit % tiles_c) * kTile;
+  float v[kPer];
 #pragma unroll
-    for (int i = 0; i < kPer; ++i) {  // all loads first
-      const int a = ty + 4 * i;
-      const int r = r0 + (src_cols ? a : tx), c = c0 + (src_cols ? tx : a);
-      v[i] = 0.f;
-      if (r < J.rows && c < J.cols) {
-        const int64_t o = row_off(r, J.s_div, J.s_hi, J.s_lo) + (int64_t)c * J.s_cs;
-        v[i] = J.src_f32 ? static_cast<const float*>(J.src)[o]
-                         : __bfloat162float(static_cast<const bf16*>(J.src)[o]);
-      }
+  for (int i = 0; i < kPer; ++i) {  // all loads first
+    const int a = ty + 4 * i;
+    const int r = r0 + (src_cols ? a : tx), c = c0 + (src_cols ? tx : a);
+    v[i] = 0.f;
+    if (r < J.rows && c < J.cols) {
+      const int64_t o = row_off(r, J.s_div, J.s_hi, J.s_lo) + (int64_t)c * J.s_cs;
+      v[i] = J.src_f32 ? static_cast<const float*>(J.src)[o]
+                       : __bfloat162float(static_cast<const bf16*>(J.src)[o]);
     }
+  }
 #pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int a = ty + 4 * i;
-      if (src_cols) tile[a][tx] = v[i];
-      else tile[tx][a] = v[i];
-    }
-    __syncthreads();
+  for (int i = 0; i < kPer; ++i) {
+    const int a = ty + 4 * i;
+    if (src_cols) tile[a][tx] = v[i];
+    else tile[tx][a] = v[i];
+  }
+  __syncthreads();
 #pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int a = ty + 4 * i;
-      const int r = r0 + (dst_cols ? a : tx), c = c0 + (dst_cols ? tx : a);
-      if (r < J.rows && c < J.cols)
-        J.dst[row_off(r, J.d_div, J.d_hi, J.d_lo) + (int64_t)c * J.d_cs] =
-            __float2bfloat16(tile[r - r0][c - c0]);
-    }
-    __syncthreads();
+  for (int i = 0; i < kPer; ++i) {
+    const int a = ty + 4 * i;
+    const int r = r0 + (dst_cols ? a : tx), c = c0 + (dst_cols ? tx : a);
+    if (r < J.rows && c < J.cols)
+      J.dst[row_off(r, J.d_div, J.d_hi, J.d_lo) + (int64_t)c * J.d_cs] =
+          __float2bfloat16(tile[r - r0][c - c0]);
+  }
+  __syncthreads();
+}
+
+// All jobs' work units form one flat range [0, total); block b takes units
+// b, b + gridDim.x, ...  Job i owns units [unit0[i], unit0[i + 1]).
+__global__ void __launch_bounds__(256, 4) copy_jobs_k(CopyJobs jobs, int64_t total) {
+  __shared__ float tile[kTile][kTile + 1];
+  for (int64_t u = blockIdx.x; u < total; u += gridDim.x) {
+    int j = 0;
+    while (j + 1 < jobs.n && u >= jobs.j[j + 1].unit0) ++j;
+    const CopyJob& J = jobs.j[j];
+    if (J.vec) copy_vec_unit(J, u - J.unit0);
+    else copy_tile_unit(J, u - J.unit0, tile);  // uniform per block: barriers are safe
   }
 }
 
@@ -124,19 +119,20 @@ __global__ void __launch_bounds__(256) copy_jobs_k(CopyJobs jobs) {
 
 void copy_jobs(const CopyJobs& jobs_in, cudaStream_t s) {
   CopyJobs jobs = jobs_in;
-  int64_t max_blocks = 1;
+  int64_t total = 0;
   for (int i = 0; i < jobs.n; ++i) {
     CopyJob& J = jobs.j[i];
     // vector path: unit column strides, 8-element aligned rows and bases
-    const uintptr_t sa = reinterpret_cast<uintptr_t>(J.src), da = reinterpret_cast<uintptr_t>(J.dst);
+    const uintptr_t sa = reinterpret_cast<uintptr_t>(J.src);
+    const uintptr_t da = reinterpret_cast<uintptr_t>(J.dst);
     J.vec = J.s_cs == 1 && J.d_cs == 1 && J.cols % 8 == 0 && J.s_hi % 8 == 0 && J.s_lo % 8 == 0 &&
-            J.d_hi % 8 == 0 && J.d_lo % 8 == 0 && sa % (J.src_f32 ? 32 : 16) == 0 && da % 16 == 0;
-    const int64_t b = J.vec ? ((int64_t)J.rows * (J.cols / 8) + 1023) / 1024
-                            : (int64_t)((J.rows + kTile - 1) / kTile) * ((J.cols + kTile - 1) / kTile);
-    if (b > max_blocks) max_blocks = b;
+            J.d_hi % 8 == 0 && J.d_lo % 8 == 0 && sa % 16 == 0 && da % 16 == 0;
+    J.unit0 = total;
+    total += J.vec ? ((int64_t)J.rows * (J.cols / 8) + kVecUnit - 1) / kVecUnit
+                   : (int64_t)((J.rows + kTile - 1) / kTile) * ((J.cols + kTile - 1) / kTile);
   }
-  const int gx = static_cast<int>(max_blocks < 148 * 8 ? max_blocks : 148 * 8);
-  copy_jobs_k<<<dim3(gx, jobs.n), 256, 0, s>>>(jobs);
+  const int grid = static_cast<int>(total < 148 * 4 ? total : 148 * 4);
+  copy_jobs_k<<<grid, 256, 0, s>>>(jobs, total);
 }
 
 }  // namespace cfb
