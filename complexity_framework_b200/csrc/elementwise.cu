@@ -691,16 +691,233 @@ __global__ void clip_coef_k(const float* sumsq, float max_norm, float* clip, flo
   if (clip != nullptr) *clip = max_norm > 0.f ? fminf(1.f, max_norm / (nrm + 1e-6f)) : 1.f;
 }
 
+// RMSNorm for H <= 1024 with the warp-owned cp.async ring of the QK kernels:
+// a warp streams its rows through NS shared-memory slots (NS-1 rows of loads
+// in flight) and computes from shared memory.  Lane l owns the 8-element
+// vectors l, l+32, ... (NV of them) of a row; in backward its d(weight)
+// partials stay in registers for the whole row loop.
+template <int NV, int NS>
+__global__ void __launch_bounds__(128) rmsnorm_fwd_ring_k(const bf16* __restrict__ x,
+                                                         const bf16* __restrict__ w,
+                                                         bf16* __restrict__ y,
+                                                         float* __restrict__ rstd, int T, int H,
+                                                         float eps) {
+  extern __shared__ __align__(16) unsigned char rn_smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, wpb = blockDim.x >> 5;
+  const int wid = blockIdx.x * wpb + warp, nw = gridDim.x * wpb;
+  const int nv = H / 8;
+  bf16* ring = reinterpret_cast<bf16*>(rn_smem) + (size_t)warp * NS * H;
+  float wv[NV][8];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = lane + 32 * k;
+    if (i < nv) load8(w + i * 8, wv[k]);
+  }
+  auto issue = [&](int it) {
+    const int row = wid + it * nw;
+    if (row < T) {
+      const bf16* src = x + (int64_t)row * H;
+      bf16* dst = ring + (it % NS) * H;
+      for (int i = lane; i < nv; i += 32) cp_async16(dst + i * 8, src + i * 8);
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int it = 0; it < NS - 1; ++it) issue(it);
+  for (int it = 0; wid + it * nw < T; ++it) {
+    issue(it + NS - 1);
+    cp_async_wait<NS - 1>();
+    __syncwarp();
+    const int row = wid + it * nw;
+    const bf16* xr = ring + (it % NS) * H;
+    float v[NV][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int i = lane + 32 * k;
+      if (i < nv) {
+        load8(xr + i * 8, v[k]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += v[k][j] * v[k][j];
+      }
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / H + eps);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int i = lane + 32 * k;
+      if (i < nv) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[k][j] = rb(v[k][j] * r) * wv[k][j];
+        store8(y + (int64_t)row * H + i * 8, v[k]);
+      }
+    }
+    if (lane == 0) rstd[row] = r;
+    __syncwarp();
+  }
+  cp_async_wait<0>();
+}
+
+template <int NV, int NS>
+__global__ void __launch_bounds__(128) rmsnorm_bwd_ring_k(
+    const bf16* __restrict__ dy, const bf16* __restrict__ x, const bf16* __restrict__ w,
+    const float* __restrict__ rstd, const bf16* __restrict__ dres, bf16* __restrict__ dx,
+    float* __restrict__ dw, int T, int H) {
+  extern __shared__ __align__(16) unsigned char rn_smem[];
+  float* sdw = reinterpret_cast<float*>(rn_smem);  // [H] block partials of d(weight)
+  float* sw = sdw + H;                               // [H] weights
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, wpb = blockDim.x >> 5;
+  const int wid = blockIdx.x * wpb + warp, nw = gridDim.x * wpb;
+  const int nv = H / 8;
+  const int rows = dres != nullptr ? 3 : 2;
+  const int slot = rows * H * 2 + 16;  // bytes: dy | x | dres rows, then rstd
+  unsigned char* ring = rn_smem + 2 * H * sizeof(float) + (size_t)warp * NS * slot;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    sdw[i] = 0.f;
+    sw[i] = __bfloat162float(w[i]);
+  }
+  __syncthreads();
+  float acc[NV][8];
+#pragma unroll
+  for (int k = 0; k < NV; ++k)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[k][j] = 0.f;
+  auto wload = [&](int i, float* wv) {
+    const float4 a = *reinterpret_cast<const float4*>(sw + i * 8);
+    const float4 b = *reinterpret_cast<const float4*>(sw + i * 8 + 4);
+    wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w;
+    wv[4] = b.x; wv[5] = b.y; wv[6] = b.z; wv[7] = b.w;
+  };
+  auto issue = [&](int it) {
+    const int row = wid + it * nw;
+    if (row < T) {
+      bf16* dst = reinterpret_cast<bf16*>(ring + (it % NS) * slot);
+      const int64_t o = (int64_t)row * H;
+      for (int i = lane; i < nv; i += 32) {
+        cp_async16(dst + i * 8, dy + o + i * 8);
+        cp_async16(dst + H + i * 8, x + o + i * 8);
+        if (dres != nullptr) cp_async16(dst + 2 * H + i * 8, dres + o + i * 8);
+      }
+      if (lane == 0) cp_async4(dst + rows * H, rstd + row);
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int it = 0; it < NS - 1; ++it) issue(it);
+  for (int it = 0; wid + it * nw < T; ++it) {
+    issue(it + NS - 1);
+    cp_async_wait<NS - 1>();
+    __syncwarp();
+    const int row = wid + it * nw;
+    const bf16* sl = reinterpret_cast<const bf16*>(ring + (it % NS) * slot);
+    const float r = *reinterpret_cast<const float*>(sl + rows * H);
+    float dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int i = lane + 32 * k;
+      if (i < nv) {
+        float xv[8], gv[8], wv[8];
+        load8(sl + H + i * 8, xv);
+        load8(sl + i * 8, gv);
+        wload(i, wv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          dot += gv[j] * wv[j] * xv[j];
+          acc[k][j] += gv[j] * rb(xv[j] * r);
+        }
+      }
+    }
+    dot = warp_sum(dot);
+    const float c = dot * r * r * r / H;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int i = lane + 32 * k;
+      if (i < nv) {
+        float xv[8], gv[8], wv[8], o[8];
+        load8(sl + H + i * 8, xv);
+        load8(sl + i * 8, gv);
+        wload(i, wv);
+        if (dres != nullptr) {
+          load8(sl + 2 * H + i * 8, o);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] += r * gv[j] * wv[j] - xv[j] * c;
+        store8(dx + (int64_t)row * H + i * 8, o);
+      }
+    }
+    __syncwarp();
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = lane + 32 * k;
+    if (i < nv) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) atomicAdd(&sdw[i * 8 + j], acc[k][j]);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < H; i += blockDim.x) atomicAdd(&dw[i], sdw[i]);
+}
+
 }  // namespace
+
+// Grid of one resident wave for a ring kernel with `smem` bytes per 4-warp block.
+template <typename K>
+static int ring_grid(K kern, size_t smem, int64_t rows) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, size_t>, int> cache;
+  const void* fn = reinterpret_cast<const void*>(kern);
+  int per_sm = 0;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find({fn, smem});
+    if (it != cache.end()) {
+      per_sm = it->second;
+    } else {
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 128, smem) != cudaSuccess ||
+          per_sm < 1)
+        per_sm = 1;
+      cache[{fn, smem}] = per_sm;
+    }
+  }
+  return grid_for(rows, 4, 148 * per_sm);
+}
+
+constexpr int kRnStages = 4;
 
 void rmsnorm_fwd(const bf16* x, const bf16* w, bf16* y, float* rstd, int64_t T, int H, float eps,
                  cudaStream_t s) {
+  const int nv = H / 8;
+  if (nv <= 128 && T < (int64_t(1) << 31)) {
+    const size_t smem = (size_t)4 * kRnStages * H * sizeof(bf16);
+    auto kern = nv <= 32 ? rmsnorm_fwd_ring_k<1, kRnStages>
+                : nv <= 64 ? rmsnorm_fwd_ring_k<2, kRnStages> : rmsnorm_fwd_ring_k<4, kRnStages>;
+    kern<<<ring_grid(kern, smem, T), 128, smem, s>>>(x, w, y, rstd, static_cast<int>(T), H, eps);
+    return;
+  }
   rmsnorm_fwd_k<<<grid_for(T, 8), 256, 0, s>>>(x, w, y, rstd, T, H, eps);
 }
 
 void rmsnorm_bwd(const bf16* dy, const bf16* x, const bf16* w, const float* rstd,
                  const bf16* dres, bf16* dx, float* dw, int64_t T, int H, cudaStream_t s) {
   const int nv = H / 8;
+  if (nv <= 128 && T < (int64_t(1) << 31)) {
+    const int rows = dres != nullptr ? 3 : 2;
+    // two stages: the compute from shared memory needs the warps more than a
+    // third row in flight (measured 52 vs 54 us at T=32768, H=896)
+    constexpr int ns = 2;
+    const size_t smem = 2 * H * sizeof(float) + (size_t)4 * ns * (rows * H * 2 + 16);
+    auto kern = nv <= 32 ? rmsnorm_bwd_ring_k<1, ns>
+                : nv <= 64 ? rmsnorm_bwd_ring_k<2, ns> : rmsnorm_bwd_ring_k<4, ns>;
+    kern<<<ring_grid(kern, smem, T), 128, smem, s>>>(dy, x, w, rstd, dres, dx, dw,
+                                                     static_cast<int>(T), H);
+    return;
+  }
   const int grid = grid_for(T, 8, 148 * 3);
   const size_t sm = 2 * H * sizeof(float);
   if (nv <= 32)

@@ -11,20 +11,30 @@ def _rms_ref(x, w, eps):
     return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)) * w.float()
 
 
-@pytest.mark.parametrize("T,H", [(4096, 896), (1000, 256), (333, 512), (64, 1024)])
-def test_rmsnorm_fwd_bwd(T, H):
-    from complexity_framework_b200.ops.fused import rmsnorm
+@pytest.mark.parametrize("skip", [False, True])
+@pytest.mark.parametrize("T,H", [(4096, 896), (1000, 256), (333, 512), (64, 1024), (77, 200),
+                                 (300, 2048)])
+def test_rmsnorm_fwd_bwd(T, H, skip):
+    from complexity_framework_b200.ops.fused import rmsnorm, rmsnorm_skip
 
     torch.manual_seed(0)
     x = torch.randn(T, H, device="cuda").bfloat16().requires_grad_()
     w = (1 + 0.1 * torch.randn(H, device="cuda")).bfloat16().requires_grad_()
-    y = rmsnorm(x, w, 1e-6)
-    g = torch.randn_like(y)
-    y.backward(g)
+    g = torch.randn(T, H, device="cuda").bfloat16()
+    gs = torch.randn(T, H, device="cuda").bfloat16()
+    if skip:  # second output is the residual stream; its gradient joins in the kernel
+        y, xs = rmsnorm_skip(x, w, 1e-6)
+        torch.autograd.backward([y, xs], [g, gs])
+    else:
+        y = rmsnorm(x, w, 1e-6)
+        y.backward(g)
     xr = x.detach().float().requires_grad_()
     wr = w.detach().float().requires_grad_()
     yr = _rms_ref(xr, wr, 1e-6)
-    yr.backward(g.float())
+    if skip:
+        torch.autograd.backward([yr, xr * 1.0], [g.float(), gs.float()])
+    else:
+        yr.backward(g.float())
     assert (y.float() - yr).abs().max() < 3e-2
     assert (x.grad.float() - xr.grad).abs().max() / xr.grad.abs().max() < 2e-2
     assert (w.grad.float() - wr.grad).abs().max() / wr.grad.abs().max() < 2e-2
