@@ -589,38 +589,69 @@ __global__ void embedding_bwd_k(const int64_t* __restrict__ ids, const bf16* __r
 }
 
 // ----------------------------------------------------------------- cross-entropy
-__global__ void ce_loss_grad_k(bf16* __restrict__ logits, const float2* __restrict__ stats,
-                               int ntiles, const int64_t* __restrict__ targets,
-                               float* __restrict__ loss, const float* __restrict__ scale_p,
-                               int64_t T, int V, int64_t ignore_index) {
+// One 256-thread block per row.  The row's per-128-column partials (max,
+// sum of exp) are combined cooperatively (one partial per thread, then block
+// max / sum), and the gradient pass keeps four 16-byte vectors per thread in
+// flight.
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, u) : v + u;
+  }
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  v = red[0];
+  for (int i = 1; i < (int)(blockDim.x >> 5); ++i) v = is_max ? fmaxf(v, red[i]) : v + red[i];
+  __syncthreads();  // red is reused by the next reduction
+  return v;
+}
+
+__global__ void __launch_bounds__(256) ce_loss_grad_k(
+    bf16* __restrict__ logits, const float2* __restrict__ stats, int ntiles,
+    const int64_t* __restrict__ targets, float* __restrict__ loss,
+    const float* __restrict__ scale_p, int64_t T, int V, int64_t ignore_index) {
+  __shared__ float red[8];
   const int64_t row = blockIdx.x;
   if (row >= T) return;
   const int tid = threadIdx.x;
   const float2* st = stats + row * ntiles;
-  // every thread reduces the (small) partial list redundantly -- no sync needed
   float m = -INFINITY;
-  for (int i = 0; i < ntiles; ++i) m = fmaxf(m, st[i].x);
+  for (int i = tid; i < ntiles; i += blockDim.x) m = fmaxf(m, st[i].x);
+  m = block_reduce(m, true, red);
   float se = 0.f;
-  for (int i = 0; i < ntiles; ++i) se += st[i].y * __expf(st[i].x - m);
+  for (int i = tid; i < ntiles; i += blockDim.x) se += st[i].y * __expf(st[i].x - m);
+  se = block_reduce(se, false, red);
   const float lse = m + __logf(se);
   const int64_t tgt = targets[row];
   const bool valid = tgt != ignore_index && tgt >= 0 && tgt < V;
   bf16* lr = logits + row * (int64_t)V;
-  if (tid == 0) {
-    loss[row] = valid ? lse - __bfloat162float(lr[tgt]) : 0.f;
-  }
+  if (tid == 0) loss[row] = valid ? lse - __bfloat162float(lr[tgt]) : 0.f;
+  __syncthreads();  // the target logit is read before any thread overwrites it
   const float scale = valid ? *scale_p : 0.f;
   const int nv = V >> 3;
-  for (int i = tid; i < nv; i += blockDim.x) {
-    float v[8];
-    load8(lr + i * 8, v);
+  constexpr int U = 4;
+  for (int i0 = tid; i0 < nv; i0 += U * blockDim.x) {
+    float v[U][8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float p = __expf(v[j] - lse);
-      if (i * 8 + j == tgt) p -= 1.f;
-      v[j] = p * scale;
+    for (int u = 0; u < U; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i < nv) load8(lr + i * 8, v[u]);
     }
-    store8(lr + i * 8, v);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i < nv) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float p = __expf(v[u][j] - lse);
+          if (i * 8 + j == tgt) p -= 1.f;
+          v[u][j] = p * scale;
+        }
+        store8(lr + i * 8, v[u]);
+      }
+    }
   }
 }
 
