@@ -677,31 +677,77 @@ __global__ void route_scales_k(const int64_t* __restrict__ ids, const int64_t* _
 }
 
 // ----------------------------------------------------------------- AdamW
-__global__ void adamw_flat_k(float* __restrict__ p, float* __restrict__ m, float* __restrict__ v,
-                             const bf16* __restrict__ g, bf16* __restrict__ p_out, int64_t n,
-                             float lr, float b1, float b2, float eps, float wd, float bc1,
-                             float bc2_sqrt, const float* __restrict__ clip) {
+__device__ __forceinline__ float adamw_elem(float& p, float& m, float& v, float g, float b1,
+                                            float b2, float eps, float decay, float step,
+                                            float bc2_sqrt) {
+  m = b1 * m + (1.f - b1) * g;
+  v = b2 * v + (1.f - b2) * g * g;
+  p = p * decay - step * m / (sqrtf(v) / bc2_sqrt + eps);
+  return p;
+}
+
+// 8 elements per thread per iteration with 16-byte accesses (the buffers are
+// flat and 128-element aligned); a scalar loop takes any ragged tail.
+__global__ void __launch_bounds__(256) adamw_flat_k(float* __restrict__ p, float* __restrict__ m,
+                                                    float* __restrict__ v,
+                                                    const bf16* __restrict__ g,
+                                                    bf16* __restrict__ p_out, int64_t n, float lr,
+                                                    float b1, float b2, float eps, float wd,
+                                                    float bc1, float bc2_sqrt,
+                                                    const float* __restrict__ clip, bool vec) {
   const float cs = clip != nullptr ? *clip : 1.f;
   const float step = lr / bc1;
   const float decay = 1.f - lr * wd;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+  const int64_t nv = vec ? n / 8 : 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const float gi = __bfloat162float(g[i]) * cs;
-    const float mi = b1 * m[i] + (1.f - b1) * gi;
-    const float vi = b2 * v[i] + (1.f - b2) * gi * gi;
+    float4* p4 = reinterpret_cast<float4*>(p) + 2 * i;
+    float4* m4 = reinterpret_cast<float4*>(m) + 2 * i;
+    float4* v4 = reinterpret_cast<float4*>(v) + 2 * i;
+    float pv[8], mv[8], vv[8], gv[8];
+    const float4 pa = p4[0], pb = p4[1], ma = m4[0], mb = m4[1], va = v4[0], vb = v4[1];
+    load8(g + 8 * i, gv);
+    pv[0] = pa.x; pv[1] = pa.y; pv[2] = pa.z; pv[3] = pa.w;
+    pv[4] = pb.x; pv[5] = pb.y; pv[6] = pb.z; pv[7] = pb.w;
+    mv[0] = ma.x; mv[1] = ma.y; mv[2] = ma.z; mv[3] = ma.w;
+    mv[4] = mb.x; mv[5] = mb.y; mv[6] = mb.z; mv[7] = mb.w;
+    vv[0] = va.x; vv[1] = va.y; vv[2] = va.z; vv[3] = va.w;
+    vv[4] = vb.x; vv[5] = vb.y; vv[6] = vb.z; vv[7] = vb.w;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      adamw_elem(pv[j], mv[j], vv[j], gv[j] * cs, b1, b2, eps, decay, step, bc2_sqrt);
+    p4[0] = make_float4(pv[0], pv[1], pv[2], pv[3]);
+    p4[1] = make_float4(pv[4], pv[5], pv[6], pv[7]);
+    m4[0] = make_float4(mv[0], mv[1], mv[2], mv[3]);
+    m4[1] = make_float4(mv[4], mv[5], mv[6], mv[7]);
+    v4[0] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+    v4[1] = make_float4(vv[4], vv[5], vv[6], vv[7]);
+    if (p_out != nullptr) store8(p_out + 8 * i, pv);
+  }
+  for (int64_t i = nv * 8 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float pi = p[i], mi = m[i], vi = v[i];
+    adamw_elem(pi, mi, vi, __bfloat162float(g[i]) * cs, b1, b2, eps, decay, step, bc2_sqrt);
+    p[i] = pi;
     m[i] = mi;
     v[i] = vi;
-    float pi = p[i] * decay;
-    pi -= step * mi / (sqrtf(vi) / bc2_sqrt + eps);
-    p[i] = pi;
     if (p_out != nullptr) p_out[i] = __float2bfloat16(pi);
   }
 }
 
-__global__ void sumsq_bf16_k(const bf16* __restrict__ g, int64_t n, float* __restrict__ out) {
+__global__ void sumsq_bf16_k(const bf16* __restrict__ g, int64_t n, float* __restrict__ out,
+                             bool vec) {
   __shared__ float red[32];
   float acc = 0.f;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+  const int64_t nv = vec ? n / 8 : 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float x[8];
+    load8(g + 8 * i, x);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc += x[j] * x[j];
+  }
+  for (int64_t i = nv * 8 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const float x = __bfloat162float(g[i]);
     acc += x * x;
@@ -1070,12 +1116,15 @@ void route_scales(const int64_t* ids, const int64_t* table, const float* route_w
 void adamw_flat(float* p, float* m, float* v, const bf16* g, bf16* p_out, int64_t n, float lr,
                 float beta1, float beta2, float eps, float wd, float bc1, float bc2,
                 const float* clip, cudaStream_t s) {
-  adamw_flat_k<<<grid_for(n, 256, 148 * 8), 256, 0, s>>>(p, m, v, g, p_out, n, lr, beta1, beta2,
-                                                         eps, wd, bc1, sqrtf(bc2), clip);
+  auto al = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+  const bool vec = al(p) && al(m) && al(v) && al(g) && (p_out == nullptr || al(p_out));
+  adamw_flat_k<<<grid_for(vec ? n / 8 + 1 : n, 256, 148 * 8), 256, 0, s>>>(
+      p, m, v, g, p_out, n, lr, beta1, beta2, eps, wd, bc1, sqrtf(bc2), clip, vec);
 }
 
 void sumsq_bf16(const bf16* g, int64_t n, float* out, cudaStream_t s) {
-  sumsq_bf16_k<<<grid_for(n, 1024, 148 * 4), 1024, 0, s>>>(g, n, out);
+  const bool vec = reinterpret_cast<uintptr_t>(g) % 16 == 0;
+  sumsq_bf16_k<<<grid_for(vec ? n / 8 + 1 : n, 1024, 148 * 4), 1024, 0, s>>>(g, n, out, vec);
 }
 
 void clip_coef(const float* sumsq, float max_norm, float* clip, float* norm, cudaStream_t s) {

@@ -125,6 +125,9 @@ class FusedAdamW(torch.optim.Optimizer):
         self.sharded = bool(shard_state) and self.world > 1
         self._flat: List[Optional[_FlatGroup]] = []
         self._step_count = 0
+        # gradients set on the parameters before the first zero_grad (assigned
+        # tensors rather than the flat views) are gathered too
+        self._gathered = False
         for group in self.param_groups:
             ps = [p for p in group["params"] if p.requires_grad]
             if not ps:
@@ -175,7 +178,7 @@ class FusedAdamW(torch.optim.Optimizer):
 
     @torch.no_grad()
     def _gather_grads(self) -> None:
-        if getattr(self, "_gathered", True):
+        if self._gathered:
             return
         for fg in self.flat_groups:
             dst, src, missing = [], [], []

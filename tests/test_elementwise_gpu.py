@@ -114,3 +114,33 @@ def test_linear_cross_entropy_matches_torch(T, H, V):
     rel = lambda a, b: float((a.float() - b).abs().max() / b.abs().max())  # noqa: E731
     assert rel(h.grad, hr.grad) < 3e-2
     assert rel(w.grad, wr.grad) < 3e-2
+
+
+def test_fused_adamw_matches_torch():
+    """Flat fp32-master AdamW kernel (8-wide vectors plus ragged tail, device
+    clip coefficient) against torch.optim.AdamW on fp32 copies."""
+    from complexity_framework_b200.training.optim import FusedAdamW
+
+    torch.manual_seed(0)
+    shapes = [(1000, 37), (129,), (64, 64), (7,)]
+    ps = [torch.nn.Parameter(torch.randn(s, device="cuda").bfloat16()) for s in shapes]
+    ref = [torch.nn.Parameter(p.detach().float().clone()) for p in ps]
+    opt = FusedAdamW(ps, lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1)
+    ropt = torch.optim.AdamW(ref, lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1, eps=1e-8)
+    for step in range(3):
+        grads = [torch.randn(s, device="cuda") for s in shapes]
+        for p, g in zip(ps, grads):
+            p.grad = g.bfloat16()
+        opt.clip_grad_norm_(1.0)
+        opt.step(clip=True)
+        opt.zero_grad()
+        gb = [g.bfloat16().float() for g in grads]
+        total = torch.sqrt(sum((g * g).sum() for g in gb))
+        coef = min(1.0, 1.0 / (float(total) + 1e-6))
+        for r, g in zip(ref, gb):
+            r.grad = g * coef
+        ropt.step()
+    for p, r in zip(ps, ref):
+        master = opt.state[p]["master"]
+        assert float((master.reshape(r.shape) - r.detach()).abs().max()) < 1e-4
+        assert float((p.detach().float() - r.detach()).abs().max()) < 2e-2
