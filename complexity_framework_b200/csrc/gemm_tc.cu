@@ -45,9 +45,7 @@ constexpr int kBK = 64;
 // output of a column chunk in flight while the next chunk is converted.
 __host__ __device__ constexpr int epi_slots(int epi) {
   return epi == EPI_SWIGLU_FWD ? 3
-         : (epi == EPI_STORE || epi == EPI_RESID || epi == EPI_CE_STATS || epi == EPI_SWIGLU_BWD)
-             ? 2
-             : 0;
+         : (epi == EPI_STORE || epi == EPI_RESID || epi == EPI_CE_STATS) ? 2 : 0;
 }
 // Epilogue operands read by TMA (32x32 bf16 boxes per column chunk): the
 // residual for EPI_RESID, the saved gate and up pre-activations for
@@ -55,11 +53,16 @@ __host__ __device__ constexpr int epi_slots(int epi) {
 __host__ __device__ constexpr int epi_loads(int epi) {
   return epi == EPI_SWIGLU_BWD ? 2 : (epi == EPI_RESID ? 1 : 0);
 }
+// Column chunks of operand boxes in flight per warp.  EPI_SWIGLU_BWD stages
+// its outputs in the consumed g/u boxes and stores them from there (no
+// separate store slots), so the same shared memory holds three chunks.
+__host__ __device__ constexpr int epi_depth(int epi) { return epi == EPI_SWIGLU_BWD ? 3 : 2; }
+constexpr int kMaxLoadDepth = 4;
 constexpr int kEpiWarps = 8;
 constexpr int kBoxBytes = 32 * 32 * 2;
 constexpr int kBarrierBytes = 512;
 
-template <int BN, bool PAIR, int SLOTS, int LOADS = 0>
+template <int BN, bool PAIR, int SLOTS, int LOADS = 0, int DEPTH = 2>
 struct GemmCfg {
   // With PAIR, a 256-row tile is split over a CTA pair: each CTA holds its 128
   // A rows and half of the BN B rows; the even CTA issues M=256 MMAs.
@@ -67,7 +70,7 @@ struct GemmCfg {
   static constexpr int A_BYTES = kBM * kBK * 2;
   static constexpr int B_BYTES = B_ROWS * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int WARP_STAGING = (SLOTS + 2 * LOADS) * kBoxBytes;
+  static constexpr int WARP_STAGING = (SLOTS + DEPTH * LOADS) * kBoxBytes;
   static constexpr int STAGING_BYTES = WARP_STAGING * kEpiWarps;
   static constexpr int STAGES = (227 * 1024 - 2048 - STAGING_BYTES) / STAGE_BYTES > 8
                                     ? 8
@@ -151,22 +154,23 @@ __device__ __forceinline__ void read_box_row(const uint8_t* box, int lane, float
   }
 }
 
-// Per-warp double-buffered TMA loads of epilogue operand boxes.  Tickets are
-// issued and consumed in the same order; ticket k uses slot k & 1.
-template <int LOADS>
+// Per-warp ring of TMA loads of epilogue operand boxes, DEPTH chunks deep.
+// Tickets are issued and consumed in the same order; ticket k uses slot
+// k % DEPTH and mbarrier phase (k / DEPTH) & 1.
+template <int LOADS, int DEPTH = 2>
 struct LoadRing {
-  uint8_t* base;    // 2 slots x LOADS boxes
-  uint64_t* bar;    // 2 mbarriers
+  uint8_t* base;    // DEPTH slots x LOADS boxes
+  uint64_t* bar;    // DEPTH mbarriers
   uint32_t issued;
   uint32_t consumed;
   int lane;
   __device__ __forceinline__ uint8_t* box(uint32_t ticket, int i) const {
-    return base + ((ticket & 1u) * LOADS + i) * kBoxBytes;
+    return base + ((ticket % DEPTH) * LOADS + i) * kBoxBytes;
   }
   // lane 0 issues the LOADS boxes at (xs[i], y)
   __device__ __forceinline__ void issue(const CUtensorMap* map, const int* xs, int y) {
     if (lane == 0) {
-      uint64_t* b = &bar[issued & 1u];
+      uint64_t* b = &bar[issued % DEPTH];
       mbar_arrive_expect_tx(b, LOADS * kBoxBytes);
 #pragma unroll
       for (int i = 0; i < LOADS; ++i) tma_load_2d(box(issued, i), map, b, xs[i], y);
@@ -174,7 +178,7 @@ struct LoadRing {
     ++issued;
   }
   __device__ __forceinline__ bool wait(volatile int* abort_flag, int* err) {
-    const bool ok = mbar_wait(&bar[consumed & 1u], (consumed >> 1) & 1u, abort_flag, err,
+    const bool ok = mbar_wait(&bar[consumed % DEPTH], (consumed / DEPTH) & 1u, abort_flag, err,
                               kErrTimeoutFull, 14);
     return ok;
   }
@@ -186,7 +190,8 @@ struct LoadRing {
   // bounded wait for copies still in flight before the CTA exits
   __device__ __forceinline__ void drain(int* err) {
     while (consumed < issued) {
-      mbar_wait(&bar[consumed & 1u], (consumed >> 1) & 1u, nullptr, err, kErrTimeoutFull, 15);
+      mbar_wait(&bar[consumed % DEPTH], (consumed / DEPTH) & 1u, nullptr, err, kErrTimeoutFull,
+                15);
       ++consumed;
     }
   }
@@ -230,7 +235,8 @@ __global__ void __launch_bounds__(384, 1)
                    GemmEpi ep, int* err) {
   constexpr int SLOTS = epi_slots(EPI);
   constexpr int LOADS = epi_loads(EPI);
-  using Cfg = GemmCfg<BN, PAIR, SLOTS, LOADS>;
+  constexpr int DEPTH = epi_depth(EPI);
+  using Cfg = GemmCfg<BN, PAIR, SLOTS, LOADS, DEPTH>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int B_ROWS = Cfg::B_ROWS;
 
@@ -243,8 +249,8 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
-  uint64_t* load_bar = tempty_bar + 2;  // 2 per epilogue warp
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(load_bar + 2 * kEpiWarps);
+  uint64_t* load_bar = tempty_bar + 2;  // kMaxLoadDepth per epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(load_bar + kMaxLoadDepth * kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
@@ -274,7 +280,7 @@ __global__ void __launch_bounds__(384, 1)
       // one arrival per epilogue warp of every CTA in the MMA group
       mbar_init(&tempty_bar[a], PAIR ? 16 : 8);
     }
-    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&load_bar[i], 1);
+    for (int i = 0; i < kMaxLoadDepth * kEpiWarps; ++i) mbar_init(&load_bar[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -513,7 +519,8 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t tempty_peer1 = mapa_shared(smem_u32(&tempty_bar[1]), 0);
     uint8_t* wstage = staging + (warp - 4) * Cfg::WARP_STAGING;
     BoxRing<SLOTS ? SLOTS : 1> ring{wstage, 0, lane};
-    LoadRing<LOADS ? LOADS : 1> lring{wstage + SLOTS * kBoxBytes, load_bar + 2 * (warp - 4), 0u,
+    LoadRing<LOADS ? LOADS : 1, DEPTH> lring{wstage + SLOTS * kBoxBytes,
+                                              load_bar + kMaxLoadDepth * (warp - 4), 0u,
                                       0u, lane};
     bool ep_ok = true;
     for (int u = unit; u < total; u += units) {
@@ -530,6 +537,8 @@ __global__ void __launch_bounds__(384, 1)
           const int xs[2] = {(ac / kSwigluBlock) * 2 * kSwigluBlock + ac % kSwigluBlock,
                              (ac / kSwigluBlock) * 2 * kSwigluBlock + ac % kSwigluBlock +
                                  kSwigluBlock};
+          if (lane == 0) bulk_wait_group_read<DEPTH - 2>();  // see the chunk loop
+          __syncwarp();
           lring.issue(&tmC1, xs, m0 + wq * 32);
         }
       } else if constexpr (EPI == EPI_RESID) {
@@ -583,6 +592,10 @@ __global__ void __launch_bounds__(384, 1)
             const int xs[2] = {(ac / kSwigluBlock) * 2 * kSwigluBlock + ac % kSwigluBlock,
                                (ac / kSwigluBlock) * 2 * kSwigluBlock + ac % kSwigluBlock +
                                    kSwigluBlock};
+            // the slot being refilled last held chunk (ticket - DEPTH)'s outputs;
+            // their store must have read it (one newer store group may pend)
+            if (lane == 0) bulk_wait_group_read<DEPTH - 2>();
+            __syncwarp();
             lring.issue(&tmC1, xs, m0 + wq * 32);
           }
           float da[32];
@@ -592,24 +605,35 @@ __global__ void __launch_bounds__(384, 1)
             ep_ok = false;
             break;
           }
+          uint8_t* gbox = lring.box(lring.consumed, 0);
+          uint8_t* ubox = lring.box(lring.consumed, 1);
           float g[32], u[32];
-          read_box_row(lring.box(lring.consumed, 0), lane, g);
-          read_box_row(lring.box(lring.consumed, 1), lane, u);
-          lring.release();
+          read_box_row(gbox, lane, g);
+          read_box_row(ubox, lane, u);
           const int blk = act_col / kSwigluBlock;
           const int w = act_col % kSwigluBlock;
           const float s = row_ok ? swiglu_col_scale(ep, row, act_col) : 0.0f;
-          float dg[32], du[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const float sg = sigmoid_f(g[i]);
-            const float sl = g[i] * sg;
             const float d = da[i] * s;
-            du[i] = d * sl;
-            dg[i] = d * u[i] * sg * (1.0f + g[i] * (1.0f - sg));
+            const float du = d * g[i] * sg;
+            g[i] = d * u[i] * sg * (1.0f + g[i] * (1.0f - sg));  // d(gate)
+            u[i] = du;                                          // d(up)
           }
+          // outputs go out from the boxes the inputs came in (each lane
+          // rewrites only the row it read)
+          stage_row_bf16(gbox, lane, g, 1.0f);
+          stage_row_bf16(ubox, lane, u, 1.0f);
+          fence_proxy_async_shared();
+          __syncwarp();
           const int x = blk * 2 * kSwigluBlock + w;
-          ring.put2(&tmC0, dg, x, du, x + kSwigluBlock, m0 + wq * 32);
+          if (lane == 0) {
+            tma_store_2d(&tmC0, gbox, x, m0 + wq * 32);
+            tma_store_2d(&tmC0, ubox, x + kSwigluBlock, m0 + wq * 32);
+            bulk_commit_group();
+          }
+          ++lring.consumed;
         }
         if (!ep_ok) break;
       } else if constexpr (EPI == EPI_CE_STATS) {
@@ -716,7 +740,7 @@ __global__ void __launch_bounds__(384, 1)
       if (acc == 0) acc_phase ^= 1;
     }
     if (LOADS > 0) lring.drain(err);
-    if (SLOTS > 0 && lane == 0) bulk_wait_group_all();
+    if ((SLOTS > 0 || EPI == EPI_SWIGLU_BWD) && lane == 0) bulk_wait_group_all();
     if constexpr (EPI == EPI_PEER_STORE) __threadfence_system();  // peer stores before exit
   }
 
@@ -782,7 +806,7 @@ template <int BN, bool A_MN, bool B_MN, int EPI, bool PAIR, int NA = 1, int NB =
 static int launch_impl(const SegMaps<NA>& ta, const SegMaps<NB>& tb, const CUtensorMap* tc,
                        int M, int N, int K, const GemmEpi& ep, int num_sms, cudaStream_t stream,
                        int* err, int ksplit = 1) {
-  using Cfg = GemmCfg<BN, PAIR, epi_slots(EPI), epi_loads(EPI)>;
+  using Cfg = GemmCfg<BN, PAIR, epi_slots(EPI), epi_loads(EPI), epi_depth(EPI)>;
   auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI, PAIR, NA, NB>;
   static int max_units = -1;  // resident CTAs (or CTA pairs), one query per instantiation
   cudaLaunchConfig_t cfg = {};
