@@ -537,9 +537,16 @@ __global__ void __launch_bounds__(384, 1)
           const int xs[2] = {(ac / kSwigluBlock) * 2 * kSwigluBlock + ac % kSwigluBlock,
                              (ac / kSwigluBlock) * 2 * kSwigluBlock + ac % kSwigluBlock +
                                  kSwigluBlock};
-          if (lane == 0) bulk_wait_group_read<DEPTH - 2>();  // see the chunk loop
+          if (lane == 0) bulk_wait_group_read<0>();  // see the chunk loop
           __syncwarp();
           lring.issue(&tmC1, xs, m0 + wq * 32);
+          if (n0 + cbeg + 32 < N) {  // and the second chunk: loads run two chunks ahead
+            const int ac2 = ac + 32;
+            const int xs2[2] = {(ac2 / kSwigluBlock) * 2 * kSwigluBlock + ac2 % kSwigluBlock,
+                                (ac2 / kSwigluBlock) * 2 * kSwigluBlock + ac2 % kSwigluBlock +
+                                    kSwigluBlock};
+            lring.issue(&tmC1, xs2, m0 + wq * 32);
+          }
         }
       } else if constexpr (EPI == EPI_RESID) {
         if (n0 + cbeg < N) {
@@ -587,14 +594,14 @@ __global__ void __launch_bounds__(384, 1)
         for (int c = cbeg; c < cbeg + BN / 2; c += 32) {
           const int act_col = n0 + c;
           if (act_col >= N) break;  // warp-uniform; later chunks are out of range too
-          if (c + 32 < cbeg + BN / 2 && act_col + 32 < N) {
-            const int ac = act_col + 32;
+          if (c + 64 < cbeg + BN / 2 && act_col + 64 < N) {
+            const int ac = act_col + 64;
             const int xs[2] = {(ac / kSwigluBlock) * 2 * kSwigluBlock + ac % kSwigluBlock,
                                (ac / kSwigluBlock) * 2 * kSwigluBlock + ac % kSwigluBlock +
                                    kSwigluBlock};
-            // the slot being refilled last held chunk (ticket - DEPTH)'s outputs;
-            // their store must have read it (one newer store group may pend)
-            if (lane == 0) bulk_wait_group_read<DEPTH - 2>();
+            // loads run two chunks ahead: the slot refilled for chunk c+2 last
+            // held chunk c-1's outputs, whose store must have read it
+            if (lane == 0) bulk_wait_group_read<0>();
             __syncwarp();
             lring.issue(&tmC1, xs, m0 + wq * 32);
           }
