@@ -46,6 +46,7 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-count", action="store_true", help="skip the kernel-launch count step")
+    p.add_argument("--no-graph", action="store_true", help="run every step eagerly")
     return p.parse_args()
 
 
@@ -159,16 +160,24 @@ def build_ours(world, args):
 
     torch.manual_seed(0)
     model = ComplexityModel(tr_hash_200m_config())
+    # one GPU: steps after the second warm-up step replay a captured CUDA graph
+    # (forward + backward + AdamW); multi-GPU steps run eagerly
     cfg = TrainingConfig(learning_rate=3e-4, warmup_steps=0, lr_scheduler="constant",
                          precision="bf16", grad_clip=1.0, max_steps=10 ** 9,
                          distributed_mode="fsdp" if world > 1 else "none",
-                         skip_param_update_check=True)
+                         skip_param_update_check=True,
+                         cuda_graph=world == 1 and not args.no_graph, cuda_graph_warmup=2)
     trainer = Trainer(model, cfg)
 
     def step(ids, sync):
         return trainer.train_step(ids, sync=sync)
 
-    return step, "fsdp-zero2 (sharded fp32 master/moments, replicated bf16 params)"
+    if world == 1:
+        mode = "single GPU, flat fp32-master fused AdamW" + (
+            ", step replayed from a CUDA graph" if cfg.cuda_graph else "")
+    else:
+        mode = "fsdp-zero2 (sharded fp32 master/moments, replicated bf16 params)"
+    return step, mode
 
 
 def count_our_kernels(step_fn, ids):

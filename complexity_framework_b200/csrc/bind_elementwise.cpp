@@ -5,6 +5,8 @@
 
 #include "kernels.h"
 
+namespace py = pybind11;
+
 namespace {
 
 using cfb::bf16;
@@ -179,7 +181,8 @@ void route_scales(const torch::Tensor& ids, const torch::Tensor& table, const to
 void adamw_flat(torch::Tensor& p, torch::Tensor& m, torch::Tensor& v, const torch::Tensor& g,
                 const c10::optional<torch::Tensor>& p_out, double lr, double b1, double b2,
                 double eps, double wd, double bc1, double bc2,
-                const c10::optional<torch::Tensor>& clip) {
+                const c10::optional<torch::Tensor>& clip,
+                const c10::optional<torch::Tensor>& hyper) {
   chk(p, torch::kFloat32, "p");
   chk(m, torch::kFloat32, "exp_avg");
   chk(v, torch::kFloat32, "exp_avg_sq");
@@ -191,11 +194,15 @@ void adamw_flat(torch::Tensor& p, torch::Tensor& m, torch::Tensor& v, const torc
     TORCH_CHECK(p_out->numel() == n, "p_out size");
   }
   if (clip.has_value()) chk(*clip, torch::kFloat32, "clip");
+  if (hyper.has_value()) {
+    chk(*hyper, torch::kFloat32, "hyper");
+    TORCH_CHECK(hyper->numel() >= 3, "hyper holds (lr, bias correction 1, bias correction 2)");
+  }
   const c10::cuda::CUDAGuard guard(p.device());
   cfb::adamw_flat(P<float>(p), P<float>(m), P<float>(v), P<bf16>(g), Popt<bf16>(p_out), n,
                   static_cast<float>(lr), static_cast<float>(b1), static_cast<float>(b2),
                   static_cast<float>(eps), static_cast<float>(wd), static_cast<float>(bc1),
-                  static_cast<float>(bc2), Popt<float>(clip), cur());
+                  static_cast<float>(bc2), Popt<float>(clip), Popt<float>(hyper), cur());
 }
 
 void sumsq_bf16(const torch::Tensor& g, torch::Tensor& out) {
@@ -308,7 +315,10 @@ void register_elementwise(pybind11::module& m) {
   m.def("embedding_bwd", &embedding_bwd);
   m.def("ce_loss_grad", &ce_loss_grad);
   m.def("route_scales", &route_scales);
-  m.def("adamw_flat", &adamw_flat);
+  m.def("adamw_flat", &adamw_flat, py::arg("p"), py::arg("m"), py::arg("v"), py::arg("g"),
+        py::arg("p_out"), py::arg("lr"), py::arg("b1"), py::arg("b2"), py::arg("eps"),
+        py::arg("wd"), py::arg("bc1"), py::arg("bc2"), py::arg("clip"),
+        py::arg("hyper") = py::none());
   m.def("sumsq_bf16", &sumsq_bf16);
   m.def("clip_coef", &clip_coef);
   m.def("paged_attention", &paged_attention);

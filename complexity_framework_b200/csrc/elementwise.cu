@@ -694,8 +694,14 @@ __global__ void __launch_bounds__(256) adamw_flat_k(float* __restrict__ p, float
                                                     bf16* __restrict__ p_out, int64_t n, float lr,
                                                     float b1, float b2, float eps, float wd,
                                                     float bc1, float bc2_sqrt,
-                                                    const float* __restrict__ clip, bool vec) {
+                                                    const float* __restrict__ clip,
+                                                    const float* __restrict__ hyper, bool vec) {
   const float cs = clip != nullptr ? *clip : 1.f;
+  if (hyper != nullptr) {
+    lr = hyper[0];
+    bc1 = hyper[1];
+    bc2_sqrt = sqrtf(hyper[2]);
+  }
   const float step = lr / bc1;
   const float decay = 1.f - lr * wd;
   const int64_t nv = vec ? n / 8 : 0;
@@ -1115,11 +1121,11 @@ void route_scales(const int64_t* ids, const int64_t* table, const float* route_w
 
 void adamw_flat(float* p, float* m, float* v, const bf16* g, bf16* p_out, int64_t n, float lr,
                 float beta1, float beta2, float eps, float wd, float bc1, float bc2,
-                const float* clip, cudaStream_t s) {
+                const float* clip, const float* hyper, cudaStream_t s) {
   auto al = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
   const bool vec = al(p) && al(m) && al(v) && al(g) && (p_out == nullptr || al(p_out));
   adamw_flat_k<<<grid_for(vec ? n / 8 + 1 : n, 256, 148 * 8), 256, 0, s>>>(
-      p, m, v, g, p_out, n, lr, beta1, beta2, eps, wd, bc1, sqrtf(bc2), clip, vec);
+      p, m, v, g, p_out, n, lr, beta1, beta2, eps, wd, bc1, sqrtf(bc2), clip, hyper, vec);
 }
 
 void sumsq_bf16(const bf16* g, int64_t n, float* out, cudaStream_t s) {

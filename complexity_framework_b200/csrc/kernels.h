@@ -45,9 +45,11 @@ void route_scales(const int64_t* ids, const int64_t* table, const float* route_w
 
 // Flat-buffer AdamW (torch.optim.AdamW semantics) with fp32 master weights;
 // writes the bf16 compute copy.  clip (device scalar or nullptr) scales grads.
+// hyper (device [lr, bc1, bc2] or nullptr) overrides lr/bc1/bc2, so a CUDA
+// graph that captured the launch follows the schedule across replays.
 void adamw_flat(float* p, float* m, float* v, const bf16* g, bf16* p_out, int64_t n, float lr,
                 float beta1, float beta2, float eps, float wd, float bc1, float bc2,
-                const float* clip, cudaStream_t s);
+                const float* clip, const float* hyper, cudaStream_t s);
 // sumsq (+=) of a bf16 vector into *out (fp32, caller zeroes).
 void sumsq_bf16(const bf16* g, int64_t n, float* out, cudaStream_t s);
 // clip = min(1, max_norm / (sqrt(sumsq) + 1e-6)); norm = sqrt(sumsq).

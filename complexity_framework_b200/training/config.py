@@ -27,6 +27,11 @@ class TrainingConfig:
     precision: str = "bf16"
     grad_clip: float = 1.0
     skip_param_update_check: bool = False
+    # capture forward + backward + optimizer of a step in one CUDA graph after
+    # `cuda_graph_warmup` eager steps (single GPU, fused AdamW); replays skip
+    # the per-kernel launch overhead
+    cuda_graph: bool = False
+    cuda_graph_warmup: int = 3
     use_fsdp: bool = True
     sharding_mode: str = "full_shard"
     checkpoint_dir: str = "checkpoints"

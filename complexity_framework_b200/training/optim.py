@@ -152,6 +152,7 @@ class FusedAdamW(torch.optim.Optimizer):
         self._norm = torch.zeros(1, device=dev, dtype=torch.float32)
         self._sq_distinct = None
         self._max_norm = 0.0
+        self._hyper = None  # device (lr, bc1, bc2) per flat group; see enable_device_hyper
         self._fused = None
         if fused_collectives is None:
             fused_collectives = os.environ.get("CFB_FUSED_DP", "1") != "0"
@@ -294,6 +295,34 @@ class FusedAdamW(torch.optim.Optimizer):
                 self._clip.fill_(1.0)
         return self._norm[0]
 
+    # ------------------------------------------------ device hyper-parameters
+    def enable_device_hyper(self) -> None:
+        """Make the AdamW kernels read (lr, bias corrections) from a device
+        buffer, filled by ``write_hyper`` before each step, instead of launch
+        arguments: a CUDA graph that captured ``step`` then follows the
+        learning-rate schedule and the step count across replays."""
+        if self._fused is not None or not self._use_kernels():
+            raise RuntimeError("device hyper-parameters need the single-process kernel path")
+        dev = self.flat_groups[0].master.device
+        self._hyper = torch.zeros(len(self.param_groups), 3, device=dev, dtype=torch.float32)
+
+    def write_hyper(self, t: int) -> None:
+        """Fill the device buffer for step ``t`` from each group's current lr."""
+        vals = []
+        for group in self.param_groups:
+            b1, b2 = group["betas"]
+            vals.append([group["lr"], 1.0 - b1 ** t, 1.0 - b2 ** t])
+        # pageable source: the copy is staged before this call returns, so the
+        # host list may be rebuilt next step while earlier work is still queued
+        self._hyper.copy_(torch.tensor(vals, dtype=torch.float32), non_blocking=True)
+
+    def finish_replayed_step(self, t: int) -> None:
+        """Host bookkeeping of a step whose kernels ran from a replayed graph."""
+        self._step_count = t
+        for fg in self.flat_groups:
+            for p in fg.params:
+                self.state[p]["step"].fill_(t)
+
     # ----------------------------------------------------------------- step
     @torch.no_grad()
     def step(self, closure=None, clip: bool = False):
@@ -309,7 +338,7 @@ class FusedAdamW(torch.optim.Optimizer):
             from ..ops import require
 
             C = require()
-        for group, fg in zip(self.param_groups, self._flat):
+        for gi, (group, fg) in enumerate(zip(self.param_groups, self._flat)):
             if fg is None:
                 continue
             b1, b2 = group["betas"]
@@ -318,7 +347,8 @@ class FusedAdamW(torch.optim.Optimizer):
             lr, wd, eps = group["lr"], group["weight_decay"], group["eps"]
             if kernels:
                 C.adamw_flat(fg.master, fg.exp_avg, fg.exp_avg_sq, fg.grad_shard, fg.compute_shard,
-                             lr, b1, b2, eps, wd, bc1, bc2, self._clip if clip else None)
+                             lr, b1, b2, eps, wd, bc1, bc2, self._clip if clip else None,
+                             None if self._hyper is None else self._hyper[gi])
             else:
                 g = fg.grad_shard.float() * (self._clip if clip else 1.0)
                 fg.exp_avg.mul_(b1).add_(g, alpha=1 - b1)

@@ -85,6 +85,7 @@ class Trainer:
         self.total_tokens = 0
         self.best_loss = float("inf")
         self._compute_loss = compute_loss
+        self._graphed = None
         self._canary = None
         self.should_stop = False
 
@@ -138,8 +139,22 @@ class Trainer:
 
         ``input_ids`` may live on the host (pinned memory is copied
         asynchronously).  Returns the loss as a Python float when ``sync``
-        (one device-to-host read), else the detached device scalar.
+        (one device-to-host read), else the detached device scalar.  With
+        ``config.cuda_graph`` the step is replayed from a captured CUDA graph
+        after the warm-up steps (``training/graph_step.py``); the returned
+        device scalar is then overwritten by the next step.
         """
+        if self.config.cuda_graph:
+            if self._graphed is None:
+                from .graph_step import GraphedTrainStep
+
+                self._graphed = GraphedTrainStep(self)
+            out = self._graphed(input_ids, labels)
+            return float(out) if sync else out
+        return self._train_step_eager(input_ids, labels, sync=sync)
+
+    def _train_step_eager(self, input_ids: torch.Tensor, labels: Optional[torch.Tensor] = None, *,
+                          sync: bool = True):
         self.model.train()
         ids = input_ids.to(self.device, non_blocking=True)
         lab = labels.to(self.device, non_blocking=True) if labels is not None else None
