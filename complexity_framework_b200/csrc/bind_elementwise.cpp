@@ -3,6 +3,10 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <mutex>
+#include <unordered_map>
+#include <utility>
+
 #include "kernels.h"
 
 namespace py = pybind11;
@@ -25,6 +29,31 @@ T* Popt(const c10::optional<torch::Tensor>& t) {
   return t.has_value() ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
 }
 cudaStream_t cur() { return at::cuda::getCurrentCUDAStream(); }
+
+// Accumulator slots for norm-weight gradients written straight to bf16: each
+// slot is 1024 floats plus a ticket word, zero between launches (the last
+// block of each launch re-zeroes its slot).  Calls take slots round-robin,
+// so launches that share a slot are kSlots calls apart; launches that run
+// concurrently on different streams must be fewer than kSlots calls apart.
+constexpr int kSlotFloats = 1024, kSlotStride = 1024 + 32, kSlots = 256;
+std::mutex g_slot_mu;
+std::unordered_map<int, std::pair<torch::Tensor, int>> g_slots;
+
+std::pair<float*, int*> grad_slot(int device, int64_t n) {
+  TORCH_CHECK(n <= kSlotFloats, "norm-weight gradient slot holds at most ", kSlotFloats,
+              " floats");
+  std::lock_guard<std::mutex> lk(g_slot_mu);
+  auto it = g_slots.find(device);
+  if (it == g_slots.end()) {
+    auto t = torch::zeros({int64_t(kSlots) * kSlotStride},
+                          torch::dtype(torch::kFloat32).device(torch::kCUDA, device));
+    it = g_slots.emplace(device, std::make_pair(t, 0)).first;
+  }
+  const int i = it->second.second;
+  it->second.second = (i + 1) % kSlots;
+  float* base = it->second.first.data_ptr<float>() + int64_t(i) * kSlotStride;
+  return {base, reinterpret_cast<int*>(base + kSlotFloats)};
+}
 
 void rmsnorm_fwd(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& y,
                  torch::Tensor& rstd, double eps) {
@@ -49,16 +78,26 @@ void rmsnorm_bwd(const torch::Tensor& dy, const torch::Tensor& x, const torch::T
   chk(w, torch::kBFloat16, "w");
   chk(rstd, torch::kFloat32, "rstd");
   chk(dx, torch::kBFloat16, "dx");
-  chk(dw, torch::kFloat32, "dw");
+  const bool bf16_dw = dw.scalar_type() == torch::kBFloat16;
+  chk(dw, bf16_dw ? torch::kBFloat16 : torch::kFloat32, "dw");
   if (dres.has_value()) chk(*dres, torch::kBFloat16, "dres");
   const int64_t H = x.size(-1);
   TORCH_CHECK(H % 8 == 0, "rmsnorm: H must be a multiple of 8");
   const int64_t T = x.numel() / H;
   TORCH_CHECK(dy.numel() == x.numel() && dx.numel() == x.numel() && dw.numel() == H,
               "rmsnorm_bwd sizes");
+  TORCH_CHECK(!bf16_dw || (H <= 1024 && T < (int64_t(1) << 31)),
+              "rmsnorm_bwd: a bf16 dw needs H <= 1024 (pass an fp32 accumulator otherwise)");
   const c10::cuda::CUDAGuard g(x.device());
-  cfb::rmsnorm_bwd(P<bf16>(dy), P<bf16>(x), P<bf16>(w), P<float>(rstd), Popt<bf16>(dres),
-                   P<bf16>(dx), P<float>(dw), T, static_cast<int>(H), cur());
+  if (bf16_dw) {
+    auto slot = grad_slot(x.get_device(), H);
+    cfb::rmsnorm_bwd(P<bf16>(dy), P<bf16>(x), P<bf16>(w), P<float>(rstd), Popt<bf16>(dres),
+                     P<bf16>(dx), slot.first, T, static_cast<int>(H), P<bf16>(dw), slot.second,
+                     cur());
+  } else {
+    cfb::rmsnorm_bwd(P<bf16>(dy), P<bf16>(x), P<bf16>(w), P<float>(rstd), Popt<bf16>(dres),
+                     P<bf16>(dx), P<float>(dw), T, static_cast<int>(H), nullptr, nullptr, cur());
+  }
 }
 
 void qk_norm_rope_fwd(const torch::Tensor& kqv, const torch::Tensor& qw, const torch::Tensor& kw,
@@ -108,19 +147,35 @@ void qk_norm_rope_bwd(const torch::Tensor& dq, const torch::Tensor& dk, const to
   chk(dv, torch::kBFloat16, "dv");
   chk(kqv, torch::kBFloat16, "kqv");
   chk(dkqv, torch::kBFloat16, "dkqv");
-  chk(dqw, torch::kFloat32, "dqw");
-  chk(dkw, torch::kFloat32, "dkw");
+  const bool bf16_dw = dqw.scalar_type() == torch::kBFloat16;
+  chk(dqw, bf16_dw ? torch::kBFloat16 : torch::kFloat32, "dqw");
+  chk(dkw, bf16_dw ? torch::kBFloat16 : torch::kFloat32, "dkw");
+  TORCH_CHECK(dqw.numel() == D && dkw.numel() == D, "dqw/dkw size");
   chk(rstd, torch::kFloat32, "rstd");
   TORCH_CHECK(D == 64 || D == 128, "qk_norm_rope: head_dim must be 64 or 128");
   TORCH_CHECK(dkqv.numel() == kqv.numel() && kqv.numel() == B * S * (Hq + 2 * Hkv) * D,
               "dkqv size");
   if (pos.has_value()) chk(*pos, torch::kInt32, "pos");
   const c10::cuda::CUDAGuard g(kqv.device());
+  float* aq = nullptr;
+  float* ak = nullptr;
+  int* ticket = nullptr;
+  if (bf16_dw) {
+    auto slot = grad_slot(kqv.get_device(), 2 * D);
+    aq = slot.first;
+    ak = slot.first + D;
+    ticket = slot.second;
+  } else {
+    aq = P<float>(dqw);
+    ak = P<float>(dkw);
+  }
   cfb::qk_norm_rope_bwd(P<bf16>(dq), P<bf16>(dk), P<bf16>(dv), P<bf16>(kqv), P<bf16>(qw),
                         P<bf16>(kw), P<float>(cos_t), P<float>(sin_t), Popt<int32_t>(pos),
-                        P<float>(rstd), P<bf16>(dkqv), P<float>(dqw), P<float>(dkw),
-                        static_cast<int>(B), static_cast<int>(S), static_cast<int>(Hq),
-                        static_cast<int>(Hkv), static_cast<int>(D), qk_norm, q_tm, cur());
+                        P<float>(rstd), P<bf16>(dkqv), aq, ak, static_cast<int>(B),
+                        static_cast<int>(S), static_cast<int>(Hq), static_cast<int>(Hkv),
+                        static_cast<int>(D), qk_norm, q_tm,
+                        bf16_dw ? P<bf16>(dqw) : nullptr, bf16_dw ? P<bf16>(dkw) : nullptr,
+                        ticket, cur());
 }
 
 void embedding_fwd(const torch::Tensor& ids, const torch::Tensor& table, torch::Tensor& out) {

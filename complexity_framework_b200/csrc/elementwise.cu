@@ -226,6 +226,29 @@ __device__ __forceinline__ float group_sum(float v) {
   return v;
 }
 
+// Norm-weight gradients without a zero-fill or a cast launch: every block adds
+// its partial into `acc` (fp32; zero on entry), the last block to arrive on
+// `ticket` writes acc to the bf16 outputs (out0 for elements < n0, out1 for
+// the rest) and re-zeroes acc and the ticket, so the slot is ready for the
+// next launch that uses it.
+__device__ void small_grad_finish(float* acc, int* ticket, int n, bf16* out0, int n0,
+                                  bf16* out1) {
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(ticket, 1) == static_cast<int>(gridDim.x) - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const bf16 v = __float2bfloat16(__ldcg(acc + i));
+    if (i < n0) out0[i] = v;
+    else out1[i - n0] = v;
+    acc[i] = 0.f;
+  }
+  if (threadIdx.x == 0) *ticket = 0;
+}
+
 
 // One warp per token.  Each warp owns a ring of NS token slots in shared
 // memory and keeps NS-1 tokens of loads in flight with cp.async (16-byte
@@ -411,7 +434,7 @@ __global__ void __launch_bounds__(128) qk_norm_rope_bwd_k(
     const float* __restrict__ cos_t, const float* __restrict__ sin_t,
     const int32_t* __restrict__ pos, const float* __restrict__ rstd, bf16* __restrict__ dkqv,
     float* __restrict__ dqw, float* __restrict__ dkw, int B, int S, int Hq, int Hkv,
-    bool qk_norm, bool q_tm) {
+    bool qk_norm, bool q_tm, bf16* dqw_out, bf16* dkw_out, int* ticket) {
   constexpr int LPH = D / 8, GPW = 32 / LPH, H2 = D / 2;
   extern __shared__ __align__(16) unsigned char qk_smem[];
   __shared__ float s_dqw[D], s_dkw[D];
@@ -552,6 +575,8 @@ __global__ void __launch_bounds__(128) qk_norm_rope_bwd_k(
       atomicAdd(&dqw[i], s_dqw[i]);
       atomicAdd(&dkw[i], s_dkw[i]);
     }
+    // dkw == dqw + D when the outputs are bf16 (one accumulator slot)
+    if (dqw_out != nullptr) small_grad_finish(dqw, ticket, 2 * D, dqw_out, D, dkw_out);
   }
 }
 
@@ -845,7 +870,7 @@ template <int NV, int NS>
 __global__ void __launch_bounds__(128) rmsnorm_bwd_ring_k(
     const bf16* __restrict__ dy, const bf16* __restrict__ x, const bf16* __restrict__ w,
     const float* __restrict__ rstd, const bf16* __restrict__ dres, bf16* __restrict__ dx,
-    float* __restrict__ dw, int T, int H) {
+    float* __restrict__ dw, int T, int H, bf16* dw_out, int* ticket) {
   extern __shared__ __align__(16) unsigned char rn_smem[];
   float* sdw = reinterpret_cast<float*>(rn_smem);  // [H] block partials of d(weight)
   float* sw = sdw + H;                               // [H] weights
@@ -944,6 +969,7 @@ __global__ void __launch_bounds__(128) rmsnorm_bwd_ring_k(
   }
   __syncthreads();
   for (int i = threadIdx.x; i < H; i += blockDim.x) atomicAdd(&dw[i], sdw[i]);
+  if (dw_out != nullptr) small_grad_finish(dw, ticket, H, dw_out, H, nullptr);
 }
 
 }  // namespace
@@ -987,7 +1013,8 @@ void rmsnorm_fwd(const bf16* x, const bf16* w, bf16* y, float* rstd, int64_t T, 
 }
 
 void rmsnorm_bwd(const bf16* dy, const bf16* x, const bf16* w, const float* rstd,
-                 const bf16* dres, bf16* dx, float* dw, int64_t T, int H, cudaStream_t s) {
+                 const bf16* dres, bf16* dx, float* dw, int64_t T, int H, bf16* dw_out,
+                 int* ticket, cudaStream_t s) {
   const int nv = H / 8;
   if (nv <= 128 && T < (int64_t(1) << 31)) {
     const int rows = dres != nullptr ? 3 : 2;
@@ -998,9 +1025,10 @@ void rmsnorm_bwd(const bf16* dy, const bf16* x, const bf16* w, const float* rstd
     auto kern = nv <= 32 ? rmsnorm_bwd_ring_k<1, ns>
                 : nv <= 64 ? rmsnorm_bwd_ring_k<2, ns> : rmsnorm_bwd_ring_k<4, ns>;
     kern<<<ring_grid(kern, smem, T), 128, smem, s>>>(dy, x, w, rstd, dres, dx, dw,
-                                                     static_cast<int>(T), H);
+                                                     static_cast<int>(T), H, dw_out, ticket);
     return;
   }
+  if (dw_out != nullptr) return;  // bf16 outputs exist only on the ring path (checked by callers)
   const int grid = grid_for(T, 8, 148 * 3);
   const size_t sm = 2 * H * sizeof(float);
   if (nv <= 32)
@@ -1080,7 +1108,7 @@ void qk_norm_rope_bwd(const bf16* dq, const bf16* dk, const bf16* dv, const bf16
                       const bf16* qw, const bf16* kw, const float* cos_t, const float* sin_t,
                       const int32_t* pos, const float* rstd, bf16* dkqv, float* dqw, float* dkw,
                       int B, int S, int Hq, int Hkv, int D, bool qk_norm, bool q_tm,
-                      cudaStream_t s) {
+                      bf16* dqw_out, bf16* dkw_out, int* ticket, cudaStream_t s) {
   const int nr = Hq + Hkv;  // bytes; matches the kernel
   const int slot = ((Hq + 2 * Hkv) * D + (qk_norm ? nr * D : 0)) * 2 + D * 4 + ((nr * 4 + 15) & ~15);
   const int64_t T = (int64_t)B * S;
@@ -1089,7 +1117,8 @@ void qk_norm_rope_bwd(const bf16* dq, const bf16* dk, const bf16* dv, const bf16
     const QkLaunch L = qk_launch(qk_norm_rope_bwd_k<DD, 4>, qk_norm_rope_bwd_k<DD, 2>, slot, T); \
     auto kern = L.stages == 4 ? qk_norm_rope_bwd_k<DD, 4> : qk_norm_rope_bwd_k<DD, 2>;          \
     kern<<<L.grid, L.warps * 32, L.smem, s>>>(dq, dk, dv, kqv, qw, kw, cos_t, sin_t, pos, rstd,  \
-                                              dkqv, dqw, dkw, B, S, Hq, Hkv, qk_norm, q_tm);    \
+                                              dkqv, dqw, dkw, B, S, Hq, Hkv, qk_norm, q_tm,     \
+                                              dqw_out, dkw_out, ticket);                        \
   }
   if (D == 64) CFB_QK_BWD(64) else CFB_QK_BWD(128)
 #undef CFB_QK_BWD

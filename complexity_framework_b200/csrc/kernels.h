@@ -12,8 +12,11 @@ using bf16 = __nv_bfloat16;
 void rmsnorm_fwd(const bf16* x, const bf16* w, bf16* y, float* rstd, int64_t T, int H, float eps,
                  cudaStream_t s);
 // dx = rmsnorm'(x)^T dy (+ dres);  dw (fp32, [H]) += sum_rows dy * x*rstd.
+// With dw_out (H <= 1024): dw is a zeroed accumulator slot with a zeroed
+// ticket; the last block writes bf16 dw_out and re-zeroes both.
 void rmsnorm_bwd(const bf16* dy, const bf16* x, const bf16* w, const float* rstd,
-                 const bf16* dres, bf16* dx, float* dw, int64_t T, int H, cudaStream_t s);
+                 const bf16* dres, bf16* dx, float* dw, int64_t T, int H, bf16* dw_out,
+                 int* ticket, cudaStream_t s);
 
 // kqv [T, (2*Hkv+Hq)*D] in k|q|v order -> per-head RMSNorm of q and k, RoPE
 // (rotate-half, cos/sin tables [P, D/2]) and scatter to head-major k/v
@@ -26,7 +29,8 @@ void qk_norm_rope_bwd(const bf16* dq, const bf16* dk, const bf16* dv, const bf16
                       const bf16* qw, const bf16* kw, const float* cos_t, const float* sin_t,
                       const int32_t* pos, const float* rstd, bf16* dkqv, float* dqw, float* dkw,
                       int B, int S, int Hq, int Hkv, int D, bool qk_norm, bool q_tm,
-                      cudaStream_t s);
+                      bf16* dqw_out, bf16* dkw_out, int* ticket, cudaStream_t s);
+// (with dqw_out/dkw_out: dqw is a zeroed [2D] accumulator slot, dkw == dqw + D)
 
 void embedding_fwd(const int64_t* ids, const bf16* table, bf16* out, int64_t T, int H, int64_t V,
                    cudaStream_t s);

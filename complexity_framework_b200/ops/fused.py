@@ -384,6 +384,14 @@ def route_scales(token_ids: torch.Tensor, route_table: torch.Tensor, route_weigh
 
 
 # ------------------------------------------------------------------ RMSNorm
+def _norm_weight_grad(w: torch.Tensor, H: int) -> torch.Tensor:
+    """Output buffer of d(norm weight): bf16, written directly by the kernel's
+    last block, for H <= 1024; a zeroed fp32 accumulator otherwise."""
+    if H <= 1024:
+        return torch.empty(w.numel(), device=w.device, dtype=torch.bfloat16)
+    return torch.zeros(w.numel(), device=w.device, dtype=torch.float32)
+
+
 class RMSNormFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, eps):
@@ -401,7 +409,7 @@ class RMSNormFn(torch.autograd.Function):
         C = require()
         x, w, rstd = ctx.saved_tensors
         dx = torch.empty_like(x)
-        dw = torch.zeros(w.numel(), device=x.device, dtype=torch.float32)
+        dw = _norm_weight_grad(w, x.shape[-1])
         C.rmsnorm_bwd(_c(dy), x, _c(w), rstd, None, dx, dw)
         return dx, dw.to(w.dtype), None
 
@@ -433,10 +441,10 @@ class RMSNormSkipFn(torch.autograd.Function):
     def backward(ctx, dy, dskip):
         C = require()
         x, w, rstd = ctx.saved_tensors
-        dx = torch.empty_like(x)
-        dw = torch.zeros(w.numel(), device=x.device, dtype=torch.float32)
         if dy is None:
             return dskip, None, None
+        dx = torch.empty_like(x)
+        dw = _norm_weight_grad(w, x.shape[-1])
         C.rmsnorm_bwd(_c(dy), x, _c(w), rstd, None if dskip is None else _c(dskip), dx, dw)
         return dx, dw.to(w.dtype), None
 
@@ -478,8 +486,9 @@ class QKNormRopeFn(torch.autograd.Function):
         B, S, Hq, Hkv, D, qk_norm = ctx.meta
         dev = kqv.device
         dkqv = torch.empty_like(kqv)
-        dqw = torch.zeros(D, device=dev, dtype=torch.float32)
-        dkw = torch.zeros(D, device=dev, dtype=torch.float32)
+        # bf16 weight gradients written by the kernel's last block (no fill / cast)
+        dqw = torch.empty(D, device=dev, dtype=torch.bfloat16)
+        dkw = torch.empty(D, device=dev, dtype=torch.bfloat16)
 
         def z(shape):
             return torch.zeros(shape, device=dev, dtype=torch.bfloat16)
@@ -491,6 +500,8 @@ class QKNormRopeFn(torch.autograd.Function):
         C.qk_norm_rope_bwd(dq, dk, dv, kqv, _c(qw), _c(kw), cos, sin, pos, rstd, dkqv, dqw, dkw,
                            B, S, Hq, Hkv, D, qk_norm, True)
         n = None
+        if not qk_norm:  # the weights are not used
+            return (dkqv, n, n, n, n, n, n, n, n, n, n)
         return (dkqv, dqw.to(qw.dtype), dkw.to(kw.dtype), n, n, n, n, n, n, n, n)
 
 

@@ -119,7 +119,7 @@ def case_norms(iters: int) -> None:
             nbytes=nbytes)
     dy = torch.randn_like(x)
     dx = torch.empty_like(x)
-    dw = torch.zeros(H, device="cuda")
+    dw = torch.empty(H, device="cuda", dtype=torch.bfloat16)  # written by the last block
     _report("rmsnorm_bwd_resid", cuda_time(
         lambda: C.rmsnorm_bwd(dy, x, w, rstd, dy, dx, dw), iters), nbytes=4.0 * T * H * 2)
     B, S, Hq, Hkv, D = 16, 2048, 14, 2, 64
@@ -137,9 +137,10 @@ def case_norms(iters: int) -> None:
     _report("qk_norm_rope_fwd", cuda_time(lambda: C.qk_norm_rope_fwd(
         kqv, qw, qw, cos, sin, pos, q, k, v, rs, B, S, Hq, Hkv, D, 1e-6, True, True), iters), nbytes=nb)
     dk = torch.empty_like(kqv)
-    dqw = torch.zeros(D, device="cuda")
+    dqw = torch.empty(D, device="cuda", dtype=torch.bfloat16)
+    dkw = torch.empty(D, device="cuda", dtype=torch.bfloat16)
     _report("qk_norm_rope_bwd", cuda_time(lambda: C.qk_norm_rope_bwd(
-        q, k, v, kqv, qw, qw, cos, sin, pos, rs, dk, dqw, dqw, B, S, Hq, Hkv, D, True, True), iters),
+        q, k, v, kqv, qw, qw, cos, sin, pos, rs, dk, dqw, dkw, B, S, Hq, Hkv, D, True, True), iters),
         nbytes=3.0 * kqv.numel() * 2)
     torch.cuda.synchronize()
     check_errors(0)
