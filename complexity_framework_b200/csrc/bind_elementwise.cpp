@@ -189,6 +189,22 @@ void embedding_fwd(const torch::Tensor& ids, const torch::Tensor& table, torch::
                      static_cast<int>(H), table.size(0), cur());
 }
 
+void embedding_bwd_sorted(const torch::Tensor& sorted_ids, const torch::Tensor& order,
+                          const torch::Tensor& dy, torch::Tensor& dtable) {
+  chk(sorted_ids, torch::kInt64, "sorted_ids");
+  chk(order, torch::kInt64, "order");
+  chk(dy, torch::kBFloat16, "dy");
+  chk(dtable, torch::kFloat32, "dtable");
+  const int64_t H = dtable.size(1);
+  TORCH_CHECK(H % 8 == 0 && H <= 1024, "embedding_bwd_sorted: H % 8 == 0 and H <= 1024");
+  TORCH_CHECK(order.numel() == sorted_ids.numel() && dy.numel() == sorted_ids.numel() * H,
+              "embedding_bwd_sorted sizes");
+  const c10::cuda::CUDAGuard g(dy.device());
+  cfb::embedding_bwd_sorted(P<int64_t>(sorted_ids), P<int64_t>(order), P<bf16>(dy),
+                            P<float>(dtable), sorted_ids.numel(), static_cast<int>(H),
+                            dtable.size(0), cur());
+}
+
 void embedding_bwd(const torch::Tensor& ids, const torch::Tensor& dy, torch::Tensor& dtable) {
   chk(ids, torch::kInt64, "ids");
   chk(dy, torch::kBFloat16, "dy");
@@ -368,6 +384,7 @@ void register_elementwise(pybind11::module& m) {
   m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd);
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
+  m.def("embedding_bwd_sorted", &embedding_bwd_sorted);
   m.def("ce_loss_grad", &ce_loss_grad);
   m.def("route_scales", &route_scales);
   m.def("adamw_flat", &adamw_flat, py::arg("p"), py::arg("m"), py::arg("v"), py::arg("g"),

@@ -613,6 +613,66 @@ __global__ void embedding_bwd_k(const int64_t* __restrict__ ids, const bf16* __r
   }
 }
 
+// Embedding backward over token ids sorted ascending (`order` maps sorted
+// position -> token row): a warp takes 32 consecutive sorted positions,
+// accumulates runs of equal ids in registers and adds each run into dtable
+// with one vector reduction per 4 floats.  Frequent ids (Zipf-distributed
+// text) then cost one atomic row-add per warp instead of one per token.
+template <int NV>
+__global__ void __launch_bounds__(256) embedding_bwd_sorted_k(
+    const int64_t* __restrict__ sorted_ids, const int64_t* __restrict__ order,
+    const bf16* __restrict__ dy, float* __restrict__ dtable, int64_t T, int H, int64_t V) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t p0 = warp * 32;
+  if (p0 >= T) return;
+  const int nv = H / 8;
+  const int64_t pl = p0 + lane;
+  // clamped like the forward; clamped ids still form contiguous runs
+  int64_t my_id = pl < T ? sorted_ids[pl] : 0;
+  my_id = my_id < 0 ? 0 : (my_id >= V ? V - 1 : my_id);
+  const int64_t my_row = pl < T ? order[pl] : 0;
+  const int n = T - p0 < 32 ? static_cast<int>(T - p0) : 32;
+  float acc[NV][8];
+#pragma unroll
+  for (int k = 0; k < NV; ++k)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[k][j] = 0.f;
+  int64_t cur = __shfl_sync(0xffffffffu, my_id, 0);
+  auto flush = [&](int64_t id) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int i = lane + 32 * k;
+      if (i < nv) {
+        float* dst = dtable + id * H + i * 8;
+        red_add_v4(dst, acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
+        red_add_v4(dst + 4, acc[k][4], acc[k][5], acc[k][6], acc[k][7]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[k][j] = 0.f;
+    }
+  };
+  for (int q = 0; q < n; ++q) {
+    const int64_t id = __shfl_sync(0xffffffffu, my_id, q);
+    const int64_t row = __shfl_sync(0xffffffffu, my_row, q);
+    if (id != cur) {  // warp-uniform
+      flush(cur);
+      cur = id;
+    }
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int i = lane + 32 * k;
+      if (i < nv) {
+        float v[8];
+        load8(dy + row * H + i * 8, v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[k][j] += v[j];
+      }
+    }
+  }
+  flush(cur);
+}
+
 // ----------------------------------------------------------------- cross-entropy
 // One 256-thread block per row.  The row's per-128-column partials (max,
 // sum of exp) are combined cooperatively (one partial per thread, then block
@@ -1132,6 +1192,18 @@ void embedding_fwd(const int64_t* ids, const bf16* table, bf16* out, int64_t T, 
 void embedding_bwd(const int64_t* ids, const bf16* dy, float* dtable, int64_t T, int H, int64_t V,
                    cudaStream_t s) {
   embedding_bwd_k<<<grid_for(T * (H / 8), 256), 256, 0, s>>>(ids, dy, dtable, T, H, V);
+}
+
+void embedding_bwd_sorted(const int64_t* sorted_ids, const int64_t* order, const bf16* dy,
+                          float* dtable, int64_t T, int H, int64_t V, cudaStream_t s) {
+  const int nv = H / 8;
+  const unsigned grid = static_cast<unsigned>((T + 255) / 256);  // 8 warps x 32 positions
+  if (nv <= 32)
+    embedding_bwd_sorted_k<1><<<grid, 256, 0, s>>>(sorted_ids, order, dy, dtable, T, H, V);
+  else if (nv <= 64)
+    embedding_bwd_sorted_k<2><<<grid, 256, 0, s>>>(sorted_ids, order, dy, dtable, T, H, V);
+  else
+    embedding_bwd_sorted_k<4><<<grid, 256, 0, s>>>(sorted_ids, order, dy, dtable, T, H, V);
 }
 
 void ce_loss_grad(bf16* logits, const float* stats, int ntiles, const int64_t* targets,

@@ -36,6 +36,10 @@ void embedding_fwd(const int64_t* ids, const bf16* table, bf16* out, int64_t T, 
                    cudaStream_t s);
 void embedding_bwd(const int64_t* ids, const bf16* dy, float* dtable, int64_t T, int H, int64_t V,
                    cudaStream_t s);
+// Same from ids sorted ascending; order[p] = token row of sorted position p.
+// H <= 1024.  dtable fp32 [V, H] (accumulated into).
+void embedding_bwd_sorted(const int64_t* sorted_ids, const int64_t* order, const bf16* dy,
+                          float* dtable, int64_t T, int H, int64_t V, cudaStream_t s);
 
 // Cross-entropy from bf16 logits and per-(row, n-tile) (max, sumexp) partials.
 // Writes loss[row] and overwrites logits with d(loss_sum*scale)/d(logits).

@@ -511,6 +511,17 @@ def qk_norm_rope(kqv, qw, kw, cos, sin, pos, Hq, Hkv, D, eps, qk_norm=True):
 
 # ---------------------------------------------------------------- embedding
 class EmbeddingFn(torch.autograd.Function):
+    """Token embedding lookup.  Backward sorts the ids and sums runs of equal
+    ids per warp before one vector atomic per run.
+
+    Tied LM head: the forward marks ``table``; the fused cross-entropy that
+    later uses the same tensor as its output weight then keeps its fp32
+    weight gradient for this backward (``table._cfb_pending_grad``), which adds
+    the embedding gradient into it and returns the sum with one cast, instead
+    of a zero-filled fp32 table, two casts and autograd's add of two bf16
+    gradients.
+    """
+
     @staticmethod
     def forward(ctx, ids, table):
         C = require()
@@ -520,14 +531,27 @@ class EmbeddingFn(torch.autograd.Function):
         ctx.save_for_backward(ids_c)
         ctx.vshape = table.shape
         ctx.dtype = table.dtype
+        ctx.table = table
+        if ctx.needs_input_grad[1]:
+            table._cfb_embedding_pending = True
         return out
 
     @staticmethod
     def backward(ctx, dy):
         C = require()
         (ids,) = ctx.saved_tensors
-        dtable = torch.zeros(ctx.vshape, device=dy.device, dtype=torch.float32)
-        C.embedding_bwd(ids, _c(dy), dtable)
+        table = ctx.table
+        dtable = getattr(table, "_cfb_pending_grad", None)
+        table._cfb_pending_grad = None
+        table._cfb_embedding_pending = False
+        if dtable is None or tuple(dtable.shape) != tuple(ctx.vshape):
+            dtable = torch.zeros(ctx.vshape, device=dy.device, dtype=torch.float32)
+        H = ctx.vshape[1]
+        if H <= 1024:
+            sorted_ids, order = torch.sort(ids.reshape(-1))
+            C.embedding_bwd_sorted(sorted_ids, order, _c(dy), dtable)
+        else:
+            C.embedding_bwd(ids, _c(dy), dtable)
         return None, dtable.to(ctx.dtype)
 
 
@@ -580,12 +604,22 @@ class LinearCrossEntropyFn(torch.autograd.Function):
         ctx.save_for_backward(dh, dw)
         ctx.hshape = hidden.shape
         ctx.wdtype = weight.dtype
+        # tied LM head: hand the fp32 weight gradient to the embedding backward
+        # (the mark is consumed: one hand-off per embedding forward)
+        ctx.tied = weight if getattr(weight, "_cfb_embedding_pending", False) else None
+        if ctx.tied is not None:
+            weight._cfb_embedding_pending = False
         return loss
 
     @staticmethod
     def backward(ctx, gout):
         dh, dw = ctx.saved_tensors
         dhidden = (dh * gout.to(dh.dtype)).view(ctx.hshape)
+        if ctx.tied is not None:
+            prev = getattr(ctx.tied, "_cfb_pending_grad", None)
+            dw.mul_(gout.float())
+            ctx.tied._cfb_pending_grad = dw if prev is None else prev.add_(dw)
+            return dhidden, None, None, None, None
         dweight = (dw * gout.float()).to(ctx.wdtype)
         return dhidden, dweight, None, None, None
 

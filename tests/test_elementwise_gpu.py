@@ -144,3 +144,32 @@ def test_fused_adamw_matches_torch():
         master = opt.state[p]["master"]
         assert float((master.reshape(r.shape) - r.detach()).abs().max()) < 1e-4
         assert float((p.detach().float() - r.detach()).abs().max()) < 2e-2
+
+
+@pytest.mark.parametrize("H", [256, 896, 2048])
+def test_embedding_backward_sorted_and_tied_head(H):
+    """Embedding grad (sorted-run accumulation, Zipf-like hot ids) and the tied
+    LM-head hand-off (CE weight gradient summed into the embedding backward)
+    against torch."""
+    import torch.nn.functional as F
+
+    from complexity_framework_b200.ops.fused import embedding, linear_cross_entropy
+
+    torch.manual_seed(0)
+    V, T = 1024, 4096
+    ids = torch.randint(0, V, (T,), device="cuda")
+    ids[::3] = 7  # a hot id
+    ids[1::5] = 0
+    w = (0.05 * torch.randn(V, H, device="cuda")).bfloat16().requires_grad_()
+    tgt = torch.randint(0, V, (T,), device="cuda")
+    x = embedding(ids.view(4, -1), w)
+    h = (x.float() * 1.5).bfloat16().reshape(T, H)
+    loss = linear_cross_entropy(h, w, tgt)
+    loss.backward()
+    wr = w.detach().float().requires_grad_()
+    hr = wr[ids] * 1.5
+    lr = F.cross_entropy(hr @ wr.t(), tgt)
+    lr.backward()
+    err = float((w.grad.float() - wr.grad).abs().max() / wr.grad.abs().max())
+    assert err < 3e-2, err
+    assert getattr(w, "_cfb_pending_grad", None) is None
