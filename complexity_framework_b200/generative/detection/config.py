@@ -1,0 +1,67 @@
+"""Detector configuration (counterpart: complexity/generative/detection/config.py
+``TRHashDetectorConfig`` and presets.py ``coco_v8_nano_config``)."""
+from __future__ import annotations
+
+from dataclasses import asdict, dataclass, field
+from typing import Tuple
+
+
+@dataclass
+class TRHashDetectorConfig:
+    image_size: int = 320
+    patch_size: int = 16
+    num_channels: int = 3
+    hidden_size: int = 192
+    num_layers: int = 4
+    num_heads: int = 6
+    num_experts: int = 4
+    top_k: int = 2
+    shared_width: int = 384
+    expert_width: int = 64
+    num_classes: int = 80
+    neck_channels: int = 128
+    reg_max: int = 16                  # distribution bins per box side (DFL)
+    # task-aligned assignment (score^alpha * IoU^beta, top-k candidates per object)
+    assign_topk: int = 10
+    assign_alpha: float = 0.5
+    assign_beta: float = 6.0
+    loss_weights: Tuple[float, float, float] = (1.0, 7.5, 1.5)  # cls, box (CIoU), dfl
+    score_threshold: float = 0.05
+    nms_iou: float = 0.6
+    max_detections: int = 300
+    class_names: Tuple[str, ...] = field(default_factory=tuple)
+
+    def __post_init__(self):
+        if self.image_size % (2 * self.patch_size):
+            raise ValueError("image_size must be a multiple of 2 * patch_size")
+
+    @property
+    def strides(self) -> Tuple[int, int, int]:
+        return (self.patch_size // 2, self.patch_size, self.patch_size * 2)
+
+    def to_dict(self) -> dict:
+        d = asdict(self)
+        d["class_names"] = list(self.class_names)
+        d["loss_weights"] = list(self.loss_weights)
+        return d
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "TRHashDetectorConfig":
+        d = dict(d)
+        d["class_names"] = tuple(d.get("class_names", ()))
+        d["loss_weights"] = tuple(d.get("loss_weights", (1.0, 7.5, 1.5)))
+        return cls(**d)
+
+
+COCO_V8_NANO_NAME = "tr-hash-det-coco-nano"
+
+
+def coco_v8_nano_config(**overrides) -> TRHashDetectorConfig:
+    """Small COCO preset (80 classes, 640 px input)."""
+    from .data import COCO_CLASS_NAMES
+
+    base = dict(image_size=640, patch_size=16, hidden_size=256, num_layers=6, num_heads=8,
+                shared_width=512, expert_width=96, num_classes=80, neck_channels=128,
+                class_names=tuple(COCO_CLASS_NAMES))
+    base.update(overrides)
+    return TRHashDetectorConfig(**base)

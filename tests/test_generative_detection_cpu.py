@@ -1,0 +1,110 @@
+"""TR-Hash detector: box ops, losses, letterboxing, COCO-style metric, training,
+checkpoint and TorchScript export (CPU)."""
+import torch
+
+from complexity_framework_b200.generative.detection import (
+    DetectorTrainer, DetectorTrainingConfig, SyntheticShapesDataset, TRHashDetectorConfig,
+    TRHashObjectDetector, box_iou, class_aware_nms, collate_detection, complete_iou,
+    distribution_focal_loss, evaluate_detections, export_detector_torchscript, greedy_nms,
+    load_detector_checkpoint, preprocess_detector_image, quality_focal_loss,
+    restore_detector_boxes, save_detector_checkpoint)
+
+
+def _brute_nms(boxes, scores, t):
+    order = scores.argsort(descending=True).tolist()
+    keep = []
+    for i in order:
+        if all(box_iou(boxes[i:i + 1], boxes[j:j + 1])[0, 0] <= t for j in keep):
+            keep.append(i)
+    return keep
+
+
+def test_nms_matches_sequential_definition():
+    g = torch.Generator().manual_seed(0)
+    xy = torch.rand(60, 2, generator=g) * 50
+    wh = torch.rand(60, 2, generator=g) * 30 + 5
+    boxes = torch.cat([xy, xy + wh], 1)
+    scores = torch.rand(60, generator=g)
+    assert greedy_nms(boxes, scores, 0.5).tolist() == _brute_nms(boxes, scores, 0.5)
+    cls = torch.randint(0, 3, (60,), generator=g)
+    keep = class_aware_nms(boxes, scores, cls, 0.5)
+    for c in range(3):  # per class it is plain NMS
+        idx = (cls == c).nonzero().squeeze(1)
+        ref = idx[torch.tensor(_brute_nms(boxes[idx], scores[idx], 0.5), dtype=torch.long)]
+        assert sorted(keep[cls[keep] == c].tolist()) == sorted(ref.tolist())
+
+
+def test_iou_and_ciou():
+    a = torch.tensor([[0., 0., 10., 10.]])
+    b = torch.tensor([[5., 0., 15., 10.]])
+    assert abs(float(box_iou(a, b)) - 50 / 150) < 1e-6
+    assert abs(float(complete_iou(a[0], a[0])) - 1.0) < 1e-5
+    # same IoU, farther centres -> lower CIoU
+    assert float(complete_iou(a[0], b[0])) < float(box_iou(a, b))
+
+
+def test_focal_losses():
+    x = torch.tensor([[2.0, -3.0]])
+    assert float(quality_focal_loss(x, torch.sigmoid(x))) < 1e-6
+    d = torch.full((1, 16), -10.0)
+    d[0, 3] = 10.0
+    assert float(distribution_focal_loss(d, torch.tensor([3.0]))) < 1e-3
+    assert float(distribution_focal_loss(d, torch.tensor([3.5]))) > 1.0
+
+
+def test_letterbox_round_trip():
+    img = torch.rand(3, 60, 100)
+    out, meta = preprocess_detector_image(img, 128)
+    assert out.shape == (3, 128, 128)
+    b = torch.tensor([[10., 5., 50., 40.]])
+    lb = b.clone()
+    lb[:, [0, 2]] = lb[:, [0, 2]] * meta.scale + meta.pad_x
+    lb[:, [1, 3]] = lb[:, [1, 3]] * meta.scale + meta.pad_y
+    assert torch.allclose(restore_detector_boxes(lb, meta), b, atol=1e-4)
+
+
+def test_coco_metric_known_cases():
+    gt = [{"boxes": torch.tensor([[0., 0., 10., 10.], [20., 20., 30., 30.]]),
+           "labels": torch.tensor([0, 1])}]
+    perfect = [{"boxes": gt[0]["boxes"], "scores": torch.tensor([0.9, 0.8]),
+                "labels": torch.tensor([0, 1])}]
+    assert abs(evaluate_detections(perfect, gt, 2)["mAP"] - 1.0) < 1e-9
+    half = [{"boxes": torch.tensor([[0., 0., 10., 10.]]), "scores": torch.tensor([0.9]),
+             "labels": torch.tensor([0])}]
+    r = evaluate_detections(half, gt, 2)
+    assert abs(r["AP50"] - 0.5) < 1e-9  # class 0 found, class 1 missed
+
+
+def _small():
+    return TRHashDetectorConfig(image_size=64, patch_size=16, hidden_size=64, num_layers=1,
+                                num_heads=4, shared_width=128, expert_width=32, num_classes=2,
+                                neck_channels=32)
+
+
+def test_detector_trains_and_predicts(tmp_path):
+    torch.manual_seed(0)
+    m = TRHashObjectDetector(_small())
+    dl = torch.utils.data.DataLoader(SyntheticShapesDataset(32, 64, 2, 2), batch_size=8,
+                                     collate_fn=collate_detection)
+    tr = DetectorTrainer(m, DetectorTrainingConfig(learning_rate=2e-3, warmup_steps=4,
+                                                   max_steps=40, ema_tau=5))
+    ev = torch.utils.data.DataLoader(SyntheticShapesDataset(16, 64, 2, 2, seed=7), batch_size=8,
+                                     collate_fn=collate_detection)
+    before = tr.evaluate(ev, use_ema=False)["AP50"]
+    for _ in range(10):
+        for im, tg in dl:
+            tr.train_step(im, tg)
+    after = tr.evaluate(ev, use_ema=False)["AP50"]
+    # the loss is IoU-weighted (it grows as boxes start to overlap), so judge by AP
+    assert after > max(0.2, before), (before, after)
+    out = m.predict(torch.rand(2, 3, 64, 64))
+    assert len(out) == 2 and set(out[0]) == {"boxes", "scores", "labels"}
+    save_detector_checkpoint(m, str(tmp_path / "det"))
+    m2 = load_detector_checkpoint(str(tmp_path / "det"))
+    x = torch.rand(1, 3, 64, 64)
+    m.eval()
+    assert torch.allclose(m(x)["boxes"], m2(x)["boxes"], atol=1e-5)
+    path = export_detector_torchscript(m, str(tmp_path / "det.pt"))
+    scores, boxes = torch.jit.load(path)(x)
+    assert torch.allclose(boxes, m(x)["boxes"], atol=1e-4)
+    assert scores.shape[-1] == 2
