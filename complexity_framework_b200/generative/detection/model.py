@@ -81,7 +81,13 @@ class TRHashObjectDetector(nn.Module):
 
     def forward(self, images: torch.Tensor,
                 targets: Optional[List[Dict[str, torch.Tensor]]] = None) -> Dict:
-        feats = self.features(images)
+        out = self.raw_outputs(self.features(images))
+        if targets is not None:
+            out.update(self.loss(out, targets))
+        return out
+
+    def raw_outputs(self, feats: List[torch.Tensor]) -> Dict:
+        """Per-point class logits, box distributions and decoded boxes of all levels."""
         cls, reg = [], []
         for f in feats:
             c, r = self.head(f)
@@ -94,17 +100,14 @@ class TRHashObjectDetector(nn.Module):
         dist = reg.view(B, A, 4, self.config.reg_max)
         ltrb = (dist.softmax(-1) * self.bins).sum(-1) * strides[None, :, None]
         boxes = torch.cat([points - ltrb[..., :2], points + ltrb[..., 2:]], -1)
-        out = {"cls_logits": cls, "box_dist": dist, "boxes": boxes, "points": points,
-               "strides": strides}
-        if targets is not None:
-            out.update(self.loss(out, targets))
-        return out
+        return {"cls_logits": cls, "box_dist": dist, "boxes": boxes, "points": points,
+                "strides": strides, "features": feats}
 
     # ------------------------------------------------------------ assignment
     @torch.no_grad()
     def assign(self, scores, boxes, points, gt_boxes, gt_labels):
         """Per image: (fg mask [A], target boxes [A, 4], target labels [A], soft
-        class-target values [A])."""
+        class-target values [A], matched object index [A])."""
         c = self.config
         A = points.shape[0]
         dev = points.device
@@ -113,7 +116,7 @@ class TRHashObjectDetector(nn.Module):
         tlab = torch.zeros(A, dtype=torch.long, device=dev)
         tval = torch.zeros(A, device=dev)
         if gt_boxes.numel() == 0:
-            return fg, tbox, tlab, tval
+            return fg, tbox, tlab, tval, torch.zeros(A, dtype=torch.long, device=dev)
         inside = ((points[None, :, 0] > gt_boxes[:, None, 0]) & (points[None, :, 0] < gt_boxes[:, None, 2])
                   & (points[None, :, 1] > gt_boxes[:, None, 1]) & (points[None, :, 1] < gt_boxes[:, None, 3]))
         iou = box_iou(gt_boxes, boxes).clamp_min(0)                  # [G, A]
@@ -138,7 +141,7 @@ class TRHashObjectDetector(nn.Module):
         align = align * cand
         norm = align / align.amax(1, keepdim=True).clamp_min(1e-9) * (iou * cand).amax(1, keepdim=True)
         tval = norm.gather(0, g[None]).squeeze(0) * fg
-        return fg, tbox, tlab, tval
+        return fg, tbox, tlab, tval, g
 
     def loss(self, out: Dict, targets: List[Dict[str, torch.Tensor]]) -> Dict[str, torch.Tensor]:
         c = self.config
@@ -146,10 +149,12 @@ class TRHashObjectDetector(nn.Module):
         points, strides = out["points"], out["strides"]
         scores = cls.detach().sigmoid()
         l_cls, l_box, l_dfl, norm = cls.new_zeros(()), cls.new_zeros(()), cls.new_zeros(()), 0.0
+        parts_extra: Dict[str, torch.Tensor] = {}
         for b, t in enumerate(targets):
             gb = t["boxes"].to(boxes.device, torch.float32)
             gl = t["labels"].to(boxes.device, torch.long)
-            fg, tbox, tlab, tval = self.assign(scores[b], boxes[b].detach(), points, gb, gl)
+            fg, tbox, tlab, tval, gidx = self.assign(scores[b], boxes[b].detach(), points, gb, gl)
+            self.extra_loss_terms(out, b, t, fg, gidx, tval, parts_extra)
             target = torch.zeros_like(cls[b])
             if fg.any():
                 target[fg, tlab[fg]] = tval[fg]
@@ -168,7 +173,14 @@ class TRHashObjectDetector(nn.Module):
         wc, wb, wd = c.loss_weights
         parts = {"loss_cls": l_cls / norm, "loss_box": l_box / norm, "loss_dfl": l_dfl / norm}
         parts["loss"] = wc * parts["loss_cls"] + wb * parts["loss_box"] + wd * parts["loss_dfl"]
+        for k, v in parts_extra.items():  # task heads of subclasses (masks, angles)
+            parts[k] = v / len(targets)
+            parts["loss"] = parts["loss"] + parts[k]
         return parts
+
+    def extra_loss_terms(self, out, b, target, fg, gidx, tval, acc) -> None:
+        """Hook for task heads built on the detector: add per-image loss terms to
+        ``acc`` (summed over images, divided by the batch size)."""
 
     # ---------------------------------------------------------- postprocess
     @torch.no_grad()
