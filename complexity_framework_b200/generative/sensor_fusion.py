@@ -1,0 +1,255 @@
+"""Multimodal sensor fusion classifier (robot / activity perception).
+
+Counterpart: complexity/generative/sensor_fusion/ (config.py
+``SENSOR_MODALITIES`` / ``TRHashSensorFusionConfig``, model.py
+``TRHashSensorFusionBlock`` / ``TRHashSensorFusionClassifier``, folds.py
+``CrossSubjectFold`` / ``resolve_cross_subject_fold``, cuhkx_records.py
+``subject_disjoint_records`` and the dataset / manifest helpers).
+
+Six streams: depth, infrared and thermal clips share one TR-Hash vision
+tower (each frame -> patch features -> pooled to a small token grid, averaged
+over time); IMU, radar and skeleton sequences are projected and pooled to a
+fixed number of tokens.  Tokens of all present streams (missing ones are
+simply absent) get modality embeddings and pass through TR-Hash blocks routed
+by ``(modality, local token position)``; the prediction mixes the fused head
+with the mean of per-modality heads (``late_fusion_weight``).
+"""
+from __future__ import annotations
+
+import json
+import random
+from dataclasses import asdict, dataclass, field
+from typing import Dict, Iterable, List, Mapping, Optional, Sequence, Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .towers import TRHashVisionBlock, TRHashVisionTower, TRHashVisionTowerConfig
+
+SENSOR_MODALITIES: Tuple[str, ...] = ("depth", "ir", "thermal", "imu", "radar", "skeleton")
+VISUAL_MODALITIES = ("depth", "ir", "thermal")
+
+
+@dataclass
+class TRHashSensorFusionConfig:
+    num_classes: int = 40
+    hidden_size: int = 256
+    num_hidden_layers: int = 4
+    num_attention_heads: int = 8
+    num_experts: int = 8
+    top_k: int = 2
+    shared_width: int = 256
+    expert_width: int = 128
+    route_seed: int = 0x71D5A17
+    dropout: float = 0.0
+    classifier_dropout: float = 0.1
+    visual_channels: Tuple[int, int, int] = (3, 1, 3)   # depth, ir, thermal
+    visual_token_grid: int = 4
+    vision_image_size: int = 64
+    vision_patch_size: int = 8
+    vision_hidden_size: int = 128
+    vision_layers: int = 2
+    vision_heads: int = 4
+    late_fusion_weight: float = 0.5
+    imu_features: int = 45
+    radar_features: int = 16
+    skeleton_joints: int = 17
+    skeleton_coordinates: int = 3
+    sequence_tokens: int = 32
+
+    @property
+    def tokens_per_stream(self) -> int:
+        return max(self.visual_token_grid ** 2, self.sequence_tokens)
+
+    @property
+    def route_vocab_size(self) -> int:
+        return len(SENSOR_MODALITIES) * self.tokens_per_stream
+
+    # TRHashVisionBlock reads these names
+    @property
+    def num_heads(self) -> int:
+        return self.num_attention_heads
+
+    def to_dict(self) -> dict:
+        return asdict(self)
+
+
+class TRHashSensorFusionBlock(TRHashVisionBlock):
+    """Attention over all streams' tokens, then the routed FFN (route id =
+    modality index * tokens_per_stream + local position)."""
+
+    def __init__(self, config: TRHashSensorFusionConfig, layer_index: int):
+        super().__init__(config, layer_index)
+
+
+class TRHashSensorFusionClassifier(nn.Module):
+    def __init__(self, config: TRHashSensorFusionConfig):
+        super().__init__()
+        self.config = c = config
+        H = c.hidden_size
+        # the visual streams share one tower; each stream's channels map to 3
+        self.vision = TRHashVisionTower(TRHashVisionTowerConfig(
+            image_size=c.vision_image_size, patch_size=c.vision_patch_size, num_channels=3,
+            hidden_size=c.vision_hidden_size, num_layers=c.vision_layers,
+            num_heads=c.vision_heads, num_experts=4, top_k=2, shared_width=2 * c.vision_hidden_size,
+            expert_width=max(16, c.vision_hidden_size // 4), use_cls_token=False))
+        self.visual_in = nn.ModuleDict({m: nn.Conv2d(ch, 3, 1)
+                                        for m, ch in zip(VISUAL_MODALITIES, c.visual_channels)})
+        self.visual_proj = nn.Linear(c.vision_hidden_size, H)
+        self.seq_in = nn.ModuleDict({
+            "imu": nn.Linear(c.imu_features, H),
+            "radar": nn.Linear(c.radar_features, H),
+            "skeleton": nn.Linear(c.skeleton_joints * c.skeleton_coordinates, H)})
+        self.modality = nn.Embedding(len(SENSOR_MODALITIES), H)
+        self.pos = nn.Parameter(torch.randn(1, c.tokens_per_stream, H) * 0.02)
+        self.blocks = nn.ModuleList(TRHashSensorFusionBlock(c, i) for i in range(c.num_hidden_layers))
+        self.norm = nn.LayerNorm(H)
+        self.drop = nn.Dropout(c.classifier_dropout)
+        self.head = nn.Linear(H, c.num_classes)
+        self.stream_heads = nn.ModuleDict({m: nn.Linear(H, c.num_classes) for m in SENSOR_MODALITIES})
+
+    def _visual_tokens(self, m: str, clip: torch.Tensor) -> torch.Tensor:
+        """[B, T, C, H, W] -> [B, grid^2, hidden]."""
+        B, T = clip.shape[:2]
+        frames = self.visual_in[m](clip.flatten(0, 1).to(self.visual_proj.weight.dtype))
+        if frames.shape[-1] != self.config.vision_image_size:
+            frames = F.interpolate(frames, size=(self.config.vision_image_size,) * 2,
+                                   mode="bilinear", align_corners=False)
+        f = self.vision.patch_features(frames)                      # [B*T, D, g, g]
+        g = self.config.visual_token_grid
+        f = F.adaptive_avg_pool2d(f, g).view(B, T, -1, g * g).mean(1)
+        return self.visual_proj(f.transpose(1, 2))
+
+    def _sequence_tokens(self, m: str, seq: torch.Tensor) -> torch.Tensor:
+        """[B, T, F] (skeleton [B, T, J, 3]) -> [B, sequence_tokens, hidden]."""
+        if seq.dim() == 4:
+            seq = seq.flatten(2)
+        x = self.seq_in[m](seq.to(self.visual_proj.weight.dtype))
+        return F.adaptive_avg_pool1d(x.transpose(1, 2), self.config.sequence_tokens).transpose(1, 2)
+
+    def forward(self, inputs: Mapping[str, torch.Tensor],
+                labels: Optional[torch.Tensor] = None) -> Dict[str, torch.Tensor]:
+        c = self.config
+        toks, ids, spans = [], [], []
+        for mi, m in enumerate(SENSOR_MODALITIES):
+            x = inputs.get(m)
+            if x is None:
+                continue
+            t = self._visual_tokens(m, x) if m in VISUAL_MODALITIES else self._sequence_tokens(m, x)
+            n = t.shape[1]
+            t = t + self.modality.weight[mi].to(t.dtype) + self.pos[:, :n].to(t.dtype)
+            spans.append((m, sum(s.shape[1] for s in toks), n))
+            toks.append(t)
+            ids.append(torch.arange(n, device=t.device) + mi * c.tokens_per_stream)
+        if not toks:
+            raise ValueError(f"no sensor stream given; expected some of {SENSOR_MODALITIES}")
+        x = torch.cat(toks, 1)
+        route = torch.cat(ids).unsqueeze(0).expand(x.shape[0], -1)
+        for blk in self.blocks:
+            x = blk(x, route)
+        x = self.norm(x)
+        fused = self.head(self.drop(x.mean(1)))
+        per = torch.stack([self.stream_heads[m](x[:, s:s + n].mean(1)) for m, s, n in spans]).mean(0)
+        w = c.late_fusion_weight
+        logits = (1 - w) * fused + w * per
+        out = {"logits": logits, "fused_logits": fused, "stream_logits": per}
+        if labels is not None:
+            out["loss"] = F.cross_entropy(logits.float(), labels)
+        return out
+
+
+def load_pretrained_visual_tower(model: TRHashSensorFusionClassifier,
+                                 tower_state: Mapping[str, torch.Tensor], strict: bool = False):
+    """Initialise the shared visual tower from a vision checkpoint's tower weights
+    (keys with or without a ``tower.`` prefix); returns the load result."""
+    sd = {k[len("tower."):] if k.startswith("tower.") else k: v for k, v in tower_state.items()}
+    own = model.vision.state_dict()
+    sd = {k: v for k, v in sd.items() if k in own and own[k].shape == v.shape}
+    return model.vision.load_state_dict(sd, strict=strict)
+
+
+# ------------------------------------------------------------- data splits
+@dataclass(frozen=True)
+class CrossSubjectFold:
+    name: str
+    train_subjects: Tuple[int, ...]
+    val_subjects: Tuple[int, ...]
+
+
+def make_cross_subject_folds(subjects: Sequence[int], k: int) -> List[CrossSubjectFold]:
+    """``k`` folds over sorted subjects; fold i validates on every k-th subject
+    starting at i, so each subject is validated exactly once."""
+    s = sorted(set(subjects))
+    out = []
+    for i in range(k):
+        val = tuple(s[i::k])
+        out.append(CrossSubjectFold(f"fold{i}", tuple(x for x in s if x not in val), val))
+    return out
+
+
+def validate_cross_subject_folds(folds: Sequence[CrossSubjectFold]) -> None:
+    seen = set()
+    for f in folds:
+        if set(f.train_subjects) & set(f.val_subjects):
+            raise ValueError(f"{f.name}: a subject is in both train and validation")
+        if set(f.val_subjects) & seen:
+            raise ValueError(f"{f.name}: a subject is validated by two folds")
+        seen |= set(f.val_subjects)
+
+
+def resolve_cross_subject_fold(name: str, folds: Sequence[CrossSubjectFold]) -> CrossSubjectFold:
+    for f in folds:
+        if f.name == name:
+            return f
+    raise KeyError(f"unknown fold {name!r}; known: {[f.name for f in folds]}")
+
+
+@dataclass
+class SensorRecord:
+    """One labelled sample: per-modality tensor files (``.pt``), label, subject."""
+    files: Dict[str, str]
+    label: int
+    subject: int
+    meta: Dict[str, str] = field(default_factory=dict)
+
+
+def save_sensor_manifest(records: Iterable[SensorRecord], path: str) -> None:
+    with open(path, "w") as f:
+        json.dump([asdict(r) for r in records], f, indent=1)
+
+
+def load_sensor_manifest(path: str) -> List[SensorRecord]:
+    with open(path) as f:
+        return [SensorRecord(**d) for d in json.load(f)]
+
+
+def subject_disjoint_records(records: Sequence[SensorRecord], val_fraction: float = 0.2,
+                             seed: int = 0) -> Tuple[List[SensorRecord], List[SensorRecord]]:
+    """Split so that no subject appears on both sides."""
+    subjects = sorted({r.subject for r in records})
+    rng = random.Random(seed)
+    rng.shuffle(subjects)
+    n_val = max(1, round(len(subjects) * val_fraction)) if len(subjects) > 1 else 0
+    val = set(subjects[:n_val])
+    return [r for r in records if r.subject not in val], [r for r in records if r.subject in val]
+
+
+class SensorDataset(torch.utils.data.Dataset):
+    def __init__(self, records: Sequence[SensorRecord]):
+        self.records = list(records)
+
+    def __len__(self):
+        return len(self.records)
+
+    def __getitem__(self, i):
+        r = self.records[i]
+        x = {m: torch.load(p, weights_only=True) for m, p in r.files.items()}
+        return x, r.label
+
+
+def collate_sensors(samples: Sequence) -> Tuple[Dict[str, torch.Tensor], torch.Tensor]:
+    """Stacks each modality present in every sample of the batch."""
+    common = set.intersection(*(set(s[0]) for s in samples))
+    batch = {m: torch.stack([s[0][m] for s in samples]) for m in sorted(common)}
+    return batch, torch.tensor([s[1] for s in samples], dtype=torch.long)
