@@ -12,6 +12,8 @@ from .audio import (AudioEncoder, AudioEncoderConfig, LogMelSpectrogram, TRHashA
                     TRHashSpeechToText, TRHashSpeechToTextConfig, TRHashTextToSpeech,
                     build_mel_filterbank)
 from .detection import TRHashDetectorConfig, TRHashObjectDetector
+from .hierarchical import (HierarchicalTowerConfig, HierarchicalTRHashVisionClassifier,
+                           HierarchicalTRHashVisionTower)
 from .image import (FrozenAutoencoderKL, TRHashImageConfig, TRHashImageEditConfig,
                     TRHashImageEditor, TRHashTextToImage)
 from .prefix_lm import PrefixLM, TokenResampler
@@ -41,4 +43,5 @@ __all__ = [
     "TRHashSemanticSegmenter", "create_vision_model", "load_vision_task_checkpoint",
     "save_vision_task_checkpoint", "FrozenAutoencoderKL", "TRHashImageConfig",
     "TRHashImageEditConfig", "TRHashImageEditor", "TRHashTextToImage",
+    "HierarchicalTowerConfig", "HierarchicalTRHashVisionTower", "HierarchicalTRHashVisionClassifier",
 ]

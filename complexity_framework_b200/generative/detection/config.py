@@ -30,19 +30,32 @@ class TRHashDetectorConfig:
     nms_iou: float = 0.6
     max_detections: int = 300
     class_names: Tuple[str, ...] = field(default_factory=tuple)
+    # "plain": one ViT-style tower at stride patch_size with a derived pyramid;
+    # "hierarchical": the windowed multi-stage tower (real stride 8/16/32 maps)
+    backbone: str = "plain"
+    hier_dims: Tuple[int, ...] = (64, 128, 256, 384)
+    hier_depths: Tuple[int, ...] = (1, 1, 2, 1)
+    hier_heads: Tuple[int, ...] = (2, 4, 8, 12)
+    hier_window: int = 8
 
     def __post_init__(self):
-        if self.image_size % (2 * self.patch_size):
+        if self.backbone not in ("plain", "hierarchical"):
+            raise ValueError("backbone must be 'plain' or 'hierarchical'")
+        if self.backbone == "plain" and self.image_size % (2 * self.patch_size):
             raise ValueError("image_size must be a multiple of 2 * patch_size")
+        if self.backbone == "hierarchical" and self.image_size % 32:
+            raise ValueError("the hierarchical backbone needs image_size % 32 == 0")
 
     @property
     def strides(self) -> Tuple[int, int, int]:
+        if self.backbone == "hierarchical":
+            return (8, 16, 32)
         return (self.patch_size // 2, self.patch_size, self.patch_size * 2)
 
     def to_dict(self) -> dict:
         d = asdict(self)
-        d["class_names"] = list(self.class_names)
-        d["loss_weights"] = list(self.loss_weights)
+        for k in ("class_names", "loss_weights", "hier_dims", "hier_depths", "hier_heads"):
+            d[k] = list(d[k])
         return d
 
     @classmethod
@@ -50,6 +63,9 @@ class TRHashDetectorConfig:
         d = dict(d)
         d["class_names"] = tuple(d.get("class_names", ()))
         d["loss_weights"] = tuple(d.get("loss_weights", (1.0, 7.5, 1.5)))
+        for k in ("hier_dims", "hier_depths", "hier_heads"):
+            if k in d:
+                d[k] = tuple(d[k])
         return cls(**d)
 
 

@@ -48,12 +48,26 @@ class TRHashObjectDetector(nn.Module):
     def __init__(self, config: TRHashDetectorConfig):
         super().__init__()
         self.config = c = config
+        C = c.neck_channels
+        if c.backbone == "hierarchical":
+            from ..hierarchical import HierarchicalTowerConfig, HierarchicalTRHashVisionTower
+
+            self.tower = HierarchicalTRHashVisionTower(HierarchicalTowerConfig(
+                image_size=c.image_size, num_channels=c.num_channels, dims=c.hier_dims,
+                depths=c.hier_depths, heads=c.hier_heads, window_size=c.hier_window,
+                num_experts=c.num_experts, top_k=c.top_k))
+            # top-down pyramid over the stride 8 / 16 / 32 stage maps
+            self.laterals = nn.ModuleList(_conv(d, C, 1) for d in c.hier_dims[1:4])
+            self.smooth = nn.ModuleList(_conv(C, C) for _ in range(3))
+            self.head = DetectionHead(C, c.num_classes, c.reg_max)
+            self.register_buffer("bins", torch.arange(c.reg_max, dtype=torch.float32),
+                                 persistent=False)
+            return
         self.tower = TRHashVisionTower(TRHashVisionTowerConfig(
             image_size=c.image_size, patch_size=c.patch_size, num_channels=c.num_channels,
             hidden_size=c.hidden_size, num_layers=c.num_layers, num_heads=c.num_heads,
             num_experts=c.num_experts, top_k=c.top_k, shared_width=c.shared_width,
             expert_width=c.expert_width, use_cls_token=False))
-        C = c.neck_channels
         self.lateral = _conv(c.hidden_size, C, 1)
         self.up = _conv(C, C)
         self.down = _conv(C, C, 3, 2)
@@ -63,6 +77,12 @@ class TRHashObjectDetector(nn.Module):
 
     # --------------------------------------------------------------- forward
     def features(self, images: torch.Tensor) -> List[torch.Tensor]:
+        if self.config.backbone == "hierarchical":
+            s8, s16, s32 = self.tower(images)[1:4]
+            p5 = self.laterals[2](s32)
+            p4 = self.laterals[1](s16) + F.interpolate(p5, size=s16.shape[-2:], mode="nearest")
+            p3 = self.laterals[0](s8) + F.interpolate(p4, size=s8.shape[-2:], mode="nearest")
+            return [self.smooth[0](p3), self.smooth[1](p4), self.smooth[2](p5)]
         p4 = self.lateral(self.tower.patch_features(images))
         p3 = self.up(F.interpolate(p4, scale_factor=2.0, mode="nearest"))
         p5 = self.down(p4)

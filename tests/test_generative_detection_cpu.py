@@ -108,3 +108,54 @@ def test_detector_trains_and_predicts(tmp_path):
     scores, boxes = torch.jit.load(path)(x)
     assert torch.allclose(boxes, m(x)["boxes"], atol=1e-4)
     assert scores.shape[-1] == 2
+
+
+def test_hierarchical_tower_and_detector(tmp_path):
+    from complexity_framework_b200.generative.hierarchical import (
+        HierarchicalTowerConfig, HierarchicalTRHashVisionClassifier, HierarchicalTRHashVisionTower)
+
+    torch.manual_seed(0)
+    hc = HierarchicalTowerConfig(image_size=64, dims=(32, 64, 64, 96), depths=(2, 1, 2, 1),
+                                 heads=(2, 2, 4, 4), window_size=4)
+    maps = HierarchicalTRHashVisionTower(hc)(torch.rand(2, 3, 64, 64))
+    assert [tuple(m.shape[1:]) for m in maps] == [(32, 16, 16), (64, 8, 8), (64, 4, 4), (96, 2, 2)]
+    # other resolutions: positions are interpolated
+    maps = HierarchicalTRHashVisionTower(hc)(torch.rand(1, 3, 96, 64))
+    assert tuple(maps[0].shape[-2:]) == (24, 16)
+    clf = HierarchicalTRHashVisionClassifier(hc, 3)
+    clf(torch.rand(2, 3, 64, 64), torch.tensor([0, 1]))["loss"].backward()
+    cfg = TRHashDetectorConfig(image_size=64, backbone="hierarchical", hier_dims=(32, 64, 64, 96),
+                               hier_depths=(1, 1, 1, 1), hier_heads=(2, 2, 4, 4), hier_window=4,
+                               num_classes=2, neck_channels=32)
+    det = TRHashObjectDetector(cfg)
+    dl = torch.utils.data.DataLoader(SyntheticShapesDataset(16, 64, 2, 2), batch_size=8,
+                                     collate_fn=collate_detection)
+    tr = DetectorTrainer(det, DetectorTrainingConfig(warmup_steps=2, max_steps=10))
+    for im, tg in dl:
+        assert all(torch.isfinite(torch.tensor(v)) for v in tr.train_step(im, tg).values())
+    save_detector_checkpoint(det, str(tmp_path / "h"))
+    back = load_detector_checkpoint(str(tmp_path / "h"))
+    det.eval()
+    x = torch.rand(1, 3, 64, 64)
+    assert torch.allclose(det(x)["boxes"], back(x)["boxes"], atol=1e-5)
+
+
+def test_window_padding_is_masked():
+    """A 3x3 grid in one 4x4 window (7 padded slots) attends exactly like the
+    same attention over the 9 real tokens."""
+    import torch.nn.functional as F
+
+    from complexity_framework_b200.generative.hierarchical import (HierarchicalBlock,
+                                                                   HierarchicalTowerConfig)
+
+    torch.manual_seed(0)
+    blk = HierarchicalBlock(16, 2, 4, False, HierarchicalTowerConfig(), 64, 0)
+    x = torch.randn(2, 9, 16)
+    win, mask, Hp, Wp = blk._windows(blk.n1(x), 3, 3)
+    got = blk._unwindows(blk.attn(win, mask), 2, 3, 3, Hp, Wp)
+    a = blk.attn
+    q, k, v = a.qkv(blk.n1(x)).view(2, 9, 3, 2, 8).permute(2, 0, 3, 1, 4)
+    rel = a.bias[:, a.rel].view(2, 4, 4, 4, 4)[:, :3, :3, :3, :3].reshape(2, 9, 9)
+    ref = F.scaled_dot_product_attention(q, k, v, attn_mask=rel[None])
+    ref = a.proj(ref.transpose(1, 2).reshape(2, 9, 16))
+    assert torch.allclose(got, ref, atol=1e-5)
