@@ -1,4 +1,6 @@
 """TR-Hash object detection (counterpart: complexity/generative/detection/)."""
+from .augmentations import (AugmentedDataset, DetectionAugment, color_jitter, horizontal_flip,
+                            mosaic, random_scale)
 from .coco_evaluation import evaluate_detections
 from .config import COCO_V8_NANO_NAME, TRHashDetectorConfig, coco_v8_nano_config
 from .data import (COCO_CLASS_NAMES, VOC_CLASS_NAMES, CocoDetectionDataset,
@@ -20,5 +22,6 @@ __all__ = [
     "VOC_CLASS_NAMES", "DetectionImageMetadata", "preprocess_detector_image",
     "restore_detector_boxes", "ModelEMA", "evaluate_detections", "save_detector_checkpoint",
     "load_detector_checkpoint", "export_detector_torchscript", "DetectorTrainer",
-    "DetectorTrainingConfig",
+    "DetectorTrainingConfig", "DetectionAugment", "AugmentedDataset", "mosaic",
+    "horizontal_flip", "random_scale", "color_jitter",
 ]

@@ -33,7 +33,17 @@ class DetectorTrainingConfig:
 
 class DetectorTrainer:
     def __init__(self, model: TRHashObjectDetector, config: Optional[DetectorTrainingConfig] = None):
+        import torch.distributed as dist
+
         self.model = model
+        # data parallel: one process per GPU; gradients are averaged by DDP
+        self.world = dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
+        self.ddp = None
+        if self.world > 1:
+            dev = next(model.parameters()).device
+            self.ddp = torch.nn.parallel.DistributedDataParallel(
+                model, device_ids=[dev.index] if dev.type == "cuda" else None,
+                find_unused_parameters=True)
         self.config = c = config or DetectorTrainingConfig()
         decay, no_decay = [], []
         for n, p in model.named_parameters():
@@ -58,7 +68,7 @@ class DetectorTrainer:
         images = images.to(dev, non_blocking=True)
         amp = self.config.amp_bf16 and dev.type == "cuda"
         with torch.autocast("cuda", dtype=torch.bfloat16, enabled=amp):
-            out = self.model(images, targets)
+            out = (self.ddp or self.model)(images, targets)
         self.optimizer.zero_grad(set_to_none=True)
         out["loss"].backward()
         torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.config.grad_clip)
@@ -74,6 +84,14 @@ class DetectorTrainer:
         dev = next(model.parameters()).device
         dets, gts = [], []
         for images, targets in loader:
-            dets += model.predict(images.to(dev))
-            gts += targets
+            dets += [{k: v.cpu() for k, v in d.items()} for d in model.predict(images.to(dev))]
+            gts += [{k: v for k, v in t.items() if torch.is_tensor(v)} for t in targets]
+        if self.world > 1:  # every rank evaluated its shard; score the union
+            import torch.distributed as dist
+
+            all_d, all_g = [None] * self.world, [None] * self.world
+            dist.all_gather_object(all_d, dets)
+            dist.all_gather_object(all_g, gts)
+            dets = [d for part in all_d for d in part]
+            gts = [g for part in all_g for g in part]
         return evaluate_detections(dets, gts, model.config.num_classes)
