@@ -93,3 +93,25 @@ def test_editor_and_tar_datasets(tmp_path):
     ids_ds = AtlasImageTarDataset(str(tar), Tok(), image_size=32)
     imgs, txt = collate_atlas_images([ids_ds[0]])
     assert len(ids_ds) == 1 and imgs.shape == (1, 3, 32, 32)
+
+
+def test_generative_trainer_resumes(tmp_path):
+    from complexity_framework_b200.generative.training import (GenerativeTrainer,
+                                                               GenerativeTrainingConfig)
+
+    torch.manual_seed(0)
+    m = TRHashTextToImage(_cfg(), FrozenAutoencoderKL(channels=16))
+    lat = torch.randn(4, 4, 4, 4)
+    ids = torch.randint(0, 64, (4, 6))
+    tr = GenerativeTrainer(m, GenerativeTrainingConfig(learning_rate=3e-3, warmup_steps=2,
+                                                       max_steps=30, log_every=1000))
+    batches = [{"latents": lat, "text_ids": ids}] * 30
+    first = tr.train_step(batches[0])["loss"]
+    last = tr.train(batches[1:], max_steps=30, log=None)["loss"]
+    assert last < first and tr.step == 30
+    tr.save(str(tmp_path / "ck"))
+    tr2 = GenerativeTrainer(TRHashTextToImage(_cfg(), FrozenAutoencoderKL(channels=16)))
+    tr2.load(str(tmp_path / "ck"))
+    assert tr2.step == 30
+    assert all(torch.equal(a, b) for a, b in zip(m.state_dict().values(),
+                                                 tr2.model.state_dict().values()))
