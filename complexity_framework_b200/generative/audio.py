@@ -12,7 +12,6 @@ is outside this package.
 """
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass
 from typing import Optional
 

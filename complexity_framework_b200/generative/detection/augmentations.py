@@ -6,7 +6,7 @@ dropping boxes that become (nearly) empty."""
 from __future__ import annotations
 
 import random
-from typing import Dict, List, Sequence, Tuple
+from typing import Dict, Sequence, Tuple
 
 import torch
 import torch.nn.functional as F

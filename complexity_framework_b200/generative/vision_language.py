@@ -13,7 +13,7 @@ from __future__ import annotations
 import io
 import tarfile
 from dataclasses import dataclass, field
-from typing import Dict, List, Optional, Sequence
+from typing import Dict, Optional, Sequence
 
 import torch
 import torch.nn as nn

@@ -20,7 +20,7 @@ from __future__ import annotations
 import json
 import math
 import os
-from typing import Dict, List, Literal, Optional, Sequence
+from typing import Dict, Literal, Optional, Sequence
 
 import torch
 import torch.nn as nn
