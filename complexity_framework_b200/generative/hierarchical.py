@@ -21,7 +21,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .towers import _engine
+from .towers import _engine, ffn_input
 
 
 @dataclass
@@ -133,7 +133,7 @@ class HierarchicalBlock(nn.Module):
             h = self.attn(h)
         x = x + h
         ids = (torch.arange(H * W, device=x.device) % self.vocab).unsqueeze(0).expand(B, -1)
-        return x + self.mlp(self.n2(x), ids)
+        return x + self.mlp(ffn_input(self.n2(x)), ids)
 
 
 class PatchMerging(nn.Module):

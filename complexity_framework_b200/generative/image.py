@@ -28,7 +28,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .towers import SelfAttention, _engine
+from .towers import SelfAttention, _engine, ffn_input
 
 
 # ------------------------------------------------------------------ codec
@@ -166,7 +166,7 @@ class TRHashDiTBlock(nn.Module):
         s1, b1, g1, s2, b2, g2 = self.ada(F.silu(c))[:, None].chunk(6, -1)
         x = x + g1 * self.attn(self.n1(x) * (1 + s1) + b1)
         x = x + self.cross(self.n2(x), ctx, ctx_mask)
-        return x + g2 * self.mlp(self.n3(x) * (1 + s2) + b2, route_ids)
+        return x + g2 * self.mlp(ffn_input(self.n3(x) * (1 + s2) + b2), route_ids)
 
 
 class TRHashTextToImage(nn.Module):

@@ -67,6 +67,14 @@ def _engine(hidden: int, vocab: int, experts: int, top_k: int, shared: int, widt
         shared_width=shared, expert_width=width, layer_index=layer, route_seed=seed))
 
 
+def ffn_input(h: torch.Tensor) -> torch.Tensor:
+    """Under CUDA bf16 autocast, LayerNorm returns fp32; the TR-Hash engine runs
+    its fused sm_100a GEMMs only on bf16 inputs, so cast to the autocast dtype."""
+    if h.is_cuda and torch.is_autocast_enabled("cuda") and h.dtype == torch.float32:
+        return h.to(torch.get_autocast_dtype("cuda"))
+    return h
+
+
 class SelfAttention(nn.Module):
     """Bidirectional multi-head attention on PyTorch SDPA (cuDNN flash on B200)."""
 
@@ -102,7 +110,7 @@ class TRHashVisionBlock(nn.Module):
     def forward(self, x: torch.Tensor, route_ids: torch.Tensor,
                 mask: Optional[torch.Tensor] = None, causal: bool = False) -> torch.Tensor:
         x = x + self.attn(self.norm1(x), mask, causal)
-        return x + self.mlp(self.norm2(x), route_ids)
+        return x + self.mlp(ffn_input(self.norm2(x)), route_ids)
 
 
 class TRHashVisionTower(nn.Module):
@@ -232,7 +240,7 @@ class TRHashVideoBlock(nn.Module):
             x = (xs + self.attn_s(self.norm_s(xs))).view(B, N, H)
         else:
             x = x + self.attn_s(self.norm_s(x))
-        return x + self.mlp(self.norm_m(x), route_ids)
+        return x + self.mlp(ffn_input(self.norm_m(x)), route_ids)
 
 
 class TRHashVideoTower(nn.Module):

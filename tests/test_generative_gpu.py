@@ -50,3 +50,20 @@ def test_detector_trains_in_bf16_on_gpu():
         for im, tg in dl:
             tr.train_step(im, tg)
     assert tr.evaluate(ev, use_ema=False)["AP50"] > 0.3
+
+
+def test_autocast_uses_fused_tr_hash_path():
+    """Generative blocks trained under bf16 autocast feed the TR-Hash engine bf16."""
+    from complexity_framework_b200.generative.towers import (TRHashVisionClassifier,
+                                                             TRHashVisionTowerConfig)
+    from complexity_framework_b200.tr_hash.config import TRHashBackend
+
+    torch.manual_seed(0)
+    cfg = TRHashVisionTowerConfig(image_size=64, patch_size=16, hidden_size=256, num_layers=1,
+                                  num_heads=4, shared_width=512, expert_width=64)
+    m = TRHashVisionClassifier(cfg, 4).cuda()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out = m(torch.randn(8, 3, 64, 64, device="cuda"), torch.randint(0, 4, (8,), device="cuda"))
+    out["loss"].backward()
+    assert m.tower.blocks[0].mlp.last_backend.selected is TRHashBackend.FUSED_CUDA
+    assert torch.isfinite(m.tower.patch.weight.grad).all()
