@@ -34,6 +34,11 @@ __device__ __forceinline__ void load8(const bf16* p, float* v) {
          d = unpack_bf16x2(u.w);
   v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
 }
+__device__ __forceinline__ void unpack8(const uint4& u, float* v) {
+  const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z),
+               d = unpack_bf16x2(u.w);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
+}
 __device__ __forceinline__ void store8(bf16* p, const float* v) {
   uint4 u;
   u.x = pack_bf16x2(v[0], v[1]);
@@ -980,13 +985,18 @@ __global__ void __launch_bounds__(128) rmsnorm_bwd_ring_k(
     const bf16* sl = reinterpret_cast<const bf16*>(ring + (it % NS) * slot);
     const float r = *reinterpret_cast<const float*>(sl + rows * H);
     float dot = 0.f;
+    // this lane's x / dy vectors stay in registers (packed bf16) for the second
+    // pass instead of being read from shared memory again
+    uint4 xq[NV], gq[NV];
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int i = lane + 32 * k;
       if (i < nv) {
         float xv[8], gv[8], wv[8];
-        load8(sl + H + i * 8, xv);
-        load8(sl + i * 8, gv);
+        xq[k] = *reinterpret_cast<const uint4*>(sl + H + i * 8);
+        gq[k] = *reinterpret_cast<const uint4*>(sl + i * 8);
+        unpack8(xq[k], xv);
+        unpack8(gq[k], gv);
         wload(i, wv);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -1002,8 +1012,8 @@ __global__ void __launch_bounds__(128) rmsnorm_bwd_ring_k(
       const int i = lane + 32 * k;
       if (i < nv) {
         float xv[8], gv[8], wv[8], o[8];
-        load8(sl + H + i * 8, xv);
-        load8(sl + i * 8, gv);
+        unpack8(xq[k], xv);
+        unpack8(gq[k], gv);
         wload(i, wv);
         if (dres != nullptr) {
           load8(sl + 2 * H + i * 8, o);
