@@ -244,6 +244,75 @@ def cmd_info(a) -> None:
     print(json.dumps(info, indent=2))
 
 
+# --------------------------------------------------------------- detection
+def cmd_train_detector(a) -> None:
+    """Train a TR-Hash detector on COCO-format data, YOLO labels, or synthetic
+    shapes; evaluates the EMA model and writes a checkpoint directory."""
+    from ..generative.detection import (AugmentedDataset, CocoDetectionDataset,
+                                        DetectionAugment, DetectorTrainer,
+                                        DetectorTrainingConfig, SyntheticShapesDataset,
+                                        TRHashDetectorConfig, TRHashObjectDetector,
+                                        YoloDetectionDataset, collate_detection,
+                                        save_detector_checkpoint)
+
+    if a.data == "synthetic":
+        train = SyntheticShapesDataset(a.synthetic_images, a.image_size, 4, a.num_classes)
+        val = SyntheticShapesDataset(max(16, a.synthetic_images // 8), a.image_size, 4,
+                                     a.num_classes, seed=1)
+    elif a.data == "coco":
+        train = CocoDetectionDataset(a.annotations, a.images, a.image_size)
+        val = CocoDetectionDataset(a.val_annotations or a.annotations,
+                                   a.val_images or a.images, a.image_size)
+    else:
+        train = YoloDetectionDataset(a.images, a.labels, a.image_size)
+        val = YoloDetectionDataset(a.val_images or a.images, a.val_labels or a.labels,
+                                   a.image_size)
+    if a.augment:
+        train = AugmentedDataset(train, DetectionAugment(seed=a.seed))
+    cfg = TRHashDetectorConfig(image_size=a.image_size, num_classes=a.num_classes,
+                               backbone=a.backbone)
+    dev = torch.device(a.device or ("cuda" if torch.cuda.is_available() else "cpu"))
+    model = TRHashObjectDetector(cfg).to(dev)
+    trainer = DetectorTrainer(model, DetectorTrainingConfig(
+        learning_rate=a.lr, max_steps=a.steps, warmup_steps=min(100, a.steps // 10)))
+    dl = torch.utils.data.DataLoader(train, batch_size=a.batch, shuffle=True, drop_last=True,
+                                     collate_fn=collate_detection, num_workers=a.workers)
+    done = False
+    while not done:
+        for images, targets in dl:
+            losses = trainer.train_step(images, targets)
+            if trainer.step % a.log_every == 0:
+                print(json.dumps({"step": trainer.step, **{k: round(v, 4) for k, v in losses.items()}}))
+            if trainer.step >= a.steps:
+                done = True
+                break
+    vl = torch.utils.data.DataLoader(val, batch_size=a.batch, collate_fn=collate_detection)
+    print(json.dumps({"eval": trainer.evaluate(vl)}))
+    save_detector_checkpoint(model, a.output, ema=trainer.ema)
+    print(json.dumps({"saved": a.output}))
+
+
+def cmd_detect(a) -> None:
+    """Run a saved detector on image files; prints boxes in original-image pixels."""
+    from torchvision.io import read_image
+
+    from ..generative.detection import (load_detector_checkpoint, preprocess_detector_image,
+                                        restore_detector_boxes)
+
+    dev = torch.device(a.device or ("cuda" if torch.cuda.is_available() else "cpu"))
+    model = load_detector_checkpoint(a.checkpoint).to(dev)
+    names = model.config.class_names
+    for path in a.images:
+        img = read_image(path).float()[:3] / 255.0
+        x, meta = preprocess_detector_image(img, model.config.image_size)
+        r = model.predict(x[None].to(dev), score_threshold=a.score)[0]
+        boxes = restore_detector_boxes(r["boxes"].cpu(), meta)
+        dets = [{"box": [round(float(v), 1) for v in b], "score": round(float(s), 4),
+                 "label": (names[int(l)] if int(l) < len(names) else int(l))}
+                for b, s, l in zip(boxes, r["scores"].cpu(), r["labels"].cpu())]
+        print(json.dumps({"image": path, "detections": dets}))
+
+
 # ------------------------------------------------------------------- parser
 def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="cfb", description="complexity_framework_b200 CLI")
@@ -294,12 +363,38 @@ def build_parser() -> argparse.ArgumentParser:
     pr = sub.add_parser("profile")
     pr.add_argument("what", choices=["model", "kernels", "throughput"])
     pr.add_argument("--model", default="tr-hash-200m")
-    pr.add_argument("--case", default="gemm", choices=["gemm", "flash", "norms"])
+    pr.add_argument("--case", default="gemm", choices=["gemm", "gemm_bn", "flash", "norms"])
     pr.add_argument("--seq-len", type=int, default=2048)
     pr.add_argument("--batch", type=int, default=1)
     pr.add_argument("--device", default=None)
     sub.add_parser("plan", help="cluster run plan (cluster_plan flags follow)", add_help=False)
     sub.add_parser("info")
+    td = sub.add_parser("train-detector", help="train a TR-Hash object detector")
+    td.add_argument("--data", choices=["synthetic", "coco", "yolo"], default="synthetic")
+    td.add_argument("--images", default=None)
+    td.add_argument("--annotations", default=None, help="COCO instances json")
+    td.add_argument("--labels", default=None, help="YOLO label directory")
+    td.add_argument("--val-images", default=None)
+    td.add_argument("--val-annotations", default=None)
+    td.add_argument("--val-labels", default=None)
+    td.add_argument("--num-classes", type=int, default=2)
+    td.add_argument("--image-size", type=int, default=320)
+    td.add_argument("--backbone", choices=["plain", "hierarchical"], default="plain")
+    td.add_argument("--synthetic-images", type=int, default=512)
+    td.add_argument("--augment", action="store_true")
+    td.add_argument("--batch", type=int, default=16)
+    td.add_argument("--steps", type=int, default=1000)
+    td.add_argument("--lr", type=float, default=1e-3)
+    td.add_argument("--workers", type=int, default=0)
+    td.add_argument("--log-every", type=int, default=50)
+    td.add_argument("--seed", type=int, default=0)
+    td.add_argument("--device", default=None)
+    td.add_argument("--output", required=True)
+    dt = sub.add_parser("detect", help="run a saved detector on images")
+    dt.add_argument("--checkpoint", required=True)
+    dt.add_argument("--score", type=float, default=0.25)
+    dt.add_argument("--device", default=None)
+    dt.add_argument("images", nargs="+")
     return ap
 
 
@@ -314,7 +409,8 @@ def main(argv: Optional[List[str]] = None) -> None:
     a = build_parser().parse_args(argv)
     {"generate": cmd_generate, "chat": cmd_chat, "bench-infer": cmd_bench_infer,
      "serve": cmd_serve, "convert": cmd_convert, "tokenize": cmd_tokenize,
-     "profile": cmd_profile, "info": cmd_info}[a.cmd](a)
+     "profile": cmd_profile, "info": cmd_info, "train-detector": cmd_train_detector,
+     "detect": cmd_detect}[a.cmd](a)
 
 
 if __name__ == "__main__":

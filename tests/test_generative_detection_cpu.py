@@ -231,3 +231,25 @@ def test_detector_trainer_data_parallel_gloo():
     (s0, a0, ap0), (s1, a1, ap1) = g
     assert abs(s0 - s1) < 1e-4 and abs(a0 - a1) < 1e-4  # replicas stayed in sync
     assert ap0 == ap1                                     # both scored the union
+
+
+def test_cli_train_detector_and_detect(tmp_path, capsys):
+    import json
+
+    from torchvision.io import write_png
+
+    from complexity_framework_b200.cli.app import main
+
+    out = str(tmp_path / "det")
+    main(["train-detector", "--data", "synthetic", "--image-size", "64", "--synthetic-images",
+          "16", "--batch", "8", "--steps", "3", "--log-every", "1", "--output", out])
+    lines = [json.loads(x) for x in capsys.readouterr().out.strip().splitlines()]
+    assert lines[0]["step"] == 1 and "mAP" in lines[-2]["eval"] and lines[-1]["saved"] == out
+    img_path = str(tmp_path / "x.png")
+    write_png((torch.rand(3, 48, 80) * 255).to(torch.uint8), img_path)
+    main(["detect", "--checkpoint", out, "--score", "0.0", img_path])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert res["image"] == img_path
+    for d in res["detections"]:
+        x0, y0, x1, y1 = d["box"]
+        assert 0 <= x0 <= x1 <= 80 and 0 <= y0 <= y1 <= 48  # original-image coordinates
