@@ -1,0 +1,215 @@
+"""Context (sequence) parallel attention: a sequence too long for one GPU is
+split into contiguous chunks, one per rank of ``group``.
+
+The reference bounds sequence length by one device; this adds the two
+standard ways to attend across the chunks:
+
+* ``ulysses_attention``: an all-to-all turns [heads, local chunk] into
+  [local heads, full sequence], attention runs per head group on the whole
+  sequence, a second all-to-all returns to sequence chunks.  Communication is
+  4 * (activation size) / P per layer; needs heads divisible by P (K/V heads
+  are repeated up to P when there are fewer).
+* ``ring_attention``: K/V chunks travel around the ring of ranks (one
+  send/receive per step); each rank merges the partial softmax of every chunk
+  into its queries with the running max / sum (online softmax).  Causal
+  attention skips chunks entirely in the future of the local queries.  In
+  backward the K/V chunk travels with its dK/dV accumulators and arrives back
+  at its owner after P hops carrying every rank's contribution.
+
+Inputs are head-major ``q [B, Hq, S_local, D]``, ``k/v [B, Hkv, S_local, D]``
+(GQA: Hq a multiple of Hkv); rank r holds sequence positions
+[r * S_local, (r + 1) * S_local).  Block math is done in fp32.  On NCCL the
+transfers go over NVLink; the operators are also exercised on gloo ranks.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+
+def _rank_world(group) -> Tuple[int, int]:
+    return dist.get_rank(group), dist.get_world_size(group)
+
+
+# ------------------------------------------------------------------ Ulysses
+def _a2a(x: torch.Tensor, group, scatter_dim: int, gather_dim: int) -> torch.Tensor:
+    """Split ``x`` along ``scatter_dim`` into P parts (part j to rank j) and
+    concatenate the parts received from ranks 0..P-1 along ``gather_dim``."""
+    P = dist.get_world_size(group)
+    parts = [c.contiguous() for c in x.chunk(P, scatter_dim)]
+    inp = torch.stack(parts)                          # [P, ...]
+    out = torch.empty_like(inp)
+    dist.all_to_all_single(out, inp, group=group)
+    return torch.cat(list(out.unbind(0)), gather_dim)
+
+
+class _AllToAll(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, group, scatter_dim, gather_dim):
+        ctx.group, ctx.dims = group, (scatter_dim, gather_dim)
+        return _a2a(x, group, scatter_dim, gather_dim)
+
+    @staticmethod
+    def backward(ctx, g):
+        s, gdim = ctx.dims
+        return _a2a(g.contiguous(), ctx.group, gdim, s), None, None, None
+
+
+def seq_to_heads(x: torch.Tensor, group) -> torch.Tensor:
+    """[B, H, S_local, D] -> [B, H / P, S, D]."""
+    return _AllToAll.apply(x, group, 1, 2)
+
+
+def heads_to_seq(x: torch.Tensor, group) -> torch.Tensor:
+    """[B, H / P, S, D] -> [B, H, S_local, D]."""
+    return _AllToAll.apply(x, group, 2, 1)
+
+
+def ulysses_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, group,
+                      causal: bool = True, scale: Optional[float] = None) -> torch.Tensor:
+    _, P = _rank_world(group)
+    Hq, Hkv = q.shape[1], k.shape[1]
+    if Hq % P:
+        raise ValueError(f"ulysses_attention needs query heads ({Hq}) divisible by {P} ranks")
+    if Hkv % P:  # repeat K/V heads so that every rank gets whole groups
+        rep = P // math.gcd(Hkv, P)
+        k, v = k.repeat_interleave(rep, 1), v.repeat_interleave(rep, 1)
+    qh, kh, vh = seq_to_heads(q, group), seq_to_heads(k, group), seq_to_heads(v, group)
+    o = F.scaled_dot_product_attention(qh, kh, vh, is_causal=causal, scale=scale,
+                                       enable_gqa=kh.shape[1] != qh.shape[1])
+    return heads_to_seq(o, group)
+
+
+# --------------------------------------------------------------------- ring
+def _ring_pass(tensors, group):
+    """Send to rank + 1, receive from rank - 1 (same shapes); returns received."""
+    r, P = _rank_world(group)
+    nxt, prv = (r + 1) % P, (r - 1) % P
+    g_nxt = dist.get_global_rank(group, nxt) if group is not None else nxt
+    g_prv = dist.get_global_rank(group, prv) if group is not None else prv
+    recv = [torch.empty_like(t) for t in tensors]
+    ops = [dist.P2POp(dist.isend, t.contiguous(), g_nxt, group) for t in tensors]
+    ops += [dist.P2POp(dist.irecv, t, g_prv, group) for t in recv]
+    for req in dist.batch_isend_irecv(ops):
+        req.wait()
+    return recv
+
+
+def _expand(k: torch.Tensor, groups: int) -> torch.Tensor:
+    return k if groups == 1 else k.repeat_interleave(groups, 1)
+
+
+def _block_mask(src: int, r: int, Sq: int, Sk: int, device) -> Optional[torch.Tensor]:
+    """Causal mask of local queries (chunk r) against keys of chunk src:
+    None = all visible, a bool [Sq, Sk] mask on the diagonal block."""
+    if src < r:
+        return None
+    return torch.ones(Sq, Sk, dtype=torch.bool, device=device).tril()
+
+
+class _RingAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, group, causal, scale):
+        r, P = _rank_world(group)
+        B, Hq, S, D = q.shape
+        G = Hq // k.shape[1]
+        qf = q.float()
+        m = torch.full((B, Hq, S, 1), -math.inf, device=q.device)
+        l = torch.zeros(B, Hq, S, 1, device=q.device)
+        acc = torch.zeros(B, Hq, S, D, device=q.device)
+        kc, vc = k, v
+        for step in range(P):
+            src = (r - step) % P
+            if not (causal and src > r):
+                s = qf @ _expand(kc, G).float().transpose(-1, -2) * scale
+                if causal:
+                    mask = _block_mask(src, r, S, kc.shape[2], q.device)
+                    if mask is not None:
+                        s = s.masked_fill(~mask, -math.inf)
+                m_new = torch.maximum(m, s.amax(-1, keepdim=True))
+                alpha = torch.exp(m - m_new)
+                p = torch.exp(s - m_new)
+                l = l * alpha + p.sum(-1, keepdim=True)
+                acc = acc * alpha + p @ _expand(vc, G).float()
+                m = m_new
+            if step < P - 1:
+                kc, vc = _ring_pass([kc, vc], group)
+        out = acc / l
+        lse = m + torch.log(l)
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.group, ctx.causal, ctx.scale = group, causal, scale
+        return out.to(q.dtype)
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, out, lse = ctx.saved_tensors
+        group, causal, scale = ctx.group, ctx.causal, ctx.scale
+        r, P = _rank_world(group)
+        B, Hq, S, D = q.shape
+        Hkv = k.shape[1]
+        G = Hq // Hkv
+        qf, do = q.float(), dout.float()
+        delta = (do * out).sum(-1, keepdim=True)
+        dq = torch.zeros_like(qf)
+        kc, vc = k, v
+        dkc = torch.zeros(k.shape, device=k.device)
+        dvc = torch.zeros(v.shape, device=v.device)
+        for step in range(P):
+            src = (r - step) % P
+            if not (causal and src > r):
+                ke, ve = _expand(kc, G).float(), _expand(vc, G).float()
+                s = qf @ ke.transpose(-1, -2) * scale
+                if causal:
+                    mask = _block_mask(src, r, S, kc.shape[2], q.device)
+                    if mask is not None:
+                        s = s.masked_fill(~mask, -math.inf)
+                p = torch.exp(s - lse)
+                dp = do @ ve.transpose(-1, -2)
+                ds = p * (dp - delta)
+                dq += ds @ ke * scale
+                dk_e = ds.transpose(-1, -2) @ qf * scale       # [B, Hq, Sk, D]
+                dv_e = p.transpose(-1, -2) @ do
+                dkc += dk_e.view(B, Hkv, G, -1, D).sum(2)
+                dvc += dv_e.view(B, Hkv, G, -1, D).sum(2)
+            # the chunk and its gradient move on together; after P hops every
+            # chunk is back at its owner with all ranks' contributions
+            kc, vc, dkc, dvc = _ring_pass([kc, vc, dkc, dvc], group)
+        return dq.to(q.dtype), dkc.to(k.dtype), dvc.to(v.dtype), None, None, None
+
+
+def ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, group,
+                   causal: bool = True, scale: Optional[float] = None) -> torch.Tensor:
+    if q.shape[1] % k.shape[1]:
+        raise ValueError("query heads must be a multiple of key/value heads")
+    scale = q.shape[-1] ** -0.5 if scale is None else scale
+    return _RingAttention.apply(q, k, v, group, causal, scale)
+
+
+def context_parallel_attention(q, k, v, group, causal: bool = True,
+                               scale: Optional[float] = None, method: str = "auto"):
+    """``method`` "ulysses" when the heads divide over the ranks (fewer, larger
+    messages), "ring" otherwise; ``auto`` picks."""
+    P = dist.get_world_size(group)
+    if method == "auto":
+        method = "ulysses" if q.shape[1] % P == 0 else "ring"
+    if method == "ulysses":
+        return ulysses_attention(q, k, v, group, causal, scale)
+    return ring_attention(q, k, v, group, causal, scale)
+
+
+def split_sequence(x: torch.Tensor, group, dim: int = 1) -> torch.Tensor:
+    """This rank's contiguous chunk of ``x`` along ``dim`` (length divisible by P)."""
+    r, P = _rank_world(group)
+    if x.shape[dim] % P:
+        raise ValueError(f"sequence length {x.shape[dim]} not divisible by {P} ranks")
+    return x.chunk(P, dim)[r]
+
+
+def chunk_positions(seq_len_local: int, group, device=None) -> torch.Tensor:
+    """Global positions of this rank's chunk (for RoPE / position embeddings)."""
+    r, _ = _rank_world(group)
+    return torch.arange(r * seq_len_local, (r + 1) * seq_len_local, device=device)

@@ -1,0 +1,66 @@
+"""Context-parallel attention (ring and Ulysses) on gloo ranks against
+single-process attention over the whole sequence: outputs and dq/dk/dv."""
+import socket
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, method, causal, q_out):
+    import torch.distributed as dist
+
+    from complexity_framework_b200.parallel.context_parallel import (
+        context_parallel_attention, split_sequence)
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+    g = torch.Generator().manual_seed(0)
+    B, Hq, Hkv, S, D = 2, 4, 2, 12, 8
+    q = torch.randn(B, Hq, S, D, generator=g)
+    k = torch.randn(B, Hkv, S, D, generator=g)
+    v = torch.randn(B, Hkv, S, D, generator=g)
+    go = torch.randn(B, Hq, S, D, generator=g)
+    # reference over the whole sequence
+    qr, kr, vr = (t.clone().requires_grad_() for t in (q, k, v))
+    o_ref = F.scaled_dot_product_attention(qr, kr, vr, is_causal=causal, enable_gqa=True)
+    (o_ref * go).sum().backward()
+    # this rank's chunk
+    ql, kl, vl = (split_sequence(t, None, 2).clone().requires_grad_() for t in (q, k, v))
+    o = context_parallel_attention(ql, kl, vl, None, causal=causal, method=method)
+    (o * split_sequence(go, None, 2)).sum().backward()
+    err = max(float((o - split_sequence(o_ref, None, 2)).abs().max()),
+              float((ql.grad - split_sequence(qr.grad, None, 2)).abs().max()),
+              float((kl.grad - split_sequence(kr.grad, None, 2)).abs().max()),
+              float((vl.grad - split_sequence(vr.grad, None, 2)).abs().max()))
+    errs = [None] * world
+    dist.all_gather_object(errs, err)
+    if rank == 0:
+        q_out.put(errs)
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("method,world", [("ring", 3), ("ring", 2), ("ulysses", 2)])
+@pytest.mark.parametrize("causal", [True, False])
+def test_context_parallel_matches_full_attention(method, world, causal):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_worker, args=(r, world, port, method, causal, q))
+          for r in range(world)]
+    for p in ps:
+        p.start()
+    errs = q.get(timeout=180)
+    for p in ps:
+        p.join(timeout=60)
+    assert max(errs) < 1e-4, errs
