@@ -165,15 +165,30 @@ class GroupedQueryAttention(nn.Module):
 
         B, S, _ = x.shape
         kqv = fused.linear(x, self.kqv_weight())
-        cos, sin = self.rotary_emb.tables(S, x.device)
+        cp = getattr(self, "cp_group", None)
+        pos = None
+        if cp is not None:  # context parallel: global positions of this rank's chunk
+            from ..parallel.context_parallel import chunk_positions
+
+            pos = chunk_positions(S, cp, x.device).to(torch.int32).expand(B, S).contiguous()
+            cos, sin = self.rotary_emb.tables(int(pos[0, -1]) + 1, x.device)
+        else:
+            cos, sin = self.rotary_emb.tables(S, x.device)
         if self.use_qk_norm:
             qw, kw, eps = self.q_norm.weight, self.k_norm.weight, self.q_norm.eps
         else:
             qw = kw = kqv.new_ones(self.head_dim)
             eps = 1e-6
-        q, k, v = fused.qk_norm_rope(kqv, qw, kw, cos, sin, None, self.num_heads,
+        q, k, v = fused.qk_norm_rope(kqv, qw, kw, cos, sin, pos, self.num_heads,
                                      self.num_kv_heads, self.head_dim, eps, self.use_qk_norm)
-        o = attn_ops.attention(q, k, v, causal=True, scale=self.attn_scale)  # [B, S, Hq*D]
+        if cp is not None:
+            from ..parallel.context_parallel import context_parallel_attention
+
+            o = context_parallel_attention(q, k, v, cp, causal=True, scale=self.attn_scale,
+                                           method=getattr(self, "cp_method", "auto"))
+            o = o.transpose(1, 2).reshape(B, S, -1)
+        else:
+            o = attn_ops.attention(q, k, v, causal=True, scale=self.attn_scale)  # [B, S, Hq*D]
         return fused.linear(o, self.o_proj.weight, residual)
 
     def forward_sp(self, x_shard: torch.Tensor, residual: torch.Tensor, B: int, S: int,
@@ -208,6 +223,18 @@ class GroupedQueryAttention(nn.Module):
         if self.use_qk_norm:
             q = self.q_norm(q)
             k = self.k_norm(k)
+        cp = getattr(self, "cp_group", None)
+        if cp is not None:
+            # context parallel: this rank's chunk starts at rank * S in the sequence
+            from ..parallel.context_parallel import chunk_positions, context_parallel_attention
+
+            pos = chunk_positions(S, cp, q.device)
+            cos, sin = self.rotary_emb(int(pos[-1]) + 1)
+            q, k = self.rotary_emb.rotate(q, k, cos[pos].to(q.dtype), sin[pos].to(q.dtype))
+            o = context_parallel_attention(q, k, v, cp, causal=True, scale=self.attn_scale,
+                                           method=getattr(self, "cp_method", "auto"))
+            o = o.transpose(1, 2).reshape(B, S, self.num_heads * self.head_dim)
+            return self.o_proj(o), None
         past = 0 if past_key_value is None else past_key_value[0].shape[2]
         kv_len = past + S
         cos, sin = self.rotary_emb(kv_len)

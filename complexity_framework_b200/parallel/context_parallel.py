@@ -91,7 +91,8 @@ def _ring_pass(tensors, group):
     nxt, prv = (r + 1) % P, (r - 1) % P
     g_nxt = dist.get_global_rank(group, nxt) if group is not None else nxt
     g_prv = dist.get_global_rank(group, prv) if group is not None else prv
-    recv = [torch.empty_like(t) for t in tensors]
+    # contiguous buffers: inputs may be strided views (e.g. head-major q/k/v)
+    recv = [torch.empty(t.shape, dtype=t.dtype, device=t.device) for t in tensors]
     ops = [dist.P2POp(dist.isend, t.contiguous(), g_nxt, group) for t in tensors]
     ops += [dist.P2POp(dist.irecv, t, g_prv, group) for t in recv]
     for req in dist.batch_isend_irecv(ops):
@@ -213,3 +214,26 @@ def chunk_positions(seq_len_local: int, group, device=None) -> torch.Tensor:
     """Global positions of this rank's chunk (for RoPE / position embeddings)."""
     r, _ = _rank_world(group)
     return torch.arange(r * seq_len_local, (r + 1) * seq_len_local, device=device)
+
+
+def enable_context_parallel(model: torch.nn.Module, group=None, method: str = "auto") -> int:
+    """Make every attention layer of ``model`` attend across the sequence chunks
+    of ``group`` (RoPE at global positions, ring or Ulysses attention); returns
+    the number of layers switched.  Feed each rank its chunk of the inputs and
+    of the globally shifted labels (``context_parallel_batch``)."""
+    n = 0
+    for m in model.modules():
+        if hasattr(m, "rotary_emb") and hasattr(m, "o_proj") and hasattr(m, "num_kv_heads"):
+            m.cp_group = group if group is not None else dist.group.WORLD
+            m.cp_method = method
+            n += 1
+    return n
+
+
+def context_parallel_batch(input_ids: torch.Tensor, group=None, ignore_index: int = -100):
+    """(this rank's input chunk, its next-token labels): labels are shifted over
+    the whole sequence before splitting, so a chunk's last position predicts
+    the first token of the next rank's chunk."""
+    labels = torch.roll(input_ids, -1, dims=1)
+    labels[:, -1] = ignore_index
+    return split_sequence(input_ids, group, 1), split_sequence(labels, group, 1)

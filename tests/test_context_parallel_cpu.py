@@ -64,3 +64,58 @@ def test_context_parallel_matches_full_attention(method, world, causal):
     for p in ps:
         p.join(timeout=60)
     assert max(errs) < 1e-4, errs
+
+
+def _model_worker(rank, world, port, method, q_out):
+    import torch.distributed as dist
+
+    from complexity_framework_b200 import ComplexityModel, ModelConfig
+    from complexity_framework_b200.parallel.context_parallel import (context_parallel_batch,
+                                                                      enable_context_parallel)
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+    torch.manual_seed(0)
+    cfg = ModelConfig(hidden_size=64, num_hidden_layers=2, num_attention_heads=4,
+                      num_key_value_heads=2, vocab_size=128, intermediate_size=64,
+                      shared_intermediate_size=128, num_experts=4, max_position_embeddings=256)
+    full = ComplexityModel(cfg)
+    ids = torch.randint(0, 128, (2, 32), generator=torch.Generator().manual_seed(3))
+    ref_loss = full.loss(ids)
+    ref_loss.backward()
+    ref_grads = [p.grad.clone() for p in full.parameters()]
+    full.zero_grad()
+    assert enable_context_parallel(full, None, method) == 2
+    x, y = context_parallel_batch(ids, None)
+    n_local = (y != -100).sum()
+    n_total = (torch.roll(ids, -1, 1)[:, :-1]).numel()
+    loss = full.loss(x, y) * n_local / n_total          # this rank's share of the mean
+    loss.backward()
+    total = loss.detach().clone()
+    dist.all_reduce(total)
+    err = abs(float(total) - float(ref_loss))
+    for p, g in zip(full.parameters(), ref_grads):
+        pg = p.grad.contiguous()
+        dist.all_reduce(pg)
+        err = max(err, float((pg - g).abs().max()))
+    errs = [None] * world
+    dist.all_gather_object(errs, err)
+    if rank == 0:
+        q_out.put(errs)
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("method", ["ring", "ulysses"])
+def test_model_context_parallel_matches_full_sequence(method):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_model_worker, args=(r, 2, port, method, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    errs = q.get(timeout=120)
+    for p in ps:
+        p.join(timeout=60)
+    assert max(errs) < 1e-4, errs
