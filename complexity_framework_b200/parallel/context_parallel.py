@@ -18,8 +18,10 @@ standard ways to attend across the chunks:
 
 Inputs are head-major ``q [B, Hq, S_local, D]``, ``k/v [B, Hkv, S_local, D]``
 (GQA: Hq a multiple of Hkv); rank r holds sequence positions
-[r * S_local, (r + 1) * S_local).  Block math is done in fp32.  On NCCL the
-transfers go over NVLink; the operators are also exercised on gloo ranks.
+[r * S_local, (r + 1) * S_local).  On CUDA bf16 the per-block attention runs on
+cuDNN's flash kernels (forward returns the block log-sum-exp; backward takes
+the global output and log-sum-exp), elsewhere in fp32.  On NCCL the transfers
+go over NVLink; the operators are also exercised on gloo ranks.
 """
 from __future__ import annotations
 
@@ -104,12 +106,60 @@ def _expand(k: torch.Tensor, groups: int) -> torch.Tensor:
     return k if groups == 1 else k.repeat_interleave(groups, 1)
 
 
-def _block_mask(src: int, r: int, Sq: int, Sk: int, device) -> Optional[torch.Tensor]:
-    """Causal mask of local queries (chunk r) against keys of chunk src:
-    None = all visible, a bool [Sq, Sk] mask on the diagonal block."""
-    if src < r:
-        return None
-    return torch.ones(Sq, Sk, dtype=torch.bool, device=device).tril()
+def _cudnn_blocks(q: torch.Tensor) -> bool:
+    """Block attention on cuDNN's flash kernels (they return the log-sum-exp the
+    ring merge needs, and their backward takes the global output / LSE)."""
+    import os
+
+    return (q.is_cuda and q.dtype in (torch.bfloat16, torch.float16) and q.shape[-1] in (64, 128)
+            and os.environ.get("CFB_RING_FP32", "0") != "1")
+
+
+def _block_forward(q, k, v, causal: bool, scale: float):
+    """Attention of q against one K/V chunk: (out fp32 [B, Hq, Sq, D],
+    lse fp32 [B, Hq, Sq, 1]); ``causal`` applies the diagonal-block mask."""
+    if _cudnn_blocks(q):
+        r = torch.ops.aten._scaled_dot_product_cudnn_attention(
+            q.contiguous(), k.contiguous(), v.contiguous(), None, True, 0.0, causal, False,
+            scale=scale)
+        return r[0].float(), r[1].float().reshape(*q.shape[:3], 1)
+    G = q.shape[1] // k.shape[1]
+    s = q.float() @ _expand(k, G).float().transpose(-1, -2) * scale
+    if causal:
+        s = s.masked_fill(~torch.ones(s.shape[-2:], dtype=torch.bool, device=s.device).tril(),
+                          -math.inf)
+    lse = torch.logsumexp(s, -1, keepdim=True)
+    return torch.exp(s - lse) @ _expand(v, G).float(), lse
+
+
+def _block_backward(do, q, k, v, out, lse, causal: bool, scale: float):
+    """(dq, dk, dv) of one block given the GLOBAL output and LSE of q's rows
+    (so the block's probabilities are exp(s - lse)); dk/dv have K/V's heads."""
+    B, Hq, S, D = q.shape
+    Hkv = k.shape[1]
+    G = Hq // Hkv
+    if _cudnn_blocks(q):
+        # undefined sequence-offset tensors select the dense (non-varlen) path;
+        # the dropout seeds are read for their device only (dropout 0)
+        seed = torch.empty(0, dtype=torch.int64, device=q.device)
+        dq, dk, dv = torch.ops.aten._scaled_dot_product_cudnn_attention_backward(
+            do.to(q.dtype).contiguous(), q.contiguous(), k.contiguous(), v.contiguous(),
+            out.to(q.dtype).contiguous(), lse.reshape(B, Hq, S, 1).contiguous(), seed, seed,
+            None, None, None, S, k.shape[2], 0.0, causal, scale=scale)
+        return dq.float(), dk.float(), dv.float()
+    qf, dof = q.float(), do.float()
+    ke, ve = _expand(k, G).float(), _expand(v, G).float()
+    s = qf @ ke.transpose(-1, -2) * scale
+    if causal:
+        s = s.masked_fill(~torch.ones(s.shape[-2:], dtype=torch.bool, device=s.device).tril(),
+                          -math.inf)
+    p = torch.exp(s - lse)
+    delta = (dof * out.float()).sum(-1, keepdim=True)
+    ds = p * (dof @ ve.transpose(-1, -2) - delta)
+    dq = ds @ ke * scale
+    dk = (ds.transpose(-1, -2) @ qf * scale).view(B, Hkv, G, -1, D).sum(2)
+    dv = (p.transpose(-1, -2) @ dof).view(B, Hkv, G, -1, D).sum(2)
+    return dq, dk, dv
 
 
 class _RingAttention(torch.autograd.Function):
@@ -117,65 +167,40 @@ class _RingAttention(torch.autograd.Function):
     def forward(ctx, q, k, v, group, causal, scale):
         r, P = _rank_world(group)
         B, Hq, S, D = q.shape
-        G = Hq // k.shape[1]
-        qf = q.float()
-        m = torch.full((B, Hq, S, 1), -math.inf, device=q.device)
-        l = torch.zeros(B, Hq, S, 1, device=q.device)
+        lse = torch.full((B, Hq, S, 1), -math.inf, device=q.device)
         acc = torch.zeros(B, Hq, S, D, device=q.device)
         kc, vc = k, v
         for step in range(P):
             src = (r - step) % P
             if not (causal and src > r):
-                s = qf @ _expand(kc, G).float().transpose(-1, -2) * scale
-                if causal:
-                    mask = _block_mask(src, r, S, kc.shape[2], q.device)
-                    if mask is not None:
-                        s = s.masked_fill(~mask, -math.inf)
-                m_new = torch.maximum(m, s.amax(-1, keepdim=True))
-                alpha = torch.exp(m - m_new)
-                p = torch.exp(s - m_new)
-                l = l * alpha + p.sum(-1, keepdim=True)
-                acc = acc * alpha + p @ _expand(vc, G).float()
-                m = m_new
+                o_b, lse_b = _block_forward(q, kc, vc, causal and src == r, scale)
+                new = torch.logaddexp(lse, lse_b)
+                acc = acc * torch.exp(lse - new) + o_b * torch.exp(lse_b - new)
+                lse = new
             if step < P - 1:
                 kc, vc = _ring_pass([kc, vc], group)
-        out = acc / l
-        lse = m + torch.log(l)
+        out = acc.to(q.dtype)
         ctx.save_for_backward(q, k, v, out, lse)
         ctx.group, ctx.causal, ctx.scale = group, causal, scale
-        return out.to(q.dtype)
+        return out
 
     @staticmethod
     def backward(ctx, dout):
         q, k, v, out, lse = ctx.saved_tensors
         group, causal, scale = ctx.group, ctx.causal, ctx.scale
         r, P = _rank_world(group)
-        B, Hq, S, D = q.shape
-        Hkv = k.shape[1]
-        G = Hq // Hkv
-        qf, do = q.float(), dout.float()
-        delta = (do * out).sum(-1, keepdim=True)
-        dq = torch.zeros_like(qf)
+        dq = torch.zeros(q.shape, device=q.device)
         kc, vc = k, v
         dkc = torch.zeros(k.shape, device=k.device)
         dvc = torch.zeros(v.shape, device=v.device)
         for step in range(P):
             src = (r - step) % P
             if not (causal and src > r):
-                ke, ve = _expand(kc, G).float(), _expand(vc, G).float()
-                s = qf @ ke.transpose(-1, -2) * scale
-                if causal:
-                    mask = _block_mask(src, r, S, kc.shape[2], q.device)
-                    if mask is not None:
-                        s = s.masked_fill(~mask, -math.inf)
-                p = torch.exp(s - lse)
-                dp = do @ ve.transpose(-1, -2)
-                ds = p * (dp - delta)
-                dq += ds @ ke * scale
-                dk_e = ds.transpose(-1, -2) @ qf * scale       # [B, Hq, Sk, D]
-                dv_e = p.transpose(-1, -2) @ do
-                dkc += dk_e.view(B, Hkv, G, -1, D).sum(2)
-                dvc += dv_e.view(B, Hkv, G, -1, D).sum(2)
+                dq_b, dk_b, dv_b = _block_backward(dout, q, kc, vc, out, lse,
+                                                   causal and src == r, scale)
+                dq += dq_b
+                dkc += dk_b
+                dvc += dv_b
             # the chunk and its gradient move on together; after P hops every
             # chunk is back at its owner with all ranks' contributions
             kc, vc, dkc, dvc = _ring_pass([kc, vc, dkc, dvc], group)

@@ -64,3 +64,50 @@ def test_context_parallel_fused_path(method):
     for p in ps:
         p.join(timeout=60)
     assert max(errs) < 3e-2, errs  # bf16 activations, same weights
+
+
+def test_ring_blocks_on_cudnn_match_sdpa():
+    """The ring's block forward / backward on cuDNN flash kernels, merged over
+    two causal chunks exactly as the ring merges them, against SDPA."""
+    import math
+
+    import torch.nn.functional as F
+
+    from complexity_framework_b200.parallel.context_parallel import (_block_backward,
+                                                                      _block_forward,
+                                                                      _cudnn_blocks)
+
+    torch.manual_seed(0)
+    B, Hq, Hkv, S, D, P = 2, 4, 2, 256, 64, 2
+    mk = lambda h: torch.randn(B, h, S, D, device="cuda").bfloat16()  # noqa: E731
+    q, k, v, go = mk(Hq), mk(Hkv), mk(Hkv), mk(Hq)
+    assert _cudnn_blocks(q)
+    qr, kr, vr = (t.float().requires_grad_() for t in (q, k, v))
+    ref = F.scaled_dot_product_attention(qr, kr, vr, is_causal=True, enable_gqa=True)
+    (ref * go.float()).sum().backward()
+    sc = D ** -0.5
+    L = S // P
+    ch = lambda t, i: t[:, :, i * L:(i + 1) * L]  # noqa: E731
+    dk = torch.zeros(B, Hkv, S, D, device="cuda")
+    dv = torch.zeros_like(dk)
+    for r in range(P):
+        lse = torch.full((B, Hq, L, 1), -math.inf, device="cuda")
+        acc = torch.zeros(B, Hq, L, D, device="cuda")
+        for src in range(r + 1):
+            o_b, lse_b = _block_forward(ch(q, r), ch(k, src), ch(v, src), src == r, sc)
+            new = torch.logaddexp(lse, lse_b)
+            acc = acc * torch.exp(lse - new) + o_b * torch.exp(lse_b - new)
+            lse = new
+        assert float((acc - ch(ref, r)).abs().max()) < 3e-2
+        out = acc.bfloat16()
+        dq = torch.zeros(B, Hq, L, D, device="cuda")
+        for src in range(r + 1):
+            a, b, c = _block_backward(ch(go, r), ch(q, r), ch(k, src), ch(v, src), out, lse,
+                                      src == r, sc)
+            dq += a
+            dk[:, :, src * L:(src + 1) * L] += b
+            dv[:, :, src * L:(src + 1) * L] += c
+        rel = float((dq - ch(qr.grad, r)).abs().max() / qr.grad.abs().max())
+        assert rel < 3e-2, rel
+    for got, want in ((dk, kr.grad), (dv, vr.grad)):
+        assert float((got - want).abs().max() / want.abs().max()) < 3e-2
