@@ -40,14 +40,31 @@ class PrefixLM(nn.Module):
 
     @torch.no_grad()
     def generate(self, prefix: torch.Tensor, bos_ids: torch.Tensor, max_new_tokens: int = 32,
-                 eos_id: Optional[int] = None) -> torch.Tensor:
-        """Greedy decoding after the prefix; returns [B, T + new] token ids."""
+                 eos_id: Optional[int] = None, use_cache: bool = True) -> torch.Tensor:
+        """Greedy decoding after the prefix; returns [B, T + new] token ids.  With
+        ``use_cache`` the prefix and prompt run once and every new token is one
+        decoder step over the key/value cache."""
+        if not use_cache:
+            ids = bos_ids
+            for _ in range(max_new_tokens):
+                nxt = self._run(prefix, ids)[:, -1].argmax(-1, keepdim=True)
+                ids = torch.cat([ids, nxt], 1)
+                if eos_id is not None and bool((nxt == eos_id).all()):
+                    break
+            return ids
+        emb = self.decoder.embed_tokens(bos_ids)
+        x = torch.cat([prefix.to(emb.dtype), emb], 1)
+        B, P = prefix.shape[:2]
+        route = torch.cat([torch.full((B, P), self.prefix_route_id, dtype=torch.long,
+                                      device=bos_ids.device), bos_ids], 1)
+        out = self.decoder(inputs_embeds=x, routing_ids=route, use_cache=True)
         ids = bos_ids
         for _ in range(max_new_tokens):
-            nxt = self._run(prefix, ids)[:, -1].argmax(-1, keepdim=True)
+            nxt = out["logits"][:, -1].argmax(-1, keepdim=True)
             ids = torch.cat([ids, nxt], 1)
             if eos_id is not None and bool((nxt == eos_id).all()):
                 break
+            out = self.decoder(nxt, past_key_values=out["past_key_values"], use_cache=True)
         return ids
 
 

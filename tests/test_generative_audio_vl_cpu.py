@@ -102,3 +102,15 @@ def test_image_text_to_text_and_tar_dataset(tmp_path):
     # the caption is decoded from the image
     out = m.generate(images[1:], torch.tensor([[1]]), max_new_tokens=4)
     assert bytes(out[0, 1:].tolist()) == b"blue"
+
+
+def test_prefix_lm_cached_generation_matches_recompute():
+    from complexity_framework_b200.generative.prefix_lm import PrefixLM
+
+    torch.manual_seed(0)
+    lm = PrefixLM(_decoder()).eval()
+    prefix = torch.randn(2, 5, 64)
+    bos = torch.tensor([[3], [7]])
+    a = lm.generate(prefix, bos, max_new_tokens=6, use_cache=True)
+    b = lm.generate(prefix, bos, max_new_tokens=6, use_cache=False)
+    assert torch.equal(a, b)
