@@ -3,7 +3,7 @@
 ``ContinuousBatcher`` keeps the reference's request/status/statistics API but
 runs on the paged engine: requests decode against their KV pages instead of
 re-running the full prefix every step (the reference batcher recomputes the
-whole padded batch per token, SURVEY §3.5).
+whole padded batch per token).
 """
 from __future__ import annotations
 

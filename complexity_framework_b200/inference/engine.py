@@ -10,7 +10,7 @@ and leave between steps; their pages return to the pool when they finish.
 API names follow complexity/inference/engine.py:25-709 (``DecodingStrategy``,
 ``GenerationConfig``, ``InferenceConfig``, ``InferenceEngine.generate``,
 ``generate_stream``, ``generate_batch``, ``add_request``/``step_serving``).
-Unlike the reference (whose paged engine cannot run, SURVEY §0.6) the cache
+Unlike the reference (whose paged engine cannot run) the cache
 is wired into the model.
 """
 from __future__ import annotations

@@ -5,8 +5,7 @@ Memory: one pool per layer of ``num_pages`` pages, each page holding
 ``k_pool[layer] : [num_pages, page_size, Hkv, D]`` (bf16 on GPU).  A sequence
 owns a list of pages; the page table maps logical block i of a sequence to a
 physical page.  Pages are allocated once per sequence for all layers (the
-reference allocated per layer while its pool held all layers, SURVEY A.3
-item 1) and attention reads the pages in place instead of gathering them into
+reference allocated per layer while its pool held all layers) and attention reads the pages in place instead of gathering them into
 a new tensor per token (reference kv_cache.py:295-308).
 
 A forward step processes a ragged batch of new tokens (prefill chunks and

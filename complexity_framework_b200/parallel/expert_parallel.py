@@ -1,4 +1,4 @@
-"""Expert parallelism for the TR-Hash FFN (absent in the reference).
+"""Expert parallelism for the TR-Hash FFN (the reference has none).
 
 Experts are sharded over an EP group: rank r owns experts
 ``[r*E/P, (r+1)*E/P)``.  Because TR-Hash routes are a pure function of the

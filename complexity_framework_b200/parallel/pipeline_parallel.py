@@ -10,8 +10,7 @@ the embedding matrix and the two copies' gradients are summed over an
 embedding group after backward, so both stay identical.
 
 The reference's hand-written schedules never communicate and run backward
-on the last stage only (complexity/parallel/pipeline_parallel.py:176-365,
-SURVEY §2.4); the names ``PipelineStage``, ``PipelineModel``,
+on the last stage only (complexity/parallel/pipeline_parallel.py:176-365); the names ``PipelineStage``, ``PipelineModel``,
 ``split_model_for_pipeline`` and ``PipelineScheduler`` are kept.
 """
 from __future__ import annotations

@@ -7,10 +7,9 @@ Shards, over a TP group of size P:
   * every routed expert: its width W (gate/up columns, down rows);
 so one decoder block needs exactly one all-reduce after attention and one
 after the FFN.  The reference shards attention only and leaves the FFN
-replicated (complexity/parallel/tensor_parallel.py:371-446, SURVEY §0.5), and
+replicated (complexity/parallel/tensor_parallel.py:371-446), and
 its backward never all-reduces the gradient of the replicated input
-(``_AllReduceFunc`` backward is identity with no copy-to-region op, SURVEY
-A.3 item 2); here ``copy_to_tp`` (identity forward, all-reduce backward) and
+(``_AllReduceFunc`` backward is identity with no copy-to-region op); here ``copy_to_tp`` (identity forward, all-reduce backward) and
 ``reduce_from_tp`` (all-reduce forward, identity backward) pair up correctly.
 
 The primitives and ``ColumnParallelLinear`` / ``RowParallelLinear`` /

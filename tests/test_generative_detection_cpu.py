@@ -95,7 +95,7 @@ def test_detector_trains_and_predicts(tmp_path):
         for im, tg in dl:
             tr.train_step(im, tg)
     after = tr.evaluate(ev, use_ema=False)["AP50"]
-    # the loss is IoU-weighted (it grows as boxes start to overlap), so judge by AP
+    # the loss is IoU-weighted (it grows as boxes start to overlap), so measure progress by AP
     assert after > max(0.2, before), (before, after)
     out = m.predict(torch.rand(2, 3, 64, 64))
     assert len(out) == 2 and set(out[0]) == {"boxes", "scores", "labels"}
