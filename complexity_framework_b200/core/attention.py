@@ -170,8 +170,9 @@ class GroupedQueryAttention(nn.Module):
         if cp is not None:  # context parallel: global positions of this rank's chunk
             from ..parallel.context_parallel import chunk_positions
 
-            pos = chunk_positions(S, cp, x.device).to(torch.int32).expand(B, S).contiguous()
-            cos, sin = self.rotary_emb.tables(int(pos[0, -1]) + 1, x.device)
+            layout = getattr(self, "cp_layout", "contiguous")
+            pos = chunk_positions(S, cp, x.device, layout).to(torch.int32).expand(B, S).contiguous()
+            cos, sin = self.rotary_emb.tables(int(pos.max()) + 1, x.device)
         else:
             cos, sin = self.rotary_emb.tables(S, x.device)
         if self.use_qk_norm:
@@ -185,7 +186,8 @@ class GroupedQueryAttention(nn.Module):
             from ..parallel.context_parallel import context_parallel_attention
 
             o = context_parallel_attention(q, k, v, cp, causal=True, scale=self.attn_scale,
-                                           method=getattr(self, "cp_method", "auto"))
+                                           method=getattr(self, "cp_method", "auto"),
+                                           layout=getattr(self, "cp_layout", "contiguous"))
             o = o.transpose(1, 2).reshape(B, S, -1)
         else:
             o = attn_ops.attention(q, k, v, causal=True, scale=self.attn_scale)  # [B, S, Hq*D]
@@ -228,11 +230,13 @@ class GroupedQueryAttention(nn.Module):
             # context parallel: this rank's chunk starts at rank * S in the sequence
             from ..parallel.context_parallel import chunk_positions, context_parallel_attention
 
-            pos = chunk_positions(S, cp, q.device)
-            cos, sin = self.rotary_emb(int(pos[-1]) + 1)
+            layout = getattr(self, "cp_layout", "contiguous")
+            pos = chunk_positions(S, cp, q.device, layout)
+            cos, sin = self.rotary_emb(int(pos.max()) + 1)
             q, k = self.rotary_emb.rotate(q, k, cos[pos].to(q.dtype), sin[pos].to(q.dtype))
             o = context_parallel_attention(q, k, v, cp, causal=True, scale=self.attn_scale,
-                                           method=getattr(self, "cp_method", "auto"))
+                                           method=getattr(self, "cp_method", "auto"),
+                                           layout=layout)
             o = o.transpose(1, 2).reshape(B, S, self.num_heads * self.head_dim)
             return self.o_proj(o), None
         past = 0 if past_key_value is None else past_key_value[0].shape[2]

@@ -162,86 +162,124 @@ def _block_backward(do, q, k, v, out, lse, causal: bool, scale: float):
     return dq, dk, dv
 
 
+def _chunk_ids(rank: int, P: int, layout: str):
+    """Global chunk ids held by ``rank``: contiguous -> [rank] of P chunks;
+    zigzag -> [rank, 2P - 1 - rank] of 2P chunks (equal causal work per rank)."""
+    return [rank] if layout == "contiguous" else [rank, 2 * P - 1 - rank]
+
+
+def _pairs(q_ids, k_ids, L: int, causal: bool):
+    """(q slice, k slice, diagonal) for every visible (query chunk, key chunk)."""
+    out = []
+    for i, cq in enumerate(q_ids):
+        for j, ck in enumerate(k_ids):
+            if causal and ck > cq:
+                continue
+            out.append((slice(i * L, (i + 1) * L), slice(j * L, (j + 1) * L), causal and ck == cq))
+    return out
+
+
 class _RingAttention(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, group, causal, scale):
+    def forward(ctx, q, k, v, group, causal, scale, layout):
         r, P = _rank_world(group)
         B, Hq, S, D = q.shape
+        q_ids = _chunk_ids(r, P, layout)
+        L = S // len(q_ids)
         lse = torch.full((B, Hq, S, 1), -math.inf, device=q.device)
         acc = torch.zeros(B, Hq, S, D, device=q.device)
         kc, vc = k, v
         for step in range(P):
             src = (r - step) % P
-            if not (causal and src > r):
-                o_b, lse_b = _block_forward(q, kc, vc, causal and src == r, scale)
-                new = torch.logaddexp(lse, lse_b)
-                acc = acc * torch.exp(lse - new) + o_b * torch.exp(lse_b - new)
-                lse = new
+            for qs, ks, diag in _pairs(q_ids, _chunk_ids(src, P, layout), L, causal):
+                o_b, lse_b = _block_forward(q[:, :, qs], kc[:, :, ks], vc[:, :, ks], diag, scale)
+                new = torch.logaddexp(lse[:, :, qs], lse_b)
+                acc[:, :, qs] = (acc[:, :, qs] * torch.exp(lse[:, :, qs] - new)
+                                 + o_b * torch.exp(lse_b - new))
+                lse[:, :, qs] = new
             if step < P - 1:
                 kc, vc = _ring_pass([kc, vc], group)
         out = acc.to(q.dtype)
         ctx.save_for_backward(q, k, v, out, lse)
-        ctx.group, ctx.causal, ctx.scale = group, causal, scale
+        ctx.group, ctx.causal, ctx.scale, ctx.layout = group, causal, scale, layout
         return out
 
     @staticmethod
     def backward(ctx, dout):
         q, k, v, out, lse = ctx.saved_tensors
-        group, causal, scale = ctx.group, ctx.causal, ctx.scale
+        group, causal, scale, layout = ctx.group, ctx.causal, ctx.scale, ctx.layout
         r, P = _rank_world(group)
+        q_ids = _chunk_ids(r, P, layout)
+        L = q.shape[2] // len(q_ids)
         dq = torch.zeros(q.shape, device=q.device)
         kc, vc = k, v
         dkc = torch.zeros(k.shape, device=k.device)
         dvc = torch.zeros(v.shape, device=v.device)
         for step in range(P):
             src = (r - step) % P
-            if not (causal and src > r):
-                dq_b, dk_b, dv_b = _block_backward(dout, q, kc, vc, out, lse,
-                                                   causal and src == r, scale)
-                dq += dq_b
-                dkc += dk_b
-                dvc += dv_b
+            for qs, ks, diag in _pairs(q_ids, _chunk_ids(src, P, layout), L, causal):
+                dq_b, dk_b, dv_b = _block_backward(dout[:, :, qs], q[:, :, qs], kc[:, :, ks],
+                                                   vc[:, :, ks], out[:, :, qs], lse[:, :, qs],
+                                                   diag, scale)
+                dq[:, :, qs] += dq_b
+                dkc[:, :, ks] += dk_b
+                dvc[:, :, ks] += dv_b
             # the chunk and its gradient move on together; after P hops every
             # chunk is back at its owner with all ranks' contributions
             kc, vc, dkc, dvc = _ring_pass([kc, vc, dkc, dvc], group)
-        return dq.to(q.dtype), dkc.to(k.dtype), dvc.to(v.dtype), None, None, None
+        return dq.to(q.dtype), dkc.to(k.dtype), dvc.to(v.dtype), None, None, None, None
 
 
 def ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, group,
-                   causal: bool = True, scale: Optional[float] = None) -> torch.Tensor:
+                   causal: bool = True, scale: Optional[float] = None,
+                   layout: str = "contiguous") -> torch.Tensor:
+    """``layout`` "zigzag": this rank's sequence is chunks r and 2P-1-r of 2P
+    (see ``split_sequence``), balancing causal work over the ranks."""
     if q.shape[1] % k.shape[1]:
         raise ValueError("query heads must be a multiple of key/value heads")
+    if layout not in ("contiguous", "zigzag"):
+        raise ValueError("layout must be 'contiguous' or 'zigzag'")
     scale = q.shape[-1] ** -0.5 if scale is None else scale
-    return _RingAttention.apply(q, k, v, group, causal, scale)
+    return _RingAttention.apply(q, k, v, group, causal, scale, layout)
 
 
 def context_parallel_attention(q, k, v, group, causal: bool = True,
-                               scale: Optional[float] = None, method: str = "auto"):
+                               scale: Optional[float] = None, method: str = "auto",
+                               layout: str = "contiguous"):
     """``method`` "ulysses" when the heads divide over the ranks (fewer, larger
-    messages), "ring" otherwise; ``auto`` picks."""
+    messages) and the layout is contiguous, "ring" otherwise; ``auto`` picks."""
     P = dist.get_world_size(group)
     if method == "auto":
-        method = "ulysses" if q.shape[1] % P == 0 else "ring"
+        method = "ulysses" if (q.shape[1] % P == 0 and layout == "contiguous") else "ring"
     if method == "ulysses":
+        if layout != "contiguous":
+            raise ValueError("ulysses attention needs the contiguous layout")
         return ulysses_attention(q, k, v, group, causal, scale)
-    return ring_attention(q, k, v, group, causal, scale)
+    return ring_attention(q, k, v, group, causal, scale, layout)
 
 
-def split_sequence(x: torch.Tensor, group, dim: int = 1) -> torch.Tensor:
-    """This rank's contiguous chunk of ``x`` along ``dim`` (length divisible by P)."""
+def split_sequence(x: torch.Tensor, group, dim: int = 1, layout: str = "contiguous") -> torch.Tensor:
+    """This rank's part of ``x`` along ``dim``: chunk r of P (contiguous), or
+    chunks r and 2P-1-r of 2P concatenated (zigzag)."""
     r, P = _rank_world(group)
-    if x.shape[dim] % P:
-        raise ValueError(f"sequence length {x.shape[dim]} not divisible by {P} ranks")
-    return x.chunk(P, dim)[r]
+    n = P if layout == "contiguous" else 2 * P
+    if x.shape[dim] % n:
+        raise ValueError(f"sequence length {x.shape[dim]} not divisible by {n} chunks")
+    chunks = x.chunk(n, dim)
+    return torch.cat([chunks[c] for c in _chunk_ids(r, P, layout)], dim)
 
 
-def chunk_positions(seq_len_local: int, group, device=None) -> torch.Tensor:
-    """Global positions of this rank's chunk (for RoPE / position embeddings)."""
-    r, _ = _rank_world(group)
-    return torch.arange(r * seq_len_local, (r + 1) * seq_len_local, device=device)
+def chunk_positions(seq_len_local: int, group, device=None,
+                    layout: str = "contiguous") -> torch.Tensor:
+    """Global positions of this rank's part (for RoPE / position embeddings)."""
+    r, P = _rank_world(group)
+    ids = _chunk_ids(r, P, layout)
+    L = seq_len_local // len(ids)
+    return torch.cat([torch.arange(c * L, (c + 1) * L, device=device) for c in ids])
 
 
-def enable_context_parallel(model: torch.nn.Module, group=None, method: str = "auto") -> int:
+def enable_context_parallel(model: torch.nn.Module, group=None, method: str = "auto",
+                            layout: str = "contiguous") -> int:
     """Make every attention layer of ``model`` attend across the sequence chunks
     of ``group`` (RoPE at global positions, ring or Ulysses attention); returns
     the number of layers switched.  Feed each rank its chunk of the inputs and
@@ -251,14 +289,17 @@ def enable_context_parallel(model: torch.nn.Module, group=None, method: str = "a
         if hasattr(m, "rotary_emb") and hasattr(m, "o_proj") and hasattr(m, "num_kv_heads"):
             m.cp_group = group if group is not None else dist.group.WORLD
             m.cp_method = method
+            m.cp_layout = layout
             n += 1
     return n
 
 
-def context_parallel_batch(input_ids: torch.Tensor, group=None, ignore_index: int = -100):
+def context_parallel_batch(input_ids: torch.Tensor, group=None, ignore_index: int = -100,
+                           layout: str = "contiguous"):
     """(this rank's input chunk, its next-token labels): labels are shifted over
     the whole sequence before splitting, so a chunk's last position predicts
     the first token of the next rank's chunk."""
     labels = torch.roll(input_ids, -1, dims=1)
     labels[:, -1] = ignore_index
-    return split_sequence(input_ids, group, 1), split_sequence(labels, group, 1)
+    return (split_sequence(input_ids, group, 1, layout),
+            split_sequence(labels, group, 1, layout))

@@ -15,7 +15,7 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, method, causal, q_out):
+def _worker(rank, world, port, method, causal, q_out, layout="contiguous"):
     import torch.distributed as dist
 
     from complexity_framework_b200.parallel.context_parallel import (
@@ -34,13 +34,13 @@ def _worker(rank, world, port, method, causal, q_out):
     o_ref = F.scaled_dot_product_attention(qr, kr, vr, is_causal=causal, enable_gqa=True)
     (o_ref * go).sum().backward()
     # this rank's chunk
-    ql, kl, vl = (split_sequence(t, None, 2).clone().requires_grad_() for t in (q, k, v))
-    o = context_parallel_attention(ql, kl, vl, None, causal=causal, method=method)
-    (o * split_sequence(go, None, 2)).sum().backward()
-    err = max(float((o - split_sequence(o_ref, None, 2)).abs().max()),
-              float((ql.grad - split_sequence(qr.grad, None, 2)).abs().max()),
-              float((kl.grad - split_sequence(kr.grad, None, 2)).abs().max()),
-              float((vl.grad - split_sequence(vr.grad, None, 2)).abs().max()))
+    sp = lambda t: split_sequence(t, None, 2, layout)  # noqa: E731
+    ql, kl, vl = (sp(t).clone().requires_grad_() for t in (q, k, v))
+    o = context_parallel_attention(ql, kl, vl, None, causal=causal, method=method, layout=layout)
+    (o * sp(go)).sum().backward()
+    err = max(float((o - sp(o_ref)).abs().max()), float((ql.grad - sp(qr.grad)).abs().max()),
+              float((kl.grad - sp(kr.grad)).abs().max()),
+              float((vl.grad - sp(vr.grad)).abs().max()))
     errs = [None] * world
     dist.all_gather_object(errs, err)
     if rank == 0:
@@ -48,15 +48,18 @@ def _worker(rank, world, port, method, causal, q_out):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("method,world", [("ring", 3), ("ring", 2), ("ulysses", 2)])
+@pytest.mark.parametrize("method,world,layout", [("ring", 3, "contiguous"),
+                                                 ("ring", 2, "contiguous"),
+                                                 ("ulysses", 2, "contiguous"),
+                                                 ("ring", 3, "zigzag")])
 @pytest.mark.parametrize("causal", [True, False])
-def test_context_parallel_matches_full_attention(method, world, causal):
+def test_context_parallel_matches_full_attention(method, world, layout, causal):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_worker, args=(r, world, port, method, causal, q))
+    ps = [ctx.Process(target=_worker, args=(r, world, port, method, causal, q, layout))
           for r in range(world)]
     for p in ps:
         p.start()
@@ -66,7 +69,7 @@ def test_context_parallel_matches_full_attention(method, world, causal):
     assert max(errs) < 1e-4, errs
 
 
-def _model_worker(rank, world, port, method, q_out):
+def _model_worker(rank, world, port, method, q_out, layout="contiguous"):
     import torch.distributed as dist
 
     from complexity_framework_b200 import ComplexityModel, ModelConfig
@@ -85,8 +88,8 @@ def _model_worker(rank, world, port, method, q_out):
     ref_loss.backward()
     ref_grads = [p.grad.clone() for p in full.parameters()]
     full.zero_grad()
-    assert enable_context_parallel(full, None, method) == 2
-    x, y = context_parallel_batch(ids, None)
+    assert enable_context_parallel(full, None, method, layout) == 2
+    x, y = context_parallel_batch(ids, None, layout=layout)
     n_local = (y != -100).sum()
     n_total = (torch.roll(ids, -1, 1)[:, :-1]).numel()
     loss = full.loss(x, y) * n_local / n_total          # this rank's share of the mean
@@ -105,14 +108,16 @@ def _model_worker(rank, world, port, method, q_out):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("method", ["ring", "ulysses"])
-def test_model_context_parallel_matches_full_sequence(method):
+@pytest.mark.parametrize("method,layout", [("ring", "contiguous"), ("ulysses", "contiguous"),
+                                           ("ring", "zigzag")])
+def test_model_context_parallel_matches_full_sequence(method, layout):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_model_worker, args=(r, 2, port, method, q)) for r in range(2)]
+    ps = [ctx.Process(target=_model_worker, args=(r, 2, port, method, q, layout))
+          for r in range(2)]
     for p in ps:
         p.start()
     errs = q.get(timeout=120)

@@ -18,7 +18,7 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, method, q_out):
+def _worker(rank, world, port, method, q_out, layout="contiguous"):
     import torch.distributed as dist
 
     from complexity_framework_b200 import ComplexityModel, ModelConfig
@@ -36,8 +36,8 @@ def _worker(rank, world, port, method, q_out):
     ids = torch.randint(0, 2048, (2, 512), generator=torch.Generator().manual_seed(3)).cuda()
     with torch.no_grad():
         ref = float(model.loss(ids))
-        enable_context_parallel(model, None, method)
-        x, y = context_parallel_batch(ids, None)
+        enable_context_parallel(model, None, method, layout)
+        x, y = context_parallel_batch(ids, None, layout=layout)
         n_local = (y != -100).sum()
         part = model.loss(x, y) * n_local / (2 * 511)
         dist.all_reduce(part)
@@ -48,8 +48,9 @@ def _worker(rank, world, port, method, q_out):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("method", ["ring", "ulysses"])
-def test_context_parallel_fused_path(method):
+@pytest.mark.parametrize("method,layout", [("ring", "contiguous"), ("ulysses", "contiguous"),
+                                           ("ring", "zigzag")])
+def test_context_parallel_fused_path(method, layout):
     import torch.multiprocessing as mp
 
     world = min(2, torch.cuda.device_count())
@@ -57,7 +58,8 @@ def test_context_parallel_fused_path(method):
     q = ctx.Queue()
     port = _port()
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    ps = [ctx.Process(target=_worker, args=(r, world, port, method, q)) for r in range(world)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, method, q, layout))
+          for r in range(world)]
     for p in ps:
         p.start()
     errs = q.get(timeout=240)
