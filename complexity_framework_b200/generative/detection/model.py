@@ -219,8 +219,8 @@ class TRHashObjectDetector(nn.Module):
             idx, lab = (p > st).nonzero(as_tuple=True)
             sc = p[idx, lab]
             bx = out["boxes"][b][idx].clamp(0, size)
-            if sc.numel() > 30000:
-                top = sc.topk(30000).indices
+            if sc.numel() > 4096:  # NMS builds a dense IoU matrix of the candidates
+                top = sc.topk(4096).indices
                 idx, lab, sc, bx = idx[top], lab[top], sc[top], bx[top]
             keep = class_aware_nms(bx, sc, lab, it)[:md]
             res.append({"boxes": bx[keep], "scores": sc[keep], "labels": lab[keep]})
