@@ -68,7 +68,9 @@ class ComplexityModel(nn.Module):
     def _init_residual_scaling(self) -> None:
         std = self.config.initializer_range / (2 * self.config.num_hidden_layers) ** 0.5
         for layer in self.layers:
-            nn.init.normal_(layer.self_attn.o_proj.weight, mean=0.0, std=std)
+            o_proj = getattr(layer.self_attn, "o_proj", None)
+            if isinstance(o_proj, nn.Linear):  # routed experts keep their zero init
+                nn.init.normal_(o_proj.weight, mean=0.0, std=std)
             engine = getattr(layer.mlp, "engine", None)
             if engine is not None:
                 nn.init.normal_(engine.expert_down, mean=0.0, std=std)
