@@ -548,3 +548,52 @@ class CausalStateConvMixer(CausalConvMixer):
         out = self.o_proj(mixed * torch.sigmoid(g))
         new = (ext[:, -(K - 1):].detach() if K > 1 else ext[:, :0], s_last) if use_cache else None
         return (out if residual is None else residual + out), new
+
+
+@register_attention("causal_fast_weight_conv")
+class CausalFastWeightConvMixer(CausalConvMixer):
+    """Gated causal convolution plus a token-addressed fast-weight memory.
+
+    Counterpart: complexity/core/attention/causal_fast_weight_conv.py:22-200.
+    The local mix (causal depthwise conv) feeds ``core.associative.
+    AssociativeMemory``: addresses from the token ids (and, with a non-zero
+    ``causal_contextual_mix_init``, from the local mix), error-correcting
+    writes when ``causal_stable_delta``.  The cache is (conv tail, memory
+    state, previous address), so decoding one token costs O(H * kernel + r^2).
+    """
+
+    def __init__(self, config: AttentionConfig):
+        super().__init__(config)
+        from .associative import AssociativeMemory
+
+        ex = config.extra
+        self.memory = AssociativeMemory(
+            config.hidden_size, int(ex.get("causal_state_rank", 16)),
+            delta=bool(ex.get("causal_stable_delta", False)),
+            contextual_mix_init=float(ex.get("causal_contextual_mix_init", 0.0)),
+            output_gate_init=float(ex.get("causal_context_gate_init", 1.0)),
+            chunk_size=int(ex.get("causal_delta_chunk_size", 256)))
+        self._token_ids: Optional[torch.Tensor] = None
+
+    def set_token_ids(self, token_ids: torch.Tensor) -> None:
+        self._token_ids = token_ids
+
+    def forward(self, hidden_states, attention_mask=None, past_key_value=None, use_cache=False,
+                residual=None, token_ids: Optional[torch.Tensor] = None, **kw):
+        ids = token_ids if token_ids is not None else self._token_ids
+        B, S, H = hidden_states.shape
+        if ids is None or tuple(ids.shape[-2:]) != (B, S) and ids.shape[-1] < S:
+            raise ValueError("causal_fast_weight_conv needs the token ids of its input")
+        ids = ids[..., -S:]
+        K = self.kernel
+        u, g = self.in_proj(hidden_states).chunk(2, -1)
+        tail = past_key_value[0] if past_key_value is not None else u.new_zeros(B, K - 1, H)
+        ext = torch.cat((tail.to(u.dtype), u), 1)
+        c = F.conv1d(ext.transpose(1, 2), self.conv.weight, self.conv.bias,
+                     groups=H).transpose(1, 2)
+        mem_state = tuple(past_key_value[1:]) if past_key_value is not None else None
+        ctx, mem_state = self.memory(c, ids, mem_state)
+        out = self.o_proj(c * torch.sigmoid(g)) + ctx.to(c.dtype)
+        new = ((ext[:, -(K - 1):].detach() if K > 1 else ext[:, :0],) + tuple(mem_state)
+               if use_cache else None)
+        return (out if residual is None else residual + out), new

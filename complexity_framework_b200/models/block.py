@@ -50,7 +50,8 @@ class TransformerBlock(nn.Module):
                 "tr_mha_num_experts", "tr_mha_adapter_rank", "tr_mha_top_k", "tr_mha_targets",
                 "causal_conv_kernel_size", "causal_state_rank", "lexical_object_rank",
                 "lexical_gqa_rank", "lexical_gqa_gate_init", "lexical_gqa_use_token_code",
-                "lexical_key_gate_init") if hasattr(config, k)})
+                "lexical_key_gate_init", "causal_stable_delta", "causal_contextual_mix_init",
+                "causal_context_gate_init", "causal_delta_chunk_size") if hasattr(config, k)})
         from ..core import attention_variants  # noqa: F401  (registers experimental types)
         attn_type = config.attention_type
         if attn_type not in ATTENTION_REGISTRY:

@@ -125,3 +125,51 @@ def test_state_conv_cached_decode_equals_full():
         o, cache = m(x[:, t:t + 1], past_key_value=cache, use_cache=True)
         outs.append(o)
     torch.testing.assert_close(torch.cat(outs, 1), full, atol=1e-5, rtol=1e-4)
+
+
+@pytest.mark.parametrize("delta", [False, True])
+def test_associative_scan_matches_recurrence(delta):
+    from complexity_framework_b200.core.associative import associative_scan
+
+    torch.manual_seed(0)
+    B, S, r = 2, 70, 8
+    q = torch.nn.functional.normalize(torch.randn(B, S, r), dim=-1)
+    k = torch.nn.functional.normalize(torch.randn(B, S, r), dim=-1)
+    v, S0 = torch.randn(B, S, r), torch.randn(B, r, r) * 0.1
+    d, w = torch.tensor(0.97), torch.tensor(0.8)
+    reads, last = associative_scan(q, k, v, S0, d, w, delta, chunk=16)
+    st = S0.clone()
+    for t in range(S):
+        torch.testing.assert_close(reads[:, t], torch.einsum("br,brc->bc", q[:, t], st),
+                                   atol=1e-4, rtol=1e-4)
+        e = v[:, t] - torch.einsum("br,brc->bc", k[:, t], st) if delta else v[:, t]
+        st = d * st + w * k[:, t, :, None] * e[:, None, :]
+    torch.testing.assert_close(last, st, atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.parametrize("delta", [False, True])
+def test_fast_weight_conv_model_and_cached_decode(delta):
+    from complexity_framework_b200.core.attention_variants import CausalFastWeightConvMixer
+
+    torch.manual_seed(0)
+    m = ComplexityModel(ModelConfig(**dict(BASE, attention_type="causal_fast_weight_conv",
+                                           causal_stable_delta=delta,
+                                           causal_contextual_mix_init=0.1)))
+    ids = torch.randint(0, 128, (2, 24))
+    loss = m.loss(ids)
+    loss.backward()
+    assert torch.isfinite(loss)
+    ids2 = ids.clone()
+    ids2[:, 12:] = (ids2[:, 12:] + 1) % 128
+    assert torch.allclose(m(ids)["logits"][:, :12], m(ids2)["logits"][:, :12], atol=1e-5)
+    mix = CausalFastWeightConvMixer(AttentionConfig(**ACFG, extra=dict(
+        causal_stable_delta=delta, causal_contextual_mix_init=0.2, causal_delta_chunk_size=4)))
+    x, tid = torch.randn(2, 11, 64), torch.randint(0, 128, (2, 11))
+    full, _ = mix(x, token_ids=tid)
+    out, cache = mix(x[:, :6], token_ids=tid[:, :6], use_cache=True)
+    outs = [out]
+    for t in range(6, 11):
+        o, cache = mix(x[:, t:t + 1], token_ids=tid[:, t:t + 1], past_key_value=cache,
+                       use_cache=True)
+        outs.append(o)
+    torch.testing.assert_close(torch.cat(outs, 1), full, atol=1e-4, rtol=1e-4)
