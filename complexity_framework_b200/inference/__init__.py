@@ -5,6 +5,7 @@ from .engine import (DecodingStrategy, GenerationConfig, InferenceConfig, Infere
 from .decoding import (LayerSkipDraft, SlidingWindowCache, SpeculativeDecoder, SpeculativeStats,
                        beam_search, paged_logits)
 from .paged import KVCache, OutOfPages, PagedBatch, PagePool, SeqChunk
+from . import chat_template  # noqa: F401  (template contract: inference.chat_template)
 
 PagedKVCache = PagePool
 
