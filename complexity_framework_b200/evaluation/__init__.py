@@ -3,7 +3,7 @@ synthetic recall probes."""
 from .benchmarks import (ARCBenchmark, BENCHMARKS, BenchmarkResult, BenchmarkRunner,
                          HellaSwagBenchmark, MMLUBenchmark, TruthfulQABenchmark,
                          WinograndeBenchmark, choice_logprobs)
-from .metrics import (bleu, compute_accuracy, compute_f1, compute_perplexity,
+from .metrics import (BertScoreEvaluator, bleu, distinct_n, self_bleu, compute_accuracy, compute_f1, compute_perplexity,
                       exact_match, expected_calibration_error, perplexity_from_loss, rouge,
                       token_f1)
 from .recall import (RecallBatch, RecallMetrics, build_associative_recall_batch,

@@ -1,5 +1,6 @@
 """Text and classification metrics: perplexity, accuracy, F1, exact match,
-BLEU, ROUGE-1/2/L, expected calibration error.
+BLEU, ROUGE-1/2/L, expected calibration error, BERTScore, distinct-n and
+self-BLEU diversity.
 
 Counterparts: complexity/evaluation/evaluator.py:31-176, :476-536 and
 metrics.py (ROUGE/BLEU).  BLEU follows Papineni et al. (2002): clipped n-gram
@@ -164,3 +165,114 @@ def expected_calibration_error(confidences: Sequence[float], correct: Sequence[b
             conf = sum(confidences[i] for i in idx) / len(idx)
             ece += len(idx) / n * abs(acc - conf)
     return ece
+
+
+# ------------------------------------------------------------ embedding / diversity
+def _hidden_states(model, ids: List[int], device) -> "torch.Tensor":
+    x = torch.tensor([ids], dtype=torch.long, device=device)
+    if _accepts(model, "return_hidden_states"):      # ComplexityModel
+        out = model(x, return_hidden_states=True, return_logits=False)
+    elif _accepts(model, "output_hidden_states"):    # HF models
+        out = model(x, output_hidden_states=True)
+    else:
+        out = model(x)
+    if isinstance(out, dict):
+        h = next((out[k] for k in ("hidden_states", "last_hidden_state", "logits")
+                  if out.get(k) is not None), None)
+    elif hasattr(out, "last_hidden_state"):
+        h = out.last_hidden_state
+    else:
+        h = out[0] if isinstance(out, (tuple, list)) else out
+    if isinstance(h, (tuple, list)):
+        h = h[-1]
+    return h[0].float()
+
+
+def _accepts(model, name: str) -> bool:
+    import inspect
+
+    try:
+        return name in inspect.signature(model.forward).parameters
+    except (TypeError, ValueError):
+        return False
+
+
+class BertScoreEvaluator:
+    """BERTScore with any token encoder (greedy cosine matching of contextual
+    token embeddings, Zhang et al. 2020): precision averages, over candidate
+    tokens, the best cosine to a reference token; recall the reverse; F1 their
+    harmonic mean.  ``pooling="mean"`` instead compares mean-pooled sentence
+    embeddings, the counterpart's definition.
+
+    Counterpart: complexity/evaluation/metrics.py:290-358.  ``encode`` maps a
+    string to token ids (a ``Tokenizer`` of this package, an HF tokenizer, or a
+    callable); the model returns hidden states ([1, T, D]) or a dict / output
+    object carrying them.
+    """
+
+    def __init__(self, model, tokenizer, device=None, pooling: str = "greedy"):
+        import torch
+
+        if pooling not in ("greedy", "mean"):
+            raise ValueError("pooling must be 'greedy' or 'mean'")
+        self.model, self.tokenizer, self.pooling = model, tokenizer, pooling
+        if device is None:
+            params = list(model.parameters()) if hasattr(model, "parameters") else []
+            device = params[0].device if params else torch.device("cpu")
+        self.device = device
+
+    def _ids(self, text: str) -> List[int]:
+        tok = self.tokenizer
+        ids = tok.encode(text) if hasattr(tok, "encode") else tok(text)
+        if isinstance(ids, dict):
+            ids = ids["input_ids"]
+        return list(ids) or [0]
+
+    def _embed(self, text: str):
+        import torch
+
+        with torch.no_grad():
+            h = _hidden_states(self.model, self._ids(text), self.device)
+        return torch.nn.functional.normalize(h, dim=-1)
+
+    def score(self, predictions: Sequence[str], references: Sequence[str]) -> Dict[str, float]:
+        if len(predictions) != len(references):
+            raise ValueError("predictions and references differ in length")
+        P, R, F = [], [], []
+        for pred, ref in zip(predictions, references):
+            a, b = self._embed(pred), self._embed(ref)
+            if self.pooling == "mean":
+                import torch
+
+                s = float(torch.nn.functional.cosine_similarity(a.mean(0), b.mean(0), dim=0))
+                p = r = s
+            else:
+                sim = a @ b.T
+                p = float(sim.max(1).values.mean())
+                r = float(sim.max(0).values.mean())
+            P.append(p)
+            R.append(r)
+            F.append(2 * p * r / (p + r) if p + r > 0 else 0.0)
+        n = max(1, len(F))
+        return {"precision": sum(P) / n, "recall": sum(R) / n, "f1": sum(F) / n}
+
+
+def distinct_n(texts: Sequence[str], max_n: int = 4) -> Dict[str, float]:
+    """Unique / total n-grams over all texts, per n (higher = more diverse)."""
+    out = {}
+    for n in range(1, max_n + 1):
+        grams = Counter()
+        for t in texts:
+            grams.update(_ngrams(t.lower().split(), n))
+        total = sum(grams.values())
+        out[f"distinct_{n}"] = len(grams) / total if total else 0.0
+    return out
+
+
+def self_bleu(texts: Sequence[str], max_n: int = 4) -> float:
+    """Mean BLEU of each text against the others (lower = more diverse)."""
+    if len(texts) < 2:
+        return 0.0
+    scores = [bleu([t], [[o for j, o in enumerate(texts) if j != i]], max_n=max_n)
+              for i, t in enumerate(texts)]
+    return sum(scores) / len(scores)
