@@ -1,6 +1,6 @@
 """Data library: token shards (native memory-mapped reader), batch loaders,
 packing, tokenizers, chat templates, streaming datasets and mixtures."""
-from .loader import (CUDAPrefetcher, DataConfig, DistributedDataLoader, InfiniteDataLoader,
+from .loader import (BackgroundTokenizer, CUDAPrefetcher, DataConfig, DistributedDataLoader, InfiniteDataLoader,
                      SyntheticTokenDataset, TokenBatchLoader, create_dataloader)
 from .packing import (PackedSequenceCollator, document_attention_mask, pack_documents,
                       packed_labels_and_positions, packing_efficiency)

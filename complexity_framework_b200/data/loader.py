@@ -248,3 +248,86 @@ class SyntheticTokenDataset(IterableDataset):
             ids = (g.zipf(self.a, size=self.seq_len + 1) - 1) % self.vocab_size
             t = torch.from_numpy(ids.astype(np.int64))
             yield {"input_ids": t[:-1], "labels": t[1:]}
+
+
+class BackgroundTokenizer:
+    """Tokenize text on a worker thread while the GPU computes; hand out
+    ``[max_length + 1]`` training windows from the token stream.
+
+    Counterpart: complexity/gpu/data_loading.py:87-120.  ``submit`` only
+    enqueues (the caller never waits for the tokenizer); the worker encodes,
+    appends an optional ``eos_id`` separator, and grows the token buffer.
+    Consecutive windows share one token (the last target of a window is the
+    first input of the next), so no token is dropped between windows.
+    ``get_batch`` returns None until a full window is buffered (``block=True``
+    waits for one, or until ``close``).
+    """
+
+    def __init__(self, tokenizer, max_length: int = 2048, buffer_size: int = 100,
+                 eos_id: Optional[int] = None):
+        self.tokenizer, self.max_length, self.eos_id = tokenizer, int(max_length), eos_id
+        self._texts: "queue.Queue[Optional[str]]" = queue.Queue(maxsize=max(1, buffer_size))
+        self._tokens: list = []
+        self._cv = threading.Condition()
+        self._closed = False
+        self._error: Optional[BaseException] = None
+        self._worker = threading.Thread(target=self._run, daemon=True)
+        self._worker.start()
+
+    def _run(self) -> None:
+        while True:
+            text = self._texts.get()
+            if text is None:
+                break
+            try:
+                ids = list(self.tokenizer.encode(text))
+            except BaseException as e:  # surfaced to the consumer
+                with self._cv:
+                    self._error = e
+                    self._cv.notify_all()
+                break
+            if self.eos_id is not None:
+                ids.append(int(self.eos_id))
+            with self._cv:
+                self._tokens.extend(ids)
+                self._cv.notify_all()
+        with self._cv:
+            self._closed = True
+            self._cv.notify_all()
+
+    def submit(self, text: str) -> None:
+        if self._closed:
+            raise RuntimeError("BackgroundTokenizer is closed")
+        self._texts.put(text)
+
+    def buffered_tokens(self) -> int:
+        with self._cv:
+            return len(self._tokens)
+
+    def get_batch(self, block: bool = False, timeout: Optional[float] = None
+                  ) -> Optional[torch.Tensor]:
+        need = self.max_length + 1
+        with self._cv:
+            if block:
+                self._cv.wait_for(lambda: len(self._tokens) >= need or self._closed
+                                  or self._error is not None, timeout)
+            if self._error is not None:
+                raise RuntimeError("tokenizer failed in the background") from self._error
+            if len(self._tokens) < need:
+                return None
+            window = self._tokens[:need]
+            del self._tokens[:self.max_length]
+        return torch.tensor(window, dtype=torch.long)
+
+    def close(self) -> None:
+        """Finish the submitted texts and stop the worker."""
+        if not self._closed:
+            self._texts.put(None)
+            self._worker.join()
+
+    def __iter__(self) -> Iterator[torch.Tensor]:
+        while True:
+            b = self.get_batch(block=True)
+            if b is None:
+                return
+            yield b
