@@ -4,4 +4,4 @@ from .rewards import (combined_reward, extract_answer, format_reward, language_q
                       mcq_exact_match_reward)
 from .online import SharedOnlineRLConfig, SharedOnlineRLLoop, SharedRLEvent
 from .tool_rewards import (VerifiedToolEpisode, build_verified_tool_episode, parse_tool_call,
-                           safe_calculator, safe_datetime, tool_call_reward, tool_rewards)
+                           batch_tool_rewards, safe_calculator, safe_datetime, tool_call_reward)

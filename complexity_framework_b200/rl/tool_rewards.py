@@ -212,6 +212,6 @@ def tool_call_reward(completion: str, episode: VerifiedToolEpisode,
     return r
 
 
-def tool_rewards(completions: List[str], episode: VerifiedToolEpisode) -> List[float]:
+def batch_tool_rewards(completions: List[str], episode: VerifiedToolEpisode) -> List[float]:
     """Batch form for a GRPO group sampled from one prompt."""
     return [tool_call_reward(c, episode) for c in completions]

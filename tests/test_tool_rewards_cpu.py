@@ -36,4 +36,4 @@ def test_reward_scores_completions():
     assert tr.tool_call_reward(wrong_call, ep) == pytest.approx(0.2 + 0.4)
     assert tr.tool_call_reward("42", ep) == pytest.approx(0.4)
     assert tr.tool_call_reward("<tool_call>{bad json</tool_call> 41", ep) == 0.0
-    assert tr.tool_rewards([ep.target_response, "no"], ep) == [pytest.approx(1.0), 0.0]
+    assert tr.batch_tool_rewards([ep.target_response, "no"], ep) == [pytest.approx(1.0), 0.0]
