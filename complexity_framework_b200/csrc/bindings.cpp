@@ -363,16 +363,32 @@ void ep_gather_combine(const std::vector<int64_t>& srcs, const torch::Tensor& id
   raise_rc(rc, "ep_gather_combine");
 }
 
-// Causal/full attention forward; writes out [B,S,Hq*D] and lse [B,Hq,S].
+// [B, H, S, D] bf16 view with a contiguous last dim and 16-byte aligned rows
+// (TMA requirements) -> strided descriptor.
+cfb::Bhsd bhsd_of(const torch::Tensor& t, const char* name) {
+  check_bf16_cuda(t, name);
+  TORCH_CHECK(t.dim() == 4, name, " must be [B, H, S, D]");
+  TORCH_CHECK(t.stride(3) == 1, name, " must have a contiguous last dimension");
+  for (int i = 0; i < 3; ++i)
+    TORCH_CHECK(t.size(i) == 1 || t.stride(i) % 8 == 0, name,
+                " strides must be multiples of 8 elements");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
+  cfb::Bhsd d;
+  d.p = t.data_ptr();
+  d.sb = t.stride(0);
+  d.sh = t.stride(1);
+  d.ss = t.stride(2);
+  return d;
+}
+
+// Causal/full attention forward; q [B,Hq,S,D] and k/v [B,Hkv,S,D] views (any
+// strides, last dim contiguous); writes out [B,S,Hq*D] and lse [B,Hq,S].
 void flash_attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
                     torch::Tensor& out, torch::Tensor& lse, double scale, bool causal) {
-  check_bf16_cuda(q, "q");
-  check_bf16_cuda(k, "k");
-  check_bf16_cuda(v, "v");
+  const cfb::Bhsd dq = bhsd_of(q, "q"), dk = bhsd_of(k, "k"), dv = bhsd_of(v, "v");
   check_bf16_cuda(out, "out");
-  TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && out.is_contiguous(),
-              "flash_attn_fwd: tensors must be contiguous");
-  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.sizes() == k.sizes(), "q/k/v must be [B,H,S,D]");
+  TORCH_CHECK(out.is_contiguous(), "flash_attn_fwd: out must be contiguous");
+  TORCH_CHECK(v.sizes() == k.sizes(), "k/v shapes differ");
   const int64_t B = q.size(0), Hq = q.size(1), S = q.size(2), D = q.size(3), Hkv = k.size(1);
   TORCH_CHECK(k.size(0) == B && k.size(2) == S && k.size(3) == D, "k shape");
   TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128");
@@ -382,11 +398,41 @@ void flash_attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch:
                   lse.numel() == B * Hq * S,
               "lse must be fp32 [B,Hq,S]");
   const c10::cuda::CUDAGuard guard(q.device());
-  const int rc = cfb::flash_fwd_launch(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
-                                       lse.data_ptr<float>(), B, Hq, Hkv, S, D,
-                                       static_cast<float>(scale), causal,
+  const int rc = cfb::flash_fwd_launch(dq, dk, dv, out.data_ptr(), lse.data_ptr<float>(), B, Hq,
+                                       Hkv, S, D, static_cast<float>(scale), causal,
                                        at::cuda::getCurrentCUDAStream(), err_ptr(q.get_device()));
   raise_rc(rc, "flash_attn_fwd");
+}
+
+// Backward of flash_attn_fwd.  o, dout, dq: [B,Hq,S,D] views (the token-major
+// [B,S,Hq*D] output seen through a transposed view is fine); dk, dv like k.
+void flash_attn_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
+                    const torch::Tensor& o, const torch::Tensor& lse, const torch::Tensor& dout,
+                    torch::Tensor& dq, torch::Tensor& dk, torch::Tensor& dv, double scale,
+                    bool causal) {
+  const cfb::Bhsd bq = bhsd_of(q, "q"), bk = bhsd_of(k, "k"), bv = bhsd_of(v, "v");
+  const cfb::Bhsd bo = bhsd_of(o, "o"), bdo = bhsd_of(dout, "dout"), bdq = bhsd_of(dq, "dq");
+  const cfb::Bhsd bdk = bhsd_of(dk, "dk"), bdv = bhsd_of(dv, "dv");
+  const int64_t B = q.size(0), Hq = q.size(1), S = q.size(2), D = q.size(3), Hkv = k.size(1);
+  TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128");
+  TORCH_CHECK(Hq % Hkv == 0, "Hq must be a multiple of Hkv");
+  TORCH_CHECK(k.sizes() == v.sizes() && dk.sizes() == k.sizes() && dv.sizes() == k.sizes() &&
+                  k.size(0) == B && k.size(2) == S && k.size(3) == D,
+              "k/v/dk/dv must be [B,Hkv,S,D]");
+  TORCH_CHECK(o.sizes() == q.sizes() && dout.sizes() == q.sizes() && dq.sizes() == q.sizes(),
+              "o/dout/dq must be [B,Hq,S,D]");
+  TORCH_CHECK(dk.strides() == dv.strides(), "dk and dv must share strides");
+  TORCH_CHECK(lse.scalar_type() == torch::kFloat32 && lse.is_contiguous() &&
+                  lse.numel() == B * Hq * S,
+              "lse must be fp32 [B,Hq,S]");
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto work = torch::empty({cfb::flash_bwd_workspace_floats(B, Hq, S, D)},
+                           torch::dtype(torch::kFloat32).device(q.device()));
+  const int rc = cfb::flash_bwd_launch(bq, bk, bv, bo, bdo, lse.data_ptr<float>(), bdq, bdk, bdv,
+                                       B, Hq, Hkv, S, D, static_cast<float>(scale), causal,
+                                       work.data_ptr<float>(), at::cuda::getCurrentCUDAStream(),
+                                       err_ptr(q.get_device()));
+  raise_rc(rc, "flash_attn_bwd");
 }
 
 cfb::PeerPtrs make_peers(const std::vector<int64_t>& grad, const std::vector<int64_t>& param,
@@ -473,6 +519,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("stats") = py::none(), py::arg("bn") = 0);
   m.def("gemm_choose_bn", &gemm_choose_bn);
   m.def("flash_attn_fwd", &flash_attn_fwd);
+  m.def("flash_attn_bwd", &flash_attn_bwd);
   m.def("dp_reduce_shard", &dp_reduce_shard);
   m.def("dp_adamw_shard", &dp_adamw_shard);
   register_elementwise(m);

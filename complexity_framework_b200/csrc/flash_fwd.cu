@@ -3,8 +3,10 @@
 //   O[b, s, h, :] = softmax(scale * Q[b,h,s,:] K[b,g(h),:,:]^T) V[b,g(h),:,:]
 //   LSE[b, h, s]  = log(sum_k exp(scale * q.k))          (for the backward)
 //
-// q: [B, Hq, S, D], k/v: [B, Hkv, S, D] (head-major, bf16), GQA group g(h) =
-// h / (Hq/Hkv) -- K/V are never replicated.  O is written token-major
+// q: [B, Hq, S, D], k/v: [B, Hkv, S, D] (bf16, any strides along b, h, s with d
+// contiguous: head-major, or the token-major q written by the QK-norm/RoPE
+// kernel, read in place through 4-D TMA maps), GQA group g(h) = h / (Hq/Hkv)
+// -- K/V are never replicated.  O is written token-major
 // [B, S, Hq*D] so the o_proj GEMM reads it directly.  D in {64, 128}.
 //
 // One CTA per (NQ x 128 query rows, b*Hq); NQ = 2 for head_dim 64, 1 for 128.
@@ -105,8 +107,6 @@ __global__ void __launch_bounds__(FlashCfg<D>::THREADS, 1)
   const int q0 = qt * CTA_Q;
   const int nkv_all = (S + kKT - 1) / kKT;
   const int nkv = causal ? min(nkv_all, (min(q0 + CTA_Q, S) - 1) / kKT + 1) : nkv_all;
-  const int q_row0 = (b * Hq + h) * S + q0;        // row in the [B*Hq*S, D] view
-  const int kv_row0 = (b * Hkv + g) * S;           // row of key 0 in the [B*Hkv*S, D] view
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
@@ -138,8 +138,8 @@ __global__ void __launch_bounds__(FlashCfg<D>::THREADS, 1)
       for (int x = 0; x < NQ; ++x)
 #pragma unroll
         for (int c = 0; c < Cfg::CHUNKS; ++c)
-          tma_load_2d(sQ + x * Cfg::Q_BYTES + c * kQT * 128, &tmQ, &bars->q_full, c * 64,
-                      q_row0 + x * kQT);
+          tma_load_4d(sQ + x * Cfg::Q_BYTES + c * kQT * 128, &tmQ, &bars->q_full, c * 64,
+                      q0 + x * kQT, h, b);
       for (int j = 0; j < nkv; ++j) {
         const int st = j % STAGES;
         const uint32_t ph = (j / STAGES) & 1;
@@ -147,10 +147,10 @@ __global__ void __launch_bounds__(FlashCfg<D>::THREADS, 1)
         mbar_arrive_expect_tx(&bars->kv_full[st], Cfg::K_BYTES + Cfg::V_BYTES);
 #pragma unroll
         for (int c = 0; c < Cfg::CHUNKS; ++c) {
-          tma_load_2d(sK + st * Cfg::K_BYTES + c * kKT * 128, &tmK, &bars->kv_full[st], c * 64,
-                      kv_row0 + j * kKT);
-          tma_load_2d(sV + st * Cfg::V_BYTES + c * kKT * 128, &tmV, &bars->kv_full[st], c * 64,
-                      kv_row0 + j * kKT);
+          tma_load_4d(sK + st * Cfg::K_BYTES + c * kKT * 128, &tmK, &bars->kv_full[st], c * 64,
+                      j * kKT, g, b);
+          tma_load_4d(sV + st * Cfg::V_BYTES + c * kKT * 128, &tmV, &bars->kv_full[st], c * 64,
+                      j * kKT, g, b);
         }
       }
     }
@@ -365,15 +365,15 @@ __global__ void __launch_bounds__(FlashCfg<D>::THREADS, 1)
 
 }  // namespace
 
-int flash_fwd_launch(const void* q, const void* k, const void* v, void* out, float* lse, int B,
+int flash_fwd_launch(const Bhsd& q, const Bhsd& k, const Bhsd& v, void* out, float* lse, int B,
                      int Hq, int Hkv, int S, int D, float scale, bool causal, cudaStream_t stream,
                      int* err) {
   if (D != 64 && D != 128) return -2;
   if (Hq % Hkv) return -3;
   CUtensorMap tq, tk, tv;
-  int rc = make_tmap_2d(&tq, q, static_cast<int64_t>(B) * Hq * S, D, D, 64, kQT);
-  if (!rc) rc = make_tmap_2d(&tk, k, static_cast<int64_t>(B) * Hkv * S, D, D, 64, kKT);
-  if (!rc) rc = make_tmap_2d(&tv, v, static_cast<int64_t>(B) * Hkv * S, D, D, 64, kKT);
+  int rc = make_bhsd_map(&tq, q, B, Hq, S, D, kQT);
+  if (!rc) rc = make_bhsd_map(&tk, k, B, Hkv, S, D, kKT);
+  if (!rc) rc = make_bhsd_map(&tv, v, B, Hkv, S, D, kKT);
   if (rc) return rc;
   const float sl2 = scale * 1.4426950408889634f;
   if (D == 64) {

@@ -766,7 +766,20 @@ __global__ void __launch_bounds__(384, 1)
 }
 
 // ---------------------------------------------------------------- host side
+// cuTensorMapEncodeTiled is a driver call: it fails with CUDA_ERROR_INVALID_CONTEXT
+// on a host thread that has no current context yet (a fresh thread whose only
+// CUDA work so far was served from PyTorch's caching allocator, e.g. the
+// autograd engine's worker thread).  Make the current device's primary context
+// current on such threads first.
+void ensure_current_context() {
+  CUcontext ctx = nullptr;
+  if (cuCtxGetCurrent(&ctx) == CUDA_SUCCESS && ctx != nullptr) return;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaSetDevice(dev);
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  ensure_current_context();
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (fn == nullptr) {
     cudaDriverEntryPointQueryResult q;
@@ -791,6 +804,30 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : static_cast<int>(r) + 1000;
+}
+
+// Generic tiled map: `rank` dims (innermost first), byte strides of dims 1..rank-1,
+// element type bf16 (fp32 = false) or fp32, 128-byte swizzle or none.  Rows
+// outside the tensor read as zero.
+int make_tmap_nd(CUtensorMap* map, const void* base, int rank, const int64_t* dims,
+                 const int64_t* byte_strides, const int* box, bool fp32, bool swizzle128) {
+  auto fn = get_encode_fn();
+  if (fn == nullptr) return -1;
+  if (rank < 1 || rank > 5) return -2;
+  cuuint64_t d[5], st[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = static_cast<cuuint64_t>(dims[i]);
+    bx[i] = static_cast<cuuint32_t>(box[i]);
+    es[i] = 1;
+    if (i > 0) st[i - 1] = static_cast<cuuint64_t>(byte_strides[i - 1]);
+  }
+  CUresult r = fn(map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                  static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, st, bx, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : static_cast<int>(r) + 1000;
 }

@@ -107,7 +107,11 @@ int gemm_tc_launch(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream, in
 int choose_bn(int M, int N, int num_sms);
 int make_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
                  int box_inner, int box_outer);
-// Same, for epilogue stores: 32 x 32 boxes with 64-byte swizzle.
+// Tiled map of `rank` (<= 5) dims given innermost first; byte_strides[i] is the
+// stride of dim i+1.  bf16 or fp32 elements, 128-byte swizzle or none.
+int make_tmap_nd(CUtensorMap* map, const void* base, int rank, const int64_t* dims,
+                 const int64_t* byte_strides, const int* box, bool fp32, bool swizzle128);
+// 2-D map for epilogue stores: 32 x 32 boxes with 64-byte swizzle.
 int make_tmap_2d_store(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
                        int64_t ld);
 

@@ -64,6 +64,10 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 extern "C" __attribute__((visibility("default"))) int cfb_weight_grad_noalloc(
     const void* dy, const void* x, int T, int N, int K, void* dw, cudaStream_t stream) {
+  // report (and leave in place) an error that earlier work left pending, so
+  // that this call never returns, or clears, a failure that is not its own
+  const cudaError_t pending = cudaPeekAtLastError();
+  if (pending != cudaSuccess) return static_cast<int>(pending);
   if (T <= 0 || N <= 0 || K <= 0) return -2;
   if (static_cast<uint64_t>(N) * static_cast<uint64_t>(K) > CFB_NOALLOC_MAX_ELEMS) return -1;
   // TMA operands: 16-byte aligned rows (N and K multiples of 8); epilogue: K % 32
@@ -96,9 +100,28 @@ extern "C" __attribute__((visibility("default"))) int cfb_weight_grad_noalloc(
   ep.ldc = K;
   ep.alpha = 1.0f;
   const int rc = cfb::gemm_tc_launch(g, ep, stream, slots.err);
-  if (rc != 0) return rc;
+  if (rc >= 1000) return rc;              // tensor-map encode failure: 1000 + CUresult
+  if (rc < 0) return -3;                  // internal launch failure
+  if (rc != 0) return rc;                 // cudaError_t
   const int grid = static_cast<int>((elems + 255) / 256 < 4096 ? (elems + 255) / 256 : 4096);
   cast_f32_to_bf16<<<grid, 256, 0, stream>>>(slots.acc, static_cast<__nv_bfloat16*>(dw),
                                              static_cast<int64_t>(elems));
   return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" __attribute__((visibility("default"))) int cfb_weight_grad_noalloc_status(
+    int out[4], cudaStream_t stream) {
+  if (out == nullptr) return -2;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (dev < 0 || dev >= kMaxDevices) return -2;
+  DeviceSlots slots;
+  const int rc0 = resolve_slots(dev, &slots);
+  if (rc0 != 0) return rc0;
+  e = cudaMemcpyAsync(out, slots.err, 4 * sizeof(int), cudaMemcpyDeviceToHost, stream);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  e = cudaMemsetAsync(slots.err, 0, 4 * sizeof(int), stream);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  return static_cast<int>(cudaStreamSynchronize(stream));
 }

@@ -23,9 +23,18 @@ extern "C" {
 
 // dW[N, K] (bf16, row-major) = dY^T X for dY [T, N] and X [T, K] (bf16, row-major,
 // leading dimensions N and K), i.e. the weight gradient of y = x W^T.
-// Returns 0 on success; a negative value for invalid arguments (-1 when
-// N*K exceeds CFB_NOALLOC_MAX_ELEMS, -2 for bad shapes or alignment); a
-// positive CUDA error code otherwise.  Allocates nothing.
+// Allocates nothing.  Return codes:
+//    0          the work was enqueued on `stream`
+//   -1          N*K exceeds CFB_NOALLOC_MAX_ELEMS
+//   -2          bad shape, alignment or device index
+//   -3          internal launch failure (the driver's tensor-map entry point is
+//               missing, or the GEMM rejected its configuration)
+//   1..999      a cudaError_t from this call's own CUDA calls, or an error that
+//               earlier work on this thread left pending (returned unchanged
+//               and left in place: this call then enqueues nothing)
+//   1000+r      the driver refused to encode an operand tensor map (CUresult r)
+// A device-side failure (a bounded wait inside the GEMM that timed out) is
+// not visible in the return code: read it with cfb_weight_grad_noalloc_status.
 //
 // Use:
 //  * The first call on a device looks up the device address of the built-in
@@ -38,6 +47,14 @@ extern "C" {
 //  * `stream` may be 0 (the legacy default stream).
 int cfb_weight_grad_noalloc(const void* dy, const void* x, int T, int N, int K, void* dw,
                             cudaStream_t stream);
+
+// Device-side status of the calls on the current device: waits for `stream`,
+// copies the error word into out[4] (out[0]: first error code, 0 = none;
+// 1: bounded wait of a stage that never filled, 2: of a stage that never
+// emptied, 3: of the accumulator hand-off; out[1]: site; out[2]: block;
+// out[3]: number of errors) and clears it.  Allocates nothing.  Returns 0, or
+// a cudaError_t / -2 like cfb_weight_grad_noalloc.
+int cfb_weight_grad_noalloc_status(int out[4], cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -17,6 +17,7 @@ SOURCES = [
     "gemm_tc.cu",
     "elementwise.cu",
     "flash_fwd.cu",
+    "flash_bwd.cu",
     "paged_attn.cu",
     "dist_fused.cu",
     "noalloc.cu",
@@ -24,6 +25,12 @@ SOURCES = [
     "ep_fused.cu",
     "pack.cu",
 ]
+
+# Link the shared system libstdc++ (the one libtorch uses).  The compiler wrapper
+# in this image cannot open its own libstdc++.so and would silently fall back to
+# libstdc++.a: a private static copy whose stream/locale state is never set up,
+# so formatting any error message inside the extension would crash.
+LINK_ARGS = ["-L/usr/lib/x86_64-linux-gnu", "-l:libstdc++.so.6"]
 
 NVCC_FLAGS = [
     "-O3",
@@ -40,6 +47,7 @@ ext = CUDAExtension(
     include_dirs=[os.path.join(HERE, CSRC)],
     extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
     libraries=["cuda"],
+    extra_link_args=LINK_ARGS,
 )
 
 # host-side data IO (memory-mapped token shards, batch gather, packing)
@@ -47,6 +55,7 @@ io_ext = CppExtension(
     name="complexity_framework_b200._io",
     sources=[os.path.join(CSRC, "io", "token_io.cpp")],
     extra_compile_args={"cxx": ["-O3", "-std=c++17"]},
+    extra_link_args=LINK_ARGS,
 )
 
 setup(

@@ -43,3 +43,52 @@ def test_flash_no_errors():
 
     torch.cuda.synchronize()
     check_errors(0)
+
+
+def _ref_grads(q, k, v, causal, scale, dout):
+    """fp32 autograd gradients of attention with K/V repeated per group."""
+    qf = q.detach().float().requires_grad_()
+    kf = k.detach().float().requires_grad_()
+    vf = v.detach().float().requires_grad_()
+    o, _ = _ref(qf, kf, vf, causal, scale)
+    o.backward(dout.float())
+    return o, qf.grad, kf.grad, vf.grad
+
+
+def _close(a, b, what):
+    err = (a.float() - b).abs().max().item()
+    tol = 2e-2 * b.abs().max().item() + 2e-3
+    assert err < tol, f"{what}: max err {err} > {tol}"
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,S,D,causal,token_major", [
+    (2, 4, 2, 256, 64, True, True), (1, 14, 2, 2048, 64, True, True),
+    (2, 4, 4, 384, 128, True, True), (1, 2, 1, 200, 64, True, False),
+    (2, 4, 2, 256, 64, False, False), (1, 2, 2, 130, 128, True, False),
+    (1, 4, 1, 320, 128, False, True)])
+def test_flash_backward(B, Hq, Hkv, S, D, causal, token_major):
+    from complexity_framework_b200.ops.flash import flash_attention
+
+    g = torch.Generator(device="cpu").manual_seed(7 * S + D)
+    if token_major:  # the layout the QK-norm/RoPE kernel writes
+        q = torch.randn(B, S, Hq, D, generator=g).cuda().bfloat16().transpose(1, 2)
+    else:
+        q = torch.randn(B, Hq, S, D, generator=g).cuda().bfloat16()
+    k = torch.randn(B, Hkv, S, D, generator=g).cuda().bfloat16()
+    v = torch.randn(B, Hkv, S, D, generator=g).cuda().bfloat16()
+    dout = torch.randn(B, S, Hq * D, generator=g).cuda().bfloat16()
+    scale = 1 / math.sqrt(D)
+    qg, kg, vg = (t.detach().requires_grad_() for t in (q, k, v))
+    out = flash_attention(qg, kg, vg, causal=causal, scale=scale)
+    out.backward(dout)
+    ro, rdq, rdk, rdv = _ref_grads(q, k, v, causal, scale, dout)
+    _close(out, ro, "out")
+    _close(qg.grad, rdq, "dq")
+    _close(kg.grad, rdk, "dk")
+    _close(vg.grad, rdv, "dv")
+    if token_major:  # dq keeps q's token-major memory layout
+        assert qg.grad.transpose(1, 2).is_contiguous()
+    from complexity_framework_b200.ops import check_errors
+
+    torch.cuda.synchronize()
+    check_errors(0)

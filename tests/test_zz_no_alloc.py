@@ -28,6 +28,18 @@ def _entry():
     return fn
 
 
+def _status():
+    import complexity_framework_b200._C as ext
+
+    lib = ctypes.CDLL(ext.__file__)
+    fn = lib.cfb_weight_grad_noalloc_status
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]
+    out = (ctypes.c_int * 4)(-1, -1, -1, -1)
+    rc = fn(out, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    return rc, list(out)
+
+
 def _call(fn, dy, x, out):
     T, N = dy.shape
     K = x.shape[1]
@@ -55,6 +67,8 @@ def test_noalloc_weight_grad_matches_existing_entry_point():
         torch.cuda.synchronize()
         _check(out, ref)
         _check(out, dy.float().t() @ x.float())   # and the fp32 definition
+        # no bounded wait of the GEMM timed out, and the status word reads clear
+        assert _status() == (0, [0, 0, 0, 0])
 
 
 def test_noalloc_rejects_oversized_output():
