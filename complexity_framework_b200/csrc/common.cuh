@@ -354,6 +354,15 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
       : "memory");
 }
 
+// 32 lanes x 8 columns store.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(
+                   taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+               "r"(r[7])
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -468,9 +477,71 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Same packing on the integer ALU instead of the conversion unit (which shares
+// the XU pipe with ex2/tanh and limits exp-heavy kernels): round half away from
+// zero by adding half a bf16 ulp to the fp32 bit pattern, then keep the high
+// halves.  Differs from round-to-nearest-even only on exact ties.  Finite
+// inputs only (no NaN payload handling).
+__device__ __forceinline__ uint32_t pack_bf16x2_alu(float lo, float hi) {
+  const uint32_t a = __float_as_uint(lo) + 0x8000u;
+  const uint32_t b = __float_as_uint(hi) + 0x8000u;
+  return __byte_perm(a, b, 0x7632);
+}
+
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
   __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&u);
   return __bfloat1622float2(v);
+}
+
+// packed fp32x2 arithmetic (one instruction for two lanes of a float2)
+__device__ __forceinline__ uint64_t f2_as_u64(float2 v) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
+  return r;
+}
+__device__ __forceinline__ float2 u64_as_f2(uint64_t u) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(u));
+  return v;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(f2_as_u64(a)), "l"(f2_as_u64(b)),
+      "l"(f2_as_u64(c)));
+  return u64_as_f2(r);
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_as_u64(a)), "l"(f2_as_u64(b)));
+  return u64_as_f2(r);
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_as_u64(a)), "l"(f2_as_u64(b)));
+  return u64_as_f2(r);
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_as_u64(a)), "l"(f2_as_u64(b)));
+  return u64_as_f2(r);
+}
+
+// 2^x for two values on the FMA pipe (no MUFU), for x <= ~0 as in softmax:
+// x = j + f with j = round(x) (adding 1.5 * 2^23 rounds to an integer in the
+// mantissa) and f in [-1/2, 1/2]; 2^f from a cubic fitted to relative error
+// (max 7.6e-5, below half a bf16 ulp by a factor of 50); 2^j enters as j added
+// to the exponent bits.  x is clamped to -125 so the result stays normal
+// (2^-125 is zero for every use of a bf16 probability).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x = make_float2(fmaxf(x.x, -125.f), fmaxf(x.y, -125.f));
+  const float2 t = add2(x, make_float2(kRound, kRound));
+  const float2 f = sub2(x, sub2(t, make_float2(kRound, kRound)));
+  float2 p = fma2(f, make_float2(0.05517098f, 0.05517098f), make_float2(0.24260971f, 0.24260971f));
+  p = fma2(p, f, make_float2(0.69326097f, 0.69326097f));
+  p = fma2(p, f, make_float2(0.9999282f, 0.9999282f));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
 }
 
 // vectorised fp32 atomic add (no return value)

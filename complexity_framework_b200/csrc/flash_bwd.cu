@@ -8,8 +8,8 @@
 // Hq/Hkv query heads of its group inside one CTA, so dK/dV need no atomics.
 //
 // Three launches:
-//   bwd_prep_k   Delta = rowsum(dO * O) and LSE in the log2 domain into
-//                [B*Hq, S_pad] buffers (padding rows: Delta 0, LSE +inf), and
+//   bwd_prep_k   Delta = rowsum(dO * O) and -LSE in the log2 domain into
+//                [B*Hq, S_pad] buffers (padding rows: Delta 0, -LSE -inf), and
 //                zero the fp32 dQ accumulator [B*Hq, S_pad, D].
 //   flash_bwd_kernel  one CTA per (128-key tile, b, kv head).  K and V stay
 //                resident in shared memory; the CTA walks every 64-query half
@@ -26,14 +26,16 @@
 //                bulk reduce-add from a 128B-swizzled staging tile.
 //   bwd_post_k   dQ(bf16) = scale * accumulator, in the layout of Q.
 //
-// Warp roles of the main kernel (512 threads):
-//   warp 0       TMA producer: K, V once; Q/dO/LSE/Delta half tiles through a ring
-//   warp 1       MMA issuer (one thread)
-//   warps 4-7    softmax-gradient warpgroup 0 (even half tiles), then the dV epilogue
-//   warps 8-11   softmax-gradient warpgroup 1 (odd half tiles), then the dK epilogue
-//   warps 12-15  dQ warpgroup: TMEM -> swizzled staging -> TMA reduce-add
+// Warp roles of the main kernel (704 threads):
+//   warps 0-3    dQ warpgroup: TMEM -> swizzled staging -> TMA reduce-add
+//   warps 4-19   four softmax-gradient warpgroups: 4-11 take the even half tiles,
+//                12-19 the odd ones; within a pair each warpgroup owns 32 of the
+//                64 query columns (one key row per thread), with packed f32x2
+//                math; afterwards they write dV (4-11) and dK (12-19)
+//   warp 20      TMA producer: K, V once; Q/dO/LSE/Delta half tiles through a ring
+//   warp 21      MMA issuer (one thread)
 // For head_dim 64, S^T/dP^T are double-buffered in TMEM, so the tensor core
-// computes the next half's S^T and dP^T while a warpgroup turns the previous
+// computes the next half's S^T and dP^T while two warpgroups turn the previous
 // one into P^T and dS^T.
 //
 // Reference counterpart: the autograd backward of F.scaled_dot_product_attention
@@ -47,6 +49,12 @@ namespace {
 
 constexpr int kKT = 128;  // keys per CTA (TMEM lanes)
 constexpr int kQH = 64;   // queries per half tile (MMA N)
+// warp roles (TMEM lane quarter = warp % 4): warps 0-3 dQ, then NSW softmax
+// warpgroups, then the producer and MMA warps
+constexpr int kSoftWarp0 = 4;
+#ifndef CFB_FLASH_NSW
+#define CFB_FLASH_NSW 2
+#endif
 
 __device__ __forceinline__ float ex2f(float x) {
   float y;
@@ -79,12 +87,19 @@ struct BwdCfg {
                               STG_BYTES + 1024 /*align*/ + 512 /*barriers*/;
   static_assert((QST * LD_BYTES) % 1024 == 0, "LSE/Delta ring keeps the next tile aligned");
   static_assert(SMEM <= 232448, "flash backward shared memory over the 227 KB limit");
-  // TMEM columns
-  static constexpr uint32_t T_DV = NBUF * 128;
+  // TMEM columns: NBUF x {S^T, dP^T} fp32 (64 + 64), one bf16 {P^T, dS^T} region
+  // (32 + 32, read by the dV/dK MMAs), dV, dK, dQ
+  static constexpr uint32_t T_PD = NBUF * 128;
+  static constexpr uint32_t T_DV = T_PD + 64;
   static constexpr uint32_t T_DK = T_DV + D;
   static constexpr uint32_t T_DQ = T_DK + D;
   static_assert(T_DQ + 64 <= 512, "TMEM budget");
-  static constexpr int THREADS = 512;
+  // softmax-gradient warpgroups: NSW / 2 per half tile, each owning CW query columns
+  static constexpr int NSW = CFB_FLASH_NSW;
+  static constexpr int CW = 2 * kQH / NSW;
+  static constexpr int PRODUCER_WARP = kSoftWarp0 + 4 * NSW;
+  static constexpr int MMA_WARP = PRODUCER_WARP + 1;
+  static constexpr int THREADS = 32 * (MMA_WARP + 1);
 };
 
 struct BwdBars {
@@ -92,6 +107,8 @@ struct BwdBars {
   uint64_t q_full[4];
   uint64_t q_empty[4];
   uint64_t s_full[2];
+  uint64_t s_consumed[2];
+  uint64_t pd_free[2];
   uint64_t ds_ready[2];
   uint64_t ds_empty[4];
   uint64_t dq_full;
@@ -114,6 +131,16 @@ struct BwdParams {
   int64_t k_sb, k_sh, k_ss;
 };
 
+// Pipeline timeline for profiling builds only (CFB_FLASH_TRACE defined): SM clock
+// stamps of each hand-off in CTA 0, event kind e and index i at g_trace[e][i].
+#ifdef CFB_FLASH_TRACE
+__device__ long long g_trace[16][512];
+#define FLASH_TRACE(e, i) \
+  do { if (blockIdx.x == 0 && (i) < 512) g_trace[e][i] = clock64(); } while (0)
+#else
+#define FLASH_TRACE(e, i) do { } while (0)
+#endif
+
 // bounded wait whose verdict is the same for every lane of the warp
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity,
                                                volatile int* abort_flag, int* err, int code,
@@ -129,7 +156,7 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(512, 1)
+__global__ void __launch_bounds__(BwdCfg<D>::THREADS, 1)
     flash_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                      const __grid_constant__ CUtensorMap tmDQ, const BwdParams p, int* err) {
@@ -145,7 +172,7 @@ __global__ void __launch_bounds__(512, 1)
   uint8_t* sV = sK + Cfg::KV_BYTES;
   uint8_t* sQ = sV + Cfg::KV_BYTES;                          // QST half tiles
   uint8_t* sdO = sQ + QST * Cfg::QH_BYTES;                   // QST half tiles
-  uint8_t* sLD = sdO + QST * Cfg::QH_BYTES;                  // QST x {lse2[64], delta[64]}
+  uint8_t* sLD = sdO + QST * Cfg::QH_BYTES;                  // QST x {-lse2[64], delta[64]}
   uint8_t* sDS = sLD + QST * Cfg::LD_BYTES;
   uint8_t* sStg = sDS + Cfg::NDS * Cfg::DS_BYTES;
   BwdBars* bars = reinterpret_cast<BwdBars*>(sStg + Cfg::STG_BYTES);
@@ -180,7 +207,9 @@ __global__ void __launch_bounds__(512, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->ds_ready[i], 4);
+      mbar_init(&bars->s_consumed[i], 4 * (Cfg::NSW / 2));  // the warps of one half
+      mbar_init(&bars->pd_free[i], 1);
+      mbar_init(&bars->ds_ready[i], 4 * (Cfg::NSW / 2));
     }
     mbar_init(&bars->dq_full, 1);
     mbar_init(&bars->dq_empty, 4);
@@ -189,13 +218,13 @@ __global__ void __launch_bounds__(512, 1)
     bars->abort = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(&bars->tmem, 512);
+  if (warp == Cfg::MMA_WARP) tmem_alloc(&bars->tmem, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem;
 
-  if (warp == 0) {
+  if (warp == Cfg::PRODUCER_WARP) {
     // ------------------------------------------------------------ producer
     if (elect_one()) {
       mbar_arrive_expect_tx(&bars->kv_full, 2 * Cfg::KV_BYTES);
@@ -213,6 +242,7 @@ __global__ void __launch_bounds__(512, 1)
         const int h = g * G + u / per_head;
         const int q0 = (t0 + u % per_head) * kQH;
         const int64_t row = (static_cast<int64_t>(b) * p.Hq + h) * p.S_pad + q0;
+        FLASH_TRACE(0, u);
         mbar_arrive_expect_tx(&bars->q_full[st], Cfg::TX_BYTES);
 #pragma unroll
         for (int c = 0; c < CH; ++c) {
@@ -228,21 +258,31 @@ __global__ void __launch_bounds__(512, 1)
       for (int u = issued - QST < 0 ? 0 : issued - QST; u < issued; ++u)
         drain_wait(&bars->q_full[u % QST], (u / QST) & 1);
     }
-  } else if (warp == 1) {
+  } else if (warp == Cfg::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
       constexpr uint32_t IDESC_S = idesc_bf16(kKT, kQH, false, false);   // S^T, dP^T
       constexpr uint32_t IDESC_G = idesc_bf16(kKT, D, false, true);      // dV, dK
       constexpr uint32_t IDESC_Q = idesc_bf16(128, PAIR ? D : kQH, true, true);  // dQ / dQ^T
-      constexpr int L = NBUF - 1;
       const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
       bool ok = mbar_wait(&bars->kv_full, 0, abort_flag, err, kErrTimeoutFull, 61);
-      for (int v = 0; v < n_iter + L && ok; ++v) {
+      // iteration v issues S^T/dP^T of half v (into buffer v % NBUF, once the
+      // softmax of half v - NBUF has read that buffer), then dV/dK (and dQ) of
+      // half v - NBUF once its P^T/dS^T are packed
+      for (int v = 0; v < n_iter + NBUF && ok; ++v) {
         if (v < n_iter) {
           const int st = v % QST;
           if (!mbar_wait(&bars->q_full[st], (v / QST) & 1, abort_flag, err, kErrTimeoutFull, 62)) {
             ok = false;
             break;
+          }
+          if (v >= NBUF) {
+            const int vp = v - NBUF;
+            if (!mbar_wait(&bars->s_consumed[vp & 1], (vp >> 1) & 1, abort_flag, err,
+                           kErrTimeoutTmem, 70)) {
+              ok = false;
+              break;
+            }
           }
           tc_fence_after();
           const uint32_t tb = tmem + (v % NBUF) * 128;
@@ -262,8 +302,9 @@ __global__ void __launch_bounds__(512, 1)
                       sw128_desc(do_base + kb, 16, 1024), IDESC_S, kk != 0 ? 1u : 0u);
           }
           umma_commit(&bars->s_full[v & 1]);
+          FLASH_TRACE(1, v);
         }
-        const int w = v - L;
+        const int w = v - NBUF;
         if (w < 0) continue;
         if (!mbar_wait(&bars->ds_ready[w & 1], (w >> 1) & 1, abort_flag, err, kErrTimeoutTmem,
                        63)) {
@@ -271,21 +312,23 @@ __global__ void __launch_bounds__(512, 1)
           break;
         }
         tc_fence_after();
+        FLASH_TRACE(2, w);
         const int st = w % QST;
-        const uint32_t tb = tmem + (w % NBUF) * 128;
         const uint32_t q_base = smem_u32(stQ(st)), do_base = smem_u32(stdO(st));
-        // dV += P^T dO, dK += dS^T Q: A from TMEM (bf16 over S^T / dP^T), B MN-major
+        // dV += P^T dO, dK += dS^T Q: A = the bf16 P^T / dS^T region of TMEM, B MN-major
 #pragma unroll
         for (int kk = 0; kk < kQH / 16; ++kk)
-          umma_bf16_ts(tmem + Cfg::T_DV, tb + kk * 8,
+          umma_bf16_ts(tmem + Cfg::T_DV, tmem + Cfg::T_PD + kk * 8,
                        sw128_desc(do_base + kk * 2048, kQH * 128, 1024), IDESC_G,
                        (w > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < kQH / 16; ++kk)
-          umma_bf16_ts(tmem + Cfg::T_DK, tb + 64 + kk * 8,
+          umma_bf16_ts(tmem + Cfg::T_DK, tmem + Cfg::T_PD + 32 + kk * 8,
                        sw128_desc(q_base + kk * 2048, kQH * 128, 1024), IDESC_G,
                        (w > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&bars->q_empty[st]);
+        // the P^T/dS^T region is free for the next half (packed by the other warpgroups)
+        umma_commit(&bars->pd_free[(w + 1) & 1]);
         if (PAIR && !(w & 1)) continue;
         const int n = PAIR ? (w >> 1) : w;       // dQ tile index
         if (!mbar_wait(&bars->dq_empty, (n & 1) ^ 1, abort_flag, err, kErrTimeoutTmem, 64)) {
@@ -293,6 +336,7 @@ __global__ void __launch_bounds__(512, 1)
           break;
         }
         tc_fence_after();
+        FLASH_TRACE(3, n);
         const int slot = n & 1;                  // ds_empty barrier of this dQ tile
         const uint32_t ds_base = smem_u32(sDS + ds_slot(PAIR ? w - 1 : w) * Cfg::DS_BYTES);
 #pragma unroll
@@ -317,13 +361,18 @@ __global__ void __launch_bounds__(512, 1)
       umma_commit(&bars->mma_done);
       drain_wait(&bars->mma_done, 0);
     }
-  } else if (warp >= 4 && warp < 12) {
-    // --------------------------------------- P^T / dS^T (one key row per thread)
-    const int wg = (warp - 4) >> 2;
+  } else if (warp >= kSoftWarp0 && warp < Cfg::PRODUCER_WARP) {
+    // ------------------- P^T / dS^T: one key row per thread, CW query columns
+    constexpr int NPH = Cfg::NSW / 2;            // warpgroups per half tile
+    constexpr int CW = Cfg::CW;
+    const int sw = (warp - kSoftWarp0) >> 2;     // softmax warpgroup
+    const int wg = sw / NPH;                     // halves w with w % 2 == wg
+    const int cp = (sw % NPH) * CW;              // first query column of this warpgroup
     const int r = (warp & 3) * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int kr = k0 + r;
     const bool key_ok = kr < p.S;
+    const float2 sl2 = make_float2(p.scale_log2, p.scale_log2);
     bool ok = true;
     for (int w = wg; w < n_iter; w += 2) {
       const int it = w >> 1;
@@ -342,60 +391,111 @@ __global__ void __launch_bounds__(512, 1)
         break;
       }
       tc_fence_after();
+      if (sw % NPH == 0 && threadIdx.x % 128 == 0) FLASH_TRACE(4, w);
       const int q0 = (t0 + w % per_head) * kQH;
-      const uint32_t tb = tmem + lane_off + (w % NBUF) * 128;
-      const float* lse2 = stLse(st);
-      const float* dl = stDelta(st);
-      const bool full = key_ok && (!p.causal || k0 + kKT - 1 <= q0) && (k0 + kKT <= p.S);
+      const uint32_t tb = tmem + lane_off + (w % NBUF) * 128 + cp;
+      const float4* nl4 = reinterpret_cast<const float4*>(stLse(st) + cp);
+      const float4* dl4 = reinterpret_cast<const float4*>(stDelta(st) + cp);
+      const bool full = key_ok && (!p.causal || k0 + kKT - 1 <= q0 + cp) && (k0 + kKT <= p.S);
+      uint32_t pk[CW / 2], dk[CW / 2];           // packed bf16 P^T and dS^T of this row
 #pragma unroll
-      for (int c0 = 0; c0 < kQH; c0 += 32) {
-        float s[32], dp[32];
-        tmem_ld32(tb + c0, s);
-        tmem_ld32(tb + 64 + c0, dp);
+      for (int j = 0; j < CW / 16; ++j) {
+        float s[16], dp[16];
+        tmem_ld16(tb + 16 * j, s);
+        tmem_ld16(tb + 64 + 16 * j, dp);
         tmem_wait_ld();
-        uint32_t pk[16], dk[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float pr[2], dsv[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int c = c0 + i + e;
-            float pv = ex2f(fmaf(s[i + e], p.scale_log2, -lse2[c]));
-            if (!full && (!key_ok || (p.causal && kr > q0 + c))) pv = 0.f;
-            pr[e] = pv;
-            dsv[e] = pv * (dp[i + e] - dl[c]);
-          }
-          pk[i / 2] = pack_bf16x2(pr[0], pr[1]);
-          dk[i / 2] = pack_bf16x2(dsv[0], dsv[1]);
+        if (j == CW / 16 - 1) {
+          // S^T/dP^T are in registers: the tensor core may refill this buffer
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->s_consumed[wg]);
         }
-        tmem_st16(tb + c0 / 2, pk);
-        tmem_st16(tb + 64 + c0 / 2, dk);
+        if (sw == 0 && threadIdx.x % 128 == 0 && j < 2) FLASH_TRACE(8 + 3 * j, w);
+        uint32_t* pkj = pk + 8 * j;
+        uint32_t* dkj = dk + 8 * j;
+        if (full) {
+          // interior half: no masking; 16 elements as 8 packed pairs
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          *reinterpret_cast<uint4*>(ds_smem + sw128_off(r, c0 + u * 8)) =
-              make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
+          for (int i4 = 0; i4 < 4; ++i4) {
+            const float4 nl = nl4[4 * j + i4];   // -log2 LSE of 4 query columns
+            const float4 dl = dl4[4 * j + i4];   // Delta of the same columns
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+              const int i = 4 * i4 + 2 * h2;
+              const float2 x = fma2(make_float2(s[i], s[i + 1]), sl2,
+                                    h2 ? make_float2(nl.z, nl.w) : make_float2(nl.x, nl.y));
+              const float2 pr = make_float2(ex2f(x.x), ex2f(x.y));
+              const float2 dsv = mul2(pr, sub2(make_float2(dp[i], dp[i + 1]),
+                                               h2 ? make_float2(dl.z, dl.w)
+                                                  : make_float2(dl.x, dl.y)));
+              pkj[i / 2] = pack_bf16x2(pr.x, pr.y);
+              dkj[i / 2] = pack_bf16x2(dsv.x, dsv.y);
+            }
+          }
+        } else {
+          // diagonal / ragged half: causal and key-range masks
+          const float* nl = stLse(st) + cp + 16 * j;
+          const float* dl = stDelta(st) + cp + 16 * j;
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            float pr[2], dsv[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int c = cp + 16 * j + i + e;  // query column within the half
+              float pv = ex2f(fmaf(s[i + e], p.scale_log2, nl[i + e]));
+              if (!key_ok || (p.causal && kr > q0 + c)) pv = 0.f;
+              pr[e] = pv;
+              dsv[e] = pv * (dp[i + e] - dl[i + e]);
+            }
+            pkj[i / 2] = pack_bf16x2(pr[0], pr[1]);
+            dkj[i / 2] = pack_bf16x2(dsv[0], dsv[1]);
+          }
+        }
+        if (sw == 0 && threadIdx.x % 128 == 0 && j < 2) FLASH_TRACE(9 + 3 * j, w);
+        // dS^T for the dQ MMA (its own shared-memory slot)
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+          *reinterpret_cast<uint4*>(ds_smem + sw128_off(r, cp + 16 * j + u * 8)) =
+              make_uint4(dkj[4 * u], dkj[4 * u + 1], dkj[4 * u + 2], dkj[4 * u + 3]);
+      }
+      // the single P^T/dS^T region: wait until the dV/dK MMAs of half w - 1 have read it
+      if (w >= 1 && !mbar_wait_warp(&bars->pd_free[wg], (((w + 1) >> 1) - 1) & 1, abort_flag,
+                                    err, kErrTimeoutTmem, 71)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t tpd = tmem + lane_off + Cfg::T_PD + cp / 2;
+#pragma unroll
+      for (int j = 0; j < CW / 16; ++j) {
+        tmem_st8(tpd + 8 * j, pk + 8 * j);
+        tmem_st8(tpd + 32 + 8 * j, dk + 8 * j);
       }
       tmem_wait_st();
+      if (sw % NPH == 0 && threadIdx.x % 128 == 0) FLASH_TRACE(14, w);
       tc_fence_before();
       fence_proxy_async_shared();
       __syncwarp();
+      if (sw % NPH == 0 && threadIdx.x % 128 == 0) FLASH_TRACE(5, w);
       if (lane == 0) mbar_arrive(&bars->ds_ready[wg]);
     }
-    // ------------------------------------------ dV (warpgroup 0) / dK (warpgroup 1)
+    // ----------- dV (warpgroups 0, 1) / dK (2, 3), half of the head dim each
     if (ok && mbar_wait_warp(&bars->dkv_full, 0, abort_flag, err, kErrTimeoutTmem, 68)) {
       tc_fence_after();
-      const uint32_t col = wg == 0 ? Cfg::T_DV : Cfg::T_DK;
-      const float f = wg == 0 ? 1.f : p.scale;
-      __nv_bfloat16* dst = (wg == 0 ? p.dv : p.dk) + b * p.k_sb + g * p.k_sh +
-                           static_cast<int64_t>(kr) * p.k_ss;
+      const bool is_dv = sw < NPH;
+      const int c0 = (sw % NPH) * (D / NPH);
+      const uint32_t col = (is_dv ? Cfg::T_DV : Cfg::T_DK) + c0;
+      const float f = is_dv ? 1.f : p.scale;
+      __nv_bfloat16* dst = (is_dv ? p.dv : p.dk) + b * p.k_sb + g * p.k_sh +
+                           static_cast<int64_t>(kr) * p.k_ss + c0;
 #pragma unroll
-      for (int c = 0; c < D; c += 32) {
-        float v[32];
-        tmem_ld32(tmem + lane_off + col + c, v);
+      for (int c = 0; c < D / NPH; c += 16) {
+        float v[16];
+        tmem_ld16(tmem + lane_off + col + c, v);
         tmem_wait_ld();
         if (key_ok) {
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
+          for (int u = 0; u < 2; ++u) {
             uint4 o;
             o.x = pack_bf16x2(v[8 * u] * f, v[8 * u + 1] * f);
             o.y = pack_bf16x2(v[8 * u + 2] * f, v[8 * u + 3] * f);
@@ -406,12 +506,12 @@ __global__ void __launch_bounds__(512, 1)
         }
       }
     }
-  } else if (warp >= 12) {
-    // ---------------------------------------------- dQ: TMEM -> staging -> reduce-add
+  } else {
+    // ----------------------- dQ (warps 0-3): TMEM -> staging -> TMA reduce-add
     const int wq = warp & 3;
     const int lt = wq * 32 + lane;                 // TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-    const bool leader = threadIdx.x == 384;
+    const bool leader = threadIdx.x == 0;
     volatile int* go = &bars->dq_go;               // leader's verdict for this tile
     const int ndq = PAIR ? n_iter / 2 : n_iter;
     for (int n = 0; n < ndq; ++n) {
@@ -424,25 +524,27 @@ __global__ void __launch_bounds__(512, 1)
       named_bar_sync(1, 128);
       if (!*go) break;
       tc_fence_after();
+      if (leader) FLASH_TRACE(6, n);
       const int u = PAIR ? 2 * n : n;
       const int h = g * G + u / per_head;
       const int q0 = (t0 + u % per_head) * kQH;
       if constexpr (PAIR) {
         // lane = query row (128 rows), 64 d values: two boxes [128 rows][32 fp32]
-        float v[64];
-        tmem_ld32(tmem + lane_off + Cfg::T_DQ, v);
-        tmem_ld32(tmem + lane_off + Cfg::T_DQ + 32, v + 32);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->dq_empty);
 #pragma unroll
-        for (int bx = 0; bx < 2; ++bx)
+        for (int bx = 0; bx < 2; ++bx) {
+          float v[32];
+          tmem_ld32(tmem + lane_off + Cfg::T_DQ + bx * 32, v);
+          tmem_wait_ld();
+          if (bx == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->dq_empty);
+          }
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             *reinterpret_cast<float4*>(sStg + bx * 16384 + lt * 128 + ((j ^ (lt & 7)) * 16)) =
-                make_float4(v[bx * 32 + 4 * j], v[bx * 32 + 4 * j + 1], v[bx * 32 + 4 * j + 2],
-                            v[bx * 32 + 4 * j + 3]);
+                make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
       } else {
         // lane = d (128), 64 query values in two passes of 32: four boxes
         // [64 rows][32 fp32], box = lt / 32
@@ -475,13 +577,14 @@ __global__ void __launch_bounds__(512, 1)
         for (int bx = 0; bx < NBX; ++bx)
           tma_reduce_add_2d(&tmDQ, sStg + bx * (PAIR ? 16384 : 8192), bx * 32, row);
         bulk_commit_group();
+        FLASH_TRACE(7, n);
       }
     }
     if (leader) bulk_wait_group_all();
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == Cfg::MMA_WARP) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -522,7 +625,7 @@ __global__ void bwd_prep_k(Bhsd o, Bhsd dout, const float* __restrict__ lse, flo
   z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
   if (part == 0) {
     delta[row] = acc;
-    lse2[row] = s < S ? lse[static_cast<int64_t>(bh) * S + s] * 1.4426950408889634f : INFINITY;
+    lse2[row] = s < S ? -lse[static_cast<int64_t>(bh) * S + s] * 1.4426950408889634f : -INFINITY;
   }
 }
 
