@@ -6,20 +6,27 @@
 // q: [B, Hq, S, D], k/v: [B, Hkv, S, D] (bf16, any strides along b, h, s with d
 // contiguous: head-major, or the token-major q written by the QK-norm/RoPE
 // kernel, read in place through 4-D TMA maps), GQA group g(h) = h / (Hq/Hkv)
-// -- K/V are never replicated.  O is written token-major
-// [B, S, Hq*D] so the o_proj GEMM reads it directly.  D in {64, 128}.
+// -- K/V are never replicated.  O is written token-major [B, S, Hq*D] so the
+// o_proj GEMM reads it directly.  D in {64, 128}.
 //
-// One CTA per (NQ x 128 query rows, b*Hq); NQ = 2 for head_dim 64, 1 for 128.
-// Warp roles:
-//   warp 0      TMA producer: the NQ Q tiles once, then K_j/V_j through a ring
-//   warp 1      MMA issuer (one thread): S_x(j) = Q_x K_j^T for every Q tile x,
-//               then PV_x(j-1) = P_x(j-1) V_{j-1}, all accumulating in TMEM
-//   warps 4..   one softmax warpgroup per Q tile, one query row per thread:
-//               read S_x(j) from TMEM (two passes: max, then exp2), fold the
-//               previous tile's PV into fp32 output registers with the running
-//               rescale, write P_x(j) (bf16) to 128B-swizzled shared memory.
-// The tensor cores compute S for one Q tile while the other tile's warpgroup
-// is in softmax, and K/V tiles are shared by the NQ Q tiles.
+// One CTA per (2 x 128 query rows, b*Hq): the two query tiles share every K/V
+// tile.  TMEM holds, per query tile x, S_x (128 fp32 columns) and the output
+// accumulator O_x (D columns); the bf16 probabilities P_x are packed in place
+// over S_x and feed the P V MMA as its TMEM A operand, so P never goes through
+// shared memory and O never through registers until the end.
+// Warp roles (320 threads):
+//   warps 0-3 / 4-7  softmax of query tile 0 / 1, one row per thread: the row
+//                    of S is read from TMEM once (128 registers), its max taken,
+//                    exponentials computed (a fixed share of them by a cubic on
+//                    the FMA pipe, the rest on MUFU), P packed back into TMEM
+//   warp 8           TMA producer: Q once, then K_j/V_j through a ring
+//   warp 9           MMA issuer: per KV tile j and query tile x,
+//                    O_x += P_x(j-1) V_{j-1}, then S_x(j) = Q_x K_j^T
+// The running max is applied lazily: O and the row sum are rescaled only when
+// the max grows by more than 2^8 (log2 units), which keeps P <= 256 (exact in
+// bf16's exponent range) and makes rescaling rare after the first KV tiles.
+// Rescaling needs no extra wait: S_x(j) is issued after O_x += P_x(j-1) V, so
+// its completion implies that the accumulation reading O_x is done.
 // Reference counterpart: F.scaled_dot_product_attention after K/V
 // repeat_interleave in complexity/core/attention/gqa.py:153-154,229-265.
 #include "common.cuh"
@@ -30,6 +37,12 @@ namespace {
 
 constexpr int kQT = 128;   // query rows per Q tile
 constexpr int kKT = 128;   // keys per KV tile
+constexpr int kNQ = 2;     // Q tiles per CTA
+constexpr float kRescaleLog2 = 8.f;  // lazy-rescale threshold (log2 units)
+
+#ifndef CFB_FLASH_FWD_POLY
+#define CFB_FLASH_FWD_POLY 2  // of every 8 element pairs, this many use the cubic
+#endif
 
 // 2^x on the SFU (hardware approximation, relative error ~2^-22)
 __device__ __forceinline__ float ex2(float x) {
@@ -40,39 +53,48 @@ __device__ __forceinline__ float ex2(float x) {
 
 template <int D>
 struct FlashCfg {
-  // head_dim 64: two Q tiles per CTA share each K/V tile (two softmax warpgroups);
-  // head_dim 128: one Q tile (shared memory holds fewer, larger tiles)
-  static constexpr int NQ = D == 64 ? 2 : 1;
-  static constexpr int STAGES = D == 64 ? 3 : 2;
+  static constexpr int STAGES = D == 64 ? 4 : 2;
   static constexpr int CHUNKS = D / 64;                 // 128-byte swizzle atoms along D
   static constexpr int Q_BYTES = kQT * D * 2;
   static constexpr int K_BYTES = kKT * D * 2;
   static constexpr int V_BYTES = kKT * D * 2;
-  static constexpr int P_BYTES = kQT * kKT * 2;         // two 64-key chunks
-  static constexpr int SMEM =
-      NQ * Q_BYTES + STAGES * (K_BYTES + V_BYTES) + NQ * P_BYTES + 1024 + 512;
-  static constexpr uint32_t TMEM_COLS = 512;            // S_x (128 each) then PV_x (D each)
-  static constexpr int THREADS = 128 + 128 * NQ;
+  static constexpr int SMEM = kNQ * Q_BYTES + STAGES * (K_BYTES + V_BYTES) + 1024 + 512;
+  static constexpr uint32_t T_O = kNQ * 128;            // O_x at T_O + x * D
+  static_assert(T_O + kNQ * D <= 512, "TMEM budget");
+  static constexpr int PRODUCER_WARP = 8;
+  static constexpr int MMA_WARP = 9;
+  static constexpr int THREADS = 320;
   static_assert(SMEM <= 232448, "flash forward shared memory over the 227 KB limit");
 };
 
 struct Bars {
   uint64_t q_full;
-  uint64_t kv_full[3];
-  uint64_t kv_empty[3];
-  uint64_t s_full[2];
-  uint64_t s_empty[2];
-  uint64_t p_full[2];
-  uint64_t pv_full[2];
-  uint64_t pv_empty[2];
+  uint64_t kv_full[4];
+  uint64_t kv_empty[4];
+  uint64_t s_full[kNQ];
+  uint64_t p_full[kNQ];
+  uint64_t o_full[kNQ];
+  uint64_t mma_done;
   uint32_t tmem;
   int abort;
 };
 
-// byte offset of element (row, col) of a [rows x 64] bf16 block in 128B-swizzle layout
-__device__ __forceinline__ uint32_t sw128_off(int row, int col) {
-  const int unit = (col >> 3) ^ (row & 7);
-  return static_cast<uint32_t>(row * 128 + unit * 16 + (col & 7) * 2);
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  const uint64_t start = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer_ns() - start > kWaitBoundNs) return;
+}
+
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity,
+                                               volatile int* abort_flag, int* err, int code,
+                                               int site) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, err, code, site));
+}
+
+// 32 lanes x 32 columns store
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  tmem_st16(taddr, r);
+  tmem_st16(taddr + 16, r + 16);
 }
 
 template <int D>
@@ -82,17 +104,15 @@ __global__ void __launch_bounds__(FlashCfg<D>::THREADS, 1)
                      float* __restrict__ lse, int B, int Hq, int Hkv, int S, float scale_log2,
                      int causal, int* err) {
   using Cfg = FlashCfg<D>;
-  constexpr int NQ = Cfg::NQ;
   constexpr int STAGES = Cfg::STAGES;
-  constexpr int CTA_Q = NQ * kQT;
+  constexpr int CTA_Q = kNQ * kQT;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint8_t* sQ = smem;                                   // NQ tiles
-  uint8_t* sK = sQ + NQ * Cfg::Q_BYTES;
+  uint8_t* sQ = smem;                                   // kNQ tiles
+  uint8_t* sK = sQ + kNQ * Cfg::Q_BYTES;
   uint8_t* sV = sK + STAGES * Cfg::K_BYTES;
-  uint8_t* sP = sV + STAGES * Cfg::V_BYTES;             // NQ tiles
-  Bars* bars = reinterpret_cast<Bars*>(sP + NQ * Cfg::P_BYTES);
+  Bars* bars = reinterpret_cast<Bars*>(sV + STAGES * Cfg::V_BYTES);
   volatile int* abort_flag = &bars->abort;
 
   const int warp = threadIdx.x / 32;
@@ -106,7 +126,11 @@ __global__ void __launch_bounds__(FlashCfg<D>::THREADS, 1)
   const int g = h / (Hq / Hkv);
   const int q0 = qt * CTA_Q;
   const int nkv_all = (S + kKT - 1) / kKT;
-  const int nkv = causal ? min(nkv_all, (min(q0 + CTA_Q, S) - 1) / kKT + 1) : nkv_all;
+  // KV tiles each query tile needs (causal: up to its last row)
+  auto nkv_of = [&](int x) {
+    return causal ? min(nkv_all, (min(q0 + (x + 1) * kQT, S) - 1) / kKT + 1) : nkv_all;
+  };
+  const int nkv = max(nkv_of(0), nkv_of(1));
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
@@ -114,36 +138,37 @@ __global__ void __launch_bounds__(FlashCfg<D>::THREADS, 1)
       mbar_init(&bars->kv_full[s], 1);
       mbar_init(&bars->kv_empty[s], 1);
     }
-    for (int i = 0; i < NQ; ++i) {
-      mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->s_empty[i], 4);
-      mbar_init(&bars->p_full[i], 4);
-      mbar_init(&bars->pv_full[i], 1);
-      mbar_init(&bars->pv_empty[i], 4);
+    for (int x = 0; x < kNQ; ++x) {
+      mbar_init(&bars->s_full[x], 1);
+      mbar_init(&bars->p_full[x], 4);
+      mbar_init(&bars->o_full[x], 1);
     }
+    mbar_init(&bars->mma_done, 1);
     bars->abort = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(&bars->tmem, Cfg::TMEM_COLS);
+  if (warp == Cfg::MMA_WARP) tmem_alloc(&bars->tmem, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem;
 
-  if (warp == 0) {
+  if (warp == Cfg::PRODUCER_WARP) {
     // ------------------------------------------------------------ producer
     if (elect_one()) {
-      mbar_arrive_expect_tx(&bars->q_full, NQ * Cfg::Q_BYTES);
+      mbar_arrive_expect_tx(&bars->q_full, kNQ * Cfg::Q_BYTES);
 #pragma unroll
-      for (int x = 0; x < NQ; ++x)
+      for (int x = 0; x < kNQ; ++x)
 #pragma unroll
         for (int c = 0; c < Cfg::CHUNKS; ++c)
           tma_load_4d(sQ + x * Cfg::Q_BYTES + c * kQT * 128, &tmQ, &bars->q_full, c * 64,
                       q0 + x * kQT, h, b);
+      int issued = 0;
       for (int j = 0; j < nkv; ++j) {
         const int st = j % STAGES;
-        const uint32_t ph = (j / STAGES) & 1;
-        if (!mbar_wait(&bars->kv_empty[st], ph ^ 1, abort_flag, err, kErrTimeoutEmpty, 30)) break;
+        if (!mbar_wait(&bars->kv_empty[st], ((j / STAGES) & 1) ^ 1, abort_flag, err,
+                       kErrTimeoutEmpty, 30))
+          break;
         mbar_arrive_expect_tx(&bars->kv_full[st], Cfg::K_BYTES + Cfg::V_BYTES);
 #pragma unroll
         for (int c = 0; c < Cfg::CHUNKS; ++c) {
@@ -152,31 +177,53 @@ __global__ void __launch_bounds__(FlashCfg<D>::THREADS, 1)
           tma_load_4d(sV + st * Cfg::V_BYTES + c * kKT * 128, &tmV, &bars->kv_full[st], c * 64,
                       j * kKT, g, b);
         }
+        ++issued;
       }
+      drain_wait(&bars->q_full, 0);
+      for (int j = issued - STAGES < 0 ? 0 : issued - STAGES; j < issued; ++j)
+        drain_wait(&bars->kv_full[j % STAGES], (j / STAGES) & 1);
     }
-  } else if (warp == 1) {
+  } else if (warp == Cfg::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
       constexpr uint32_t IDESC_S = idesc_bf16(kQT, kKT, false, false);
       constexpr uint32_t IDESC_PV = idesc_bf16(kQT, D, false, true);
+      const int nkv_x[kNQ] = {nkv_of(0), nkv_of(1)};
       bool ok = mbar_wait(&bars->q_full, 0, abort_flag, err, kErrTimeoutFull, 31);
+      // O_x += P_x(jp) V_jp, A = the bf16 P_x packed over S_x in TMEM
+      auto issue_pv = [&](int x, int jp) -> bool {
+        if (!mbar_wait(&bars->p_full[x], jp & 1, abort_flag, err, kErrTimeoutFull, 32))
+          return false;
+        tc_fence_after();
+        const uint32_t v_base = smem_u32(sV + (jp % STAGES) * Cfg::V_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < kKT / 16; ++kk)
+          umma_bf16_ts(tmem + Cfg::T_O + x * D, tmem + x * 128 + kk * 8,
+                       sw128_desc(v_base + kk * 2048, kKT * 128, 1024), IDESC_PV,
+                       (jp > 0 || kk > 0) ? 1u : 0u);
+        return true;
+      };
       for (int j = 0; j <= nkv && ok; ++j) {
         const int st = j % STAGES;
-        if (j < nkv) {
-          if (!mbar_wait(&bars->kv_full[st], (j / STAGES) & 1, abort_flag, err, kErrTimeoutFull,
-                         34)) {
-            ok = false;
-            break;
-          }
-          const uint32_t k_base = smem_u32(sK + st * Cfg::K_BYTES);
+        if (j < nkv &&
+            !mbar_wait(&bars->kv_full[st], (j / STAGES) & 1, abort_flag, err, kErrTimeoutFull,
+                       34)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k_base = smem_u32(sK + st * Cfg::K_BYTES);
 #pragma unroll
-          for (int x = 0; x < NQ; ++x) {
-            // S_x(j) overwrites S_x(j-1): wait until its softmax has read it
-            if (!mbar_wait(&bars->s_empty[x], (j & 1) ^ 1, abort_flag, err, kErrTimeoutTmem, 35)) {
+        for (int x = 0; x < kNQ; ++x) {
+          if (j > 0 && j - 1 < nkv_x[x]) {
+            if (!issue_pv(x, j - 1)) {
               ok = false;
               break;
             }
-            tc_fence_after();
+            if (j - 1 == nkv_x[x] - 1) umma_commit(&bars->o_full[x]);  // last accumulation
+          }
+          if (j < nkv_x[x]) {
+            // S_x(j) = Q_x K_j^T (after O_x += P_x(j-1) V: S_x holds P_x until then)
             const uint32_t q_base = smem_u32(sQ + x * Cfg::Q_BYTES);
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
@@ -186,181 +233,149 @@ __global__ void __launch_bounds__(FlashCfg<D>::THREADS, 1)
             }
             umma_commit(&bars->s_full[x]);
           }
-          if (!ok) break;
         }
-        if (j > 0) {
-          // PV_x(j-1) = P_x(j-1) V_{j-1}
-          const int jp = j - 1;
-          const int sp = jp % STAGES;
-          const uint32_t v_base = smem_u32(sV + sp * Cfg::V_BYTES);
-#pragma unroll
-          for (int x = 0; x < NQ; ++x) {
-            if (!mbar_wait(&bars->p_full[x], jp & 1, abort_flag, err, kErrTimeoutFull, 32) ||
-                !mbar_wait(&bars->pv_empty[x], (jp & 1) ^ 1, abort_flag, err, kErrTimeoutTmem,
-                           33)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t p_base = smem_u32(sP + x * Cfg::P_BYTES);
-#pragma unroll
-            for (int kk = 0; kk < kKT / 16; ++kk) {
-              const uint64_t ad =
-                  sw128_desc(p_base + (kk >> 2) * (kQT * 128) + (kk & 3) * 32, 16, 1024);
-              const uint64_t bd = sw128_desc(v_base + kk * 2048, kKT * 128, 1024);
-              umma_bf16(tmem + NQ * 128 + x * D, ad, bd, IDESC_PV, kk != 0 ? 1u : 0u);
-            }
-            umma_commit(&bars->pv_full[x]);
-          }
-          if (!ok) break;
-          umma_commit(&bars->kv_empty[sp]);  // K and V of tile j-1 are no longer needed
-        }
+        if (!ok) break;
+        if (j > 0) umma_commit(&bars->kv_empty[(j - 1) % STAGES]);  // K/V of tile j-1 done
       }
+      umma_commit(&bars->mma_done);
+      drain_wait(&bars->mma_done, 0);
     }
-  } else if (warp >= 4) {
-    // ------------------------------------------------ softmax + correction
-    const int x = (warp - 4) >> 2;               // which Q tile this warpgroup owns
+  } else if (warp < 4 * kNQ) {
+    // ------------------------------------------------------------ softmax
+    const int x = warp >> 2;                     // which Q tile this warpgroup owns
     const int wq = warp & 3;
     const int r = wq * 32 + lane;                 // query row within the tile
     const int qpos = q0 + x * kQT + r;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const uint32_t t_s = tmem + x * 128 + lane_off;
-    const uint32_t t_pv = tmem + NQ * 128 + x * D + lane_off;
-    uint8_t* pt = sP + x * Cfg::P_BYTES;
-    float o[D];
-#pragma unroll
-    for (int i = 0; i < D; ++i) o[i] = 0.f;
-    float m = -INFINITY;      // running max (log2 domain)
-    float l = 0.f;            // running sum
-    float alpha_prev = 1.f;   // rescale owed to the output when PV_{j-1} is folded in
+    const uint32_t t_o = tmem + Cfg::T_O + x * D + lane_off;
+    const int nkv_mine = nkv_of(x);
+    float m_used = -INFINITY;  // max the current exponentials are relative to (log2 units)
+    float l = 0.f;             // running sum of exponentials
+    const float2 sl2 = make_float2(scale_log2, scale_log2);
     bool ok = true;
 
-    for (int j = 0; j < nkv && ok; ++j) {
-      if (!mbar_wait(&bars->s_full[x], j & 1, abort_flag, err, kErrTimeoutTmem, 37)) {
+    for (int j = 0; j < nkv_mine && ok; ++j) {
+      if (!mbar_wait_warp(&bars->s_full[x], j & 1, abort_flag, err, kErrTimeoutTmem, 37)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      float s[kKT];
+#pragma unroll
+      for (int c = 0; c < kKT; c += 32) tmem_ld32(t_s + c, s + c);
+      tmem_wait_ld();
       const int k0 = j * kKT;
       int kmax = S - k0;   // keys valid for this row: < S and (causal) <= qpos
       if (causal) kmax = min(kmax, qpos - k0 + 1);
-      const bool full = kmax >= kKT;  // interior tile: no masking needed
-      float mx = -INFINITY;
+      if (kmax < kKT) {
 #pragma unroll
-      for (int c = 0; c < kKT; c += 32) {
-        float v[32];
-        tmem_ld32(t_s + c, v);
-        tmem_wait_ld();
-        if (full) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c + i < kmax) mx = fmaxf(mx, v[i]);
-        }
+        for (int c = 0; c < kKT; ++c)
+          if (c >= kmax) s[c] = -INFINITY;
       }
-      const float m_new = fmaxf(m, mx * scale_log2);
-      const float alpha = (m == -INFINITY) ? 0.f : ex2(m - m_new);
-      const float msub = (m_new == -INFINITY) ? 0.f : m_new;
-      // fold PV_{j-1} before P_j overwrites P_{j-1} in shared memory
-      if (j > 0) {
-        if (!mbar_wait(&bars->pv_full[x], (j - 1) & 1, abort_flag, err, kErrTimeoutTmem, 36)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+      // row max over 8 independent partial maxima (a serial chain would cost
+      // 128 dependent instructions of latency)
+      float mp[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mp[i] = s[i];
+#pragma unroll
+      for (int c = 8; c < kKT; ++c) mp[c & 7] = fmaxf(mp[c & 7], s[c]);
+      const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+      const float m_new = fmaxf(m_used, mx * scale_log2);
+      // lazy rescale: only when the max grew by more than 2^kRescaleLog2
+      const bool grow = m_new > m_used + kRescaleLog2;
+      if (__any_sync(0xffffffffu, grow && m_used != -INFINITY)) {
+        // O_x already holds P V of earlier tiles (their MMAs completed before S_x(j))
+        const float alpha = (grow && m_used != -INFINITY) ? ex2(m_used - m_new) : 1.f;
 #pragma unroll
         for (int c = 0; c < D; c += 32) {
-          float v[32];
-          tmem_ld32(t_pv + c, v);
+          float o[32];
+          uint32_t u[32];
+          tmem_ld32(t_o + c, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[c + i] = o[c + i] * alpha_prev + v[i];
+          for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(o[i] * alpha);
+          tmem_st32(t_o + c, u);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->pv_empty[x]);
+        tmem_wait_st();
       }
-      float rs = 0.f;
+      if (grow) {
+        if (m_used != -INFINITY) l *= ex2(m_used - m_new);
+        m_used = m_new;
+      }
+      // rows with no valid key so far: every exponential is 0
+      const float msub = m_used == -INFINITY ? 0.f : m_used;
+      const float2 nm = make_float2(-msub, -msub);
+      float2 rs2[4] = {};                        // four independent partial row sums
 #pragma unroll
       for (int c = 0; c < kKT; c += 32) {
-        float v[32];
-        tmem_ld32(t_s + c, v);
-        tmem_wait_ld();
         uint32_t pk[16];
-        if (full) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float p0 = ex2(v[i] * scale_log2 - msub);
-            const float p1 = ex2(v[i + 1] * scale_log2 - msub);
-            rs += p0 + p1;
-            pk[i / 2] = pack_bf16x2(p0, p1);
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float p0 = (c + i < kmax) ? ex2(v[i] * scale_log2 - msub) : 0.f;
-            const float p1 = (c + i + 1 < kmax) ? ex2(v[i + 1] * scale_log2 - msub) : 0.f;
-            rs += p0 + p1;
-            pk[i / 2] = pack_bf16x2(p0, p1);
-          }
+        for (int i = 0; i < 32; i += 2) {
+          const float2 xv = fma2(make_float2(s[c + i], s[c + i + 1]), sl2, nm);
+          const float2 pv = ((i >> 1) % 8) < CFB_FLASH_FWD_POLY
+                                ? exp2_poly2(xv)
+                                : make_float2(ex2(xv.x), ex2(xv.y));
+          rs2[(i >> 1) & 3] = add2(rs2[(i >> 1) & 3], pv);
+          pk[i / 2] = pack_bf16x2(pv.x, pv.y);
         }
-        uint8_t* chunk = pt + (c >> 6) * (kQT * 128);
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          *reinterpret_cast<uint4*>(chunk + sw128_off(r, (c & 63) + u * 8)) =
-              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        tmem_st16(t_s + c / 2, pk);              // bf16 P over already-read S columns
       }
-      // S_j has been read: the MMA warp may overwrite this buffer
+      l += ((rs2[0].x + rs2[0].y) + (rs2[1].x + rs2[1].y)) +
+           ((rs2[2].x + rs2[2].y) + (rs2[3].x + rs2[3].y));
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->s_empty[x]);
-      // P_j visible to the tensor core (async proxy) before signalling
-      fence_proxy_async_shared();
-      __syncwarp();
       if (lane == 0) mbar_arrive(&bars->p_full[x]);
-      l = l * alpha + rs;
-      m = m_new;
-      alpha_prev = alpha;
     }
-    if (ok && nkv > 0) {
-      const int jl = nkv - 1;
-      if (mbar_wait(&bars->pv_full[x], jl & 1, abort_flag, err, kErrTimeoutTmem, 38)) {
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < D; c += 32) {
-          float v[32];
-          tmem_ld32(t_pv + c, v);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[c + i] = o[c + i] * alpha_prev + v[i];
-        }
-      }
-    }
-    if (qpos < S) {
+    if (ok && nkv_mine > 0 &&
+        mbar_wait_warp(&bars->o_full[x], 0, abort_flag, err, kErrTimeoutTmem, 38)) {
+      tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* orow = out + (static_cast<int64_t>(b) * S + qpos) * Hq * D + h * D;
 #pragma unroll
-      for (int c = 0; c < D; c += 8) {
-        uint4 w;
-        w.x = pack_bf16x2(o[c] * inv, o[c + 1] * inv);
-        w.y = pack_bf16x2(o[c + 2] * inv, o[c + 3] * inv);
-        w.z = pack_bf16x2(o[c + 4] * inv, o[c + 5] * inv);
-        w.w = pack_bf16x2(o[c + 6] * inv, o[c + 7] * inv);
-        *reinterpret_cast<uint4*>(orow + c) = w;
+      for (int c = 0; c < D; c += 32) {
+        float o[32];
+        tmem_ld32(t_o + c, o);
+        tmem_wait_ld();
+        if (qpos < S) {
+#pragma unroll
+          for (int u = 0; u < 32; u += 8) {
+            uint4 w;
+            w.x = pack_bf16x2(o[u] * inv, o[u + 1] * inv);
+            w.y = pack_bf16x2(o[u + 2] * inv, o[u + 3] * inv);
+            w.z = pack_bf16x2(o[u + 4] * inv, o[u + 5] * inv);
+            w.w = pack_bf16x2(o[u + 6] * inv, o[u + 7] * inv);
+            *reinterpret_cast<uint4*>(orow + c + u) = w;
+          }
+        }
       }
-      if (lse != nullptr)
+      if (qpos < S && lse != nullptr)
         lse[(static_cast<int64_t>(b) * Hq + h) * S + qpos] =
-            l > 0.f ? (m + __log2f(l)) * 0.69314718055994531f : -INFINITY;
+            l > 0.f ? (m_used + __log2f(l)) * 0.69314718055994531f : -INFINITY;
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == Cfg::MMA_WARP) {
     tc_fence_after();
-    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    tmem_dealloc(tmem, 512);
   }
+}
+
+template <int D>
+int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, void* out,
+               float* lse, int B, int Hq, int Hkv, int S, float sl2, bool causal,
+               cudaStream_t stream, int* err) {
+  using Cfg = FlashCfg<D>;
+  auto kern = flash_fwd_kernel<D>;
+  const dim3 grid(((S + kNQ * kQT - 1) / (kNQ * kQT)) * B * Hq);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM))
+    return static_cast<int>(cudaGetLastError());
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM, stream>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(out),
+                                                  lse, B, Hq, Hkv, S, sl2, causal ? 1 : 0, err);
+  return static_cast<int>(cudaGetLastError());
 }
 
 }  // namespace
@@ -376,24 +391,8 @@ int flash_fwd_launch(const Bhsd& q, const Bhsd& k, const Bhsd& v, void* out, flo
   if (!rc) rc = make_bhsd_map(&tv, v, B, Hkv, S, D, kKT);
   if (rc) return rc;
   const float sl2 = scale * 1.4426950408889634f;
-  if (D == 64) {
-    using Cfg = FlashCfg<64>;
-    auto kern = flash_fwd_kernel<64>;
-    const dim3 grid(((S + Cfg::NQ * kQT - 1) / (Cfg::NQ * kQT)) * B * Hq);
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM))
-      return static_cast<int>(cudaGetLastError());
-    kern<<<grid, Cfg::THREADS, Cfg::SMEM, stream>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(out),
-                                                    lse, B, Hq, Hkv, S, sl2, causal ? 1 : 0, err);
-  } else {
-    using Cfg = FlashCfg<128>;
-    auto kern = flash_fwd_kernel<128>;
-    const dim3 grid(((S + Cfg::NQ * kQT - 1) / (Cfg::NQ * kQT)) * B * Hq);
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM))
-      return static_cast<int>(cudaGetLastError());
-    kern<<<grid, Cfg::THREADS, Cfg::SMEM, stream>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(out),
-                                                    lse, B, Hq, Hkv, S, sl2, causal ? 1 : 0, err);
-  }
-  return static_cast<int>(cudaGetLastError());
+  return D == 64 ? launch_fwd<64>(tq, tk, tv, out, lse, B, Hq, Hkv, S, sl2, causal, stream, err)
+                 : launch_fwd<128>(tq, tk, tv, out, lse, B, Hq, Hkv, S, sl2, causal, stream, err);
 }
 
 }  // namespace cfb
