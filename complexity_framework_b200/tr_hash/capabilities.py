@@ -109,7 +109,7 @@ def select_backend(config: TRHashEngineConfig, *, device_type: str,
 
     reasons = []
     if device_type != "cuda":
-        reasons.append("fused CUDA requires CUDA")
+        reasons.extend(("fused CUDA requires CUDA", "CGGR requires CUDA"))
         return decide(TRHashBackend.PYTORCH, reasons)
     if not fused_cuda_available:
         reasons.append("sm_100a extension is not built")

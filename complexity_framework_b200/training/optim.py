@@ -72,6 +72,10 @@ class _FlatGroup:
         with torch.no_grad():
             for p, o, n in zip(params, self.offsets, self.sizes):
                 self.compute[o:o + n].copy_(p.detach().reshape(-1))
+                # gradients that already exist (optimizer built after a backward)
+                # move into the flat buffer instead of being dropped by rebind()
+                if p.grad is not None:
+                    self.grad[o:o + n].copy_(p.grad.reshape(-1))
             masters = torch.zeros(off, device=dev, dtype=torch.float32)
             for p, o, n in zip(params, self.offsets, self.sizes):
                 masters[o:o + n].copy_(p.detach().reshape(-1).float())

@@ -1,5 +1,7 @@
-"""Fused tensor-parallel GEMMs on 2 GPUs: all-gather fused into the GEMM's TMA
-loads from peer memory, reduce-scatter by NVLink stores of fp32 partials.
+"""Fused tensor-parallel GEMMs on 2 GPUs: the all-gather runs inside the GEMM
+(copier warps pull peer row chunks over NVLink into the local gathered operand,
+which the TMA producer then reads), the reduce-scatter writes local bf16
+partials that a finish kernel sums by reading the owned rows of every peer.
 Forward and backward are compared with the same math on one GPU in fp32."""
 import os
 import socket
