@@ -363,6 +363,127 @@ void ep_gather_combine(const std::vector<int64_t>& srcs, const torch::Tensor& id
   raise_rc(rc, "ep_gather_combine");
 }
 
+// Grouped GEMM: gemm() plus the group tables of GemmGroups (gemm_tc.h).
+// mode 1: tile_group int32 [M / 256], b_stride; mode 2: k_start int32 [groups + 1],
+// c_stride (fp32 atomic epilogue only).
+void gemm_grouped(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, int64_t M,
+                  int64_t N, int64_t K, int64_t epi, const c10::optional<torch::Tensor>& out,
+                  const c10::optional<torch::Tensor>& gu, const c10::optional<torch::Tensor>& act,
+                  const c10::optional<torch::Tensor>& row_scale, int64_t expert_width,
+                  int64_t mode, const c10::optional<torch::Tensor>& tile_group,
+                  const c10::optional<torch::Tensor>& k_start, int64_t groups, int64_t b_stride,
+                  int64_t c_stride, double alpha) {
+  cfb::GemmArgs g;
+  cfb::GemmEpi ep;
+  const bool swiglu = epi == cfb::EPI_SWIGLU_FWD || epi == cfb::EPI_SWIGLU_BWD;
+  build_gemm(g, ep, false, false, false, A, a_mn, B, b_mn, M, N, K, epi, out, c10::nullopt, alpha,
+             gu, act, row_scale, 0, swiglu ? expert_width : 0, swiglu ? 1 : 0, 1.0, c10::nullopt,
+             0);
+  TORCH_CHECK(groups > 0, "gemm_grouped: groups must be positive");
+  ep.grp.mode = static_cast<int>(mode);
+  ep.grp.ngroups = static_cast<int>(groups);
+  if (mode == 1) {
+    TORCH_CHECK(tile_group.has_value() && tile_group->scalar_type() == torch::kInt32 &&
+                    tile_group->is_contiguous() && tile_group->is_cuda() &&
+                    tile_group->numel() >= M / 256,
+                "mode 1 needs int32 tile_group [M / 256]");
+    TORCH_CHECK(M % 256 == 0, "mode 1: M must be a multiple of 256");
+    TORCH_CHECK(b_stride > 0, "mode 1 needs b_stride");
+    TORCH_CHECK(b_mn ? B.size(0) >= groups * b_stride : B.size(0) >= groups * b_stride,
+                "gemm_grouped: B holds fewer than groups * b_stride rows");
+    ep.grp.tile_group = tile_group->data_ptr<int>();
+    ep.grp.b_stride = b_stride;
+  } else if (mode == 2) {
+    TORCH_CHECK(k_start.has_value() && k_start->scalar_type() == torch::kInt32 &&
+                    k_start->is_contiguous() && k_start->is_cuda() &&
+                    k_start->numel() >= groups + 1,
+                "mode 2 needs int32 k_start [groups + 1]");
+    TORCH_CHECK(epi == cfb::EPI_F32_ATOMIC && a_mn && b_mn,
+                "mode 2 is the fp32 atomic weight-gradient GEMM with MN-major operands");
+    TORCH_CHECK(out->size(0) >= groups * c_stride && c_stride >= M, "mode 2: out too small");
+    ep.grp.k_start = k_start->data_ptr<int>();
+    ep.grp.c_stride = c_stride;
+  } else {
+    TORCH_CHECK(false, "gemm_grouped: mode must be 1 or 2");
+  }
+  const int rc = cfb::gemm_tc_launch(g, ep, at::cuda::getCurrentCUDAStream(),
+                                     err_ptr(A.get_device()));
+  raise_rc(rc, "gemm_grouped");
+}
+
+// Expert-contiguous plan of routes int64 [k, T] over E experts with per-slot
+// weights slot_w fp32 [k]: (seg_start [E+1], tile_group [R/256], row_token [R],
+// row_weight [R], token_pos [k*T]) with R = moe_rows_bound(k*T, E).
+std::vector<torch::Tensor> moe_plan(const torch::Tensor& routes, int64_t E,
+                                    const torch::Tensor& slot_w) {
+  TORCH_CHECK(routes.is_cuda() && routes.scalar_type() == torch::kInt64 && routes.dim() == 2 &&
+                  routes.is_contiguous(),
+              "routes must be contiguous int64 [k, T] on CUDA");
+  TORCH_CHECK(slot_w.is_cuda() && slot_w.scalar_type() == torch::kFloat32 &&
+                  slot_w.numel() == routes.size(0),
+              "slot_w must be fp32 [k] on CUDA");
+  const c10::cuda::CUDAGuard guard(routes.device());
+  const int64_t k = routes.size(0), T = routes.size(1);
+  const int64_t R = cfb::moe_rows_bound(k * T, static_cast<int>(E));
+  auto i32 = torch::dtype(torch::kInt32).device(routes.device());
+  const int64_t nblk = (k * T + 1023) / 1024;
+  auto blk = torch::empty({nblk * E}, i32);
+  auto seg = torch::empty({E + 1}, i32);
+  auto tiles = torch::empty({R / 256}, i32);
+  auto row_token = torch::empty({R}, i32);
+  auto row_weight = torch::empty({R}, torch::dtype(torch::kFloat32).device(routes.device()));
+  auto token_pos = torch::empty({k * T}, i32);
+  const int rc = cfb::moe_plan_launch(routes.data_ptr<int64_t>(), static_cast<int>(k), T,
+                                      static_cast<int>(E), slot_w.data_ptr<float>(),
+                                      blk.data_ptr<int>(), seg.data_ptr<int>(),
+                                      tiles.data_ptr<int>(), row_token.data_ptr<int>(),
+                                      row_weight.data_ptr<float>(), token_pos.data_ptr<int>(),
+                                      at::cuda::getCurrentCUDAStream());
+  raise_rc(rc, "moe_plan");
+  return {seg, tiles, row_token, row_weight, token_pos};
+}
+
+// dst [R, H] = scale * src[row_token] (zero rows where row_token < 0)
+torch::Tensor moe_gather(const torch::Tensor& src, const torch::Tensor& row_token, double scale) {
+  check_bf16_cuda(src, "src");
+  TORCH_CHECK(src.dim() == 2 && src.is_contiguous(), "src must be contiguous [T, H]");
+  TORCH_CHECK(row_token.scalar_type() == torch::kInt32 && row_token.is_contiguous(),
+              "row_token must be contiguous int32");
+  const c10::cuda::CUDAGuard guard(src.device());
+  auto dst = torch::empty({row_token.numel(), src.size(1)}, src.options());
+  const int rc = cfb::moe_gather_launch(src.data_ptr(), row_token.data_ptr<int>(), dst.data_ptr(),
+                                        row_token.numel(), static_cast<int>(src.size(1)),
+                                        static_cast<float>(scale), num_sms(src.get_device()),
+                                        at::cuda::getCurrentCUDAStream());
+  raise_rc(rc, "moe_gather");
+  return dst;
+}
+
+// out [T, H] = base + scale * sum_j src[token_pos[j*T + t]]
+torch::Tensor moe_combine(const torch::Tensor& src, const torch::Tensor& token_pos, int64_t k,
+                          double scale, const c10::optional<torch::Tensor>& base) {
+  check_bf16_cuda(src, "src");
+  TORCH_CHECK(src.dim() == 2 && src.is_contiguous(), "src must be contiguous [R, H]");
+  TORCH_CHECK(token_pos.scalar_type() == torch::kInt32 && token_pos.is_contiguous() &&
+                  token_pos.numel() % k == 0,
+              "token_pos must be contiguous int32 [k*T]");
+  const int64_t T = token_pos.numel() / k, H = src.size(1);
+  if (base.has_value()) {
+    check_bf16_cuda(*base, "base");
+    TORCH_CHECK(base->is_contiguous() && base->numel() == T * H, "base must be [T, H]");
+  }
+  const c10::cuda::CUDAGuard guard(src.device());
+  auto out = torch::empty({T, H}, src.options());
+  const int rc = cfb::moe_combine_launch(src.data_ptr(), token_pos.data_ptr<int>(),
+                                         base.has_value() ? base->data_ptr() : nullptr,
+                                         out.data_ptr(), T, static_cast<int>(H),
+                                         static_cast<int>(k), static_cast<float>(scale),
+                                         num_sms(src.get_device()),
+                                         at::cuda::getCurrentCUDAStream());
+  raise_rc(rc, "moe_combine");
+  return out;
+}
+
 // [B, H, S, D] bf16 view with a contiguous last dim and 16-byte aligned rows
 // (TMA requirements) -> strided descriptor.
 cfb::Bhsd bhsd_of(const torch::Tensor& t, const char* name) {
@@ -518,6 +639,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("expert_width") = 0, py::arg("n_experts") = 0, py::arg("shared_scale") = 1.0,
         py::arg("stats") = py::none(), py::arg("bn") = 0);
   m.def("gemm_choose_bn", &gemm_choose_bn);
+  m.def("gemm_grouped", &gemm_grouped, "grouped tcgen05 GEMM", py::arg("A"), py::arg("a_mn"),
+        py::arg("B"), py::arg("b_mn"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epi"),
+        py::arg("out") = py::none(), py::arg("gu") = py::none(), py::arg("act") = py::none(),
+        py::arg("row_scale") = py::none(), py::arg("expert_width") = 0, py::arg("mode") = 1,
+        py::arg("tile_group") = py::none(), py::arg("k_start") = py::none(),
+        py::arg("groups") = 1, py::arg("b_stride") = 0, py::arg("c_stride") = 0,
+        py::arg("alpha") = 1.0);
+  m.def("moe_plan", &moe_plan);
+  m.def("moe_gather", &moe_gather);
+  m.def("moe_combine", &moe_combine, py::arg("src"), py::arg("token_pos"), py::arg("k"),
+        py::arg("scale") = 1.0, py::arg("base") = py::none());
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_bwd", &flash_attn_bwd);
   m.def("dp_reduce_shard", &dp_reduce_shard);

@@ -226,6 +226,41 @@ struct SegMaps {
   }
 };
 
+// One work unit of the persistent schedule: output tile t (row tile t / num_n),
+// K blocks [kb0, kb1), group g.  Every role decodes the same units, so a unit
+// without work is skipped by all of them (no loads, MMAs or epilogue hand-off).
+struct Unit {
+  int t, kb0, kb1, g;
+  bool skip;
+};
+
+__device__ __forceinline__ Unit decode_unit(int u, int num_tiles, int num_n, int num_m,
+                                            int m_shift, int ksplit, int nk, const GemmGroups& gr) {
+  Unit r;
+  if (gr.mode == 2) {
+    const int per_group = num_tiles * ksplit;
+    r.g = u / per_group;
+    const int rem = u % per_group;
+    r.t = rem / ksplit;
+    const int s = rem % ksplit;
+    const int g0 = __ldg(gr.k_start + r.g) / 64, g1 = __ldg(gr.k_start + r.g + 1) / 64;
+    r.kb0 = g0 + s * (g1 - g0) / ksplit;
+    r.kb1 = g0 + (s + 1) * (g1 - g0) / ksplit;
+    r.skip = r.kb0 >= r.kb1;
+    return r;
+  }
+  r.t = u / ksplit;
+  r.kb0 = (u % ksplit) * nk / ksplit;
+  r.kb1 = ((u % ksplit) + 1) * nk / ksplit;
+  r.g = 0;
+  r.skip = false;
+  if (gr.mode == 1) {
+    r.g = __ldg(gr.tile_group + (r.t / num_n + m_shift) % num_m);
+    r.skip = r.g < 0;
+  }
+  return r;
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI, bool PAIR, int NA = 1, int NB = 1>
 __global__ void __launch_bounds__(384, 1)
     gemm_tc_kernel(const __grid_constant__ SegMaps<NA> tmA,
@@ -268,7 +303,7 @@ __global__ void __launch_bounds__(384, 1)
   const int nk = (K + kBK - 1) / kBK;
   // work unit u = (tile u / ksplit, K slice u % ksplit); ksplit > 1 only with the
   // fp32 atomic epilogue, which sums the partial products of the slices
-  const int total = num_tiles * ksplit;
+  const int total = num_tiles * ksplit * (ep.grp.mode == 2 ? ep.grp.ngroups : 1);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -320,10 +355,13 @@ __global__ void __launch_bounds__(384, 1)
         ok = sys_wait_all(ep.sync.pad, ep.sync.world, ep.sync.rank, ep.sync.round, ep.sync.epoch,
                           abort_flag, err, 16);
       for (int u = unit; u < total && ok; u += units) {
-        const int t = u / ksplit;
-        const int kb0 = (u % ksplit) * nk / ksplit, kb1 = ((u % ksplit) + 1) * nk / ksplit;
+        const Unit un = decode_unit(u, num_tiles, num_n, num_m, m_shift, ksplit, nk, ep.grp);
+        if (un.skip) continue;
+        const int t = un.t, kb0 = un.kb0, kb1 = un.kb1;
         const int m0 = ((t / num_n + m_shift) % num_m) * Cfg::TILE_M + static_cast<int>(rank) * kBM;
         const int n0 = (t % num_n) * BN;
+        // row-grouped: this group's B rows (K-major B) or K rows (MN-major B)
+        const int b_off = ep.grp.mode == 1 ? static_cast<int>(un.g * ep.grp.b_stride) : 0;
         if (ep.ag.active) {
           // rows owned by a peer: wait until a copier warp has gathered them
           const int owner = m0 / ep.ag.rows;
@@ -345,7 +383,9 @@ __global__ void __launch_bounds__(384, 1)
         // this CTA's B rows: half of the (possibly narrower) tail tile when paired
         const int n_rem = N - n0;
         const int n_this = n_rem < BN ? n_rem : BN;
-        const int nb0 = PAIR ? n0 + static_cast<int>(rank) * (n_this / 2) : n0;
+        const int nb0 = (PAIR ? n0 + static_cast<int>(rank) * (n_this / 2) : n0) +
+                        (B_MN ? 0 : b_off);
+        const int kb_off = B_MN ? b_off : 0;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty, 10)) {
             ok = false;
@@ -370,7 +410,7 @@ __global__ void __launch_bounds__(384, 1)
               const CUtensorMap* mb = tmB.pick(nb0, &rb);
               tma_load_2d_pair(sB, mb, bar, kb * kBK, rb);
             } else {
-              const CUtensorMap* mb = tmB.pick(kb * kBK, &rb);
+              const CUtensorMap* mb = tmB.pick(kb * kBK + kb_off, &rb);
 #pragma unroll
               for (int i = 0; i < B_ROWS / 64; ++i)
                 tma_load_2d_pair(sB + i * 64 * kBK * 2, mb, bar, nb0 + 64 * i, rb);
@@ -388,10 +428,10 @@ __global__ void __launch_bounds__(384, 1)
                 tma_load_2d(sA + i * 64 * kBK * 2, ma, &full_bar[stage], m0 + 64 * i, ra);
             }
             if constexpr (!B_MN) {
-              const CUtensorMap* mb = tmB.pick(n0, &rb);
+              const CUtensorMap* mb = tmB.pick(nb0, &rb);
               tma_load_2d(sB, mb, &full_bar[stage], kb * kBK, rb);
             } else {
-              const CUtensorMap* mb = tmB.pick(kb * kBK, &rb);
+              const CUtensorMap* mb = tmB.pick(kb * kBK + kb_off, &rb);
 #pragma unroll
               for (int i = 0; i < BN / 64; ++i)
                 tma_load_2d(sB + i * 64 * kBK * 2, mb, &full_bar[stage], n0 + 64 * i, rb);
@@ -413,8 +453,9 @@ __global__ void __launch_bounds__(384, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int u = unit; u < total && ok; u += units) {
-        const int t = u / ksplit;
-        const int kb0 = (u % ksplit) * nk / ksplit, kb1 = ((u % ksplit) + 1) * nk / ksplit;
+        const Unit un = decode_unit(u, num_tiles, num_n, num_m, m_shift, ksplit, nk, ep.grp);
+        if (un.skip) continue;
+        const int t = un.t, kb0 = un.kb0, kb1 = un.kb1;
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, abort_flag, err, kErrTimeoutTmem, 11)) {
           ok = false;
           break;
@@ -524,7 +565,11 @@ __global__ void __launch_bounds__(384, 1)
                                       0u, lane};
     bool ep_ok = true;
     for (int u = unit; u < total; u += units) {
-      const int t = u / ksplit;
+      const Unit un = decode_unit(u, num_tiles, num_n, num_m, m_shift, ksplit, nk, ep.grp);
+      if (un.skip) continue;
+      const int t = un.t;
+      // K-grouped weight gradients: this group's output rows
+      const int64_t c_row0 = ep.grp.mode == 2 ? un.g * ep.grp.c_stride : 0;
       const int m_blk = (t / num_n + m_shift) % num_m;
       const int n_blk = t % num_n;
       const int m0 = m_blk * Cfg::TILE_M + static_cast<int>(rank) * kBM;
@@ -712,7 +757,7 @@ __global__ void __launch_bounds__(384, 1)
                 out[q] = make_float4(v[4 * q] * ep.alpha, v[4 * q + 1] * ep.alpha,
                                      v[4 * q + 2] * ep.alpha, v[4 * q + 3] * ep.alpha);
             } else if constexpr (EPI == EPI_F32_ATOMIC) {
-              float* out = reinterpret_cast<float*>(ep.c) + static_cast<int64_t>(row) * ep.ldc + n0 + c;
+              float* out = reinterpret_cast<float*>(ep.c) + (c_row0 + row) * ep.ldc + n0 + c;
 #pragma unroll
               for (int q = 0; q < 8; ++q)
                 red_add_v4(out + 4 * q, v[4 * q] * ep.alpha, v[4 * q + 1] * ep.alpha,
@@ -771,9 +816,19 @@ __global__ void __launch_bounds__(384, 1)
 // CUDA work so far was served from PyTorch's caching allocator, e.g. the
 // autograd engine's worker thread).  Make the current device's primary context
 // current on such threads first.
+// Driver entry points are looked up through the runtime, so the extension has
+// no link-time dependency on libcuda (it imports on machines without a driver).
 void ensure_current_context() {
+  using GetCurrentFn = CUresult (*)(CUcontext*);
+  static GetCurrentFn get_current = nullptr;
+  if (get_current == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q);
+    get_current = reinterpret_cast<GetCurrentFn>(p);
+  }
   CUcontext ctx = nullptr;
-  if (cuCtxGetCurrent(&ctx) == CUDA_SUCCESS && ctx != nullptr) return;
+  if (get_current != nullptr && get_current(&ctx) == CUDA_SUCCESS && ctx != nullptr) return;
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaSetDevice(dev);
 }
@@ -876,10 +931,13 @@ static int launch_impl(const SegMaps<NA>& ta, const SegMaps<NB>& tb, const CUten
       max_units = num_sms;
     }
   }
-  const int tiles = ((M + Cfg::TILE_M - 1) / Cfg::TILE_M) * ((N + BN - 1) / BN);
+  // K-grouped weight gradients: every group contributes its own tiles; its K
+  // range is about K / groups on average
+  const int groups = ep.grp.mode == 2 ? ep.grp.ngroups : 1;
+  const int tiles = ((M + Cfg::TILE_M - 1) / Cfg::TILE_M) * ((N + BN - 1) / BN) * groups;
   if (EPI == EPI_F32_ATOMIC && ksplit == 0) {
     // pick the K split that fills the machine best (>= 8 K blocks per slice)
-    const int nk = (K + kBK - 1) / kBK;
+    const int nk = (K / groups + kBK - 1) / kBK;
     int best = 1;
     double best_eff = 0.0;
     for (int ks = 1; ks <= 16 && nk / ks >= 8; ++ks) {
@@ -1068,12 +1126,21 @@ int gemm_tc_launch(const GemmArgs& g, const GemmEpi& ep, cudaStream_t stream, in
   SegMaps<1> ta, tb;
   ta.seg_rows = tb.seg_rows = 0;
   ta.nseg = tb.nseg = 1;
+  if (ep.grp.mode == 1 && (ep.grp.tile_group == nullptr || ep.grp.ngroups <= 0 ||
+                           ep.grp.b_stride <= 0 || g.M % 256 != 0))
+    return -9;
+  if (ep.grp.mode == 2 && (ep.grp.k_start == nullptr || ep.grp.ngroups <= 0 || !g.a_mn ||
+                           !g.b_mn || g.epi != EPI_F32_ATOMIC))
+    return -9;
   int rc = g.a_mn ? make_operand_map(&ta.m[0], g.A, true, g.K, g.M, g.lda, kBM)
                   : make_operand_map(&ta.m[0], g.A, false, g.M, g.K, g.lda, kBM);
   if (rc) return rc;
+  // row-grouped: B holds every group's rows
+  const int64_t b_rows = ep.grp.mode == 1 ? ep.grp.ngroups * ep.grp.b_stride : -1;
   // pair mode: each CTA loads half of a K-major B tile
-  rc = g.b_mn ? make_operand_map(&tb.m[0], g.B, true, g.K, g.N, g.ldb, bn)
-              : make_operand_map(&tb.m[0], g.B, false, g.N, g.K, g.ldb, g.M > kBM ? bn / 2 : bn);
+  rc = g.b_mn ? make_operand_map(&tb.m[0], g.B, true, b_rows > 0 ? b_rows : g.K, g.N, g.ldb, bn)
+              : make_operand_map(&tb.m[0], g.B, false, b_rows > 0 ? b_rows : g.N, g.K, g.ldb,
+                                 g.M > kBM ? bn / 2 : bn);
   if (rc) return rc;
   CUtensorMap tc[2];
   rc = epilogue_maps(g, ep, tc);

@@ -58,6 +58,24 @@ struct AgCopy {
   int active = 0;
 };
 
+// Grouped GEMMs (expert-parallel work inside one launch).
+//  mode 1, row-grouped: the A rows are sorted into per-group segments padded to
+//    the 256-row tile; tile_group[m_tile] is the group of each 256-row tile (< 0:
+//    no work) and B's storage rows of group g start at g * b_stride (N rows of a
+//    K-major B, K rows of an MN-major B).
+//  mode 2, K-grouped (weight gradients): group g multiplies the K rows
+//    [k_start[g], k_start[g+1]) of MN-major A and B (multiples of 64) into output
+//    rows [g * c_stride, g * c_stride + M); work units are (group, tile, K slice).
+// The tables live in device memory, so segment sizes never reach the host.
+struct GemmGroups {
+  int mode = 0;
+  const int* tile_group = nullptr;
+  const int* k_start = nullptr;
+  int ngroups = 0;
+  int64_t b_stride = 0;
+  int64_t c_stride = 0;
+};
+
 struct GemmEpi {
   void* c = nullptr;
   int64_t ldc = 0;
@@ -78,6 +96,7 @@ struct GemmEpi {
   int64_t peer_rows = 0;        // rows owned by each rank
   DistSync sync;
   AgCopy ag;
+  GemmGroups grp;
 };
 
 struct GemmArgs {

@@ -92,4 +92,15 @@ struct CopyJobs {
 };
 void copy_jobs(const CopyJobs& jobs, cudaStream_t s);
 
+// Expert-contiguous routed experts (moe_grouped.cu).  routes int64 [k, T];
+// rows_bound = moe_rows_bound(k*T, E) sorted rows (segments padded to 256).
+int moe_rows_bound(int64_t n_assign, int E);
+int moe_plan_launch(const int64_t* routes, int k, int64_t T, int E, const float* slot_w,
+                    int* blk_hist, int* seg_start, int* tile_group, int* row_token,
+                    float* row_weight, int* token_pos, cudaStream_t stream);
+int moe_gather_launch(const void* src, const int* row_token, void* dst, int64_t rows, int H,
+                      float scale, int num_sms, cudaStream_t stream);
+int moe_combine_launch(const void* src, const int* token_pos, const void* base, void* out,
+                       int64_t T, int H, int k, float scale, int num_sms, cudaStream_t stream);
+
 }  // namespace cfb

@@ -146,7 +146,64 @@ def case_norms(iters: int) -> None:
     check_errors(0)
 
 
-CASES = {"gemm": case_gemm, "gemm_bn": case_gemm_bn, "flash": case_flash, "norms": case_norms}
+def _zipf_ids(T, V, seed=0, s=1.1):
+    g = torch.Generator().manual_seed(seed)
+    p = torch.arange(1, V + 1, dtype=torch.float64).pow(-s)
+    order = torch.randperm(V, generator=g)
+    return order[torch.multinomial(p / p.sum(), T, replacement=True, generator=g)]
+
+
+def case_moe(iters: int) -> None:
+    """One TR-Hash FFN layer (shared SwiGLU + top-2 routed experts), forward + backward,
+    at the expert shapes of the 1B and 7B configurations: this framework's engine
+    (grouped tcgen05 kernels) and, when installed, the reference engine (its Triton
+    CGGR path), same weights, Zipf(1.1) token ids."""
+    import os
+    import sys
+
+    from ..tr_hash import TRHashEngine, TRHashEngineConfig
+
+    shapes = [("1b_e16_w256", 16384, 2048, 5632, 16, 256, "token_id_balanced_hash"),
+              ("7b_e8_w512", 8192, 4096, 11008, 8, 512, "modulo_cyclic")]
+    ref_root = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(
+        os.path.abspath(__file__)))), "baseline", "_ref")
+    ref = None
+    if os.path.isdir(os.path.join(ref_root, "complexity")):
+        sys.path.insert(0, ref_root)
+        try:
+            import complexity.tr_hash as ref
+        except Exception as exc:  # pragma: no cover - depends on the install
+            print(json.dumps({"reference": f"unavailable: {exc}"}))
+        finally:
+            sys.path.remove(ref_root)
+    for name, T, H, S, E, W, strat in shapes:
+        kw = dict(hidden_size=H, vocab_size=32000, num_experts=E, top_k=2, shared_width=S,
+                  expert_width=W, routing_strategy=strat, precision="bf16")
+        ids = _zipf_ids(T, 32000).view(1, T).cuda()
+        x = (torch.randn(1, T, H, device="cuda") * 0.5).bfloat16()
+        dy = torch.randn(1, T, H, device="cuda").bfloat16()
+        fl = 2.0 * 3 * T * H * (2 * S + 3 * 2 * W)   # fwd + bwd (x3) of gate|up and down GEMMs
+        arms = [("ours", TRHashEngine(TRHashEngineConfig(**kw)))]
+        if ref is not None:
+            arms.append(("reference", ref.TRHashEngine(ref.TRHashEngineConfig(**kw))))
+        for arm, eng in arms:
+            eng = eng.cuda().to(torch.bfloat16)
+            if arm == "reference":
+                eng.load_state_dict(arms[0][1].state_dict(), strict=False)
+            xx = x.clone().requires_grad_()
+
+            def run():
+                out = eng(xx, ids)
+                out.backward(dy)
+
+            ms = cuda_time(run, iters)
+            _report(f"moe_fwd_bwd_{name}_{arm}", ms, fl)
+    torch.cuda.synchronize()
+    check_errors(0)
+
+
+CASES = {"gemm": case_gemm, "gemm_bn": case_gemm_bn, "flash": case_flash, "norms": case_norms,
+         "moe": case_moe}
 
 
 def main(argv=None) -> None:

@@ -316,13 +316,16 @@ class TRHashEngine(nn.Module):
             routed = ep(flat, routes, self._route_weights)
             out = (self._shared_ep(flat) + self.config.routed_output_scale * routed).view(B, S, H)
             return out if residual is None else residual + out
-        shared = self._shared(flat)
         if backend is TRHashBackend.CGGR:
+            # shared SwiGLU as one fused gate|up + down GEMM pair on CUDA bf16,
+            # routed experts on the grouped kernels
+            shared_term = self._shared_ep(flat)
             routed = self._grouped_forward(flat, token_ids.reshape(-1))
         else:
+            shared_term = self.config.shared_output_scale * self._shared(flat)
             routes = self._routes(token_ids).reshape(self.config.top_k, -1)
             routed = self._reference_routed(flat, routes)
-        out = self.config.shared_output_scale * shared + self.config.routed_output_scale * routed
+        out = shared_term + self.config.routed_output_scale * routed
         out = out.view(B, S, H)
         return out if residual is None else residual + out
 

@@ -24,6 +24,7 @@ SOURCES = [
     "tp_fused.cu",
     "ep_fused.cu",
     "pack.cu",
+    "moe_grouped.cu",
 ]
 
 # Link the shared system libstdc++ (the one libtorch uses).  The compiler wrapper
