@@ -41,6 +41,13 @@ class MLPConfig:
     active_num_experts: Optional[int] = None
     active_expert_width: Optional[int] = None
     attention_type: str = "gqa"
+    # lexical MLPs
+    lexical_object_rank: int = 16
+    lexical_object_gate_init: float = 0.1
+    micro_num_experts: int = 4
+    micro_expert_width: int = 16
+    micro_expert_gate_init: float = 0.1
+    bias: bool = False
     extra: Dict[str, Any] = field(default_factory=dict)
 
 

@@ -78,8 +78,13 @@ class TransformerBlock(nn.Module):
             top_k=config.top_k, top_k_primary_weight=config.top_k_primary_weight,
             layer_idx=layer_idx, use_custom_kernels=config.use_custom_kernels,
             use_cggr=config.use_cggr, active_num_experts=config.active_num_experts,
-            active_expert_width=config.active_expert_width, attention_type=attn_type)
-        from ..core import dense_mlp  # noqa: F401  (registers dense MLP types)
+            active_expert_width=config.active_expert_width, attention_type=attn_type,
+            lexical_object_rank=config.lexical_object_rank,
+            lexical_object_gate_init=config.lexical_object_gate_init,
+            micro_num_experts=config.micro_num_experts,
+            micro_expert_width=config.micro_expert_width,
+            micro_expert_gate_init=config.micro_expert_gate_init)
+        from ..core import dense_mlp, lexical_mlp  # noqa: F401  (registers MLP types)
         self.mlp = MLP_REGISTRY.build(config.mlp_type, mlp_cfg)
 
     def forward(self, hidden_states: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,

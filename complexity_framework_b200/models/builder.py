@@ -48,8 +48,20 @@ class ComplexityModel(nn.Module):
 
             self.embed_positions = LearnedPositionalEmbedding(config.max_position_embeddings,
                                                               config.hidden_size)
+        from ..core.lexical_mlp import LEXICAL_MLP_TYPES
+
+        lexical = config.mlp_type in LEXICAL_MLP_TYPES
+        if lexical and config.tie_lexical_object_embeddings:
+            # one [vocab, rank] table shared by every layer, owned by the model
+            self.lexical_token_scale = self.layers[0].mlp.token_scale
+            for layer in self.layers:
+                layer.mlp.tie_token_scale(self.lexical_token_scale)
         self._gradient_checkpointing = False
         self.apply(self._init_weights)
+        if lexical:  # as in the reference: the first (or shared) table starts at zero
+            table = (self.lexical_token_scale if hasattr(self, "lexical_token_scale")
+                     else self.layers[0].mlp.token_scale)
+            nn.init.zeros_(table.weight)
         self._init_residual_scaling()
         self._apply_mup_init_scaling()
 
