@@ -91,6 +91,13 @@ class TransformerBlock(nn.Module):
                 past_key_value: Optional[Any] = None, use_cache: bool = False,
                 token_ids: Optional[torch.Tensor] = None, **unused
                 ) -> Tuple[torch.Tensor, Optional[Any], None]:
+        if token_ids is not None and token_ids.is_floating_point():
+            # routing ids carried as float between pipeline stages: the integer
+            # ids route; a zero-valued term gives the carried ids the (zero)
+            # gradient the pipeline runtime sends back to the previous stage
+            ids_f = token_ids
+            token_ids = ids_f.long()
+            hidden_states = hidden_states + (ids_f * 0).unsqueeze(-1).to(hidden_states.dtype)
         h, hidden_states = self._norm_skip(self.input_layernorm, hidden_states)
         if token_ids is not None and hasattr(self.self_attn, "set_token_ids"):
             self.self_attn.set_token_ids(token_ids)

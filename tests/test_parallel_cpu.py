@@ -160,3 +160,54 @@ def _zero_body(rank, world, tmp, mode):
 @pytest.mark.parametrize("mode", ["ddp", "fsdp"])
 def test_data_parallel_matches_single(mode):
     _run(2, _zero_body, mode)
+
+
+def _export_pp_body(rank, world, tmp):
+    """Export-traced pipe (torch.distributed.pipelining), 2 stages x 2 microbatches,
+    1F1B: the last stage's loss and a first-stage gradient match one process."""
+    from complexity_framework_b200.parallel.pipeline_export import (ExportPipelineRunner,
+                                                                      trace_pipeline)
+
+    def loss_fn(hidden, labels):
+        logits = hidden @ ref.embed_tokens.weight.detach().t()
+        return torch.nn.functional.cross_entropy(logits.reshape(-1, logits.size(-1)),
+                                                 labels.reshape(-1))
+
+    ref = _model()
+    ids = _ids(n=4, s=16)
+    labels = torch.roll(ids, -1, 1)
+    # single process: the same model, head weight treated as a constant
+    hidden = ref(ids, return_logits=False)["last_hidden_state"]
+    full = 0.5 * (loss_fn(hidden[:2], labels[:2]) + loss_fn(hidden[2:], labels[2:]))
+    full.backward()
+    want_grad = ref.layers[0].self_attn.o_proj.weight.grad.clone()
+
+    model = _model()
+    pipe = trace_pipeline(model, ids[:2], pp_size=world)
+    runner = ExportPipelineRunner(pipe, rank, world, torch.device("cpu"), n_microbatches=2,
+                                  loss_fn=loss_fn, schedule="1f1b")
+    out = runner.step(ids if rank == 0 else None, labels if rank == world - 1 else None)
+    if rank == world - 1:
+        assert torch.allclose(out, full.detach(), atol=1e-5), (out, full)
+    if rank == 0:
+        g = dict(runner.module.named_parameters())
+        name = next(n for n in g if n.endswith("layers.0.self_attn.o_proj.weight"))
+        # the schedule scales each microbatch's loss by 1 / n_microbatches, so the
+        # accumulated gradient is that of the mean over microbatches
+        assert torch.allclose(g[name].grad, want_grad, atol=1e-6)
+
+
+def test_export_pipeline_two_stages_match_single_process():
+    _run(2, _export_pp_body)
+
+
+def test_export_pipeline_split_spec():
+    from torch.distributed.pipelining import SplitPoint
+
+    from complexity_framework_b200.parallel.pipeline_export import pipeline_split_spec
+
+    assert pipeline_split_spec(32, 8) == {f"layers.{i}": SplitPoint.BEGINNING
+                                          for i in range(4, 32, 4)}
+    with pytest.raises(ValueError, match="divisible"):
+        pipeline_split_spec(30, 8)
+    assert pipeline_split_spec(30, 8, require_even=False)["layers.3"] is SplitPoint.BEGINNING
