@@ -160,13 +160,14 @@ def build_ours(world, args):
 
     torch.manual_seed(0)
     model = ComplexityModel(tr_hash_200m_config())
-    # one GPU: steps after the second warm-up step replay a captured CUDA graph
-    # (forward + backward + AdamW); multi-GPU steps run eagerly
+    # steps after the second warm-up step replay a captured CUDA graph (forward +
+    # backward + AdamW; on several GPUs also the fused NVLink reduce, whose barrier
+    # epochs and hyper-parameters live on the device)
     cfg = TrainingConfig(learning_rate=3e-4, warmup_steps=0, lr_scheduler="constant",
                          precision="bf16", grad_clip=1.0, max_steps=10 ** 9,
                          distributed_mode="fsdp" if world > 1 else "none",
                          skip_param_update_check=True,
-                         cuda_graph=world == 1 and not args.no_graph, cuda_graph_warmup=2)
+                         cuda_graph=not args.no_graph, cuda_graph_warmup=2)
     trainer = Trainer(model, cfg)
 
     def step(ids, sync):
@@ -176,7 +177,9 @@ def build_ours(world, args):
         mode = "single GPU, flat fp32-master fused AdamW" + (
             ", step replayed from a CUDA graph" if cfg.cuda_graph else "")
     else:
-        mode = "fsdp-zero2 (sharded fp32 master/moments, replicated bf16 params)"
+        mode = ("zero2 data parallel: fused NVLink gradient reduce + sharded fp32 AdamW "
+                "(replicated bf16 params)" + (", step replayed from a CUDA graph"
+                                               if cfg.cuda_graph else ""))
     return step, mode
 
 

@@ -579,7 +579,7 @@ void dp_reduce_shard(const std::vector<int64_t>& grad, const std::vector<int64_t
                      const std::vector<int64_t>& pad, const std::vector<int64_t>& slots,
                      int64_t rank, int64_t lo, int64_t n, torch::Tensor& gs,
                      torch::Tensor& sumsq_local, torch::Tensor& ticket, int64_t epoch,
-                     bool publish) {
+                     bool publish, const c10::optional<torch::Tensor>& epoch_dev) {
   TORCH_CHECK(gs.is_cuda() && gs.scalar_type() == torch::kBFloat16 && gs.numel() >= n,
               "gs must be this rank's bf16 gradient shard");
   const c10::cuda::CUDAGuard guard(gs.device());
@@ -587,8 +587,9 @@ void dp_reduce_shard(const std::vector<int64_t>& grad, const std::vector<int64_t
   const int rc = cfb::fused_reduce_shard(pp, lo, n,
                                          reinterpret_cast<__nv_bfloat16*>(gs.data_ptr()),
                                          sumsq_local.data_ptr<float>(), ticket.data_ptr<int>(),
-                                         static_cast<int>(epoch), publish,
-                                         num_sms(gs.get_device()),
+                                         static_cast<int>(epoch),
+                                         epoch_dev.has_value() ? epoch_dev->data_ptr<int>() : nullptr,
+                                         publish, num_sms(gs.get_device()),
                                          at::cuda::getCurrentCUDAStream(), err_ptr(gs.get_device()));
   raise_rc(rc, "dp_reduce_shard");
 }
@@ -599,7 +600,13 @@ void dp_adamw_shard(const std::vector<int64_t>& grad, const std::vector<int64_t>
                     int64_t rank, int64_t lo, int64_t n, torch::Tensor& master, torch::Tensor& m,
                     torch::Tensor& v, const torch::Tensor& gs, double lr, double b1, double b2,
                     double eps, double wd, double bc1, double bc2, double max_norm,
-                    torch::Tensor& norm_out, torch::Tensor& ticket, int64_t epoch) {
+                    torch::Tensor& norm_out, torch::Tensor& ticket, int64_t epoch,
+                    const c10::optional<torch::Tensor>& epoch_dev,
+                    const c10::optional<torch::Tensor>& hyper) {
+  if (hyper.has_value())
+    TORCH_CHECK(hyper->is_cuda() && hyper->scalar_type() == torch::kFloat32 &&
+                    hyper->is_contiguous() && hyper->numel() >= 3,
+                "hyper must be contiguous fp32 (lr, bc1, bc2) on CUDA");
   for (const auto* t : {&master, &m, &v}) {
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat32 && t->numel() >= n,
                 "fp32 optimizer shard");
@@ -613,6 +620,8 @@ void dp_adamw_shard(const std::vector<int64_t>& grad, const std::vector<int64_t>
       static_cast<float>(b2), static_cast<float>(eps), static_cast<float>(wd),
       static_cast<float>(bc1), static_cast<float>(bc2), static_cast<float>(max_norm),
       norm_out.data_ptr<float>(), ticket.data_ptr<int>(), static_cast<int>(epoch),
+      epoch_dev.has_value() ? epoch_dev->data_ptr<int>() : nullptr,
+      hyper.has_value() ? hyper->data_ptr<float>() : nullptr,
       num_sms(master.get_device()), at::cuda::getCurrentCUDAStream(), err_ptr(master.get_device()));
   raise_rc(rc, "dp_adamw_shard");
 }
@@ -652,7 +661,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale") = 1.0, py::arg("base") = py::none());
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_bwd", &flash_attn_bwd);
-  m.def("dp_reduce_shard", &dp_reduce_shard);
-  m.def("dp_adamw_shard", &dp_adamw_shard);
+  m.def("dp_reduce_shard", &dp_reduce_shard, py::arg("grad"), py::arg("param"), py::arg("pad"),
+        py::arg("slots"), py::arg("rank"), py::arg("lo"), py::arg("n"), py::arg("gs"),
+        py::arg("sumsq_local"), py::arg("ticket"), py::arg("epoch"), py::arg("publish"),
+        py::arg("epoch_dev") = py::none());
+  m.def("dp_adamw_shard", &dp_adamw_shard, py::arg("grad"), py::arg("param"), py::arg("pad"),
+        py::arg("slots"), py::arg("rank"), py::arg("lo"), py::arg("n"), py::arg("master"),
+        py::arg("m"), py::arg("v"), py::arg("gs"), py::arg("lr"), py::arg("b1"), py::arg("b2"),
+        py::arg("eps"), py::arg("wd"), py::arg("bc1"), py::arg("bc2"), py::arg("max_norm"),
+        py::arg("norm_out"), py::arg("ticket"), py::arg("epoch"),
+        py::arg("epoch_dev") = py::none(), py::arg("hyper") = py::none());
+  m.def("dp_epoch_bump", [](torch::Tensor& e) {
+    TORCH_CHECK(e.is_cuda() && e.scalar_type() == torch::kInt32, "epoch counter: int32 CUDA");
+    const c10::cuda::CUDAGuard guard(e.device());
+    raise_rc(cfb::fused_epoch_bump(e.data_ptr<int>(), at::cuda::getCurrentCUDAStream()),
+             "dp_epoch_bump");
+  });
   register_elementwise(m);
 }

@@ -21,6 +21,10 @@
 // This replaces NCCL reduce-scatter + fp32 cast + AdamW + NCCL all-gather
 // (four passes and two collectives) with two kernels.
 //
+// Barrier epochs come either from the host or from a device step counter
+// (bumped by a one-thread kernel at the start of each step), so a CUDA graph
+// that captured a whole multi-GPU step advances them on every replay; the
+// AdamW step likewise reads (lr, bias corrections) from a device buffer.
 // Every wait on a peer is bounded by %globaltimer; on expiry the kernel
 // records kErrPeerTimeout (site = waiting rank) and returns, so a missing or
 // dead peer surfaces as a host-visible error instead of a hung GPU.
@@ -65,12 +69,21 @@ __device__ bool wait_peers(const PeerPtrs& pp, int round, int epoch, int* err) {
   return true;
 }
 
+// The barrier epoch of a launch: a host value, or (graph-replayable) the
+// device step counter * 16 + the launch's offset within the step.
+__device__ __forceinline__ int resolve_epoch(int epoch, const int* epoch_dev) {
+  return epoch_dev != nullptr ? __ldcg(epoch_dev) * 16 + epoch : epoch;
+}
+
+__global__ void epoch_bump_kernel(int* e) { e[0] += 1; }
+
 __global__ void reduce_shard_kernel(PeerPtrs pp, int64_t lo, int64_t n,
                                     __nv_bfloat16* __restrict__ gs,
                                     float* __restrict__ sumsq_local, int* __restrict__ ticket,
-                                    int epoch, int publish, int* err) {
+                                    int epoch, const int* epoch_dev, int publish, int* err) {
   __shared__ int ok;
   __shared__ float red[32];
+  epoch = resolve_epoch(epoch, epoch_dev);
   if (threadIdx.x == 0) {
     if (blockIdx.x == 0) signal_peers(pp, 0, epoch);
     ok = wait_peers(pp, 0, epoch, err) ? 1 : 0;
@@ -136,9 +149,16 @@ __global__ void adamw_shard_kernel(PeerPtrs pp, int64_t lo, int64_t n, float* __
                                    const __nv_bfloat16* __restrict__ gs, float lr, float b1, float b2,
                                    float eps, float wd, float bc1, float bc2_sqrt, float max_norm,
                                    float* __restrict__ norm_out, int* __restrict__ ticket,
-                                   int epoch, int* err) {
+                                   int epoch, const int* epoch_dev, const float* hyper,
+                                   int* err) {
   __shared__ int ok;
   __shared__ float coef;
+  epoch = resolve_epoch(epoch, epoch_dev);
+  if (hyper != nullptr) {  // (lr, bias correction 1, bias correction 2) of this step
+    lr = hyper[0];
+    bc1 = hyper[1];
+    bc2_sqrt = sqrtf(hyper[2]);
+  }
   if (threadIdx.x == 0) {
     if (blockIdx.x == 0) signal_peers(pp, 1, epoch);
     ok = wait_peers(pp, 1, epoch, err) ? 1 : 0;
@@ -206,13 +226,18 @@ __global__ void adamw_shard_kernel(PeerPtrs pp, int64_t lo, int64_t n, float* __
 
 }  // namespace
 
+int fused_epoch_bump(int* epoch_dev, cudaStream_t s) {
+  epoch_bump_kernel<<<1, 1, 0, s>>>(epoch_dev);
+  return static_cast<int>(cudaGetLastError());
+}
+
 int fused_reduce_shard(const PeerPtrs& pp, int64_t lo, int64_t n, __nv_bfloat16* gs,
                        float* sumsq_local,
-                       int* ticket, int epoch, bool publish, int num_sms, cudaStream_t s,
-                       int* err) {
+                       int* ticket, int epoch, const int* epoch_dev, bool publish, int num_sms,
+                       cudaStream_t s, int* err) {
   if (pp.world < 1 || pp.world > kMaxRanks || n % 8 != 0 || lo % 8 != 0) return -2;
   const int grid = num_sms;  // all blocks resident: block 0 always runs
-  reduce_shard_kernel<<<grid, 512, 0, s>>>(pp, lo, n, gs, sumsq_local, ticket, epoch,
+  reduce_shard_kernel<<<grid, 512, 0, s>>>(pp, lo, n, gs, sumsq_local, ticket, epoch, epoch_dev,
                                            publish ? 1 : 0, err);
   return static_cast<int>(cudaGetLastError());
 }
@@ -221,11 +246,12 @@ int fused_adamw_shard(const PeerPtrs& pp, int64_t lo, int64_t n, float* master, 
                       const __nv_bfloat16* gs, float lr, float b1, float b2, float eps, float wd,
                       float bc1,
                       float bc2, float max_norm, float* norm_out, int* ticket, int epoch,
-                      int num_sms, cudaStream_t s, int* err) {
+                      const int* epoch_dev, const float* hyper, int num_sms, cudaStream_t s,
+                      int* err) {
   if (pp.world < 1 || pp.world > kMaxRanks || n % 8 != 0 || lo % 8 != 0) return -2;
   adamw_shard_kernel<<<num_sms, 512, 0, s>>>(pp, lo, n, master, m, v, gs, lr, b1, b2, eps, wd,
                                              bc1, sqrtf(bc2), max_norm, norm_out, ticket, epoch,
-                                             err);
+                                             epoch_dev, hyper, err);
   return static_cast<int>(cudaGetLastError());
 }
 

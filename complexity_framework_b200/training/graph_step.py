@@ -12,9 +12,11 @@ optimizer's device hyper-parameters (learning rate and bias corrections of
 the upcoming step, see ``FusedAdamW.enable_device_hyper``), replays, and does
 the Python bookkeeping (step counters, lr scheduler).
 
-Eligibility: one process (no data/tensor/expert parallel collectives: the
-fused NVLink kernels count barrier epochs on the host), the flat fused AdamW
-on CUDA, fixed input shapes.  Anything else runs the eager step.
+Eligibility: the flat fused AdamW on CUDA and fixed input shapes, in one
+process or data-parallel on the fused NVLink reduce + AdamW kernels (their
+barrier epochs and hyper-parameters live on the device, so every replay
+advances them on all ranks alike).  Tensor/expert-parallel steps and the NCCL
+data-parallel path run eagerly.
 """
 from __future__ import annotations
 
@@ -41,11 +43,13 @@ class GraphedTrainStep:
         tr = self.tr
         if not torch.cuda.is_available():
             return "no CUDA device"
-        if tr.world > 1 or tr.sp_ws is not None or getattr(tr.model, "ep", None) is not None:
-            return "multi-process step (collectives count epochs on the host)"
         opt = tr.optimizer
         if not isinstance(opt, FusedAdamW) or not opt._use_kernels():
             return "needs the fused AdamW kernels"
+        if tr.sp_ws is not None or getattr(tr.model, "ep", None) is not None:
+            return "tensor/expert-parallel step (their barriers count epochs on the host)"
+        if tr.world > 1 and opt._fused is None:
+            return "multi-process step on NCCL collectives (only the fused NVLink path replays)"
         return None
 
     # ----------------------------------------------------------------- body

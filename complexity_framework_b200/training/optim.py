@@ -305,8 +305,8 @@ class FusedAdamW(torch.optim.Optimizer):
         buffer, filled by ``write_hyper`` before each step, instead of launch
         arguments: a CUDA graph that captured ``step`` then follows the
         learning-rate schedule and the step count across replays."""
-        if self._fused is not None or not self._use_kernels():
-            raise RuntimeError("device hyper-parameters need the single-process kernel path")
+        if not self._use_kernels():
+            raise RuntimeError("device hyper-parameters need the fused AdamW kernels")
         dev = self.flat_groups[0].master.device
         self._hyper = torch.zeros(len(self.param_groups), 3, device=dev, dtype=torch.float32)
 
@@ -458,29 +458,34 @@ class _FusedDP:
         dev = opt.flat_groups[0].compute.device
         self.sumsq = torch.zeros(1, device=dev, dtype=torch.float32)
         self.ticket = torch.zeros(2, device=dev, dtype=torch.int32)
+        # barrier epochs live on the device (bumped by a kernel each step), so a
+        # captured step keeps every rank's barriers in lockstep across replays
+        self.epoch_dev = torch.zeros(1, device=dev, dtype=torch.int32)
 
     def step(self, t: int, max_norm: float) -> None:
         from ..ops import require
 
         C = require()
         opt = self.opt
-        base = t * 16
+        C.dp_epoch_bump(self.epoch_dev)
         # reduce every group first: the partial norms of all groups accumulate in
         # one counter; the last group's last block publishes the total
         for i, g in enumerate(self.groups):
             fg = g["fg"]
             C.dp_reduce_shard(g["grad"], g["param"], g["pad"], g["slots"], self.rank, fg.lo,
-                              fg.shard, g["gs"], self.sumsq, self.ticket[0:1], base + i + 1,
-                              i == len(self.groups) - 1)
+                              fg.shard, g["gs"], self.sumsq, self.ticket[0:1], i + 1,
+                              i == len(self.groups) - 1, self.epoch_dev)
         for i, g in enumerate(self.groups):
             fg = g["fg"]
-            group = next(gr for gr, f in zip(opt.param_groups, opt._flat) if f is fg)
+            gi, group = next((k, gr) for k, (gr, f) in enumerate(zip(opt.param_groups, opt._flat))
+                             if f is fg)
             b1, b2 = group["betas"]
             C.dp_adamw_shard(g["grad"], g["param"], g["pad"], g["slots"], self.rank, fg.lo,
                              fg.shard, fg.master, fg.exp_avg, fg.exp_avg_sq, g["gs"],
                              group["lr"], b1, b2, group["eps"], group["weight_decay"],
                              1.0 - b1 ** t, 1.0 - b2 ** t, max_norm, opt._norm,
-                             self.ticket[1:2], base + i + 1)
+                             self.ticket[1:2], i + 1, self.epoch_dev,
+                             None if opt._hyper is None else opt._hyper[gi])
         for p_group, fg in zip(opt.param_groups, opt._flat):
             if fg is None:
                 continue

@@ -95,3 +95,54 @@ def test_fused_dp_matches_nccl_two_gpus():
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     diffs = dict(q.get() for _ in range(2))
     assert max(diffs.values()) < 2e-2, diffs
+
+
+def _graph_body(rank, world, port, q):
+    """Fused NVLink data parallel: the replayed CUDA-graph step equals the eager
+    step (device barrier epochs and device lr / bias corrections across replays)."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank), CFB_FUSED_DP="1")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", rank))
+    from complexity_framework_b200 import ComplexityModel, ModelConfig
+    from complexity_framework_b200.ops import check_errors
+    from complexity_framework_b200.training import Trainer, TrainingConfig
+
+    cfg = dict(hidden_size=256, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+               vocab_size=2048, intermediate_size=256, shared_intermediate_size=512,
+               num_experts=4, top_k=2, max_position_embeddings=256)
+    batches = [torch.randint(0, 2048, (4, 128), generator=torch.Generator().manual_seed(10 * rank + i))
+               for i in range(6)]
+    res = []
+    for graph in (False, True):
+        torch.manual_seed(0)
+        tr = Trainer(ComplexityModel(ModelConfig(**cfg)),
+                     TrainingConfig(learning_rate=1e-3, warmup_steps=2, lr_scheduler="cosine",
+                                    max_steps=6, grad_clip=1.0, distributed_mode="fsdp",
+                                    skip_param_update_check=True, cuda_graph=graph,
+                                    cuda_graph_warmup=2))
+        assert tr.optimizer._fused is not None
+        for b in batches:
+            tr.train_step(b)
+        if graph:
+            assert tr._graphed is not None and tr._graphed.graph is not None
+        res.append(torch.cat([p.detach().float().reshape(-1) for p in tr.model.parameters()]))
+    torch.cuda.synchronize()
+    check_errors(rank)
+    q.put((rank, (res[0] - res[1]).abs().max().item()))
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_dp_graph_replay_matches_eager_two_gpus():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_graph_body, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    diffs = dict(q.get() for _ in range(2))
+    assert max(diffs.values()) < 1e-2, diffs
