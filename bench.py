@@ -1,6 +1,7 @@
 """Headline benchmark: TR-HASH 200M pretraining throughput (train tokens/s per box).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --workload decode ...   (7B paged-KV serving, bench_decode.py)
 
 N > 1 is launched by torchrun (one process per GPU, NCCL).  Workload: the
 released 200M TR-GQA/TR-Hash architecture, random init, synthetic Zipf(1.1)
@@ -47,6 +48,8 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-count", action="store_true", help="skip the kernel-launch count step")
     p.add_argument("--no-graph", action="store_true", help="run every step eagerly")
+    p.add_argument("--workload", choices=("train", "decode"), default="train",
+                   help="train: the 200M pretraining headline; decode: 7B paged-KV serving")
     return p.parse_args()
 
 
@@ -248,6 +251,11 @@ def build_reference(world, args):
 def main():
     args = parse()
     world, rank, local = init_dist(args.gpus)
+    if args.workload == "decode":
+        sys.path.insert(0, ROOT)
+        import bench_decode
+
+        return bench_decode.main(args, world, rank, local, sys.modules[__name__])
     B, S, V = args.batch, args.seq, 32000
     try:
         build = build_ours if args.impl == "ours" else build_reference

@@ -121,7 +121,20 @@ class GroupedQueryAttention(nn.Module):
 
     # --------------------------------------------------------------- helpers
     def kqv_weight(self) -> torch.Tensor:
-        return torch.cat((self.k_proj.weight, self.q_proj.weight, self.v_proj.weight), 0)
+        ws = (self.k_proj.weight, self.q_proj.weight, self.v_proj.weight)
+        if self.training or torch.is_grad_enabled():
+            return torch.cat(ws, 0)
+        # inference: reuse one concatenated copy while the weights are unchanged
+        # (keyed on storage and version counter; dropped by train())
+        key = tuple((w.data_ptr(), w._version) for w in ws)
+        got = getattr(self, "_kqv_cache", None)
+        if got is None or got[0] != key:
+            got = self._kqv_cache = (key, torch.cat(ws, 0))
+        return got[1]
+
+    def train(self, mode: bool = True):
+        self._kqv_cache = None
+        return super().train(mode)
 
     def _project(self, x: torch.Tensor):
         kd = self.num_kv_heads * self.head_dim
@@ -297,6 +310,22 @@ class GroupedQueryAttention(nn.Module):
             kqv = fused.linear(x, self.kqv_weight())
         else:
             kqv = F.linear(x, self.kqv_weight())
+        if (fused_ok and type(self.rotary_emb) is RotaryEmbedding and self.head_dim in (64, 128)
+                and cache.pool.dtype == torch.bfloat16
+                and (not self.use_qk_norm or self.q_norm.weight.dtype == torch.bfloat16)):
+            # one kernel: qk-norm + RoPE of the new tokens, k/v straight into the pool
+            from ..ops._ext import require
+
+            cos_h, sin_h = self.rotary_emb.tables(cache.max_position + 1, x.device)
+            q = torch.empty(N, self.num_heads, self.head_dim, device=x.device, dtype=x.dtype)
+            norm = self.use_qk_norm
+            require().paged_qkv_rope(kqv.view(N, -1), self.q_norm.weight if norm else None,
+                                     self.k_norm.weight if norm else None, cos_h, sin_h,
+                                     cache.positions, cache.slots, q, cache.pool.k[layer_idx],
+                                     cache.pool.v[layer_idx],
+                                     float(self.q_norm.eps) if norm else 0.0)
+            o = cache.attend(layer_idx, q, self.attn_scale)
+            return fused.linear(o.reshape(1, N, qd), self.o_proj.weight, residual)
         k, q, v = kqv.view(N, -1).split((kd, qd, kd), -1)
         q = q.reshape(N, self.num_heads, self.head_dim)
         k = k.reshape(N, self.num_kv_heads, self.head_dim)

@@ -311,14 +311,64 @@ void paged_attention(const torch::Tensor& q, const torch::Tensor& k_pool,
   TORCH_CHECK(out.sizes() == q.sizes(), "out shape");
   (void)max_q_len;
   const c10::cuda::CUDAGuard g(q.device());
-  const int rc = cfb::paged_attention(P<bf16>(q), P<bf16>(k_pool), P<bf16>(v_pool),
-                                      P<int32_t>(page_table), P<int32_t>(cu_q),
-                                      P<int32_t>(kv_lens), P<bf16>(out), static_cast<int>(N),
-                                      static_cast<int>(num_seqs),
-                                      static_cast<int>(page_table.size(1)), static_cast<int>(Hq),
-                                      static_cast<int>(Hkv), static_cast<int>(D),
-                                      static_cast<int>(page), static_cast<float>(scale), cur());
+  const int max_pages = static_cast<int>(page_table.size(1));
+  int pps = 0, splits = 0;
+  cfb::paged_attention_split(static_cast<int>(N), static_cast<int>(Hkv),
+                             max_pages * static_cast<int>(page),
+                             at::cuda::getCurrentDeviceProperties()->multiProcessorCount, &pps,
+                             &splits);
+  torch::Tensor ws_o, ws_lse;
+  if (splits > 1) {
+    const auto f32 = q.options().dtype(torch::kFloat32);
+    ws_o = torch::empty({N * Hq * splits * D}, f32);
+    ws_lse = torch::empty({N * Hq * splits}, f32);
+  }
+  const int rc = cfb::paged_attention(
+      P<bf16>(q), P<bf16>(k_pool), P<bf16>(v_pool), P<int32_t>(page_table), P<int32_t>(cu_q),
+      P<int32_t>(kv_lens), P<bf16>(out), splits > 1 ? ws_o.data_ptr<float>() : nullptr,
+      splits > 1 ? ws_lse.data_ptr<float>() : nullptr, static_cast<int>(N),
+      static_cast<int>(num_seqs), max_pages, static_cast<int>(Hq), static_cast<int>(Hkv),
+      static_cast<int>(D), static_cast<int>(page), pps, splits, static_cast<float>(scale), cur());
   TORCH_CHECK(rc == 0, "paged_attention failed with code ", rc);
+}
+
+void paged_qkv_rope(const torch::Tensor& kqv, const c10::optional<torch::Tensor>& qw,
+                    const c10::optional<torch::Tensor>& kw, const torch::Tensor& cos_t,
+                    const torch::Tensor& sin_t, const torch::Tensor& pos,
+                    const torch::Tensor& slots, torch::Tensor& q_out, torch::Tensor& k_layer,
+                    torch::Tensor& v_layer, double eps) {
+  chk(kqv, torch::kBFloat16, "kqv");
+  chk(q_out, torch::kBFloat16, "q_out");
+  chk(k_layer, torch::kBFloat16, "k_layer");
+  chk(v_layer, torch::kBFloat16, "v_layer");
+  chk(cos_t, torch::kFloat32, "cos");
+  chk(sin_t, torch::kFloat32, "sin");
+  chk(pos, torch::kLong, "positions");
+  chk(slots, torch::kLong, "slots");
+  TORCH_CHECK(q_out.dim() == 3 && k_layer.dim() == 4 && v_layer.sizes() == k_layer.sizes(),
+              "q_out [N,Hq,D], pools [pages,page,Hkv,D]");
+  const int64_t N = q_out.size(0), Hq = q_out.size(1), D = q_out.size(2);
+  const int64_t Hkv = k_layer.size(2);
+  TORCH_CHECK(k_layer.size(3) == D && (D == 64 || D == 128), "head dim 64 or 128");
+  TORCH_CHECK(kqv.dim() == 2 && kqv.size(0) == N && kqv.size(1) == (Hq + 2 * Hkv) * D,
+              "kqv [N, (2 Hkv + Hq) D]");
+  TORCH_CHECK(pos.numel() == N && slots.numel() == N, "one position and slot per token");
+  TORCH_CHECK(cos_t.dim() == 2 && cos_t.size(1) == D / 2 && sin_t.sizes() == cos_t.sizes(),
+              "cos/sin tables [P, D/2]");
+  const bool norm = qw.has_value();
+  TORCH_CHECK(norm == kw.has_value(), "q and k norm weights go together");
+  if (norm) {
+    chk(*qw, torch::kBFloat16, "q_norm weight");
+    chk(*kw, torch::kBFloat16, "k_norm weight");
+    TORCH_CHECK(qw->numel() == D && kw->numel() == D, "norm weights [D]");
+  }
+  const c10::cuda::CUDAGuard g(kqv.device());
+  const int rc = cfb::paged_qkv_rope(
+      P<bf16>(kqv), norm ? P<bf16>(*qw) : nullptr, norm ? P<bf16>(*kw) : nullptr,
+      P<float>(cos_t), P<float>(sin_t), P<int64_t>(pos), P<int64_t>(slots), P<bf16>(q_out),
+      P<bf16>(k_layer), P<bf16>(v_layer), static_cast<int>(N), static_cast<int>(Hq),
+      static_cast<int>(Hkv), static_cast<int>(D), static_cast<float>(eps), norm, cur());
+  TORCH_CHECK(rc == 0, "paged_qkv_rope failed with code ", rc);
 }
 
 // geom: 10 ints per job (rows, cols, s_div, s_hi, s_lo, s_cs, d_div, d_hi, d_lo,
@@ -394,4 +444,5 @@ void register_elementwise(pybind11::module& m) {
   m.def("sumsq_bf16", &sumsq_bf16);
   m.def("clip_coef", &clip_coef);
   m.def("paged_attention", &paged_attention);
+  m.def("paged_qkv_rope", &paged_qkv_rope);
 }

@@ -65,11 +65,25 @@ void clip_coef(const float* sumsq, float max_norm, float* clip, float* norm, cud
 
 // Causal attention of ragged new-token queries q [N,Hq,D] over paged K/V pools
 // [pages, page_size, Hkv, D]; page_table [num_seqs, max_pages], cu_q [num_seqs+1],
-// kv_lens [num_seqs] (int32).  Writes out [N,Hq,D].
+// kv_lens [num_seqs] (int32).  Writes out [N,Hq,D].  The KV range is split
+// into `splits` ranges of `pages_per_split` pages (splits * pages_per_split >=
+// max_pages); with splits > 1, ws_o [N*Hq*splits*D] and ws_lse [N*Hq*splits]
+// (fp32) hold the partials.
 int paged_attention(const bf16* q, const bf16* k_pool, const bf16* v_pool,
                     const int32_t* page_table, const int32_t* cu_q, const int32_t* kv_lens,
-                    bf16* out, int N, int num_seqs, int max_pages, int Hq, int Hkv, int D,
-                    int page_size, float scale, cudaStream_t s);
+                    bf16* out, float* ws_o, float* ws_lse, int N, int num_seqs, int max_pages,
+                    int Hq, int Hkv, int D, int page_size, int pages_per_split, int splits,
+                    float scale, cudaStream_t s);
+// RMSNorm (optional) + RoPE of the new tokens' q/k heads from kqv [N, (Hkv+Hq+Hkv)*D];
+// q -> q_out [N,Hq,D], k and v -> their slots of one layer's pools [*, Hkv, D].
+int paged_qkv_rope(const bf16* kqv, const bf16* qw, const bf16* kw, const float* cos_t,
+                   const float* sin_t, const int64_t* pos, const int64_t* slots, bf16* q_out,
+                   bf16* k_layer, bf16* v_layer, int N, int Hq, int Hkv, int D, float eps,
+                   bool qk_norm, cudaStream_t s);
+// KV split of paged_attention for N query tokens, Hkv heads and page tables
+// `max_pages` wide (about eight CTAs per SM).
+void paged_attention_split(int N, int Hkv, int max_kv, int num_sms, int* pages_per_split,
+                           int* splits);
 
 // Batched strided 2-D copies (pack.cu): dst(r, c) = src(r, c) for r < rows,
 // c < cols, where a side's element offset is (r / div) * hi + (r % div) * lo

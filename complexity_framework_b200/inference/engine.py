@@ -70,6 +70,10 @@ class InferenceConfig:
     prefill_chunk_size: int = 2048
     dtype: Optional[torch.dtype] = None
     device: Optional[torch.device] = None
+    # decode-only steps of greedy requests replay a captured CUDA graph per
+    # padded batch size (CUDA only)
+    cuda_graph_decode: bool = True
+    decode_graph_buckets: Sequence[int] = (1, 2, 4, 8, 16, 32, 64, 128, 256)
 
 
 @dataclass
@@ -84,6 +88,13 @@ class _Req:
     first_token_time: Optional[float] = None
     finish_time: Optional[float] = None
     generator: Optional[torch.Generator] = None
+
+
+def plain_greedy(gen: GenerationConfig) -> bool:
+    """Greedy decoding with no history-dependent logit processing: the next
+    token is the argmax, so a whole batch is selected on the device at once."""
+    return (not gen.sampling or gen.temperature <= 0) and gen.repetition_penalty == 1.0 \
+        and gen.no_repeat_ngram_size == 0
 
 
 def sample_next(logits: torch.Tensor, gen: GenerationConfig, history: Sequence[int],
@@ -144,6 +155,7 @@ class InferenceEngine:
         self.pool = PagePool(mc.num_hidden_layers, mc.num_key_value_heads, mc.head_dim, pages,
                              self.config.page_size, dtype=self.dtype, device=self.device)
         self._ids = itertools.count()
+        self._graphs: Dict[int, tuple] = {}
         self.requests: Dict[int, _Req] = {}
         self.waiting: List[int] = []
         self.running: List[int] = []
@@ -186,9 +198,88 @@ class InferenceEngine:
         return len(r.prompt) + len(r.output) >= self.config.max_cache_length
 
     # ---------------------------------------------------------------- step
+    # --------------------------------------------------- graph-replayed decode
+    def _graph_eligible(self) -> bool:
+        return (self.config.cuda_graph_decode and self.device.type == "cuda" and bool(self.running)
+                and not self.waiting and all(plain_greedy(self.requests[r].gen)
+                                             for r in self.running)
+                and len(self.running) <= max(self.config.decode_graph_buckets))
+
+    def _decode_graph(self, size: int):
+        """(static batch, graph, next-token buffer) for a padded decode batch."""
+        from .paged import StaticDecodeBatch
+
+        got = self._graphs.get(size)
+        if got is not None:
+            return got
+        cfg = self.config
+        max_pages = -(-cfg.max_cache_length // cfg.page_size)
+        sb = StaticDecodeBatch(self.pool, size, max_pages, cfg.max_cache_length - 1)
+        sb.fill([])
+
+        def body():
+            sb.expand()
+            hidden = forward_paged(self.model, sb.ids, sb)
+            return self.model.logits(hidden[None])[0].argmax(-1)
+
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):  # lazy initialisation outside the capture
+            body()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            out = body()
+        got = (sb, g, out)
+        self._graphs[size] = got
+        return got
+
+    def warmup_decode_graphs(self, max_batch: Optional[int] = None) -> List[int]:
+        """Capture the decode graph of every bucket up to ``max_batch`` (default:
+        ``max_batch_size``) now, so no capture lands inside serving."""
+        if not (self.config.cuda_graph_decode and self.device.type == "cuda"):
+            return []
+        limit = max_batch or self.config.max_batch_size
+        sizes = [b for b in self.config.decode_graph_buckets if b <= limit]
+        bigger = [b for b in self.config.decode_graph_buckets if b > limit]
+        if bigger and (not sizes or sizes[-1] < limit):
+            sizes.append(bigger[0])
+        with torch.no_grad():
+            for b in sizes:
+                self._decode_graph(b)
+        return sizes
+
+    def _graph_decode_step(self) -> List[int]:
+        rids = list(self.running)
+        size = min(b for b in self.config.decode_graph_buckets if b >= len(rids))
+        sb, graph, out = self._decode_graph(size)
+        entries = []
+        for rid in rids:
+            r = self.requests[rid]
+            entries.append((rid, r.output[-1], len(r.prompt) + len(r.output) - 1))
+        sb.fill(entries)
+        graph.replay()
+        toks = out[:len(rids)].tolist()   # the step's only device-to-host read
+        sb.commit()
+        finished = []
+        for rid, tok in zip(rids, toks):
+            r = self.requests[rid]
+            r.output.append(int(tok))
+            if self._stop(r, int(tok)):
+                self._finish(r)
+                self.running.remove(rid)
+                finished.append(rid)
+        self.stats["steps"] += 1
+        self.stats["tokens_decoded"] += len(rids)
+        self.stats["graph_steps"] = self.stats.get("graph_steps", 0) + 1
+        return finished
+
     @torch.no_grad()
     def step(self) -> List[int]:
         """Run one batched forward; returns ids of requests that finished."""
+        if self._graph_eligible():
+            return self._graph_decode_step()
         budget = self.config.max_tokens_per_step
         chunks: List[SeqChunk] = []
         toks: List[int] = []
@@ -226,11 +317,16 @@ class InferenceEngine:
         last = torch.tensor([c - 1 for c in batch._cu_host[1:]], device=self.device)
         logits = self.model.logits(hidden[last][None])[0]
         finished = []
+        # greedy rows: one argmax over the batch and a single device-to-host read
+        greedy = None
+        if all(plain_greedy(r.gen) for r in owners):
+            greedy = logits.argmax(-1).tolist()
         now = time.perf_counter()
         for i, (c, r) in enumerate(zip(chunks, owners)):
             if c.start + c.length < len(r.prompt):
                 continue  # mid-prompt chunk: no token yet
-            tok = sample_next(logits[i], r.gen, r.prompt + r.output, r.generator)
+            tok = (greedy[i] if greedy is not None
+                   else sample_next(logits[i], r.gen, r.prompt + r.output, r.generator))
             r.output.append(tok)
             if r.first_token_time is None:
                 r.first_token_time = now

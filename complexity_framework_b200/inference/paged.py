@@ -245,6 +245,120 @@ class PagedBatch:
         return out
 
 
+class StaticDecodeBatch(PagedBatch):
+    """A decode-only batch of ``size`` sequences (one new token each) whose
+    device tensors never move, so a forward over it can be captured in a CUDA
+    graph once and replayed every step.
+
+    All per-step inputs (token ids, positions, cache slots, kv lengths, page
+    table rows) live in ONE int32 device buffer, refilled from a pinned host
+    buffer by a single copy.  A row keeps its sequence while that sequence runs,
+    so the host only appends a page id when a sequence crosses a page boundary.
+    Rows past the live requests are padding: they attend over one scratch page
+    reserved at construction and write their K/V there.
+    """
+
+    SCRATCH_SEQ = -1
+
+    def __init__(self, pool: PagePool, size: int, max_pages: int, max_position: int):
+        self.pool = pool
+        self.size, self.max_pages = size, max_pages
+        dev = pool.device
+        if self.SCRATCH_SEQ not in pool.pages:
+            pool.allocate_sequence(self.SCRATCH_SEQ)
+            pool.reserve(self.SCRATCH_SEQ, 1)
+        self.scratch_page = pool.pages[self.SCRATCH_SEQ][0]
+        B = size
+        # layout: ids | positions | slots | kv_lens | page table [size, max_pages]
+        n = B * (4 + max_pages)
+        self.host = torch.zeros(n, dtype=torch.int32).pin_memory()
+        self._h = self.host.numpy()
+        self.dev = torch.zeros(n, dtype=torch.int32, device=dev)
+        self.ids32 = self.dev[0:B]
+        self._pos32 = self.dev[B:2 * B]
+        self._slots32 = self.dev[2 * B:3 * B]
+        self.paged_kv_lens = self.dev[3 * B:4 * B]
+        self.paged_table = self.dev[4 * B:].view(B, max_pages)
+        self.page_table, self.kv_lens = self.paged_table, self.paged_kv_lens
+        self.max_position = max_position
+        self.num_tokens = B
+        self.chunks = [SeqChunk(-1, 0, 1) for _ in range(B)]
+        self.fresh, self.paged = [], list(range(B))
+        self._cu_host = list(range(B + 1))
+        self.paged_tokens = torch.arange(B, dtype=torch.long, device=dev)
+        self.paged_cu = torch.arange(B + 1, dtype=torch.int32, device=dev)
+        self.cu_q = self.paged_cu
+        # long index tensors the model reads (filled from the int32 buffer by
+        # ``expand``, a device op that a captured graph replays)
+        self.positions = torch.zeros(B, dtype=torch.long, device=dev)
+        self.slots = torch.zeros(B, dtype=torch.long, device=dev)
+        self.ids = torch.zeros(B, dtype=torch.long, device=dev)
+        self._row_seq = [None] * B   # sequence of each row
+        self._row_pages = [0] * B    # pages of that sequence already in the table row
+        self._live = []
+        for i in range(B):
+            self._set_padding(i)
+
+    def _set_padding(self, i: int) -> None:
+        B, mp, h = self.size, self.max_pages, self._h
+        P = self.pool
+        h[4 * B + i * mp:4 * B + (i + 1) * mp] = 0
+        h[4 * B + i * mp] = self.scratch_page
+        h[i] = 0
+        h[B + i] = 0
+        h[2 * B + i] = self.scratch_page * P.page_size
+        h[3 * B + i] = 1
+        self._row_seq[i] = None
+        self._row_pages[i] = 0
+
+    def expand(self) -> None:
+        self.positions.copy_(self._pos32)
+        self.slots.copy_(self._slots32)
+        self.ids.copy_(self.ids32)
+
+    def fill(self, entries) -> None:
+        """``entries[i] = (seq_id, token, position)`` for row i (at most ``size``
+        live rows, the rest padding): reserves the page each new token lands on
+        and stages every input with one host-to-device copy."""
+        P = self.pool
+        B, mp, h = self.size, self.max_pages, self._h
+        if len(entries) > B:
+            raise ValueError(f"{len(entries)} requests for a decode batch of {B}")
+        if self.SCRATCH_SEQ not in P.pages:  # the pool was reset: take a new scratch page
+            P.allocate_sequence(self.SCRATCH_SEQ)
+            P.reserve(self.SCRATCH_SEQ, 1)
+            self.scratch_page = P.pages[self.SCRATCH_SEQ][0]
+            for i in range(B):
+                self._set_padding(i)
+        for i in range(B):
+            if i >= len(entries):
+                if self._row_seq[i] is not None:
+                    self._set_padding(i)
+                continue
+            sid, tok, t = entries[i]
+            if self._row_seq[i] != sid:
+                h[4 * B + i * mp:4 * B + (i + 1) * mp] = 0
+                self._row_seq[i], self._row_pages[i] = sid, 0
+            P.reserve(sid, t + 1 - P.lengths[sid])
+            pages = P.pages[sid]
+            if len(pages) > mp:
+                raise ValueError(f"sequence {sid} needs {len(pages)} pages; the graph holds {mp}")
+            for j in range(self._row_pages[i], len(pages)):
+                h[4 * B + i * mp + j] = pages[j]
+            self._row_pages[i] = len(pages)
+            h[i], h[B + i], h[3 * B + i] = tok, t, t + 1
+            h[2 * B + i] = pages[t // P.page_size] * P.page_size + t % P.page_size
+        self.dev.copy_(self.host, non_blocking=True)
+        self._live = [(e[0], e[2]) for e in entries]
+
+    def commit(self) -> None:
+        for sid, t in self._live:
+            self.pool.lengths[sid] = max(self.pool.lengths[sid], t + 1)
+
+    def max_q_len(self) -> int:
+        return 1
+
+
 class KVCache:
     """Contiguous per-layer KV cache ``[L, B, Hkv, Smax, D]`` (API of the reference KVCache)."""
 

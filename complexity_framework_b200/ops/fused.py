@@ -31,6 +31,16 @@ def _few_tiles(M: int, N: int) -> bool:
     return ((M + 255) // 256) * ((N + 255) // 256) < 2 * _PAIR_UNITS
 
 
+_SKINNY = os.environ.get("CFB_SKINNY_GEMM", "1") != "0"
+
+
+def _skinny(M: int, N: int, K: int) -> bool:
+    """Decode-shaped ``x @ W^T``: at most 128 rows and too few output tiles to
+    occupy the GPU (under half a wave of 256-wide tiles), with enough K to
+    split."""
+    return _SKINNY and M <= 128 and (N + 255) // 256 < _PAIR_UNITS and K >= 512 and N % 8 == 0
+
+
 def _c(t: torch.Tensor) -> torch.Tensor:
     return t if t.is_contiguous() else t.contiguous()
 
@@ -44,6 +54,23 @@ def gemm_nt(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] =
     N = w.shape[0]
     if out is None:
         out = torch.empty(M, N, device=x.device, dtype=torch.bfloat16)
+    if _skinny(M, N, K):
+        # few rows (decoding): the weight is the long operand.  C^T = W x^T puts
+        # N on the 128/256-row tile side and splits K over CTAs with fp32
+        # atomics, so enough CTAs stream the weight to saturate HBM; one fused
+        # elementwise pass then transposes, scales, adds the residual and casts.
+        Mp = (M + 31) // 32 * 32  # the GEMM's N side is a multiple of 32
+        xp = x if Mp == M else torch.nn.functional.pad(x, (0, 0, 0, Mp - M))
+        acc = torch.zeros(N, Mp, device=x.device, dtype=torch.float32)
+        C.gemm(w, False, xp, False, N, Mp, K, EPI_F32_ATOMIC, out=acc)
+        acc = acc[:, :M]
+        if residual is not None:
+            torch.add(residual, acc.t(), alpha=alpha, out=out)
+        elif alpha != 1.0:
+            torch.mul(acc.t(), alpha, out=out)
+        else:
+            out.copy_(acc.t())
+        return out
     if residual is not None:
         C.gemm(x, False, w, False, M, N, K, EPI_RESID, out=out, residual=_c(residual), alpha=alpha)
     else:

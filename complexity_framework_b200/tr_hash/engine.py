@@ -97,9 +97,42 @@ class TRHashEngine(nn.Module):
         self._active_expert_width = W
         self._active_route_table = self.route_table
         self._fused_shared_gate_up_weight: Optional[torch.Tensor] = None
+        # inference-only packed (gate|up, down) weights: (key, w_gu, w_down)
+        self._packed_cache: Optional[tuple] = None
 
     # ------------------------------------------------------------ housekeeping
+    def train(self, mode: bool = True):
+        self._packed_cache = None
+        return super().train(mode)
+
+    def invalidate_packed_cache(self) -> None:
+        """Drop the inference copy of the packed weights (call after updating
+        weights in place while in eval mode)."""
+        self._packed_cache = None
+
+    def _packed_for_inference(self):
+        """Packed (w_gu, w_down) reused across eval-mode, no-grad forwards.
+
+        Decoding runs a few tokens per forward, so re-packing the whole FFN
+        (the shared SwiGLU and every expert) each call would cost more than the
+        GEMMs.  The copy is keyed on each weight's storage and version counter
+        and dropped by ``train()``; CUDA graphs captured over it keep reading the
+        same tensors.
+        """
+        from ..ops import fused
+
+        sg, su, sd = self._shared_weights()
+        ws = (sg, su, self.expert_gate, self.expert_up, sd, self.expert_down)
+        key = tuple((w.data_ptr(), w._version) for w in ws if w is not None)
+        got = self._packed_cache
+        if got is None or got[0] != key:
+            with torch.no_grad():
+                w_gu, w_down = fused.pack_trhash_weights(*ws)
+            got = self._packed_cache = (key, w_gu, w_down)
+        return got[1], got[2]
+
     def _apply(self, fn, recurse: bool = True):
+        self._packed_cache = None
         aliased = self._active_route_table is self.route_table
         super()._apply(fn, recurse=recurse)
         self._active_route_table = self.route_table if aliased else fn(self._active_route_table)
@@ -279,6 +312,11 @@ class TRHashEngine(nn.Module):
         if (fused.packable(wg, self.expert_gate) and not any(
                 getattr(m, "is_lora_adapter", False)
                 for m in (self.shared_gate, self.shared_up, self.shared_down) if m is not None)):
+            if not (self.training or torch.is_grad_enabled()):
+                w_gu, w_down = self._packed_for_inference()
+                return fused.trhash_mlp(hidden, w_gu, w_down, scales, residual,
+                                        cfg.shared_width, cfg.expert_width, cfg.num_experts,
+                                        cfg.shared_output_scale)
             # packing and gradient unpacking fused into the MLP's own autograd node
             return fused.trhash_mlp_params(hidden, wg, wu, self.expert_gate, self.expert_up, wd,
                                            self.expert_down, scales, residual, cfg.shared_width,

@@ -188,3 +188,21 @@ def test_trhash_mlp_params_matches_packed():
         # same GEMMs; the packed path rounds the weight gradient to bf16 before
         # the autograd scatter, this one after the fp32 split-K sum
         assert float((a.float() - b.float()).abs().max()) <= 1e-2 * float(b.abs().max()) + 1e-6
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (5, 6144, 4096), (64, 4096, 15104),
+                                   (100, 896, 3328), (128, 4096, 4096)])
+@pytest.mark.parametrize("resid", [False, True])
+def test_skinny_gemm_nt(M, N, K, resid):
+    """Decode-shaped x @ W^T: swapped operands, split-K fp32 atomics, fused
+    transpose/residual/cast pass."""
+    from complexity_framework_b200.ops import fused
+
+    assert fused._skinny(M, N, K)
+    g = torch.Generator().manual_seed(M + N + K)
+    x = torch.randn(M, K, generator=g).cuda().bfloat16()
+    w = (torch.randn(N, K, generator=g) * K ** -0.5).cuda().bfloat16()
+    r = torch.randn(M, N, generator=g).cuda().bfloat16() if resid else None
+    out = fused.gemm_nt(x, w, r, alpha=0.5)
+    ref = 0.5 * (x.float() @ w.float().t()) + (r.float() if resid else 0)
+    _check(out, ref)

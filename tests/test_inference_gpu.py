@@ -31,6 +31,34 @@ def test_paged_attention_kernel_matches_reference():
     assert (out.float() - ref.float()).abs().max().item() < 2e-2
 
 
+@pytest.mark.parametrize("n_seqs,D,G", [(64, 128, 4), (3, 64, 8), (1, 128, 1)])
+def test_paged_decode_split_kv_matches_reference(n_seqs, D, G):
+    """Decode steps over long ragged sequences: the split-KV kernel (several
+    page ranges per sequence, combined afterwards) against the fp32 reference."""
+    from complexity_framework_b200.inference.paged import PagedBatch, PagePool, SeqChunk
+
+    torch.manual_seed(1)
+    Hkv = 8 if G < 8 else 2
+    Hq = Hkv * G
+    g = torch.Generator().manual_seed(2)
+    lens = torch.randint(1, 2300, (n_seqs,), generator=g).tolist()
+    pool = PagePool(1, Hkv, D, sum(-(-(n + 1) // 16) for n in lens) + 4, 16,
+                    dtype=torch.bfloat16, device="cuda")
+    for sid, n in enumerate(lens):
+        pool.allocate_sequence(sid)
+        b = PagedBatch(pool, [SeqChunk(sid, 0, n)])
+        b.write(0, torch.randn(n, Hkv, D, device="cuda"), torch.randn(n, Hkv, D, device="cuda"))
+        b.commit()
+    b = PagedBatch(pool, [SeqChunk(sid, n, 1) for sid, n in enumerate(lens)])
+    b.write(0, torch.randn(n_seqs, Hkv, D, device="cuda"), torch.randn(n_seqs, Hkv, D,
+                                                                      device="cuda"))
+    q = torch.randn(n_seqs, Hq, D, device="cuda").bfloat16()
+    out = b.attend(0, q, D ** -0.5)
+    ref = b._attend_reference(0, q, D ** -0.5)
+    assert torch.isfinite(out.float()).all()
+    assert (out.float() - ref.float()).abs().max().item() < 2e-2
+
+
 def test_engine_gpu_matches_fp32_greedy():
     from complexity_framework_b200 import ComplexityModel, ModelConfig
     from complexity_framework_b200.inference import GenerationConfig, InferenceEngine
@@ -51,3 +79,71 @@ def test_engine_gpu_matches_fp32_greedy():
         top2 = lg.topk(2).indices.tolist()
         assert o[0] in top2
         assert len(o) == 8
+
+
+def test_graph_decode_matches_eager_engine():
+    """Decode-only greedy steps replayed from captured CUDA graphs (padded batch
+    buckets, static page tables) produce exactly the eager engine's tokens."""
+    from complexity_framework_b200 import ComplexityModel, ModelConfig
+    from complexity_framework_b200.inference.engine import (GenerationConfig, InferenceConfig,
+                                                            InferenceEngine)
+
+    torch.manual_seed(0)
+    cfg = ModelConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=4,
+                      num_key_value_heads=2, vocab_size=2048, intermediate_size=256,
+                      shared_intermediate_size=512, num_experts=4, top_k=2,
+                      max_position_embeddings=512)
+    model = ComplexityModel(cfg).cuda().to(torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, 2048, (int(n),), generator=g).tolist()
+               for n in (5, 17, 40, 33, 64, 9)]
+    outs = {}
+    for graph in (False, True):
+        eng = InferenceEngine(model, InferenceConfig(max_cache_length=512, max_batch_size=8,
+                                                     cuda_graph_decode=graph))
+        rids = [eng.add_request(p, GenerationConfig(max_new_tokens=12 + 5 * i))
+                for i, p in enumerate(prompts)]
+        while eng.has_pending():
+            eng.step()
+        outs[graph] = [eng.requests[r].output for r in rids]
+        if graph:
+            assert eng.stats.get("graph_steps", 0) > 0
+    assert outs[True] == outs[False]
+
+
+@pytest.mark.parametrize("D,qk_norm", [(128, True), (64, False)])
+def test_paged_qkv_rope_kernel(D, qk_norm):
+    """qk-norm + RoPE + pool write of the new tokens against torch math."""
+    from complexity_framework_b200.core.layers import RotaryEmbedding
+    from complexity_framework_b200.ops import require
+
+    torch.manual_seed(0)
+    N, Hq, Hkv, pages, page = 7, 8, 2, 6, 16
+    kqv = torch.randn(N, (Hq + 2 * Hkv) * D, device="cuda").bfloat16()
+    qw = (1 + 0.1 * torch.randn(D, device="cuda")).bfloat16()
+    kw = (1 + 0.1 * torch.randn(D, device="cuda")).bfloat16()
+    rot = RotaryEmbedding(D).cuda()
+    cos, sin = rot.tables(200, "cuda")
+    pos = torch.tensor([0, 5, 17, 99, 150, 3, 199], device="cuda")
+    slots = torch.randperm(pages * page, device="cuda")[:N]
+    kp = torch.zeros(pages, page, Hkv, D, device="cuda", dtype=torch.bfloat16)
+    vp = torch.zeros_like(kp)
+    q = torch.empty(N, Hq, D, device="cuda", dtype=torch.bfloat16)
+    require().paged_qkv_rope(kqv, qw if qk_norm else None, kw if qk_norm else None, cos, sin,
+                             pos, slots, q, kp, vp, 1e-6)
+    x = kqv.float().view(N, Hq + 2 * Hkv, D)
+    k_, q_, v_ = x[:, :Hkv], x[:, Hkv:Hkv + Hq], x[:, Hkv + Hq:]
+
+    def prep(t, w):
+        if qk_norm:
+            t = t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+        c = torch.cat((cos[pos], cos[pos]), -1)[:, None]
+        s = torch.cat((sin[pos], sin[pos]), -1)[:, None]
+        t1, t2 = t[..., :D // 2], t[..., D // 2:]
+        return t * c + torch.cat((-t2, t1), -1) * s
+
+    assert (q.float() - prep(q_, qw)).abs().max() < 3e-2
+    kf = kp.view(-1, Hkv, D)[slots].float()
+    vf = vp.view(-1, Hkv, D)[slots].float()
+    assert (kf - prep(k_, kw)).abs().max() < 3e-2
+    assert torch.equal(vf, v_)
