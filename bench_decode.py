@@ -2,7 +2,7 @@
 
     python bench.py --workload decode [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload: 64 concurrent requests per GPU, prompt lengths uniform in [128, 2048]
+Workload: 64 concurrent requests, prompt lengths uniform in [128, 2048]
 with uniform random token ids (seeded), 256 greedy tokens each, KV page size
 16, bf16 weights with random init.  Architecture: 32 layers, hidden 4096, GQA
 32/8 (head_dim 128), vocab 32000, shared SwiGLU 11008, 8 routed experts of
@@ -12,8 +12,9 @@ A "step" is one complete serving run of the 64 requests (prefill and decode);
 a warm-up step runs the same prompts with 8 new tokens.  Reported:
 
 * ``value``: decode tokens/s over the decode phase (from the first step with
-  no prompt left to prefill to the end), timed with CUDA events, summed over
-  ranks (each rank serves its own 64 requests);
+  no prompt left to prefill to the end), timed with CUDA events, max over
+  ranks; with N GPUs the model is tensor parallel over all N (every rank runs
+  the same engine schedule on its shard), so the work is fixed ("strong");
 * ``ttft_p50_ms``: median time from submission to a request's first token;
 * ``e2e``: the same decode rate on the host clock, through the public engine
   API, with prompts handed over as host lists and every step's tokens read
@@ -37,10 +38,10 @@ import time
 import torch
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-METRIC = "decode tokens/s (sum over ranks) TR-GQA 7B paged-KV engine"
+METRIC = "decode tokens/s TR-GQA 7B paged-KV engine (tensor parallel over the GPUs)"
 N_REQ, NEW_TOKENS, PROMPT_MIN, PROMPT_MAX, PAGE = 64, 256, 128, 2048, 16
 ARCH = dict(hidden_size=4096, num_hidden_layers=32, num_attention_heads=32,
-            num_key_value_heads=8, intermediate_size=512, shared_intermediate_size=11008,
+            num_key_value_heads=8, intermediate_size=4096, shared_intermediate_size=11008,
             vocab_size=32000, num_experts=8, top_k=2, routing_strategy="modulo_cyclic",
             attention_type="gqa", mlp_type="tr_hash_engine", shared_expert=True,
             max_position_embeddings=4096, tie_word_embeddings=False)
@@ -54,7 +55,7 @@ def prompts(seed: int):
 
 # ------------------------------------------------------------------ our arm
 class OursDecode:
-    def __init__(self):
+    def __init__(self, world: int = 1):
         sys.path.insert(0, ROOT)
         from complexity_framework_b200 import ComplexityModel, ModelConfig
         from complexity_framework_b200.inference.engine import InferenceConfig, InferenceEngine
@@ -64,6 +65,14 @@ class OursDecode:
             model = ComplexityModel(ModelConfig(**ARCH))
         # route tables are built on the host; move them with everything else
         self.model = model.to("cuda").to(torch.bfloat16).eval()
+        self.tp = world
+        if world > 1:
+            import torch.distributed as dist
+
+            from complexity_framework_b200.parallel.tp_inference import enable_tp_decode
+
+            enable_tp_decode(self.model, dist.group.WORLD)
+            torch.cuda.empty_cache()
         self.cfg = InferenceConfig(max_cache_length=PROMPT_MAX + NEW_TOKENS, page_size=PAGE,
                                    max_batch_size=N_REQ, max_tokens_per_step=8192,
                                    prefill_chunk_size=2048)
@@ -71,6 +80,10 @@ class OursDecode:
         self.graph_sizes = self.engine.warmup_decode_graphs(N_REQ)
         self.mode = ("paged-KV engine, chunked prefill, decode steps replayed from CUDA graphs "
                      f"(buckets {self.graph_sizes})")
+        if world > 1:
+            comm = self.model.tp_decode
+            self.mode += (f"; tensor parallel x{world}: fused peer-memory all-reduce + residual "
+                          f"per attention and FFN ({'NVLS multimem' if comm.uses_multicast else 'unicast'})")
 
     def run(self, ps, new_tokens):
         from complexity_framework_b200.inference.engine import GenerationConfig
@@ -126,7 +139,7 @@ class OursDecode:
 
 # ------------------------------------------------------------ reference arm
 class ReferenceDecode:
-    def __init__(self):
+    def __init__(self, world: int = 1):
         ref_root = os.path.join(ROOT, "baseline", "_ref")
         if not os.path.isdir(os.path.join(ref_root, "complexity")):
             raise RuntimeError("reference not installed under baseline/_ref")
@@ -140,6 +153,16 @@ class ReferenceDecode:
         self.model = model.to("cuda").to(torch.bfloat16).eval()
         self.mode = ("reference model KV-cache API: left-padded batch, one prefill, "
                      "one batched forward per token")
+        if world > 1:
+            from complexity.parallel.tensor_parallel import (init_tensor_parallel_group,
+                                                             make_parallel)
+
+            init_tensor_parallel_group(world)
+            make_parallel(self.model, world)
+            # its parallel layers are created on the host: move them over
+            self.model = self.model.to("cuda").to(torch.bfloat16)
+            torch.cuda.empty_cache()
+            self.mode += f"; reference make_parallel tensor parallel x{world} (attention sharded)"
 
     @torch.no_grad()
     def run(self, ps, new_tokens):
@@ -181,7 +204,7 @@ def main(args, world, rank, local, helpers):
     import torch.distributed as dist
 
     try:
-        arm = OursDecode() if args.impl == "ours" else ReferenceDecode()
+        arm = OursDecode(world) if args.impl == "ours" else ReferenceDecode(world)
     except Exception as exc:
         if args.impl == "reference":
             if rank == 0:
@@ -189,7 +212,7 @@ def main(args, world, rank, local, helpers):
                                   f"{str(exc).splitlines()[0] if str(exc) else ''}"}))
             return
         raise
-    ps = prompts(4321 + rank)
+    ps = prompts(4321)  # tensor parallel: every rank serves the same requests
     for _ in range(args.warmup):
         arm.run(ps, 8)
     helpers.barrier(world)
@@ -207,8 +230,8 @@ def main(args, world, rank, local, helpers):
     dec_wall = helpers.max_over_ranks(sum(r["decode_wall_ms"] for r in runs), world)
     tot_wall = helpers.max_over_ranks(sum(r["total_wall_ms"] for r in runs), world)
     ttft = helpers.max_over_ranks(statistics.median(r["ttft_p50_ms"] for r in runs), world)
-    dec_tokens = sum(r["decode_tokens"] for r in runs) * world
-    tot_tokens = sum(r["total_tokens"] for r in runs) * world
+    dec_tokens = sum(r["decode_tokens"] for r in runs)
+    tot_tokens = sum(r["total_tokens"] for r in runs)
     value = dec_tokens / (dec_ms / 1000.0)
     launches = None
     if args.impl == "ours" and not args.no_count:
@@ -218,14 +241,14 @@ def main(args, world, rank, local, helpers):
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": dec_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": dec_ms / args.steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: uniform random prompt ids, lengths U[128,2048], random-init weights",
             "config": {"model": "TR-GQA 7B (32L, H4096, GQA 32/8, shared 11008, 8 experts W512 "
                                 "top-2 modulo_cyclic, V32000)",
-                       "requests_per_gpu": N_REQ, "new_tokens": NEW_TOKENS,
+                       "requests": N_REQ, "new_tokens": NEW_TOKENS,
                        "prompt_len": [PROMPT_MIN, PROMPT_MAX], "page_size": PAGE,
-                       "parallelism": f"dp{world} (one engine per GPU)", "mode": arm.mode,
+                       "parallelism": f"tp{world}", "mode": arm.mode,
                        "l2": "15 GB of weights read per decode step (no flush needed)"},
             "ttft_p50_ms": ttft,
             "output_tokens_per_s_incl_prefill": tot_tokens / (tot_wall / 1000.0),

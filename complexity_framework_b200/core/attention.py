@@ -136,6 +136,24 @@ class GroupedQueryAttention(nn.Module):
         self._kqv_cache = None
         return super().train(mode)
 
+    def _tp_out(self, o2: torch.Tensor, residual, N: int, fused_ok: bool) -> torch.Tensor:
+        """Tensor parallel: residual + all-reduce of this rank's o_proj partial."""
+        from ..parallel.tp_inference import tp_reduce_add
+
+        w = self.o_proj.weight
+
+        def partial(out):
+            if fused_ok:
+                from ..ops import fused
+
+                return fused.gemm_nt(o2, w, None, out=out)
+            y = F.linear(o2, w)
+            return y if out is None else out.copy_(y)
+
+        y = tp_reduce_add(getattr(self, "tp_decode", None), getattr(self, "tp_site", 0),
+                          partial, N, residual, self.tp_group)
+        return y.view(1, N, -1)
+
     def _project(self, x: torch.Tensor):
         kd = self.num_kv_heads * self.head_dim
         qd = self.num_heads * self.head_dim
@@ -325,6 +343,8 @@ class GroupedQueryAttention(nn.Module):
                                      cache.pool.v[layer_idx],
                                      float(self.q_norm.eps) if norm else 0.0)
             o = cache.attend(layer_idx, q, self.attn_scale)
+            if getattr(self, "tp_group", None) is not None:
+                return self._tp_out(o.reshape(N, qd), residual, N, True)
             return fused.linear(o.reshape(1, N, qd), self.o_proj.weight, residual)
         k, q, v = kqv.view(N, -1).split((kd, qd, kd), -1)
         q = q.reshape(N, self.num_heads, self.head_dim)
@@ -342,6 +362,8 @@ class GroupedQueryAttention(nn.Module):
         q, k = self.rotary_emb.rotate(q, k, c, s)
         cache.write(layer_idx, k, v)
         o = cache.attend(layer_idx, q, self.attn_scale)  # [N, Hq, D]
+        if getattr(self, "tp_group", None) is not None:
+            return self._tp_out(o.reshape(N, qd), residual, N, fused_ok)
         o = o.reshape(1, N, qd)
         if fused_ok:
             from ..ops import fused

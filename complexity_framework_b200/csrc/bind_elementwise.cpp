@@ -371,6 +371,24 @@ void paged_qkv_rope(const torch::Tensor& kqv, const c10::optional<torch::Tensor>
   TORCH_CHECK(rc == 0, "paged_qkv_rope failed with code ", rc);
 }
 
+void skinny_finish(const torch::Tensor& acc, const c10::optional<torch::Tensor>& resid,
+                   torch::Tensor& out, double alpha) {
+  TORCH_CHECK(acc.is_cuda() && acc.scalar_type() == torch::kFloat32 && acc.dim() == 2 &&
+                  acc.stride(1) == 1, "acc: fp32 [N, >=M] row-major");
+  chk(out, torch::kBFloat16, "out");
+  TORCH_CHECK(out.dim() == 2, "out [M, N]");
+  const int64_t M = out.size(0), N = out.size(1);
+  TORCH_CHECK(acc.size(0) == N && acc.size(1) >= M, "acc [N, >=M]");
+  if (resid.has_value()) {
+    chk(*resid, torch::kBFloat16, "residual");
+    TORCH_CHECK(resid->numel() == M * N, "residual [M, N]");
+  }
+  const c10::cuda::CUDAGuard g(out.device());
+  cfb::skinny_finish(P<float>(acc), static_cast<int>(acc.stride(0)),
+                     resid.has_value() ? P<bf16>(*resid) : nullptr, P<bf16>(out),
+                     static_cast<int>(M), static_cast<int>(N), static_cast<float>(alpha), cur());
+}
+
 // geom: 10 ints per job (rows, cols, s_div, s_hi, s_lo, s_cs, d_div, d_hi, d_lo,
 // d_cs), element offsets relative to each tensor's data pointer.  Every job's
 // largest source and destination offsets are checked against the tensors.
@@ -445,4 +463,5 @@ void register_elementwise(pybind11::module& m) {
   m.def("clip_coef", &clip_coef);
   m.def("paged_attention", &paged_attention);
   m.def("paged_qkv_rope", &paged_qkv_rope);
+  m.def("skinny_finish", &skinny_finish);
 }

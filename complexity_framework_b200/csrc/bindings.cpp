@@ -12,6 +12,7 @@
 
 #include "dist_fused.h"
 #include "tp_fused.h"
+#include "tp_decode.h"
 #include "ep_fused.h"
 #include "flash.h"
 #include "gemm_tc.h"
@@ -315,6 +316,39 @@ void tp_barrier(const std::vector<int64_t>& pads, int64_t rank, int64_t round, i
                                  at::cuda::getCurrentCUDAStream(),
                                  err_ptr(static_cast<int>(device)));
   raise_rc(rc, "tp_barrier");
+}
+
+// out = residual + sum over ranks of their partial buffers (decode tensor parallelism).
+void tp_allreduce(const std::vector<int64_t>& bufs, const std::vector<int64_t>& pads,
+                  int64_t mc, int64_t rank, const c10::optional<torch::Tensor>& residual,
+                  torch::Tensor& out, torch::Tensor& epoch, torch::Tensor& ticket) {
+  check_bf16_cuda(out, "out");
+  TORCH_CHECK(out.is_contiguous(), "out must be contiguous");
+  TORCH_CHECK(!bufs.empty() && bufs.size() <= cfb::kTpMaxRanks && pads.size() == bufs.size(),
+              "1..8 ranks with one pad each");
+  TORCH_CHECK(epoch.is_cuda() && epoch.scalar_type() == torch::kInt32 && ticket.is_cuda() &&
+                  ticket.scalar_type() == torch::kInt32, "epoch / ticket: int32 CUDA");
+  cfb::TpArPtrs pp{};
+  pp.world = static_cast<int>(bufs.size());
+  pp.rank = static_cast<int>(rank);
+  for (size_t i = 0; i < bufs.size(); ++i) {
+    pp.buf[i] = reinterpret_cast<const __nv_bfloat16*>(bufs[i]);
+    pp.pad[i] = reinterpret_cast<int*>(pads[i]);
+  }
+  pp.mc = reinterpret_cast<const __nv_bfloat16*>(mc);
+  const __nv_bfloat16* r = nullptr;
+  if (residual.has_value()) {
+    check_bf16_cuda(*residual, "residual");
+    TORCH_CHECK(residual->is_contiguous() && residual->numel() == out.numel(),
+                "residual must be contiguous like out");
+    r = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+  }
+  const int dev = out.get_device();
+  const c10::cuda::CUDAGuard guard(out.device());
+  const int rc = cfb::tp_allreduce(pp, r, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                                   out.numel(), epoch.data_ptr<int>(), ticket.data_ptr<int>(),
+                                   num_sms(dev), at::cuda::getCurrentCUDAStream(), err_ptr(dev));
+  raise_rc(rc, "tp_allreduce");
 }
 
 // out[i] = residual[i] + sum_j w[i,j] * rows of peers' buffers (EP dispatch / combine).
@@ -639,6 +673,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_dist", &gemm_dist);
   m.def("tp_rs_finish", &tp_rs_finish);
   m.def("tp_barrier", &tp_barrier);
+  m.def("tp_allreduce", &tp_allreduce);
   m.def("ep_gather_combine", &ep_gather_combine);
   m.def("gemm", &gemm, "tcgen05 GEMM with fused epilogues", py::arg("A"), py::arg("a_mn"),
         py::arg("B"), py::arg("b_mn"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epi"),

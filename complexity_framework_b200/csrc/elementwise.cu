@@ -87,6 +87,75 @@ __global__ void rmsnorm_fwd_k(const bf16* __restrict__ x, const bf16* __restrict
   }
 }
 
+// Wide rows, few of them (decoding: 64 rows of 4096): one 256-thread CTA per
+// row, the row held in registers (NC chunks of 8 per thread), block reduction.
+template <int NC>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_row_k(const bf16* __restrict__ x,
+                                                          const bf16* __restrict__ w,
+                                                          bf16* __restrict__ y,
+                                                          float* __restrict__ rstd, int H,
+                                                          float eps) {
+  __shared__ float red[8];
+  const int64_t row = blockIdx.x;
+  const bf16* xr = x + row * H;
+  const int nv = H >> 3;
+  float v[NC][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int i = threadIdx.x + c * 256;
+    if (i < nv) {
+      load8(xr + i * 8, v[c]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[c][j] * v[c][j];
+    }
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) tot += red[k];
+  const float r = rsqrtf(tot / H + eps);
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int i = threadIdx.x + c * 256;
+    if (i < nv) {
+      float wv[8];
+      load8(w + i * 8, wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[c][j] = rb(v[c][j] * r) * wv[j];
+      store8(y + row * H + i * 8, v[c]);
+    }
+  }
+  if (threadIdx.x == 0) rstd[row] = r;
+}
+
+// out[m, n] = bf16(alpha * acc[n, m] (+ resid[m, n])): the transposed fp32
+// result of a swapped-operand split-K GEMM, one 32 x 32 tile per block.
+__global__ void __launch_bounds__(256) skinny_finish_k(const float* __restrict__ acc, int ldacc,
+                                                        const bf16* __restrict__ resid,
+                                                        bf16* __restrict__ out, int M, int N,
+                                                        float alpha) {
+  __shared__ float tile[32][33];
+  const int n0 = blockIdx.x * 32, m0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int k = ty; k < 32; k += 8) {
+    const int n = n0 + k, m = m0 + tx;
+    tile[k][tx] = (n < N && m < M) ? acc[static_cast<int64_t>(n) * ldacc + m] : 0.f;
+  }
+  __syncthreads();
+  for (int k = ty; k < 32; k += 8) {
+    const int m = m0 + k, n = n0 + tx;
+    if (m < M && n < N) {
+      const int64_t o = static_cast<int64_t>(m) * N + n;
+      float v = alpha * tile[tx][k];
+      if (resid != nullptr) v += __bfloat162float(resid[o]);
+      out[o] = __float2bfloat16(v);
+    }
+  }
+}
+
 __global__ void rmsnorm_bwd_k(const bf16* __restrict__ dy, const bf16* __restrict__ x,
                               const bf16* __restrict__ w, const float* __restrict__ rstd,
                               const bf16* __restrict__ dres, bf16* __restrict__ dx,
@@ -1079,7 +1148,20 @@ void rmsnorm_fwd(const bf16* x, const bf16* w, bf16* y, float* rstd, int64_t T, 
     kern<<<ring_grid(kern, smem, T), 128, smem, s>>>(x, w, y, rstd, static_cast<int>(T), H, eps);
     return;
   }
+  if (T <= 8192 && nv <= 4 * 256 && T < (int64_t(1) << 31)) {
+    const int nc = (nv + 255) / 256;
+    if (nc == 1) rmsnorm_fwd_row_k<1><<<T, 256, 0, s>>>(x, w, y, rstd, H, eps);
+    else if (nc == 2) rmsnorm_fwd_row_k<2><<<T, 256, 0, s>>>(x, w, y, rstd, H, eps);
+    else rmsnorm_fwd_row_k<4><<<T, 256, 0, s>>>(x, w, y, rstd, H, eps);
+    return;
+  }
   rmsnorm_fwd_k<<<grid_for(T, 8), 256, 0, s>>>(x, w, y, rstd, T, H, eps);
+}
+
+void skinny_finish(const float* acc, int ldacc, const bf16* resid, bf16* out, int M, int N,
+                   float alpha, cudaStream_t s) {
+  skinny_finish_k<<<dim3((N + 31) / 32, (M + 31) / 32), 256, 0, s>>>(acc, ldacc, resid, out, M,
+                                                                     N, alpha);
 }
 
 void rmsnorm_bwd(const bf16* dy, const bf16* x, const bf16* w, const float* rstd,

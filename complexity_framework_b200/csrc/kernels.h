@@ -9,6 +9,9 @@ namespace cfb {
 using bf16 = __nv_bfloat16;
 
 // RMSNorm over the last dim H (H % 8 == 0).  y = bf16(bf16(x*rstd) * w).
+// out[m, n] = bf16(alpha * acc[n, m] (+ resid[m, n])) for m < M, n < N (acc row stride ldacc).
+void skinny_finish(const float* acc, int ldacc, const bf16* resid, bf16* out, int M, int N,
+                   float alpha, cudaStream_t s);
 void rmsnorm_fwd(const bf16* x, const bf16* w, bf16* y, float* rstd, int64_t T, int H, float eps,
                  cudaStream_t s);
 // dx = rmsnorm'(x)^T dy (+ dres);  dw (fp32, [H]) += sum_rows dy * x*rstd.

@@ -53,20 +53,51 @@ __device__ __forceinline__ void cp_async_wait() {
 
 template <int D>
 struct PagedSmem {
-  static constexpr int K_ROW = D * 2 + 16;             // bytes, padded
-  static constexpr int K_BYTES = kPage * K_ROW;
-  static constexpr int V_BYTES = kPage * D * 2;
-  static constexpr int STAGE = K_BYTES + V_BYTES;
+  static constexpr int ROW = D * 2 + 16;               // bytes per K or V row, padded
+  static constexpr int K_BYTES = kPage * ROW;
+  static constexpr int STAGE = 2 * K_BYTES;            // K page then V page
   static constexpr int WARP = 2 * STAGE;
   static constexpr int RING = kWarps * WARP;
 };
 
 template <int D, int G>
 constexpr int paged_smem_bytes() {
-  // ring (reused for the warp merge) + fp32 queries + (m, l) per warp and head
-  return PagedSmem<D>::RING + G * D * 4 + 2 * kWarps * G * 4;
+  // ring (reused for the warp merge: kWarps x G x D fp32) + (m, l) per warp and head
+  return (PagedSmem<D>::RING > kWarps * G * D * 4 ? PagedSmem<D>::RING : kWarps * G * D * 4) +
+         2 * kWarps * G * 4;
 }
 
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                          uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+// d += a (16x16 bf16, row) * b (16x8 bf16, col), fp32 accumulators
+__device__ __forceinline__ void mma16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack2_bf16(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// Per page (16 keys) and warp, on 16x8x16 bf16 tensor-core fragments: the G
+// query heads of this KV head are the rows of a 16-row tile (rows >= G are
+// zero), S = Q K^T is two 16x8 tiles (keys 0-7, 8-15) over D/16 k-steps with
+// K fragments from ldmatrix; the online softmax runs on the accumulator
+// fragments (lane owns rows lane/4 and lane/4+8, keys 2(lane%4)+{0,1} of each
+// tile); P re-packs in registers into the A operand of O += P V, whose V
+// fragments come from ldmatrix.trans.  This keeps the instruction count per
+// page near 200, so the loop is bound by HBM rather than by issue.
 template <int D, int G>
 __global__ void __launch_bounds__(128)
     paged_attn_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_pool,
@@ -75,21 +106,21 @@ __global__ void __launch_bounds__(128)
                       bf16* __restrict__ out, float* __restrict__ ws_o,
                       float* __restrict__ ws_lse, int num_seqs, int max_pages, int Hq, int Hkv,
                       int pages_per_split, int splits, float scale_log2) {
+  static_assert(G <= 16, "one 16-row tile of query heads");
   using S = PagedSmem<D>;
-  constexpr int DL = D / 32;        // output dims owned per lane
-  constexpr int DH = D / 2;         // dims per half-warp in the score phase
+  constexpr int KS = D / 16;          // k-steps of Q K^T
+  constexpr int NT = D / 8;           // n-tiles of O
   constexpr int CHUNKS = D * 2 / 16;  // 16-byte chunks per K or V row
+  constexpr int MERGE = S::RING > kWarps * G * D * 4 ? S::RING : kWarps * G * D * 4;
   extern __shared__ __align__(128) uint8_t smem[];
-  float* sq = reinterpret_cast<float*>(smem + S::RING);          // [G][D]
-  float* s_m = sq + G * D;                                        // [kWarps][G]
+  float* s_m = reinterpret_cast<float*>(smem + MERGE);            // [kWarps][G]
   float* s_l = s_m + kWarps * G;                                  // [kWarps][G]
 
   const int split = blockIdx.x;
   const int kvh = blockIdx.y;
   const int tok = blockIdx.z;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  // sequence of this token (binary search over cu_q)
-  int lo = 0, hi = num_seqs - 1;
+  int lo = 0, hi = num_seqs - 1;  // sequence of this token (binary search over cu_q)
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
     if (cu_q[mid] <= tok) lo = mid; else hi = mid - 1;
@@ -109,7 +140,7 @@ __global__ void __launch_bounds__(128)
   }
   const int32_t* pt = page_table + static_cast<int64_t>(seq) * max_pages;
 
-  // ---- this warp's pages: p_begin + warp + kWarps * i
+  // ---- this warp's pages: p_begin + warp + kWarps * i, through a 2-stage ring
   const int first = p_begin + warp;
   const int count = first < p_end ? (p_end - first + kWarps - 1) / kWarps : 0;
   uint8_t* ring = smem + warp * S::WARP;
@@ -121,132 +152,164 @@ __global__ void __launch_bounds__(128)
     for (int c = lane; c < kPage * CHUNKS; c += 32) {
       const int r = c / CHUNKS, x = c % CHUNKS;
       const int64_t g = base + static_cast<int64_t>(r) * Hkv * D + x * 8;
-      cp_async16(st + r * S::K_ROW + x * 16, k_pool + g);
-      cp_async16(st + S::K_BYTES + r * D * 2 + x * 16, v_pool + g);
+      cp_async16(st + r * S::ROW + x * 16, k_pool + g);
+      cp_async16(st + S::K_BYTES + r * S::ROW + x * 16, v_pool + g);
     }
   };
   if (count > 0) issue(0);
   cp_async_commit();
 
-  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
-    const int g = i / D, d = i % D;
-    sq[i] = __bfloat162float(q[(orow + g) * D + d]);
-  }
-  __syncthreads();
-
-  float m[G], l[G], acc[G][DL];
+  // ---- Q as A fragments: rows = heads (>= G are zero), one 16x16 tile per k-step
+  const int fr = lane >> 2, fc = (lane & 3) * 2;
+  uint32_t qa[KS][4];
+  {
+    const bf16* q0 = q + orow * D;
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.f;
-#pragma unroll
-    for (int j = 0; j < DL; ++j) acc[g][j] = 0.f;
+    for (int ks = 0; ks < KS; ++ks) {
+      const int c0 = ks * 16 + fc;
+      auto ld2 = [&](int row, int col) -> uint32_t {
+        if (row >= G) return 0u;
+        return *reinterpret_cast<const uint32_t*>(q0 + row * D + col);
+      };
+      qa[ks][0] = ld2(fr, c0);
+      qa[ks][1] = ld2(fr + 8, c0);
+      qa[ks][2] = ld2(fr, c0 + 8);
+      qa[ks][3] = ld2(fr + 8, c0 + 8);
+    }
   }
-  const int key_in_page = lane & (kPage - 1);
-  const int half = lane / kPage;
+  float o[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // rows fr, fr + 8
+  const uint32_t ring_s = static_cast<uint32_t>(__cvta_generic_to_shared(ring));
+  // ldmatrix row addresses: lane supplies row (lane & 7) of matrix (lane >> 3)
+  const int lm = lane >> 3, lr = lane & 7;
 
   for (int i = 0; i < count; ++i) {
     if (i + 1 < count) issue(i + 1);
     cp_async_commit();
     cp_async_wait<1>();
     __syncwarp();
-    const uint8_t* st = ring + (i & 1) * S::STAGE;
+    const uint32_t st = ring_s + (i & 1) * S::STAGE;
     const int p = first + kWarps * i;
-    const int key = p * kPage + key_in_page;
-    const bool valid = key < n_keys;
-    // ---- scores of key `key_in_page` for every head (each half-warp covers D/2)
-    float s[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) s[g] = 0.f;
-    {
-      const uint8_t* kr = st + key_in_page * S::K_ROW + half * DH * 2;
-#pragma unroll
-      for (int d = 0; d < DH; d += 8) {
-        const uint4 w = *reinterpret_cast<const uint4*>(kr + d * 2);
-        const float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y), c = unpack_bf16x2(w.z),
-                     e = unpack_bf16x2(w.w);
-        const float kv8[8] = {a.x, a.y, b.x, b.y, c.x, c.y, e.x, e.y};
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float* qg = sq + g * D + half * DH + d;
-#pragma unroll
-          for (int u = 0; u < 8; ++u) s[g] = fmaf(qg[u], kv8[u], s[g]);
-        }
-      }
-    }
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      s[g] += __shfl_xor_sync(0xffffffffu, s[g], kPage);   // join the two halves of D
-      s[g] = valid ? s[g] * scale_log2 : -INFINITY;
-    }
-    // ---- online softmax over the page's keys, per head
-    float pexp[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float mx = s[g];
-#pragma unroll
-      for (int o = kPage / 2; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float m_new = fmaxf(m[g], mx);
-      const float alpha = m[g] == -INFINITY ? 0.f : exp2f(m[g] - m_new);
-      pexp[g] = valid ? exp2f(s[g] - m_new) : 0.f;
-      float ps = pexp[g];
-#pragma unroll
-      for (int o = kPage / 2; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-      l[g] = l[g] * alpha + ps;
-      m[g] = m_new;
-#pragma unroll
-      for (int j = 0; j < DL; ++j) acc[g][j] *= alpha;
-    }
-    // ---- P.V: lane owns dims [lane*DL, lane*DL+DL) for every head
     const int nk = min(kPage, n_keys - p * kPage);
-    const uint8_t* vs = st + S::K_BYTES + lane * DL * 2;
-    for (int t = 0; t < nk; ++t) {
-      float vv[DL];
+    if (nk < kPage) {  // partial last page: zero the unwritten V rows (P is 0 there)
+      uint8_t* vs = ring + (i & 1) * S::STAGE + S::K_BYTES;
+      for (int c = lane; c < (kPage - nk) * CHUNKS; c += 32)
+        *reinterpret_cast<uint4*>(vs + (nk + c / CHUNKS) * S::ROW + (c % CHUNKS) * 16) =
+            make_uint4(0, 0, 0, 0);
+      __syncwarp();
+    }
+    // ---- S = Q K^T: tile 0 = keys 0-7, tile 1 = keys 8-15
+    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int j = 0; j < DL; j += 2) {
-        const float2 f = __bfloat1622float2(
-            *reinterpret_cast<const __nv_bfloat162*>(vs + t * D * 2 + j * 2));
-        vv[j] = f.x;
-        vv[j + 1] = f.y;
-      }
+    for (int ks = 0; ks < KS; ++ks) {
+      // matrices: (keys 0-7, dims +0), (keys 0-7, +8), (keys 8-15, +0), (keys 8-15, +8)
+      const uint32_t addr = st + ((lm >> 1) * 8 + lr) * S::ROW + (ks * 16 + (lm & 1) * 8) * 2;
+      uint32_t b00, b01, b10, b11;
+      ldsm_x4(addr, b00, b01, b10, b11);
+      mma16816(s0, qa[ks], b00, b01);
+      mma16816(s1, qa[ks], b10, b11);
+    }
+    // ---- online softmax on the fragments (exp2 domain), masked past n_keys
+    const int k0 = fc, k1 = fc + 1, k2 = 8 + fc, k3 = 9 + fc;
+    s0[0] = k0 < nk ? s0[0] * scale_log2 : -INFINITY;
+    s0[1] = k1 < nk ? s0[1] * scale_log2 : -INFINITY;
+    s0[2] = k0 < nk ? s0[2] * scale_log2 : -INFINITY;
+    s0[3] = k1 < nk ? s0[3] * scale_log2 : -INFINITY;
+    s1[0] = k2 < nk ? s1[0] * scale_log2 : -INFINITY;
+    s1[1] = k3 < nk ? s1[1] * scale_log2 : -INFINITY;
+    s1[2] = k2 < nk ? s1[2] * scale_log2 : -INFINITY;
+    s1[3] = k3 < nk ? s1[3] * scale_log2 : -INFINITY;
+    float mx0 = fmaxf(fmaxf(s0[0], s0[1]), fmaxf(s1[0], s1[1]));
+    float mx1 = fmaxf(fmaxf(s0[2], s0[3]), fmaxf(s1[2], s1[3]));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);  // finite: key 0 is valid
+    const float a0 = exp2f(m0 - mn0), a1 = exp2f(m1 - mn1);  // exp2(-inf) = 0 on the first page
+    m0 = mn0;
+    m1 = mn1;
+    float p0[4], p1[4];
+    p0[0] = exp2f(s0[0] - mn0);
+    p0[1] = exp2f(s0[1] - mn0);
+    p0[2] = exp2f(s0[2] - mn1);
+    p0[3] = exp2f(s0[3] - mn1);
+    p1[0] = exp2f(s1[0] - mn0);
+    p1[1] = exp2f(s1[1] - mn0);
+    p1[2] = exp2f(s1[2] - mn1);
+    p1[3] = exp2f(s1[3] - mn1);
+    l0 = l0 * a0 + (p0[0] + p0[1] + p1[0] + p1[1]);  // lane-partial row sums
+    l1 = l1 * a1 + (p0[2] + p0[3] + p1[2] + p1[3]);
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float pt_g = __shfl_sync(0xffffffffu, pexp[g], t);
+    for (int j = 0; j < NT; ++j) {
+      o[j][0] *= a0;
+      o[j][1] *= a0;
+      o[j][2] *= a1;
+      o[j][3] *= a1;
+    }
+    // ---- O += P V: P as the A fragment (rows = heads, k = the page's 16 keys)
+    uint32_t pa[4] = {pack2_bf16(p0[0], p0[1]), pack2_bf16(p0[2], p0[3]),
+                      pack2_bf16(p1[0], p1[1]), pack2_bf16(p1[2], p1[3])};
 #pragma unroll
-        for (int j = 0; j < DL; ++j) acc[g][j] = fmaf(pt_g, vv[j], acc[g][j]);
-      }
+    for (int j = 0; j < NT; j += 2) {
+      // matrices (trans): (keys 0-7, dims j*8), (keys 8-15, j*8), (keys 0-7, j*8+8), (8-15, +8)
+      const uint32_t addr =
+          st + S::K_BYTES + ((lm & 1) * 8 + lr) * S::ROW + (j * 8 + (lm >> 1) * 8) * 2;
+      uint32_t v0, v1, v2, v3;
+      ldsm_x4_t(addr, v0, v1, v2, v3);
+      mma16816(o[j], pa, v0, v1);
+      mma16816(o[j + 1], pa, v2, v3);
     }
     __syncwarp();  // every lane is done with this stage before it is refilled
   }
   cp_async_wait<0>();
+  // full row sums across the quad
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
 
-  // ---- merge the warps (the ring is free now)
+  // ---- merge the warps (the ring is free now): rows < G only
   __syncthreads();
   float* s_acc = reinterpret_cast<float*>(smem);  // [kWarps][G][D]
-  if (lane == 0) {
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      s_m[warp * G + g] = m[g];
-      s_l[warp * G + g] = l[g];
+  if ((lane & 3) == 0) {
+    if (fr < G) {
+      s_m[warp * G + fr] = m0;
+      s_l[warp * G + fr] = l0;
+    }
+    if (fr + 8 < G) {
+      s_m[warp * G + fr + 8] = m1;
+      s_l[warp * G + fr + 8] = l1;
     }
   }
 #pragma unroll
-  for (int g = 0; g < G; ++g)
-#pragma unroll
-    for (int j = 0; j < DL; ++j) s_acc[(warp * G + g) * D + lane * DL + j] = acc[g][j];
+  for (int j = 0; j < NT; ++j) {
+    const int d = j * 8 + fc;
+    if (fr < G) {
+      s_acc[(warp * G + fr) * D + d] = o[j][0];
+      s_acc[(warp * G + fr) * D + d + 1] = o[j][1];
+    }
+    if (fr + 8 < G) {
+      s_acc[(warp * G + fr + 8) * D + d] = o[j][2];
+      s_acc[(warp * G + fr + 8) * D + d + 1] = o[j][3];
+    }
+  }
   __syncthreads();
-  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
-    const int g = i / D, d = i % D;
+  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+    const int g = idx / D, d = idx % D;
     float mm = -INFINITY;
     for (int w = 0; w < kWarps; ++w) mm = fmaxf(mm, s_m[w * G + g]);
-    float ll = 0.f, o = 0.f;
+    float ll = 0.f, acc = 0.f;
     for (int w = 0; w < kWarps; ++w) {
-      if (s_m[w * G + g] == -INFINITY) continue;
-      const float f = exp2f(s_m[w * G + g] - mm);
+      const float mw = s_m[w * G + g];
+      if (mw == -INFINITY) continue;  // a warp without pages
+      const float f = exp2f(mw - mm);
       ll += s_l[w * G + g] * f;
-      o += s_acc[(w * G + g) * D + d] * f;
+      acc += s_acc[(w * G + g) * D + d] * f;
     }
-    const float val = ll > 0.f ? o / ll : 0.f;
+    const float val = ll > 0.f ? acc / ll : 0.f;
     if (splits == 1) {
       out[(orow + g) * D + d] = __float2bfloat16(val);
     } else {

@@ -152,7 +152,10 @@ class InferenceEngine:
         mc = model.config
         pages = self.config.num_pages or (
             self.config.max_batch_size * self.config.max_cache_length // self.config.page_size)
-        self.pool = PagePool(mc.num_hidden_layers, mc.num_key_value_heads, mc.head_dim, pages,
+        # KV heads held by this rank (fewer than the config's under tensor parallelism)
+        kv_heads = getattr(getattr(model.layers[0], "self_attn", None), "num_kv_heads",
+                           mc.num_key_value_heads)
+        self.pool = PagePool(mc.num_hidden_layers, kv_heads, mc.head_dim, pages,
                              self.config.page_size, dtype=self.dtype, device=self.device)
         self._ids = itertools.count()
         self._graphs: Dict[int, tuple] = {}

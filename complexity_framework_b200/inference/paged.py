@@ -208,7 +208,11 @@ class PagedBatch:
                                  kf.transpose(0, 1)[None].contiguous(),
                                  vf.transpose(0, 1)[None].contiguous(), True, scale)
             out[a:e] = o.view(e - a, Hq, D)
-        if self.paged:
+        if self.paged and not self.fresh:  # every token reads pages: no gather/scatter
+            C.paged_attention(q.contiguous(), P.k[layer], P.v[layer], self.paged_table,
+                              self.paged_cu, self.paged_kv_lens, out, float(scale),
+                              int(self.max_q_len()))
+        elif self.paged:
             qs = q.index_select(0, self.paged_tokens).contiguous()
             os_ = torch.empty_like(qs)
             C.paged_attention(qs, P.k[layer], P.v[layer], self.paged_table, self.paged_cu,

@@ -63,13 +63,7 @@ def gemm_nt(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] =
         xp = x if Mp == M else torch.nn.functional.pad(x, (0, 0, 0, Mp - M))
         acc = torch.zeros(N, Mp, device=x.device, dtype=torch.float32)
         C.gemm(w, False, xp, False, N, Mp, K, EPI_F32_ATOMIC, out=acc)
-        acc = acc[:, :M]
-        if residual is not None:
-            torch.add(residual, acc.t(), alpha=alpha, out=out)
-        elif alpha != 1.0:
-            torch.mul(acc.t(), alpha, out=out)
-        else:
-            out.copy_(acc.t())
+        C.skinny_finish(acc, None if residual is None else _c(residual), out, alpha)
         return out
     if residual is not None:
         C.gemm(x, False, w, False, M, N, K, EPI_RESID, out=out, residual=_c(residual), alpha=alpha)
@@ -314,6 +308,25 @@ def _trhash_forward(ctx, h, w_gu, w_down, row_scale, residual, shared_width, exp
     ctx.has_res = residual is not None
     ctx.shape = shape
     return out.view(*shape[:-1], Hout)
+
+
+def trhash_mlp_infer(h, w_gu, w_down, row_scale, shared_width, expert_width, n_experts,
+                     shared_scale, out: Optional[torch.Tensor] = None,
+                     residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Inference ``act @ Wd^T (+ residual)`` of ``TRHashMLPFn`` (no autograd state),
+    written into ``out`` when given (e.g. a tensor-parallel partial buffer)."""
+    C = require()
+    H = h.shape[-1]
+    h2 = _c(h.reshape(-1, H))
+    T = h2.shape[0]
+    A2 = w_gu.shape[0]
+    gu = torch.empty(T, A2, device=h.device, dtype=torch.bfloat16)
+    act = torch.empty(T, A2 // 2, device=h.device, dtype=torch.bfloat16)
+    C.gemm(h2, False, w_gu, False, T, A2, H, EPI_SWIGLU_FWD, gu=gu, act=act,
+           row_scale=row_scale, shared_width=shared_width, expert_width=expert_width,
+           n_experts=n_experts, shared_scale=shared_scale)
+    r2 = None if residual is None else residual.reshape(T, w_down.shape[0])
+    return gemm_nt(act, w_down, r2, out=out)
 
 
 def _trhash_backward(ctx, dout, wgrad_dtype, down_transposed: bool = False):

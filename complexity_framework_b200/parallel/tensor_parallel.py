@@ -204,12 +204,32 @@ def _shard(p: torch.Tensor, dim: int, P: int, r: int) -> nn.Parameter:
     return out
 
 
-def make_parallel(model: nn.Module, group=None) -> nn.Module:
+def _block_split(n: int, P: int, r: int, block: int):
+    """(start, size) of rank r's share of n columns dealt in whole blocks:
+    the first (n/block) % P ranks get one block more."""
+    nb = n // block
+    per, extra = divmod(nb, P)
+    start = (r * per + min(r, extra)) * block
+    return start, (per + (1 if r < extra else 0)) * block
+
+
+def _shard_range(p: torch.Tensor, dim: int, start: int, size: int, sizes) -> nn.Parameter:
+    out = nn.Parameter(p.detach().narrow(dim, start, size).clone(), requires_grad=p.requires_grad)
+    out._tp_shard_dim = dim
+    out._tp_shard_sizes = tuple(sizes)
+    return out
+
+
+def make_parallel(model: nn.Module, group=None, shared_block: int = 0) -> nn.Module:
     """Shard a full-weight ``ComplexityModel`` in place over ``group`` (default: TP group).
 
     Load the full checkpoint first; each rank keeps its slice.  Embedding and
     LM head stay replicated (their gradients are averaged by data parallelism
-    or are identical across TP ranks).
+    or are identical across TP ranks).  With ``shared_block`` > 0 a shared
+    SwiGLU width whose even split is not a multiple of the block is dealt in
+    whole blocks instead (ranks may then hold different widths, e.g. 11008 over
+    8 ranks as 11 or 10 blocks of 128), which keeps every rank on the fused
+    SwiGLU kernel.
     """
     group = group if group is not None else _TP["group"]
     P, r = tp_world(group), tp_rank(group)
@@ -249,16 +269,30 @@ def make_parallel(model: nn.Module, group=None) -> nn.Module:
         eng = getattr(layer.mlp, "engine", None)
         if eng is not None:
             cfg = eng.config
-            if cfg.expert_width % P or cfg.shared_width % P:
+            sw = cfg.shared_width
+            blocked = (shared_block > 0 and sw % shared_block == 0
+                       and (sw % P or (sw // P) % shared_block))
+            if cfg.expert_width % P or (sw % P and not blocked):
                 raise ValueError("expert and shared widths must be divisible by the TP size")
+            local_sw = sw // P
             if eng.shared_gate is not None:
-                eng.shared_gate.weight = _shard(eng.shared_gate.weight, 0, P, r)
-                eng.shared_up.weight = _shard(eng.shared_up.weight, 0, P, r)
-                eng.shared_down.weight = _shard(eng.shared_down.weight, 1, P, r)
+                if blocked:
+                    sizes = [_block_split(sw, P, q, shared_block)[1] for q in range(P)]
+                    start, local_sw = _block_split(sw, P, r, shared_block)
+                    eng.shared_gate.weight = _shard_range(eng.shared_gate.weight, 0, start,
+                                                          local_sw, sizes)
+                    eng.shared_up.weight = _shard_range(eng.shared_up.weight, 0, start,
+                                                        local_sw, sizes)
+                    eng.shared_down.weight = _shard_range(eng.shared_down.weight, 1, start,
+                                                          local_sw, sizes)
+                else:
+                    eng.shared_gate.weight = _shard(eng.shared_gate.weight, 0, P, r)
+                    eng.shared_up.weight = _shard(eng.shared_up.weight, 0, P, r)
+                    eng.shared_down.weight = _shard(eng.shared_down.weight, 1, P, r)
             eng.expert_gate = _shard(eng.expert_gate, 2, P, r)
             eng.expert_up = _shard(eng.expert_up, 2, P, r)
             eng.expert_down = _shard(eng.expert_down, 1, P, r)
-            eng.config = replace(cfg, shared_width=cfg.shared_width // P,
+            eng.config = replace(cfg, shared_width=local_sw,
                                  expert_width=cfg.expert_width // P)
             eng._active_expert_width = eng.config.expert_width
             eng.tp_group = group
@@ -270,15 +304,27 @@ def gather_tp_state_dict(model: nn.Module, group=None) -> dict:
     """Full (unsharded) state dict from a TP-sharded model (collective over the TP group)."""
     group = group if group is not None else getattr(model, "tp_group", _TP["group"])
     P = tp_world(group)
-    shard_dims = {}
+    shard_dims, shard_sizes = {}, {}
     for name, p in model.named_parameters():
         if hasattr(p, "_tp_shard_dim"):
             shard_dims[name] = p._tp_shard_dim
+            shard_sizes[name] = getattr(p, "_tp_shard_sizes", None)
     out = {}
     for name, t in model.state_dict().items():
         if name in shard_dims and P > 1:
-            parts = [torch.empty_like(t) for _ in range(P)]
-            dist.all_gather(parts, t.contiguous(), group=group)
-            t = torch.cat(parts, shard_dims[name])
+            dim, sizes = shard_dims[name], shard_sizes[name]
+            if sizes is None:
+                parts = [torch.empty_like(t) for _ in range(P)]
+                dist.all_gather(parts, t.contiguous(), group=group)
+                t = torch.cat(parts, dim)
+            else:  # uneven block shards: gather padded to the largest, then trim
+                big = max(sizes)
+                pad = list(t.shape)
+                pad[dim] = big
+                buf = t.new_zeros(pad)
+                buf.narrow(dim, 0, t.shape[dim]).copy_(t)
+                parts = [torch.empty_like(buf) for _ in range(P)]
+                dist.all_gather(parts, buf, group=group)
+                t = torch.cat([q.narrow(dim, 0, n) for q, n in zip(parts, sizes)], dim)
         out[name] = t
     return out

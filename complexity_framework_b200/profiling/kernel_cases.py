@@ -202,7 +202,43 @@ def case_moe(iters: int) -> None:
     check_errors(0)
 
 
-CASES = {"gemm": case_gemm, "gemm_bn": case_gemm_bn, "flash": case_flash, "norms": case_norms,
+def case_decode(iters: int) -> None:
+    """One decode step's per-layer kernels of the 7B serving benchmark: split-KV
+    paged attention over 64 sequences (lengths 128..2303, GQA 32/8, D 128) and
+    the skinny split-K projections (M = 64)."""
+    from ..inference.paged import PagedBatch, PagePool, SeqChunk
+    from ..ops import fused
+
+    C = require()
+    torch.manual_seed(0)
+    g = torch.Generator().manual_seed(4321)
+    lens = torch.randint(128, 2304, (64,), generator=g).tolist()
+    Hq, Hkv, D = 32, 8, 128
+    pool = PagePool(1, Hkv, D, sum(-(-(n + 1) // 16) for n in lens), 16,
+                    dtype=torch.bfloat16, device="cuda")
+    for sid, n in enumerate(lens):
+        pool.allocate_sequence(sid)
+        pool.reserve(sid, n + 1)
+        pool.lengths[sid] = n
+    pool.k.normal_()
+    pool.v.normal_()
+    b = PagedBatch(pool, [SeqChunk(sid, n, 1) for sid, n in enumerate(lens)])
+    q = torch.randn(64, Hq, D, device="cuda").bfloat16()
+    out = torch.empty_like(q)
+    kv_bytes = sum(n + 1 for n in lens) * Hkv * D * 2 * 2
+    _report("paged_attention_decode", cuda_time(lambda: C.paged_attention(
+        q, pool.k[0], pool.v[0], b.paged_table, b.paged_cu, b.paged_kv_lens, out,
+        D ** -0.5, 1), iters), nbytes=kv_bytes)
+    x = torch.randn(64, 4096, device="cuda").bfloat16()
+    for name, N, K in (("skinny_qkv", 6144, 4096), ("skinny_o", 4096, 4096),
+                       ("skinny_down", 4096, 15104)):
+        w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+        xk = x if K == 4096 else torch.randn(64, K, device="cuda").bfloat16()
+        _report(name, cuda_time(lambda: fused.gemm_nt(xk, w), iters), 2.0 * 64 * N * K,
+                nbytes=N * K * 2)
+
+
+CASES = {"decode": case_decode, "gemm": case_gemm, "gemm_bn": case_gemm_bn, "flash": case_flash, "norms": case_norms,
          "moe": case_moe}
 
 

@@ -131,6 +131,37 @@ class TRHashEngine(nn.Module):
             got = self._packed_cache = (key, w_gu, w_down)
         return got[1], got[2]
 
+    INFER_DENSE_ROWS = 1024  # eval-mode rows up to which dense-masked experts are used
+
+    def _inference_dense_ready(self, x: torch.Tensor) -> bool:
+        """Eval-mode FFN on the fused dense-masked kernels (decoding reads every
+        expert's weights anyway, so the masked columns cost no extra bytes)."""
+        from ..ops import fused
+
+        sg = self.shared_gate.weight if self.shared_gate is not None else None
+        return (not (self.training or torch.is_grad_enabled()) and x.is_cuda
+                and x.dtype == torch.bfloat16 and self.expert_gate.dtype == torch.bfloat16
+                and not self.is_reduced_capacity and fused.packable(sg, self.expert_gate)
+                and self.config.expert_width % 32 == 0 and self.config.num_experts <= 16
+                and not any(getattr(m, "is_lora_adapter", False)
+                            for m in (self.shared_gate, self.shared_up, self.shared_down)
+                            if m is not None))
+
+    def _fused_partial(self, hidden: torch.Tensor, token_ids: torch.Tensor,
+                       out: Optional[torch.Tensor],
+                       residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """FFN output (this rank's partial under tensor parallelism) plus
+        ``residual`` when given, into ``out`` when given."""
+        from ..ops import fused
+
+        cfg = self.config
+        scales = fused.route_scales(token_ids, self._active_route_table, self._route_weights,
+                                    cfg.num_experts, cfg.routed_output_scale)
+        w_gu, w_down = self._packed_for_inference()
+        return fused.trhash_mlp_infer(hidden, w_gu, w_down, scales, cfg.shared_width,
+                                      cfg.expert_width, cfg.num_experts,
+                                      cfg.shared_output_scale, out, residual)
+
     def _apply(self, fn, recurse: bool = True):
         self._packed_cache = None
         aliased = self._active_route_table is self.route_table
@@ -387,6 +418,25 @@ class TRHashEngine(nn.Module):
                                         f"{hidden_states.dtype}",), False, False)
         self.last_backend = decision
         tp = getattr(self, "tp_group", None)
+        H = hidden_states.shape[-1]
+        kernels = decision.selected in (TRHashBackend.FUSED_CUDA, TRHashBackend.CGGR)
+        if (tp is None and kernels and hidden_states.numel() // H <= self.INFER_DENSE_ROWS
+                and self._inference_dense_ready(hidden_states)):
+            # decoding: few rows read every expert's weights anyway, so the
+            # dense-masked fused kernels are the bandwidth-optimal choice
+            return self._fused_partial(hidden_states, token_ids, None,
+                                       residual).view_as(hidden_states)
+        if (tp is not None and kernels and hasattr(self, "tp_site")
+                and self._inference_dense_ready(hidden_states)):
+            # tensor-parallel inference: partial FFN into the symmetric buffer of
+            # this call site, then one fused all-reduce + residual
+            from ..parallel.tp_inference import tp_reduce_add
+
+            rows = hidden_states.numel() // H
+            y = tp_reduce_add(getattr(self, "tp_decode", None), self.tp_site,
+                              lambda out: self._fused_partial(hidden_states, token_ids, out),
+                              rows, residual, tp)
+            return y.view_as(hidden_states)
         if tp is not None:
             # tensor parallel: this rank holds a slice of every width; sum the slices
             from ..parallel.tensor_parallel import copy_to_tp, reduce_from_tp

@@ -25,6 +25,7 @@ SOURCES = [
     "ep_fused.cu",
     "pack.cu",
     "moe_grouped.cu",
+    "tp_decode.cu",
 ]
 
 # Link the shared system libstdc++ (the one libtorch uses).  The compiler wrapper

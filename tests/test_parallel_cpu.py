@@ -93,6 +93,41 @@ def test_tensor_parallel_matches_single():
     _run(2, _tp_body)
 
 
+def _tp_decode_body(rank, world, tmp):
+    """Tensor-parallel paged decoding (uneven 128-column shared blocks) gives the
+    single-process engine's greedy tokens; the sharded weights gather back."""
+    from complexity_framework_b200.inference.engine import (GenerationConfig, InferenceConfig,
+                                                            InferenceEngine)
+    from complexity_framework_b200.parallel import gather_tp_state_dict
+    from complexity_framework_b200.parallel.tp_inference import enable_tp_decode
+
+    cfg = dict(CFG, hidden_size=64, shared_intermediate_size=384, intermediate_size=64)
+
+    def model():
+        torch.manual_seed(0)
+        return ComplexityModel(ModelConfig(**cfg)).eval()
+
+    prompts = [torch.randint(0, 256, (n,), generator=torch.Generator().manual_seed(n)).tolist()
+               for n in (5, 11, 3)]
+    gen = GenerationConfig(max_new_tokens=6)
+    want = InferenceEngine(model(), InferenceConfig(max_cache_length=64)).generate_tokens(
+        prompts, gen)
+    ref_state = model().state_dict()
+    m = enable_tp_decode(model(), dist.group.WORLD)
+    eng = m.layers[0].mlp.engine
+    # 384 = 3 blocks of 128 over 2 ranks: rank 0 holds 256 columns, rank 1 holds 128
+    assert eng.config.shared_width == (256 if rank == 0 else 128)
+    got = InferenceEngine(m, InferenceConfig(max_cache_length=64)).generate_tokens(prompts, gen)
+    assert got == want, (got, want)
+    full = gather_tp_state_dict(m)
+    for k, v in ref_state.items():
+        assert torch.allclose(full[k].float(), v.float()), k
+
+
+def test_tensor_parallel_decode_matches_single():
+    _run(2, _tp_decode_body)
+
+
 def _pp_body(rank, world, tmp, schedule):
     from complexity_framework_b200.parallel import PipelineModel
 
