@@ -389,6 +389,26 @@ void skinny_finish(const torch::Tensor& acc, const c10::optional<torch::Tensor>&
                      static_cast<int>(M), static_cast<int>(N), static_cast<float>(alpha), cur());
 }
 
+void skinny_swiglu(const torch::Tensor& acc, const torch::Tensor& row_scale, torch::Tensor& act,
+                   int64_t shared_width, int64_t expert_width, int64_t n_experts,
+                   double shared_scale) {
+  TORCH_CHECK(acc.is_cuda() && acc.scalar_type() == torch::kFloat32 && acc.dim() == 2 &&
+                  acc.stride(1) == 1, "acc: fp32 [2A, >=T] row-major");
+  chk(act, torch::kBFloat16, "act");
+  chk(row_scale, torch::kFloat32, "row_scale");
+  TORCH_CHECK(act.dim() == 2, "act [T, A]");
+  const int64_t T = act.size(0), A = act.size(1);
+  TORCH_CHECK(A % 128 == 0 && acc.size(0) == 2 * A && acc.size(1) >= T, "acc [2A, >=T]");
+  TORCH_CHECK(A == shared_width || (expert_width > 0 && n_experts > 0 &&
+                                    row_scale.numel() >= T * n_experts),
+              "row_scale [T, n_experts]");
+  const c10::cuda::CUDAGuard g(act.device());
+  cfb::skinny_swiglu(P<float>(acc), static_cast<int>(acc.stride(0)), P<float>(row_scale),
+                     P<bf16>(act), static_cast<int>(T), static_cast<int>(A),
+                     static_cast<int>(shared_width), static_cast<int>(expert_width > 0 ? expert_width : 1),
+                     static_cast<int>(n_experts), static_cast<float>(shared_scale), cur());
+}
+
 // geom: 10 ints per job (rows, cols, s_div, s_hi, s_lo, s_cs, d_div, d_hi, d_lo,
 // d_cs), element offsets relative to each tensor's data pointer.  Every job's
 // largest source and destination offsets are checked against the tensors.
@@ -464,4 +484,5 @@ void register_elementwise(pybind11::module& m) {
   m.def("paged_attention", &paged_attention);
   m.def("paged_qkv_rope", &paged_qkv_rope);
   m.def("skinny_finish", &skinny_finish);
+  m.def("skinny_swiglu", &skinny_swiglu);
 }

@@ -156,6 +156,42 @@ __global__ void __launch_bounds__(256) skinny_finish_k(const float* __restrict__
   }
 }
 
+// act[t, c] = silu(g) * u * scale(t, c) from the transposed fp32 result of a
+// swapped-operand split-K gate|up GEMM: acc[r, t] over the packed rows, gate
+// column c at row (c / 128) * 256 + c % 128 and its up column 128 rows later.
+// scale = shared_scale for c < shared_width, else row_scale[t, expert(c)].
+// One 32 (c) x 32 (t) tile per block, transposed through shared memory.
+__global__ void __launch_bounds__(256) skinny_swiglu_k(
+    const float* __restrict__ acc, int ldacc, const float* __restrict__ row_scale,
+    bf16* __restrict__ act, int T, int A, int shared_width, int expert_width, int n_experts,
+    float shared_scale) {
+  __shared__ float tg[32][33], tu[32][33];
+  const int c0 = blockIdx.x * 32, t0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int k = ty; k < 32; k += 8) {
+    const int c = c0 + k, t = t0 + tx;
+    float g = 0.f, u = 0.f;
+    if (c < A && t < T) {
+      const int64_t rg = static_cast<int64_t>(c / 128) * 256 + c % 128;
+      g = acc[rg * ldacc + t];
+      u = acc[(rg + 128) * ldacc + t];
+    }
+    tg[k][tx] = g;
+    tu[k][tx] = u;
+  }
+  __syncthreads();
+  for (int k = ty; k < 32; k += 8) {
+    const int t = t0 + k, c = c0 + tx;
+    if (t < T && c < A) {
+      const float g = rb(tg[tx][k]), u = rb(tu[tx][k]);
+      float sc = shared_scale;
+      if (c >= shared_width)
+        sc = row_scale[static_cast<int64_t>(t) * n_experts + (c - shared_width) / expert_width];
+      act[static_cast<int64_t>(t) * A + c] = __float2bfloat16(g / (1.f + __expf(-g)) * u * sc);
+    }
+  }
+}
+
 __global__ void rmsnorm_bwd_k(const bf16* __restrict__ dy, const bf16* __restrict__ x,
                               const bf16* __restrict__ w, const float* __restrict__ rstd,
                               const bf16* __restrict__ dres, bf16* __restrict__ dx,
@@ -1156,6 +1192,13 @@ void rmsnorm_fwd(const bf16* x, const bf16* w, bf16* y, float* rstd, int64_t T, 
     return;
   }
   rmsnorm_fwd_k<<<grid_for(T, 8), 256, 0, s>>>(x, w, y, rstd, T, H, eps);
+}
+
+void skinny_swiglu(const float* acc, int ldacc, const float* row_scale, bf16* act, int T, int A,
+                   int shared_width, int expert_width, int n_experts, float shared_scale,
+                   cudaStream_t s) {
+  skinny_swiglu_k<<<dim3((A + 31) / 32, (T + 31) / 32), 256, 0, s>>>(
+      acc, ldacc, row_scale, act, T, A, shared_width, expert_width, n_experts, shared_scale);
 }
 
 void skinny_finish(const float* acc, int ldacc, const bf16* resid, bf16* out, int M, int N,

@@ -12,6 +12,11 @@ using bf16 = __nv_bfloat16;
 // out[m, n] = bf16(alpha * acc[n, m] (+ resid[m, n])) for m < M, n < N (acc row stride ldacc).
 void skinny_finish(const float* acc, int ldacc, const bf16* resid, bf16* out, int M, int N,
                    float alpha, cudaStream_t s);
+// act[t, c] = silu(g) * u * scale(t, c) from acc [2A packed gate|up rows, >= T] (fp32,
+// row stride ldacc): gate row of c = (c/128)*256 + c%128, up row 128 later.
+void skinny_swiglu(const float* acc, int ldacc, const float* row_scale, bf16* act, int T, int A,
+                   int shared_width, int expert_width, int n_experts, float shared_scale,
+                   cudaStream_t s);
 void rmsnorm_fwd(const bf16* x, const bf16* w, bf16* y, float* rstd, int64_t T, int H, float eps,
                  cudaStream_t s);
 // dx = rmsnorm'(x)^T dy (+ dres);  dw (fp32, [H]) += sum_rows dy * x*rstd.

@@ -16,8 +16,8 @@
 //   over many SMs.  The host picks the pages per split from the batch size so
 //   a decode step launches several CTAs per SM.
 // * each of the four warps streams its pages (page w, w+4, ...) through a
-//   two-stage cp.async ring in shared memory: the next page's 2 x 4 KB of K/V
-//   is in flight while the current one is consumed.  K rows are padded by 16
+//   three-stage cp.async ring in shared memory: the next two pages' K/V
+//   (2 x 4 KB each) are in flight while the current one is consumed.  K rows are padded by 16
 //   bytes so the 16 lanes reading different keys hit different banks.
 // * inside a warp, lanes (key t, half) form the dot products of page key t
 //   over half of D for all heads; then lanes own D/32 output dims and
@@ -56,7 +56,8 @@ struct PagedSmem {
   static constexpr int ROW = D * 2 + 16;               // bytes per K or V row, padded
   static constexpr int K_BYTES = kPage * ROW;
   static constexpr int STAGE = 2 * K_BYTES;            // K page then V page
-  static constexpr int WARP = 2 * STAGE;
+  static constexpr int NSTAGE = 3;                     // pages in flight per warp: 2
+  static constexpr int WARP = NSTAGE * STAGE;
   static constexpr int RING = kWarps * WARP;
 };
 
@@ -140,13 +141,13 @@ __global__ void __launch_bounds__(128)
   }
   const int32_t* pt = page_table + static_cast<int64_t>(seq) * max_pages;
 
-  // ---- this warp's pages: p_begin + warp + kWarps * i, through a 2-stage ring
+  // ---- this warp's pages: p_begin + warp + kWarps * i, through a 3-stage ring
   const int first = p_begin + warp;
   const int count = first < p_end ? (p_end - first + kWarps - 1) / kWarps : 0;
   uint8_t* ring = smem + warp * S::WARP;
   auto issue = [&](int i) {
     const int page = __ldg(pt + first + kWarps * i);
-    uint8_t* st = ring + (i & 1) * S::STAGE;
+    uint8_t* st = ring + (i % S::NSTAGE) * S::STAGE;
     const int64_t base = (static_cast<int64_t>(page) * kPage * Hkv + kvh) * D;
 #pragma unroll
     for (int c = lane; c < kPage * CHUNKS; c += 32) {
@@ -156,8 +157,11 @@ __global__ void __launch_bounds__(128)
       cp_async16(st + S::K_BYTES + r * S::ROW + x * 16, v_pool + g);
     }
   };
-  if (count > 0) issue(0);
-  cp_async_commit();
+#pragma unroll
+  for (int j = 0; j < S::NSTAGE - 1; ++j) {  // one commit group per ring slot, even if empty
+    if (j < count) issue(j);
+    cp_async_commit();
+  }
 
   // ---- Q as A fragments: rows = heads (>= G are zero), one 16x16 tile per k-step
   const int fr = lane >> 2, fc = (lane & 3) * 2;
@@ -186,15 +190,16 @@ __global__ void __launch_bounds__(128)
   const int lm = lane >> 3, lr = lane & 7;
 
   for (int i = 0; i < count; ++i) {
-    if (i + 1 < count) issue(i + 1);
+    if (i + S::NSTAGE - 1 < count) issue(i + S::NSTAGE - 1);
     cp_async_commit();
-    cp_async_wait<1>();
+    cp_async_wait<S::NSTAGE - 1>();  // page i has landed
     __syncwarp();
-    const uint32_t st = ring_s + (i & 1) * S::STAGE;
+    const int slot = i % S::NSTAGE;
+    const uint32_t st = ring_s + slot * S::STAGE;
     const int p = first + kWarps * i;
     const int nk = min(kPage, n_keys - p * kPage);
     if (nk < kPage) {  // partial last page: zero the unwritten V rows (P is 0 there)
-      uint8_t* vs = ring + (i & 1) * S::STAGE + S::K_BYTES;
+      uint8_t* vs = ring + slot * S::STAGE + S::K_BYTES;
       for (int c = lane; c < (kPage - nk) * CHUNKS; c += 32)
         *reinterpret_cast<uint4*>(vs + (nk + c / CHUNKS) * S::ROW + (c % CHUNKS) * 16) =
             make_uint4(0, 0, 0, 0);

@@ -320,11 +320,21 @@ def trhash_mlp_infer(h, w_gu, w_down, row_scale, shared_width, expert_width, n_e
     h2 = _c(h.reshape(-1, H))
     T = h2.shape[0]
     A2 = w_gu.shape[0]
-    gu = torch.empty(T, A2, device=h.device, dtype=torch.bfloat16)
     act = torch.empty(T, A2 // 2, device=h.device, dtype=torch.bfloat16)
-    C.gemm(h2, False, w_gu, False, T, A2, H, EPI_SWIGLU_FWD, gu=gu, act=act,
-           row_scale=row_scale, shared_width=shared_width, expert_width=expert_width,
-           n_experts=n_experts, shared_scale=shared_scale)
+    if _skinny(T, A2, H):
+        # few rows: swapped operands + split-K (see gemm_nt), SwiGLU in the pass
+        # that transposes the fp32 result
+        Tp = (T + 31) // 32 * 32
+        hp = h2 if Tp == T else torch.nn.functional.pad(h2, (0, 0, 0, Tp - T))
+        acc = torch.zeros(A2, Tp, device=h.device, dtype=torch.float32)
+        C.gemm(w_gu, False, hp, False, A2, Tp, H, EPI_F32_ATOMIC, out=acc)
+        C.skinny_swiglu(acc, _c(row_scale.float()), act, shared_width, expert_width, n_experts,
+                        shared_scale)
+    else:
+        gu = torch.empty(T, A2, device=h.device, dtype=torch.bfloat16)
+        C.gemm(h2, False, w_gu, False, T, A2, H, EPI_SWIGLU_FWD, gu=gu, act=act,
+               row_scale=row_scale, shared_width=shared_width, expert_width=expert_width,
+               n_experts=n_experts, shared_scale=shared_scale)
     r2 = None if residual is None else residual.reshape(T, w_down.shape[0])
     return gemm_nt(act, w_down, r2, out=out)
 

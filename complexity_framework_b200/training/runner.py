@@ -67,6 +67,10 @@ class TrainRunner:
         p.add_argument("--model", type=str, default=None, help="preset name or config.json/yaml")
         p.add_argument("--data", type=str, default=None, help="token shard directory")
         p.add_argument("--synthetic", action="store_true", help="Zipf synthetic token ids")
+        p.add_argument("--token-mixture", type=str, default=None,
+                       help="pretokenized corpus mixture directory (mixture_manifest.json)")
+        p.add_argument("--replay-plan", type=str, default=None,
+                       help="token replay plan for --token-mixture")
         p.add_argument("--tokenizer", type=str, default=None)
         p.add_argument("--target-tokens", type=str, default=str(self.default_target_tokens))
         p.add_argument("--batch-size", type=int, default=self.default_batch_size)
@@ -120,6 +124,30 @@ class TrainRunner:
 
     # ------------------------------------------------------------------ data
     def build_batches(self, args, rank: int, world: int, start_batch: int):
+        if args.token_mixture:
+            from ..data.corpus_mixture import PretokenizedCorpusMixtureDataset
+
+            # every optimizer step consumes one batch of batch_size rows on each
+            # rank: a resumed run skips exactly the rows it already trained on
+            skip = start_batch * args.batch_size
+            ds = PretokenizedCorpusMixtureDataset(args.token_mixture, rank=rank,
+                                                  world_size=world,
+                                                  replay_plan=args.replay_plan,
+                                                  resume_skip_rows=skip)
+            if ds.seq_len != args.seq_len:
+                raise SystemExit(f"--seq-len {args.seq_len} but the mixture has rows of "
+                                 f"{ds.seq_len} tokens")
+
+            def rows():
+                buf_x, buf_y = [], []
+                for item in ds:
+                    buf_x.append(item["input_ids"])
+                    buf_y.append(item["labels"])
+                    if len(buf_x) == args.batch_size:
+                        yield torch.stack(buf_x), torch.stack(buf_y)
+                        buf_x, buf_y = [], []
+
+            return rows()
         if args.data:
             from ..data.loader import TokenBatchLoader
 
@@ -128,7 +156,7 @@ class TrainRunner:
                                     if args.token_packs > 1 else "random",
                                     start_batch=start_batch)
         if not args.synthetic:
-            raise SystemExit("pass --data <token shard> or --synthetic")
+            raise SystemExit("pass --data <token shard>, --token-mixture <dir> or --synthetic")
         g = torch.Generator().manual_seed(args.seed + 7919 * rank)
         vocab = self.cfg.vocab_size
 

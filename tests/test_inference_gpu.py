@@ -147,3 +147,30 @@ def test_paged_qkv_rope_kernel(D, qk_norm):
     vf = vp.view(-1, Hkv, D)[slots].float()
     assert (kf - prep(k_, kw)).abs().max() < 3e-2
     assert torch.equal(vf, v_)
+
+
+@pytest.mark.parametrize("rows", [1, 37, 64, 128])
+def test_inference_dense_ffn_matches_reference(rows):
+    """Eval-mode TR-Hash FFN on few rows (decode shapes): dense-masked kernels with
+    the skinny split-K gate|up GEMM + SwiGLU pass, against the fp32 reference."""
+    from complexity_framework_b200 import ComplexityModel, ModelConfig
+    from complexity_framework_b200.tr_hash import TRHashBackend
+
+    torch.manual_seed(0)
+    cfg = ModelConfig(hidden_size=512, num_hidden_layers=1, num_attention_heads=8,
+                      num_key_value_heads=2, vocab_size=2048, intermediate_size=512,
+                      shared_intermediate_size=1408, num_experts=8, top_k=2,
+                      routing_strategy="modulo_cyclic", max_position_embeddings=256)
+    m = ComplexityModel(cfg).cuda().to(torch.bfloat16).eval()
+    eng = m.layers[0].mlp.engine
+    x = torch.randn(1, rows, 512, device="cuda").bfloat16()
+    ids = torch.randint(0, 2048, (1, rows), device="cuda")
+    res = torch.randn_like(x)
+    with torch.no_grad():
+        got = eng(x, ids, residual=res).float()
+        ref_eng = m.float().layers[0].mlp.engine
+        ref_eng.config = type(ref_eng.config)(**{**ref_eng.config.__dict__,
+                                                 "backend": TRHashBackend.PYTORCH})
+        want = ref_eng(x.float(), ids, residual=res.float())
+    err = ((got - want).abs().max() / want.abs().max()).item()
+    assert err < 2e-2, err

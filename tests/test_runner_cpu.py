@@ -51,6 +51,35 @@ def test_runner_token_shard(tmp_path):
     assert s["steps"] == 3
 
 
+def test_runner_token_mixture_resume_skips_trained_rows(tmp_path, monkeypatch):
+    from complexity_framework_b200.data import corpus_mixture as cm
+
+    rng = np.random.default_rng(1)
+    cm.write_token_mixture(tmp_path / "mix", {"a": (0.5, rng.integers(0, 256, 16 * 40 + 1)),
+                                              "b": (0.5, rng.integers(0, 256, 16 * 40 + 1))},
+                           16, 16)
+    seen = []
+    orig = cm.PretokenizedCorpusMixtureDataset.__iter__
+
+    def spy(self):
+        for item in orig(self):
+            seen.append(tuple(item["input_ids"].tolist()))
+            yield item
+
+    monkeypatch.setattr(cm.PretokenizedCorpusMixtureDataset, "__iter__", spy)
+    ck = tmp_path / "ck"
+    base = ["--token-mixture", str(tmp_path / "mix"), "--batch-size", "2", "--seq-len", "16",
+            "--checkpoint-dir", str(ck), "--save-steps", "3", "--precision", "fp32",
+            "--no-progress"]
+    assert _runner().main(base + ["--max-steps", "3"])["steps"] == 3
+    first = list(seen[:6])
+    seen.clear()
+    assert _runner().main(base + ["--max-steps", "5", "--resume", "auto"])["steps"] == 5
+    full = list(cm.PretokenizedCorpusMixtureDataset(tmp_path / "mix"))
+    rows = [tuple(x["input_ids"].tolist()) for x in full]
+    assert first == rows[:6] and seen[:4] == rows[6:10]  # resumed on the next unseen rows
+
+
 def test_cluster_plan_and_tokens():
     assert parse_tokens("200B") == 200 * 10 ** 9 and parse_tokens("1.5m") == 1_500_000
     p = ClusterRunPlan("x", parse_tokens("70b"), 1024, 201_194_368, ParallelPlan(1, 1, 8, 8, 8))
