@@ -48,6 +48,8 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-count", action="store_true", help="skip the kernel-launch count step")
     p.add_argument("--no-graph", action="store_true", help="run every step eagerly")
+    p.add_argument("--zero3", action="store_true",
+                   help="multi-GPU: ZeRO-3 (per-block parameter shards) instead of ZeRO-2")
     p.add_argument("--workload", choices=("train", "decode"), default="train",
                    help="train: the 200M pretraining headline; decode: 7B paged-KV serving")
     return p.parse_args()
@@ -168,7 +170,8 @@ def build_ours(world, args):
     # epochs and hyper-parameters live on the device)
     cfg = TrainingConfig(learning_rate=3e-4, warmup_steps=0, lr_scheduler="constant",
                          precision="bf16", grad_clip=1.0, max_steps=10 ** 9,
-                         distributed_mode="fsdp" if world > 1 else "none",
+                         distributed_mode=(("zero3" if args.zero3 else "fsdp") if world > 1
+                                           else "none"),
                          skip_param_update_check=True,
                          cuda_graph=not args.no_graph, cuda_graph_warmup=2)
     trainer = Trainer(model, cfg)
@@ -179,6 +182,9 @@ def build_ours(world, args):
     if world == 1:
         mode = "single GPU, flat fp32-master fused AdamW" + (
             ", step replayed from a CUDA graph" if cfg.cuda_graph else "")
+    elif args.zero3:
+        mode = ("zero3 data parallel: per-block bf16 parameter shards gathered over NVLink one "
+                "block ahead, gradient reduce-scatter overlapped with backward, sharded fp32 AdamW")
     else:
         mode = ("zero2 data parallel: fused NVLink gradient reduce + sharded fp32 AdamW "
                 "(replicated bf16 params)" + (", step replayed from a CUDA graph"

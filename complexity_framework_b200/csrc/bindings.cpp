@@ -13,6 +13,7 @@
 #include "dist_fused.h"
 #include "tp_fused.h"
 #include "tp_decode.h"
+#include "fsdp.h"
 #include "ep_fused.h"
 #include "flash.h"
 #include "gemm_tc.h"
@@ -316,6 +317,31 @@ void tp_barrier(const std::vector<int64_t>& pads, int64_t rank, int64_t round, i
                                  at::cuda::getCurrentCUDAStream(),
                                  err_ptr(static_cast<int>(device)));
   raise_rc(rc, "tp_barrier");
+}
+
+// ZeRO-3: gather every rank's bf16 shard of a unit into this rank's full buffer.
+void fsdp_gather(const std::vector<int64_t>& shards, const std::vector<int64_t>& pads,
+                 int64_t rank, torch::Tensor& dst, int64_t shard, int64_t round,
+                 int64_t epoch) {
+  check_bf16_cuda(dst, "dst");
+  TORCH_CHECK(dst.is_contiguous(), "dst must be contiguous");
+  TORCH_CHECK(!shards.empty() && shards.size() <= cfb::kFsdpMaxRanks &&
+                  pads.size() == shards.size(), "1..8 ranks with one pad each");
+  TORCH_CHECK(dst.numel() >= shard * static_cast<int64_t>(shards.size()), "dst too small");
+  TORCH_CHECK(round >= 0 && round < 4, "pads hold 4 rounds");
+  cfb::FsdpPeers pp{};
+  pp.world = static_cast<int>(shards.size());
+  pp.rank = static_cast<int>(rank);
+  for (size_t i = 0; i < shards.size(); ++i) {
+    pp.shard[i] = reinterpret_cast<const __nv_bfloat16*>(shards[i]);
+    pp.pad[i] = reinterpret_cast<int*>(pads[i]);
+  }
+  const int dev = dst.get_device();
+  const c10::cuda::CUDAGuard guard(dst.device());
+  const int rc = cfb::fsdp_gather(pp, reinterpret_cast<__nv_bfloat16*>(dst.data_ptr()), shard,
+                                  static_cast<int>(round), static_cast<int>(epoch), num_sms(dev),
+                                  at::cuda::getCurrentCUDAStream(), err_ptr(dev));
+  raise_rc(rc, "fsdp_gather");
 }
 
 // out = residual + sum over ranks of their partial buffers (decode tensor parallelism).
@@ -674,6 +700,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_rs_finish", &tp_rs_finish);
   m.def("tp_barrier", &tp_barrier);
   m.def("tp_allreduce", &tp_allreduce);
+  m.def("fsdp_gather", &fsdp_gather);
   m.def("ep_gather_combine", &ep_gather_combine);
   m.def("gemm", &gemm, "tcgen05 GEMM with fused epilogues", py::arg("A"), py::arg("a_mn"),
         py::arg("B"), py::arg("b_mn"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epi"),

@@ -3,7 +3,9 @@
 The work happens in the flat-buffer optimizer (``training.optim.FusedAdamW``):
 ``ddp`` all-reduces each flat gradient buffer once per step, ``fsdp`` (ZeRO-2)
 reduce-scatters it, updates the fp32 master shard and all-gathers the bf16
-parameters.  These helpers keep the call sites of
+parameters; ``FULL_SHARD`` selects ZeRO-3 (``parallel/fsdp.py``: parameters
+sharded per block, gathered one block ahead, gradients reduce-scattered
+during backward).  These helpers keep the call sites of
 complexity/parallel/data_parallel.py:79-271 (``wrap_model_fsdp``,
 ``simple_ddp``, ``GradientAccumulator``, ``ShardingMode``) working: they tag
 the model with its data-parallel mode and broadcast rank 0's weights.
@@ -46,7 +48,13 @@ def wrap_model_fsdp(model: nn.Module, sharding_mode: ShardingMode = ShardingMode
     dtype = {PrecisionMode.BF16: torch.bfloat16, PrecisionMode.FP16: torch.float16,
              PrecisionMode.FP32: torch.float32}[PrecisionMode(precision)]
     model = model.to(dtype)
-    model.dp_mode = "ddp" if ShardingMode(sharding_mode) is ShardingMode.NO_SHARD else "fsdp"
+    mode = ShardingMode(sharding_mode)
+    # FULL_SHARD: parameters, gradient owners and optimizer state sharded per
+    # block (ZeRO-3, parallel/fsdp.py, installed by the Trainer);
+    # SHARD_GRAD_OP / HYBRID_SHARD: replicated bf16 parameters with sharded
+    # optimizer state (ZeRO-2, the fused NVLink reduce + AdamW path)
+    model.dp_mode = {ShardingMode.NO_SHARD: "ddp",
+                     ShardingMode.FULL_SHARD: "zero3"}.get(mode, "fsdp")
     model.dp_group = process_group
     broadcast_parameters(model, process_group)
     return model

@@ -44,7 +44,7 @@ class TrainingConfig:
     log_dir: str = "logs"
     num_workers: int = 4
     pin_memory: bool = True
-    distributed_mode: str = "auto"  # auto | none | ddp | fsdp
+    distributed_mode: str = "auto"  # auto | none | ddp | fsdp (ZeRO-2) | zero3
 
     def __post_init__(self) -> None:
         checks = (
@@ -63,8 +63,8 @@ class TrainingConfig:
             (self.log_steps > 0, "log_steps must be positive"),
             (self.eval_steps >= 0, "eval_steps must be non-negative"),
             (self.num_workers >= 0, "num_workers must be non-negative"),
-            (self.distributed_mode in ("auto", "none", "ddp", "fsdp"),
-             "distributed_mode must be auto, none, ddp or fsdp"),
+            (self.distributed_mode in ("auto", "none", "ddp", "fsdp", "zero3"),
+             "distributed_mode must be auto, none, ddp, fsdp or zero3"),
         )
         for ok, msg in checks:
             if not ok:

@@ -59,7 +59,9 @@ class Trainer:
         self.model = model.to(device=self.device, dtype=dtype)
         mode = self.config.distributed_mode
         if mode == "auto":
-            mode = ("fsdp" if self.config.use_fsdp else "ddp") if self.world > 1 else "none"
+            tagged = getattr(self.model, "dp_mode", None)  # set by wrap_model_fsdp / simple_ddp
+            mode = ((tagged or ("fsdp" if self.config.use_fsdp else "ddp"))
+                    if self.world > 1 else "none")
         self.distributed_mode = mode
         self.sp_ws = getattr(self.model, "sp_ws", None)
         if self.sp_ws is not None:
@@ -71,6 +73,16 @@ class Trainer:
             mode = "none"
         if self.world > 1:
             self._broadcast_parameters(process_group)
+        self.zero3 = None
+        if mode == "zero3":
+            # parameters, gradients' owners and optimizer state sharded per block
+            from ..parallel.fsdp import ShardedModel
+
+            if self.world == 1:
+                mode = "none"
+            else:
+                self.zero3 = ShardedModel(self.model, process_group)
+        self.distributed_mode = mode
         self.optimizer = self._build_optimizer(process_group, mode)
         sched_opt = getattr(self.optimizer, "optimizer", self.optimizer)
         self.scheduler = build_scheduler(sched_opt, kind=self.config.lr_scheduler,
@@ -96,6 +108,13 @@ class Trainer:
         adalomo, musgd, adam, sgd) -> that optimizer behind a bucketed all-reduce."""
         cfg = self.config
         kind = cfg.optimizer_type.lower()
+        if mode == "zero3":
+            from ..parallel.fsdp import Zero3AdamW
+
+            if kind != "adamw":
+                raise ValueError("zero3 sharding supports the adamw optimizer")
+            return Zero3AdamW(self.zero3, lr=cfg.learning_rate, betas=(0.9, 0.95),
+                              weight_decay=cfg.weight_decay)
         if kind == "adamw":
             groups = default_param_groups(self.model, cfg.weight_decay)
             return FusedAdamW(groups, lr=cfg.learning_rate, betas=(0.9, 0.95),
@@ -209,6 +228,10 @@ class Trainer:
 
     # ------------------------------------------------- canary update check
     def _snapshot(self):
+        if self.zero3 is not None:  # parameters live in per-rank shards between steps
+            us = self.zero3.all_units()
+            return [(u.shard_buf, u.shard_buf.reshape(-1)[:64].clone())
+                    for u in (us[0], us[len(us) // 2], us[-1])]
         ps = [p for p in self.model.parameters() if p.requires_grad]
         picks = [ps[0], ps[len(ps) // 2], ps[-1]]
         return [(p, p.detach().reshape(-1)[:64].clone()) for p in picks]

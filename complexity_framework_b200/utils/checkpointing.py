@@ -38,6 +38,13 @@ def gather_full_state_dict(model: torch.nn.Module) -> Tuple[Dict[str, torch.Tens
     on, rank, _ = _dist()
     if on:
         dist.barrier()
+    z3 = getattr(model, "zero3", None)
+    if z3 is not None:  # ZeRO-3: gather every unit first (collective)
+        with z3.summon_full_params():
+            # copies: the gathered buffers are freed when the context exits
+            sd = {k: v.detach().to("cpu", copy=True).contiguous()
+                  for k, v in model.state_dict().items()}
+        return (sd if rank == 0 else {}), rank == 0
     out = {}
     for k, v in model.state_dict().items():
         if hasattr(v, "full_tensor"):
@@ -138,7 +145,11 @@ class CheckpointManager:
         _, rank, _ = _dist()
         path = Path(path)
         ck = torch.load(path / "checkpoint.pt", map_location=map_location, weights_only=False)
-        model.load_state_dict(ck["model"], strict=False)
+        z3 = getattr(model, "zero3", None)
+        if z3 is not None:
+            z3.load_full_state_dict(ck["model"])
+        else:
+            model.load_state_dict(ck["model"], strict=False)
         if scheduler is not None and ck.get("scheduler") is not None:
             scheduler.load_state_dict(ck["scheduler"])
         opt_path = path / f"optimizer_rank{rank}.pt"

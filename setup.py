@@ -26,6 +26,7 @@ SOURCES = [
     "pack.cu",
     "moe_grouped.cu",
     "tp_decode.cu",
+    "fsdp.cu",
 ]
 
 # Link the shared system libstdc++ (the one libtorch uses).  The compiler wrapper

@@ -146,3 +146,60 @@ def test_fused_dp_graph_replay_matches_eager_two_gpus():
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     diffs = dict(q.get() for _ in range(2))
     assert max(diffs.values()) < 1e-2, diffs
+
+
+def _zero3_body(rank, world, port, q):
+    """ZeRO-3 over NVLink (per-block shards, gathers one block ahead, gradient
+    reduce-scatter during backward) trains like the ZeRO-2 fused path."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", rank))
+    from complexity_framework_b200 import ComplexityModel, ModelConfig
+    from complexity_framework_b200.ops import check_errors
+    from complexity_framework_b200.training import Trainer, TrainingConfig
+
+    cfg = dict(hidden_size=256, num_hidden_layers=3, num_attention_heads=4, num_key_value_heads=2,
+               vocab_size=2048, intermediate_size=256, shared_intermediate_size=512,
+               num_experts=4, top_k=2, max_position_embeddings=256)
+    batches = [torch.randint(0, 2048, (4, 128), generator=torch.Generator().manual_seed(10 * rank + i))
+               for i in range(4)]
+    res, losses = [], []
+    for mode in ("fsdp", "zero3"):
+        torch.manual_seed(0)
+        tr = Trainer(ComplexityModel(ModelConfig(**cfg)),
+                     TrainingConfig(learning_rate=1e-3, warmup_steps=0, lr_scheduler="constant",
+                                    grad_clip=1.0, distributed_mode=mode,
+                                    skip_param_update_check=False))
+        assert (tr.zero3 is not None) == (mode == "zero3")
+        if tr.zero3 is not None:
+            assert tr.zero3.fused
+        ls = [tr.train_step(b) for b in batches]
+        losses.append(ls)
+        if tr.zero3 is not None:
+            sd = tr.zero3.full_state_dict()
+            res.append(torch.cat([sd[n].float().reshape(-1) for n, _ in
+                                  tr.model.named_parameters()]))
+        else:
+            res.append(torch.cat([p.detach().float().reshape(-1) for p in tr.model.parameters()]))
+    torch.cuda.synchronize()
+    check_errors(rank)
+    q.put((rank, (res[0] - res[1]).abs().max().item(),
+           max(abs(a - b) for a, b in zip(*losses))))
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_zero3_matches_zero2_two_gpus():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_zero3_body, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = dict((r, (d, l)) for r, d, l in (q.get() for _ in range(2)))
+    for r, (d, l) in res.items():
+        assert d < 2e-2 and l < 2e-2, (r, d, l)
