@@ -131,6 +131,8 @@ __global__ void moe_scatter_k(const int64_t* __restrict__ routes, int64_t n, int
     row_token[pos] = static_cast<int>(t);
     row_weight[pos] = slot_w[a / T];
     token_pos[a] = pos;
+  } else if (a < n) {
+    token_pos[a] = -1;  // an assignment outside [0, E) has no row
   }
 }
 
@@ -172,6 +174,7 @@ __global__ void moe_combine_k(const __nv_bfloat16* __restrict__ src, const int* 
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int j = 0; j < k; ++j) {
       const int pos = token_pos[j * T + t];
+      if (pos < 0) continue;  // an assignment without a row contributes nothing
       const uint4 v = reinterpret_cast<const uint4*>(src + static_cast<int64_t>(pos) * H)[c];
       const uint32_t* w = reinterpret_cast<const uint32_t*>(&v);
 #pragma unroll

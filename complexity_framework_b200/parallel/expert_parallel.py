@@ -65,7 +65,7 @@ class ExpertParallelRouted(nn.Module):
             setattr(self, name, p)
 
     def forward(self, flat_x: torch.Tensor, routes: torch.Tensor,
-                route_weights: torch.Tensor) -> torch.Tensor:
+                route_weights: torch.Tensor, **unused) -> torch.Tensor:
         k, T = routes.shape
         H = flat_x.shape[1]
         P, El = self.P, self.E_local

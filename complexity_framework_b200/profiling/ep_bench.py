@@ -5,9 +5,10 @@
 
 Times forward + backward of the routed experts of one TR-Hash layer
 (E = 8 experts of width 512, top-2, H = 896, 16384 tokens per rank), CUDA
-events, max over ranks:
-  * fused : ``parallel.ep_fused.FusedExpertParallelRouted`` (pull-based P2P
-            dispatch / combine, tcgen05 SwiGLU GEMM pair per local expert)
+events, max over ranks, SM clocks sampled during each timed loop:
+  * fused : ``parallel.ep_fused.FusedExpertParallelRouted`` (token ids gathered
+            once, device plan, pull-based P2P dispatch / combine, grouped
+            tcgen05 GEMMs over the local experts)
   * nccl  : ``parallel.expert_parallel.ExpertParallelRouted`` (all_to_all_single
             + index_select / index_add, matmuls per local expert)
 """
@@ -45,23 +46,35 @@ def main():
     nccl = ExpertParallelRouted(eng, None).cuda()
 
     def run(mod):
-        y = mod(x, routes, eng._route_weights)
+        if mod is fused:  # routes of every rank follow from the token ids
+            y = mod(x, routes, eng._route_weights, token_ids=ids, route_fn=eng._routes)
+        else:
+            y = mod(x, routes, eng._route_weights)
         y.backward(gout)
 
     res = {"H": H, "E": E, "W": W, "top_k": k, "tokens_per_rank": T,
            "world": dist.get_world_size()}
+    from .timing import ClockSampler
+
+    iters = 300  # about a second per path: long enough for the clock sampler
+
     for name, mod in (("fused", fused), ("nccl", nccl)):
         for _ in range(3):
             run(mod)
         dist.barrier()
         torch.cuda.synchronize()
+        clocks = ClockSampler(torch.cuda.current_device())
+        if rank == 0:
+            clocks.start()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        for _ in range(10):
+        for _ in range(iters):
             run(mod)
         e.record()
         torch.cuda.synchronize()
-        ms = torch.tensor([s.elapsed_time(e) / 10], device="cuda")
+        if rank == 0:
+            res[name + "_clocks"] = clocks.stop()
+        ms = torch.tensor([s.elapsed_time(e) / iters], device="cuda")
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         res[name + "_fwd_bwd_ms"] = round(float(ms), 4)
     check_errors(torch.cuda.current_device())

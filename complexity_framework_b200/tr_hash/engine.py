@@ -382,7 +382,8 @@ class TRHashEngine(nn.Module):
         if ep is not None:
             # expert parallel: shared SwiGLU locally, routed experts via all-to-all
             routes = self._routes(token_ids).reshape(self.config.top_k, -1)
-            routed = ep(flat, routes, self._route_weights)
+            routed = ep(flat, routes, self._route_weights, token_ids=token_ids,
+                        route_fn=self._routes)
             out = (self._shared_ep(flat) + self.config.routed_output_scale * routed).view(B, S, H)
             return out if residual is None else residual + out
         if backend is TRHashBackend.CGGR:
