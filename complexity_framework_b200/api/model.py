@@ -13,10 +13,10 @@ from typing import Dict, Iterable, List, Optional, Sequence, Union
 
 import torch
 
-from .config.model_config import ModelConfig, get_preset
-from .data.tokenization import ChatTemplate, Message, Tokenizer, get_tokenizer
-from .inference.engine import GenerationConfig, InferenceEngine
-from .models.builder import ComplexityModel
+from ..config.model_config import ModelConfig, get_preset
+from ..data.tokenization import ChatTemplate, Message, Tokenizer, get_tokenizer
+from ..inference.engine import GenerationConfig, InferenceEngine
+from ..models.builder import ComplexityModel
 
 
 class Model:
@@ -76,10 +76,10 @@ class Model:
               seq_len: int = 256, lr: float = 3e-4, **cfg_kw) -> Dict:
         """Tokenise ``texts`` (strings, or a .txt/.jsonl path) into a temporary token
         shard and train on it with the framework Trainer."""
-        from .data.loader import TokenBatchLoader
-        from .data.streaming import iter_texts
-        from .data.token_shards import write_token_shard
-        from .training import Trainer, TrainingConfig
+        from ..data.loader import TokenBatchLoader
+        from ..data.streaming import iter_texts
+        from ..data.token_shards import write_token_shard
+        from ..training import Trainer, TrainingConfig
 
         if isinstance(texts, (str, Path)) and Path(texts).exists():
             texts = iter_texts([str(texts)])

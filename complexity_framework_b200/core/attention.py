@@ -157,11 +157,18 @@ class GroupedQueryAttention(nn.Module):
     def _project(self, x: torch.Tensor):
         kd = self.num_kv_heads * self.head_dim
         qd = self.num_heads * self.head_dim
+        if not self._plain_projections():  # quantised / adapted projection modules
+            return self.k_proj(x), self.q_proj(x), self.v_proj(x)
         kqv = F.linear(x, self.kqv_weight())
         return kqv.split((kd, qd, kd), -1)
 
+    def _plain_projections(self) -> bool:
+        return all(isinstance(getattr(m, "weight", None), torch.Tensor)
+                   for m in (self.k_proj, self.q_proj, self.v_proj, self.o_proj))
+
     def fused_eligible(self, x: torch.Tensor, attention_mask, past_key_value, use_cache) -> bool:
-        return (use_fused(x) and self.q_proj.weight.dtype == torch.bfloat16
+        return (use_fused(x) and self._plain_projections()
+                and self.q_proj.weight.dtype == torch.bfloat16
                 and attention_mask is None and past_key_value is None and not use_cache
                 and self.is_causal and self.sliding_window is None
                 and (self.attention_dropout == 0.0 or not self.training)
