@@ -14,6 +14,14 @@ inference.py, serve.py, convert.py, tokenize.py, profile.py, info.py):
     cfb profile {model,kernels,throughput}
     cfb plan [cluster plan flags]
     cfb info
+
+Grouped form (``cli/groups.py``): ``cfb train {run,resume,validate,create-config}``,
+``cfb inference {generate,chat,batch,benchmark}``, ``cfb tokenize {train,
+train-sentencepiece,extend,merge,encode,decode,count,preprocess,info,special-tokens,
+benchmark}``, ``cfb profile {model,gpu,throughput,attention,kernels}``,
+``cfb convert {...}``, ``cfb serve {start,benchmark-server,openai-proxy}``,
+``cfb info {version,model,config,tokens,benchmark-env}``, ``cfb quickstart``,
+``cfb shell``.
 """
 from __future__ import annotations
 
@@ -400,6 +408,10 @@ def build_parser() -> argparse.ArgumentParser:
 
 def main(argv: Optional[List[str]] = None) -> None:
     argv = list(sys.argv[1:] if argv is None else argv)
+    from .groups import dispatch
+
+    if dispatch(argv):  # cfb <group> <command> ... (train run, tokenize count, info env, ...)
+        return
     if argv and argv[0] == "train":
         return cmd_train(argv[1:])
     if argv and argv[0] == "plan":
