@@ -412,6 +412,12 @@ def main(argv: Optional[List[str]] = None) -> None:
 
     if dispatch(argv):  # cfb <group> <command> ... (train run, tokenize count, info env, ...)
         return
+    run_flat(argv)
+
+
+def run_flat(argv: List[str]) -> None:
+    """Run one of the flat commands (``cfb convert to-gguf ...``); grouped
+    commands that share a name with a flat one end here without re-dispatch."""
     if argv and argv[0] == "train":
         return cmd_train(argv[1:])
     if argv and argv[0] == "plan":

@@ -487,13 +487,13 @@ def _shell(argv: List[str]) -> None:
 
 def _flat(name: str) -> Callable[[List[str]], None]:
     def run(argv: List[str]) -> None:
-        flat.main([name] + argv)
+        flat.run_flat([name] + argv)
     return run
 
 
 def _flat_kind(name: str, kind: str) -> Callable[[List[str]], None]:
     def run(argv: List[str]) -> None:
-        flat.main([name, kind] + argv)
+        flat.run_flat([name, kind] + argv)
     return run
 
 
