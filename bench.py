@@ -2,6 +2,8 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     python bench.py --workload decode ...   (7B paged-KV serving, bench_decode.py)
+    python bench.py --workload ep1b|tp7b ... (1B expert-parallel / 7B tensor-parallel
+                                              training, bench_train_large.py)
 
 N > 1 is launched by torchrun (one process per GPU, NCCL).  Workload: the
 released 200M TR-GQA/TR-Hash architecture, random init, synthetic Zipf(1.1)
@@ -51,8 +53,9 @@ def parse():
     p.add_argument("--no-graph", action="store_true", help="run every step eagerly")
     p.add_argument("--zero3", action="store_true",
                    help="multi-GPU: ZeRO-3 (per-block parameter shards) instead of ZeRO-2")
-    p.add_argument("--workload", choices=("train", "decode"), default="train",
-                   help="train: the 200M pretraining headline; decode: 7B paged-KV serving")
+    p.add_argument("--workload", choices=("train", "decode", "ep1b", "tp7b"), default="train",
+                   help="train: the 200M pretraining headline; decode: 7B paged-KV serving; "
+                        "ep1b: 1B expert-parallel training; tp7b: 7B tensor-parallel training")
     return p.parse_args()
 
 
@@ -214,6 +217,14 @@ def main():
         import bench_decode
 
         return bench_decode.main(args, world, rank, local, sys.modules[__name__])
+    if args.workload in ("ep1b", "tp7b"):
+        sys.path.insert(0, ROOT)
+        import bench_train_large
+
+        bench_train_large.main(args, world, rank, local, sys.modules[__name__])
+        if world > 1:
+            dist.destroy_process_group()
+        return
     B, S, V = args.batch, args.seq, 32000
     try:
         build = build_ours if args.impl == "ours" else build_reference

@@ -141,6 +141,8 @@ class Trainer:
     def _broadcast_parameters(self, pg) -> None:
         src = dist.get_global_rank(pg, 0) if pg is not None else 0
         for p in self.model.parameters():
+            if getattr(p, "_ep_local", False):
+                continue  # expert-parallel shard: each rank owns different experts
             dist.broadcast(p.data, src=src, group=pg)
         for b in self.model.buffers():
             if b.is_floating_point():

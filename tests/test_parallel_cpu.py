@@ -176,6 +176,39 @@ def test_expert_parallel_matches_single():
     _run(2, _ep_body)
 
 
+def _ep_trainer_body(rank, world, tmp, mode):
+    """Trainer over an expert-parallel model: replicated parameters averaged over
+    ranks, expert shards kept rank-local (not overwritten by the start-up
+    broadcast) and averaged by 1/world; three AdamW steps with clipping equal
+    one process on the whole batch."""
+    from complexity_framework_b200.parallel import make_expert_parallel
+    from complexity_framework_b200.training import Trainer, TrainingConfig
+
+    ids_all = _ids(4, seed=11)
+    cfg = TrainingConfig(learning_rate=1e-3, warmup_steps=0, lr_scheduler="constant",
+                         precision="fp32", grad_clip=0.5, distributed_mode=mode,
+                         checkpoint_dir=tmp)
+    single = Trainer(_model(), cfg, device="cpu", process_group=dist.new_group([rank]))
+    for _ in range(3):
+        single.train_step(ids_all)
+    tr = Trainer(make_expert_parallel(_model(), dist.group.WORLD), cfg, device="cpu")
+    for _ in range(3):
+        tr.train_step(ids_all.chunk(world)[rank])
+    want = dict(single.model.named_parameters())
+    for n, p in tr.model.named_parameters():
+        if ".ep." in n:
+            ep = tr.model.layers[int(n.split(".")[1])].mlp.engine.ep
+            full = want[n.replace(".ep.", ".")][ep.lo:ep.lo + ep.E_local]
+            assert torch.allclose(p, full, atol=2e-5), n
+        else:
+            assert torch.allclose(p, want[n], atol=2e-5), n
+
+
+@pytest.mark.parametrize("mode", ["ddp", "fsdp"])
+def test_expert_parallel_trainer_matches_single(mode):
+    _run(2, _ep_trainer_body, mode)
+
+
 def _zero_body(rank, world, tmp, mode):
     from complexity_framework_b200.training import Trainer, TrainingConfig
 
