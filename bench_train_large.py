@@ -12,7 +12,9 @@ tcgen05 expert GEMMs (``parallel/ep_fused.py``), token ids gathered once per
 forward; the replicated parameters are data parallel (NCCL reduce-scatter,
 sharded fp32 AdamW, all-gather).  Per-GPU work is fixed ("weak").  The
 reference has no expert parallelism: its arm runs the same model under its
-own ``wrap_model_fsdp`` (N > 1) with every expert on every rank.
+own ``ClusterModel`` data parallel in DDP mode (N > 1) with every expert on
+every rank (its FSDP mode fails in its Triton grouped GEMM on this config:
+fp32 activations against bf16 expert weights).
 
 ``tp7b``: TR-MHA 7B, 32 layers, hidden 4096, 32 MHA heads (head_dim 128),
 shared SwiGLU 11008, 8 routed experts of width 512, top-2 modulo_cyclic, seq
@@ -45,12 +47,12 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 
 EP1B = dict(hidden_size=2048, num_hidden_layers=24, num_attention_heads=16,
-            num_key_value_heads=4, intermediate_size=256, shared_intermediate_size=5632,
+            num_key_value_heads=4, intermediate_size=16 * 256, shared_intermediate_size=5632,
             vocab_size=32000, num_experts=16, top_k=2, routing_strategy="token_id_balanced_hash",
             attention_type="gqa", mlp_type="tr_hash_engine", shared_expert=True,
             max_position_embeddings=2048)
 TP7B = dict(hidden_size=4096, num_hidden_layers=32, num_attention_heads=32,
-            num_key_value_heads=32, intermediate_size=512, shared_intermediate_size=11008,
+            num_key_value_heads=32, intermediate_size=8 * 512, shared_intermediate_size=11008,
             vocab_size=32000, num_experts=8, top_k=2, routing_strategy="modulo_cyclic",
             attention_type="mha", mlp_type="tr_hash_engine", shared_expert=True,
             max_position_embeddings=4096)
@@ -138,11 +140,16 @@ def build_reference(workload, world):
     autocast = True
     if workload == "ep1b":
         if world > 1:
-            from complexity.parallel import wrap_model_fsdp
+            # its FSDP arm (bf16 parameters) fails in the CGGR Triton grouped GEMM
+            # on this config (fp32 activations against bf16 expert weights), so
+            # the reference's DDP mode runs: fp32 parameters under bf16 autocast
+            from complexity.parallel.cluster import ClusterConfig, ClusterModel
 
-            model = wrap_model_fsdp(model)
-            mode = ("reference has no expert parallelism: fsdp2 full_shard (wrap_model_fsdp, "
-                    "bf16 params), every expert on every rank")
+            cluster = ClusterModel(model, ClusterConfig(tp_size=1, pp_size=1, dp_size=world,
+                                                        use_ddp=True))
+            model = cluster.model
+            mode = ("reference has no expert parallelism: ClusterModel(dp_size=N, use_ddp=True) "
+                    "(fp32 params + bf16 autocast), every expert on every rank")
         else:
             mode = "single device (fp32 params + bf16 autocast, reference Trainer default)"
     else:
@@ -157,7 +164,8 @@ def build_reference(workload, world):
         autocast = False
         mode = (f"reference ClusterModel(tp_size={world}): attention sharded, FFN replicated, "
                 "bf16 params")
-    head = model.lm_head if getattr(model, "lm_head", None) is not None else model.embed_tokens
+    inner = getattr(model, "module", model)
+    head = inner.lm_head if getattr(inner, "lm_head", None) is not None else inner.embed_tokens
     decay = [p for n, p in model.named_parameters() if "norm" not in n and "bias" not in n]
     nodecay = [p for n, p in model.named_parameters() if "norm" in n or "bias" in n]
     opt = torch.optim.AdamW([{"params": decay, "weight_decay": 0.1},

@@ -11,6 +11,7 @@ from __future__ import annotations
 from dataclasses import dataclass, field
 from typing import Any, Dict, Optional
 
+import torch.nn.functional as F
 import torch.nn as nn
 
 from ..tr_hash import (AttentionBackbone, TRHashBackend, TRHashEngine, TRHashEngineConfig,
@@ -140,8 +141,23 @@ class TRHashEngineMLP(nn.Module):
         cfg = eng.config
         scales = fused.route_scales(token_ids, eng._active_route_table, eng._route_weights,
                                     cfg.num_experts, cfg.routed_output_scale)
-        w_gu, w_down = eng.packed_weights()
-        return TPMLPFn.apply(h_shard, w_gu, w_down, scales, residual, ws, name, cfg.shared_width,
+        sw = cfg.shared_width
+        wg, wu, wd = eng._shared_weights()
+        if wg is not None and wg.shape[0] % 128:
+            # a TP shard of the shared width that is not a whole number of the
+            # epilogue's 128-column gate|up blocks (11008 / 8 = 1376): zero rows
+            # of gate/up and zero columns of down pad it, so the padded
+            # activations are silu(0) * 0 = 0 and add nothing
+            pad = -wg.shape[0] % 128
+            wg, wu = F.pad(wg, (0, 0, 0, pad)), F.pad(wu, (0, 0, 0, pad))
+            wd = F.pad(wd, (0, pad))
+            sw = wg.shape[0]
+            w_gu = fused.pack_gate_up(wg, wu, eng.expert_gate, eng.expert_up)
+            w_down = fused.pack_down(wd, eng.expert_down)
+        else:
+            sw = wg.shape[0] if wg is not None else 0
+            w_gu, w_down = eng.packed_weights()
+        return TPMLPFn.apply(h_shard, w_gu, w_down, scales, residual, ws, name, sw,
                              cfg.expert_width, cfg.num_experts, cfg.shared_output_scale)
 
     def set_top_k_primary_weight(self, weight: float) -> None:

@@ -153,7 +153,7 @@ def test_fused_sequence_parallel_model_two_gpus():
         assert not bad, (r, bad)
 
 
-def _trainer_body(rank, world, port, q):
+def _trainer_body(rank, world, port, q, shared=512):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -167,7 +167,7 @@ def _trainer_body(rank, world, port, q):
 
     cfg = ModelConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=4,
                       num_key_value_heads=2, vocab_size=2048, intermediate_size=256,
-                      shared_intermediate_size=512, num_experts=4, top_k=2,
+                      shared_intermediate_size=shared, num_experts=4, top_k=2,
                       routing_strategy="token_id_multi_hash", max_position_embeddings=256)
     tc = dict(learning_rate=2e-3, warmup_steps=0, lr_scheduler="constant",
               skip_param_update_check=True)
@@ -204,11 +204,12 @@ def _trainer_body(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_trainer_fused_sequence_parallel_two_gpus():
+@pytest.mark.parametrize("shared", [512, 384])  # 384 / 2 = 192: shard padded to 256
+def test_trainer_fused_sequence_parallel_two_gpus(shared):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_trainer_body, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_trainer_body, args=(r, 2, port, q, shared)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
