@@ -36,8 +36,24 @@ class SFTDataset:
         return len(self.rows)
 
     def __getitem__(self, i):
-        ids, labels = encode_chat(self.tok, self.rows[i]["messages"], self.tpl, self.max_len)
+        row = self.rows[i]
+        if "messages" not in row and "prompt" in row and "completion" in row:
+            return encode_prompt_completion(self.tok, row["prompt"], row["completion"],
+                                            self.max_len)
+        ids, labels = encode_chat(self.tok, row["messages"], self.tpl, self.max_len)
         return ids, labels
+
+
+def encode_prompt_completion(tok, prompt: str, completion: str, max_len: Optional[int] = None):
+    """Raw prompt/completion record: labels on the completion (and EOS) only."""
+    p, c = list(tok.encode(prompt)), list(tok.encode(completion))
+    eos = getattr(tok, "eos_token_id", None)
+    if eos is not None:
+        c.append(int(eos))
+    ids, labels = p + c, [IGNORE_INDEX] * len(p) + c
+    if max_len is not None:
+        ids, labels = ids[:max_len], labels[:max_len]
+    return ids, labels
 
 
 def shift_labels(labels: torch.Tensor) -> torch.Tensor:
@@ -198,6 +214,12 @@ def main(argv=None) -> Dict:
     ap.add_argument("--early-stopping-min-epochs", type=int, default=1)
     ap.add_argument("--save-best", action="store_true")
     ap.add_argument("--resume", default=None, help="'auto' or a checkpoint directory")
+    ap.add_argument("--max-steps", type=int, default=0,
+                    help="stop after this many optimizer steps (0 = run the epochs)")
+    ap.add_argument("--lora-targets", default=None,
+                    help="comma-separated module names for LoRA (default: the standard set)")
+    ap.add_argument("--merge-lora", action="store_true",
+                    help="merge the trained LoRA deltas and save a full checkpoint in final/")
     a = ap.parse_args(argv)
     if (a.curriculum is None) != (a.curriculum_stage is None):
         raise SystemExit("--curriculum and --curriculum-stage go together")
@@ -220,7 +242,10 @@ def _run(a, rank, world, device, ComplexityModel, TrainingConfig, LoRAConfig, ap
     torch.manual_seed(a.seed)
     model = ComplexityModel.from_pretrained(a.model)
     if a.lora_rank > 0:
-        apply_lora(model, LoRAConfig(r=a.lora_rank, alpha=a.lora_alpha))
+        lcfg = LoRAConfig(r=a.lora_rank, alpha=a.lora_alpha)
+        if a.lora_targets:
+            lcfg.target_modules = [t.strip() for t in a.lora_targets.split(",") if t.strip()]
+        apply_lora(model, lcfg)
     ds = SFTDataset(a.data, tok, a.seq_len, a.chat_format)
     pad = tok.pad_token_id or 0
     keep = list(range(len(ds)))
@@ -247,7 +272,11 @@ def _run(a, rank, world, device, ComplexityModel, TrainingConfig, LoRAConfig, ap
         weighted = False
     steps_per_epoch = len(rank_epoch_items(list(range(len(items))), rank, world,
                                            a.batch_size)) // a.batch_size
+    if a.max_steps > 0 and steps_per_epoch > 0:
+        a.epochs = max(a.epochs, -(-a.max_steps // steps_per_epoch))
     total_steps = steps_per_epoch * a.epochs
+    if a.max_steps > 0:
+        total_steps = min(total_steps, a.max_steps)
     cfg = TrainingConfig(max_steps=total_steps, learning_rate=a.lr,
                          warmup_steps=max(1, total_steps // 20), lr_scheduler="cosine",
                          precision=a.precision, weight_decay=0.0, checkpoint_dir=a.output,
@@ -313,12 +342,17 @@ def _run(a, rank, world, device, ComplexityModel, TrainingConfig, LoRAConfig, ap
             last = tr.train_step(ids, lab)
             tr._emit("on_step_end", tr.global_step, {"loss": last})
             sft["step_in_epoch"] = s + 1
+            if a.max_steps > 0 and tr.global_step >= total_steps:
+                stop = True
+                break
             if a.eval_steps > 0 and tr.global_step % a.eval_steps == 0:
                 if evaluate_and_select(epoch + (s + 1) / steps_per_epoch):
                     stop = True
                     break
         if stop:
-            sft["stopped_early"] = True
+            sft["stopped_early"] = tr.global_step < total_steps
+            if not sft["stopped_early"]:
+                _save_sft_state(tr, "epoch", dict(sft))
             break
         sft["epoch"], sft["step_in_epoch"] = epoch + 1, 0
         if a.eval_steps <= 0 and evaluate_and_select(epoch + 1):
@@ -340,7 +374,11 @@ def _run(a, rank, world, device, ComplexityModel, TrainingConfig, LoRAConfig, ap
         if a.lora_rank > 0:
             torch.save(lora_state_dict(model), out / "adapter.pt")
         (out / "sft_summary.json").write_text(json.dumps(summary, indent=2, default=float))
-    if a.lora_rank <= 0:
+    if a.lora_rank > 0 and a.merge_lora:
+        from .lora import merge_lora
+
+        merge_lora(model)
+    if a.lora_rank <= 0 or a.merge_lora:
         model.save_pretrained(out / "final")
     return summary
 

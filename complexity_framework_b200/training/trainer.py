@@ -165,7 +165,7 @@ class Trainer:
         after the warm-up steps (``training/graph_step.py``); the returned
         device scalar is then overwritten by the next step.
         """
-        if self.config.cuda_graph:
+        if self.config.cuda_graph and not isinstance(input_ids, dict):
             if self._graphed is None:
                 from .graph_step import GraphedTrainStep
 
@@ -177,12 +177,22 @@ class Trainer:
     def _train_step_eager(self, input_ids: torch.Tensor, labels: Optional[torch.Tensor] = None, *,
                           sync: bool = True):
         self.model.train()
-        ids = input_ids.to(self.device, non_blocking=True)
-        lab = labels.to(self.device, non_blocking=True) if labels is not None else None
+        if isinstance(input_ids, dict):
+            # structured batch (e.g. contrastive pairs): tensors moved as a whole,
+            # the loss callable receives the dict
+            ids = {k: (v.to(self.device, non_blocking=True) if torch.is_tensor(v) else v)
+                   for k, v in input_ids.items()}
+            n_tok = sum(int(v.numel()) for k, v in ids.items()
+                        if k.endswith("input_ids") and torch.is_tensor(v))
+            lab = None
+        else:
+            ids = input_ids.to(self.device, non_blocking=True)
+            lab = labels.to(self.device, non_blocking=True) if labels is not None else None
+            n_tok = ids.numel()
         loss = self.compute_loss(ids, lab)
         loss.backward()
         self._finish_step()
-        self.total_tokens += ids.numel() * self.world
+        self.total_tokens += n_tok * self.world
         out = loss.detach()
         if self.sp_ws is not None:
             # each TP rank returned its share of the global mean loss
@@ -252,6 +262,8 @@ class Trainer:
     @staticmethod
     def _split_batch(batch):
         if isinstance(batch, dict):
+            if "input_ids" not in batch:
+                return batch, None  # structured batch for a custom compute_loss
             return batch["input_ids"], batch.get("labels")
         if isinstance(batch, (tuple, list)):
             return batch[0], (batch[1] if len(batch) > 1 else None)
