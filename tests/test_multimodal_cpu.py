@@ -2,8 +2,9 @@
 import torch
 
 from complexity_framework_b200 import ComplexityModel, ModelConfig
-from complexity_framework_b200.multimodal import (AudioEncoder, EncoderConfig, VideoEncoder,
-                                                  VisionEncoder, VisionLanguageModel)
+from complexity_framework_b200.multimodal.encoders import (AudioEncoder, EncoderConfig, VideoEncoder,
+                                                           VisionEncoder)
+from complexity_framework_b200.multimodal.fusion import VisionLanguageModel
 
 
 def test_encoders_shapes():
