@@ -13,6 +13,10 @@ from .losses import distribution_focal_loss, quality_focal_loss
 from .model import TRHashObjectDetector
 from .ops import box_iou, class_aware_nms, complete_iou, complete_iou_loss, greedy_nms
 from .trainer import DetectorTrainer, DetectorTrainingConfig
+from .metrics import DetectionMetricsAccumulator, evaluate_predictions
+from .checkpointing import load_training_state, save_training_state
+from .distributed import DistributedContext, DistributedEvalSampler
+from .train import DetectorRunConfig, train_detector
 
 __all__ = [
     "TRHashDetectorConfig", "TRHashObjectDetector", "box_iou", "class_aware_nms",
@@ -23,5 +27,7 @@ __all__ = [
     "restore_detector_boxes", "ModelEMA", "evaluate_detections", "save_detector_checkpoint",
     "load_detector_checkpoint", "export_detector_torchscript", "DetectorTrainer",
     "DetectorTrainingConfig", "DetectionAugment", "AugmentedDataset", "mosaic",
-    "horizontal_flip", "random_scale", "color_jitter",
+    "horizontal_flip", "random_scale", "color_jitter", "DetectionMetricsAccumulator",
+    "evaluate_predictions", "save_training_state", "load_training_state", "DistributedContext",
+    "DistributedEvalSampler", "DetectorRunConfig", "train_detector",
 ]
