@@ -267,9 +267,21 @@ class TRHashTextToImage(nn.Module):
         return self.codec.decode(z).clamp(-1, 1) if self.codec is not None else z
 
 
+def sample_edit_condition_dropout(batch: int, *, caption_dropout: float, source_dropout: float,
+                                  device, generator: Optional[torch.Generator] = None):
+    """(drop_text, drop_source) masks for classifier-free-guidance training of
+    edits.  An instruction means nothing without its source image, so dropping
+    the source drops the text too (the unconditional branch); dropping only the
+    text keeps the image-only branch."""
+    dt = torch.rand(batch, device=device, generator=generator) < caption_dropout
+    ds = torch.rand(batch, device=device, generator=generator) < source_dropout
+    return dt | ds, ds
+
+
 @dataclass
 class TRHashImageEditConfig(TRHashImageConfig):
     in_channels_extra: int = 4
+    source_drop_prob: float = 0.0    # > 0: also train the unconditional (no source) branch
 
 
 class TRHashImageEditor(TRHashTextToImage):
@@ -288,8 +300,15 @@ class TRHashImageEditor(TRHashTextToImage):
             if target_latents is None:
                 target_latents = self.codec.encode(target)
         B = target_latents.shape[0]
-        drop = torch.rand(B, device=target_latents.device) < self.config.cond_drop_prob
-        ctx = self.text_context(text_ids, text_states, drop if self.training else None)
+        drop_text = drop_src = None
+        if self.training:
+            drop_text, drop_src = sample_edit_condition_dropout(
+                B, caption_dropout=self.config.cond_drop_prob,
+                source_dropout=getattr(self.config, "source_drop_prob", 0.0),
+                device=target_latents.device)
+            # a dropped source is an all-zero latent (the null image condition)
+            source_latents = source_latents * (~drop_src).to(source_latents.dtype)[:, None, None, None]
+        ctx = self.text_context(text_ids, text_states, drop_text)
         return {"loss": self.flow_loss(target_latents, ctx, extra=source_latents)}
 
     @torch.no_grad()

@@ -145,3 +145,59 @@ def test_vlm_training_stages_checkpoints_and_resume(tmp_path):
     assert s2["steps"] == 8 and s2["log"][0]["step"] == 7
     with pytest.raises(ValueError):
         prune_checkpoints(tmp_path / "run", 0)
+
+
+# ------------------------------------------------------------ image models
+def _img_cfg(cls, **kw):
+    base = dict(image_size=32, hidden_size=32, num_layers=1, num_heads=2, shared_width=64,
+                expert_width=32, text_vocab_size=256, text_dim=32, cond_drop_prob=0.2)
+    base.update(kw)
+    return cls(**base)
+
+
+def test_edit_condition_dropout_is_joint():
+    from complexity_framework_b200.generative.image import sample_edit_condition_dropout
+
+    g = torch.Generator().manual_seed(0)
+    dt, ds = sample_edit_condition_dropout(4000, caption_dropout=0.1, source_dropout=0.2,
+                                           device="cpu", generator=g)
+    assert bool((dt | ~ds).all())                 # a dropped source always drops the text
+    assert 0.25 < float(dt.float().mean()) < 0.31   # 1 - 0.9 * 0.8 = 0.28
+
+
+def test_image_and_edit_training_drivers(tmp_path):
+    from complexity_framework_b200.generative.image import (FrozenAutoencoderKL,
+                                                            TRHashImageEditConfig,
+                                                            TRHashImageEditor, TRHashImageConfig,
+                                                            TRHashTextToImage)
+    from complexity_framework_b200.generative.image_training import (ImageTrainConfig,
+                                                                     tokenize_captions,
+                                                                     train_image_model)
+
+    ids, mask = tokenize_captions(ByteTok(), ["ab", ""], 8)
+    assert ids.shape == (2, 2) and mask.tolist() == [[True, True], [True, False]]
+    torch.manual_seed(0)
+    m = TRHashTextToImage(_img_cfg(TRHashImageConfig), FrozenAutoencoderKL(channels=16))
+    imgs = torch.rand(6, 3, 32, 32) * 2 - 1
+    batches = [(imgs[:3], ["red", "blue", "red"]), (imgs[3:], ["blue", "red", "blue"])]
+    cfg = ImageTrainConfig(max_steps=5, sft_steps=2, sft_lr_scale=0.5, save_steps=2,
+                           keep_checkpoints=2, log_steps=1, bf16=False, warmup_steps=1,
+                           learning_rate=1e-3, output=str(tmp_path / "t2i"))
+    s = train_image_model(m, ByteTok(), batches, cfg, sft_batches=batches[:1])
+    assert [e["stage"] for e in s["log"]] == ["pretrain"] * 3 + ["sft"] * 2
+    assert s["log"][3]["lr"] < s["log"][2]["lr"]      # SFT runs at a scaled learning rate
+    assert sorted(p.name for p in (tmp_path / "t2i").glob("step_*")) == ["step_0000004",
+                                                                         "step_0000005"]
+    s2 = train_image_model(TRHashTextToImage(_img_cfg(TRHashImageConfig),
+                                             FrozenAutoencoderKL(channels=16)),
+                           ByteTok(), batches, ImageTrainConfig(**{**cfg.__dict__,
+                                                                   "max_steps": 6,
+                                                                   "resume": True}))
+    assert s2["steps"] == 6 and s2["log"][0]["step"] == 6
+    ed = TRHashImageEditor(_img_cfg(TRHashImageEditConfig, source_drop_prob=0.3),
+                           FrozenAutoencoderKL(channels=16))
+    eb = [(imgs[:3], imgs[3:], ["make it red", "blue", "flip"])]
+    s3 = train_image_model(ed, ByteTok(), eb, ImageTrainConfig(
+        max_steps=2, bf16=False, warmup_steps=1, save_steps=10, log_steps=1,
+        output=str(tmp_path / "edit")), edit=True)
+    assert s3["steps"] == 2 and all(torch.isfinite(torch.tensor(e["loss"])) for e in s3["log"])
