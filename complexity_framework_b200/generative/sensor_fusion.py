@@ -57,6 +57,7 @@ class TRHashSensorFusionConfig:
     skeleton_joints: int = 17
     skeleton_coordinates: int = 3
     sequence_tokens: int = 32
+    modality_gate: bool = False   # learned per-sample gate over the stream heads
 
     @property
     def tokens_per_stream(self) -> int:
@@ -108,6 +109,8 @@ class TRHashSensorFusionClassifier(nn.Module):
         self.drop = nn.Dropout(c.classifier_dropout)
         self.head = nn.Linear(H, c.num_classes)
         self.stream_heads = nn.ModuleDict({m: nn.Linear(H, c.num_classes) for m in SENSOR_MODALITIES})
+        if c.modality_gate:
+            self.gate = nn.Linear(H, 1)
 
     def _visual_tokens(self, m: str, clip: torch.Tensor) -> torch.Tensor:
         """[B, T, C, H, W] -> [B, grid^2, hidden]."""
@@ -129,7 +132,12 @@ class TRHashSensorFusionClassifier(nn.Module):
         return F.adaptive_avg_pool1d(x.transpose(1, 2), self.config.sequence_tokens).transpose(1, 2)
 
     def forward(self, inputs: Mapping[str, torch.Tensor],
-                labels: Optional[torch.Tensor] = None) -> Dict[str, torch.Tensor]:
+                labels: Optional[torch.Tensor] = None,
+                masks: Optional[Mapping[str, torch.Tensor]] = None) -> Dict[str, torch.Tensor]:
+        """``inputs``: the streams present in the batch; ``masks`` (optional):
+        per-stream [B] bools marking the samples that really have that stream
+        (absent samples carry zeros and are masked out of attention, pooling
+        and the stream heads).  Every sample needs at least one stream."""
         c = self.config
         toks, ids, spans = [], [], []
         for mi, m in enumerate(SENSOR_MODALITIES):
@@ -145,15 +153,45 @@ class TRHashSensorFusionClassifier(nn.Module):
         if not toks:
             raise ValueError(f"no sensor stream given; expected some of {SENSOR_MODALITIES}")
         x = torch.cat(toks, 1)
-        route = torch.cat(ids).unsqueeze(0).expand(x.shape[0], -1)
+        B = x.shape[0]
+        present = torch.stack([
+            (masks[m].to(x.device).bool() if masks is not None and m in masks
+             else torch.ones(B, dtype=torch.bool, device=x.device)) for m, _, _ in spans], 1)
+        if not bool(present.any(1).all()):
+            raise ValueError("every sample must expose at least one sensor stream")
+        tok_keep = torch.cat([present[:, i:i + 1].expand(-1, n)
+                              for i, (_, _, n) in enumerate(spans)], 1)
+        attn = None
+        if not bool(tok_keep.all()):
+            attn = torch.zeros(B, 1, 1, x.shape[1], device=x.device, dtype=x.dtype)
+            attn = attn.masked_fill(~tok_keep[:, None, None, :], float("-inf"))
+        route = torch.cat(ids).unsqueeze(0).expand(B, -1)
         for blk in self.blocks:
-            x = blk(x, route)
+            x = blk(x, route, attn)
         x = self.norm(x)
-        fused = self.head(self.drop(x.mean(1)))
-        per = torch.stack([self.stream_heads[m](x[:, s:s + n].mean(1)) for m, s, n in spans]).mean(0)
+        kf = tok_keep.to(x.dtype)[..., None]
+        fused = self.head(self.drop((x * kf).sum(1) / kf.sum(1).clamp_min(1)))
+        pooled = torch.stack([x[:, s:s + n].mean(1) for _, s, n in spans], 1)   # [B, S, H]
+        stream = torch.stack([self.stream_heads[m](pooled[:, i])
+                              for i, (m, _, _) in enumerate(spans)], 1)     # [B, S, C]
+        if c.modality_gate:
+            score = self.gate(pooled).squeeze(-1).float().masked_fill(~present, float("-inf"))
+            weights = score.softmax(1)
+        else:
+            weights = present.float() / present.float().sum(1, keepdim=True)
+        per = (stream.float() * weights[..., None]).sum(1).to(fused.dtype)
         w = c.late_fusion_weight
         logits = (1 - w) * fused + w * per
-        out = {"logits": logits, "fused_logits": fused, "stream_logits": per}
+        full = torch.zeros(B, len(SENSOR_MODALITIES), c.num_classes, device=x.device,
+                           dtype=stream.dtype)
+        full_w = torch.zeros(B, len(SENSOR_MODALITIES), device=x.device)
+        full_mask = torch.zeros(B, len(SENSOR_MODALITIES), dtype=torch.bool, device=x.device)
+        for i, (m, _, _) in enumerate(spans):
+            j = SENSOR_MODALITIES.index(m)
+            full[:, j], full_w[:, j], full_mask[:, j] = stream[:, i], weights[:, i], present[:, i]
+        out = {"logits": logits, "fused_logits": fused, "stream_logits": per,
+               "modality_logits": full, "modality_weights": full_w, "modality_mask": full_mask,
+               "features": (x * kf).sum(1) / kf.sum(1).clamp_min(1)}
         if labels is not None:
             out["loss"] = F.cross_entropy(logits.float(), labels)
         return out
@@ -246,6 +284,19 @@ class SensorDataset(torch.utils.data.Dataset):
         r = self.records[i]
         x = {m: torch.load(p, weights_only=True) for m, p in r.files.items()}
         return x, r.label
+
+
+def collate_sensors_masked(samples: Sequence):
+    """-> (inputs, masks, labels): every stream present in ANY sample is stacked,
+    zero-filled where a sample lacks it, with a per-sample presence mask."""
+    names = [m for m in SENSOR_MODALITIES if any(m in s[0] for s in samples)]
+    inputs, masks = {}, {}
+    for m in names:
+        ref = next(s[0][m] for s in samples if m in s[0])
+        inputs[m] = torch.stack([s[0][m] if m in s[0] else torch.zeros_like(ref)
+                                 for s in samples])
+        masks[m] = torch.tensor([m in s[0] for s in samples])
+    return inputs, masks, torch.tensor([s[1] for s in samples], dtype=torch.long)
 
 
 def collate_sensors(samples: Sequence) -> Tuple[Dict[str, torch.Tensor], torch.Tensor]:
