@@ -246,7 +246,13 @@ def _run(a, rank, world, device, ComplexityModel, TrainingConfig, LoRAConfig, ap
         if a.lora_targets:
             lcfg.target_modules = [t.strip() for t in a.lora_targets.split(",") if t.strip()]
         apply_lora(model, lcfg)
-    ds = SFTDataset(a.data, tok, a.seq_len, a.chat_format)
+    if Path(a.data).is_dir():  # pre-tokenised SFT shards (input_ids.bin / labels.bin)
+        from ..data.sft_shards import SFTTokenShardDataset
+
+        ds = SFTTokenShardDataset(a.data, a.seq_len)
+        ds.rows = [{} for _ in range(len(ds))]
+    else:
+        ds = SFTDataset(a.data, tok, a.seq_len, a.chat_format)
     pad = tok.pad_token_id or 0
     keep = list(range(len(ds)))
     stage = None
