@@ -9,7 +9,9 @@ document) and document ids (for block-diagonal attention masks).
 """
 from __future__ import annotations
 
-from typing import Dict, List, Sequence
+import math as _math
+from dataclasses import dataclass as _dataclass
+from typing import Dict, List, Sequence, Tuple
 
 import torch
 
@@ -71,3 +73,116 @@ class PackedSequenceCollator:
 
 def packing_efficiency(doc_ids: torch.Tensor) -> float:
     return float((doc_ids >= 0).float().mean())
+
+
+# ------------------------------------------------ packing plans (no truncation)
+# Counterpart of complexity/training/sequence_packing.py:16-158: next-fit packs
+# of whole examples (never split or dropped) with a separator budget between
+# neighbours, utilisation statistics, and exact data-parallel epoch boundaries.
+
+@_dataclass(frozen=True)
+class SequencePackingPlan:
+    packs: Tuple[Tuple[int, ...], ...]
+    lengths: Tuple[int, ...]
+    sequence_length: int
+    separator_tokens: int
+
+    @property
+    def source_items(self) -> int:
+        return len(self.lengths)
+
+    @property
+    def packed_items(self) -> int:
+        return len(self.packs)
+
+    @property
+    def source_tokens(self) -> int:
+        return sum(self.lengths)
+
+    @property
+    def separator_count(self) -> int:
+        return sum(max(0, len(p) - 1) for p in self.packs)
+
+    @property
+    def capacity_tokens(self) -> int:
+        return self.packed_items * self.sequence_length
+
+    @property
+    def payload_utilization(self) -> float:
+        return self.source_tokens / max(1, self.capacity_tokens)
+
+    @property
+    def occupied_utilization(self) -> float:
+        return ((self.source_tokens + self.separator_count * self.separator_tokens)
+                / max(1, self.capacity_tokens))
+
+    @property
+    def naive_payload_utilization(self) -> float:
+        return self.source_tokens / max(1, self.source_items * self.sequence_length)
+
+    @property
+    def compression_ratio(self) -> float:
+        return self.source_items / max(1, self.packed_items)
+
+    def assert_exact_coverage(self) -> None:
+        if sorted(i for p in self.packs for i in p) != list(range(self.source_items)):
+            raise ValueError("packing plan must contain every source item exactly once")
+        for p in self.packs:
+            if (sum(self.lengths[i] for i in p) + max(0, len(p) - 1) * self.separator_tokens
+                    > self.sequence_length):
+                raise ValueError("packing plan contains an over-capacity sequence")
+
+
+def pack_example_lengths(lengths, *, sequence_length: int,
+                         separator_tokens: int = 1) -> SequencePackingPlan:
+    """Stable next-fit: examples stay in order; a pack closes when the next
+    example (plus a separator) would overflow the window."""
+    L, sep = int(sequence_length), int(separator_tokens)
+    if L < 1:
+        raise ValueError("sequence_length must be positive")
+    if sep < 0:
+        raise ValueError("separator_tokens cannot be negative")
+    ls = tuple(int(x) for x in lengths)
+    if not ls:
+        raise ValueError("cannot pack an empty example set")
+    if any(x < 1 or x > L for x in ls):
+        raise ValueError("every example length must be within the sequence window")
+    packs: List[Tuple[int, ...]] = []
+    cur: List[int] = []
+    used = 0
+    for i, n in enumerate(ls):
+        need = n + (sep if cur else 0)
+        if cur and used + need > L:
+            packs.append(tuple(cur))
+            cur, used, need = [], 0, n
+        cur.append(i)
+        used += need
+    packs.append(tuple(cur))
+    plan = SequencePackingPlan(tuple(packs), ls, L, sep)
+    plan.assert_exact_coverage()
+    return plan
+
+
+@_dataclass(frozen=True)
+class EpochSchedule:
+    items: int
+    world_size: int
+    batch_size_per_rank: int
+    epochs: int
+    steps_per_epoch: int
+    total_steps: int
+
+    def epoch_steps(self) -> Tuple[int, ...]:
+        """Global step count at the end of each epoch."""
+        return tuple(self.steps_per_epoch * e for e in range(1, self.epochs + 1))
+
+
+def resolve_epoch_schedule(*, items: int, world_size: int, batch_size_per_rank: int,
+                           epochs: int) -> EpochSchedule:
+    """ceil(ceil(items / world) / batch) steps per epoch on every rank."""
+    vals = dict(items=int(items), world_size=int(world_size),
+                batch_size_per_rank=int(batch_size_per_rank), epochs=int(epochs))
+    if any(v < 1 for v in vals.values()):
+        raise ValueError("epoch schedule values must all be positive")
+    spe = _math.ceil(_math.ceil(vals["items"] / vals["world_size"]) / vals["batch_size_per_rank"])
+    return EpochSchedule(**vals, steps_per_epoch=spe, total_steps=spe * vals["epochs"])

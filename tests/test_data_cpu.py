@@ -94,3 +94,19 @@ def test_byte_tokenizer_and_chat_labels():
     assert "hello" in trained and "hi" not in trained.replace("hello", "")
     text = ChatTemplate("chatml").apply(msgs, add_generation_prompt=True)
     assert text.endswith("<|im_start|>assistant\n")
+
+
+def test_sequence_packing_plan_and_epoch_schedule():
+    import pytest
+
+    from complexity_framework_b200.data.packing import pack_example_lengths, resolve_epoch_schedule
+
+    plan = pack_example_lengths([3, 4, 2, 8, 1, 1], sequence_length=8, separator_tokens=1)
+    assert plan.packs == ((0, 1), (2,), (3,), (4, 5))
+    assert plan.source_tokens == 19 and plan.separator_count == 2
+    assert plan.compression_ratio == 1.5
+    assert abs(plan.occupied_utilization - 21 / 32) < 1e-12
+    with pytest.raises(ValueError, match="within the sequence window"):
+        pack_example_lengths([9], sequence_length=8)
+    s = resolve_epoch_schedule(items=10, world_size=3, batch_size_per_rank=2, epochs=3)
+    assert s.steps_per_epoch == 2 and s.total_steps == 6 and s.epoch_steps() == (2, 4, 6)
