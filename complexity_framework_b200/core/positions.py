@@ -82,3 +82,14 @@ class LearnedPositionalEmbedding(nn.Module):
     def forward(self, hidden: torch.Tensor, offset: int = 0) -> torch.Tensor:
         S = hidden.shape[1]
         return hidden + self.weight[offset:offset + S].to(hidden.dtype)[None]
+
+
+# reference class names (complexity/core/position/rotary.py:82-394); the
+# rotary ones take the same leading (dim, max_seq_len, theta) arguments
+from .layers import DynamicNTKRotaryEmbedding as DynamicNTKRoPE  # noqa: E402
+from .layers import RotaryEmbedding as StandardRoPE  # noqa: E402
+from .layers import YaRNRotaryEmbedding as YaRNRoPE  # noqa: E402
+
+PartialRoPE = PartialRotaryEmbedding
+ALiBiPositionBias = ALiBiPositionalBias
+LearnedPositionEmbedding = LearnedPositionalEmbedding

@@ -85,3 +85,55 @@ class GradientAccumulator:
     @property
     def should_step(self) -> bool:
         return self.count % self.steps == 0
+
+
+# ---------------------------------------------- reference configuration names
+_MODE_TO_DP = {ShardingMode.FULL_SHARD: "zero3", ShardingMode.SHARD_GRAD_OP: "fsdp",
+               ShardingMode.HYBRID_SHARD: "fsdp", ShardingMode.NO_SHARD: "ddp"}
+
+
+def get_sharding_strategy(mode: ShardingMode) -> str:
+    """The data-parallel mode a sharding mode selects here: FULL_SHARD -> ZeRO-3
+    (``zero3``), SHARD_GRAD_OP / HYBRID_SHARD -> ZeRO-2 (``fsdp``: sharded
+    gradients and optimizer state, replicated bf16 parameters), NO_SHARD ->
+    ``ddp`` (complexity/parallel/data_parallel.py:54-62 returns torch FSDP enums)."""
+    return _MODE_TO_DP[ShardingMode(mode)]
+
+
+def get_mixed_precision(mode: PrecisionMode):
+    """Compute dtype of a precision mode (None for fp32): parameters run in it,
+    the optimizer keeps fp32 masters, gradients reduce in it."""
+    mode = PrecisionMode(mode)
+    return None if mode == PrecisionMode.FP32 else (
+        torch.float16 if mode == PrecisionMode.FP16 else torch.bfloat16)
+
+
+class DataParallelConfig:
+    def __init__(self, sharding_mode: ShardingMode = ShardingMode.FULL_SHARD,
+                 precision: PrecisionMode = PrecisionMode.BF16, cpu_offload: bool = False,
+                 gradient_accumulation_steps: int = 1, sync_module_states: bool = True):
+        if cpu_offload:
+            raise ValueError("cpu_offload is not supported: 180 GB of HBM per B200 holds the "
+                             "sharded fp32 state of every configuration here")
+        self.sharding_mode, self.precision = ShardingMode(sharding_mode), PrecisionMode(precision)
+        self.cpu_offload = cpu_offload
+        self.gradient_accumulation_steps = int(gradient_accumulation_steps)
+        self.sync_module_states = sync_module_states
+
+    @property
+    def distributed_mode(self) -> str:
+        return get_sharding_strategy(self.sharding_mode)
+
+
+def resolve_dist_timeout_s(is_multi_node: bool, env=None) -> int:
+    """Collective timeout: ``COMPLEXITY_DIST_TIMEOUT_S``, else 1800 s across nodes
+    and 600 s on one node."""
+    import os
+
+    env = os.environ if env is None else env
+    return int(env.get("COMPLEXITY_DIST_TIMEOUT_S", 1800 if is_multi_node else 600))
+
+
+def cleanup() -> None:
+    if dist.is_available() and dist.is_initialized():
+        dist.destroy_process_group()

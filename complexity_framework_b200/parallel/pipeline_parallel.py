@@ -238,3 +238,67 @@ class PipelineScheduler:
 
     def run(self, micro_batches):
         return self.pipeline.train_step(micro_batches)
+
+
+# --------------------------------------------------- reference helper names
+from dataclasses import dataclass as _dataclass  # noqa: E402
+from enum import Enum as _Enum  # noqa: E402
+
+
+class PipelineSchedule(_Enum):
+    GPIPE = "gpipe"
+    ONE_F_ONE_B = "1f1b"
+    INTERLEAVED = "interleaved"
+
+
+@_dataclass
+class PipelineConfig:
+    """Stages, micro-batches per step and schedule (complexity/parallel/
+    pipeline_parallel.py:26-38).  ``INTERLEAVED`` (virtual stages) is not built:
+    the export-based pipeline (``parallel/pipeline_export.py``) is the
+    alternative for finer stage splits."""
+    num_stages: int
+    num_micro_batches: int = 4
+    schedule: PipelineSchedule = PipelineSchedule.ONE_F_ONE_B
+
+    def __post_init__(self):
+        self.schedule = PipelineSchedule(self.schedule)
+        if self.schedule is PipelineSchedule.INTERLEAVED:
+            raise ValueError("interleaved (virtual-stage) schedules are not built; use gpipe "
+                             "or 1f1b")
+
+
+def get_pipeline_parallel_rank(group=None) -> int:
+    return dist.get_rank(group) if dist.is_available() and dist.is_initialized() else 0
+
+
+def get_pipeline_parallel_world_size(group=None) -> int:
+    return dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+
+
+def send_forward(tensor: torch.Tensor, next_rank: int, group=None) -> None:
+    """Activation to the next stage (NCCL / gloo point-to-point)."""
+    if dist.is_available() and dist.is_initialized():
+        dist.send(tensor.contiguous(), next_rank, group=group)
+
+
+def recv_forward(tensor_shape, dtype: torch.dtype, prev_rank: int, device,
+                 group=None) -> torch.Tensor:
+    t = torch.zeros(tuple(tensor_shape), dtype=dtype, device=device)
+    if dist.is_available() and dist.is_initialized():
+        dist.recv(t, prev_rank, group=group)
+    return t
+
+
+def send_backward(tensor: torch.Tensor, prev_rank: int, group=None) -> None:
+    """Activation gradient to the previous stage."""
+    if dist.is_available() and dist.is_initialized():
+        dist.send(tensor.contiguous(), prev_rank, group=group)
+
+
+def recv_backward(tensor_shape, dtype: torch.dtype, next_rank: int, device,
+                  group=None) -> torch.Tensor:
+    t = torch.zeros(tuple(tensor_shape), dtype=dtype, device=device)
+    if dist.is_available() and dist.is_initialized():
+        dist.recv(t, next_rank, group=group)
+    return t

@@ -328,3 +328,93 @@ def gather_tp_state_dict(model: nn.Module, group=None) -> dict:
                 t = torch.cat([q.narrow(dim, 0, n) for q, n in zip(parts, sizes)], dim)
         out[name] = t
     return out
+
+
+# --------------------------------------------------- reference helper names
+# complexity/parallel/tensor_parallel.py:29-175 keeps the TP group in module
+# state built from an integer size; the same calls work here on top of the
+# group-based primitives above.
+def init_tensor_parallel_group(tp_size) -> None:
+    """Create the TP groups (consecutive ranks, ``tp_size`` each; every rank must
+    call) and make this rank's group the default; a process group may be passed
+    instead of a size."""
+    if not (dist.is_available() and dist.is_initialized()):
+        _TP["group"] = None
+        return
+    if not isinstance(tp_size, int):
+        _TP["group"] = tp_size
+        return
+    world = dist.get_world_size()
+    if tp_size <= 1:
+        _TP["group"] = None
+        return
+    if world % tp_size:
+        raise ValueError(f"world size {world} is not divisible by tp_size {tp_size}")
+    mine = None
+    for start in range(0, world, tp_size):
+        g = dist.new_group(list(range(start, start + tp_size)))
+        if start <= dist.get_rank() < start + tp_size:
+            mine = g
+    _TP["group"] = mine
+
+
+def get_tensor_parallel_world_size() -> int:
+    return tp_world()
+
+
+def get_tensor_parallel_rank() -> int:
+    return tp_rank()
+
+
+def get_tensor_parallel_group():
+    return _TP["group"]
+
+
+def all_reduce(tensor: torch.Tensor) -> torch.Tensor:
+    """Sum over the TP group (identity gradient)."""
+    return reduce_from_tp(tensor)
+
+
+class _ReduceScatterDim(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, dim, group):
+        ctx.dim, ctx.group = dim, group
+        parts = [p.contiguous() for p in x.chunk(dist.get_world_size(group), dim)]
+        out = torch.empty_like(parts[0])
+        dist.reduce_scatter(out, parts, group=group)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        parts = [torch.empty_like(g) for _ in range(dist.get_world_size(ctx.group))]
+        dist.all_gather(parts, g.contiguous(), group=ctx.group)
+        return torch.cat(parts, ctx.dim), None, None
+
+
+class _AllGatherDim(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, dim, group):
+        ctx.dim, ctx.group = dim, group
+        parts = [torch.empty_like(x) for _ in range(dist.get_world_size(group))]
+        dist.all_gather(parts, x.contiguous(), group=group)
+        return torch.cat(parts, dim)
+
+    @staticmethod
+    def backward(ctx, g):
+        P = dist.get_world_size(ctx.group)
+        parts = [p.contiguous() for p in g.chunk(P, ctx.dim)]
+        out = torch.empty_like(parts[0])
+        dist.reduce_scatter(out, parts, group=ctx.group)
+        return out, None, None
+
+
+def reduce_scatter(tensor: torch.Tensor, dim: int = -1) -> torch.Tensor:
+    """Sum over the TP group, keep this rank's slice along ``dim`` (backward: all-gather)."""
+    g = _TP["group"]
+    return tensor if tp_world(g) == 1 else _ReduceScatterDim.apply(tensor, dim, g)
+
+
+def all_gather(tensor: torch.Tensor, dim: int = -1) -> torch.Tensor:
+    """Concatenate every rank's tensor along ``dim`` (backward: reduce-scatter)."""
+    g = _TP["group"]
+    return tensor if tp_world(g) == 1 else _AllGatherDim.apply(tensor, dim, g)

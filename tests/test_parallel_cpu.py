@@ -315,3 +315,32 @@ def _zero3_body(rank, world, tmp):
 
 def test_zero3_matches_single_process():
     _run(2, _zero3_body)
+
+
+def _helpers_body(rank, world, tmp):
+    from complexity_framework_b200.parallel import pipeline_parallel as PP
+    from complexity_framework_b200.parallel import tensor_parallel as TP
+
+    TP.init_tensor_parallel_group(world)
+    assert TP.get_tensor_parallel_world_size() == world and TP.get_tensor_parallel_rank() == rank
+    x = torch.full((2, 4), float(rank + 1), requires_grad=True)
+    g = TP.all_gather(x, dim=-1)
+    assert g.shape == (2, 4 * world) and torch.equal(g[:, 4:], torch.full((2, 4), 2.0))
+    (g * torch.arange(8.0)).sum().backward()  # backward: reduce-scatter of the gradient
+    assert torch.allclose(x.grad, world * torch.arange(8.0)[rank * 4:(rank + 1) * 4].expand(2, 4))
+    y = torch.arange(8.0).repeat(2, 1) * (rank + 1)
+    rs = TP.reduce_scatter(y, dim=-1)
+    assert torch.equal(rs, 3 * torch.arange(8.0)[rank * 4:(rank + 1) * 4].repeat(2, 1))
+    assert torch.equal(TP.all_reduce(torch.ones(3)), torch.full((3,), float(world)))
+    if rank == 0:
+        PP.send_forward(torch.arange(6.0).view(2, 3), 1)
+        got = PP.recv_backward((2, 3), torch.float32, 1, "cpu")
+        assert torch.equal(got, -torch.arange(6.0).view(2, 3))
+    else:
+        got = PP.recv_forward((2, 3), torch.float32, 0, "cpu")
+        PP.send_backward(-got, 0)
+    assert PP.get_pipeline_parallel_world_size() == world
+
+
+def test_reference_helper_names_gloo():
+    _run(2, _helpers_body)
