@@ -280,3 +280,47 @@ class SlidingWindowCache:
     @property
     def seq_len(self) -> int:
         return self.total[0]
+
+
+# --------------------------------------------------- reference API names
+@dataclass
+class SpeculativeConfig:
+    """complexity/inference/speculative.py:26-33."""
+    num_speculative_tokens: int = 5
+    acceptance_threshold: float = 0.0
+    temperature: float = 1.0
+    top_k: Optional[int] = None
+    top_p: Optional[float] = None
+
+
+class SelfSpeculativeDecoder:
+    """Self-speculative decoding: the first ``exit_layer`` layers of the model
+    (with its final norm and head) draft ``num_speculative_tokens`` tokens, the
+    full model verifies them in one pass over the paged cache
+    (complexity/inference/speculative.py:338-420)."""
+
+    def __init__(self, model, exit_layer: int, config: Optional[SpeculativeConfig] = None,
+                 page_size: int = 16):
+        self.model, self.exit_layer = model, exit_layer
+        self.config = config or SpeculativeConfig()
+        self.decoder = SpeculativeDecoder(model, LayerSkipDraft(model, exit_layer),
+                                          num_draft_tokens=self.config.num_speculative_tokens,
+                                          page_size=page_size)
+
+    def generate(self, input_ids, max_new_tokens: int = 100, eos_token_id: Optional[int] = None,
+                 seed: Optional[int] = None):
+        """``input_ids``: [1, T] tensor or a token list; returns the same kind."""
+        as_tensor = torch.is_tensor(input_ids)
+        prompt = input_ids.reshape(-1).tolist() if as_tensor else list(input_ids)
+        temp = self.config.temperature if self.config.temperature != 1.0 or seed is not None \
+            else 0.0
+        out = self.decoder.generate(prompt, max_new_tokens=max_new_tokens, temperature=temp,
+                                    eos_token_id=eos_token_id, seed=seed)
+        seq = prompt + list(out)          # the decoder returns the new tokens only
+        if as_tensor:
+            return torch.tensor(seq, dtype=torch.long, device=input_ids.device)[None]
+        return seq
+
+    def get_statistics(self) -> dict:
+        st = getattr(self.decoder, "stats", None)
+        return dict(vars(st)) if st is not None else {}
