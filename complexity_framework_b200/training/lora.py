@@ -198,3 +198,109 @@ def count_trainable(model: nn.Module) -> Dict[str, int]:
     tot = sum(p.numel() for p in model.parameters())
     tr = sum(p.numel() for p in model.parameters() if p.requires_grad)
     return {"total": tot, "trainable": tr}
+
+
+# ------------------------------------------------- reference adapter helpers
+# complexity/training/lora.py:234-339 names adapters by their module (dense)
+# or "<module>.<expert tensor>" (stacked experts) and keeps adapter-only state
+# dicts under "<name>.lora_A" / "<name>.lora_B"; the same names are used here
+# for both the parametrised weights and the LoRALinear wrapper.
+def lora_modules(model: nn.Module) -> Dict[str, nn.Module]:
+    """Dense adapters by module name (LoRALinear wrappers and LoRADelta weights)."""
+    out: Dict[str, nn.Module] = {}
+    for name, mod in model.named_modules():
+        if isinstance(mod, LoRALinear):
+            out[name] = mod
+        elif parametrize.is_parametrized(mod, "weight"):
+            p = mod.parametrizations["weight"]
+            if len(p) == 1 and isinstance(p[0], LoRADelta):
+                out[name] = p[0]
+    return out
+
+
+def expert_lora_modules(model: nn.Module):
+    """``{"<module>.<tensor>": (parent, tensor name, LoRAExpertTensor)}``."""
+    out = {}
+    for name, mod in model.named_modules():
+        if not parametrize.is_parametrized(mod):
+            continue
+        for tname, plist in mod.parametrizations.items():
+            if len(plist) == 1 and isinstance(plist[0], LoRAExpertTensor):
+                out[f"{name}.{tname}" if name else tname] = (mod, tname, plist[0])
+    return out
+
+
+def adapter_state_dict(model: nn.Module) -> Dict[str, torch.Tensor]:
+    st = {}
+    for name, m in lora_modules(model).items():
+        st[f"{name}.lora_A"], st[f"{name}.lora_B"] = m.lora_A.detach().cpu(), m.lora_B.detach().cpu()
+    for name, (_, _, m) in expert_lora_modules(model).items():
+        st[f"{name}.lora_A"], st[f"{name}.lora_B"] = m.lora_A.detach().cpu(), m.lora_B.detach().cpu()
+    return st
+
+
+def load_adapter_state_dict(model: nn.Module, state: Dict[str, torch.Tensor]) -> None:
+    """Load adapter weights; the key set must match this model's adapters exactly."""
+    mods = {**lora_modules(model), **{k: v[2] for k, v in expert_lora_modules(model).items()}}
+    expected = {f"{n}.{p}" for n in mods for p in ("lora_A", "lora_B")}
+    if set(state) != expected:
+        miss, extra = sorted(expected - set(state)), sorted(set(state) - expected)
+        raise ValueError(f"adapter state does not match the model's adapters "
+                         f"(missing {miss[:4]}, unexpected {extra[:4]})")
+    with torch.no_grad():
+        for n, m in mods.items():
+            m.lora_A.copy_(state[f"{n}.lora_A"])
+            m.lora_B.copy_(state[f"{n}.lora_B"])
+
+
+def _delta(m: nn.Module) -> torch.Tensor:
+    if isinstance(m, LoRAExpertTensor):
+        return torch.bmm(m.lora_A, m.lora_B) * m.scale
+    return (m.lora_B @ m.lora_A) * m.scale
+
+
+def unmerge_adapter_from_base(model: nn.Module) -> None:
+    """Given base weights that already contain the adapters' update, subtract it
+    so base + adapter is again the merged model (the inverse of merging)."""
+    with torch.no_grad():
+        for name, m in lora_modules(model).items():
+            if isinstance(m, LoRALinear):
+                m.base.weight.sub_(_delta(m).to(m.base.weight.dtype))
+            else:
+                owner = model.get_submodule(name)
+                orig = owner.parametrizations["weight"].original
+                orig.sub_(_delta(m).to(orig.dtype))
+        for parent, tname, m in expert_lora_modules(model).values():
+            orig = parent.parametrizations[tname].original
+            orig.sub_(_delta(m).to(orig.dtype))
+
+
+def merged_model_state_dict(model: nn.Module) -> Dict[str, torch.Tensor]:
+    """The plain checkpoint state (adapters folded in) without changing ``model``."""
+    out: Dict[str, torch.Tensor] = {}
+    dense = lora_modules(model)
+    experts = expert_lora_modules(model)
+    for key, val in model.state_dict().items():
+        if key.endswith(".lora_A") or key.endswith(".lora_B"):
+            continue
+        if ".parametrizations." in key:
+            owner, rest = key.split(".parametrizations.", 1)
+            tname = rest.split(".")[0]
+            if not rest.endswith(".original"):
+                continue
+            a = dense.get(owner) if tname == "weight" else None
+            e = experts.get(f"{owner}.{tname}")
+            m = a if a is not None else (e[2] if e is not None else None)
+            out[f"{owner}.{tname}"] = (val + _delta(m).to(val.dtype)).detach() if m is not None \
+                else val
+            continue
+        if key.endswith(".base.weight") and key[:-len(".base.weight")] in dense:
+            m = dense[key[:-len(".base.weight")]]
+            w = val if getattr(m, "merged", False) else val + _delta(m).to(val.dtype)
+            out[key[:-len(".base.weight")] + ".weight"] = w.detach()
+            continue
+        if ".base." in key and key.split(".base.")[0] in dense:
+            out[key.replace(".base.", ".")] = val
+            continue
+        out[key] = val
+    return out

@@ -62,3 +62,48 @@ def test_lora_linear_merge_unmerge():
     assert torch.allclose(l(x), y, atol=1e-5)
     l.unmerge()
     assert torch.allclose(l(x), y, atol=1e-5)
+
+
+def test_reference_adapter_helpers():
+    import torch
+
+    from complexity_framework_b200 import ComplexityModel, ModelConfig
+    from complexity_framework_b200.training.lora import (LoRAConfig, adapter_state_dict,
+                                                         apply_lora, expert_lora_modules,
+                                                         load_adapter_state_dict, lora_modules,
+                                                         merged_model_state_dict,
+                                                         unmerge_adapter_from_base)
+
+    torch.manual_seed(0)
+    cfg = ModelConfig(hidden_size=32, num_hidden_layers=1, num_attention_heads=4,
+                      num_key_value_heads=2, vocab_size=64, intermediate_size=32,
+                      shared_intermediate_size=64, num_experts=2, top_k=2,
+                      max_position_embeddings=32)
+    base = ComplexityModel(cfg)
+    m = ComplexityModel(cfg)
+    m.load_state_dict(base.state_dict())
+    apply_lora(m, LoRAConfig(r=2, include_experts=True))
+    with torch.no_grad():  # non-zero B so the adapters change the output
+        for name, mod in {**lora_modules(m), **{k: v[2] for k, v in expert_lora_modules(m).items()}}.items():
+            mod.lora_B.normal_(std=0.1)
+    assert lora_modules(m) and expert_lora_modules(m)
+    sd = adapter_state_dict(m)
+    assert all(k.endswith((".lora_A", ".lora_B")) for k in sd)
+    ids = torch.randint(0, 64, (1, 8))
+    want = m(ids)["logits"]
+    merged = merged_model_state_dict(m)
+    assert set(merged) == set(base.state_dict())
+    plain = ComplexityModel(cfg)
+    plain.load_state_dict(merged)
+    assert torch.allclose(plain(ids)["logits"], want, atol=1e-5)
+    # a merged checkpoint + its adapter: unmerge restores the original base
+    m2 = ComplexityModel(cfg)
+    m2.load_state_dict(merged)
+    apply_lora(m2, LoRAConfig(r=2, include_experts=True))
+    load_adapter_state_dict(m2, sd)
+    unmerge_adapter_from_base(m2)
+    assert torch.allclose(m2(ids)["logits"], want, atol=1e-5)
+    import pytest
+
+    with pytest.raises(ValueError, match="does not match"):
+        load_adapter_state_dict(m2, {k: v for k, v in list(sd.items())[1:]})
