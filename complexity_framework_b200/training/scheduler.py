@@ -6,6 +6,7 @@ implemented as one ``LambdaLR`` multiplier function per schedule.
 from __future__ import annotations
 
 import math
+from typing import Optional
 
 import torch
 
@@ -40,3 +41,30 @@ def build_scheduler(optimizer: torch.optim.Optimizer, *, kind: str = "auto", war
                              min_ratio=min_lr_ratio, wsd_decay_ratio=wsd_decay_ratio)
 
     return torch.optim.lr_scheduler.LambdaLR(optimizer, fn)
+
+
+# reference entry points (complexity/training/scheduler.py:12-80)
+def resolve_scheduler_name(config, model=None) -> str:
+    """``auto`` resolves to cosine; any other name is returned unchanged."""
+    name = getattr(config, "lr_scheduler", "auto")
+    return "cosine" if name == "auto" else name
+
+
+def get_lr_scheduler(optimizer: torch.optim.Optimizer, config=None,
+                     num_training_steps: Optional[int] = None, model=None,
+                     scheduler_type: Optional[str] = None,
+                     num_warmup_steps: Optional[int] = None):
+    """Scheduler from a ``TrainingConfig`` (or from the explicit arguments)."""
+    if config is None:
+        if num_training_steps is None:
+            raise ValueError("num_training_steps is required when config is not provided")
+        kind = scheduler_type or "cosine"
+        return build_scheduler(optimizer, kind=kind, warmup_steps=num_warmup_steps or 0,
+                               total_steps=num_training_steps)
+    kind = scheduler_type or resolve_scheduler_name(config, model)
+    return build_scheduler(optimizer, kind=kind,
+                           warmup_steps=(config.warmup_steps if num_warmup_steps is None
+                                         else num_warmup_steps),
+                           total_steps=num_training_steps or config.max_steps,
+                           min_lr_ratio=getattr(config, "min_lr_ratio", 0.1),
+                           wsd_decay_ratio=getattr(config, "wsd_decay_ratio", 0.2))

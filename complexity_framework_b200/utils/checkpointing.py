@@ -178,3 +178,50 @@ def load_weights_only(model: torch.nn.Module, path: str) -> None:
     else:
         sd = torch.load(p / "checkpoint.pt", map_location="cpu", weights_only=False)["model"]
     model.load_state_dict(sd, strict=False)
+
+
+# ----------------------------------------------- reference helper names
+from dataclasses import asdict as _asdict, dataclass as _dataclass  # noqa: E402
+
+
+@_dataclass
+class TrainingState:
+    """Scalar training progress (complexity/utils/checkpointing.py:128-142)."""
+    step: int = 0
+    epoch: int = 0
+    best_loss: float = float("inf")
+    total_tokens: int = 0
+    learning_rate: float = 0.0
+
+    def to_dict(self) -> dict:
+        return _asdict(self)
+
+    @classmethod
+    def from_dict(cls, data: dict) -> "TrainingState":
+        return cls(**{k: v for k, v in data.items() if k in cls.__dataclass_fields__})
+
+
+def enable_activation_checkpointing(model, checkpoint_layers: bool = True) -> None:
+    """Recompute each decoder layer's activations in backward (models that
+    expose ``gradient_checkpointing_enable``; otherwise every child of
+    ``model.layers`` is wrapped)."""
+    if not checkpoint_layers:
+        return
+    if hasattr(model, "gradient_checkpointing_enable"):
+        model.gradient_checkpointing_enable()
+        return
+    from torch.utils.checkpoint import checkpoint
+
+    for layer in getattr(model, "layers", []):
+        fwd = layer.forward
+
+        def wrapped(*a, _f=fwd, **k):
+            return checkpoint(_f, *a, use_reentrant=False, **k)
+        layer.forward = wrapped
+
+
+def checkpoint_sequential(functions, input, segments: int = 1, **kwargs):
+    """Run ``functions`` in order, recomputing each segment's activations in backward."""
+    from torch.utils.checkpoint import checkpoint_sequential as _cs
+
+    return _cs(list(functions), max(1, segments), input, use_reentrant=False, **kwargs)

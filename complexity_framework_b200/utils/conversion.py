@@ -263,3 +263,55 @@ def create_hf_config(config: ModelConfig, model_type: str = "llama") -> Dict[str
             "rope_theta": config.rope_theta,
             "max_position_embeddings": config.max_position_embeddings,
             "tie_word_embeddings": config.tie_word_embeddings, "torch_dtype": "bfloat16"}
+
+
+def load_from_huggingface(model_name_or_path: str, model, model_type: str = "llama",
+                          device: str = "cpu"):
+    """Load a local Hugging Face Llama-family checkpoint directory (safetensors
+    or a PyTorch bin) into ``model`` through ``convert_hf_state_dict``; keys the
+    HF model lacks (TR-Hash experts, route tables) keep their initial values.
+    Hub downloads are not available offline: pass a directory."""
+    p = Path(model_name_or_path)
+    if not p.is_dir():
+        raise FileNotFoundError(f"{p} is not a local checkpoint directory (no network access "
+                                "to download from the Hub)")
+    sd: Dict[str, torch.Tensor] = {}
+    files = sorted(p.glob("*.safetensors"))
+    if files:
+        from safetensors.torch import load_file
+
+        for f in files:
+            sd.update(load_file(str(f), device=device))
+    else:
+        for f in sorted(p.glob("pytorch_model*.bin")):
+            sd.update(torch.load(f, map_location=device, weights_only=True))
+    if not sd:
+        raise FileNotFoundError(f"no weights (*.safetensors / pytorch_model*.bin) in {p}")
+    mapped = convert_hf_state_dict(sd, model_type)
+    missing, unexpected = model.load_state_dict(mapped, strict=False)
+    if unexpected:
+        raise ValueError(f"unmapped Hugging Face keys: {unexpected[:5]}")
+    return model
+
+
+def save_to_huggingface(model, save_path: str, model_type: str = "llama", config=None) -> str:
+    """Write ``config.json`` + ``model.safetensors`` in Llama-family layout (the
+    shared SwiGLU is the dense MLP; routed experts have no HF counterpart and
+    are left out)."""
+    from safetensors.torch import save_file
+
+    out = Path(save_path)
+    out.mkdir(parents=True, exist_ok=True)
+    cfg = config or model.config
+    sd = {k: v.detach().contiguous().cpu() for k, v in
+          convert_to_hf_state_dict(model.state_dict(), model_type).items()
+          if not any(k.endswith(s) for s in ROUTE_BUFFER_SUFFIXES + EXPERT_PARAM_SUFFIXES)
+          and ".engine." not in k}
+    save_file(sd, str(out / "model.safetensors"))
+    (out / "config.json").write_text(json.dumps(create_hf_config(cfg, model_type), indent=2))
+    return str(out)
+
+
+def push_to_hub(*args, **kwargs):
+    raise RuntimeError("push_to_hub needs network access, which this environment does not "
+                       "have; use save_to_huggingface and upload the directory separately")
