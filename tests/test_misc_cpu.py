@@ -81,3 +81,35 @@ def test_safety_clamps():
     m(torch.randint(0, 128, (1, 8)))
     assert get_safety_stats(m)["calls"] == 1
     remove_safety(m)
+
+
+def test_integer_ops_reference_names_match_reference():
+    import os
+    import sys
+
+    import torch
+
+    from complexity_framework_b200.core import integer_ops as I
+
+    ref_root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                            "baseline", "_ref")
+    g = torch.Generator().manual_seed(0)
+    w, x = torch.randn(16, 32, generator=g), torch.randn(4, 32, generator=g)
+    qw, sw = I.quantize_weight_int8(w)
+    y = I.int8_linear(x, qw, sw)
+    assert torch.allclose(y, x @ w.t(), atol=0.1, rtol=0.05)
+    gg, uu = I.int8_fused_gate_up(x, qw, sw, 8)
+    assert gg.shape == (4, 8) and torch.allclose(torch.cat([gg, uu], -1), y)
+    z = torch.arange(-1200, 1201, 7, dtype=torch.int32)
+    if not os.path.isdir(os.path.join(ref_root, "complexity")):
+        return
+    sys.path.insert(0, ref_root)
+    try:
+        from complexity.core import integer_ops as R
+    finally:
+        sys.path.remove(ref_root)
+    for name in ("silu_integer", "sigmoid_integer", "softplus_integer"):
+        assert torch.equal(getattr(I, name)(z), getattr(R, name)(z)), name
+    a, b = torch.randn(3, 5, generator=g), torch.randn(3, 5, generator=g)
+    assert torch.equal(I.silu_multiply_integer(a, b), R.silu_multiply_integer(a, b))
+    assert torch.equal(I.quantize_weight_int8(w)[0], R.quantize_weight_int8(w)[0])
