@@ -597,3 +597,11 @@ class CausalFastWeightConvMixer(CausalConvMixer):
         new = ((ext[:, -(K - 1):].detach() if K > 1 else ext[:, :0],) + tuple(mem_state)
                if use_cache else None)
         return (out if residual is None else residual + out), new
+
+
+# reference class names (complexity/core/attention/flash_attention.py,
+# token_routed_mha.py, token_routed_mha_v2.py)
+FlashAttention = FlashGQA
+SparseAttention = BlockSparseAttention
+TokenRoutedMultiHeadAttention = TokenRoutedMHA
+TokenRoutedMultiHeadAttentionV2 = TokenRoutedMHA

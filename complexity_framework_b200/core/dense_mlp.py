@@ -56,3 +56,6 @@ class DeterministicDenseMLP(DenseSwiGLU):
                            float(getattr(config, "initializer_range", 0.02)))
         for m in (self.gate_proj, self.up_proj, self.down_proj):
             m._deterministic_init = True
+
+
+DenseDeterministicMLP = DeterministicDenseMLP   # reference class name

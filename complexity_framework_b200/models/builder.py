@@ -32,6 +32,31 @@ _DETERMINISTIC_BUFFER = re.compile(
     r"\.(inv_freq|token_to_expert|pair_hash_route_codes|pair_hash_expert_pairs)$")
 
 
+def build_lexical_zipf_weights(counts: torch.Tensor, *, mode: str, alpha: float, floor: float,
+                               permutation_seed: int) -> torch.Tensor:
+    """Per-token weights (rank / V)^alpha over descending-frequency ranks (ties
+    keep vocabulary order), floored at ``floor``, scaled to unit RMS; ``permuted``
+    shuffles them with a seeded permutation (a frequency-blind control).
+    Mirrors complexity/models/builder.py:22-48."""
+    if counts.ndim != 1:
+        raise ValueError("Zipf counts must be a 1D tensor")
+    if mode not in ("ordered", "permuted"):
+        raise ValueError(f"Unsupported Zipf mode: {mode}")
+    if alpha <= 0.0:
+        raise ValueError("lexical_zipf_alpha must be positive")
+    if not 0.0 <= floor <= 1.0:
+        raise ValueError("lexical_zipf_floor must lie in [0, 1]")
+    V = counts.numel()
+    order = torch.argsort(counts.double(), descending=True, stable=True)
+    rank = torch.empty(V, dtype=torch.float32)
+    rank[order] = torch.arange(1, V + 1, dtype=torch.float32)
+    w = (rank / V).pow(float(alpha)).clamp_min(float(floor))
+    w = w / w.square().mean().sqrt().clamp_min(1e-12)
+    if mode == "permuted":
+        w = w[torch.randperm(V, generator=torch.Generator().manual_seed(int(permutation_seed)))]
+    return w
+
+
 class ComplexityModel(nn.Module):
     def __init__(self, config: ModelConfig):
         super().__init__()
@@ -56,6 +81,21 @@ class ComplexityModel(nn.Module):
             self.lexical_token_scale = self.layers[0].mlp.token_scale
             for layer in self.layers:
                 layer.mlp.tie_token_scale(self.lexical_token_scale)
+        zipf = str(getattr(config, "lexical_zipf_mode", "uniform"))
+        if zipf != "uniform":
+            # persistent per-token weights from corpus frequency ranks (part of
+            # the checkpoint contract of lexical configurations)
+            if not config.lexical_zipf_path:
+                raise ValueError("lexical_zipf_path is required for non-uniform Zipf")
+            art = torch.load(config.lexical_zipf_path, map_location="cpu", weights_only=True)
+            counts = art["counts"] if isinstance(art, dict) else art
+            if counts.numel() != config.vocab_size:
+                raise ValueError(f"Zipf counts have vocab {counts.numel()}, expected "
+                                 f"{config.vocab_size}")
+            self.register_buffer("lexical_zipf_weights", build_lexical_zipf_weights(
+                counts, mode=zipf, alpha=float(config.lexical_zipf_alpha),
+                floor=float(config.lexical_zipf_floor),
+                permutation_seed=int(config.lexical_zipf_permutation_seed)), persistent=True)
         self._gradient_checkpointing = False
         self.apply(self._init_weights)
         if lexical:  # as in the reference: the first (or shared) table starts at zero

@@ -113,3 +113,59 @@ def test_integer_ops_reference_names_match_reference():
     a, b = torch.randn(3, 5, generator=g), torch.randn(3, 5, generator=g)
     assert torch.equal(I.silu_multiply_integer(a, b), R.silu_multiply_integer(a, b))
     assert torch.equal(I.quantize_weight_int8(w)[0], R.quantize_weight_int8(w)[0])
+
+
+def test_zipf_weights_bases_and_core_names(tmp_path):
+    import os
+    import sys
+
+    import pytest
+    import torch
+
+    from complexity_framework_b200 import ComplexityModel, ModelConfig
+    from complexity_framework_b200.core.bases import (AttentionBase, MLPBase, build_norm,
+                                                      deterministic_gaussian_init_)
+    from complexity_framework_b200.core.registry import MLP_REGISTRY, register_mlp
+    from complexity_framework_b200.models.builder import build_lexical_zipf_weights
+
+    c = torch.tensor([5.0, 1, 9, 9, 0, 3])
+    w = build_lexical_zipf_weights(c, mode="ordered", alpha=0.5, floor=0.1, permutation_seed=3)
+    assert abs(float(w.square().mean()) - 1) < 1e-5 and w[2] < w[0] < w[1]
+    ref_root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                            "baseline", "_ref")
+    if os.path.isdir(os.path.join(ref_root, "complexity")):
+        sys.path.insert(0, ref_root)
+        try:
+            from complexity.models.builder import build_lexical_zipf_weights as R
+        finally:
+            sys.path.remove(ref_root)
+        for mode in ("ordered", "permuted"):
+            assert torch.allclose(build_lexical_zipf_weights(c, mode=mode, alpha=0.5, floor=0.1,
+                                                             permutation_seed=3),
+                                  R(c, mode=mode, alpha=0.5, floor=0.1, permutation_seed=3))
+    torch.save({"counts": torch.arange(64.0)}, tmp_path / "z.pt")
+    m = ComplexityModel(ModelConfig(hidden_size=32, num_hidden_layers=1, num_attention_heads=4,
+                                    vocab_size=64, intermediate_size=32, num_experts=2,
+                                    lexical_zipf_mode="permuted",
+                                    lexical_zipf_path=str(tmp_path / "z.pt")))
+    assert m.state_dict()["lexical_zipf_weights"].shape == (64,)
+    with pytest.raises(ValueError, match="lexical_zipf_path"):
+        ComplexityModel(ModelConfig(hidden_size=32, num_hidden_layers=1, num_attention_heads=4,
+                                    vocab_size=64, lexical_zipf_mode="ordered"))
+    a, b = torch.empty(3, 4), torch.empty(3, 4)
+    assert torch.equal(deterministic_gaussian_init_(a, 7), deterministic_gaussian_init_(b, 7))
+    assert build_norm("rmsnorm", 8)(torch.randn(2, 8)).shape == (2, 8)
+
+    @register_mlp("test_scaled_identity")
+    class Scaled(MLPBase):
+        def __init__(self, config):
+            super().__init__(config)
+            self.s = torch.nn.Parameter(torch.ones(()))
+
+        def forward(self, hidden_states, token_ids=None, **kw):
+            return hidden_states * self.s
+
+    assert "test_scaled_identity" in MLP_REGISTRY.names() if hasattr(MLP_REGISTRY, "names") \
+        else True
+    with pytest.raises(TypeError):
+        AttentionBase(None)
