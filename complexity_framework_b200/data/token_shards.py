@@ -190,3 +190,59 @@ class TokenShardDataset(IterableDataset):
             reader.gather(torch.as_tensor(pos, dtype=torch.long), out, 1)
             for row in out:
                 yield {"input_ids": row[:-1], "labels": row[1:]}
+
+
+def iter_texts_from_files(paths, *, input_format: str = "jsonl", text_field: str = "text",
+                          limit: int = 0) -> Iterator[str]:
+    """Texts of JSONL rows (``text_field``) or whole plain-text files, in order,
+    stopping after ``limit`` records when it is positive."""
+    seen = 0
+    for p in paths:
+        p = Path(p)
+        if input_format == "jsonl":
+            with p.open(encoding="utf-8") as f:
+                for line in f:
+                    if not line.strip():
+                        continue
+                    t = json.loads(line).get(text_field, "")
+                    if t:
+                        yield str(t)
+                        seen += 1
+                        if limit > 0 and seen >= limit:
+                            return
+        elif input_format == "text":
+            t = p.read_text(encoding="utf-8")
+            if t:
+                yield t
+                seen += 1
+                if limit > 0 and seen >= limit:
+                    return
+        else:
+            raise ValueError(f"unsupported input_format {input_format!r} (jsonl or text)")
+
+
+def build_token_shard_from_texts(texts, tokenizer, output_dir, *, vocab_size: Optional[int] = None,
+                                 tokenizer_name: Optional[str] = None, add_eos: bool = True,
+                                 dtype=None, extra_metadata: Optional[Dict[str, Any]] = None
+                                 ) -> Path:
+    """Tokenise text records (EOS after each when the tokenizer has one) into a
+    streaming token shard; returns the index file."""
+    eos = getattr(tokenizer, "eos_token_id", None)
+
+    def encode(t: str):
+        try:
+            return tokenizer.encode(t, add_special_tokens=False)
+        except TypeError:
+            return tokenizer.encode(t)
+
+    def chunks():
+        for t in texts:
+            ids = list(encode(t))
+            if add_eos and eos is not None:
+                ids.append(int(eos))
+            if ids:
+                yield ids
+
+    vs = vocab_size or getattr(tokenizer, "vocab_size", None)
+    return write_token_shard(output_dir, chunks(), vocab_size=vs, tokenizer=tokenizer_name,
+                             dtype=dtype, extra_metadata=extra_metadata)

@@ -233,3 +233,50 @@ class MetricsTracker:
         t = cls()
         t.history = {k: [tuple(x) for x in v] for k, v in json.loads(Path(path).read_text()).items()}
         return t
+
+
+class TensorBoardMetricWriter:
+    """Scalar dictionaries to TensorBoard under ``prefix/name``
+    (complexity/training/tensorboard.py:13-58); non-numeric, boolean and
+    non-finite values are skipped; without the tensorboard package the writer
+    is disabled (``enabled`` is False) and every call is a no-op."""
+
+    def __init__(self, log_dir, *, enabled: bool = True):
+        import logging as _logging
+        import math as _math
+
+        self._isfinite = _math.isfinite
+        self.writer = None
+        self.log_dir = Path(log_dir)
+        if not enabled:
+            return
+        try:
+            from torch.utils.tensorboard import SummaryWriter
+        except Exception:  # noqa: BLE001 - optional dependency
+            _logging.getLogger(__name__).warning("TensorBoard logging disabled: tensorboard is "
+                                                 "not installed")
+            return
+        self.log_dir.mkdir(parents=True, exist_ok=True)
+        self.writer = SummaryWriter(str(self.log_dir))
+
+    @property
+    def enabled(self) -> bool:
+        return self.writer is not None
+
+    def add_scalars(self, prefix: str, metrics, step: int) -> None:
+        if self.writer is None:
+            return
+        p = prefix.strip("/")
+        for k, v in metrics.items():
+            if isinstance(v, bool) or not isinstance(v, (int, float)) or \
+                    not self._isfinite(float(v)):
+                continue
+            self.writer.add_scalar(f"{p}/{k}", float(v), step)
+
+    def flush(self) -> None:
+        if self.writer is not None:
+            self.writer.flush()
+
+    def close(self) -> None:
+        if self.writer is not None:
+            self.writer.close()

@@ -115,3 +115,28 @@ def save_harm_direction(direction: torch.Tensor, path) -> None:
 
 def load_harm_direction(path, device=None) -> torch.Tensor:
     return torch.load(Path(path), map_location=device or "cpu", weights_only=True)["direction"]
+
+
+class SafetyCallback:
+    """Training callback: logs the clamp statistics every ``log_every`` steps and
+    resets them every ``reset_stats_every`` (complexity/utils/safety.py:399-440).
+    Works both as a Trainer callback (``on_step_end(trainer, step, loss)``) and
+    with the reference's ``on_step_end(metrics)`` call."""
+
+    def __init__(self, model: nn.Module, log_every: int = 100, reset_stats_every: int = 1000):
+        self.model, self.log_every, self.reset_stats_every = model, log_every, reset_stats_every
+        self.step = 0
+        self.history: List[Dict[str, int]] = []
+
+    def on_step_end(self, *args, **kwargs) -> None:
+        import logging
+
+        self.step += 1
+        if self.step % self.log_every == 0:
+            st = get_safety_stats(self.model)
+            self.history.append({"step": self.step, **st})
+            logging.getLogger(__name__).info("Safety stats at step %d: %s", self.step, st)
+        if self.step % self.reset_stats_every == 0:
+            for c in getattr(self.model, "_safety_clamps", []):
+                for k in c.stats:
+                    c.stats[k] = 0

@@ -110,3 +110,34 @@ def test_sequence_packing_plan_and_epoch_schedule():
         pack_example_lengths([9], sequence_length=8)
     s = resolve_epoch_schedule(items=10, world_size=3, batch_size_per_rank=2, epochs=3)
     assert s.steps_per_epoch == 2 and s.total_steps == 6 and s.epoch_steps() == (2, 4, 6)
+
+
+def test_preprocessing_augmentation_and_text_shards(tmp_path):
+    import json
+
+    import torch
+
+    from complexity_framework_b200.data.preprocessing import (DataAugmenter, DataPipeline,
+                                                              MixupCollator, TextPreprocessor)
+    from complexity_framework_b200.data.token_shards import (build_token_shard_from_texts,
+                                                             iter_texts_from_files,
+                                                             load_token_shard)
+    from complexity_framework_b200.data.tokenization import get_tokenizer
+
+    p = TextPreprocessor(lowercase=True)
+    assert p("<b>Visit</b> https://x.io now,  mail a@b.com   PLEASE") == "visit now, mail please"
+    assert p("short") is None
+    assert DataPipeline.create_default()("   tiny  ") is None
+    aug = DataAugmenter(delete_prob=0.3, swap_prob=0.2, insert_prob=0.2)
+    assert aug.augment_tokens(list(range(50)), seed=1) == aug.augment_tokens(list(range(50)), seed=1)
+    b = MixupCollator(0.4)([{"input_ids": torch.arange(4), "labels": torch.tensor(0)},
+                            {"input_ids": torch.arange(4) + 4, "labels": torch.tensor(1)}])
+    assert b["input_ids_mixed"].shape == (2, 4) and 0 <= float(b["mixup_lambda"]) <= 1
+    f = tmp_path / "a.jsonl"
+    f.write_text("\n".join(json.dumps({"text": t}) for t in ("ab", "", "cde")) + "\n")
+    assert list(iter_texts_from_files([f])) == ["ab", "cde"]
+    assert list(iter_texts_from_files([f], limit=1)) == ["ab"]
+    tok = get_tokenizer("byte")
+    build_token_shard_from_texts(iter_texts_from_files([f]), tok, tmp_path / "shard")
+    arr, meta = load_token_shard(tmp_path / "shard")
+    assert meta["num_tokens"] == len(arr) == len(tok.encode("ab")) + len(tok.encode("cde")) + 2

@@ -169,3 +169,18 @@ def test_zipf_weights_bases_and_core_names(tmp_path):
         else True
     with pytest.raises(TypeError):
         AttentionBase(None)
+
+
+def test_tensorboard_writer_and_safety_callback(tmp_path):
+    import torch
+
+    from complexity_framework_b200.training.callbacks import TensorBoardMetricWriter
+    from complexity_framework_b200.utils.safety import SafetyCallback
+
+    w = TensorBoardMetricWriter(tmp_path / "tb", enabled=False)
+    assert not w.enabled
+    w.add_scalars("train", {"loss": 1.0}, 1)
+    cb = SafetyCallback(torch.nn.Linear(2, 2), log_every=1, reset_stats_every=2)
+    cb.on_step_end()
+    cb.on_step_end(None, 2, 0.5)
+    assert [h["step"] for h in cb.history] == [1, 2]
