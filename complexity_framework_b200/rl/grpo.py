@@ -151,5 +151,5 @@ class GRPOTrainer:
             torch.nn.utils.clip_grad_norm_(self.model.parameters(), cfg.max_grad_norm)
             self.opt.step()
         self.step_count += 1
-        stats["loss"] = float(loss)
+        stats["loss"] = float(loss.detach())
         return stats
