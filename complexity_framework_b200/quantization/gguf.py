@@ -9,6 +9,7 @@ metadata, tensor infos (name, dims innermost first, type, offset) and the
 from __future__ import annotations
 
 import struct
+from dataclasses import dataclass
 from enum import IntEnum
 from pathlib import Path
 from typing import Any, Dict, List, Tuple
@@ -86,6 +87,16 @@ def dequantize_q8_0(raw: bytes, n: int) -> np.ndarray:
     return (arr["q"].astype(np.float32) * arr["d"].astype(np.float32)[:, None]).reshape(-1)[:n]
 
 
+@dataclass
+class GGUFTensorInfo:
+    """One tensor-info record: name, dims (innermost first), type, and byte
+    offset inside the aligned data section."""
+    name: str
+    dims: List[int]
+    dtype: GGUFQuantType
+    offset: int
+
+
 class GGUFWriter:
     def __init__(self, path, arch: str = "tr_hash"):
         self.path = Path(path)
@@ -111,21 +122,25 @@ class GGUFWriter:
             raise ValueError(f"unsupported tensor type {qtype}")
         self.tensors.append((name, list(reversed(a.shape)), qtype, raw))
 
+    def tensor_infos(self) -> List[GGUFTensorInfo]:
+        """The tensor-info records ``write`` emits, with their data offsets."""
+        out, off = [], 0
+        for name, dims, qt, raw in self.tensors:
+            out.append(GGUFTensorInfo(name, list(dims), qt, off))
+            off += (len(raw) + ALIGN - 1) // ALIGN * ALIGN
+        return out
+
     def write(self) -> Path:
         head = bytearray(struct.pack("<IIQQ", GGUF_MAGIC, GGUF_VERSION, len(self.tensors),
                                      len(self.meta)))
         for k, v in self.meta.items():
             _kv(head, k, v)
-        off = 0
-        offsets = []
-        for name, dims, qt, raw in self.tensors:
-            _s(head, name)
-            head += struct.pack("<I", len(dims))
-            for d in dims:
+        for info in self.tensor_infos():
+            _s(head, info.name)
+            head += struct.pack("<I", len(info.dims))
+            for d in info.dims:
                 head += struct.pack("<Q", d)
-            head += struct.pack("<IQ", int(qt), off)
-            offsets.append(off)
-            off += (len(raw) + ALIGN - 1) // ALIGN * ALIGN
+            head += struct.pack("<IQ", int(info.dtype), info.offset)
         head += b"\0" * ((-len(head)) % ALIGN)
         with self.path.open("wb") as f:
             f.write(head)

@@ -48,6 +48,14 @@ def newton_schulz(M: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.T
     return X.to(M.dtype)
 
 
+def zeroth_power_newton_schulz(matrix: torch.Tensor) -> torch.Tensor:
+    """Orthogonal factor of one 2-D matrix (five Newton-Schulz steps), the
+    MuSGD helper of complexity/training/musgd.py:14."""
+    if matrix.ndim != 2:
+        raise ValueError("MuSGD orthogonalization expects a 2D matrix")
+    return newton_schulz(matrix)
+
+
 def newton_schulz_adaptive(M: torch.Tensor, min_steps: int = 5, max_steps: int = 10,
                            tol: float = 1e-2, eps: float = 1e-7) -> Tuple[torch.Tensor, int]:
     """Newton-Schulz iterated until the relative change falls under ``tol``.

@@ -104,3 +104,19 @@ def test_trainer_with_optimizer_type(kind, tmp_path):
         l1 = tr.train_step(ids)
     assert l1 < l0
     tr.save_checkpoint()
+
+
+def test_zeroth_power_newton_schulz():
+    import pytest
+
+    from complexity_framework_b200.training.optimizers import zeroth_power_newton_schulz
+
+    torch.manual_seed(0)
+    m = torch.randn(32, 16)
+    o = zeroth_power_newton_schulz(m)
+    assert o.shape == m.shape
+    # singular values pushed into the quintic's band around 1
+    s = torch.linalg.svdvals(o)
+    assert s.min() > 0.5 and s.max() < 1.3
+    with pytest.raises(ValueError):
+        zeroth_power_newton_schulz(torch.randn(2, 3, 4))

@@ -63,3 +63,21 @@ def test_gguf_export(tmp_path):
     p = export_gguf(model, tmp_path / "m.gguf", GGUFQuantType.Q8_0)
     h = read_gguf_header(p)
     assert h["magic"] == 0x46554747 and h["version"] == 3 and h["n_tensors"] > 10
+
+
+def test_gguf_tensor_infos_match_written_header(tmp_path):
+    import struct
+
+    from complexity_framework_b200.quantization import GGUFQuantType, GGUFTensorInfo, GGUFWriter
+
+    w = GGUFWriter(tmp_path / "m.gguf")
+    w.add_tensor("a", torch.randn(3, 5), GGUFQuantType.F32)     # 60 bytes -> 64
+    w.add_tensor("b", torch.randn(2, 64), GGUFQuantType.Q8_0)
+    infos = w.tensor_infos()
+    assert infos[0] == GGUFTensorInfo("a", [5, 3], GGUFQuantType.F32, 0)
+    assert infos[1].offset == 64 and infos[1].dims == [64, 2]
+    raw = w.write().read_bytes()
+    # the "a" tensor info in the header: name, ndims, dims, type, offset
+    i = raw.index(struct.pack("<Q", 1) + b"a")
+    nd, d0, d1, t, off = struct.unpack_from("<IQQIQ", raw, i + 9)
+    assert (nd, d0, d1, t, off) == (2, 5, 3, 0, 0)
