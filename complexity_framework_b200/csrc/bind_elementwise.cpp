@@ -293,7 +293,7 @@ void clip_coef(const torch::Tensor& sumsq, double max_norm, torch::Tensor& clip,
 void paged_attention(const torch::Tensor& q, const torch::Tensor& k_pool,
                      const torch::Tensor& v_pool, const torch::Tensor& page_table,
                      const torch::Tensor& cu_q, const torch::Tensor& kv_lens, torch::Tensor& out,
-                     double scale, int64_t max_q_len) {
+                     double scale, int64_t max_q_len, int64_t pages_per_split) {
   chk(q, torch::kBFloat16, "q");
   chk(k_pool, torch::kBFloat16, "k_pool");
   chk(v_pool, torch::kBFloat16, "v_pool");
@@ -317,6 +317,10 @@ void paged_attention(const torch::Tensor& q, const torch::Tensor& k_pool,
                              max_pages * static_cast<int>(page),
                              at::cuda::getCurrentDeviceProperties()->multiProcessorCount, &pps,
                              &splits);
+  if (pages_per_split > 0) {  // caller's split (tuning); 0 keeps the automatic choice
+    pps = static_cast<int>(pages_per_split);
+    splits = (max_pages + pps - 1) / pps;
+  }
   torch::Tensor ws_o, ws_lse;
   if (splits > 1) {
     const auto f32 = q.options().dtype(torch::kFloat32);
@@ -481,7 +485,9 @@ void register_elementwise(pybind11::module& m) {
         py::arg("hyper") = py::none());
   m.def("sumsq_bf16", &sumsq_bf16);
   m.def("clip_coef", &clip_coef);
-  m.def("paged_attention", &paged_attention);
+  m.def("paged_attention", &paged_attention, py::arg("q"), py::arg("k_pool"), py::arg("v_pool"),
+        py::arg("page_table"), py::arg("cu_q"), py::arg("kv_lens"), py::arg("out"),
+        py::arg("scale"), py::arg("max_q_len"), py::arg("pages_per_split") = 0);
   m.def("paged_qkv_rope", &paged_qkv_rope);
   m.def("skinny_finish", &skinny_finish);
   m.def("skinny_swiglu", &skinny_swiglu);

@@ -14,11 +14,11 @@ from .bench import (ActivationMemoryProfiler, MemoryStats, MemoryTracker, Profil
                     estimate_macs, estimate_model_memory, find_optimal_batch_size,
                     get_memory_stats, get_model_complexity, memory_snapshot)
 from .timing import (LatencyProfiler, MemoryProfiler, ProfilerContext, StepTimer,
-                     ThroughputBenchmark, cuda_time, load_measured_peaks, max_over_ranks, nvtx_range,
+                     ThroughputBenchmark, cuda_graph_time, cuda_time, load_measured_peaks, max_over_ranks, nvtx_range,
                      roofline)
 
 __all__ = ["FLOPSCounter", "LatencyProfiler", "MemoryProfiler", "ModelComplexity",
-           "ProfilerContext", "StepTimer", "ThroughputBenchmark", "count_parameters", "cuda_time",
+           "ProfilerContext", "StepTimer", "ThroughputBenchmark", "count_parameters", "cuda_graph_time", "cuda_time",
            "estimate_transformer_flops", "load_measured_peaks", "max_over_ranks",
            "model_flops_per_token", "nvtx_range", "parameter_breakdown", "profile_model_flops",
            "roofline", "ActivationMemoryProfiler", "MemoryStats", "MemoryTracker", "ProfileResult",

@@ -17,7 +17,7 @@ import json
 import torch
 
 from ..ops import check_errors, require
-from .timing import cuda_time, load_measured_peaks
+from .timing import cuda_graph_time, cuda_time, load_measured_peaks
 
 
 def _report(name, ms, flops=0.0, nbytes=0.0):
@@ -229,13 +229,33 @@ def case_decode(iters: int) -> None:
     _report("paged_attention_decode", cuda_time(lambda: C.paged_attention(
         q, pool.k[0], pool.v[0], b.paged_table, b.paged_cu, b.paged_kv_lens, out,
         D ** -0.5, 1), iters), nbytes=kv_bytes)
+    ref = out.clone()
+    for pps in (8, 12, 16, 24, 32):   # fixed splits against the automatic choice
+        C.paged_attention(q, pool.k[0], pool.v[0], b.paged_table, b.paged_cu, b.paged_kv_lens,
+                          out, D ** -0.5, 1, pps)
+        print(json.dumps({"case": f"paged_attention_decode_pps{pps}_maxdiff",
+                          "value": float((out.float() - ref.float()).abs().max())}), flush=True)
+        _report(f"paged_attention_decode_pps{pps}", cuda_time(lambda: C.paged_attention(
+            q, pool.k[0], pool.v[0], b.paged_table, b.paged_cu, b.paged_kv_lens, out,
+            D ** -0.5, 1, pps), iters), nbytes=kv_bytes)
     x = torch.randn(64, 4096, device="cuda").bfloat16()
     for name, N, K in (("skinny_qkv", 6144, 4096), ("skinny_o", 4096, 4096),
                        ("skinny_down", 4096, 15104)):
-        w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+        # enough weight copies that one graph's calls stream more than L2 (126 MB)
+        copies = max(2, -(-300_000_000 // (N * K * 2)))
+        ws = [(torch.randn(N, K, device="cuda") * 0.02).bfloat16() for _ in range(copies)]
         xk = x if K == 4096 else torch.randn(64, K, device="cuda").bfloat16()
-        _report(name, cuda_time(lambda: fused.gemm_nt(xk, w), iters), 2.0 * 64 * N * K,
-                nbytes=N * K * 2)
+        turn = [0]
+
+        def call():
+            turn[0] += 1
+            return fused.gemm_nt(xk, ws[turn[0] % copies])
+
+        # graph-replayed as in serving: eager launches of these few-microsecond
+        # kernels would time the host
+        _report(name, cuda_graph_time(call, iters, calls_per_graph=2 * copies),
+                2.0 * 64 * N * K, nbytes=N * K * 2)
+        del ws
 
 
 CASES = {"decode": case_decode, "gemm": case_gemm, "gemm_bn": case_gemm_bn, "flash": case_flash, "norms": case_norms,

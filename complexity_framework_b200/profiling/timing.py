@@ -80,6 +80,30 @@ def cuda_time(fn: Callable, iters: int = 10, warmup: int = 3) -> float:
     return s.elapsed_time(e) / iters
 
 
+def cuda_graph_time(fn: Callable, iters: int = 10, calls_per_graph: int = 10,
+                    warmup: int = 3) -> float:
+    """Mean device milliseconds of one ``fn()`` call with ``calls_per_graph``
+    calls captured in one CUDA graph and the graph replayed ``iters`` times.
+
+    For kernels of a few microseconds, eager timing measures the host's launch
+    cost instead of the GPU; serving replays such kernels from graphs, and this
+    times them the same way.  Falls back to ``cuda_time`` on CPU."""
+    if not torch.cuda.is_available():
+        return cuda_time(fn, iters, warmup)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(warmup):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(calls_per_graph):
+            fn()
+    g.replay()
+    return cuda_time(g.replay, iters, warmup) / calls_per_graph
+
+
 class StepTimer:
     """Per-step device time via CUDA events (host clock on CPU); tokens/s and MFU."""
 
