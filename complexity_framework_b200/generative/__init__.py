@@ -19,6 +19,7 @@ from .image import (FrozenAutoencoderKL, TRHashImageConfig, TRHashImageEditConfi
 from .prefix_lm import PrefixLM, TokenResampler
 from .sensor_fusion import (SENSOR_MODALITIES, TRHashSensorFusionBlock,
                             TRHashSensorFusionClassifier, TRHashSensorFusionConfig)
+from .sensor_structured import IMUDeviceGraphTokenizer, SkeletonGraphTokenizer, gradient_reverse
 from .towers import (TRHashVideoBlock, TRHashVideoClassifier, TRHashVideoTower,
                      TRHashVideoTowerConfig, TRHashVisionBlock, TRHashVisionClassifier,
                      TRHashVisionTower, TRHashVisionTowerConfig)
@@ -29,7 +30,8 @@ from .vision_tasks import (SUPPORTED_VISION_TASKS, TRHashDepthEstimator, TRHashI
                            TRHashSemanticSegmenter, create_vision_model,
                            load_vision_task_checkpoint, save_vision_task_checkpoint)
 
-__all__ = [
+__all__ = ["IMUDeviceGraphTokenizer", "SkeletonGraphTokenizer", "gradient_reverse",
+           
     "TRHashImageTextToText", "TRHashVisionLanguageConfig", "TRHashVisionTower",
     "TRHashVisionTowerConfig", "TRHashVisionBlock", "TRHashVisionClassifier",
     "VisualTokenResampler", "TRHashSpeechToText", "TRHashSpeechToTextConfig",

@@ -58,6 +58,8 @@ class TRHashSensorFusionConfig:
     skeleton_coordinates: int = 3
     sequence_tokens: int = 32
     modality_gate: bool = False   # learned per-sample gate over the stream heads
+    structured_encoders: bool = False  # graph encoders for skeleton / 45-channel IMU
+    num_subjects: int = 0         # > 0: subject head behind gradient reversal
 
     @property
     def tokens_per_stream(self) -> int:
@@ -102,6 +104,16 @@ class TRHashSensorFusionClassifier(nn.Module):
             "imu": nn.Linear(c.imu_features, H),
             "radar": nn.Linear(c.radar_features, H),
             "skeleton": nn.Linear(c.skeleton_joints * c.skeleton_coordinates, H)})
+        if c.structured_encoders:
+            from .sensor_structured import IMUDeviceGraphTokenizer, SkeletonGraphTokenizer
+
+            self.structured = nn.ModuleDict()
+            if (c.skeleton_joints, c.skeleton_coordinates) == (17, 3):
+                self.structured["skeleton"] = SkeletonGraphTokenizer(17, 3, H, c.sequence_tokens)
+            if c.imu_features == 45:
+                self.structured["imu"] = IMUDeviceGraphTokenizer(45, H, c.sequence_tokens)
+        if c.num_subjects > 0:
+            self.subject_head = nn.Linear(H, c.num_subjects)
         self.modality = nn.Embedding(len(SENSOR_MODALITIES), H)
         self.pos = nn.Parameter(torch.randn(1, c.tokens_per_stream, H) * 0.02)
         self.blocks = nn.ModuleList(TRHashSensorFusionBlock(c, i) for i in range(c.num_hidden_layers))
@@ -126,6 +138,9 @@ class TRHashSensorFusionClassifier(nn.Module):
 
     def _sequence_tokens(self, m: str, seq: torch.Tensor) -> torch.Tensor:
         """[B, T, F] (skeleton [B, T, J, 3]) -> [B, sequence_tokens, hidden]."""
+        enc = getattr(self, "structured", None)
+        if enc is not None and m in enc:
+            return enc[m](seq.to(self.visual_proj.weight.dtype))
         if seq.dim() == 4:
             seq = seq.flatten(2)
         x = self.seq_in[m](seq.to(self.visual_proj.weight.dtype))
@@ -133,11 +148,14 @@ class TRHashSensorFusionClassifier(nn.Module):
 
     def forward(self, inputs: Mapping[str, torch.Tensor],
                 labels: Optional[torch.Tensor] = None,
-                masks: Optional[Mapping[str, torch.Tensor]] = None) -> Dict[str, torch.Tensor]:
+                masks: Optional[Mapping[str, torch.Tensor]] = None,
+                subject_adversarial_scale: float = 0.0) -> Dict[str, torch.Tensor]:
         """``inputs``: the streams present in the batch; ``masks`` (optional):
         per-stream [B] bools marking the samples that really have that stream
         (absent samples carry zeros and are masked out of attention, pooling
-        and the stream heads).  Every sample needs at least one stream."""
+        and the stream heads).  Every sample needs at least one stream.  With
+        ``num_subjects`` > 0, ``subject_logits`` come from the pooled features
+        through gradient reversal scaled by ``subject_adversarial_scale``."""
         c = self.config
         toks, ids, spans = [], [], []
         for mi, m in enumerate(SENSOR_MODALITIES):
@@ -192,6 +210,11 @@ class TRHashSensorFusionClassifier(nn.Module):
         out = {"logits": logits, "fused_logits": fused, "stream_logits": per,
                "modality_logits": full, "modality_weights": full_w, "modality_mask": full_mask,
                "features": (x * kf).sum(1) / kf.sum(1).clamp_min(1)}
+        if c.num_subjects > 0:
+            from .sensor_structured import gradient_reverse
+
+            out["subject_logits"] = self.subject_head(
+                gradient_reverse(out["features"], subject_adversarial_scale))
         if labels is not None:
             out["loss"] = F.cross_entropy(logits.float(), labels)
         return out
