@@ -160,12 +160,47 @@ class CheckpointManager:
             return json.load(fh)
 
 
-def peek_latest_checkpoint_step(checkpoint_dir: str) -> Optional[int]:
-    p = CheckpointManager(checkpoint_dir).latest()
-    if p is None:
+def _foreign_checkpoint_step(p: Path) -> Optional[int]:
+    """Step of a reference-layout checkpoint directory ``<name>_<step>``, or
+    None when it is not one or was left incomplete: complete means
+    ``checkpoint.pt`` (or a distributed ``.metadata``) exists; the step comes
+    from ``training_state.json`` when present, else from the name."""
+    m = re.fullmatch(r".+_(\d+)", p.name)
+    if not m or not p.is_dir():
         return None
-    with open(p / STATE_FILE) as fh:
-        return int(json.load(fh)["step"])
+    if not ((p / "checkpoint.pt").exists() or (p / ".metadata").exists()):
+        return None
+    try:
+        with open(p / STATE_FILE) as fh:
+            return int(json.load(fh)["step"])
+    except (OSError, ValueError, KeyError):
+        return int(m.group(1))
+
+
+def peek_latest_checkpoint_step(checkpoint_dir: str) -> Optional[int]:
+    """Global step of the newest complete checkpoint under ``checkpoint_dir``
+    without loading any state (for a resume-time data skip), or None.
+
+    Reads this framework's ``<tag>-<step>`` directories (complete once their
+    training state is written) and the reference's ``<name>_<step>`` ones
+    (complexity/utils/checkpointing.py peek_latest_checkpoint_step: complete once
+    ``checkpoint.pt`` or ``.metadata`` exists), so a run can resume a
+    directory written by either framework."""
+    root = Path(checkpoint_dir)
+    if not root.is_dir():
+        return None
+    steps = []
+    p = CheckpointManager(checkpoint_dir).latest()
+    if p is not None:
+        with open(p / STATE_FILE) as fh:
+            steps.append(int(json.load(fh)["step"]))
+    for d in root.iterdir():
+        if re.fullmatch(r"(.+)-(\d+)", d.name):
+            continue                      # this framework's layout, handled above
+        st = _foreign_checkpoint_step(d)
+        if st is not None:
+            steps.append(st)
+    return max(steps) if steps else None
 
 
 def load_weights_only(model: torch.nn.Module, path: str) -> None:

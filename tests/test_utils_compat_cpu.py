@@ -81,3 +81,44 @@ def test_huggingface_directory_roundtrip(tmp_path):
         load_from_huggingface("org/model-on-hub", dst)
     with pytest.raises(RuntimeError, match="network"):
         push_to_hub(src, "x")
+
+
+def _ref_ckpt(base, name, step, *, complete=True, has_state=True, marker="checkpoint.pt"):
+    import json
+    d = base / name
+    d.mkdir(parents=True)
+    if complete:
+        (d / marker).write_bytes(b"x")
+    if has_state:
+        (d / "training_state.json").write_text(json.dumps({"step": step}))
+    return d
+
+
+def test_peek_reads_reference_layout_checkpoints(tmp_path):
+    from complexity_framework_b200.utils.checkpointing import peek_latest_checkpoint_step
+
+    assert peek_latest_checkpoint_step(tmp_path / "missing") is None
+    assert peek_latest_checkpoint_step(tmp_path) is None
+    _ref_ckpt(tmp_path, "token_pack_001_4133", 4133)
+    (tmp_path / "token_pack_002_9999").mkdir()                # crashed mid-save
+    assert peek_latest_checkpoint_step(tmp_path) == 4133
+    _ref_ckpt(tmp_path, "token_pack_002_8265", 8265, has_state=False)   # step from the name
+    _ref_ckpt(tmp_path, "interrupted_5000", 5000)
+    assert peek_latest_checkpoint_step(tmp_path) == 8265
+    other = tmp_path / "meta"
+    _ref_ckpt(other, "step_500", 500, marker=".metadata")
+    assert peek_latest_checkpoint_step(other) == 500
+
+
+def test_peek_mixes_both_layouts(tmp_path):
+    import torch
+
+    from complexity_framework_b200.utils.checkpointing import (CheckpointManager,
+                                                               peek_latest_checkpoint_step)
+
+    m = torch.nn.Linear(2, 2)
+    CheckpointManager(str(tmp_path)).save(m, None, step=9000, tag="step")
+    _ref_ckpt(tmp_path, "token_pack_001_4133", 4133)
+    assert peek_latest_checkpoint_step(tmp_path) == 9000
+    (tmp_path / "step-12000").mkdir()      # ours, incomplete (no training state)
+    assert peek_latest_checkpoint_step(tmp_path) == 9000
