@@ -10,9 +10,11 @@ from __future__ import annotations
 from dataclasses import dataclass
 from typing import List, Optional
 
+import torch
 import torch.nn as nn
 
-from ..generative.sensor_fusion import TRHashSensorFusionClassifier, TRHashSensorFusionConfig
+from ..generative.sensor_fusion import (SENSOR_MODALITIES, TRHashSensorFusionClassifier,
+                                        TRHashSensorFusionConfig)
 from ..generative.towers import TRHashVisionTowerConfig
 from ..generative.vision_language import TRHashImageTextToText, TRHashVisionLanguageConfig
 from ..multimodal.encoders import (AudioEncoder, EncoderConfig, PatchEmbedding, VideoEncoder,
@@ -163,15 +165,24 @@ class Fusion:
 
 
 class Robot:
-    """TR-Hash sensor fusion (IMU, radar, skeleton, depth / IR / thermal frames)."""
+    """TR-Hash sensor fusion (IMU, radar, skeleton, depth / IR / thermal frames).
+
+    Follows complexity/api Robot: visual clips are [batch, channels, time,
+    height, width] unless ``visual_layout`` says otherwise, and the model is
+    cast to the config's ``precision``."""
+
+    MODALITIES = SENSOR_MODALITIES
 
     @classmethod
     def config(cls, **kwargs) -> TRHashSensorFusionConfig:
+        kwargs.setdefault("visual_layout", "bcthw")
         return TRHashSensorFusionConfig(**kwargs)
 
     @classmethod
     def from_config(cls, config: TRHashSensorFusionConfig) -> nn.Module:
-        return TRHashSensorFusionClassifier(config)
+        dtype = {"fp32": torch.float32, "bf16": torch.bfloat16,
+                 "fp16": torch.float16}[config.precision]
+        return TRHashSensorFusionClassifier(config).to(dtype)
 
     @classmethod
     def model(cls, **kwargs) -> nn.Module:

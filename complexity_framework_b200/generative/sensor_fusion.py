@@ -8,7 +8,9 @@ Counterpart: complexity/generative/sensor_fusion/ (config.py
 
 Six streams: depth, infrared and thermal clips share one TR-Hash vision
 tower (each frame -> patch features -> pooled to a small token grid, averaged
-over time); IMU, radar and skeleton sequences are projected and pooled to a
+over time, or pooled to a (time, height, width) token lattice; clips come as
+[B, T, C, H, W] or, with ``visual_layout="bcthw"``, the reference's
+[B, C, T, H, W]); IMU, radar and skeleton sequences are projected and pooled to a
 fixed number of tokens.  Tokens of all present streams (missing ones are
 simply absent) get modality embeddings and pass through TR-Hash blocks routed
 by ``(modality, local token position)``; the prediction mixes the fused head
@@ -19,7 +21,7 @@ from __future__ import annotations
 import json
 import random
 from dataclasses import asdict, dataclass, field
-from typing import Dict, Iterable, List, Mapping, Optional, Sequence, Tuple
+from typing import Dict, Iterable, List, Mapping, Optional, Sequence, Tuple, Union
 
 import torch
 import torch.nn as nn
@@ -45,12 +47,28 @@ class TRHashSensorFusionConfig:
     dropout: float = 0.0
     classifier_dropout: float = 0.1
     visual_channels: Tuple[int, int, int] = (3, 1, 3)   # depth, ir, thermal
-    visual_token_grid: int = 4
+    # int g: g x g spatial tokens per clip, averaged over time; (t, h, w):
+    # a 3-D lattice of t*h*w tokens over time and space
+    visual_token_grid: Union[int, Tuple[int, int, int]] = 4
+    # clip layout: "btchw" ([B, T, C, H, W]) or "bcthw" ([B, C, T, H, W], the
+    # reference's; the ``Robot`` facade defaults to it)
+    visual_layout: str = "btchw"
     vision_image_size: int = 64
     vision_patch_size: int = 8
     vision_hidden_size: int = 128
     vision_layers: int = 2
     vision_heads: int = 4
+    vision_num_experts: int = 4
+    vision_top_k: int = 2
+    vision_shared_width: int = 0     # 0: 2 x vision_hidden_size
+    vision_expert_width: int = 0     # 0: max(16, vision_hidden_size // 4)
+    # The reference's hierarchical tower splits vision_layers into windowed
+    # stages; this tower is one flat stage with global attention over the
+    # (small) patch grid, so the split is validated and otherwise unused.
+    vision_stage_depths: Tuple[int, ...] = ()
+    vision_window_size: int = 0
+    precision: str = "bf16"          # fp32 | bf16 | fp16: dtype ``Robot.from_config`` casts to
+    layer_norm_eps: float = 1e-5
     late_fusion_weight: float = 0.5
     imu_features: int = 45
     radar_features: int = 16
@@ -61,9 +79,32 @@ class TRHashSensorFusionConfig:
     structured_encoders: bool = False  # graph encoders for skeleton / 45-channel IMU
     num_subjects: int = 0         # > 0: subject head behind gradient reversal
 
+    def __post_init__(self):
+        if not isinstance(self.visual_token_grid, int):
+            self.visual_token_grid = tuple(int(v) for v in self.visual_token_grid)
+            if len(self.visual_token_grid) != 3 or min(self.visual_token_grid) <= 0:
+                raise ValueError("visual_token_grid must be an int or (time, height, width)")
+        self.visual_channels = tuple(self.visual_channels)
+        self.vision_stage_depths = tuple(self.vision_stage_depths)
+        if self.visual_layout not in ("btchw", "bcthw"):
+            raise ValueError("visual_layout must be 'btchw' or 'bcthw'")
+        if self.precision not in ("fp32", "bf16", "fp16"):
+            raise ValueError("precision must be fp32, bf16 or fp16")
+        if self.vision_stage_depths and sum(self.vision_stage_depths) != self.vision_layers:
+            raise ValueError("vision_layers must equal sum(vision_stage_depths)")
+        if not 0 < self.vision_top_k <= self.vision_num_experts:
+            raise ValueError("invalid vision expert routing configuration")
+        if self.hidden_size % self.num_attention_heads:
+            raise ValueError("hidden_size must be divisible by num_attention_heads")
+
+    @property
+    def visual_tokens(self) -> int:
+        g = self.visual_token_grid
+        return g * g if isinstance(g, int) else g[0] * g[1] * g[2]
+
     @property
     def tokens_per_stream(self) -> int:
-        return max(self.visual_token_grid ** 2, self.sequence_tokens)
+        return max(self.visual_tokens, self.sequence_tokens)
 
     @property
     def route_vocab_size(self) -> int:
@@ -95,8 +136,10 @@ class TRHashSensorFusionClassifier(nn.Module):
         self.vision = TRHashVisionTower(TRHashVisionTowerConfig(
             image_size=c.vision_image_size, patch_size=c.vision_patch_size, num_channels=3,
             hidden_size=c.vision_hidden_size, num_layers=c.vision_layers,
-            num_heads=c.vision_heads, num_experts=4, top_k=2, shared_width=2 * c.vision_hidden_size,
-            expert_width=max(16, c.vision_hidden_size // 4), use_cls_token=False))
+            num_heads=c.vision_heads, num_experts=c.vision_num_experts, top_k=c.vision_top_k,
+            shared_width=c.vision_shared_width or 2 * c.vision_hidden_size,
+            expert_width=c.vision_expert_width or max(16, c.vision_hidden_size // 4),
+            use_cls_token=False))
         self.visual_in = nn.ModuleDict({m: nn.Conv2d(ch, 3, 1)
                                         for m, ch in zip(VISUAL_MODALITIES, c.visual_channels)})
         self.visual_proj = nn.Linear(c.vision_hidden_size, H)
@@ -117,7 +160,7 @@ class TRHashSensorFusionClassifier(nn.Module):
         self.modality = nn.Embedding(len(SENSOR_MODALITIES), H)
         self.pos = nn.Parameter(torch.randn(1, c.tokens_per_stream, H) * 0.02)
         self.blocks = nn.ModuleList(TRHashSensorFusionBlock(c, i) for i in range(c.num_hidden_layers))
-        self.norm = nn.LayerNorm(H)
+        self.norm = nn.LayerNorm(H, eps=c.layer_norm_eps)
         self.drop = nn.Dropout(c.classifier_dropout)
         self.head = nn.Linear(H, c.num_classes)
         self.stream_heads = nn.ModuleDict({m: nn.Linear(H, c.num_classes) for m in SENSOR_MODALITIES})
@@ -125,7 +168,10 @@ class TRHashSensorFusionClassifier(nn.Module):
             self.gate = nn.Linear(H, 1)
 
     def _visual_tokens(self, m: str, clip: torch.Tensor) -> torch.Tensor:
-        """[B, T, C, H, W] -> [B, grid^2, hidden]."""
+        """A clip ([B, T, C, H, W], or [B, C, T, H, W] with the "bcthw"
+        layout) -> [B, visual_tokens, hidden]."""
+        if self.config.visual_layout == "bcthw":
+            clip = clip.transpose(1, 2)
         B, T = clip.shape[:2]
         frames = self.visual_in[m](clip.flatten(0, 1).to(self.visual_proj.weight.dtype))
         if frames.shape[-1] != self.config.vision_image_size:
@@ -133,7 +179,11 @@ class TRHashSensorFusionClassifier(nn.Module):
                                    mode="bilinear", align_corners=False)
         f = self.vision.patch_features(frames)                      # [B*T, D, g, g]
         g = self.config.visual_token_grid
-        f = F.adaptive_avg_pool2d(f, g).view(B, T, -1, g * g).mean(1)
+        if isinstance(g, int):
+            f = F.adaptive_avg_pool2d(f, g).view(B, T, -1, g * g).mean(1)
+        else:   # (time, height, width) lattice
+            f = f.view(B, T, *f.shape[1:]).transpose(1, 2)          # [B, D, T, g, g]
+            f = F.adaptive_avg_pool3d(f, g).flatten(2)              # [B, D, t*h*w]
         return self.visual_proj(f.transpose(1, 2))
 
     def _sequence_tokens(self, m: str, seq: torch.Tensor) -> torch.Tensor:
