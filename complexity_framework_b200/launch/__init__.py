@@ -9,7 +9,9 @@ verify_token_shards.py).
 """
 from .launcher import build_torchrun_command, launch
 from .replay import build_replay_plan, verify_token_data
-from .supervisor import RunSupervisor, SupervisorConfig, seconds_since_last_write
+from .supervisor import (RunSupervisor, SupervisorConfig, restart_program, seconds_since_last_write,
+                         watch_once, watch_supervisord)
 
 __all__ = ["build_torchrun_command", "launch", "build_replay_plan", "verify_token_data",
-           "RunSupervisor", "SupervisorConfig", "seconds_since_last_write"]
+           "RunSupervisor", "SupervisorConfig", "seconds_since_last_write", "restart_program",
+           "watch_once", "watch_supervisord"]

@@ -132,3 +132,50 @@ class RunSupervisor:
 
     def _on_signal(self, signum, frame):  # noqa: ARG002
         self._stop = True
+
+
+# ------------------------------------------- external watchdog (supervisord)
+def restart_program(program: str, runner=subprocess.run) -> bool:
+    """``supervisorctl restart <program>``; True when it exits 0.  For runs
+    that supervisord owns (the process cannot be a child of this one)."""
+    logger.error("%s: progress file stale, restarting through supervisorctl", program)
+    res = runner(["supervisorctl", "restart", program], capture_output=True, text=True)
+    if res.returncode != 0:
+        logger.error("restart of %s failed: %s %s", program, (res.stdout or "").strip(),
+                     (res.stderr or "").strip())
+        return False
+    return True
+
+
+def watch_once(log_file: Path, program: str, stall_seconds: float,
+               now: Optional[float] = None, restart=restart_program) -> bool:
+    """One staleness check: restart ``program`` (and return True) when
+    ``log_file`` exists and has not been written for over ``stall_seconds``;
+    a file that does not exist yet means the run is still starting."""
+    idle = seconds_since_last_write(log_file, now=now)
+    if idle is None or idle <= stall_seconds:
+        return False
+    restart(program)
+    return True
+
+
+def watch_supervisord(log_file: Path, program: str, stall_seconds: float = 900.0,
+                      poll_seconds: float = 60.0, cooldown_seconds: Optional[float] = None,
+                      max_checks: Optional[int] = None, sleep=time.sleep, clock=time.time,
+                      restart=restart_program) -> int:
+    """Poll forever (or ``max_checks`` times); restarts are at least
+    ``cooldown_seconds`` apart (default ``stall_seconds``, so a run that is
+    broken is not restarted faster than it could write a fresh line).  Keep
+    ``stall_seconds`` above the collective timeout so a hung collective
+    errors out before the watchdog fires.  Returns the number of restarts."""
+    cooldown = stall_seconds if cooldown_seconds is None else cooldown_seconds
+    last, restarts, checks = float("-inf"), 0, 0
+    while max_checks is None or checks < max_checks:
+        now = clock()
+        if now - last >= cooldown and watch_once(Path(log_file), program, stall_seconds, now,
+                                                 restart=restart):
+            last, restarts = now, restarts + 1
+        checks += 1
+        if max_checks is None or checks < max_checks:
+            sleep(poll_seconds)
+    return restarts

@@ -80,3 +80,36 @@ def test_replay_plan_and_verify(tmp_path):
     shard.write_bytes(bytes(b))
     r = verify_token_data(tmp_path)
     assert not r["ok"] and r["bad"][0]["problem"] == "sha256"
+
+
+def test_supervisord_watchdog(tmp_path):
+    import os
+    from types import SimpleNamespace
+
+    from complexity_framework_b200.launch import (restart_program, seconds_since_last_write,
+                                                  watch_once, watch_supervisord)
+
+    log = tmp_path / "train.log"
+    assert seconds_since_last_write(log) is None
+    calls = []
+    assert not watch_once(log, "train", 60, restart=calls.append)       # not written yet
+    log.write_text("step 1\n")
+    os.utime(log, (1000.0, 1000.0))
+    assert seconds_since_last_write(log, now=1030.0) == 30.0
+    assert not watch_once(log, "train", 60, now=1030.0, restart=calls.append)
+    assert watch_once(log, "train", 60, now=1100.0, restart=calls.append) and calls == ["train"]
+
+    ran = []
+    ok = restart_program("train", runner=lambda cmd, **kw: ran.append(cmd) or
+                         SimpleNamespace(returncode=0, stdout="", stderr=""))
+    assert ok and ran == [["supervisorctl", "restart", "train"]]
+    assert not restart_program("train", runner=lambda cmd, **kw:
+                               SimpleNamespace(returncode=1, stdout="", stderr="no such"))
+
+    # stale the whole time: restarts respect the cooldown (every 3rd poll here)
+    t = iter(range(2000, 2000 + 60 * 10, 60))
+    restarted = []
+    n = watch_supervisord(log, "train", stall_seconds=100, poll_seconds=60,
+                          cooldown_seconds=150, max_checks=9, sleep=lambda s: None,
+                          clock=lambda: float(next(t)), restart=restarted.append)
+    assert n == 3 and restarted == ["train"] * 3
