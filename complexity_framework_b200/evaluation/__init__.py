@@ -1,7 +1,7 @@
 """Evaluation: perplexity and text metrics, multiple-choice benchmarks,
 synthetic recall probes."""
 from .benchmarks import (ARCBenchmark, BENCHMARKS, BenchmarkResult, BenchmarkRunner,
-                         HellaSwagBenchmark, MMLUBenchmark, TruthfulQABenchmark,
+                         HellaSwagBenchmark, MMLUBenchmark, PIQABenchmark, TruthfulQABenchmark,
                          WinograndeBenchmark, choice_logprobs)
 from .metrics import (BertScoreEvaluator, bleu, distinct_n, self_bleu, compute_accuracy, compute_f1, compute_perplexity,
                       exact_match, expected_calibration_error, perplexity_from_loss, rouge,

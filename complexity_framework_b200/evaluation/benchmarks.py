@@ -126,7 +126,30 @@ class TruthfulQABenchmark(Benchmark):
         return "Q: " + r["question"] + "\nA:", [" " + c for c in t["choices"]], t["labels"].index(1)
 
 
-BENCHMARKS = {"mmlu": MMLUBenchmark, "hellaswag": HellaSwagBenchmark,
+class PIQABenchmark(Benchmark):
+    """Rows: {"goal", "sol1", "sol2", "label": 0|1}; zero-shot continuation
+    log-likelihood of each solution after "Question: <goal>\nAnswer:".
+    ``accuracy`` is acc_norm (log-likelihood per byte of the solution);
+    ``details[-1]`` carries both acc and acc_norm."""
+    name = "piqa"
+
+    def run(self, model, tokenizer) -> BenchmarkResult:
+        rows = self.load()
+        acc = acc_norm = 0
+        for r in rows:
+            ctx = "Question: " + r["goal"] + "\nAnswer:"
+            sols = [" " + r["sol1"], " " + r["sol2"]]
+            lp = choice_logprobs(model, tokenizer, ctx, sols, normalize=False)
+            per_byte = [v / max(1, len(c.encode("utf-8"))) for v, c in zip(lp, sols)]
+            gold = int(r["label"])
+            acc += int(max(range(2), key=lp.__getitem__) == gold)
+            acc_norm += int(max(range(2), key=per_byte.__getitem__) == gold)
+        n = max(1, len(rows))
+        return BenchmarkResult(self.name, acc_norm / n, len(rows),
+                               [{"acc": acc / n, "acc_norm": acc_norm / n}])
+
+
+BENCHMARKS = {"mmlu": MMLUBenchmark, "piqa": PIQABenchmark, "hellaswag": HellaSwagBenchmark,
               "winogrande": WinograndeBenchmark, "arc": ARCBenchmark,
               "truthfulqa": TruthfulQABenchmark}
 

@@ -1,0 +1,102 @@
+"""Behaviour regression gate: response checks, sandboxed code cases, the
+PIQA floor, chat-report generation and PIQA scoring on a tiny model."""
+import json
+
+import pytest
+
+from complexity_framework_b200.evaluation.regression_gate import (audit_regression, check_response,
+                                                                  generate_chat_report,
+                                                                  run_python_cases)
+
+PANEL = {
+    "schema_version": 1, "id": "tiny-panel",
+    "generation": {"max_tokens": 4, "temperature": 0.0, "top_p": 1.0, "top_k": 0},
+    "piqa": {"baseline_acc_norm": 0.70, "maximum_absolute_drop": 0.01, "examples": 2},
+    "prompts": [
+        {"id": "hi", "capability": "conversation", "prompt": "Hi!",
+         "checks": {"required_any": ["hello", "hi"], "max_words": 10}},
+        {"id": "mul", "capability": "math", "prompt": "12 x 11?",
+         "checks": {"required_numbers": ["132"]}},
+        {"id": "sq", "capability": "code", "prompt": "Write square(x).",
+         "checks": {"python_function": "square",
+                    "cases": [{"args": [3], "expected": 9}, {"args": [-2], "expected": 4}]}},
+        {"id": "mem", "capability": "multi_turn_memory",
+         "messages": [{"role": "user", "content": "My cat is Tom."},
+                      {"role": "assistant", "content": "Noted."},
+                      {"role": "user", "content": "Cat's name?"}],
+         "checks": {"required_all": ["tom"]}},
+        {"id": "bul", "capability": "instruction_constraints", "prompt": "Two tips.",
+         "checks": {"exact_bullets": 2, "max_words_per_bullet": 4}},
+    ],
+}
+GOOD = {"hi": "Hello there", "mul": "It is 132.", "sq": "```python\ndef square(x):\n    return x * x\n```",
+        "mem": "Your cat is Tom.", "bul": "- drink water\n- sleep well"}
+
+
+def test_checks():
+    items = {i["id"]: i for i in PANEL["prompts"]}
+    assert all(check_response(items[k], v) == [] for k, v in GOOD.items())
+    assert check_response(items["hi"], "") == ["empty_response"]
+    assert check_response(items["hi"], "good day " * 8)[0].startswith("missing_any")
+    assert any(f.startswith("too_many_words") for f in check_response(items["hi"], "hi " * 11))
+    assert check_response(items["mul"], "It is 1320.") == ["missing_number:132"]
+    assert check_response(items["bul"], "- a\n- b\n- c") == ["bullet_count:3"]
+    assert check_response(items["bul"], "- one two three four five\n- ok") == ["long_bullets:0"]
+
+
+def test_code_sandbox():
+    cases = [{"args": [3], "expected": 9}]
+    assert run_python_cases("def square(x):\n    return x * x", "square", cases) is None
+    assert run_python_cases("def square(x):\n    return x + x", "square", cases).startswith(
+        "case_0_expected_9_got_6")
+    assert run_python_cases("import os\ndef square(x):\n    return x*x", "square", cases) == \
+        "unsafe_python_import"
+    assert run_python_cases("import math\ndef square(x):\n    return int(math.pow(x, 2))",
+                            "square", cases) is None
+    assert run_python_cases("def square(x):\n    return x.__class__", "square", cases) == \
+        "unsafe_dunder_access"
+    assert run_python_cases("def square(x):\n    while True:\n        pass", "square", cases,
+                            timeout_s=1.0) == "python_timeout:TimeoutError"
+    assert run_python_cases("def sq(x):\n    return x", "square", cases) == \
+        "missing_function:square"
+    assert run_python_cases("def square(x) return", "square", cases).startswith("invalid_python")
+    assert run_python_cases("open('f', 'w')\ndef square(x):\n    return x*x", "square",
+                            cases) == "python_exec_error:NameError"
+
+
+def test_audit_combines_behaviour_template_and_piqa():
+    report = {"chat_template_applied": True,
+              "results": [{"id": k, "response": v} for k, v in GOOD.items()]}
+    ok = audit_regression(PANEL, report, {"benchmarks": {"piqa": {"acc_norm": 0.695}}})
+    assert ok["passed"] and ok["piqa_threshold"] == pytest.approx(0.69)
+    low = audit_regression(PANEL, report, {"benchmarks": {"piqa": {"acc_norm": 0.68}}})
+    assert not low["passed"] and "piqa" in low["failures"]
+    raw = audit_regression(PANEL, {**report, "chat_template_applied": False},
+                           {"benchmarks": {"piqa": {"acc_norm": 0.9}}})
+    assert raw["failures"] == {"chat_template": ["official_chat_template_not_applied"]}
+
+
+def test_report_and_piqa_on_a_tiny_model(tmp_path):
+    import torch
+
+    from complexity_framework_b200 import ComplexityModel, ModelConfig
+    from complexity_framework_b200.data import ByteTokenizer
+    from complexity_framework_b200.evaluation import PIQABenchmark
+
+    tok = ByteTokenizer()
+    torch.manual_seed(0)
+    m = ComplexityModel(ModelConfig(hidden_size=64, num_hidden_layers=1, num_attention_heads=4,
+                                    num_key_value_heads=2, vocab_size=tok.vocab_size,
+                                    intermediate_size=64, shared_intermediate_size=128,
+                                    num_experts=4, top_k=2, routing_strategy="modulo_cyclic",
+                                    max_position_embeddings=1024)).eval()
+    rep = generate_chat_report(m, tok, PANEL)
+    assert rep["chat_template_applied"] and [r["id"] for r in rep["results"]] == \
+        [p["id"] for p in PANEL["prompts"]]
+    p = tmp_path / "piqa.jsonl"
+    p.write_text("\n".join(json.dumps(r) for r in [
+        {"goal": "Dry wet hands", "sol1": "use a towel", "sol2": "use water", "label": 0},
+        {"goal": "Open a jar", "sol1": "twist the lid", "sol2": "paint the lid", "label": 0}]))
+    res = PIQABenchmark(str(p)).run(m, tok)
+    assert res.num_samples == 2 and 0.0 <= res.accuracy <= 1.0
+    assert set(res.details[-1]) == {"acc", "acc_norm"}
