@@ -100,3 +100,44 @@ def test_report_and_piqa_on_a_tiny_model(tmp_path):
     res = PIQABenchmark(str(p)).run(m, tok)
     assert res.num_samples == 2 and 0.0 <= res.accuracy <= 1.0
     assert set(res.details[-1]) == {"acc", "acc_norm"}
+
+
+def _release_fixture(tmp_path, rows, ours=False):
+    import csv
+    ev, ck, mp = tmp_path / "eval", tmp_path / "ckpt", tmp_path / "metrics.csv"
+    tmp_path.mkdir(parents=True, exist_ok=True)
+    with mp.open("w", newline="") as fh:
+        w = csv.DictWriter(fh, fieldnames=("step", "matched_eval_loss", "matched_eval_ppl"))
+        w.writeheader()
+        for step, _a, _n, loss, _p in rows:
+            w.writerow({"step": step, "matched_eval_loss": loss, "matched_eval_ppl": 3.0})
+    for e, (step, acc, accn, _l, passed) in enumerate(rows, start=1):
+        d = ev / f"epoch_{e:02d}_step_{step:06d}"
+        d.mkdir(parents=True)
+        (d / "piqa.json").write_text(json.dumps({"checkpoint_step": step, "benchmarks": {
+            "piqa": {"acc": acc, "acc_norm": accn, "correct": 1, "correct_norm": 1}}}))
+        (d / "promotion.json").write_text(json.dumps({"passed": passed, "failures": {}}))
+        c = ck / (f"step-{step}" if ours else f"step_{step:06d}")
+        c.mkdir(parents=True)
+        (c / ("training_state.json" if ours else "checkpoint.pt")).write_text("{}")
+    return ev, mp, ck
+
+
+def test_release_selection(tmp_path):
+    from complexity_framework_b200.evaluation.release import select_release_checkpoint
+
+    s = select_release_checkpoint(*_release_fixture(tmp_path / "a", [
+        (100, 0.70, 0.70, 1.3, True), (200, 0.75, 0.75, 1.2, False),
+        (300, 0.71, 0.72, 1.4, True)]), expected_epochs=3)
+    assert s["release_ready"] and s["selected"]["step"] == 300
+    assert s["candidates"][1]["promotion_passed"] is False
+    s = select_release_checkpoint(*_release_fixture(tmp_path / "b", [
+        (100, 0.70, 0.71, 1.3, True), (200, 0.70, 0.71, 1.1, True),
+        (300, 0.69, 0.70, 1.0, True)], ours=True))
+    assert s["selected"]["step"] == 200          # eval loss breaks the PIQA tie
+    s = select_release_checkpoint(*_release_fixture(tmp_path / "c", [
+        (100, 0.7, 0.7, 1.0, False), (200, 0.7, 0.7, 1.0, False)]))
+    assert not s["release_ready"] and s["selected"] is None
+    with pytest.raises(ValueError):
+        select_release_checkpoint(*_release_fixture(tmp_path / "d", [(1, .5, .5, 1., True)]),
+                                  expected_epochs=3)
