@@ -141,3 +141,55 @@ def test_release_selection(tmp_path):
     with pytest.raises(ValueError):
         select_release_checkpoint(*_release_fixture(tmp_path / "d", [(1, .5, .5, 1., True)]),
                                   expected_epochs=3)
+
+
+@pytest.mark.parametrize("layout,dtype", [("ours", None), ("reference", "bfloat16")])
+def test_export_release(tmp_path, layout, dtype):
+    import torch
+    from safetensors import safe_open
+
+    from complexity_framework_b200 import ComplexityModel, ModelConfig
+    from complexity_framework_b200.evaluation.release import export_release
+    from complexity_framework_b200.utils.checkpointing import CheckpointManager
+
+    cfg = ModelConfig(hidden_size=32, num_hidden_layers=1, num_attention_heads=2,
+                      num_key_value_heads=1, vocab_size=64, intermediate_size=32,
+                      shared_intermediate_size=64, num_experts=4, top_k=2,
+                      routing_strategy="modulo_cyclic", max_position_embeddings=64)
+    torch.manual_seed(0)
+    m = ComplexityModel(cfg)
+    if layout == "ours":
+        ck = CheckpointManager(str(tmp_path / "ck")).save(m, None, step=200, tag="step")
+    else:
+        ck = tmp_path / "ck" / "step_000200"
+        ck.mkdir(parents=True)
+        torch.save({"step": 200, "model": m.state_dict(), "config": cfg.to_dict()},
+                   ck / "checkpoint.pt")
+    sel = {"epoch": 2, "step": 200, "checkpoint": str(ck), "promotion_passed": True,
+           "piqa_acc": 0.69, "piqa_acc_norm": 0.70, "matched_eval_loss": 1.2,
+           "matched_eval_ppl": 3.3}
+    sp = tmp_path / "summary.json"
+    sp.write_text(json.dumps({"release_ready": True, "selection_policy": "p", "selected": sel,
+                              "candidates": [sel]}))
+    tok = tmp_path / "tok"
+    tok.mkdir()
+    (tok / "tokenizer.json").write_text("{}")
+    (tok / "tokenizer_config.json").write_text(json.dumps(
+        {"eos_token": "</s>", "added_tokens_decoder": {"0": {"content": "</s>"}}}))
+    out = tmp_path / "release"
+    man = export_release(sp, out, tokenizer_dir=tok, weights_dtype=dtype)
+    want = "bfloat16" if dtype else "float32"
+    conf = json.loads((out / "config.json").read_text())
+    assert conf["model_type"] == "tr_hash_moe" and conf["architectures"] == ["TRHashForCausalLM"]
+    assert conf["num_experts_per_tok"] == 2 and conf["eos_token_id"] == 0
+    assert conf["torch_dtype"] == want and man["weights_dtype"] == want
+    assert man["selected_epoch"] == 2 and man["behavior_gate_passed"] and man["weights_sha256"]
+    assert (out / "tokenizer.json").is_file() and "Apache-2.0" in (out / "README.md").read_text()
+    with safe_open(str(out / "model.safetensors"), "pt") as f:
+        assert f.metadata()["format"] == "pt"
+        assert f.get_tensor("embed_tokens.weight").dtype == getattr(torch, want)
+    # the release directory loads back as a model with the same config
+    back = ComplexityModel.from_pretrained(str(out))
+    assert back.config.num_experts == 4
+    with pytest.raises(FileExistsError):
+        export_release(sp, out)
