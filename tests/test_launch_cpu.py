@@ -113,3 +113,46 @@ def test_supervisord_watchdog(tmp_path):
                           cooldown_seconds=150, max_checks=9, sleep=lambda s: None,
                           clock=lambda: float(next(t)), restart=restarted.append)
     assert n == 3 and restarted == ["train"] * 3
+
+
+def test_collect_run_artifacts(tmp_path):
+    import hashlib
+    import json
+
+    import pytest
+    import torch
+    from safetensors.torch import load_file
+
+    from complexity_framework_b200.launch.artifacts import collect_run_artifacts
+
+    ck = tmp_path / "ck" / "step_000010"
+    ck.mkdir(parents=True)
+    tied = torch.randn(8, 4)
+    torch.save({"step": 10, "model": {"embed.weight": tied, "lm_head.weight": tied},
+                "config": {"hidden_size": 4}, "optimizer": {"huge": 1}}, ck / "checkpoint.pt")
+    run = tmp_path / "run"
+    run.mkdir()
+    (run / "metrics.csv").write_text("step,loss\n10,2.0\n")
+    (run / "train.log").write_text("ok\n")
+    (run / "notes.bin").write_bytes(b"skip")
+    data = tmp_path / "data" / "train"
+    data.mkdir(parents=True)
+    (data / "tokens.idx.json").write_text("{}")
+    (data / "tokens.bin").write_bytes(b"\0" * 64)
+    tok = tmp_path / "tok"
+    tok.mkdir()
+    (tok / "tokenizer.json").write_text("{}")
+    out = tmp_path / "out"
+    man = collect_run_artifacts("r", str(ck), str(run), str(out), str(tmp_path / "data"), str(tok))
+    w = load_file(str(out / "model.safetensors"))
+    assert torch.equal(w["embed.weight"], tied) and torch.equal(w["lm_head.weight"], tied)
+    cfg = json.loads((out / "model_config.json").read_text())
+    assert cfg["checkpoint_step"] == 10 and cfg["model"]["hidden_size"] == 4
+    assert man["checkpoint"]["sha256"] == hashlib.sha256((ck / "checkpoint.pt").read_bytes()
+                                                         ).hexdigest()
+    paths = {f["path"] for f in man["files"]}
+    assert {"model.safetensors", "metrics.csv", "train.log", "dataset/train/tokens.idx.json",
+            "tokenizer/tokenizer.json"} <= paths
+    assert "notes.bin" not in paths and "dataset/train/tokens.bin" not in paths
+    with pytest.raises(FileExistsError):
+        collect_run_artifacts("r", str(ck), str(run), str(out))
