@@ -70,3 +70,44 @@ def test_classifier_with_structured_encoders_and_subject_head():
         num_classes=5, hidden_size=64, num_hidden_layers=1, num_attention_heads=4,
         num_experts=4, shared_width=64, expert_width=32, sequence_tokens=8))
     assert not hasattr(plain, "structured") and "subject_logits" not in plain(inputs)
+
+
+def _diag_model_and_batches():
+    from complexity_framework_b200.generative.sensor_fusion import collate_sensors_masked
+
+    torch.manual_seed(0)
+    cfg = TRHashSensorFusionConfig(num_classes=4, hidden_size=64, num_hidden_layers=1,
+                                   num_attention_heads=4, num_experts=4, shared_width=64,
+                                   expert_width=32, sequence_tokens=8, classifier_dropout=0.0)
+    m = TRHashSensorFusionClassifier(cfg)
+    samples = [({"imu": torch.randn(12, 45), "skeleton": torch.randn(12, 17, 3)}, i % 4)
+               for i in range(6)] + [({"imu": torch.randn(12, 45)}, 1), ({"imu": torch.randn(12, 45)}, 2)]
+    batches = []
+    for j in range(0, 8, 4):
+        inputs, masks, labels = collate_sensors_masked(samples[j:j + 4])
+        batches.append((inputs, masks, labels, torch.tensor([0, 0, 1, 1])))
+    return m, batches
+
+
+def test_sensor_diagnostics():
+    from complexity_framework_b200.generative.sensor_diagnostics import (
+        evaluate_late_fusion_sweep, evaluate_sensor_mode, hash_route_diagnostics)
+
+    m, batches = _diag_model_and_batches()
+    d = hash_route_diagnostics(m)["layers"]
+    assert d and all(sum(v["expert_assignments"]) == v["routes"] * v["top_k"] for v in d.values())
+    allm = evaluate_sensor_mode(m, batches, "cpu")
+    assert allm["examples"] == 8 and set(allm["by_subject"]) == {"0", "1"}
+    sk = evaluate_sensor_mode(m, batches, "cpu", modality="skeleton")
+    assert sk["examples"] == 6 and sk["mode"] == "skeleton"
+    sweep = evaluate_late_fusion_sweep(m, batches, "cpu", late_weights=(0.0, 1.0),
+                                       gate_temperatures=(1.0,), stream_boosts={"skeleton": (1.0, 2.0)})
+    assert len(sweep["results"]) == 4 and sweep["examples"] == 8
+    # w = 1, T = 1, boost 1 is the model's own mixing (late_fusion_weight 0.5 =
+    # (fused + per) / 2): same predictions as the plain evaluation
+    own = next(r for r in sweep["results"] if r["late_weight"] == 1.0
+               and r["boosts"] == {"skeleton": 1.0})
+    assert own["accuracy"] == pytest.approx(allm["accuracy"])
+    assert own["macro_f1"] == pytest.approx(allm["macro_f1"])
+    with pytest.raises(ValueError):
+        evaluate_late_fusion_sweep(m, batches, "cpu", gate_temperatures=(0.0,))
