@@ -253,3 +253,26 @@ def test_cli_train_detector_and_detect(tmp_path, capsys):
     for d in res["detections"]:
         x0, y0, x1, y1 = d["box"]
         assert 0 <= x0 <= x1 <= 80 and 0 <= y0 <= y1 <= 48  # original-image coordinates
+
+
+def test_release_evaluation_branches_and_timing():
+    import pytest
+
+    from complexity_framework_b200.generative.detection.release_eval import (
+        BRANCHES, branches_to_run, evaluate_release, percentile, timing_summary)
+
+    with pytest.raises(ValueError, match="NMS-free"):
+        branches_to_run("both", has_nms_free=False)
+    assert branches_to_run("o2m-nms", has_nms_free=False) == ("o2m-nms",)
+    assert branches_to_run("both", has_nms_free=True) == BRANCHES
+    s = timing_summary([0.1, 0.3, 0.2], image_count=12)
+    assert s["mean_batch_ms"] == pytest.approx(200.0) and s["p50_batch_ms"] == pytest.approx(200.0)
+    assert s["p95_batch_ms"] == pytest.approx(300.0) and s["images_per_second"] == pytest.approx(20.0)
+    assert s["measured_seconds"] == pytest.approx(0.6) and percentile([], 0.95) == 0.0
+    torch.manual_seed(0)
+    m = TRHashObjectDetector(_small())
+    ds = SyntheticShapesDataset(6, 64, 2, 2, seed=3)
+    ims, tgs = collate_detection([ds[i] for i in range(6)])
+    r = evaluate_release(m, ims, tgs, batch_size=4, warmup=1)
+    assert set(r) == {"o2m-nms"} and {"mAP", "AP50"} <= set(r["o2m-nms"]["metrics"])
+    assert r["o2m-nms"]["timing"]["images_per_second"] > 0
